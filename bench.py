@@ -1,0 +1,420 @@
+"""Benchmark of the Chelis B200 backend (one JSON line on rank 0).
+
+Headline workload (its largest size): C = A.B, row-major,
+M = N = K = 8192, f32, A and B ~ U(-1, 1) (seed 1), through the library's
+matmul entry (3xTF32 on tcgen05: split pre-pass + tensor-core main kernel).
+Metric: TFLOP/s of useful work (2 N^3 per product), whole job.
+
+  value     device-resident inputs, CUDA-event timed over exactly --steps
+            products after --warmup untimed ones (inputs of 512 MiB exceed
+            the 126 MB L2, so no flush is needed), max over ranks.
+  e2e       the same product through the C ABI from pinned host buffers:
+            H2D of A and B, the product, D2H of C inside every timed step.
+  roofline  the tensor-core main kernel alone on pre-split operands, timed
+            with CUDA events on its stream: pipe FLOPs (3 tf32 MMAs per
+            product term) per launch / mean launch time, against the tf32
+            tensor peak = measured dense bf16 / 2.
+  extra     the other configurations (f64 GEMM, batched GEMM, fused chain
+            forward / adjoint, vmap covariance, MLP step) at one GPU.
+  --gpus N  (torchrun) every rank multiplies its own 8192^3 pair: replicas,
+            weak scaling; there is no collective on this path.
+
+`--impl reference` times the reference C lane's algorithm (the oracle port:
+canonical tree over k, -O2 -ffp-contract=off, OpenMP on every host core) on
+a bounded sample of output rows of the same product.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_HEADLINE = 8192
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return dict(hbm=float(p["hbm_gbs"]), bf16=float(p["bf16_tflops"]),
+                    bf16_sustained=float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                    source="measured")
+    except Exception:
+        return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+def load_traffic(name):
+    try:
+        with open(TRAFFIC_PATH) as f:
+            return json.load(f).get(name)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- helpers
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_region(fn, steps, world):
+    """CUDA-event time of `steps` calls of fn on the current stream (ms),
+    bracketed by barrier + synchronize; max over ranks."""
+    import torch
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(stop), world)
+
+
+# ---------------------------------------------------------------- workloads
+
+def bench_gemm_headline(args, world, rank, peaks):
+    import torch
+    from chelis_b200 import lib as L
+    from chelis_b200 import ops, workloads as W
+    n = args.n
+    a, b = W.torch_gemm_inputs(n, n, n, torch.float32, seed=1 + rank)
+    c = torch.empty((n, n), dtype=torch.float32, device="cuda")
+    flops = 2.0 * n ** 3
+
+    def step():
+        ops.matmul(a, b, out=c)
+
+    for _ in range(args.warmup):
+        step()
+    ops.device_status()
+    l0 = ops.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = time_region(step, args.steps, world)
+    launches = ops.launch_count() - l0
+    ops.device_status()
+    value = world * flops * args.steps / (ms * 1e-3) / 1e12
+
+    # roofline: the tcgen05 main kernel alone on pre-split operands
+    kp = (n + 31) // 32 * 32
+    ahi = torch.empty((n, kp), dtype=torch.float32, device="cuda")
+    alo, bhi, blo = torch.empty_like(ahi), torch.empty_like(ahi), torch.empty_like(ahi)
+    L.call("chelis_cuda_tf32x3_split", 0, n, n, a.data_ptr(), n, 0, 1, ahi.data_ptr(), alo.data_ptr())
+    L.call("chelis_cuda_tf32x3_split", 1, n, n, b.data_ptr(), n, 0, 1, bhi.data_ptr(), blo.data_ptr())
+
+    def main_only():
+        L.call("chelis_cuda_sgemm_tf32x3_presplit", n, n, n, 1, ahi.data_ptr(), alo.data_ptr(),
+               bhi.data_ptr(), blo.data_ptr(), c.data_ptr(), n, 0)
+
+    for _ in range(3):
+        main_only()
+    kms = time_region(main_only, args.steps, 1) / args.steps
+    pipe = 3.0 * flops / (kms * 1e-3) / 1e12
+    tf32_peak = peaks["bf16"] / 2.0
+    del ahi, alo, bhi, blo
+
+    # e2e: pinned host buffers through the C ABI every step
+    ha = a.cpu().pin_memory()
+    hb = b.cpu().pin_memory()
+    hc = torch.empty((n, n), dtype=torch.float32).pin_memory()
+    da, db = torch.empty_like(a), torch.empty_like(b)
+
+    def e2e_step():
+        da.copy_(ha, non_blocking=True)
+        db.copy_(hb, non_blocking=True)
+        ops.matmul(da, db, out=c)
+        hc.copy_(c, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    ems = time_region(e2e_step, max(2, args.steps // 2), world)
+    e2e_value = world * flops * max(2, args.steps // 2) / (ems * 1e-3) / 1e12
+    return dict(
+        value=value, ms_per_step=ms / args.steps, launches=launches, clocks=clk.summary(),
+        roofline={"bound": "tensor", "achieved": round(pipe, 2), "peak": tf32_peak,
+                  "unit": "TFLOP/s", "frac": round(pipe / tf32_peak, 4),
+                  "traffic": load_traffic("gemm_tf32x3_8192"),
+                  "kernel": "tf32x3::gemm_kernel (tcgen05.mma kind::tf32, 3 MMAs per product term)",
+                  "kernel_ms": round(kms, 4),
+                  "peak_source": f"{peaks['source']} dense bf16 / 2 (tf32 issues at half the f16 rate)"},
+        e2e={"value": round(e2e_value, 2), "unit": "TFLOP/s",
+             "h2d_bytes_per_step": 2 * n * n * 4, "d2h_bytes_per_step": n * n * 4},
+    )
+
+
+def bench_extras(args, peaks):
+    """The other configurations, one GPU, short timed loops (CUDA events)."""
+    import torch
+    from chelis_b200 import ops, workloads as W
+    out = {}
+    hbm = peaks["hbm"]
+
+    def timed(fn, steps, warm=3):
+        for _ in range(warm):
+            fn()
+        return time_region(fn, steps, 1) / steps
+
+    # f64 GEMM 8192^3 on DMMA
+    n = 8192
+    a, b = W.torch_gemm_inputs(n, n, n, torch.float64, seed=1)
+    c = torch.empty((n, n), dtype=torch.float64, device="cuda")
+    ms = timed(lambda: ops.matmul(a, b, out=c), 3, 1)
+    out["gemm_f64_8192"] = {"tflops": round(2 * n ** 3 / ms / 1e9, 2), "ms": round(ms, 3)}
+    del a, b, c
+    # f32 GEMM sweep (smaller sizes)
+    sweep = {}
+    for n in (512, 1024, 2048, 4096):
+        a, b = W.torch_gemm_inputs(n, n, n, torch.float32, seed=1)
+        c = torch.empty((n, n), dtype=torch.float32, device="cuda")
+        ms = timed(lambda: ops.matmul(a, b, out=c), 10)
+        sweep[str(n)] = round(2 * n ** 3 / ms / 1e9, 2)
+    out["gemm_f32_sweep_tflops"] = sweep
+    # batched 256 x 512^3 f32
+    a, b = W.torch_gemm_inputs(512, 512, 512, torch.float32, seed=1, batch=256)
+    c = torch.empty((256, 512, 512), dtype=torch.float32, device="cuda")
+    ms = timed(lambda: ops.matmul(a, b, out=c), 10)
+    out["gemm_f32_batched_256x512"] = {"tflops": round(256 * 2 * 512 ** 3 / ms / 1e9, 2),
+                                       "ms": round(ms, 3)}
+    del a, b, c
+    # fused chain fwd / adjoint
+    x, g, be = W.torch_chain_inputs()
+    rows, hidden = x.shape
+    state = {}
+
+    def fwd():
+        state["rs"], state["st"] = ops.chain_fwd(x, g, be, 1e-5, 42, 0.1, want_stats=True)
+
+    fms = timed(fwd, 10)
+    bms = timed(lambda: ops.chain_bwd(x, g, be, 1e-5, 42, 0.1, 0, state["st"]), 10)
+    fbytes = rows * hidden * 4 + 2 * hidden * 4 + rows * 4 + rows * 16
+    bbytes = 2 * rows * hidden * 4 + 4 * hidden * 4 + rows * 16
+    out["chain_fwd"] = {"gbs": round(fbytes / fms / 1e6, 1), "ms": round(fms, 4),
+                        "frac_hbm": round(fbytes / fms / 1e6 / hbm, 3)}
+    out["chain_bwd"] = {"gbs": round(bbytes / bms / 1e6, 1), "ms": round(bms, 4),
+                        "frac_hbm": round(bbytes / bms / 1e6 / hbm, 3)}
+    del x, g, be, state
+    # vmap covariance / risk
+    r, w = W.torch_portfolio_inputs()
+    ms = timed(lambda: ops.portfolio(r, w), 3, 1)
+    cnt = r.shape[0]
+    pbytes = r.numel() * 8 + w.numel() * 8 + cnt * (64 * 64 + 1 + 252) * 8
+    out["portfolio"] = {"portfolios_per_s": round(cnt / ms * 1e3, 1), "ms": round(ms, 3),
+                        "gbs": round(pbytes / ms / 1e6, 1),
+                        "fp64_tflops": round(cnt * 2.10e6 / ms / 1e9, 2)}
+    del r, w
+    # MLP step
+    x, labels, w1, b1, w2, b2 = W.torch_mlp_inputs()
+    ms = timed(lambda: ops.mlp_step(x, labels, w1, b1, w2, b2), 20)
+    out["mlp_step"] = {"us_per_step": round(ms * 1e3, 1)}
+    return out
+
+
+# ---------------------------------------------------------------- reference arm
+
+def cpu_gemm_sample(n, budget_s, seed=1):
+    """Oracle (reference C lane algorithm) on a bounded sample of output rows
+    of the n^3 f32 product; returns (TFLOP/s, rows, seconds, threads)."""
+    import numpy as np
+    from chelis_b200 import workloads as W
+    from oracle import oracle as O
+    a, b = W.gemm_inputs(n, n, n, np.float32, seed=seed)
+    O.lib()
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    t0 = time.perf_counter()
+    O.gemm(a[:threads], b)
+    dt = time.perf_counter() - t0
+    per_row = dt / threads
+    rows = int(max(threads, min(n, budget_s / max(per_row, 1e-9))))
+    rows = (rows // threads) * threads or threads
+    t0 = time.perf_counter()
+    O.gemm(a[:rows], b)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * n * n / dt / 1e12, rows, dt, threads
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    n = args.n
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, rows, dt, threads = cpu_gemm_sample(n, args.ref_budget / max(1, args.steps))
+        if i >= args.warmup:
+            vals.append((v, rows, dt))
+    value = statistics.median(v for v, _, _ in vals)
+    rows = vals[-1][1]
+    line = {
+        "impl": "reference", "metric": "gemm_f32_tflops", "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.median(dt for _, _, dt in vals) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic U(-1,1) seed 1",
+        "config": {"workload": f"gemm_f32 row-major {n}x{n}x{n} (config 2)",
+                   "sample": f"{rows} of {n} output rows per step"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows x {n} cols of C, k = {n}, canonical tree over k"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="chelis", choices=["chelis", "reference"])
+    ap.add_argument("--n", type=int, default=N_HEADLINE)
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ref-budget", type=float, default=60.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    world, rank, local = dist_setup(args)
+    peaks = load_peaks()
+    res = bench_gemm_headline(args, world, rank, peaks)
+    extras = None
+    if world == 1 and not args.no_extras:
+        extras = bench_extras(args, peaks)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+        v, rows, dt, threads = cpu_gemm_sample(args.n, 15.0)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{rows} of {args.n} output rows of the {args.n}^3 f32 product "
+                         f"({dt:.1f} s), oracle restatement of the C lane"}
+    if rank == 0:
+        line = {
+            "metric": "gemm_f32_tflops", "value": round(res["value"], 2), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(res["ms_per_step"], 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic U(-1,1) seed 1 (per-rank seed offset)",
+            "config": {"workload": f"gemm_f32 row-major {args.n}x{args.n}x{args.n} (config 2, 3xTF32)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs 512 MiB > L2, no flush"},
+            "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
+            "gpu_launches": res["launches"], "clocks": res["clocks"],
+        }
+        if extras is not None:
+            line["extra"] = extras
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

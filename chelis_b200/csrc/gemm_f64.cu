@@ -1,0 +1,218 @@
+// gemm_f64.cu -- f64 GEMM on the FP64 tensor path (DMMA, mma.sync m16n8k4
+// .f64) for the matmul lowering with an f64 accumulator
+// (spec/05-risc-primitives.md:4962-5000).  Replaces
+// chelis_hipblas_dgemm_*_row_major (chelis_hip_runtime.h:271-404).
+//
+// CTA tile 128 x 128, k-slab 16, 256 threads = 8 warps in a 2 x 4 grid,
+// warp tile 64 x 32 = 4 x 4 m16n8 accumulators (64 doubles per thread).
+// Tiles are staged global -> registers -> shared memory with one slab of
+// register prefetch (double-buffered shared memory), so any layout, leading
+// dimension and ragged edge is handled by the same code path.  Shared
+// memory rows are XOR-swizzled at 16-byte granularity so that the DMMA
+// fragment reads of a half-warp hit 16 distinct bank pairs.
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "common.cuh"
+
+namespace chelis {
+
+extern std::atomic<uint64_t> g_launches;
+int gemm_mode();
+template <typename T>
+int launch_exact_gemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const T *a,
+                      int64_t lda, int64_t stride_a, const T *b, int64_t ldb, int64_t stride_b,
+                      T *c, int64_t ldc, int64_t stride_c, int64_t batch, cudaStream_t s);
+int validate_gemm_args(int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                       int64_t batch, int trans_a, int trans_b);
+
+namespace dmma {
+
+constexpr int BM = 128, BN = 128, BK = 16, THREADS = 256;
+constexpr int LOADS = BM * BK / THREADS;  // 8 doubles per thread per operand
+constexpr int SMEM_BYTES = 2 * (BM * BK + BK * BN) * 8;  // 64 KiB, double-buffered
+
+// element offsets inside the swizzled tiles
+__device__ __forceinline__ int a_off(int r, int k) { return r * BK + (k ^ ((r & 3) << 2)); }
+__device__ __forceinline__ int b_off(int k, int n) { return k * BN + (n ^ ((k & 3) << 2)); }
+
+__device__ __forceinline__ void dmma_16x8x4(double (&d)[4], double a0, double a1, double b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+        "{%0,%1,%2,%3};"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a0), "d"(a1), "d"(b0));
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    dgemm_kernel(int64_t m, int64_t n, int64_t k, const double *__restrict__ a, int64_t sa_r,
+                 int64_t sa_k, int64_t sa_b, const double *__restrict__ b, int64_t sb_k,
+                 int64_t sb_n, int64_t sb_b, double *__restrict__ c, int64_t ldc,
+                 int64_t sc_b) {
+    extern __shared__ __align__(16) double dsmem[];
+    double (*As)[BM * BK] = reinterpret_cast<double (*)[BM * BK]>(dsmem);
+    double (*Bs)[BK * BN] = reinterpret_cast<double (*)[BK * BN]>(dsmem + 2 * BM * BK);
+
+    const int64_t bz = blockIdx.z;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+    a += bz * sa_b;
+    b += bz * sb_b;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int wm = warp >> 2;  // 0..1 -> 64-row half
+    const int wn = warp & 3;   // 0..3 -> 32-col quarter
+    const int g = lane >> 2, t = lane & 3;
+    const bool a_kfast = (sa_k == 1);
+    const bool b_nfast = (sb_n == 1);
+
+    double ra[LOADS], rb[LOADS];
+    auto load_slab = [&](int64_t k0) {
+#pragma unroll
+        for (int j = 0; j < LOADS; ++j) {
+            const int e = tid + j * THREADS;
+            int r, kk;
+            if (a_kfast) { r = e / BK; kk = e % BK; } else { kk = e / BM; r = e % BM; }
+            const int64_t gr = m0 + r, gk = k0 + kk;
+            ra[j] = (gr < m && gk < k) ? a[gr * sa_r + gk * sa_k] : 0.0;
+        }
+#pragma unroll
+        for (int j = 0; j < LOADS; ++j) {
+            const int e = tid + j * THREADS;
+            int kk, nn;
+            if (b_nfast) { kk = e / BN; nn = e % BN; } else { nn = e / BK; kk = e % BK; }
+            const int64_t gk = k0 + kk, gn = n0 + nn;
+            rb[j] = (gk < k && gn < n) ? b[gk * sb_k + gn * sb_n] : 0.0;
+        }
+    };
+    auto store_slab = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < LOADS; ++j) {
+            const int e = tid + j * THREADS;
+            int r, kk;
+            if (a_kfast) { r = e / BK; kk = e % BK; } else { kk = e / BM; r = e % BM; }
+            As[buf][a_off(r, kk)] = ra[j];
+        }
+#pragma unroll
+        for (int j = 0; j < LOADS; ++j) {
+            const int e = tid + j * THREADS;
+            int kk, nn;
+            if (b_nfast) { kk = e / BN; nn = e % BN; } else { nn = e / BK; kk = e % BK; }
+            Bs[buf][b_off(kk, nn)] = rb[j];
+        }
+    };
+
+    double acc[4][4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.0;
+
+    const int64_t nslab = (k + BK - 1) / BK;
+    load_slab(0);
+    store_slab(0);
+    __syncthreads();
+    for (int64_t s = 0; s < nslab; ++s) {
+        const int buf = static_cast<int>(s & 1);
+        if (s + 1 < nslab) load_slab((s + 1) * BK);
+        const double *Ab = As[buf];
+        const double *Bb = Bs[buf];
+#pragma unroll
+        for (int kk = 0; kk < BK; kk += 4) {
+            double af[4][2], bf[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = wm * 64 + i * 16 + g;
+                af[i][0] = Ab[a_off(r, kk + t)];
+                af[i][1] = Ab[a_off(r + 8, kk + t)];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bf[j] = Bb[b_off(kk + t, wn * 32 + j * 8 + g)];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_16x8x4(acc[i][j], af[i][0], af[i][1], bf[j]);
+        }
+        if (s + 1 < nslab) {
+            store_slab(buf ^ 1);
+        }
+        __syncthreads();
+    }
+
+    double *cb = c + bz * sc_b;
+    const bool vec = ((ldc & 1) == 0) && ((reinterpret_cast<uintptr_t>(cb) & 15) == 0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t col = n0 + wn * 32 + j * 8 + 2 * t;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int64_t row = m0 + wm * 64 + i * 16 + g + h * 8;
+                if (row >= m) continue;
+                double *dst = cb + row * ldc + col;
+                const double v0 = acc[i][j][2 * h], v1 = acc[i][j][2 * h + 1];
+                if (vec && col + 1 < n) {
+                    *reinterpret_cast<double2 *>(dst) = make_double2(v0, v1);
+                } else {
+                    if (col < n) dst[0] = v0;
+                    if (col + 1 < n) dst[1] = v1;
+                }
+            }
+        }
+    }
+}
+
+}  // namespace dmma
+
+int launch_dgemm_dmma(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
+                      int64_t lda, int64_t stride_a, const double *b, int64_t ldb,
+                      int64_t stride_b, double *c, int64_t ldc, int64_t stride_c, int64_t batch,
+                      cudaStream_t s) {
+    const int64_t sa_r = trans_a ? 1 : lda, sa_k = trans_a ? lda : 1;
+    const int64_t sb_k = trans_b ? 1 : ldb, sb_n = trans_b ? ldb : 1;
+    dim3 grid(static_cast<unsigned>((n + dmma::BN - 1) / dmma::BN),
+              static_cast<unsigned>((m + dmma::BM - 1) / dmma::BM),
+              static_cast<unsigned>(batch));
+    static bool attr_set = false;
+    if (!attr_set) {
+        CHELIS_TRY(check_cuda(cudaFuncSetAttribute(dmma::dgemm_kernel,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   dmma::SMEM_BYTES),
+                              "cudaFuncSetAttribute(dgemm_kernel)"));
+        attr_set = true;
+    }
+    dmma::dgemm_kernel<<<grid, dmma::THREADS, dmma::SMEM_BYTES, s>>>(m, n, k, a, sa_r, sa_k, stride_a, b, sb_k,
+                                                       sb_n, stride_b, c, ldc, stride_c);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("dgemm_kernel(dmma)");
+    return CHELIS_CUDA_OK;
+}
+
+}  // namespace chelis
+
+using namespace chelis;
+
+extern "C" int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                                 const double *a, int64_t lda, int64_t stride_a, const double *b,
+                                 int64_t ldb, int64_t stride_b, double *c, int64_t ldc,
+                                 int64_t stride_c, int64_t batch) {
+    CHELIS_TRY(validate_gemm_args(m, n, k, lda, ldb, ldc, batch, trans_a, trans_b));
+    if (m == 0 || n == 0 || batch == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    if (k == 0) {
+        for (int64_t bb = 0; bb < batch; ++bb)
+            CHELIS_TRY(check_cuda(cudaMemset2DAsync(c + bb * stride_c, ldc * sizeof(double), 0,
+                                                    n * sizeof(double), m, s),
+                                  "cudaMemset2DAsync"));
+        return CHELIS_CUDA_OK;
+    }
+    if (gemm_mode() == CHELIS_CUDA_GEMM_EXACT_TREE)
+        return launch_exact_gemm<double>(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb,
+                                         stride_b, c, ldc, stride_c, batch, s);
+    return launch_dgemm_dmma(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb, stride_b, c,
+                             ldc, stride_c, batch, s);
+}

@@ -1,0 +1,622 @@
+// gemm_tf32x3.cu -- f32 GEMM on the sm_100a tensor cores with 3xTF32
+// split-accumulate, plus the bit-exact CUDA-core "canonical tree" GEMM.
+//
+// Replaces chelis_hipblas_sgemm_*_row_major
+// (crates/chelis-backend-hip/runtime/chelis_hip_runtime.h:48-267).
+//
+// 3xTF32: each f32 operand x is split into hi = RN_tf32(x) and
+// lo = RN_tf32(x - hi) (x - hi is exact in f32).  The product a.b is then
+// accumulated as a_lo.b_hi + a_hi.b_lo + a_hi.b_hi in the f32 accumulator
+// of tcgen05.mma kind::tf32; the dropped a_lo.b_lo term is below 2^-22
+// relative.  The split runs as a pre-pass that also lays both operands out
+// K-major ([rows][Kp], Kp = K rounded up to 32, zero padded), so the main
+// kernel streams four K-major tiles per stage with TMA (128-byte swizzle).
+//
+// Main kernel (one 128 x 256 output tile per CTA, 192 threads):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5   epilogue: tcgen05.ld of the 128 x 256 f32 accumulator
+//               (TMEM lanes = rows, 256 columns) and stores to C
+// Every mbarrier wait is bounded (common.cuh) so a fault in the pipeline
+// reports CHELIS_CUDA_ERR_TIMEOUT instead of hanging the GPU.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace chelis {
+
+extern std::atomic<uint64_t> g_launches;
+int gemm_mode();
+
+namespace tf32x3 {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 32;  // 32 f32 = 128 bytes = one swizzle row
+constexpr int STAGES = 2;
+constexpr int A_TILE_BYTES = BM * BK * 4;  // 16 KiB
+constexpr int B_TILE_BYTES = BN * BK * 4;  // 32 KiB
+constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;
+
+struct Params {
+    int64_t m, n;
+    int32_t num_kb;       // Kp / BK
+    int64_t a_rows_per_batch, b_rows_per_batch;  // rows of the split buffers per batch item
+    float *c;
+    int64_t ldc, stride_c;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_ahi,
+                const __grid_constant__ CUtensorMap map_alo,
+                const __grid_constant__ CUtensorMap map_bhi,
+                const __grid_constant__ CUtensorMap map_blo, Params p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte alignment for the swizzle atoms
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *accum_full = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+    volatile uint32_t *abort_flag = tmem_slot + 1;
+    volatile int32_t *consumed = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
+    int32_t issued = 0;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+    const int64_t batch = blockIdx.z;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum_full, 1);
+        *abort_flag = 0;
+        *consumed = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&map_ahi);
+        prefetch_tensormap(&map_alo);
+        prefetch_tensormap(&map_bhi);
+        prefetch_tensormap(&map_blo);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const int32_t ya = static_cast<int32_t>(batch * p.a_rows_per_batch + m0);
+            const int32_t yb = static_cast<int32_t>(batch * p.b_rows_per_batch + n0);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t phase = (kb / STAGES) & 1;
+                if (!mbar_wait_bounded(&empty[s], phase ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                unsigned char *st = smem + s * STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                const int32_t x = kb * BK;
+                tma_load_2d(st, &map_ahi, &full[s], x, ya);
+                tma_load_2d(st + A_TILE_BYTES, &map_alo, &full[s], x, ya);
+                tma_load_2d(st + 2 * A_TILE_BYTES, &map_bhi, &full[s], x, yb);
+                tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &map_blo, &full[s], x, yb);
+                issued = kb + 1;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(BM, BN);
+            bool ok = true;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t phase = (kb / STAGES) & 1;
+                if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
+                    ok = false;
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + s * STAGE_BYTES);
+                const uint32_t ahi = st, alo = st + A_TILE_BYTES;
+                const uint32_t bhi = st + 2 * A_TILE_BYTES;
+                const uint32_t blo = bhi + B_TILE_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+                    const uint32_t acc = (kb | kk) ? 1u : 0u;
+                    mma_tf32_ss(tmem_base, sw128_kmajor_desc(alo + off),
+                                sw128_kmajor_desc(bhi + off), idesc, acc);
+                    mma_tf32_ss(tmem_base, sw128_kmajor_desc(ahi + off),
+                                sw128_kmajor_desc(blo + off), idesc, 1u);
+                    mma_tf32_ss(tmem_base, sw128_kmajor_desc(ahi + off),
+                                sw128_kmajor_desc(bhi + off), idesc, 1u);
+                }
+                mma_commit(&empty[s]);
+                *consumed = kb + 1;
+            }
+            // Signal the epilogue either way; on abort it skips the stores.
+            (void)ok;
+            mma_commit(accum_full);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const bool ok = mbar_wait_bounded(accum_full, 0, DEVERR_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        if (ok && !*abort_flag) {
+            const int64_t row = m0 + quad * 32 + lane;
+            float *crow = p.c + batch * p.stride_c + row * p.ldc;
+            const bool row_ok = row < p.m;
+            const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
+                                ((p.stride_c & 3) == 0);
+#pragma unroll 1
+            for (int cb = 0; cb < BN / 32; ++cb) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + cb * 32, r);
+                tmem_wait_ld();
+                const int64_t col0 = n0 + cb * 32;
+                if (row_ok) {
+                    if (vec_ok && col0 + 32 <= p.n) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                   __uint_as_float(r[j + 2]),
+                                                   __uint_as_float(r[j + 3]));
+                            *reinterpret_cast<float4 *>(crow + col0 + j) = v;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n) crow[col0 + j] = __uint_as_float(r[j]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    // On an aborted pipeline, let TMA copies that were issued but never
+    // consumed land before the CTA exits (bounded as well).
+    if (warp == 0 && lane == 0 && *abort_flag) {
+        for (int kb = *consumed; kb < issued; ++kb)
+            mbar_wait_bounded(&full[kb % STAGES], (kb / STAGES) & 1, DEVERR_TIMEOUT_PRODUCER);
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// split pre-pass: src element (r, k) at src[b*sb + r*sr + k*sk] ->
+// hi/lo[b][r][k] (K-major, row stride kp), zero for k >= K.
+// A 32 x 32 tile goes through shared memory so that both the read (along the
+// unit-stride axis of the source) and the write (along k) are coalesced.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float rna_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+__global__ void split_kernel(const float *__restrict__ src, int64_t rows, int64_t k,
+                             int64_t sr, int64_t sk, int64_t sb, int64_t kp,
+                             float *__restrict__ hi, float *__restrict__ lo) {
+    __shared__ float tile[32][33];
+    const int64_t b = blockIdx.z;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const float *s = src + b * sb;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    if (sk == 1) {
+        // rows contiguous along k: read row-wise
+        for (int i = ty; i < 32; i += 8) {
+            int64_t r = r0 + i, kk = k0 + tx;
+            tile[i][tx] = (r < rows && kk < k) ? s[r * sr + kk] : 0.0f;
+        }
+    } else {
+        // contiguous along rows (a transposed operand): read column-wise
+        for (int i = ty; i < 32; i += 8) {
+            int64_t r = r0 + tx, kk = k0 + i;
+            tile[tx][i] = (r < rows && kk < k) ? s[r * sr + kk * sk] : 0.0f;
+        }
+    }
+    __syncthreads();
+    float *h = hi + b * rows * kp;
+    float *l = lo + b * rows * kp;
+    for (int i = ty; i < 32; i += 8) {
+        int64_t r = r0 + i, kk = k0 + tx;
+        if (r < rows && kk < kp) {
+            float x = tile[i][tx];
+            float xh = rna_tf32(x);
+            float xl = isfinite(x) ? rna_tf32(__fsub_rn(x, xh)) : 0.0f;
+            h[r * kp + kk] = xh;
+            l[r * kp + kk] = xl;
+        }
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+int make_kmajor_map(CUtensorMap *map, const float *base, int64_t rows, int64_t kp, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(kp), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kp) * 4};
+    cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CHELIS_CUDA_OK;
+}
+
+}  // namespace tf32x3
+
+// ---------------------------------------------------------------------------
+// exact canonical-tree GEMM on CUDA cores (bit-identical to the C lane's
+// inlined product sum, crates/chelis-backend-c/src/emit.rs:8431-8640).
+// Each thread owns 1 row x 4 columns.  Leaves fl(a*b) enter, in increasing
+// k, a carry tree: an aligned block of 32 leaves is a complete subtree and
+// is reduced with a static schedule; block sums (and a final partial block)
+// enter an outer carry tree whose levels live in registers.
+// ---------------------------------------------------------------------------
+namespace exact {
+
+constexpr int TM = 32, TN = 32, TK = 32, THREADS = 256;
+constexpr int MAXD = 14;  // outer levels: up to 2^14 blocks of 32 (k <= 524288)
+
+template <typename T>
+struct Carry {
+    T level[MAXD];
+};
+
+template <typename T>
+__device__ __forceinline__ T add_rn(T a, T b);
+template <>
+__device__ __forceinline__ float add_rn<float>(float a, float b) { return __fadd_rn(a, b); }
+template <>
+__device__ __forceinline__ double add_rn<double>(double a, double b) { return __dadd_rn(a, b); }
+template <typename T>
+__device__ __forceinline__ T mul_rn(T a, T b);
+template <>
+__device__ __forceinline__ float mul_rn<float>(float a, float b) { return __fmul_rn(a, b); }
+template <>
+__device__ __forceinline__ double mul_rn<double>(double a, double b) { return __dmul_rn(a, b); }
+
+// push `carry` as leaf number `count` of the outer tree
+template <typename T>
+__device__ __forceinline__ void push(Carry<T> &t, uint32_t count, T carry) {
+    bool active = true;
+#pragma unroll
+    for (int d = 0; d < MAXD; ++d) {
+        const bool bit = (count >> d) & 1u;
+        if (active) {
+            if (bit) {
+                carry = add_rn(t.level[d], carry);
+            } else {
+                t.level[d] = carry;
+                active = false;
+            }
+        }
+    }
+}
+template <typename T>
+__device__ __forceinline__ T total(const Carry<T> &t, uint32_t count) {
+    T tot = T(0);
+    bool found = false;
+#pragma unroll
+    for (int d = 0; d < MAXD; ++d) {
+        if ((count >> d) & 1u) {
+            tot = found ? add_rn(t.level[d], tot) : t.level[d];
+            found = true;
+        }
+    }
+    return tot;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS)
+    gemm_exact_kernel(int64_t m, int64_t n, int64_t k, const T *__restrict__ a, int64_t sa_r,
+                      int64_t sa_k, int64_t sa_b, const T *__restrict__ b, int64_t sb_k,
+                      int64_t sb_c, int64_t sb_b, T *__restrict__ c, int64_t ldc,
+                      int64_t sc_b) {
+    __shared__ T as[TM][TK + 1];
+    __shared__ T bs[TK][TN + 1];
+    const int64_t bb = blockIdx.z;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * TM;
+    const int64_t c0 = static_cast<int64_t>(blockIdx.x) * TN;
+    const int tr = threadIdx.x / 8;       // 0..31 row in tile
+    const int tc = (threadIdx.x % 8) * 4;  // 0..28 first of 4 columns
+    a += bb * sa_b;
+    b += bb * sb_b;
+    Carry<T> tree[4];
+    uint32_t blocks = 0;
+    for (int64_t k0 = 0; k0 < k; k0 += TK) {
+        for (int i = threadIdx.x; i < TM * TK; i += THREADS) {
+            int rr = i / TK, kk = i % TK;
+            int64_t gr = r0 + rr, gk = k0 + kk;
+            as[rr][kk] = (gr < m && gk < k) ? a[gr * sa_r + gk * sa_k] : T(0);
+        }
+        for (int i = threadIdx.x; i < TK * TN; i += THREADS) {
+            int kk = i / TN, cc = i % TN;
+            int64_t gk = k0 + kk, gc = c0 + cc;
+            bs[kk][cc] = (gc < n && gk < k) ? b[gk * sb_k + gc * sb_c] : T(0);
+        }
+        __syncthreads();
+        const int64_t valid = (k - k0) < TK ? (k - k0) : TK;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            // streaming carry tree over the `valid` leaves of this block; a
+            // full block (valid == 32) reduces to the perfect 32-leaf subtree
+            T lv[6];
+            uint32_t cnt = 0;
+            for (int kk = 0; kk < valid; ++kk) {
+                T carry = mul_rn(as[tr][kk], bs[kk][tc + j]);
+                bool active = true;
+#pragma unroll
+                for (int d = 0; d < 6; ++d) {
+                    const bool bit = (cnt >> d) & 1u;
+                    if (active) {
+                        if (bit) {
+                            carry = add_rn(lv[d], carry);
+                        } else {
+                            lv[d] = carry;
+                            active = false;
+                        }
+                    }
+                }
+                ++cnt;
+            }
+            T bsum = T(0);
+            bool found = false;
+#pragma unroll
+            for (int d = 0; d < 6; ++d) {
+                if ((cnt >> d) & 1u) {
+                    bsum = found ? add_rn(lv[d], bsum) : lv[d];
+                    found = true;
+                }
+            }
+            push(tree[j], blocks, bsum);
+        }
+        ++blocks;
+        __syncthreads();
+    }
+    const int64_t gr = r0 + tr;
+    if (gr < m) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t gc = c0 + tc + j;
+            if (gc < n) c[bb * sc_b + gr * ldc + gc] = k > 0 ? total(tree[j], blocks) : T(0);
+        }
+    }
+}
+
+}  // namespace exact
+
+template <typename T>
+int launch_exact_gemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const T *a,
+                      int64_t lda, int64_t stride_a, const T *b, int64_t ldb, int64_t stride_b,
+                      T *c, int64_t ldc, int64_t stride_c, int64_t batch, cudaStream_t s) {
+    int64_t sa_r = trans_a ? 1 : lda, sa_k = trans_a ? lda : 1;
+    int64_t sb_k = trans_b ? 1 : ldb, sb_c = trans_b ? ldb : 1;
+    dim3 grid(static_cast<unsigned>((n + exact::TN - 1) / exact::TN),
+              static_cast<unsigned>((m + exact::TM - 1) / exact::TM),
+              static_cast<unsigned>(batch));
+    exact::gemm_exact_kernel<T><<<grid, exact::THREADS, 0, s>>>(
+        m, n, k, a, sa_r, sa_k, stride_a, b, sb_k, sb_c, stride_b, c, ldc, stride_c);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("gemm_exact_kernel");
+    return CHELIS_CUDA_OK;
+}
+template int launch_exact_gemm<float>(int, int, int64_t, int64_t, int64_t, const float *, int64_t,
+                                      int64_t, const float *, int64_t, int64_t, float *, int64_t,
+                                      int64_t, int64_t, cudaStream_t);
+template int launch_exact_gemm<double>(int, int, int64_t, int64_t, int64_t, const double *,
+                                       int64_t, int64_t, const double *, int64_t, int64_t,
+                                       double *, int64_t, int64_t, int64_t, cudaStream_t);
+
+// Split both operands into caller-provided scratch and run the tcgen05
+// kernel.  `scratch` must hold 2 * (m + n) * kp floats per batch item.
+int sgemm_3xtf32_with_scratch(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                              const float *a, int64_t lda, int64_t stride_a, const float *b,
+                              int64_t ldb, int64_t stride_b, float *c, int64_t ldc,
+                              int64_t stride_c, int64_t batch, float *scratch, cudaStream_t s) {
+    using namespace tf32x3;
+    const int64_t kp = (k + BK - 1) / BK * BK;
+    float *ahi = scratch;
+    float *alo = ahi + batch * m * kp;
+    float *bhi = alo + batch * m * kp;
+    float *blo = bhi + batch * n * kp;
+    // op(A)[i, kk] = a[i*lda + kk] (no trans) or a[kk*lda + i] (trans)
+    {
+        int64_t sr = trans_a ? 1 : lda, sk = trans_a ? lda : 1;
+        dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((m + 31) / 32),
+                  static_cast<unsigned>(batch));
+        split_kernel<<<grid, dim3(32, 8), 0, s>>>(a, m, k, sr, sk, stride_a, kp, ahi, alo);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("split_kernel(A)");
+    }
+    // op(B)[kk, j] -> K-major rows j: element (j, kk) = b[kk*ldb + j] (no
+    // trans) or b[j*ldb + kk] (trans)
+    {
+        int64_t sr = trans_b ? ldb : 1, sk = trans_b ? 1 : ldb;
+        dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((n + 31) / 32),
+                  static_cast<unsigned>(batch));
+        split_kernel<<<grid, dim3(32, 8), 0, s>>>(b, n, k, sr, sk, stride_b, kp, bhi, blo);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("split_kernel(B)");
+    }
+    CUtensorMap mahi, malo, mbhi, mblo;
+    CHELIS_TRY(make_kmajor_map(&mahi, ahi, batch * m, kp, BM));
+    CHELIS_TRY(make_kmajor_map(&malo, alo, batch * m, kp, BM));
+    CHELIS_TRY(make_kmajor_map(&mbhi, bhi, batch * n, kp, BN));
+    CHELIS_TRY(make_kmajor_map(&mblo, blo, batch * n, kp, BN));
+    static bool attr_set = false;
+    if (!attr_set) {
+        CHELIS_TRY(check_cuda(cudaFuncSetAttribute(gemm_kernel,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   SMEM_BYTES),
+                              "cudaFuncSetAttribute(gemm_kernel)"));
+        attr_set = true;
+    }
+    Params p;
+    p.m = m;
+    p.n = n;
+    p.num_kb = static_cast<int32_t>(kp / BK);
+    p.a_rows_per_batch = m;
+    p.b_rows_per_batch = n;
+    p.c = c;
+    p.ldc = ldc;
+    p.stride_c = stride_c;
+    dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>((m + BM - 1) / BM),
+              static_cast<unsigned>(batch));
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mahi, malo, mbhi, mblo, p);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("gemm_kernel(3xtf32)");
+    return CHELIS_CUDA_OK;
+}
+
+size_t sgemm_3xtf32_scratch_bytes(int64_t m, int64_t n, int64_t k, int64_t batch) {
+    const int64_t kp = (k + tf32x3::BK - 1) / tf32x3::BK * tf32x3::BK;
+    return static_cast<size_t>(2 * (m + n) * kp * batch) * sizeof(float);
+}
+
+int validate_gemm_args(int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                       int64_t batch, int trans_a, int trans_b) {
+    if (m < 0 || n < 0 || k < 0 || batch < 0)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
+    if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "matmul extent beyond 2^30");
+    const int64_t a_cols = trans_a ? m : k, b_cols = trans_b ? k : n;
+    if ((a_cols > 0 && lda < a_cols) || (b_cols > 0 && ldb < b_cols) || (n > 0 && ldc < n))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
+    return CHELIS_CUDA_OK;
+}
+
+}  // namespace chelis
+
+using namespace chelis;
+
+extern "C" int chelis_cuda_tf32x3_split(int trans, int64_t rows, int64_t k, const float *src,
+                                        int64_t ld, int64_t stride, int64_t batch, float *hi,
+                                        float *lo) {
+    if (rows < 0 || k < 0 || batch < 0)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
+    if (rows == 0 || batch == 0) return CHELIS_CUDA_OK;
+    const int64_t kp = (k + tf32x3::BK - 1) / tf32x3::BK * tf32x3::BK;
+    if (kp == 0) return CHELIS_CUDA_OK;
+    const int64_t sr = trans ? 1 : ld, sk = trans ? ld : 1;
+    dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((rows + 31) / 32),
+              static_cast<unsigned>(batch));
+    tf32x3::split_kernel<<<grid, dim3(32, 8), 0, current_stream()>>>(src, rows, k, sr, sk, stride,
+                                                                     kp, hi, lo);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("split_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+extern "C" int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t batch,
+                                                 const float *a_hi, const float *a_lo,
+                                                 const float *b_hi, const float *b_lo, float *c,
+                                                 int64_t ldc, int64_t stride_c) {
+    using namespace tf32x3;
+    if (m < 0 || n < 0 || k <= 0 || batch < 0 || ldc < n)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
+    if (m == 0 || n == 0 || batch == 0) return CHELIS_CUDA_OK;
+    const int64_t kp = (k + BK - 1) / BK * BK;
+    CUtensorMap mahi, malo, mbhi, mblo;
+    CHELIS_TRY(make_kmajor_map(&mahi, a_hi, batch * m, kp, BM));
+    CHELIS_TRY(make_kmajor_map(&malo, a_lo, batch * m, kp, BM));
+    CHELIS_TRY(make_kmajor_map(&mbhi, b_hi, batch * n, kp, BN));
+    CHELIS_TRY(make_kmajor_map(&mblo, b_lo, batch * n, kp, BN));
+    CHELIS_TRY(check_cuda(cudaFuncSetAttribute(gemm_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               SMEM_BYTES),
+                          "cudaFuncSetAttribute(gemm_kernel)"));
+    Params p;
+    p.m = m;
+    p.n = n;
+    p.num_kb = static_cast<int32_t>(kp / BK);
+    p.a_rows_per_batch = m;
+    p.b_rows_per_batch = n;
+    p.c = c;
+    p.ldc = ldc;
+    p.stride_c = stride_c;
+    dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>((m + BM - 1) / BM),
+              static_cast<unsigned>(batch));
+    gemm_kernel<<<grid, THREADS, SMEM_BYTES, current_stream()>>>(mahi, malo, mbhi, mblo, p);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("gemm_kernel(3xtf32)");
+    return CHELIS_CUDA_OK;
+}
+
+extern "C" int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                                 const float *a, int64_t lda, int64_t stride_a, const float *b,
+                                 int64_t ldb, int64_t stride_b, float *c, int64_t ldc,
+                                 int64_t stride_c, int64_t batch) {
+    CHELIS_TRY(validate_gemm_args(m, n, k, lda, ldb, ldc, batch, trans_a, trans_b));
+    if (m == 0 || n == 0 || batch == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    if (k == 0) {
+        // empty contraction: exact zero (the empty Sum, [05-OP-30])
+        for (int64_t bb = 0; bb < batch; ++bb)
+            CHELIS_TRY(check_cuda(cudaMemset2DAsync(c + bb * stride_c, ldc * sizeof(float), 0,
+                                                    n * sizeof(float), m, s),
+                                  "cudaMemset2DAsync"));
+        return CHELIS_CUDA_OK;
+    }
+    if (gemm_mode() == CHELIS_CUDA_GEMM_EXACT_TREE)
+        return launch_exact_gemm<float>(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb,
+                                        stride_b, c, ldc, stride_c, batch, s);
+    if (batch * (m > n ? m : n) > INT32_MAX)
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "batched matmul rows beyond 2^31");
+    void *scratch = nullptr;
+    CHELIS_TRY(scratch_alloc(&scratch, sgemm_3xtf32_scratch_bytes(m, n, k, batch), s));
+    int st = sgemm_3xtf32_with_scratch(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb,
+                                       stride_b, c, ldc, stride_c, batch,
+                                       static_cast<float *>(scratch), s);
+    scratch_free(scratch, s);
+    return st;
+}

@@ -1,0 +1,10 @@
+// libchelis_cuda.cu -- the library is compiled as one translation unit so
+// that device globals (the bounded-wait error word) have a single
+// definition without relocatable device code.
+#include "runtime.cu"
+#include "gemm_tf32x3.cu"
+#include "gemm_f64.cu"
+#include "rows.cu"
+#include "portfolio.cu"
+#include "mlp.cu"
+#include "abi.cu"

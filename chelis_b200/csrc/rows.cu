@@ -1,0 +1,1026 @@
+// rows.cu -- fused elementwise / reduction groups over the last axis of a
+// [rows, hidden] f32 tensor, and their adjoints:
+//   layer_norm (tier2.rs:1248-1375), softmax (tier2.rs:1079-1180) and its
+//   adjoint (grad.rs:2248-2280), keyed dropout / DropoutReplay
+//   (dtype_semantics.rs:4256-4280), row sum / max, the fused chain
+//   layer_norm -> softmax -> dropout -> row sum and its adjoint, column sums,
+//   bool count and cumsum.
+//
+// Row layout in registers.  A CTA of T threads owns one row at a time.  The
+// row is cut into "chunks" of 4*T elements; thread t holds elements
+// [4t, 4t+4) of every chunk (one float4 per chunk: 128-bit coalesced loads).
+// NC = ceil(hidden / 4T) chunks are held in registers (NC <= 8).
+//
+// Sums use the canonical adjacent-pair tree (spec/05-risc-primitives.md:
+// 452-466, 515-531) bit for bit: every chunk is an aligned power-of-two
+// block, so its sum is a subtree (thread-local pairs, then the warp and
+// block xor butterflies); the chunk sums then combine pass by pass.  A
+// ragged last chunk uses the same butterfly with absent operands passed
+// through (the tree over a prefix of leaves).
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace chelis {
+
+extern std::atomic<uint64_t> g_launches;
+int rows_mode();
+
+namespace rows {
+
+// ---------------------------------------------------------------------------
+// block-level canonical tree
+// ---------------------------------------------------------------------------
+// Reduce v[c][0..3] (thread t's 4 leaves of chunk c, valid when the element
+// index is < n) to the canonical tree total over all n leaves.  `red` is
+// shared scratch of at least NC * (T/32) floats.  Every thread returns the
+// total.  Ends with a __syncthreads so `red` can be reused.
+template <int T, int NC>
+__device__ __forceinline__ float block_tree(const float (&v)[NC][4], int n, float *red) {
+    constexpr int W = T / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool full = (n == NC * 4 * T);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        float s;
+        if (full) {
+            s = __fadd_rn(__fadd_rn(v[c][0], v[c][1]), __fadd_rn(v[c][2], v[c][3]));
+            s = warp_tree_full(s);
+        } else {
+            const int e0 = c * 4 * T + 4 * threadIdx.x;
+            const int cnt = n - e0;  // leaves of this thread still valid
+            const float s01 = tree_pair(v[c][0], cnt > 0, v[c][1], cnt > 1);
+            const float s23 = tree_pair(v[c][2], cnt > 2, v[c][3], cnt > 3);
+            s = tree_pair(s01, cnt > 0, s23, cnt > 2);
+            bool valid = cnt > 0;
+            s = warp_tree(s, valid);
+            if (!valid) s = __int_as_float(0x7fc00001);  // marker, never read as a leaf
+        }
+        if (lane == 0) red[c * W + warp] = s;
+    }
+    __syncthreads();
+    // every thread: butterfly over the W warp sums of each chunk, then the
+    // pass-by-pass tree over the chunk sums
+    float chunk[NC];
+    int nchunks = 0;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int c0 = c * 4 * T;
+        if (c0 < n) {
+            float w[W];
+#pragma unroll
+            for (int i = 0; i < W; ++i) w[i] = red[c * W + i];
+            // number of warps with at least one valid leaf in this chunk
+            const int per_warp = 4 * 32;
+            int vw = (n - c0 + per_warp - 1) / per_warp;
+            if (vw > W) vw = W;
+#pragma unroll
+            for (int width = 1; width < W; width <<= 1) {
+#pragma unroll
+                for (int i = 0; i + width < W; i += 2 * width) {
+                    const bool lv = i < vw, rv = i + width < vw;
+                    w[i] = tree_pair(w[i], lv, w[i + width], rv);
+                }
+            }
+            chunk[c] = w[0];
+            ++nchunks;
+        }
+    }
+    // pass-by-pass over nchunks (<= NC) values
+#pragma unroll
+    for (int width = 1; width < NC; width <<= 1) {
+#pragma unroll
+        for (int i = 0; i + width < NC; i += 2 * width) {
+            const bool lv = i < nchunks, rv = i + width < nchunks;
+            chunk[i] = tree_pair(chunk[i], lv, chunk[i + width], rv);
+        }
+    }
+    __syncthreads();
+    return chunk[0];
+}
+
+// Row maximum (order-free except for NaN, which fmaxf would drop: a NaN
+// anywhere makes the result NaN, as the first-NaN rule of [05-OP-12] does
+// for softmax, where only NaN-ness matters downstream).
+template <int T, int NC>
+__device__ __forceinline__ float block_max(const float (&v)[NC][4], int n, float *red) {
+    constexpr int W = T / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m = -INFINITY;
+    bool nan = false;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int e = c * 4 * T + 4 * threadIdx.x + i;
+            if (e < n) {
+                m = fmaxf(m, v[c][i]);
+                nan |= isnan(v[c][i]);
+            }
+        }
+    m = warp_max(m);
+    nan = __any_sync(0xffffffffu, nan);
+    if (lane == 0) red[warp] = nan ? __int_as_float(0x7fc00000) : m;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int i = 1; i < W; ++i) {
+        const float o = red[i];
+        r = (isnan(r) || isnan(o)) ? __int_as_float(0x7fc00000) : fmaxf(r, o);
+    }
+    __syncthreads();
+    return r;
+}
+
+template <int NC, int T>
+__device__ __forceinline__ void load_row(float (&v)[NC][4], const float *__restrict__ row, int n,
+                                         bool vec) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int e0 = c * 4 * T + 4 * threadIdx.x;
+        if (vec && e0 + 3 < n) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(row + e0));
+            v[c][0] = q.x;
+            v[c][1] = q.y;
+            v[c][2] = q.z;
+            v[c][3] = q.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = (e0 + i < n) ? row[e0 + i] : 0.0f;
+        }
+    }
+}
+
+template <int NC, int T>
+__device__ __forceinline__ void store_row(const float (&v)[NC][4], float *__restrict__ row, int n,
+                                          bool vec) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int e0 = c * 4 * T + 4 * threadIdx.x;
+        if (vec && e0 + 3 < n) {
+            *reinterpret_cast<float4 *>(row + e0) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (e0 + i < n) row[e0 + i] = v[c][i];
+        }
+    }
+}
+
+__device__ __forceinline__ float canon(float x) {
+    return isnan(x) ? __int_as_float(0x7fc00000) : x;
+}
+
+struct ChainParams {
+    const float *x, *gamma, *beta;
+    float eps;
+    uint64_t key;
+    uint64_t threshold;  // dropout keep threshold on (word >> 11)
+    float den;           // fl(1 - rate)
+    float rden;          // 1 / den (FAST mode)
+    float one_over_den;  // fl(1 / den): DropoutReplay of a unit cotangent
+    float hf, rh;        // hidden as f32, 1/hidden
+    int64_t rows;
+    int hidden;
+    int64_t index_base;
+    float *rowsum;      // fwd
+    float *stats;       // [rows][4]: mean, d, max, Z (optional)
+    const float *stats_in;
+    float *dx;          // bwd
+    float *dgamma_part, *dbeta_part;  // [grid][hidden] partials (bwd)
+    int rows_per_cta;
+};
+
+// ---------------------------------------------------------------------------
+// forward: one row per CTA iteration
+// ---------------------------------------------------------------------------
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T) chain_fwd_kernel(ChainParams p) {
+    __shared__ float red[NC * (T / 32) + 8];
+    const int n = p.hidden;
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
+    float g[NC][4], b[NC][4];
+    load_row<NC, T>(g, p.gamma, n, (reinterpret_cast<uintptr_t>(p.gamma) & 15) == 0 && n % 4 == 0);
+    load_row<NC, T>(b, p.beta, n, (reinterpret_cast<uintptr_t>(p.beta) & 15) == 0 && n % 4 == 0);
+    for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+        float v[NC][4];
+        load_row<NC, T>(v, p.x + r * n, n, vec);
+        // mean = tree(x) / hidden
+        const float s1 = block_tree<T, NC>(v, n, red);
+        const float mean = EXACT ? __fdiv_rn(s1, p.hf) : __fmul_rn(s1, p.rh);
+        float c2[NC][4];
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[c][i] = __fsub_rn(v[c][i], mean);  // centered
+                c2[c][i] = __fmul_rn(v[c][i], v[c][i]);
+            }
+        const float s2 = block_tree<T, NC>(c2, n, red);
+        const float var = EXACT ? __fdiv_rn(s2, p.hf) : __fmul_rn(s2, p.rh);
+        const float d = __fsqrt_rn(__fadd_rn(var, p.eps));
+        const float rd = __fdiv_rn(1.0f, d);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float nn = EXACT ? __fdiv_rn(v[c][i], d) : __fmul_rn(v[c][i], rd);
+                v[c][i] = __fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]);  // y
+            }
+        const float mx = block_max<T, NC>(v, n, red);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = expf(__fsub_rn(v[c][i], mx));  // e
+        const float z = block_tree<T, NC>(v, n, red);
+        const float rz = __fdiv_rn(1.0f, z);
+        const uint64_t base = static_cast<uint64_t>(p.index_base + r * n);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int e = c * 4 * T + 4 * threadIdx.x + i;
+                const float s = EXACT ? __fdiv_rn(v[c][i], z) : __fmul_rn(v[c][i], rz);
+                const bool keep = e < n && dropout_keep(p.key, base + e, p.threshold);
+                v[c][i] = keep ? (EXACT ? __fdiv_rn(s, p.den) : __fmul_rn(s, p.rden)) : 0.0f;
+            }
+        const float rs = block_tree<T, NC>(v, n, red);
+        if (threadIdx.x == 0) {
+            p.rowsum[r] = canon(rs);
+            if (p.stats) {
+                float4 st = make_float4(mean, d, mx, z);
+                *reinterpret_cast<float4 *>(p.stats + 4 * r) = st;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// adjoint of loss = sum(rowsum): dx, and per-CTA partial dgamma / dbeta
+// ---------------------------------------------------------------------------
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T) chain_bwd_kernel(ChainParams p) {
+    __shared__ float red[NC * (T / 32) + 8];
+    const int n = p.hidden;
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(p.dx) & 15) == 0);
+    float g[NC][4], b[NC][4], pg[NC][4], pb[NC][4];
+    const bool pvec = (reinterpret_cast<uintptr_t>(p.gamma) & 15) == 0 && n % 4 == 0;
+    load_row<NC, T>(g, p.gamma, n, pvec);
+    load_row<NC, T>(b, p.beta, n, (reinterpret_cast<uintptr_t>(p.beta) & 15) == 0 && n % 4 == 0);
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pg[c][i] = pb[c][i] = 0.0f;
+
+    const int64_t r_begin = static_cast<int64_t>(blockIdx.x) * p.rows_per_cta;
+    int64_t r_end = r_begin + p.rows_per_cta;
+    if (r_end > p.rows) r_end = p.rows;
+    for (int64_t r = r_begin; r < r_end; ++r) {
+        float x[NC][4];
+        load_row<NC, T>(x, p.x + r * n, n, vec);
+        float mean, d, mx, z;
+        if (p.stats_in) {
+            const float4 st = *reinterpret_cast<const float4 *>(p.stats_in + 4 * r);
+            mean = st.x;
+            d = st.y;
+            mx = st.z;
+            z = st.w;
+        } else {
+            const float s1 = block_tree<T, NC>(x, n, red);
+            mean = EXACT ? __fdiv_rn(s1, p.hf) : __fmul_rn(s1, p.rh);
+            float t2[NC][4];
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float cc = __fsub_rn(x[c][i], mean);
+                    t2[c][i] = __fmul_rn(cc, cc);
+                }
+            const float s2 = block_tree<T, NC>(t2, n, red);
+            const float var = EXACT ? __fdiv_rn(s2, p.hf) : __fmul_rn(s2, p.rh);
+            d = __fsqrt_rn(__fadd_rn(var, p.eps));
+            const float rd0 = __fdiv_rn(1.0f, d);
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float cc = __fsub_rn(x[c][i], mean);
+                    const float nn = EXACT ? __fdiv_rn(cc, d) : __fmul_rn(cc, rd0);
+                    t2[c][i] = __fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]);
+                }
+            mx = block_max<T, NC>(t2, n, red);
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) t2[c][i] = expf(__fsub_rn(t2[c][i], mx));
+            z = block_tree<T, NC>(t2, n, red);
+        }
+        const float rd = __fdiv_rn(1.0f, d);
+        const float rz = __fdiv_rn(1.0f, z);
+        const uint64_t base = static_cast<uint64_t>(p.index_base + r * n);
+        // s (softmax output) and ds (replayed unit cotangent); x becomes c
+        float s[NC][4], ds[NC][4], gy[NC][4];
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int e = c * 4 * T + 4 * threadIdx.x + i;
+                const float cc = __fsub_rn(x[c][i], mean);
+                x[c][i] = cc;
+                const float nn = EXACT ? __fdiv_rn(cc, d) : __fmul_rn(cc, rd);
+                const float y = __fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]);
+                const float ee = expf(__fsub_rn(y, mx));
+                s[c][i] = EXACT ? __fdiv_rn(ee, z) : __fmul_rn(ee, rz);
+                const bool keep = e < n && dropout_keep(p.key, base + e, p.threshold);
+                ds[c][i] = keep ? p.one_over_den : 0.0f;
+                gy[c][i] = __fmul_rn(ds[c][i], s[c][i]);
+            }
+        const float q = block_tree<T, NC>(gy, n, red);
+        const float two_d = __fmul_rn(2.0f, d);
+        const float r2d = __fdiv_rn(1.0f, two_d);
+        // dy = s * (ds - q); dn = dy * gamma; dt = -((dn * n) / d) / (2d)
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int e = c * 4 * T + 4 * threadIdx.x + i;
+                const float dy = __fmul_rn(s[c][i], __fsub_rn(ds[c][i], q));
+                const float nn = EXACT ? __fdiv_rn(x[c][i], d) : __fmul_rn(x[c][i], rd);
+                if (e < n) {
+                    pg[c][i] = __fadd_rn(pg[c][i], __fmul_rn(dy, nn));
+                    pb[c][i] = __fadd_rn(pb[c][i], dy);
+                }
+                const float dn = __fmul_rn(dy, g[c][i]);
+                const float qq = EXACT ? __fdiv_rn(__fmul_rn(dn, nn), d)
+                                       : __fmul_rn(__fmul_rn(dn, nn), rd);
+                gy[c][i] = EXACT ? __fdiv_rn(-qq, two_d) : __fmul_rn(-qq, r2d);  // dt
+                s[c][i] = EXACT ? __fdiv_rn(dn, d) : __fmul_rn(dn, rd);          // dc1
+            }
+        const float dvar = block_tree<T, NC>(gy, n, red);
+        const float ds2 = EXACT ? __fdiv_rn(dvar, p.hf) : __fmul_rn(dvar, p.rh);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pr = __fmul_rn(ds2, x[c][i]);
+                const float dc = __fadd_rn(__fadd_rn(pr, pr), s[c][i]);
+                s[c][i] = dc;
+                gy[c][i] = -dc;
+            }
+        const float dm = block_tree<T, NC>(gy, n, red);
+        const float ds1 = EXACT ? __fdiv_rn(dm, p.hf) : __fmul_rn(dm, p.rh);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s[c][i] = canon(__fadd_rn(ds1, s[c][i]));
+        store_row<NC, T>(s, p.dx + r * n, n, vec);
+    }
+    store_row<NC, T>(pg, p.dgamma_part + static_cast<int64_t>(blockIdx.x) * n, n, pvec);
+    store_row<NC, T>(pb, p.dbeta_part + static_cast<int64_t>(blockIdx.x) * n, n, pvec);
+}
+
+// ---------------------------------------------------------------------------
+// standalone row ops
+// ---------------------------------------------------------------------------
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T)
+    layer_norm_kernel(const float *__restrict__ xin, const float *__restrict__ gamma,
+                      const float *__restrict__ beta, float eps, float *__restrict__ yout,
+                      int64_t rows, int n) {
+    __shared__ float red[NC * (T / 32) + 8];
+    const float hf = static_cast<float>(n), rh = __fdiv_rn(1.0f, hf);
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(xin) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(yout) & 15) == 0);
+    float g[NC][4], b[NC][4];
+    load_row<NC, T>(g, gamma, n, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && n % 4 == 0);
+    load_row<NC, T>(b, beta, n, (reinterpret_cast<uintptr_t>(beta) & 15) == 0 && n % 4 == 0);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float v[NC][4], c2[NC][4];
+        load_row<NC, T>(v, xin + r * n, n, vec);
+        const float s1 = block_tree<T, NC>(v, n, red);
+        const float mean = EXACT ? __fdiv_rn(s1, hf) : __fmul_rn(s1, rh);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[c][i] = __fsub_rn(v[c][i], mean);
+                c2[c][i] = __fmul_rn(v[c][i], v[c][i]);
+            }
+        const float s2 = block_tree<T, NC>(c2, n, red);
+        const float var = EXACT ? __fdiv_rn(s2, hf) : __fmul_rn(s2, rh);
+        const float d = __fsqrt_rn(__fadd_rn(var, eps));
+        const float rd = __fdiv_rn(1.0f, d);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float nn = EXACT ? __fdiv_rn(v[c][i], d) : __fmul_rn(v[c][i], rd);
+                v[c][i] = canon(__fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]));
+            }
+        store_row<NC, T>(v, yout + r * n, n, vec);
+    }
+}
+
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T)
+    softmax_kernel(const float *__restrict__ xin, float *__restrict__ yout, int64_t rows, int n) {
+    __shared__ float red[NC * (T / 32) + 8];
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(xin) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(yout) & 15) == 0);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float v[NC][4];
+        load_row<NC, T>(v, xin + r * n, n, vec);
+        const float mx = block_max<T, NC>(v, n, red);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = expf(__fsub_rn(v[c][i], mx));
+        const float z = block_tree<T, NC>(v, n, red);
+        const float rz = __fdiv_rn(1.0f, z);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[c][i] = canon(EXACT ? __fdiv_rn(v[c][i], z) : __fmul_rn(v[c][i], rz));
+        store_row<NC, T>(v, yout + r * n, n, vec);
+    }
+}
+
+template <int T, int NC>
+__global__ void __launch_bounds__(T)
+    softmax_bwd_kernel(const float *__restrict__ yin, const float *__restrict__ gin,
+                       float *__restrict__ dx, int64_t rows, int n) {
+    __shared__ float red[NC * (T / 32) + 8];
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(yin) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(gin) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(dx) & 15) == 0);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float y[NC][4], g[NC][4], gy[NC][4];
+        load_row<NC, T>(y, yin + r * n, n, vec);
+        load_row<NC, T>(g, gin + r * n, n, vec);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) gy[c][i] = __fmul_rn(g[c][i], y[c][i]);
+        const float q = block_tree<T, NC>(gy, n, red);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) gy[c][i] = canon(__fmul_rn(y[c][i], __fsub_rn(g[c][i], q)));
+        store_row<NC, T>(gy, dx + r * n, n, vec);
+    }
+}
+
+// Row sum of arbitrary width: chunk subtrees of 4T leaves, chunk sums
+// pushed by thread 0 into a carry tree (the C lane's streaming form).
+template <int T>
+__global__ void __launch_bounds__(T)
+    row_sum_kernel(const float *__restrict__ x, int64_t rows, int64_t cols,
+                   float *__restrict__ out) {
+    __shared__ float red[T / 32 + 8];
+    float level[40];
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float *row = x + r * cols;
+        int64_t count = 0;
+        for (int64_t c0 = 0; c0 < cols; c0 += 4 * T) {
+            float v[1][4];
+            const int64_t rem = cols - c0;
+            const int nvalid = rem < 4 * T ? static_cast<int>(rem) : 4 * T;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int e = 4 * threadIdx.x + i;
+                v[0][i] = e < nvalid ? row[c0 + e] : 0.0f;
+            }
+            const float s = block_tree<T, 1>(v, nvalid, red);
+            if (threadIdx.x == 0) {
+                float carry = s;
+                int depth = 0;
+                for (int64_t pending = count++; pending & 1; pending >>= 1, ++depth)
+                    carry = __fadd_rn(level[depth], carry);
+                level[depth] = carry;
+            }
+        }
+        if (threadIdx.x == 0) {
+            float total = 0.0f;
+            bool found = false;
+            int depth = 0;
+            for (int64_t remaining = count; remaining; remaining >>= 1, ++depth) {
+                if (remaining & 1) {
+                    total = found ? __fadd_rn(level[depth], total) : level[depth];
+                    found = true;
+                }
+            }
+            out[r] = canon(total);
+        }
+    }
+}
+
+// [05-OP-12]: first NaN (with its payload) wins, else the maximum with the
+// first representation among equals.  One warp per row.
+__global__ void row_max_kernel(const float *__restrict__ x, int64_t rows, int64_t cols,
+                               float *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += warps) {
+        const float *row = x + r * cols;
+        float best = 0.0f;
+        int64_t bi = INT64_MAX;  // index of the selected element
+        for (int64_t j = lane; j < cols; j += 32) {
+            const float v = row[j];
+            bool take;
+            if (bi == INT64_MAX) take = true;
+            else if (isnan(best)) take = false;  // an earlier NaN stays
+            else if (isnan(v)) take = true;
+            else take = v > best;
+            if (take) { best = v; bi = j; }
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            bool take;
+            if (oi == INT64_MAX) take = false;
+            else if (bi == INT64_MAX) take = true;
+            else if (isnan(best) || isnan(ob)) {
+                take = isnan(ob) && (!isnan(best) || oi < bi);
+            } else if (ob > best) take = true;
+            else if (ob == best) take = oi < bi;
+            else take = false;
+            if (take) { best = ob; bi = oi; }
+        }
+        if (lane == 0) out[r] = best;
+    }
+}
+
+// Column sums (axis 0) of [rows, cols]: aligned row blocks of RB leaves
+// (complete subtrees of the canonical tree over rows) reduced per column
+// with a register carry tree, then the block sums reduced the same way by a
+// second launch.  A partial last block is the tree over its prefix.
+constexpr int COL_RB = 64;
+__global__ void col_block_kernel(const float *__restrict__ x, int64_t rows, int64_t cols,
+                                 int64_t rb, float *__restrict__ out) {
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t blk = blockIdx.y;
+    if (col >= cols) return;
+    const int64_t r0 = blk * rb;
+    int64_t r1 = r0 + rb;
+    if (r1 > rows) r1 = rows;
+    float level[40];
+    int64_t count = 0;
+    for (int64_t r = r0; r < r1; ++r) {
+        float carry = x[r * cols + col];
+        int depth = 0;
+        for (int64_t pending = count++; pending & 1; pending >>= 1, ++depth)
+            carry = __fadd_rn(level[depth], carry);
+        level[depth] = carry;
+    }
+    float total = 0.0f;
+    bool found = false;
+    int depth = 0;
+    for (int64_t remaining = count; remaining; remaining >>= 1, ++depth) {
+        if (remaining & 1) {
+            total = found ? __fadd_rn(level[depth], total) : level[depth];
+            found = true;
+        }
+    }
+    out[blk * cols + col] = total;
+}
+
+// ---------------------------------------------------------------------------
+// dropout, count, cumsum
+// ---------------------------------------------------------------------------
+__global__ void dropout_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t n,
+                               uint64_t key, uint64_t threshold, float den, int64_t index_base) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const bool keep = dropout_keep(key, static_cast<uint64_t>(index_base + i), threshold);
+        y[i] = keep ? canon(__fdiv_rn(x[i], den)) : 0.0f;
+    }
+}
+
+__global__ void dropout_mask_kernel(uint8_t *__restrict__ keep, int64_t n, uint64_t key,
+                                    uint64_t threshold, int64_t index_base) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        keep[i] = dropout_keep(key, static_cast<uint64_t>(index_base + i), threshold) ? 1 : 0;
+}
+
+__global__ void count_kernel(const uint8_t *__restrict__ x, int64_t n,
+                             unsigned long long *__restrict__ out) {
+    unsigned long long c = 0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        c += x[i] ? 1ull : 0ull;
+    for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+    if ((threadIdx.x & 31) == 0) atomicAdd(out, c);
+}
+
+// Sequential scan per lane ([05-OP-53]): 4 warps per CTA, a warp owns 32
+// lanes; each 32-step
+// slab of the 32 lanes is staged through shared memory so the global reads
+// and writes stay coalesced while each thread scans its own lane in order.
+template <typename V>
+__global__ void cumsum_kernel(const V *__restrict__ x, V *__restrict__ y, int64_t lanes,
+                              int64_t len, int reverse) {
+    __shared__ V tile[4][32][33];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t lane0 = (static_cast<int64_t>(blockIdx.x) * 4 + w) * 32;
+    if (lane0 >= lanes) return;
+    V acc = V(0);
+    bool first = true;
+    const int64_t nslab = (len + 31) / 32;
+    for (int64_t sb = 0; sb < nslab; ++sb) {
+        const int64_t slab = reverse ? (nslab - 1 - sb) : sb;
+        const int64_t t0 = slab * 32;
+        // stage: row i of the tile = lane (lane0 + i), columns t0..t0+31
+        for (int i = 0; i < 32; ++i) {
+            const int64_t l = lane0 + i, t = t0 + lane;
+            tile[w][i][lane] = (l < lanes && t < len) ? x[l * len + t] : V(0);
+        }
+        __syncwarp();
+        const int64_t my = lane0 + lane;
+        const int cnt = static_cast<int>((len - t0) < 32 ? (len - t0) : 32);
+        for (int jj = 0; jj < cnt; ++jj) {
+            const int j = reverse ? (cnt - 1 - jj) : jj;
+            const V v = tile[w][lane][j];
+            acc = first ? v : acc + v;
+            first = false;
+            tile[w][lane][j] = isnan(acc) ? V(NAN) : acc;
+        }
+        __syncwarp();
+        for (int i = 0; i < 32; ++i) {
+            const int64_t l = lane0 + i, t = t0 + lane;
+            if (l < lanes && t < len) y[l * len + t] = tile[w][i][lane];
+        }
+        __syncwarp();
+        (void)my;
+    }
+}
+
+}  // namespace rows
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+// Least 53-bit integer u whose f32 rounding reaches rate * 2^53, so that
+// keep <=> (word >> 11) >= u reproduces round_f32(unit) >= rate exactly
+// (PreparedDropout::apply, dtype_semantics.rs:4265-4277).
+uint64_t dropout_threshold(float rate) {
+    const double target = static_cast<double>(rate) * 9007199254740992.0;  // exact
+    uint64_t lo = 0, hi = 1ull << 53;  // answer in [lo, hi]
+    while (lo < hi) {
+        const uint64_t mid = lo + (hi - lo) / 2;
+        const float f = static_cast<float>(mid);  // RN to f32 of an exact integer
+        if (static_cast<double>(f) >= target) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+namespace {
+
+int check_rate(float rate) {
+    if (!(rate >= 0.0f && rate < 1.0f))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at f32");
+    return CHELIS_CUDA_OK;
+}
+
+template <typename F>
+int dispatch_nc(int hidden, int threads, F &&f) {
+    const int per = 4 * threads;
+    const int nc = (hidden + per - 1) / per;
+    if (nc <= 1) return f(std::integral_constant<int, 1>());
+    if (nc <= 2) return f(std::integral_constant<int, 2>());
+    if (nc <= 4) return f(std::integral_constant<int, 4>());
+    if (nc <= 8) return f(std::integral_constant<int, 8>());
+    return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "row width %d beyond %d", hidden, 8 * per);
+}
+
+int rows_grid(int64_t rows, int per_sm) {
+    int64_t g = static_cast<int64_t>(sm_count()) * per_sm;
+    if (rows < g) g = rows;
+    return static_cast<int>(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStream_t s);
+
+}  // namespace chelis
+
+using namespace chelis;
+using namespace chelis::rows;
+
+namespace chelis {
+
+// Canonical column sums of a [rows, cols] matrix into out[cols] (two-level
+// aligned-block scheme; one scratch buffer of ceil(rows/64) * cols floats
+// when rows > 64).
+int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStream_t s) {
+    if (cols == 0) return CHELIS_CUDA_OK;
+    if (rows == 0)
+        return check_cuda(cudaMemsetAsync(out, 0, cols * sizeof(float), s), "cudaMemsetAsync");
+    const unsigned cb = static_cast<unsigned>((cols + 127) / 128);
+    if (rows <= COL_RB) {
+        col_block_kernel<<<dim3(cb, 1), 128, 0, s>>>(x, rows, cols, rows, out);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("col_block_kernel");
+        return CHELIS_CUDA_OK;
+    }
+    const int64_t nb = (rows + COL_RB - 1) / COL_RB;
+    void *tmp = nullptr;
+    CHELIS_TRY(scratch_alloc(&tmp, static_cast<size_t>(nb * cols) * sizeof(float), s));
+    col_block_kernel<<<dim3(cb, static_cast<unsigned>(nb)), 128, 0, s>>>(x, rows, cols, COL_RB,
+                                                                        static_cast<float *>(tmp));
+    g_launches++;
+    int st = check_cuda(cudaGetLastError(), "col_block_kernel");
+    if (st == CHELIS_CUDA_OK) st = col_sum_into(static_cast<float *>(tmp), nb, cols, out, s);
+    scratch_free(tmp, s);
+    return st;
+}
+
+// Shared by chelis_cuda_chain_bwd and any caller that supplies its own
+// partial buffers: `part` holds 2 * grid * hidden floats.
+int chain_bwd_with_partials(const float *x, const float *gamma, const float *beta, float eps,
+                            uint64_t key, float rate, int64_t rows, int64_t hidden,
+                            int64_t index_base, const float *row_stats, float *dx, float *dgamma,
+                            float *dbeta, float *part, int grid, cudaStream_t s);
+
+int chain_bwd_grid(int64_t rows) { return rows_grid(rows, 4); }
+
+}  // namespace chelis
+
+namespace {
+ChainParams make_chain_params(const float *x, const float *gamma, const float *beta, float eps,
+                              uint64_t key, float rate, int64_t rows, int64_t hidden,
+                              int64_t index_base) {
+    ChainParams p{};
+    p.x = x;
+    p.gamma = gamma;
+    p.beta = beta;
+    p.eps = eps;
+    p.key = key;
+    p.threshold = dropout_threshold(rate);
+    volatile float one = 1.0f;
+    p.den = one - rate;
+    p.rden = 1.0f / p.den;
+    p.one_over_den = 1.0f / p.den;
+    p.hf = static_cast<float>(hidden);
+    p.rh = 1.0f / p.hf;
+    p.rows = rows;
+    p.hidden = static_cast<int>(hidden);
+    p.index_base = index_base;
+    return p;
+}
+
+template <int T>
+int launch_chain_fwd(const ChainParams &p, cudaStream_t s) {
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    return dispatch_nc(p.hidden, T, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        const unsigned grid = static_cast<unsigned>(p.rows < 65535 * 16 ? p.rows : 65535 * 16);
+        if (exact) chain_fwd_kernel<T, NC, true><<<grid, T, 0, s>>>(p);
+        else chain_fwd_kernel<T, NC, false><<<grid, T, 0, s>>>(p);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("chain_fwd_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+template <int T>
+int launch_chain_bwd(const ChainParams &p, int grid, cudaStream_t s) {
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    return dispatch_nc(p.hidden, T, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        if (exact) chain_bwd_kernel<T, NC, true><<<grid, T, 0, s>>>(p);
+        else chain_bwd_kernel<T, NC, false><<<grid, T, 0, s>>>(p);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("chain_bwd_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+constexpr int kRowThreads = 256;
+
+int check_rows_args(const void *x, int64_t rows, int64_t hidden) {
+    if (rows < 0 || hidden < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in rows at i64");
+    if (hidden > 8 * 4 * kRowThreads || hidden > INT32_MAX)
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "row width %lld beyond %d",
+                         static_cast<long long>(hidden), 8 * 4 * kRowThreads);
+    (void)x;
+    return CHELIS_CUDA_OK;
+}
+}  // namespace
+
+namespace chelis {
+int chain_bwd_with_partials(const float *x, const float *gamma, const float *beta, float eps,
+                            uint64_t key, float rate, int64_t rows, int64_t hidden,
+                            int64_t index_base, const float *row_stats, float *dx, float *dgamma,
+                            float *dbeta, float *part, int grid, cudaStream_t s) {
+    ChainParams p = make_chain_params(x, gamma, beta, eps, key, rate, rows, hidden, index_base);
+    p.stats_in = row_stats;
+    p.dx = dx;
+    p.dgamma_part = part;
+    p.dbeta_part = part + static_cast<int64_t>(grid) * hidden;
+    p.rows_per_cta = static_cast<int>((rows + grid - 1) / grid);
+    CHELIS_TRY(launch_chain_bwd<kRowThreads>(p, grid, s));
+    CHELIS_TRY(col_sum_into(p.dgamma_part, grid, hidden, dgamma, s));
+    CHELIS_TRY(col_sum_into(p.dbeta_part, grid, hidden, dbeta, s));
+    return CHELIS_CUDA_OK;
+}
+}  // namespace chelis
+
+extern "C" {
+
+int chelis_cuda_chain_fwd(const float *x, const float *gamma, const float *beta, float eps,
+                          uint64_t key, float rate, int64_t rows, int64_t hidden,
+                          int64_t index_base, float *rowsum, float *row_stats) {
+    CHELIS_TRY(check_rows_args(x, rows, hidden));
+    CHELIS_TRY(check_rate(rate));
+    if (hidden == 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in layer_norm at f32");
+    if (rows == 0) return CHELIS_CUDA_OK;
+    ChainParams p = make_chain_params(x, gamma, beta, eps, key, rate, rows, hidden, index_base);
+    p.rowsum = rowsum;
+    p.stats = row_stats;
+    return launch_chain_fwd<kRowThreads>(p, current_stream());
+}
+
+int chelis_cuda_chain_bwd(const float *x, const float *gamma, const float *beta, float eps,
+                          uint64_t key, float rate, int64_t rows, int64_t hidden,
+                          int64_t index_base, const float *row_stats, float *dx, float *dgamma,
+                          float *dbeta) {
+    CHELIS_TRY(check_rows_args(x, rows, hidden));
+    CHELIS_TRY(check_rate(rate));
+    if (hidden == 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in layer_norm at f32");
+    cudaStream_t s = current_stream();
+    if (rows == 0) {
+        CHELIS_TRY(check_cuda(cudaMemsetAsync(dgamma, 0, hidden * sizeof(float), s), "memset"));
+        return check_cuda(cudaMemsetAsync(dbeta, 0, hidden * sizeof(float), s), "memset");
+    }
+    const int grid = chain_bwd_grid(rows);
+    void *part = nullptr;
+    CHELIS_TRY(scratch_alloc(&part, static_cast<size_t>(2) * grid * hidden * sizeof(float), s));
+    int st = chain_bwd_with_partials(x, gamma, beta, eps, key, rate, rows, hidden, index_base,
+                                     row_stats, dx, dgamma, dbeta, static_cast<float *>(part),
+                                     grid, s);
+    scratch_free(part, s);
+    return st;
+}
+
+int chelis_cuda_layer_norm_f32(const float *x, const float *gamma, const float *beta, float eps,
+                               float *y, int64_t rows, int64_t hidden) {
+    CHELIS_TRY(check_rows_args(x, rows, hidden));
+    if (hidden == 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in layer_norm at f32");
+    if (rows == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    const int n = static_cast<int>(hidden);
+    const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
+    return dispatch_nc(n, kRowThreads, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        if (exact) layer_norm_kernel<kRowThreads, NC, true><<<grid, kRowThreads, 0, s>>>(x, gamma, beta, eps, y, rows, n);
+        else layer_norm_kernel<kRowThreads, NC, false><<<grid, kRowThreads, 0, s>>>(x, gamma, beta, eps, y, rows, n);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("layer_norm_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+int chelis_cuda_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols) {
+    CHELIS_TRY(check_rows_args(x, rows, cols));
+    if (rows == 0 || cols == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    const int n = static_cast<int>(cols);
+    const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
+    return dispatch_nc(n, kRowThreads, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        if (exact) softmax_kernel<kRowThreads, NC, true><<<grid, kRowThreads, 0, s>>>(x, y, rows, n);
+        else softmax_kernel<kRowThreads, NC, false><<<grid, kRowThreads, 0, s>>>(x, y, rows, n);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("softmax_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+int chelis_cuda_softmax_rows_bwd_f32(const float *y, const float *g, float *dx, int64_t rows,
+                                     int64_t cols) {
+    CHELIS_TRY(check_rows_args(y, rows, cols));
+    if (rows == 0 || cols == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    const int n = static_cast<int>(cols);
+    const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
+    return dispatch_nc(n, kRowThreads, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        softmax_bwd_kernel<kRowThreads, NC><<<grid, kRowThreads, 0, s>>>(y, g, dx, rows, n);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("softmax_bwd_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+int chelis_cuda_row_sum_f32(const float *x, int64_t rows, int64_t cols, float *out) {
+    if (rows < 0 || cols < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in sum at i64");
+    if (rows == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    if (cols == 0) return check_cuda(cudaMemsetAsync(out, 0, rows * sizeof(float), s), "memset");
+    const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
+    row_sum_kernel<256><<<grid, 256, 0, s>>>(x, rows, cols, out);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("row_sum_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_col_sum_f32(const float *x, int64_t rows, int64_t cols, float *out) {
+    if (rows < 0 || cols < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in sum at i64");
+    return col_sum_into(x, rows, cols, out, current_stream());
+}
+
+int chelis_cuda_row_max_f32(const float *x, int64_t rows, int64_t cols, float *out) {
+    if (rows < 0 || cols < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in max_reduce at i64");
+    if (rows == 0) return CHELIS_CUDA_OK;
+    if (cols == 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in max_reduce at f32");
+    cudaStream_t s = current_stream();
+    int64_t blocks = (rows * 32 + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    row_max_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, cols, out);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("row_max_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_count_bool(const uint8_t *x, int64_t n, int64_t *out_device) {
+    if (n < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in count at i64");
+    cudaStream_t s = current_stream();
+    CHELIS_TRY(check_cuda(cudaMemsetAsync(out_device, 0, sizeof(int64_t), s), "memset"));
+    if (n == 0) return CHELIS_CUDA_OK;
+    int64_t blocks = (n + 1023) / 1024;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    count_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        x, n, reinterpret_cast<unsigned long long *>(out_device));
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("count_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_dropout_f32(const float *x, float *y, int64_t n, uint64_t key, float rate,
+                            int64_t index_base) {
+    CHELIS_TRY(check_rate(rate));
+    if (n < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at i64");
+    if (n == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    volatile float one = 1.0f;
+    const float den = one - rate;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    dropout_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, y, n, key,
+                                                               dropout_threshold(rate), den,
+                                                               index_base);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("dropout_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_dropout_mask(uint8_t *keep, int64_t n, uint64_t key, float rate,
+                             int64_t index_base) {
+    CHELIS_TRY(check_rate(rate));
+    if (n < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at i64");
+    if (n == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    dropout_mask_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        keep, n, key, dropout_threshold(rate), index_base);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("dropout_mask_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_cumsum_f64(const double *x, double *y, int64_t lanes, int64_t len, int reverse) {
+    if (lanes < 0 || len < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in cumsum at i64");
+    if (lanes == 0 || len == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    const unsigned grid = static_cast<unsigned>((lanes + 127) / 128);
+    cumsum_kernel<double><<<grid, 128, 0, s>>>(x, y, lanes, len, reverse);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("cumsum_kernel<f64>");
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_cumsum_f32(const float *x, float *y, int64_t lanes, int64_t len, int reverse) {
+    if (lanes < 0 || len < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in cumsum at i64");
+    if (lanes == 0 || len == 0) return CHELIS_CUDA_OK;
+    cudaStream_t s = current_stream();
+    const unsigned grid = static_cast<unsigned>((lanes + 127) / 128);
+    cumsum_kernel<float><<<grid, 128, 0, s>>>(x, y, lanes, len, reverse);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("cumsum_kernel<f32>");
+    return CHELIS_CUDA_OK;
+}
+
+}  // extern "C"

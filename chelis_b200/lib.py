@@ -1,0 +1,141 @@
+"""ctypes binding of libchelis_cuda.so (the C ABI declared in
+include/chelis_cuda.h).
+
+There is no fallback: if the shared library is missing or cannot be loaded
+the import raises, and every entry point that returns a non-zero status
+raises ChelisCudaError with the library's message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libchelis_cuda.so")
+
+c_i64 = ctypes.c_int64
+c_u64 = ctypes.c_uint64
+c_i32 = ctypes.c_int32
+c_int = ctypes.c_int
+c_f32 = ctypes.c_float
+c_vp = ctypes.c_void_p
+
+
+class GpuTensor(ctypes.Structure):
+    """chelis_gpu_tensor (crates/chelis-backend-hip/runtime/chelis_device_descriptor.h:8-18)."""
+    _fields_ = [
+        ("data", c_vp),
+        ("shape", ctypes.POINTER(c_i64)),
+        ("strides", ctypes.POINTER(c_i64)),
+        ("count", c_i64),
+        ("byte_capacity", c_i64),
+        ("rank", c_i32),
+        ("dtype", ctypes.c_uint8),
+        ("ownership", ctypes.c_uint8),
+        ("reserved", ctypes.c_uint8 * 2),
+    ]
+
+
+DTYPE_F32, DTYPE_F64, DTYPE_I32, DTYPE_BOOL, DTYPE_I64 = 0, 1, 2, 3, 4
+GEMM_3XTF32, GEMM_EXACT_TREE = 0, 1
+ROWS_EXACT, ROWS_FAST = 0, 1
+STATUS_NAMES = {0: "OK", 1: "DOMAIN", 2: "OVERFLOW", 3: "CUDA", 4: "UNSUPPORTED", 5: "TIMEOUT",
+                6: "NO_DEVICE"}
+
+
+class ChelisCudaError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+_P = ctypes.POINTER(GpuTensor)
+_PP = ctypes.POINTER(c_vp)
+
+# name -> (restype, argtypes); every int-returning entry is a status code.
+SIGNATURES = {
+    "chelis_cuda_version": (c_int, []),
+    "chelis_cuda_last_error": (ctypes.c_char_p, []),
+    "chelis_cuda_init": (c_int, [c_i32]),
+    "chelis_cuda_set_stream": (c_int, [c_vp]),
+    "chelis_cuda_get_stream": (c_vp, []),
+    "chelis_cuda_synchronize": (c_int, []),
+    "chelis_cuda_device_status": (c_int, []),
+    "chelis_cuda_launch_count": (c_u64, []),
+    "chelis_cuda_set_gemm_mode": (c_int, [c_int]),
+    "chelis_cuda_get_gemm_mode": (c_int, []),
+    "chelis_cuda_set_rows_mode": (c_int, [c_int]),
+    "chelis_cuda_get_rows_mode": (c_int, []),
+    "chelis_device_tensor_alloc_shape": (c_vp, [ctypes.c_uint8, c_i32, ctypes.POINTER(c_i64)]),
+    "chelis_device_tensor_borrow_shape": (c_vp, [ctypes.c_uint8, c_i32, ctypes.POINTER(c_i64), c_vp, c_i64]),
+    "chelis_device_tensor_import": (c_vp, [_P]),
+    "chelis_device_tensor_view": (_P, [c_vp]),
+    "chelis_device_tensor_device": (c_i32, [c_vp]),
+    "chelis_device_tensor_clone": (c_vp, [c_vp]),
+    "chelis_device_tensor_release": (None, [c_vp]),
+    "chelis_device_tensor_copy_from_host_bytes": (c_int, [c_vp, c_vp, c_i64]),
+    "chelis_device_tensor_copy_to_host_bytes": (c_int, [c_vp, c_i64, c_vp]),
+    "chelis_cuda_sgemm_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64]),
+    "chelis_cuda_dgemm_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64]),
+    "chelis_cuda_sgemm_batched_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64, c_i64]),
+    "chelis_cuda_sgemm_strided_batched_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "chelis_cuda_dgemm_batched_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64, c_i64]),
+    "chelis_cuda_dgemm_strided_batched_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "chelis_cuda_sgemm": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    "chelis_cuda_dgemm": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    "chelis_cuda_tf32x3_split": (c_int, [c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "chelis_cuda_sgemm_tf32x3_presplit": (c_int, [c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64]),
+    "chelis_cuda_row_sum_f32": (c_int, [c_vp, c_i64, c_i64, c_vp]),
+    "chelis_cuda_col_sum_f32": (c_int, [c_vp, c_i64, c_i64, c_vp]),
+    "chelis_cuda_row_max_f32": (c_int, [c_vp, c_i64, c_i64, c_vp]),
+    "chelis_cuda_count_bool": (c_int, [c_vp, c_i64, c_vp]),
+    "chelis_cuda_dropout_f32": (c_int, [c_vp, c_vp, c_i64, c_u64, c_f32, c_i64]),
+    "chelis_cuda_dropout_mask": (c_int, [c_vp, c_i64, c_u64, c_f32, c_i64]),
+    "chelis_cuda_layer_norm_f32": (c_int, [c_vp, c_vp, c_vp, c_f32, c_vp, c_i64, c_i64]),
+    "chelis_cuda_softmax_rows_f32": (c_int, [c_vp, c_vp, c_i64, c_i64]),
+    "chelis_cuda_softmax_rows_bwd_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64]),
+    "chelis_cuda_chain_fwd": (c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "chelis_cuda_chain_bwd": (c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "chelis_cuda_cumsum_f64": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int]),
+    "chelis_cuda_cumsum_f32": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int]),
+    "chelis_cuda_portfolio_f64": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "chelis_cuda_mlp_step": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "chelis_chain_fwd_device": (c_int, [_PP, c_i32, _PP, c_i32]),
+    "chelis_chain_grad_device": (c_int, [_PP, c_i32, _PP, c_i32]),
+    "chelis_portfolio_device": (c_int, [_PP, c_i32, _PP, c_i32]),
+    "chelis_matmul_device": (c_int, [_PP, c_i32, _PP, c_i32]),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (and on first use declare) libchelis_cuda.so.  Raises if absent."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: run `python -m chelis_b200.build` (nvcc, sm_100a); "
+                "there is no CPU fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().chelis_cuda_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise ChelisCudaError(status, last_error())
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise on failure."""
+    check(getattr(load(), name)(*args))

@@ -1,0 +1,228 @@
+"""Host-side calls of the CUDA backend on torch-owned device memory.
+
+torch provides device memory and streams only; every computation is one of
+libchelis_cuda.so's kernels, reached through the C ABI (chelis_b200.lib).
+Each wrapper enqueues on torch's current CUDA stream and returns torch
+tensors.  Names and argument meanings follow the reference's operations
+(matmul, layer_norm, softmax, dropout, sum, max_reduce, count, cumsum).
+"""
+from __future__ import annotations
+
+import contextlib
+
+import torch
+
+from . import lib as L
+
+_initialised: set[int] = set()
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _prepare(*tensors: torch.Tensor) -> None:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("chelis_b200 ops take CUDA tensors (device memory)")
+        if not t.is_contiguous():
+            raise ValueError("chelis_b200 ops take contiguous tensors")
+        dev = t.device.index
+    if dev is None:
+        dev = torch.cuda.current_device()
+    if dev not in _initialised:
+        L.call("chelis_cuda_init", dev)
+        _initialised.add(dev)
+    L.load().chelis_cuda_set_stream(torch.cuda.current_stream(dev).cuda_stream)
+
+
+@contextlib.contextmanager
+def gemm_mode(mode: int):
+    lib = L.load()
+    old = lib.chelis_cuda_get_gemm_mode()
+    L.call("chelis_cuda_set_gemm_mode", mode)
+    try:
+        yield
+    finally:
+        L.call("chelis_cuda_set_gemm_mode", old)
+
+
+@contextlib.contextmanager
+def rows_mode(mode: int):
+    lib = L.load()
+    old = lib.chelis_cuda_get_rows_mode()
+    L.call("chelis_cuda_set_rows_mode", mode)
+    try:
+        yield
+    finally:
+        L.call("chelis_cuda_set_rows_mode", old)
+
+
+def device_status() -> None:
+    """Raise if a bounded device wait gave up since the last check."""
+    L.call("chelis_cuda_device_status")
+
+
+def launch_count() -> int:
+    return int(L.load().chelis_cuda_launch_count())
+
+
+# ---------------------------------------------------------------- matmul
+
+def matmul(a: torch.Tensor, b: torch.Tensor, trans_a: bool = False, trans_b: bool = False,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """op(A).op(B) for f32 (3xTF32 tensor cores, or the exact tree mode) or f64
+    (DMMA); rank-3 operands are a strided batch."""
+    if a.dtype != b.dtype or a.dtype not in (torch.float32, torch.float64):
+        raise ValueError("matmul takes two f32 or two f64 tensors")
+    batched = a.dim() == 3
+    if batched != (b.dim() == 3) or a.dim() not in (2, 3):
+        raise ValueError("matmul takes rank-2 or rank-3 operands of equal rank")
+    _prepare(a, b, out)
+    ar, ac = a.shape[-2:]
+    br, bc = b.shape[-2:]
+    m, k = (ac, ar) if trans_a else (ar, ac)
+    k2, n = (bc, br) if trans_b else (br, bc)
+    if k != k2:
+        raise ValueError(f"contraction extents differ: {k} vs {k2}")
+    batch = a.shape[0] if batched else 1
+    shape = (batch, m, n) if batched else (m, n)
+    if out is None:
+        out = torch.empty(shape, dtype=a.dtype, device=a.device)
+    name = "chelis_cuda_sgemm" if a.dtype == torch.float32 else "chelis_cuda_dgemm"
+    L.call(name, int(trans_a), int(trans_b), m, n, k, a.data_ptr(), ac, ar * ac,
+           b.data_ptr(), bc, br * bc, out.data_ptr(), n, m * n, batch)
+    return out
+
+
+# ---------------------------------------------------------------- rows
+
+def row_sum(x: torch.Tensor) -> torch.Tensor:
+    _prepare(x)
+    out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_row_sum_f32", x.data_ptr(), x.shape[0], x.shape[1], out.data_ptr())
+    return out
+
+
+def col_sum(x: torch.Tensor) -> torch.Tensor:
+    _prepare(x)
+    out = torch.empty(x.shape[1], dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_col_sum_f32", x.data_ptr(), x.shape[0], x.shape[1], out.data_ptr())
+    return out
+
+
+def row_max(x: torch.Tensor) -> torch.Tensor:
+    _prepare(x)
+    out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_row_max_f32", x.data_ptr(), x.shape[0], x.shape[1], out.data_ptr())
+    return out
+
+
+def count(x: torch.Tensor) -> int:
+    _prepare(x)
+    out = torch.empty(1, dtype=torch.int64, device=x.device)
+    L.call("chelis_cuda_count_bool", x.data_ptr(), x.numel(), out.data_ptr())
+    return int(out.item())
+
+
+def dropout(x: torch.Tensor, key: int, rate: float, index_base: int = 0) -> torch.Tensor:
+    _prepare(x)
+    y = torch.empty_like(x)
+    L.call("chelis_cuda_dropout_f32", x.data_ptr(), y.data_ptr(), x.numel(), key, rate, index_base)
+    return y
+
+
+def dropout_mask(n: int, key: int, rate: float, index_base: int = 0,
+                 device: torch.device | None = None) -> torch.Tensor:
+    keep = torch.empty(n, dtype=torch.uint8, device=device or "cuda")
+    _prepare(keep)
+    L.call("chelis_cuda_dropout_mask", keep.data_ptr(), n, key, rate, index_base)
+    return keep
+
+
+def layer_norm(x, gamma, beta, eps: float) -> torch.Tensor:
+    _prepare(x, gamma, beta)
+    y = torch.empty_like(x)
+    L.call("chelis_cuda_layer_norm_f32", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps,
+           y.data_ptr(), x.shape[0], x.shape[1])
+    return y
+
+
+def softmax_rows(x) -> torch.Tensor:
+    _prepare(x)
+    y = torch.empty_like(x)
+    L.call("chelis_cuda_softmax_rows_f32", x.data_ptr(), y.data_ptr(), x.shape[0], x.shape[1])
+    return y
+
+
+def softmax_rows_bwd(y, g) -> torch.Tensor:
+    _prepare(y, g)
+    dx = torch.empty_like(y)
+    L.call("chelis_cuda_softmax_rows_bwd_f32", y.data_ptr(), g.data_ptr(), dx.data_ptr(),
+           y.shape[0], y.shape[1])
+    return dx
+
+
+def chain_fwd(x, gamma, beta, eps: float, key: int, rate: float, index_base: int = 0,
+              want_stats: bool = False):
+    _prepare(x, gamma, beta)
+    rows, hidden = x.shape
+    rowsum = torch.empty(rows, dtype=torch.float32, device=x.device)
+    stats = torch.empty((rows, 4), dtype=torch.float32, device=x.device) if want_stats else None
+    L.call("chelis_cuda_chain_fwd", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps, key,
+           rate, rows, hidden, index_base, rowsum.data_ptr(), _ptr(stats))
+    return (rowsum, stats) if want_stats else rowsum
+
+
+def chain_bwd(x, gamma, beta, eps: float, key: int, rate: float, index_base: int = 0,
+              stats: torch.Tensor | None = None):
+    _prepare(x, gamma, beta, stats)
+    rows, hidden = x.shape
+    dx = torch.empty_like(x)
+    dg = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    db = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_chain_bwd", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps, key,
+           rate, rows, hidden, index_base, _ptr(stats), dx.data_ptr(), dg.data_ptr(),
+           db.data_ptr())
+    return dx, dg, db
+
+
+def cumsum(x: torch.Tensor, reverse: bool = False) -> torch.Tensor:
+    _prepare(x)
+    y = torch.empty_like(x)
+    name = "chelis_cuda_cumsum_f64" if x.dtype == torch.float64 else "chelis_cuda_cumsum_f32"
+    L.call(name, x.data_ptr(), y.data_ptr(), x.shape[0], x.shape[1], int(reverse))
+    return y
+
+
+# ---------------------------------------------------------------- programs
+
+def portfolio(r: torch.Tensor, w: torch.Tensor):
+    _prepare(r, w)
+    count_, t, a = r.shape
+    sigma = torch.empty((count_, a, a), dtype=torch.float64, device=r.device)
+    risk = torch.empty(count_, dtype=torch.float64, device=r.device)
+    cum = torch.empty((count_, t), dtype=torch.float64, device=r.device)
+    L.call("chelis_cuda_portfolio_f64", r.data_ptr(), w.data_ptr(), count_, t, a,
+           sigma.data_ptr(), risk.data_ptr(), cum.data_ptr())
+    return sigma, risk, cum
+
+
+def mlp_step(x, labels, w1, b1, w2, b2):
+    _prepare(x, labels, w1, b1, w2, b2)
+    batch, din = x.shape
+    dh = w1.shape[1]
+    dout = w2.shape[1]
+    dev = x.device
+    loss = torch.empty(1, dtype=torch.float32, device=dev)
+    dw1 = torch.empty_like(w1)
+    db1 = torch.empty_like(b1)
+    dw2 = torch.empty_like(w2)
+    db2 = torch.empty_like(b2)
+    L.call("chelis_cuda_mlp_step", x.data_ptr(), labels.data_ptr(), w1.data_ptr(),
+           b1.data_ptr(), w2.data_ptr(), b2.data_ptr(), batch, din, dh, dout, loss.data_ptr(),
+           dw1.data_ptr(), db1.data_ptr(), dw2.data_ptr(), db2.data_ptr())
+    return loss, dw1, db1, dw2, db2

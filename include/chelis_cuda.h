@@ -1,0 +1,299 @@
+/*
+ * chelis_cuda.h -- C ABI of the B200-native (sm_100a) CUDA backend for Chelis.
+ *
+ * This library fills the slot of the reference's GPU lane
+ * (crates/chelis-backend-hip).  Its entry points are the ones generated Chelis
+ * code and a future `chelis-backend-cuda` crate bind through `extern "C"`:
+ * plain pointers, sizes and the `chelis_gpu_tensor` descriptor, no C++ or
+ * torch types.  Each declaration names the reference interface it replaces
+ * (file:line within the reference project).
+ *
+ * Conventions
+ *  - Every function returning `int` returns CHELIS_CUDA_OK (0) on success or
+ *    a CHELIS_CUDA_ERR_* code; `chelis_cuda_last_error()` then holds a
+ *    message for the calling thread.  The reference aborts instead
+ *    (crates/chelis-backend-hip/runtime/chelis_hip_runtime.h:20-44); the
+ *    messages keep the reference's "numeric trap: <kind> in <op> at <dtype>"
+ *    wording where one applies.
+ *  - Work is enqueued on the calling thread's stream (chelis_cuda_set_stream;
+ *    default: the legacy default stream) of the current device.  Pointers
+ *    are device pointers unless a parameter name says `host`.
+ *  - Row-major layouts throughout, as in the reference's GEMM helpers.
+ */
+#ifndef CHELIS_CUDA_H
+#define CHELIS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- dtype ids: crates/chelis-runtime/include/chelis_runtime_dtype.h:6-18 ---- */
+#ifndef CHELIS_RUNTIME_DTYPE_H
+typedef uint8_t chelis_dtype;
+enum {
+    CHELIS_DTYPE_F32 = 0,
+    CHELIS_DTYPE_F64 = 1,
+    CHELIS_DTYPE_I32 = 2,
+    CHELIS_DTYPE_BOOL = 3,
+    CHELIS_DTYPE_I64 = 4,
+    CHELIS_DTYPE_BF16 = 5,
+    CHELIS_DTYPE_F16 = 6,
+    CHELIS_DTYPE_I8 = 7,
+    CHELIS_DTYPE_I16 = 8,
+    CHELIS_DTYPE_KEY = 9
+};
+#endif
+
+/* ---- device descriptor: crates/chelis-backend-hip/runtime/chelis_device_descriptor.h:8-18 ---- */
+#ifndef CHELIS_DEVICE_DESCRIPTOR_H
+typedef int64_t chelis_device_metadata;
+typedef int32_t chelis_device_rank;
+typedef struct {
+    void *data;
+    const int64_t *shape;
+    const int64_t *strides; /* in elements */
+    int64_t count;
+    int64_t byte_capacity;
+    int32_t rank;
+    chelis_dtype dtype;
+    uint8_t ownership; /* 0 = borrowed, 1 = owned */
+    uint8_t reserved[2];
+} chelis_gpu_tensor;
+#endif
+
+/* ---- status codes ---- */
+enum {
+    CHELIS_CUDA_OK = 0,
+    CHELIS_CUDA_ERR_DOMAIN = 1,      /* "numeric trap: domain ..." */
+    CHELIS_CUDA_ERR_OVERFLOW = 2,    /* "numeric trap: overflow ..." */
+    CHELIS_CUDA_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+    CHELIS_CUDA_ERR_UNSUPPORTED = 4, /* shape/dtype/layout this build does not admit */
+    CHELIS_CUDA_ERR_TIMEOUT = 5,     /* a bounded device wait gave up */
+    CHELIS_CUDA_ERR_NO_DEVICE = 6
+};
+
+/* GEMM arithmetic for f32 (matmul lowering, spec/05-risc-primitives.md:4962-5000). */
+enum {
+    CHELIS_CUDA_GEMM_3XTF32 = 0,   /* tcgen05 tensor cores, split-accumulate (default) */
+    CHELIS_CUDA_GEMM_EXACT_TREE = 1 /* CUDA cores, canonical tree over k: bit-identical to the C lane */
+};
+/* Fused row kernels: EXACT follows the C lane op for op (IEEE div/sqrt, no
+ * contraction, canonical trees); FAST rewrites divisions as reciprocal
+ * multiplies (tolerance parity only). */
+enum { CHELIS_CUDA_ROWS_EXACT = 0, CHELIS_CUDA_ROWS_FAST = 1 };
+
+/* =========================================================================
+ * Runtime
+ * replaces the per-call hiprtc compile + launch helpers
+ * (crates/chelis-backend-hip/runtime/chelis_hip_runtime.h:409-485): kernels
+ * are compiled ahead of time for sm_100a, so there is nothing to JIT.
+ * ========================================================================= */
+int chelis_cuda_version(void);
+const char *chelis_cuda_last_error(void);
+/* Select and initialise a device (the reference always uses hipGetDevice's
+ * current device: chelis_device_owner.cpp current_device()). */
+int chelis_cuda_init(int32_t device);
+/* Per-thread stream used by every later call on this thread (NULL = legacy default). */
+int chelis_cuda_set_stream(void *cuda_stream);
+void *chelis_cuda_get_stream(void);
+int chelis_cuda_synchronize(void);
+/* Read-and-clear the device error word (bounded-wait timeouts); returns
+ * CHELIS_CUDA_ERR_TIMEOUT if any kernel gave up since the last call.
+ * Synchronises the stream.  Replaces the debug failure flag readback of
+ * chelis_hip_runtime.h:487-524. */
+int chelis_cuda_device_status(void);
+/* Number of kernels this library launched since process start (all threads). */
+uint64_t chelis_cuda_launch_count(void);
+int chelis_cuda_set_gemm_mode(int mode);
+int chelis_cuda_get_gemm_mode(void);
+int chelis_cuda_set_rows_mode(int mode);
+int chelis_cuda_get_rows_mode(void);
+
+/* =========================================================================
+ * Device tensor owner
+ * crates/chelis-backend-hip/runtime/chelis_device_owner.h:16-24
+ * ========================================================================= */
+typedef struct chelis_device_tensor_owner chelis_device_tensor_owner;
+/* chelis_device_tensor_alloc(plan) (owner.h:16): the metadata plan is a Rust
+ * runtime object; this entry takes its dtype/rank/shape directly.  Owned,
+ * zero-filled, canonical row-major strides. */
+chelis_device_tensor_owner *chelis_device_tensor_alloc_shape(chelis_dtype dtype, int32_t rank,
+                                                             const int64_t *shape);
+/* chelis_device_tensor_borrow(plan, data, capacity) (owner.h:17). */
+chelis_device_tensor_owner *chelis_device_tensor_borrow_shape(chelis_dtype dtype, int32_t rank,
+                                                              const int64_t *shape, void *data,
+                                                              int64_t byte_capacity);
+/* owner.h:18 -- borrow a foreign packet (ownership must be 0). */
+chelis_device_tensor_owner *chelis_device_tensor_import(const chelis_gpu_tensor *packet);
+/* owner.h:19 */
+const chelis_gpu_tensor *chelis_device_tensor_view(const chelis_device_tensor_owner *owner);
+/* owner.h:20 */
+int32_t chelis_device_tensor_device(const chelis_device_tensor_owner *owner);
+/* owner.h:21 -- canonical-stride copy; strided sources gather in one kernel
+ * (the reference issues one hipMemcpy per element: owner.cpp:224-237). */
+chelis_device_tensor_owner *chelis_device_tensor_clone(const chelis_device_tensor_owner *source);
+/* owner.h:22 */
+void chelis_device_tensor_release(chelis_device_tensor_owner *owner);
+/* owner.h:23-24 (chelis_tensor is a Rust host object; these take bytes). */
+int chelis_device_tensor_copy_from_host_bytes(chelis_device_tensor_owner *destination,
+                                              const void *host, int64_t bytes);
+int chelis_device_tensor_copy_to_host_bytes(void *host, int64_t bytes,
+                                            const chelis_device_tensor_owner *source);
+
+/* =========================================================================
+ * GEMM helper ABI
+ * crates/chelis-backend-hip/runtime/chelis_hip_runtime.h:48-404
+ * (chelis_hipblas_*_row_major), dispatched from emit.rs:4718-4842.
+ * C = A.B, row-major, contiguous matrix slices (the reference's
+ * chelis_gpu_matrix_slices_contiguous precondition, :80-87); count == 0 is a
+ * no-op (emit.rs:4806).
+ * ========================================================================= */
+/* chelis_hipblas_sgemm_row_major (:48-78) */
+int chelis_cuda_sgemm_row_major(const chelis_gpu_tensor *a, const chelis_gpu_tensor *b,
+                                const chelis_gpu_tensor *out, int64_t m, int64_t n, int64_t k);
+/* chelis_hipblas_dgemm_row_major (:271-300) */
+int chelis_cuda_dgemm_row_major(const chelis_gpu_tensor *a, const chelis_gpu_tensor *b,
+                                const chelis_gpu_tensor *out, int64_t m, int64_t n, int64_t k);
+/* chelis_hipblas_sgemm_batched_row_major (:167-220): leading axes are the batch */
+int chelis_cuda_sgemm_batched_row_major(const chelis_gpu_tensor *a, const chelis_gpu_tensor *b,
+                                        const chelis_gpu_tensor *out, int64_t m, int64_t n,
+                                        int64_t k, int64_t batch_count);
+/* chelis_hipblas_sgemm_strided_batched_row_major (:222-267) */
+int chelis_cuda_sgemm_strided_batched_row_major(const chelis_gpu_tensor *a,
+                                                const chelis_gpu_tensor *b,
+                                                const chelis_gpu_tensor *out, int64_t m,
+                                                int64_t n, int64_t k, int64_t batch_count,
+                                                int64_t a_batch_stride, int64_t b_batch_stride,
+                                                int64_t out_batch_stride);
+/* chelis_hipblas_dgemm_batched_row_major (:302-355) */
+int chelis_cuda_dgemm_batched_row_major(const chelis_gpu_tensor *a, const chelis_gpu_tensor *b,
+                                        const chelis_gpu_tensor *out, int64_t m, int64_t n,
+                                        int64_t k, int64_t batch_count);
+/* chelis_hipblas_dgemm_strided_batched_row_major (:357-404) */
+int chelis_cuda_dgemm_strided_batched_row_major(const chelis_gpu_tensor *a,
+                                                const chelis_gpu_tensor *b,
+                                                const chelis_gpu_tensor *out, int64_t m,
+                                                int64_t n, int64_t k, int64_t batch_count,
+                                                int64_t a_batch_stride, int64_t b_batch_stride,
+                                                int64_t out_batch_stride);
+
+/* Raw-pointer GEMM used by the helpers above and by the AD programs:
+ * C[b] = op(A[b]) . op(B[b]) for b < batch, op = transpose when trans_* != 0.
+ * Leading dimensions are row strides in elements.  The matmul adjoint of
+ * [05-OP-51] (spec/05-risc-primitives.md:4247-4250) is this call with a
+ * transposed operand.  Mode CHELIS_CUDA_GEMM_3XTF32 keeps split operand
+ * copies in stream-ordered scratch for the duration of the call. */
+int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const float *a,
+                      int64_t lda, int64_t stride_a, const float *b, int64_t ldb,
+                      int64_t stride_b, float *c, int64_t ldc, int64_t stride_c, int64_t batch);
+int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
+                      int64_t lda, int64_t stride_a, const double *b, int64_t ldb,
+                      int64_t stride_b, double *c, int64_t ldc, int64_t stride_c, int64_t batch);
+/* 3xTF32 in two halves, for operands reused across many products (weights):
+ * split op(X) (rows x k, op = transpose when trans != 0) into K-major hi/lo
+ * copies of rows x kp floats per batch item (kp = k rounded up to 32, zero
+ * padded), then multiply pre-split operands: C[b] = A[b] . B[b]^T where A is
+ * m x kp and B is n x kp (B split from op(B)^T, i.e. with the transposed
+ * flag of the row-major product).  No reference counterpart: hipBLAS has no
+ * split form (chelis_hip_runtime.h:48-78 is the single-call slot). */
+int chelis_cuda_tf32x3_split(int trans, int64_t rows, int64_t k, const float *src, int64_t ld,
+                             int64_t stride, int64_t batch, float *hi, float *lo);
+int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t batch,
+                                      const float *a_hi, const float *a_lo, const float *b_hi,
+                                      const float *b_lo, float *c, int64_t ldc, int64_t stride_c);
+
+/* =========================================================================
+ * Fused elementwise / reduction groups and their adjoints.
+ * The reference JIT-compiles per-DAG kernel strings (kernels.rs:2175-2468,
+ * fused_elementwise / reduce_fused; row reductions :1703-2014) and rejects
+ * Softmax, sqrt and Dropout on HIP (emit.rs:1572-1583, 2763-2775).
+ * ========================================================================= */
+/* [05-OP-30] sum over the last axis / first axis of a [rows, cols] f32 tensor,
+ * canonical adjacent-pair tree (kernels.rs:1703-1755 left-folds instead). */
+int chelis_cuda_row_sum_f32(const float *x, int64_t rows, int64_t cols, float *out);
+int chelis_cuda_col_sum_f32(const float *x, int64_t rows, int64_t cols, float *out);
+/* [05-OP-12] max_reduce over the last axis (first NaN wins). kernels.rs:1802 */
+int chelis_cuda_row_max_f32(const float *x, int64_t rows, int64_t cols, float *out);
+/* [05-OP-29] exact i64 count of a bool tensor (kernels.rs:375-520). */
+int chelis_cuda_count_bool(const uint8_t *x, int64_t n, int64_t *out_device);
+/* [05-OP-37] keyed dropout / DropoutReplay on a flat f32 tensor whose first
+ * element has flat index `index_base` (dtype_semantics.rs:4256-4280). */
+int chelis_cuda_dropout_f32(const float *x, float *y, int64_t n, uint64_t key, float rate,
+                            int64_t index_base);
+/* Keep mask (1 = kept) of the same draw; bit-exact with the C lane. */
+int chelis_cuda_dropout_mask(uint8_t *keep, int64_t n, uint64_t key, float rate,
+                             int64_t index_base);
+/* layer_norm over the last axis (tier2.rs:1248-1375). */
+int chelis_cuda_layer_norm_f32(const float *x, const float *gamma, const float *beta, float eps,
+                               float *y, int64_t rows, int64_t hidden);
+/* softmax over the last axis (tier2.rs:1079-1180) and its adjoint
+ * y * (g - sum(g * y)) (grad.rs:2248-2280). */
+int chelis_cuda_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols);
+int chelis_cuda_softmax_rows_bwd_f32(const float *y, const float *g, float *dx, int64_t rows,
+                                     int64_t cols);
+/* The fused chain layer_norm -> softmax -> dropout -> row sum over a
+ * [rows, hidden] f32 tensor.  `row_stats` (optional, 4 floats per row:
+ * mean, sqrt(var+eps), softmax max, softmax denominator) is written for the
+ * adjoint to reuse. */
+int chelis_cuda_chain_fwd(const float *x, const float *gamma, const float *beta, float eps,
+                          uint64_t key, float rate, int64_t rows, int64_t hidden,
+                          int64_t index_base, float *rowsum, float *row_stats);
+/* Adjoint of loss = sum(rowsum) w.r.t. x, gamma and beta.  With row_stats
+ * NULL the forward statistics are recomputed.  dgamma/dbeta are complete
+ * (reduced over all rows) on return. */
+int chelis_cuda_chain_bwd(const float *x, const float *gamma, const float *beta, float eps,
+                          uint64_t key, float rate, int64_t rows, int64_t hidden,
+                          int64_t index_base, const float *row_stats, float *dx, float *dgamma,
+                          float *dbeta);
+/* Cumsum ([05-OP-53], spec/05-risc-primitives.md:4310-4325) along the last
+ * axis of [lanes, len]; reverse != 0 is the decreasing scan (the adjoint).
+ * kernels.rs:2793-2895 */
+int chelis_cuda_cumsum_f64(const double *x, double *y, int64_t lanes, int64_t len, int reverse);
+int chelis_cuda_cumsum_f32(const float *x, float *y, int64_t lanes, int64_t len, int reverse);
+
+/* =========================================================================
+ * vmap'd programs (vectorize_axis0, crates/chelis-ir-core/src/vmap.rs:9-56)
+ * ========================================================================= */
+/* Covariance / risk per portfolio, f64: r [count, t, a], w [count, a] ->
+ * sigma [count, a, a] = (R-mean)^T (R-mean) / (t-1), risk [count] =
+ * sqrt(w^T sigma w), cum [count, t] = cumsum_t(R.w). */
+int chelis_cuda_portfolio_f64(const double *r, const double *w, int64_t count, int64_t t,
+                              int64_t a, double *sigma, double *risk, double *cum);
+
+/* 2-layer MLP forward + adjoint (matmul, add, relu, softmax cross-entropy,
+ * mean; grads w.r.t. w1, b1, w2, b2).  labels are i64 class ids. */
+int chelis_cuda_mlp_step(const float *x, const int64_t *labels, const float *w1,
+                         const float *b1, const float *w2, const float *b2, int64_t batch,
+                         int64_t din, int64_t dh, int64_t dout, float *loss, float *dw1,
+                         float *db1, float *dw2, float *db2);
+
+/* =========================================================================
+ * Generated-entry device ABI (emit.rs:838-958, `f_device`): inputs borrowed,
+ * outputs newly allocated owners the caller releases.  One entry per program
+ * this backend ships whole.
+ * ========================================================================= */
+/* inputs: x[rows,hidden], gamma[hidden], beta[hidden]; outputs: rowsum[rows].
+ * eps = 1e-5, key = 42, rate = 0.1 are the program's constants. */
+int chelis_chain_fwd_device(const chelis_device_tensor_owner *const *inputs,
+                            chelis_device_rank n_in, chelis_device_tensor_owner **outputs,
+                            chelis_device_rank n_out);
+/* inputs: x, gamma, beta; outputs: dx, dgamma, dbeta */
+int chelis_chain_grad_device(const chelis_device_tensor_owner *const *inputs,
+                             chelis_device_rank n_in, chelis_device_tensor_owner **outputs,
+                             chelis_device_rank n_out);
+/* inputs: r[count,t,a], w[count,a]; outputs: sigma, risk, cum */
+int chelis_portfolio_device(const chelis_device_tensor_owner *const *inputs,
+                            chelis_device_rank n_in, chelis_device_tensor_owner **outputs,
+                            chelis_device_rank n_out);
+/* inputs: a[m,k], b[k,n] (f32 or f64, batched when rank 3); outputs: c */
+int chelis_matmul_device(const chelis_device_tensor_owner *const *inputs,
+                         chelis_device_rank n_in, chelis_device_tensor_owner **outputs,
+                         chelis_device_rank n_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,105 @@
+/*
+ * chelis_oracle.h -- CPU restatement of the Chelis C backend's numeric
+ * semantics for the tensor-DAG hot path (matmul, sum/max reductions, layer
+ * norm, softmax, keyed dropout, cumsum, cross-entropy and their adjoints).
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the CUDA
+ * backend.  Only the test suite, __graft_entry__.smoke() and the cpu_baseline
+ * leg of bench.py may load it.  The product library (libchelis_cuda.so)
+ * never links or calls it.
+ *
+ * Every function cites the reference file:line whose behaviour it restates.
+ * Floating point follows the C lane's build: -O2 -ffp-contract=off
+ * -fno-fast-math (crates/chelis-backend-c/src/toolchain.rs:235-246), so
+ * every addition and multiplication is a separately rounded IEEE operation.
+ * Transcendentals come from the reference's vendored CORE-MATH
+ * (crates/chelis-crmath/csrc/crmath_ffi.c:15-45), built by oracle/Makefile
+ * into oracle/_ref/.
+ */
+#ifndef CHELIS_ORACLE_H
+#define CHELIS_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- keyed randomness: crates/chelis-numeric-core/src/dtype_semantics.rs:4508-4540 ---- */
+uint64_t orc_splitmix64(uint64_t v);
+uint64_t orc_word(uint64_t key, uint64_t index);
+uint64_t orc_derive(uint64_t key, uint64_t j);
+double orc_unit(uint64_t key, uint64_t index);
+
+/* ---- canonical adjacent-pair tree: spec/05-risc-primitives.md:515-531 ---- */
+float orc_tree_sum_f32(const float *x, int64_t n, int64_t stride);
+double orc_tree_sum_f64(const double *x, int64_t n, int64_t stride);
+/* sum over axis 1 of a [rows, cols] row-major tensor -> out[rows] */
+void orc_row_sum_f32(const float *x, int64_t rows, int64_t cols, float *out);
+/* sum over axis 0 of a [rows, cols] row-major tensor -> out[cols] */
+void orc_col_sum_f32(const float *x, int64_t rows, int64_t cols, float *out);
+void orc_row_max_f32(const float *x, int64_t rows, int64_t cols, float *out);
+int64_t orc_count_bool(const uint8_t *x, int64_t n);
+
+/* ---- matmul = Sum(Mul(Expand A, Expand B)) over k, tree in increasing k:
+ *      crates/chelis-backend-c/src/emit.rs:8431-8640 ---- */
+void orc_sgemm(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+               int64_t row_begin, int64_t row_end);
+void orc_dgemm(const double *a, const double *b, double *c, int64_t m, int64_t n, int64_t k,
+               int64_t row_begin, int64_t row_end);
+/* general strides: C[i,j] = tree_k A[i*sa0 + k*sa1] * B[k*sb0 + j*sb1] */
+void orc_sgemm_strided(const float *a, int64_t sa0, int64_t sa1, const float *b, int64_t sb0,
+                       int64_t sb1, float *c, int64_t m, int64_t n, int64_t k);
+void orc_dgemm_strided(const double *a, int64_t sa0, int64_t sa1, const double *b, int64_t sb0,
+                       int64_t sb1, double *c, int64_t m, int64_t n, int64_t k);
+
+/* ---- dropout: PreparedDropout::apply, dtype_semantics.rs:4256-4280 ---- */
+void orc_dropout_f32(const float *x, float *y, int64_t n, uint64_t key, float rate,
+                     int64_t index_base);
+void orc_dropout_mask(uint8_t *keep, int64_t n, uint64_t key, float rate, int64_t index_base);
+
+/* ---- row ops (tier2.rs:1079-1375, spec/05-risc-primitives.md:5021-5093) ---- */
+void orc_layer_norm_f32(const float *x, const float *gamma, const float *beta, float eps,
+                        float *y, int64_t rows, int64_t hidden);
+void orc_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols);
+void orc_softmax_rows_bwd_f32(const float *y, const float *g, float *dx, int64_t rows,
+                              int64_t cols);
+
+/* ---- the fused chain: layer_norm -> softmax -> dropout -> row sum (forward),
+ *      and its reverse-mode adjoint for loss = sum of the row sums ---- */
+void orc_chain_fwd(const float *x, const float *gamma, const float *beta, float eps,
+                   uint64_t key, float rate, int64_t rows, int64_t hidden, int64_t index_base,
+                   float *rowsum);
+void orc_chain_bwd(const float *x, const float *gamma, const float *beta, float eps,
+                   uint64_t key, float rate, int64_t rows, int64_t hidden, int64_t index_base,
+                   float *dx, float *dgamma_rows, float *dbeta_rows);
+
+/* ---- cumsum: spec/05-risc-primitives.md:4310-4325 ---- */
+void orc_cumsum_f64(const double *x, double *y, int64_t lanes, int64_t len, int reverse);
+void orc_cumsum_f32(const float *x, float *y, int64_t lanes, int64_t len, int reverse);
+
+/* ---- vmap'd covariance / risk (f64) ---- */
+void orc_portfolio(const double *r, const double *w, int64_t count, int64_t t, int64_t a,
+                   double *sigma, double *risk, double *cum);
+
+/* ---- 2-layer MLP forward + adjoint ---- */
+void orc_mlp_step(const float *x, const int64_t *labels, const float *w1, const float *b1,
+                  const float *w2, const float *b2, int64_t batch, int64_t din, int64_t dh,
+                  int64_t dout, float *loss, float *dw1, float *db1, float *dw2, float *db2);
+
+/* ---- single finalized f32 operations ([04-NUM-2]) ---- */
+float orc_add_f32(float a, float b);
+float orc_mul_f32(float a, float b);
+float orc_div_f32(float a, float b);
+float orc_sqrt_f32(float a);
+
+/* ---- CORE-MATH passthroughs for pinning against the reference fixtures ---- */
+float orc_expf(float x);
+float orc_logf(float x);
+float orc_erfcf(float x);
+double orc_exp(double x);
+double orc_sqrt(double x);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

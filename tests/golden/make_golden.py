@@ -1,0 +1,51 @@
+"""Regenerate the golden fixtures under tests/golden/ from the reference tree.
+
+Run in a container where the reference is mounted (default /root/reference,
+or pass its path).  The outputs are committed; tests never read the reference
+tree at run time.
+
+* crmath_f32.txt -- the f32 exp / log / erfc rows of the reference's CORE-MATH
+  canary fixture (crates/chelis-crmath/tests/fixtures/canary.txt): function,
+  input bits, expected bits.  They pin the oracle's transcendentals.
+* ieee_f32.txt -- the f32 add / mul / div / sqrt rows of
+  crates/chelis-crmath/tests/fixtures/profile_obligations.txt: primitive,
+  expected bits, operand bits.  They pin the oracle's finalized arithmetic
+  (round to nearest even, subnormals kept, canonical NaN).
+"""
+import os
+import sys
+
+REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+FIX = os.path.join(REF, "crates/chelis-crmath/tests/fixtures")
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def rows(path, keep):
+    with open(path) as f:
+        for line in f:
+            line = line.split("#", 1)[0].strip()
+            if not line:
+                continue
+            parts = line.split()
+            if keep(parts):
+                yield parts
+
+
+def main():
+    canary = list(rows(os.path.join(FIX, "canary.txt"),
+                       lambda p: p[1] == "f32" and p[0] in ("exp", "log", "erfc")))
+    with open(os.path.join(OUT, "crmath_f32.txt"), "w") as f:
+        f.write("# function input-bits expected-bits (from the reference CORE-MATH canary fixture)\n")
+        for p in canary:
+            f.write(f"{p[0]} {p[2]} {p[3]}\n")
+    ieee = list(rows(os.path.join(FIX, "profile_obligations.txt"),
+                     lambda p: p[1] == "f32" and p[0] in ("add", "mul", "div", "sqrt")))
+    with open(os.path.join(OUT, "ieee_f32.txt"), "w") as f:
+        f.write("# primitive expected-bits operand-bits... (from the reference profile obligations)\n")
+        for p in ieee:
+            f.write(" ".join([p[0]] + p[2:]) + "\n")
+    print(len(canary), len(ieee))
+
+
+if __name__ == "__main__":
+    main()

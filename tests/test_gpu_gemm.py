@@ -1,0 +1,143 @@
+"""GEMM parity on the GPU against the oracle (canonical tree over k).
+
+Tolerances (stated per the north star: f32 rel <= 1e-5, f64 rel <= 1e-12
+after reductions) are componentwise and scaled by the reduction's own
+magnitude:  |C - C_ref|_ij <= rtol * (|A| . |B|)_ij.  That is the standard
+bound of a length-k dot product; it does not blow up where C_ij cancels to
+near zero.  The exact-tree mode is compared bit for bit.
+"""
+import numpy as np
+import pytest
+
+from chelis_b200 import lib as L
+from chelis_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 1, 1), (17, 33, 45), (128, 256, 32), (300, 500, 700), (512, 512, 512),
+          (129, 257, 1000), (64, 8, 4096)]
+
+
+def _rel_err(c, ref, a, b, ta=False, tb=False):
+    import torch
+    A = torch.as_tensor(a, dtype=torch.float64).abs()
+    B = torch.as_tensor(b, dtype=torch.float64).abs()
+    A = A.T if ta else A
+    B = B.T if tb else B
+    bound = (A @ B).numpy()
+    err = np.abs(c.astype(np.float64) - ref.astype(np.float64))
+    return float((err / np.maximum(bound, 1e-300)).max())
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_sgemm_3xtf32_matches_oracle(cuda, orc, m, n, k):
+    import torch
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=m + n + k)
+    c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    cuda.device_status()
+    ref = orc.gemm(a, b)
+    assert _rel_err(c, ref, a, b) <= 1e-5
+
+
+@pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
+def test_sgemm_transposed_operands(cuda, orc, ta, tb):
+    import torch
+    m, n, k = 190, 130, 310
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=5)
+    at = a.T.copy() if ta else a
+    bt = b.T.copy() if tb else b
+    c = cuda.matmul(torch.from_numpy(at).cuda(), torch.from_numpy(bt).cuda(), ta, tb).cpu().numpy()
+    ref = orc.gemm(a, b)
+    assert _rel_err(c, ref, a, b) <= 1e-5
+
+
+def test_sgemm_batched_matches_oracle(cuda, orc):
+    import torch
+    a, b = W.gemm_inputs(96, 160, 200, np.float32, seed=2, batch=5)
+    c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    for i in range(5):
+        assert _rel_err(c[i], orc.gemm(a[i], b[i]), a[i], b[i]) <= 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (37, 45, 33), (64, 96, 100), (128, 64, 1025)])
+def test_sgemm_exact_tree_is_bit_exact(cuda, orc, m, n, k):
+    import torch
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=k)
+    with cuda.gemm_mode(L.GEMM_EXACT_TREE):
+        c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    ref = orc.gemm(a, b)
+    assert (c.view(np.uint32) == ref.view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_dgemm_matches_oracle(cuda, orc, m, n, k):
+    import torch
+    a, b = W.gemm_inputs(m, n, k, np.float64, seed=m * 3 + k)
+    c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    ref = orc.gemm(a, b)
+    assert _rel_err(c, ref, a, b) <= 1e-12
+
+
+def test_dgemm_transposed_and_batched(cuda, orc):
+    import torch
+    a, b = W.gemm_inputs(70, 90, 130, np.float64, seed=8, batch=3)
+    c = cuda.matmul(torch.from_numpy(a.transpose(0, 2, 1).copy()).cuda(),
+                    torch.from_numpy(b).cuda(), True, False).cpu().numpy()
+    for i in range(3):
+        assert _rel_err(c[i], orc.gemm(a[i], b[i]), a[i], b[i]) <= 1e-12
+
+
+def test_dgemm_exact_tree_is_bit_exact(cuda, orc):
+    import torch
+    a, b = W.gemm_inputs(50, 70, 300, np.float64, seed=4)
+    with cuda.gemm_mode(L.GEMM_EXACT_TREE):
+        c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert (c.view(np.uint64) == orc.gemm(a, b).view(np.uint64)).all()
+
+
+@pytest.mark.parametrize("dtype,rtol", [(np.float32, 1e-5), (np.float64, 1e-12)])
+def test_full_size_8192_sampled_rows(cuda, orc, dtype, rtol):
+    """BASELINE config 2 at its largest size: every output computed on the
+    GPU, a bounded sample of rows checked against the oracle."""
+    import torch
+    n = 8192
+    a, b = W.gemm_inputs(n, n, n, dtype, seed=1)
+    c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda())
+    torch.cuda.synchronize()
+    cuda.device_status()
+    rows = [0, 1, 127, 128, 4095, 8191]
+    for r in rows:
+        ref = orc.gemm(a[r:r + 1], b)
+        got = c[r:r + 1].cpu().numpy()
+        assert _rel_err(got, ref, a[r:r + 1], b) <= rtol, r
+
+
+def test_row_major_helper_abi(cuda, orc):
+    """chelis_cuda_sgemm_row_major through chelis_gpu_tensor descriptors
+    (the chelis_hipblas_sgemm_row_major slot)."""
+    import ctypes
+    import torch
+    m, n, k = 33, 65, 47
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=12)
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    tc = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    keep = []
+
+    def desc(t):
+        shape = (ctypes.c_int64 * 2)(*t.shape)
+        strides = (ctypes.c_int64 * 2)(*t.stride())
+        keep.extend([shape, strides])
+        d = L.GpuTensor()
+        d.data, d.shape, d.strides = t.data_ptr(), shape, strides
+        d.count, d.byte_capacity, d.rank, d.dtype = t.numel(), t.numel() * 4, 2, L.DTYPE_F32
+        return d
+
+    cuda._prepare(ta)
+    da, db, dc = desc(ta), desc(tb), desc(tc)
+    L.call("chelis_cuda_sgemm_row_major", ctypes.byref(da), ctypes.byref(db), ctypes.byref(dc), m, n, k)
+    torch.cuda.synchronize()
+    assert _rel_err(tc.cpu().numpy(), orc.gemm(a, b), a, b) <= 1e-5
+    # non-contiguous slices are rejected like the reference's precondition
+    bad = desc(tb)
+    bad.strides = (ctypes.c_int64 * 2)(1, k)
+    assert L.load().chelis_cuda_sgemm_row_major(ctypes.byref(da), ctypes.byref(bad), ctypes.byref(dc), m, n, k) == 1
