@@ -60,10 +60,37 @@ int sm_count() {
     return g_sm_count[d];
 }
 
+// The library's own stream-ordered pool per device.  Freed scratch stays
+// mapped (release threshold = unlimited) so repeated calls reuse it instead
+// of re-mapping physical memory at every synchronisation point; the
+// process's default pool is left as it is.
+static int library_pool(cudaMemPool_t *out) {
+    static cudaMemPool_t pools[64] = {};
+    int d = 0;
+    CHELIS_TRY(check_cuda(cudaGetDevice(&d), "cudaGetDevice"));
+    if (d < 0 || d >= 64) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "device index %d", d);
+    if (!pools[d]) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = d;
+        cudaMemPool_t pool;
+        CHELIS_TRY(check_cuda(cudaMemPoolCreate(&pool, &props), "cudaMemPoolCreate"));
+        uint64_t threshold = UINT64_MAX;
+        CHELIS_TRY(check_cuda(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold),
+                              "cudaMemPoolSetAttribute"));
+        pools[d] = pool;
+    }
+    *out = pools[d];
+    return CHELIS_CUDA_OK;
+}
+
 int scratch_alloc(void **ptr, size_t bytes, cudaStream_t stream) {
     *ptr = nullptr;
     if (bytes == 0) return CHELIS_CUDA_OK;
-    return check_cuda(cudaMallocAsync(ptr, bytes, stream), "cudaMallocAsync(scratch)");
+    cudaMemPool_t pool;
+    CHELIS_TRY(library_pool(&pool));
+    return check_cuda(cudaMallocFromPoolAsync(ptr, bytes, pool, stream), "cudaMallocFromPoolAsync(scratch)");
 }
 
 void scratch_free(void *ptr, cudaStream_t stream) {
