@@ -8,3 +8,4 @@
 #include "portfolio.cu"
 #include "mlp.cu"
 #include "abi.cu"
+#include "chain_noalloc.cu"

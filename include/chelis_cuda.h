@@ -248,6 +248,22 @@ int chelis_cuda_chain_bwd(const float *x, const float *gamma, const float *beta,
                           uint64_t key, float rate, int64_t rows, int64_t hidden,
                           int64_t index_base, const float *row_stats, float *dx, float *dgamma,
                           float *dbeta);
+/* chelis_cuda_chain_bwd for callers that cannot let the library allocate
+ * device memory (a host that budgets its whole device arena up front and
+ * hands out every buffer itself, or one that bans driver allocation while it
+ * runs).  No counterpart in the reference.  Same arguments and results as
+ * chelis_cuda_chain_bwd; its scratch is one 10 MiB device array per GPU,
+ * held until the process exits.  Limits: hidden <= 4096 (larger rows return
+ * CHELIS_CUDA_ERR_UNSUPPORTED).  Calls that overlap on the GPU share that
+ * array and race; order them.  The first call on a device resolves the
+ * array's address with that device current: make it before any stream
+ * capture.  dgamma / dbeta use a different CTA grouping than
+ * chelis_cuda_chain_bwd, so they agree with it within tolerance, dx bit for
+ * bit. */
+int chelis_cuda_chain_bwd_noalloc(const float *x, const float *gamma, const float *beta,
+                                  float eps, uint64_t key, float rate, int64_t rows,
+                                  int64_t hidden, int64_t index_base, const float *row_stats,
+                                  float *dx, float *dgamma, float *dbeta);
 /* Cumsum ([05-OP-53], spec/05-risc-primitives.md:4310-4325) along the last
  * axis of [lanes, len]; reverse != 0 is the decreasing scan (the adjoint).
  * kernels.rs:2793-2895 */
