@@ -79,7 +79,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -188,10 +188,16 @@ def bench_gemm_headline(args, world, rank, peaks):
     for _ in range(args.warmup):
         step()
     ops.device_status()
-    l0 = ops.launch_count()
     with ClockSampler(torch.cuda.current_device()) as clk:
+        # the sampler needs ~1 s to start; keep the GPU busy with untimed
+        # products until it reports, then time exactly args.steps
+        t0 = time.time()
+        while not clk.lines and time.time() - t0 < 5.0:
+            step()
+            torch.cuda.synchronize()
+        l0 = ops.launch_count()
         ms = time_region(step, args.steps, world)
-    launches = ops.launch_count() - l0
+        launches = ops.launch_count() - l0
     ops.device_status()
     value = world * flops * args.steps / (ms * 1e-3) / 1e12
 
@@ -282,12 +288,13 @@ def bench_extras(args, peaks):
     state = {}
 
     def fwd():
-        state["rs"], state["st"] = ops.chain_fwd(x, g, be, 1e-5, 42, 0.1, want_stats=True)
+        state["rs"], state["saved"] = ops.chain_fwd_save(x, g, be, 1e-5, 42, 0.1)
 
     fms = timed(fwd, 10)
-    bms = timed(lambda: ops.chain_bwd(x, g, be, 1e-5, 42, 0.1, 0, state["st"]), 10)
-    fbytes = rows * hidden * 4 + 2 * hidden * 4 + rows * 4 + rows * 16
-    bbytes = 2 * rows * hidden * 4 + 4 * hidden * 4 + rows * 16
+    bms = timed(lambda: ops.chain_bwd_saved(x, g, be, 1e-5, 0.1, state["saved"]), 10)
+    saved = state["saved"].numel() * 4
+    fbytes = rows * hidden * 4 + 2 * hidden * 4 + rows * 4 + saved
+    bbytes = 2 * rows * hidden * 4 + 4 * hidden * 4 + saved
     out["chain_fwd"] = {"gbs": round(fbytes / fms / 1e6, 1), "ms": round(fms, 4),
                         "frac_hbm": round(fbytes / fms / 1e6 / hbm, 3)}
     out["chain_bwd"] = {"gbs": round(bbytes / bms / 1e6, 1), "ms": round(bms, 4),
@@ -364,7 +371,7 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="chelis", choices=["chelis", "reference"])
     ap.add_argument("--n", type=int, default=N_HEADLINE)

@@ -258,6 +258,39 @@ __global__ void split_kernel(const float *__restrict__ src, int64_t rows, int64_
     }
 }
 
+// Row-contiguous source (sk == 1): a plain streaming split, one float4 in
+// and two float4 out per thread step; columns [k, kp) are written as zeros.
+__global__ void split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t k,
+                                  int64_t sr, int64_t sb, int64_t kp, float *__restrict__ hi,
+                                  float *__restrict__ lo) {
+    const int64_t b = blockIdx.y;
+    const float *s = src + b * sb;
+    float *h = hi + b * rows * kp;
+    float *l = lo + b * rows * kp;
+    const int64_t q = kp / 4;  // float4 per output row
+    const bool vec = (k % 4 == 0) && (sr % 4 == 0) && ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * q;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / q, c0 = (i % q) * 4;
+        float x[4];
+        if (vec && c0 + 3 < k) {
+            const float4 v = __ldcs(reinterpret_cast<const float4 *>(s + r * sr + c0));
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) x[j] = (c0 + j < k) ? s[r * sr + c0 + j] : 0.0f;
+        }
+        float xh[4], xl[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            xh[j] = rna_tf32(x[j]);
+            xl[j] = isfinite(x[j]) ? rna_tf32(__fsub_rn(x[j], xh[j])) : 0.0f;
+        }
+        *reinterpret_cast<float4 *>(h + r * kp + c0) = make_float4(xh[0], xh[1], xh[2], xh[3]);
+        *reinterpret_cast<float4 *>(l + r * kp + c0) = make_float4(xl[0], xl[1], xl[2], xl[3]);
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -457,6 +490,29 @@ template int launch_exact_gemm<double>(int, int, int64_t, int64_t, int64_t, cons
                                        int64_t, int64_t, const double *, int64_t, int64_t,
                                        double *, int64_t, int64_t, int64_t, cudaStream_t);
 
+// Split rows x k of a source (element (r, kk) at src[b*sb + r*sr + kk*sk])
+// into K-major hi / lo copies of kp columns per row.
+int launch_split(const float *src, int64_t rows, int64_t k, int64_t sr, int64_t sk, int64_t sb,
+                 int64_t batch, int64_t kp, float *hi, float *lo, cudaStream_t s) {
+    using namespace tf32x3;
+    if (sk == 1) {
+        int64_t blocks = (rows * (kp / 4) + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+        if (blocks > cap) blocks = cap;
+        split_rows_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batch)), 256,
+                            0, s>>>(src, rows, k, sr, sb, kp, hi, lo);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("split_rows_kernel");
+        return CHELIS_CUDA_OK;
+    }
+    dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((rows + 31) / 32),
+              static_cast<unsigned>(batch));
+    split_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, k, sr, sk, sb, kp, hi, lo);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("split_kernel");
+    return CHELIS_CUDA_OK;
+}
+
 // Split both operands into caller-provided scratch and run the tcgen05
 // kernel.  `scratch` must hold 2 * (m + n) * kp floats per batch item.
 int sgemm_3xtf32_with_scratch(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
@@ -470,24 +526,12 @@ int sgemm_3xtf32_with_scratch(int trans_a, int trans_b, int64_t m, int64_t n, in
     float *bhi = alo + batch * m * kp;
     float *blo = bhi + batch * n * kp;
     // op(A)[i, kk] = a[i*lda + kk] (no trans) or a[kk*lda + i] (trans)
-    {
-        int64_t sr = trans_a ? 1 : lda, sk = trans_a ? lda : 1;
-        dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((m + 31) / 32),
-                  static_cast<unsigned>(batch));
-        split_kernel<<<grid, dim3(32, 8), 0, s>>>(a, m, k, sr, sk, stride_a, kp, ahi, alo);
-        g_launches++;
-        CHELIS_LAUNCH_CHECK("split_kernel(A)");
-    }
+    CHELIS_TRY(launch_split(a, m, k, trans_a ? 1 : lda, trans_a ? lda : 1, stride_a, batch, kp,
+                            ahi, alo, s));
     // op(B)[kk, j] -> K-major rows j: element (j, kk) = b[kk*ldb + j] (no
     // trans) or b[j*ldb + kk] (trans)
-    {
-        int64_t sr = trans_b ? ldb : 1, sk = trans_b ? 1 : ldb;
-        dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((n + 31) / 32),
-                  static_cast<unsigned>(batch));
-        split_kernel<<<grid, dim3(32, 8), 0, s>>>(b, n, k, sr, sk, stride_b, kp, bhi, blo);
-        g_launches++;
-        CHELIS_LAUNCH_CHECK("split_kernel(B)");
-    }
+    CHELIS_TRY(launch_split(b, n, k, trans_b ? ldb : 1, trans_b ? 1 : ldb, stride_b, batch, kp,
+                            bhi, blo, s));
     CUtensorMap mahi, malo, mbhi, mblo;
     CHELIS_TRY(make_kmajor_map(&mahi, ahi, batch * m, kp, BM));
     CHELIS_TRY(make_kmajor_map(&malo, alo, batch * m, kp, BM));
@@ -547,14 +591,8 @@ extern "C" int chelis_cuda_tf32x3_split(int trans, int64_t rows, int64_t k, cons
     if (rows == 0 || batch == 0) return CHELIS_CUDA_OK;
     const int64_t kp = (k + tf32x3::BK - 1) / tf32x3::BK * tf32x3::BK;
     if (kp == 0) return CHELIS_CUDA_OK;
-    const int64_t sr = trans ? 1 : ld, sk = trans ? ld : 1;
-    dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((rows + 31) / 32),
-              static_cast<unsigned>(batch));
-    tf32x3::split_kernel<<<grid, dim3(32, 8), 0, current_stream()>>>(src, rows, k, sr, sk, stride,
-                                                                     kp, hi, lo);
-    g_launches++;
-    CHELIS_LAUNCH_CHECK("split_kernel");
-    return CHELIS_CUDA_OK;
+    return launch_split(src, rows, k, trans ? 1 : ld, trans ? ld : 1, stride, batch, kp, hi, lo,
+                        current_stream());
 }
 
 extern "C" int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t batch,

@@ -5,6 +5,7 @@
 #include "gemm_tf32x3.cu"
 #include "gemm_f64.cu"
 #include "rows.cu"
+#include "chain.cu"
 #include "portfolio.cu"
 #include "mlp.cu"
 #include "abi.cu"

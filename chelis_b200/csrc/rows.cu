@@ -174,215 +174,6 @@ __device__ __forceinline__ float canon(float x) {
     return isnan(x) ? __int_as_float(0x7fc00000) : x;
 }
 
-struct ChainParams {
-    const float *x, *gamma, *beta;
-    float eps;
-    uint64_t key;
-    uint64_t threshold;  // dropout keep threshold on (word >> 11)
-    float den;           // fl(1 - rate)
-    float rden;          // 1 / den (FAST mode)
-    float one_over_den;  // fl(1 / den): DropoutReplay of a unit cotangent
-    float hf, rh;        // hidden as f32, 1/hidden
-    int64_t rows;
-    int hidden;
-    int64_t index_base;
-    float *rowsum;      // fwd
-    float *stats;       // [rows][4]: mean, d, max, Z (optional)
-    const float *stats_in;
-    float *dx;          // bwd
-    float *dgamma_part, *dbeta_part;  // [grid][hidden] partials (bwd)
-    int rows_per_cta;
-};
-
-// ---------------------------------------------------------------------------
-// forward: one row per CTA iteration
-// ---------------------------------------------------------------------------
-template <int T, int NC, bool EXACT>
-__global__ void __launch_bounds__(T) chain_fwd_kernel(ChainParams p) {
-    __shared__ float red[NC * (T / 32) + 8];
-    const int n = p.hidden;
-    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
-    float g[NC][4], b[NC][4];
-    load_row<NC, T>(g, p.gamma, n, (reinterpret_cast<uintptr_t>(p.gamma) & 15) == 0 && n % 4 == 0);
-    load_row<NC, T>(b, p.beta, n, (reinterpret_cast<uintptr_t>(p.beta) & 15) == 0 && n % 4 == 0);
-    for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
-        float v[NC][4];
-        load_row<NC, T>(v, p.x + r * n, n, vec);
-        // mean = tree(x) / hidden
-        const float s1 = block_tree<T, NC>(v, n, red);
-        const float mean = EXACT ? __fdiv_rn(s1, p.hf) : __fmul_rn(s1, p.rh);
-        float c2[NC][4];
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                v[c][i] = __fsub_rn(v[c][i], mean);  // centered
-                c2[c][i] = __fmul_rn(v[c][i], v[c][i]);
-            }
-        const float s2 = block_tree<T, NC>(c2, n, red);
-        const float var = EXACT ? __fdiv_rn(s2, p.hf) : __fmul_rn(s2, p.rh);
-        const float d = __fsqrt_rn(__fadd_rn(var, p.eps));
-        const float rd = __fdiv_rn(1.0f, d);
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float nn = EXACT ? __fdiv_rn(v[c][i], d) : __fmul_rn(v[c][i], rd);
-                v[c][i] = __fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]);  // y
-            }
-        const float mx = block_max<T, NC>(v, n, red);
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[c][i] = expf(__fsub_rn(v[c][i], mx));  // e
-        const float z = block_tree<T, NC>(v, n, red);
-        const float rz = __fdiv_rn(1.0f, z);
-        const uint64_t base = static_cast<uint64_t>(p.index_base + r * n);
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int e = c * 4 * T + 4 * threadIdx.x + i;
-                const float s = EXACT ? __fdiv_rn(v[c][i], z) : __fmul_rn(v[c][i], rz);
-                const bool keep = e < n && dropout_keep(p.key, base + e, p.threshold);
-                v[c][i] = keep ? (EXACT ? __fdiv_rn(s, p.den) : __fmul_rn(s, p.rden)) : 0.0f;
-            }
-        const float rs = block_tree<T, NC>(v, n, red);
-        if (threadIdx.x == 0) {
-            p.rowsum[r] = canon(rs);
-            if (p.stats) {
-                float4 st = make_float4(mean, d, mx, z);
-                *reinterpret_cast<float4 *>(p.stats + 4 * r) = st;
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
-// adjoint of loss = sum(rowsum): dx, and per-CTA partial dgamma / dbeta
-// ---------------------------------------------------------------------------
-template <int T, int NC, bool EXACT>
-__global__ void __launch_bounds__(T) chain_bwd_kernel(ChainParams p) {
-    __shared__ float red[NC * (T / 32) + 8];
-    const int n = p.hidden;
-    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
-                     ((reinterpret_cast<uintptr_t>(p.dx) & 15) == 0);
-    float g[NC][4], b[NC][4], pg[NC][4], pb[NC][4];
-    const bool pvec = (reinterpret_cast<uintptr_t>(p.gamma) & 15) == 0 && n % 4 == 0;
-    load_row<NC, T>(g, p.gamma, n, pvec);
-    load_row<NC, T>(b, p.beta, n, (reinterpret_cast<uintptr_t>(p.beta) & 15) == 0 && n % 4 == 0);
-#pragma unroll
-    for (int c = 0; c < NC; ++c)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) pg[c][i] = pb[c][i] = 0.0f;
-
-    const int64_t r_begin = static_cast<int64_t>(blockIdx.x) * p.rows_per_cta;
-    int64_t r_end = r_begin + p.rows_per_cta;
-    if (r_end > p.rows) r_end = p.rows;
-    for (int64_t r = r_begin; r < r_end; ++r) {
-        float x[NC][4];
-        load_row<NC, T>(x, p.x + r * n, n, vec);
-        float mean, d, mx, z;
-        if (p.stats_in) {
-            const float4 st = *reinterpret_cast<const float4 *>(p.stats_in + 4 * r);
-            mean = st.x;
-            d = st.y;
-            mx = st.z;
-            z = st.w;
-        } else {
-            const float s1 = block_tree<T, NC>(x, n, red);
-            mean = EXACT ? __fdiv_rn(s1, p.hf) : __fmul_rn(s1, p.rh);
-            float t2[NC][4];
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float cc = __fsub_rn(x[c][i], mean);
-                    t2[c][i] = __fmul_rn(cc, cc);
-                }
-            const float s2 = block_tree<T, NC>(t2, n, red);
-            const float var = EXACT ? __fdiv_rn(s2, p.hf) : __fmul_rn(s2, p.rh);
-            d = __fsqrt_rn(__fadd_rn(var, p.eps));
-            const float rd0 = __fdiv_rn(1.0f, d);
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float cc = __fsub_rn(x[c][i], mean);
-                    const float nn = EXACT ? __fdiv_rn(cc, d) : __fmul_rn(cc, rd0);
-                    t2[c][i] = __fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]);
-                }
-            mx = block_max<T, NC>(t2, n, red);
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) t2[c][i] = expf(__fsub_rn(t2[c][i], mx));
-            z = block_tree<T, NC>(t2, n, red);
-        }
-        const float rd = __fdiv_rn(1.0f, d);
-        const float rz = __fdiv_rn(1.0f, z);
-        const uint64_t base = static_cast<uint64_t>(p.index_base + r * n);
-        // s (softmax output) and ds (replayed unit cotangent); x becomes c
-        float s[NC][4], ds[NC][4], gy[NC][4];
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int e = c * 4 * T + 4 * threadIdx.x + i;
-                const float cc = __fsub_rn(x[c][i], mean);
-                x[c][i] = cc;
-                const float nn = EXACT ? __fdiv_rn(cc, d) : __fmul_rn(cc, rd);
-                const float y = __fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]);
-                const float ee = expf(__fsub_rn(y, mx));
-                s[c][i] = EXACT ? __fdiv_rn(ee, z) : __fmul_rn(ee, rz);
-                const bool keep = e < n && dropout_keep(p.key, base + e, p.threshold);
-                ds[c][i] = keep ? p.one_over_den : 0.0f;
-                gy[c][i] = __fmul_rn(ds[c][i], s[c][i]);
-            }
-        const float q = block_tree<T, NC>(gy, n, red);
-        const float two_d = __fmul_rn(2.0f, d);
-        const float r2d = __fdiv_rn(1.0f, two_d);
-        // dy = s * (ds - q); dn = dy * gamma; dt = -((dn * n) / d) / (2d)
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int e = c * 4 * T + 4 * threadIdx.x + i;
-                const float dy = __fmul_rn(s[c][i], __fsub_rn(ds[c][i], q));
-                const float nn = EXACT ? __fdiv_rn(x[c][i], d) : __fmul_rn(x[c][i], rd);
-                if (e < n) {
-                    pg[c][i] = __fadd_rn(pg[c][i], __fmul_rn(dy, nn));
-                    pb[c][i] = __fadd_rn(pb[c][i], dy);
-                }
-                const float dn = __fmul_rn(dy, g[c][i]);
-                const float qq = EXACT ? __fdiv_rn(__fmul_rn(dn, nn), d)
-                                       : __fmul_rn(__fmul_rn(dn, nn), rd);
-                gy[c][i] = EXACT ? __fdiv_rn(-qq, two_d) : __fmul_rn(-qq, r2d);  // dt
-                s[c][i] = EXACT ? __fdiv_rn(dn, d) : __fmul_rn(dn, rd);          // dc1
-            }
-        const float dvar = block_tree<T, NC>(gy, n, red);
-        const float ds2 = EXACT ? __fdiv_rn(dvar, p.hf) : __fmul_rn(dvar, p.rh);
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float pr = __fmul_rn(ds2, x[c][i]);
-                const float dc = __fadd_rn(__fadd_rn(pr, pr), s[c][i]);
-                s[c][i] = dc;
-                gy[c][i] = -dc;
-            }
-        const float dm = block_tree<T, NC>(gy, n, red);
-        const float ds1 = EXACT ? __fdiv_rn(dm, p.hf) : __fmul_rn(dm, p.rh);
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) s[c][i] = canon(__fadd_rn(ds1, s[c][i]));
-        store_row<NC, T>(s, p.dx + r * n, n, vec);
-    }
-    store_row<NC, T>(pg, p.dgamma_part + static_cast<int64_t>(blockIdx.x) * n, n, pvec);
-    store_row<NC, T>(pb, p.dbeta_part + static_cast<int64_t>(blockIdx.x) * n, n, pvec);
-}
-
 // ---------------------------------------------------------------------------
 // standalone row ops
 // ---------------------------------------------------------------------------
@@ -744,67 +535,9 @@ int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStr
     return st;
 }
 
-// Shared by chelis_cuda_chain_bwd and any caller that supplies its own
-// partial buffers: `part` holds 2 * grid * hidden floats.
-int chain_bwd_with_partials(const float *x, const float *gamma, const float *beta, float eps,
-                            uint64_t key, float rate, int64_t rows, int64_t hidden,
-                            int64_t index_base, const float *row_stats, float *dx, float *dgamma,
-                            float *dbeta, float *part, int grid, cudaStream_t s);
-
-int chain_bwd_grid(int64_t rows) { return rows_grid(rows, 4); }
-
 }  // namespace chelis
 
 namespace {
-ChainParams make_chain_params(const float *x, const float *gamma, const float *beta, float eps,
-                              uint64_t key, float rate, int64_t rows, int64_t hidden,
-                              int64_t index_base) {
-    ChainParams p{};
-    p.x = x;
-    p.gamma = gamma;
-    p.beta = beta;
-    p.eps = eps;
-    p.key = key;
-    p.threshold = dropout_threshold(rate);
-    volatile float one = 1.0f;
-    p.den = one - rate;
-    p.rden = 1.0f / p.den;
-    p.one_over_den = 1.0f / p.den;
-    p.hf = static_cast<float>(hidden);
-    p.rh = 1.0f / p.hf;
-    p.rows = rows;
-    p.hidden = static_cast<int>(hidden);
-    p.index_base = index_base;
-    return p;
-}
-
-template <int T>
-int launch_chain_fwd(const ChainParams &p, cudaStream_t s) {
-    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
-    return dispatch_nc(p.hidden, T, [&](auto ncv) -> int {
-        constexpr int NC = decltype(ncv)::value;
-        const unsigned grid = static_cast<unsigned>(p.rows < 65535 * 16 ? p.rows : 65535 * 16);
-        if (exact) chain_fwd_kernel<T, NC, true><<<grid, T, 0, s>>>(p);
-        else chain_fwd_kernel<T, NC, false><<<grid, T, 0, s>>>(p);
-        g_launches++;
-        CHELIS_LAUNCH_CHECK("chain_fwd_kernel");
-        return CHELIS_CUDA_OK;
-    });
-}
-
-template <int T>
-int launch_chain_bwd(const ChainParams &p, int grid, cudaStream_t s) {
-    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
-    return dispatch_nc(p.hidden, T, [&](auto ncv) -> int {
-        constexpr int NC = decltype(ncv)::value;
-        if (exact) chain_bwd_kernel<T, NC, true><<<grid, T, 0, s>>>(p);
-        else chain_bwd_kernel<T, NC, false><<<grid, T, 0, s>>>(p);
-        g_launches++;
-        CHELIS_LAUNCH_CHECK("chain_bwd_kernel");
-        return CHELIS_CUDA_OK;
-    });
-}
-
 constexpr int kRowThreads = 256;
 
 int check_rows_args(const void *x, int64_t rows, int64_t hidden) {
@@ -817,60 +550,7 @@ int check_rows_args(const void *x, int64_t rows, int64_t hidden) {
 }
 }  // namespace
 
-namespace chelis {
-int chain_bwd_with_partials(const float *x, const float *gamma, const float *beta, float eps,
-                            uint64_t key, float rate, int64_t rows, int64_t hidden,
-                            int64_t index_base, const float *row_stats, float *dx, float *dgamma,
-                            float *dbeta, float *part, int grid, cudaStream_t s) {
-    ChainParams p = make_chain_params(x, gamma, beta, eps, key, rate, rows, hidden, index_base);
-    p.stats_in = row_stats;
-    p.dx = dx;
-    p.dgamma_part = part;
-    p.dbeta_part = part + static_cast<int64_t>(grid) * hidden;
-    p.rows_per_cta = static_cast<int>((rows + grid - 1) / grid);
-    CHELIS_TRY(launch_chain_bwd<kRowThreads>(p, grid, s));
-    CHELIS_TRY(col_sum_into(p.dgamma_part, grid, hidden, dgamma, s));
-    CHELIS_TRY(col_sum_into(p.dbeta_part, grid, hidden, dbeta, s));
-    return CHELIS_CUDA_OK;
-}
-}  // namespace chelis
-
 extern "C" {
-
-int chelis_cuda_chain_fwd(const float *x, const float *gamma, const float *beta, float eps,
-                          uint64_t key, float rate, int64_t rows, int64_t hidden,
-                          int64_t index_base, float *rowsum, float *row_stats) {
-    CHELIS_TRY(check_rows_args(x, rows, hidden));
-    CHELIS_TRY(check_rate(rate));
-    if (hidden == 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in layer_norm at f32");
-    if (rows == 0) return CHELIS_CUDA_OK;
-    ChainParams p = make_chain_params(x, gamma, beta, eps, key, rate, rows, hidden, index_base);
-    p.rowsum = rowsum;
-    p.stats = row_stats;
-    return launch_chain_fwd<kRowThreads>(p, current_stream());
-}
-
-int chelis_cuda_chain_bwd(const float *x, const float *gamma, const float *beta, float eps,
-                          uint64_t key, float rate, int64_t rows, int64_t hidden,
-                          int64_t index_base, const float *row_stats, float *dx, float *dgamma,
-                          float *dbeta) {
-    CHELIS_TRY(check_rows_args(x, rows, hidden));
-    CHELIS_TRY(check_rate(rate));
-    if (hidden == 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in layer_norm at f32");
-    cudaStream_t s = current_stream();
-    if (rows == 0) {
-        CHELIS_TRY(check_cuda(cudaMemsetAsync(dgamma, 0, hidden * sizeof(float), s), "memset"));
-        return check_cuda(cudaMemsetAsync(dbeta, 0, hidden * sizeof(float), s), "memset");
-    }
-    const int grid = chain_bwd_grid(rows);
-    void *part = nullptr;
-    CHELIS_TRY(scratch_alloc(&part, static_cast<size_t>(2) * grid * hidden * sizeof(float), s));
-    int st = chain_bwd_with_partials(x, gamma, beta, eps, key, rate, rows, hidden, index_base,
-                                     row_stats, dx, dgamma, dbeta, static_cast<float *>(part),
-                                     grid, s);
-    scratch_free(part, s);
-    return st;
-}
 
 int chelis_cuda_layer_norm_f32(const float *x, const float *gamma, const float *beta, float eps,
                                float *y, int64_t rows, int64_t hidden) {

@@ -96,7 +96,10 @@ SIGNATURES = {
     "chelis_cuda_softmax_rows_bwd_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64]),
     "chelis_cuda_chain_fwd": (c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "chelis_cuda_chain_bwd": (c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
-    "chelis_cuda_chain_bwd_noalloc": (c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "chelis_cuda_chain_saved_bytes": (c_i64, [c_i64, c_i64]),
+    "chelis_cuda_chain_fwd_save": (c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "chelis_cuda_chain_bwd_saved": (c_int, [c_vp, c_vp, c_vp, c_f32, c_f32, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "chelis_cuda_chain_bwd_noalloc":(c_int, [c_vp, c_vp, c_vp, c_f32, c_u64, c_f32, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "chelis_cuda_cumsum_f64": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int]),
     "chelis_cuda_cumsum_f32": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int]),
     "chelis_cuda_portfolio_f64": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]),

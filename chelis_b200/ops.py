@@ -190,6 +190,31 @@ def chain_bwd(x, gamma, beta, eps: float, key: int, rate: float, index_base: int
     return dx, dg, db
 
 
+def chain_fwd_save(x, gamma, beta, eps: float, key: int, rate: float, index_base: int = 0):
+    """Forward that also returns the saved state (statistics + keep bits)."""
+    _prepare(x, gamma, beta)
+    rows, hidden = x.shape
+    nbytes = int(L.load().chelis_cuda_chain_saved_bytes(rows, hidden))
+    if nbytes < 0:
+        raise ValueError("unsupported chain shape")
+    saved = torch.empty(max(nbytes, 16) // 4, dtype=torch.float32, device=x.device)
+    rowsum = torch.empty(rows, dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_chain_fwd_save", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps, key,
+           rate, rows, hidden, index_base, rowsum.data_ptr(), saved.data_ptr())
+    return rowsum, saved
+
+
+def chain_bwd_saved(x, gamma, beta, eps: float, rate: float, saved: torch.Tensor):
+    _prepare(x, gamma, beta, saved)
+    rows, hidden = x.shape
+    dx = torch.empty_like(x)
+    dg = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    db = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_chain_bwd_saved", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), eps,
+           rate, rows, hidden, saved.data_ptr(), dx.data_ptr(), dg.data_ptr(), db.data_ptr())
+    return dx, dg, db
+
+
 def cumsum(x: torch.Tensor, reverse: bool = False) -> torch.Tensor:
     _prepare(x)
     y = torch.empty_like(x)

@@ -248,6 +248,20 @@ int chelis_cuda_chain_bwd(const float *x, const float *gamma, const float *beta,
                           uint64_t key, float rate, int64_t rows, int64_t hidden,
                           int64_t index_base, const float *row_stats, float *dx, float *dgamma,
                           float *dbeta);
+/* The chain forward that also saves what its adjoint needs: per-row
+ * statistics and the keyed-dropout keep bits (one bit per element), in a
+ * 16-byte aligned device buffer of chelis_cuda_chain_saved_bytes(rows,
+ * hidden) bytes.  chelis_cuda_chain_bwd_saved then runs the adjoint without
+ * recomputing the RNG or any forward reduction.  PyTorch-style saved state;
+ * the reference materialises forward intermediates instead (the C lane
+ * keeps every DAG node's tensor). */
+int64_t chelis_cuda_chain_saved_bytes(int64_t rows, int64_t hidden);
+int chelis_cuda_chain_fwd_save(const float *x, const float *gamma, const float *beta, float eps,
+                               uint64_t key, float rate, int64_t rows, int64_t hidden,
+                               int64_t index_base, float *rowsum, void *saved);
+int chelis_cuda_chain_bwd_saved(const float *x, const float *gamma, const float *beta, float eps,
+                                float rate, int64_t rows, int64_t hidden, const void *saved,
+                                float *dx, float *dgamma, float *dbeta);
 /* chelis_cuda_chain_bwd for callers that cannot let the library allocate
  * device memory (a host that budgets its whole device arena up front and
  * hands out every buffer itself, or one that bans driver allocation while it

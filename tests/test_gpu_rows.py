@@ -151,6 +151,27 @@ def test_chain_fwd_bwd_small(cuda, orc, rows, hidden, mode):
     assert bits_equal(dg2.cpu().numpy(), dg.cpu().numpy())
 
 
+@pytest.mark.parametrize("rows,hidden", [(3, 1), (9, 333), (64, 4096), (5, 8192)])
+@pytest.mark.parametrize("mode", [L.ROWS_EXACT, L.ROWS_FAST])
+def test_chain_saved_state_matches_recompute(cuda, orc, rows, hidden, mode):
+    """Forward with saved statistics + keep bits, adjoint from them: the keep
+    bits equal the oracle's mask and the adjoint equals the recomputing one."""
+    x, g, b = W.chain_inputs(rows, hidden, seed=rows * 7 + hidden)
+    eps, key, rate = W.CHAIN_EPS, W.CHAIN_KEY, W.CHAIN_RATE
+    X, G, B = t(x), t(g), t(b)
+    with cuda.rows_mode(mode):
+        rs, saved = cuda.chain_fwd_save(X, G, B, float(eps), key, float(rate))
+        rs2 = cuda.chain_fwd(X, G, B, float(eps), key, float(rate))
+        dx, dg, db = cuda.chain_bwd_saved(X, G, B, float(eps), float(rate), saved)
+        dx2, dg2, db2 = cuda.chain_bwd(X, G, B, float(eps), key, float(rate))
+    assert bits_equal(rs.cpu().numpy(), rs2.cpu().numpy())
+    assert bits_equal(dx.cpu().numpy(), dx2.cpu().numpy())
+    assert bits_equal(dg.cpu().numpy(), dg2.cpu().numpy())
+    dx_ref, dg_ref, db_ref = orc.chain_bwd(x, g, b, eps, key, rate)
+    assert rowwise_ok(dx.cpu().numpy(), dx_ref) <= RTOL
+    assert normwise(db.cpu().numpy(), db_ref) <= RTOL
+
+
 def test_chain_full_config_size(cuda, orc):
     """Config 3 at full size (16384 x 4096): forward and adjoint on the GPU
     against the oracle on the same seeded inputs."""
