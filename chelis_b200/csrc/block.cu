@@ -1,0 +1,608 @@
+// block.cu -- the pre-LN transformer block, forward and reverse mode, f32.
+//
+//   h1 = layer_norm(x; g1, b1)                      (tier2.rs:1248-1375)
+//   [q k v] = h1 . Wqkv                              (three matmuls, fused)
+//   per head: p = softmax(where(causal, (q.k^T)*scale, -inf)); o = p.v
+//                                                   (spec 05 section 4.7)
+//   x2 = x + o . Wo
+//   h2 = layer_norm(x2; g2, b2)
+//   y  = x2 + gelu(h2 . W1) . W2                    (gelu = m(x)*Phi(x),
+//                                                    spec 05 section 3.3)
+// and the vector-Jacobian product for an upstream cotangent dy: dx and the
+// gradients of Wqkv, Wo, W1, W2, g1, b1, g2, b2 (grad.rs adjoint graphs;
+// the matmul adjoint is a matmul with a transposed operand, [05-OP-51]).
+//
+// Every matmul runs on the tcgen05 3xTF32 kernel (chelis_cuda_sgemm); the
+// row work runs on the kernels below.  Attention is materialised per head
+// ([B*H, S, S] scores), the unfused form of the reference graph.
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "common.cuh"
+
+namespace chelis {
+
+extern std::atomic<uint64_t> g_launches;
+int rows_mode();
+
+namespace block {
+
+using chain::Red;
+using chain::at;
+using chain::canon;
+using chain::div_;
+using chain::exp_;
+using chain::ld4;
+using chain::load4;
+using chain::quad;
+using chain::stage;
+using chain::tree4;
+using chain::tree_parts;
+
+// ---------------------------------------------------------------------------
+// layer_norm forward, saving (mean, sqrt(var + eps)) per row
+// ---------------------------------------------------------------------------
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T) ln_fwd_kernel(const float *__restrict__ x,
+                                                   const float *__restrict__ gamma,
+                                                   const float *__restrict__ beta, float eps,
+                                                   float *__restrict__ y, float2 *__restrict__ stats,
+                                                   int64_t rows, int n) {
+    extern __shared__ __align__(16) float smem[];
+    float *sg = smem, *sb = sg + NC * 4 * T;
+    Red<T, NC> rs{sb + NC * 4 * T};
+    const float hf = static_cast<float>(n), rh = __fdiv_rn(1.0f, hf);
+    const bool vec = (n % 4 == 0);
+    stage<NC, T>(sg, gamma, n);
+    stage<NC, T>(sb, beta, n);
+    __syncthreads();
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float v[NC][4];
+        load4<NC, T>(v, x + r * n, n, vec);
+        const float mean = div_<EXACT>(tree4<T, NC>(v, n, rs), hf, rh);
+        float part[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = __fsub_rn(v[c][i], mean);
+            part[c] = quad(__fmul_rn(v[c][0], v[c][0]), __fmul_rn(v[c][1], v[c][1]),
+                           __fmul_rn(v[c][2], v[c][2]), __fmul_rn(v[c][3], v[c][3]),
+                           n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+        }
+        const float var = div_<EXACT>(tree_parts<T, NC>(part, n, rs), hf, rh);
+        const float d = __fsqrt_rn(__fadd_rn(var, eps));
+        const float rd = __fdiv_rn(1.0f, d);
+        float *yr = y + r * n;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const float4 g4 = ld4<T>(sg, c), b4 = ld4<T>(sb, c);
+            const int e0 = c * 4 * T + 4 * threadIdx.x;
+            float o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                o[i] = canon(__fadd_rn(__fmul_rn(div_<EXACT>(v[c][i], d, rd), at(g4, i)), at(b4, i)));
+            if (vec && e0 + 3 < n) *reinterpret_cast<float4 *>(yr + e0) = make_float4(o[0], o[1], o[2], o[3]);
+            else
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (e0 + i < n) yr[e0 + i] = o[i];
+        }
+        if (threadIdx.x == 0) stats[r] = make_float2(mean, d);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// layer_norm adjoint (the LN part of the chain adjoint): dx = resid + dLN,
+// per-CTA dgamma / dbeta partials
+// ---------------------------------------------------------------------------
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T) ln_bwd_kernel(const float *__restrict__ x,
+                                                   const float *__restrict__ dy,
+                                                   const float2 *__restrict__ stats,
+                                                   const float *__restrict__ gamma,
+                                                   const float *__restrict__ resid,
+                                                   float *__restrict__ dx, float *__restrict__ pg_out,
+                                                   float *__restrict__ pb_out, int64_t rows, int n,
+                                                   int rows_per_cta) {
+    extern __shared__ __align__(16) float smem[];
+    constexpr int L = NC * 4 * T;
+    float *sg = smem, *pg = sg + L, *pb = pg + L;
+    Red<T, NC> rs{pb + L};
+    const float hf = static_cast<float>(n), rh = __fdiv_rn(1.0f, hf);
+    const bool vec = (n % 4 == 0);
+    stage<NC, T>(sg, gamma, n);
+    stage<NC, T>(pg, nullptr, n);
+    stage<NC, T>(pb, nullptr, n);
+    __syncthreads();
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > rows) r1 = rows;
+    for (int64_t r = r0; r < r1; ++r) {
+        float c_[NC][4], g_[NC][4];
+        load4<NC, T>(c_, x + r * n, n, vec);
+        load4<NC, T>(g_, dy + r * n, n, vec);
+        const float2 st = stats[r];
+        const float mean = st.x, d = st.y;
+        const float rd = __fdiv_rn(1.0f, d);
+        const float two_d = __fmul_rn(2.0f, d);
+        const float r2d = __fdiv_rn(1.0f, two_d);
+        float part[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const float4 gm = ld4<T>(sg, c);
+            float4 pg4 = ld4<T>(pg, c), pb4 = ld4<T>(pb, c);
+            float dt[4], dyn[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float cc = __fsub_rn(c_[c][i], mean);
+                c_[c][i] = cc;
+                const float nn = div_<EXACT>(cc, d, rd);
+                const float g = g_[c][i];
+                dyn[i] = __fmul_rn(g, nn);
+                const float dn = __fmul_rn(g, at(gm, i));
+                dt[i] = div_<EXACT>(-div_<EXACT>(__fmul_rn(dn, nn), d, rd), two_d, r2d);
+                g_[c][i] = div_<EXACT>(dn, d, rd);  // dc1
+            }
+            pg4.x = __fadd_rn(pg4.x, dyn[0]); pg4.y = __fadd_rn(pg4.y, dyn[1]);
+            pg4.z = __fadd_rn(pg4.z, dyn[2]); pg4.w = __fadd_rn(pg4.w, dyn[3]);
+            const int e0 = c * 4 * T + 4 * threadIdx.x;
+            float dyv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dyv[i] = (e0 + i < n) ? dy[r * n + e0 + i] : 0.0f;
+            pb4.x = __fadd_rn(pb4.x, dyv[0]); pb4.y = __fadd_rn(pb4.y, dyv[1]);
+            pb4.z = __fadd_rn(pb4.z, dyv[2]); pb4.w = __fadd_rn(pb4.w, dyv[3]);
+            reinterpret_cast<float4 *>(pg)[c * T + threadIdx.x] = pg4;
+            reinterpret_cast<float4 *>(pb)[c * T + threadIdx.x] = pb4;
+            part[c] = quad(dt[0], dt[1], dt[2], dt[3], n - e0);
+        }
+        const float ds2 = div_<EXACT>(tree_parts<T, NC>(part, n, rs), hf, rh);
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            float m4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pr = __fmul_rn(ds2, c_[c][i]);
+                const float dc = __fadd_rn(__fadd_rn(pr, pr), g_[c][i]);
+                g_[c][i] = dc;
+                m4[i] = -dc;
+            }
+            part[c] = quad(m4[0], m4[1], m4[2], m4[3], n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+        }
+        const float ds1 = div_<EXACT>(tree_parts<T, NC>(part, n, rs), hf, rh);
+        float *dxr = dx + r * n;
+        const float *rr = resid ? resid + r * n : nullptr;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int e0 = c * 4 * T + 4 * threadIdx.x;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (e0 + i < n) {
+                    float v = __fadd_rn(ds1, g_[c][i]);
+                    if (rr) v = __fadd_rn(rr[e0 + i], v);
+                    dxr[e0 + i] = canon(v);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n; e += T) {
+        pg_out[static_cast<int64_t>(blockIdx.x) * n + e] = pg[e];
+        pb_out[static_cast<int64_t>(blockIdx.x) * n + e] = pb[e];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// causal softmax over [rows = BH*S, S] in place: p = softmax(where(j <= i,
+// s*scale, -inf)), i = row % S.  Masked entries become exact +0.
+// ---------------------------------------------------------------------------
+template <int T, int NC, bool EXACT>
+__global__ void __launch_bounds__(T) causal_softmax_kernel(float *__restrict__ s, int64_t rows,
+                                                           int n, float scale) {
+    __shared__ float redbuf[2 * (NC * (T / 32) + 8)];
+    Red<T, NC> rs{redbuf};
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const int qi = static_cast<int>(r % n);
+        float v[NC][4];
+        load4<NC, T>(v, s + r * n, n, true);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int e = c * 4 * T + 4 * threadIdx.x + i;
+                v[c][i] = (e <= qi) ? __fmul_rn(v[c][i], scale) : -INFINITY;
+            }
+        const float mx = chain::row_max<T, NC>(v, n, rs);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = exp_<EXACT>(__fsub_rn(v[c][i], mx));
+        const float z = tree4<T, NC>(v, n, rs);
+        const float rz = __fdiv_rn(1.0f, z);
+        float *o = s + r * n;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int e0 = c * 4 * T + 4 * threadIdx.x;
+            float w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = canon(div_<EXACT>(v[c][i], z, rz));
+            if (e0 < n) *reinterpret_cast<float4 *>(o + e0) = make_float4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// dS = (P * (dP - sum(dP * P))) * scale, in place over dP
+template <int T, int NC>
+__global__ void __launch_bounds__(T) softmax_scaled_bwd_kernel(const float *__restrict__ p,
+                                                               float *__restrict__ dp,
+                                                               int64_t rows, int n, float scale) {
+    __shared__ float redbuf[2 * (NC * (T / 32) + 8)];
+    Red<T, NC> rs{redbuf};
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float y[NC][4], g[NC][4], gy[NC][4];
+        load4<NC, T>(y, p + r * n, n, true);
+        load4<NC, T>(g, dp + r * n, n, true);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) gy[c][i] = __fmul_rn(g[c][i], y[c][i]);
+        const float q = tree4<T, NC>(gy, n, rs);
+        float *o = dp + r * n;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int e0 = c * 4 * T + 4 * threadIdx.x;
+            float w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                w[i] = canon(__fmul_rn(__fmul_rn(y[c][i], __fsub_rn(g[c][i], q)), scale));
+            if (e0 < n) *reinterpret_cast<float4 *>(o + e0) = make_float4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// gelu = m(x) * Phi(x) with the compensated Phi graph of spec 05 section 3.3
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float phi_graph(float x) {
+    const float c = 0.70710677f;          // RN_f32(1/sqrt(2))
+    const float cl = 1.2101671e-08f;      // RN_f32(1/sqrt(2) - c)
+    const float k = 1.1283792f;           // RN_f32(2/sqrt(pi))
+    const float sp = 4097.0f;             // Veltkamp splitter for f32
+    const float e = erfcf(__fmul_rn(-x, c));
+    const float z = (fabsf(x) < 64.0f) ? x : 0.0f;
+    const float a = -z;
+    const float th = __fmul_rn(a, c);
+    const float ta = __fmul_rn(sp, a);
+    const float ah = __fsub_rn(ta, __fsub_rn(ta, a));
+    const float al = __fsub_rn(a, ah);
+    const float tc = __fmul_rn(sp, c);
+    const float ch = __fsub_rn(tc, __fsub_rn(tc, c));
+    const float cr = __fsub_rn(c, ch);
+    float tl = __fsub_rn(__fmul_rn(ah, ch), th);
+    tl = __fadd_rn(tl, __fmul_rn(ah, cr));
+    tl = __fadd_rn(tl, __fmul_rn(al, ch));
+    tl = __fadd_rn(tl, __fmul_rn(al, cr));
+    tl = __fadd_rn(tl, __fmul_rn(a, cl));
+    const float corr = __fmul_rn(__fmul_rn(k, expf(-__fmul_rn(th, th))), tl);
+    return __fmul_rn(0.5f, __fsub_rn(e, corr));
+}
+
+__global__ void gelu_fwd_kernel(const float *__restrict__ u, float *__restrict__ g, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float x = u[i];
+        const float m = (x < -3.40282347e+38f) ? -0.0f : x;
+        g[i] = canon(__fmul_rn(m, phi_graph(x)));
+    }
+}
+
+// d gelu / dx = Phi(x) + x * phi(x), phi the standard normal density
+__global__ void gelu_bwd_kernel(const float *__restrict__ u, float *__restrict__ dg, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float x = u[i];
+        const float pdf = __fmul_rn(0.3989422804f, expf(__fmul_rn(-0.5f, __fmul_rn(x, x))));
+        const float der = isinf(x) ? (x > 0.0f ? 1.0f : 0.0f) : __fadd_rn(phi_graph(x), __fmul_rn(x, pdf));
+        dg[i] = canon(__fmul_rn(dg[i], der));
+    }
+}
+
+// y = a + b
+__global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                           float *__restrict__ y, int64_t n4) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 p = reinterpret_cast<const float4 *>(a)[i];
+        const float4 q = reinterpret_cast<const float4 *>(b)[i];
+        reinterpret_cast<float4 *>(y)[i] = make_float4(__fadd_rn(p.x, q.x), __fadd_rn(p.y, q.y),
+                                                       __fadd_rn(p.z, q.z), __fadd_rn(p.w, q.w));
+    }
+}
+
+// [B, S, 3, H, D] <-> three [B, H, S, D]; dir 0: split, 1: merge
+__global__ void qkv_permute_kernel(float *__restrict__ qkv, float *__restrict__ q,
+                                   float *__restrict__ k, float *__restrict__ v, int b_, int s_,
+                                   int h_, int d4, int dir) {
+    const int64_t total = static_cast<int64_t>(b_) * s_ * 3 * h_ * d4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t t = i;
+        const int dd = static_cast<int>(t % d4); t /= d4;
+        const int hh = static_cast<int>(t % h_); t /= h_;
+        const int w = static_cast<int>(t % 3); t /= 3;
+        const int ss = static_cast<int>(t % s_); t /= s_;
+        const int bb = static_cast<int>(t);
+        float *dst = (w == 0 ? q : w == 1 ? k : v);
+        const int64_t o = ((static_cast<int64_t>(bb) * h_ + hh) * s_ + ss) * d4 + dd;
+        float4 *pa = reinterpret_cast<float4 *>(qkv) + i;
+        float4 *pb = reinterpret_cast<float4 *>(dst) + o;
+        if (dir == 0) *pb = *pa;
+        else *pa = *pb;
+    }
+}
+
+// [B, H, S, D] <-> [B, S, H, D]; dir 0: heads -> rows, 1: rows -> heads
+__global__ void heads_permute_kernel(float *__restrict__ hsd, float *__restrict__ shd, int b_,
+                                     int s_, int h_, int d4, int dir) {
+    const int64_t total = static_cast<int64_t>(b_) * s_ * h_ * d4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t t = i;
+        const int dd = static_cast<int>(t % d4); t /= d4;
+        const int hh = static_cast<int>(t % h_); t /= h_;
+        const int ss = static_cast<int>(t % s_); t /= s_;
+        const int bb = static_cast<int>(t);
+        const int64_t o = ((static_cast<int64_t>(bb) * h_ + hh) * s_ + ss) * d4 + dd;
+        float4 *ps = reinterpret_cast<float4 *>(shd) + i;
+        float4 *ph = reinterpret_cast<float4 *>(hsd) + o;
+        if (dir == 0) *ps = *ph;
+        else *ph = *ps;
+    }
+}
+
+}  // namespace block
+}  // namespace chelis
+
+// ---------------------------------------------------------------------------
+// host orchestration
+// ---------------------------------------------------------------------------
+using namespace chelis;
+
+namespace {
+
+struct BlockDims {
+    int64_t B, S, D, H, Dh, F, BS, BH;
+};
+
+int block_dims(const chelis_block_params *p, BlockDims &d) {
+    if (!p || p->batch <= 0 || p->seq <= 0 || p->d_model <= 0 || p->heads <= 0 || p->d_ff <= 0 ||
+        p->d_model % p->heads)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in transformer_block at i64");
+    d.B = p->batch; d.S = p->seq; d.D = p->d_model; d.H = p->heads; d.F = p->d_ff;
+    d.Dh = d.D / d.H; d.BS = d.B * d.S; d.BH = d.B * d.H;
+    if (d.D > 8192 || d.S > 8192 || d.D % 4 || d.Dh % 4 || d.S % 4 || d.F % 4)
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED,
+                         "transformer block admits d_model, seq <= 8192 and d_model, seq, d_ff "
+                         "and the head dim multiples of 4");
+    return CHELIS_CUDA_OK;
+}
+
+// workspace layout in floats
+struct Ws {
+    float *h1, *qkv, *q, *k, *v, *P, *oh, *o, *x2, *h2, *u, *g, *dg, *dh2, *dx2, *dO, *doh, *dP,
+        *dq, *dk, *dv, *dqkv, *dh1, *part;
+    float2 *st1, *st2;
+    int64_t total;
+};
+
+int ln_grid() { return sm_count() * 2; }
+
+Ws carve(const BlockDims &d, float *base) {
+    Ws w{};
+    int64_t off = 0;
+    auto take = [&](int64_t n) {
+        float *p = base ? base + off : nullptr;
+        off += (n + 63) / 64 * 64;
+        return p;
+    };
+    const int64_t act = d.BS * d.D, big = d.BH * d.S * d.S, ff = d.BS * d.F;
+    w.h1 = take(act); w.qkv = take(3 * act); w.q = take(act); w.k = take(act); w.v = take(act);
+    w.P = take(big); w.oh = take(act); w.o = take(act); w.x2 = take(act); w.h2 = take(act);
+    w.u = take(ff); w.g = take(ff); w.dg = take(ff); w.dh2 = take(act); w.dx2 = take(act);
+    w.dO = take(act); w.doh = take(act); w.dP = take(big); w.dq = take(act); w.dk = take(act);
+    w.dv = take(act); w.dqkv = take(3 * act); w.dh1 = take(act);
+    w.part = take(2 * static_cast<int64_t>(ln_grid()) * d.D);
+    w.st1 = reinterpret_cast<float2 *>(take(2 * d.BS));
+    w.st2 = reinterpret_cast<float2 *>(take(2 * d.BS));
+    w.total = off;
+    return w;
+}
+
+unsigned grid_for(int64_t n, int per = 256) {
+    int64_t g = (n + per - 1) / per;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    return static_cast<unsigned>(g > cap ? cap : (g < 1 ? 1 : g));
+}
+
+template <typename F>
+int with_rows_nc(int64_t n, F &&f) {
+    const int64_t c = (n + 1023) / 1024;
+    if (c <= 1) return f(std::integral_constant<int, 1>());
+    if (c <= 2) return f(std::integral_constant<int, 2>());
+    if (c <= 4) return f(std::integral_constant<int, 4>());
+    return f(std::integral_constant<int, 8>());
+}
+
+template <typename K>
+int smem_attr(K k, size_t bytes) {
+    return check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(bytes)),
+                      "cudaFuncSetAttribute(block)");
+}
+
+int ln_fwd(const float *x, const float *g, const float *b, float eps, float *y, float2 *st,
+           int64_t rows, int64_t n, cudaStream_t s) {
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    return with_rows_nc(n, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        const size_t smem = 2 * NC * 1024 * sizeof(float) + 2 * (NC * 8 + 8) * sizeof(float);
+        const unsigned grid = static_cast<unsigned>(rows < sm_count() * 8 ? rows : sm_count() * 8);
+        if (exact) {
+            CHELIS_TRY(smem_attr(block::ln_fwd_kernel<256, NC, true>, smem));
+            block::ln_fwd_kernel<256, NC, true><<<grid, 256, smem, s>>>(x, g, b, eps, y, st, rows, static_cast<int>(n));
+        } else {
+            CHELIS_TRY(smem_attr(block::ln_fwd_kernel<256, NC, false>, smem));
+            block::ln_fwd_kernel<256, NC, false><<<grid, 256, smem, s>>>(x, g, b, eps, y, st, rows, static_cast<int>(n));
+        }
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("ln_fwd_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+int ln_bwd(const float *x, const float *dy, const float2 *st, const float *g, const float *resid,
+           float *dx, float *part, float *dgamma, float *dbeta, int64_t rows, int64_t n,
+           cudaStream_t s) {
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    int grid = ln_grid();
+    if (grid > rows) grid = static_cast<int>(rows);
+    const int rpc = static_cast<int>((rows + grid - 1) / grid);
+    float *pg = part, *pb = part + static_cast<int64_t>(grid) * n;
+    CHELIS_TRY(with_rows_nc(n, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        const size_t smem = 3 * NC * 1024 * sizeof(float) + 2 * (NC * 8 + 8) * sizeof(float);
+        if (exact) {
+            CHELIS_TRY(smem_attr(block::ln_bwd_kernel<256, NC, true>, smem));
+            block::ln_bwd_kernel<256, NC, true><<<grid, 256, smem, s>>>(x, dy, st, g, resid, dx, pg, pb, rows, static_cast<int>(n), rpc);
+        } else {
+            CHELIS_TRY(smem_attr(block::ln_bwd_kernel<256, NC, false>, smem));
+            block::ln_bwd_kernel<256, NC, false><<<grid, 256, smem, s>>>(x, dy, st, g, resid, dx, pg, pb, rows, static_cast<int>(n), rpc);
+        }
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("ln_bwd_kernel");
+        return CHELIS_CUDA_OK;
+    }));
+    CHELIS_TRY(col_sum_into(pg, grid, n, dgamma, s));
+    return col_sum_into(pb, grid, n, dbeta, s);
+}
+
+int softmax_causal(float *P, int64_t rows, int64_t n, float scale, cudaStream_t s) {
+    const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
+    return with_rows_nc(n, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        const unsigned grid = static_cast<unsigned>(rows < sm_count() * 16 ? rows : sm_count() * 16);
+        if (exact) block::causal_softmax_kernel<256, NC, true><<<grid, 256, 0, s>>>(P, rows, static_cast<int>(n), scale);
+        else block::causal_softmax_kernel<256, NC, false><<<grid, 256, 0, s>>>(P, rows, static_cast<int>(n), scale);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("causal_softmax_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+int softmax_bwd_scaled(const float *P, float *dP, int64_t rows, int64_t n, float scale, cudaStream_t s) {
+    return with_rows_nc(n, [&](auto ncv) -> int {
+        constexpr int NC = decltype(ncv)::value;
+        const unsigned grid = static_cast<unsigned>(rows < sm_count() * 16 ? rows : sm_count() * 16);
+        block::softmax_scaled_bwd_kernel<256, NC><<<grid, 256, 0, s>>>(P, dP, rows, static_cast<int>(n), scale);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("softmax_scaled_bwd_kernel");
+        return CHELIS_CUDA_OK;
+    });
+}
+
+int add(const float *a, const float *b, float *y, int64_t n, cudaStream_t s) {
+    block::add_kernel<<<grid_for(n / 4), 256, 0, s>>>(a, b, y, n / 4);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("add_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+// row-major C = op(A) . op(B) on the calling thread's stream
+int mm(int ta, int tb, int64_t m, int64_t n, int64_t k, const float *a, int64_t lda,
+       const float *b, int64_t ldb, float *c, int64_t ldc, int64_t batch = 1, int64_t sa = 0,
+       int64_t sb = 0, int64_t sc = 0) {
+    return chelis_cuda_sgemm(ta, tb, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc, batch);
+}
+
+}  // namespace
+
+extern "C" int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p) {
+    BlockDims d;
+    if (block_dims(p, d) != CHELIS_CUDA_OK) return -1;
+    return carve(d, nullptr).total * static_cast<int64_t>(sizeof(float));
+}
+
+extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *workspace) {
+    BlockDims d;
+    CHELIS_TRY(block_dims(p, d));
+    cudaStream_t s = current_stream();
+    void *owned = nullptr;
+    float *base = static_cast<float *>(workspace);
+    if (!base) {
+        CHELIS_TRY(scratch_alloc(&owned, carve(d, nullptr).total * sizeof(float), s));
+        base = static_cast<float *>(owned);
+    }
+    Ws w = carve(d, base);
+    const float scale = 1.0f / sqrtf(static_cast<float>(d.Dh));
+    const int64_t D = d.D, S = d.S, Dh = d.Dh, F = d.F, BS = d.BS, BH = d.BH;
+    const int d4 = static_cast<int>(Dh / 4);
+    int st = CHELIS_CUDA_OK;
+    do {
+        // ---------------- forward ----------------
+        if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, w.h1, w.st1, BS, D, s))) break;
+        if ((st = mm(0, 0, BS, 3 * D, D, w.h1, D, p->w_qkv, 3 * D, w.qkv, 3 * D))) break;
+        block::qkv_permute_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
+            w.qkv, w.q, w.k, w.v, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 0);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
+        if ((st = mm(0, 1, S, S, Dh, w.q, Dh, w.k, Dh, w.P, S, BH, S * Dh, S * Dh, S * S))) break;
+        if ((st = softmax_causal(w.P, BH * S, S, scale, s))) break;
+        if ((st = mm(0, 0, S, Dh, S, w.P, S, w.v, Dh, w.oh, Dh, BH, S * S, S * Dh, S * Dh))) break;
+        block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
+            w.oh, w.o, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 0);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
+        if ((st = mm(0, 0, BS, D, D, w.o, D, p->w_o, D, w.x2, D))) break;
+        if ((st = add(p->x, w.x2, w.x2, BS * D, s))) break;
+        if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) break;
+        if ((st = mm(0, 0, BS, F, D, w.h2, D, p->w_1, F, w.u, F))) break;
+        block::gelu_fwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.g, BS * F);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "gelu_fwd_kernel"))) break;
+        if ((st = mm(0, 0, BS, D, F, w.g, F, p->w_2, D, p->y, D))) break;
+        if ((st = add(w.x2, p->y, p->y, BS * D, s))) break;
+        if (!p->dy) break;
+        // ---------------- reverse mode ----------------
+        const float *dy = p->dy;
+        if ((st = mm(1, 0, F, D, BS, w.g, F, dy, D, p->dw_2, D))) break;
+        if ((st = mm(0, 1, BS, F, D, dy, D, p->w_2, D, w.dg, F))) break;
+        block::gelu_bwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.dg, BS * F);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "gelu_bwd_kernel"))) break;
+        if ((st = mm(1, 0, D, F, BS, w.h2, D, w.dg, F, p->dw_1, F))) break;
+        if ((st = mm(0, 1, BS, D, F, w.dg, F, p->w_1, F, w.dh2, D))) break;
+        if ((st = ln_bwd(w.x2, w.dh2, w.st2, p->ln2_gamma, dy, w.dx2, w.part, p->dln2_gamma,
+                         p->dln2_beta, BS, D, s))) break;
+        if ((st = mm(1, 0, D, D, BS, w.o, D, w.dx2, D, p->dw_o, D))) break;
+        if ((st = mm(0, 1, BS, D, D, w.dx2, D, p->w_o, D, w.dO, D))) break;
+        block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
+            w.doh, w.dO, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 1);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
+        if ((st = mm(0, 1, S, S, Dh, w.doh, Dh, w.v, Dh, w.dP, S, BH, S * Dh, S * Dh, S * S))) break;
+        if ((st = mm(1, 0, S, Dh, S, w.P, S, w.doh, Dh, w.dv, Dh, BH, S * S, S * Dh, S * Dh))) break;
+        if ((st = softmax_bwd_scaled(w.P, w.dP, BH * S, S, scale, s))) break;
+        if ((st = mm(0, 0, S, Dh, S, w.dP, S, w.k, Dh, w.dq, Dh, BH, S * S, S * Dh, S * Dh))) break;
+        if ((st = mm(1, 0, S, Dh, S, w.dP, S, w.q, Dh, w.dk, Dh, BH, S * S, S * Dh, S * Dh))) break;
+        block::qkv_permute_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
+            w.dqkv, w.dq, w.dk, w.dv, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 1);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
+        if ((st = mm(1, 0, D, 3 * D, BS, w.h1, D, w.dqkv, 3 * D, p->dw_qkv, 3 * D))) break;
+        if ((st = mm(0, 1, BS, D, 3 * D, w.dqkv, 3 * D, p->w_qkv, 3 * D, w.dh1, D))) break;
+        if ((st = ln_bwd(p->x, w.dh1, w.st1, p->ln1_gamma, w.dx2, p->dx, w.part, p->dln1_gamma,
+                         p->dln1_beta, BS, D, s))) break;
+    } while (0);
+    if (owned) scratch_free(owned, s);
+    return st;
+}

@@ -8,5 +8,6 @@
 #include "chain.cu"
 #include "portfolio.cu"
 #include "mlp.cu"
+#include "block.cu"
 #include "abi.cu"
 #include "chain_noalloc.cu"

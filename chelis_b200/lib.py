@@ -36,6 +36,15 @@ class GpuTensor(ctypes.Structure):
     ]
 
 
+class BlockParams(ctypes.Structure):
+    """chelis_block_params (include/chelis_cuda.h)."""
+    _fields_ = [(n, c_i64) for n in ("batch", "seq", "d_model", "heads", "d_ff")] + [
+        ("eps", c_f32)] + [(n, c_vp) for n in (
+            "x", "dy", "w_qkv", "w_o", "w_1", "w_2", "ln1_gamma", "ln1_beta", "ln2_gamma",
+            "ln2_beta", "y", "dx", "dw_qkv", "dw_o", "dw_1", "dw_2", "dln1_gamma", "dln1_beta",
+            "dln2_gamma", "dln2_beta")]
+
+
 DTYPE_F32, DTYPE_F64, DTYPE_I32, DTYPE_BOOL, DTYPE_I64 = 0, 1, 2, 3, 4
 GEMM_3XTF32, GEMM_EXACT_TREE = 0, 1
 ROWS_EXACT, ROWS_FAST = 0, 1
@@ -104,6 +113,8 @@ SIGNATURES = {
     "chelis_cuda_cumsum_f32": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int]),
     "chelis_cuda_portfolio_f64": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "chelis_cuda_mlp_step": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "chelis_cuda_block_workspace_bytes": (c_i64, [ctypes.POINTER(BlockParams)]),
+    "chelis_cuda_block_step": (c_int, [ctypes.POINTER(BlockParams), c_vp]),
     "chelis_chain_fwd_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_chain_grad_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_portfolio_device": (c_int, [_PP, c_i32, _PP, c_i32]),

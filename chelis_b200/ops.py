@@ -236,6 +236,53 @@ def portfolio(r: torch.Tensor, w: torch.Tensor):
     return sigma, risk, cum
 
 
+BLOCK_WEIGHTS = ("w_qkv", "w_o", "w_1", "w_2", "ln1_gamma", "ln1_beta", "ln2_gamma", "ln2_beta")
+
+
+def block_step(x, weights: dict, heads: int, eps: float = 1e-5, dy=None, workspace=None,
+               out: dict | None = None):
+    """Transformer block forward (+ vector-Jacobian product when dy is given).
+    Returns a dict with y and, with dy, dx and d<weight> for every weight."""
+    import ctypes
+    _prepare(x, dy, *[weights[k] for k in BLOCK_WEIGHTS])
+    batch, seq, d = x.shape
+    dff = weights["w_1"].shape[1]
+    o = out if out is not None else {}
+    if "y" not in o:
+        o["y"] = torch.empty_like(x)
+    if dy is not None:
+        if "dx" not in o:
+            o["dx"] = torch.empty_like(x)
+        for k in BLOCK_WEIGHTS:
+            if "d" + k not in o:
+                o["d" + k] = torch.empty_like(weights[k])
+    p = L.BlockParams()
+    p.batch, p.seq, p.d_model, p.heads, p.d_ff, p.eps = batch, seq, d, heads, dff, eps
+    p.x = x.data_ptr()
+    p.dy = dy.data_ptr() if dy is not None else None
+    for k in BLOCK_WEIGHTS:
+        setattr(p, k, weights[k].data_ptr())
+    p.y = o["y"].data_ptr()
+    if dy is not None:
+        p.dx = o["dx"].data_ptr()
+        for k in BLOCK_WEIGHTS:
+            setattr(p, "d" + k if k.startswith("w") else "d" + k, o["d" + k].data_ptr())
+    L.call("chelis_cuda_block_step", ctypes.byref(p),
+           None if workspace is None else workspace.data_ptr())
+    return o
+
+
+def block_workspace(x, weights: dict, heads: int) -> torch.Tensor:
+    import ctypes
+    batch, seq, d = x.shape
+    p = L.BlockParams()
+    p.batch, p.seq, p.d_model, p.heads, p.d_ff = batch, seq, d, heads, weights["w_1"].shape[1]
+    nbytes = int(L.load().chelis_cuda_block_workspace_bytes(ctypes.byref(p)))
+    if nbytes < 0:
+        raise ValueError("transformer block shape not admitted")
+    return torch.empty(nbytes // 4 + 64, dtype=torch.float32, device=x.device)
+
+
 def mlp_step(x, labels, w1, b1, w2, b2):
     _prepare(x, labels, w1, b1, w2, b2)
     batch, din = x.shape

@@ -101,3 +101,51 @@ def torch_mlp_inputs(seed=0, device="cuda", **shape):
     import torch
     arrs = mlp_inputs(seed=seed, **shape)
     return tuple(torch.from_numpy(np.ascontiguousarray(a)).to(device) for a in arrs)
+
+
+# ---- config 4: transformer block, B=8, S=2048, d=1024, 16 heads x 64, ff 4096, seed 3
+BLOCK_SHAPE = dict(batch=8, seq=2048, d_model=1024, heads=16, d_ff=4096)
+
+
+def block_inputs(batch=8, seq=2048, d_model=1024, heads=16, d_ff=4096, seed=3):
+    """x ~ N(0,1), upstream cotangent dy ~ N(0,1), Xavier-uniform weights
+    (bound sqrt(6 / (fan_in + fan_out)) per matrix; the q, k, v blocks of
+    w_qkv are three d x d matrices), layer-norm gamma = 1, beta = 0."""
+    rng = np.random.default_rng(seed)
+    d, f = d_model, d_ff
+
+    def xavier(fi, fo, shape):
+        a = np.sqrt(6.0 / (fi + fo))
+        return rng.uniform(-a, a, size=shape).astype(np.float32)
+
+    x = rng.standard_normal((batch, seq, d), dtype=np.float32)
+    dy = rng.standard_normal((batch, seq, d), dtype=np.float32)
+    w = {
+        "w_qkv": np.concatenate([xavier(d, d, (d, d)) for _ in range(3)], axis=1),
+        "w_o": xavier(d, d, (d, d)),
+        "w_1": xavier(d, f, (d, f)),
+        "w_2": xavier(f, d, (f, d)),
+        "ln1_gamma": np.ones(d, np.float32), "ln1_beta": np.zeros(d, np.float32),
+        "ln2_gamma": np.ones(d, np.float32), "ln2_beta": np.zeros(d, np.float32),
+    }
+    return x, dy, w
+
+
+def torch_block_inputs(batch=8, seq=2048, d_model=1024, heads=16, d_ff=4096, seed=3, device="cuda"):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    d, f = d_model, d_ff
+
+    def xavier(fi, fo, shape):
+        a = float(np.sqrt(6.0 / (fi + fo)))
+        return (torch.rand(shape, generator=g, device=device) * 2 - 1) * a
+
+    x = torch.randn((batch, seq, d), generator=g, device=device)
+    dy = torch.randn((batch, seq, d), generator=g, device=device)
+    w = {
+        "w_qkv": torch.cat([xavier(d, d, (d, d)) for _ in range(3)], dim=1).contiguous(),
+        "w_o": xavier(d, d, (d, d)), "w_1": xavier(d, f, (d, f)), "w_2": xavier(f, d, (f, d)),
+        "ln1_gamma": torch.ones(d, device=device), "ln1_beta": torch.zeros(d, device=device),
+        "ln2_gamma": torch.ones(d, device=device), "ln2_beta": torch.zeros(d, device=device),
+    }
+    return x, dy, w

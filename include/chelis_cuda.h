@@ -300,6 +300,31 @@ int chelis_cuda_mlp_step(const float *x, const int64_t *labels, const float *w1,
                          int64_t din, int64_t dh, int64_t dout, float *loss, float *dw1,
                          float *db1, float *dw2, float *db2);
 
+/* A pre-LN transformer block (the post-LN ReLU block of
+ * examples/transformer_block.ch rearranged): causal multi-head softmax
+ * attention (spec/05-risc-primitives.md:5146-5181), layer_norm
+ * (:5065-5093) and a GELU MLP (gelu = m(x)*Phi(x), :1353-1400), forward and,
+ * when dy != NULL, the vector-Jacobian product for upstream cotangent dy.
+ * Row-major f32; w_qkv is [d_model, 3*d_model] with the q, k and v column
+ * blocks in that order and heads contiguous inside each (head h owns
+ * columns h*head_dim .. (h+1)*head_dim - 1 of a block); no biases.  The
+ * attention scale is 1/sqrt(head_dim). */
+typedef struct {
+    int64_t batch, seq, d_model, heads, d_ff;
+    float eps;
+    const float *x, *dy;                 /* [batch, seq, d_model]; dy may be NULL */
+    const float *w_qkv, *w_o, *w_1, *w_2;
+    const float *ln1_gamma, *ln1_beta, *ln2_gamma, *ln2_beta;
+    float *y, *dx;
+    float *dw_qkv, *dw_o, *dw_1, *dw_2;
+    float *dln1_gamma, *dln1_beta, *dln2_gamma, *dln2_beta;
+} chelis_block_params;
+/* Bytes of device workspace chelis_cuda_block_step needs (-1: shape not admitted). */
+int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p);
+/* workspace: device memory of chelis_cuda_block_workspace_bytes bytes, or
+ * NULL to take it from the library's stream-ordered pool for the call. */
+int chelis_cuda_block_step(const chelis_block_params *p, void *workspace);
+
 /* =========================================================================
  * Generated-entry device ABI (emit.rs:838-958, `f_device`): inputs borrowed,
  * outputs newly allocated owners the caller releases.  One entry per program
