@@ -275,12 +275,6 @@ def bench_extras(args, peaks):
         ms = timed(lambda: ops.matmul(a, b, out=c), 10)
         sweep[str(n)] = round(2 * n ** 3 / ms / 1e9, 2)
     out["gemm_f32_sweep_tflops"] = sweep
-    # batched 256 x 512^3 f32
-    a, b = W.torch_gemm_inputs(512, 512, 512, torch.float32, seed=1, batch=256)
-    c = torch.empty((256, 512, 512), dtype=torch.float32, device="cuda")
-    ms = timed(lambda: ops.matmul(a, b, out=c), 10)
-    out["gemm_f32_batched_256x512"] = {"tflops": round(256 * 2 * 512 ** 3 / ms / 1e9, 2),
-                                       "ms": round(ms, 3)}
     del a, b, c
     # fused chain fwd / adjoint
     x, g, be = W.torch_chain_inputs()
@@ -300,19 +294,69 @@ def bench_extras(args, peaks):
     out["chain_bwd"] = {"gbs": round(bbytes / bms / 1e6, 1), "ms": round(bms, 4),
                         "frac_hbm": round(bbytes / bms / 1e6 / hbm, 3)}
     del x, g, be, state
-    # vmap covariance / risk
-    r, w = W.torch_portfolio_inputs()
-    ms = timed(lambda: ops.portfolio(r, w), 3, 1)
-    cnt = r.shape[0]
-    pbytes = r.numel() * 8 + w.numel() * 8 + cnt * (64 * 64 + 1 + 252) * 8
-    out["portfolio"] = {"portfolios_per_s": round(cnt / ms * 1e3, 1), "ms": round(ms, 3),
-                        "gbs": round(pbytes / ms / 1e6, 1),
-                        "fp64_tflops": round(cnt * 2.10e6 / ms / 1e9, 2)}
-    del r, w
     # MLP step
     x, labels, w1, b1, w2, b2 = W.torch_mlp_inputs()
     ms = timed(lambda: ops.mlp_step(x, labels, w1, b1, w2, b2), 20)
     out["mlp_step"] = {"us_per_step": round(ms * 1e3, 1)}
+    return out
+
+
+def bench_sharded(args, world, rank, peaks):
+    """The configurations that shard across GPUs, at every N (max over ranks):
+    config 4 data-parallel (per-rank batch shard of 8, one NCCL all-reduce of
+    the flat gradient buffer per step), config 5 and the batched GEMM of
+    config 2 along their vmap axis (no collective)."""
+    import torch
+    from chelis_b200 import dp, ops, workloads as W
+    out = {}
+    # config 4: transformer block fwd + VJP, DP over the global batch of 8
+    shape = dict(W.BLOCK_SHAPE)
+    a, b = dp.shard(shape["batch"], world, rank)
+    local = dict(shape, batch=b - a)
+    x, dy, w = W.torch_block_inputs(seed=3 + rank, **local)
+    names = list(ops.BLOCK_WEIGHTS)
+    grads = dp.FlatGrads({"d" + k: tuple(w[k].shape) for k in names}, "cuda")
+    res = {"y": torch.empty_like(x), "dx": torch.empty_like(x)}
+    res.update({k: grads[k] for k in grads.views})
+    ws = ops.block_workspace(x, w, shape["heads"])
+
+    def step():
+        ops.block_step(x, w, shape["heads"], 1e-5, dy, workspace=ws, out=res)
+        dp.allreduce_sum(grads.flat, world)
+
+    for _ in range(3):
+        step()
+    steps = 5
+    ms = time_region(step, steps, world) / steps
+    S, D, F = shape["seq"], shape["d_model"], shape["d_ff"]
+    per_sample = 3 * (2 * S * 3 * D * D + 2 * S * S * D + 2 * S * D * D + 4 * S * D * F)
+    out["block_dp"] = {"samples_per_s": round(shape["batch"] / ms * 1e3, 1),
+                       "ms_per_step": round(ms, 3), "per_rank_batch": b - a,
+                       "tflops": round(shape["batch"] * per_sample / ms / 1e9, 1),
+                       "flop_per_sample": per_sample,
+                       "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1),
+                       "scaling": "strong (global batch 8)"}
+    del x, dy, w, grads, res, ws
+    # config 5: covariance / risk, 65536 portfolios split across ranks
+    cnt = W.PORTFOLIO_SHAPE["count"]
+    a, b = dp.shard(cnt, world, rank)
+    r, wv = W.torch_portfolio_inputs(count=b - a, seed=4 + rank)
+    for _ in range(2):
+        ops.portfolio(r, wv)
+    ms = time_region(lambda: ops.portfolio(r, wv), 3, world) / 3
+    out["portfolio_vmap"] = {"portfolios_per_s": round(cnt / ms * 1e3, 1), "ms": round(ms, 3),
+                             "fp64_tflops": round(cnt * 2.10e6 / ms / 1e9, 2),
+                             "scaling": "strong (65536 portfolios)"}
+    del r, wv
+    # config 2b: 256 x [512 x 512] . [512 x 512] f32, batch split across ranks
+    a, b = dp.shard(256, world, rank)
+    A, B = W.torch_gemm_inputs(512, 512, 512, torch.float32, seed=1 + rank, batch=b - a)
+    C = torch.empty((b - a, 512, 512), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        ops.matmul(A, B, out=C)
+    ms = time_region(lambda: ops.matmul(A, B, out=C), 10, world) / 10
+    out["gemm_batched_vmap"] = {"tflops": round(256 * 2 * 512 ** 3 / ms / 1e9, 2),
+                                "ms": round(ms, 3), "scaling": "strong (batch 256)"}
     return out
 
 
@@ -392,8 +436,9 @@ def main():
     peaks = load_peaks()
     res = bench_gemm_headline(args, world, rank, peaks)
     extras = None
-    if world == 1 and not args.no_extras:
-        extras = bench_extras(args, peaks)
+    if not args.no_extras:
+        extras = bench_extras(args, peaks) if world == 1 else {}
+        extras.update(bench_sharded(args, world, rank, peaks))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
