@@ -46,6 +46,8 @@ enum : unsigned int {
     DEVERR_TIMEOUT_PRODUCER = 1u,
     DEVERR_TIMEOUT_MMA = 2u,
     DEVERR_TIMEOUT_EPILOGUE = 4u,
+    DEVERR_TIMEOUTS = 7u,
+    DEVERR_BAD_INDEX = 8u,  // an index operand outside its axis ([05-OP-52])
 };
 
 __device__ __forceinline__ void report_device_error(unsigned int code) {

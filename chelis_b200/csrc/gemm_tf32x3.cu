@@ -330,14 +330,17 @@ int make_kmajor_map(CUtensorMap *map, const float *base, int64_t rows, int64_t k
 // ---------------------------------------------------------------------------
 // exact canonical-tree GEMM on CUDA cores (bit-identical to the C lane's
 // inlined product sum, crates/chelis-backend-c/src/emit.rs:8431-8640).
-// Each thread owns 1 row x 4 columns.  Leaves fl(a*b) enter, in increasing
-// k, a carry tree: an aligned block of 32 leaves is a complete subtree and
-// is reduced with a static schedule; block sums (and a final partial block)
-// enter an outer carry tree whose levels live in registers.
+// A CTA is 8 warps; warp w owns output row r0 + w and 32 columns.  For each
+// aligned block of 32 leaves (k0 .. k0+31, a complete subtree of the
+// canonical tree over k) lane l forms the 32 products a[r, k0+l]*b[k0+l, j]
+// and a halving warp butterfly reduces them: adjacent leaves pair first, as
+// the tree requires, and every lane ends holding the block sum of one
+// column.  Block sums (and a ragged last block, the tree of its prefix)
+// then enter that lane's outer carry tree, whose levels live in registers.
 // ---------------------------------------------------------------------------
 namespace exact {
 
-constexpr int TM = 32, TN = 32, TK = 32, THREADS = 256;
+constexpr int RW = 8, TN = 32, TK = 32, THREADS = 256;
 constexpr int MAXD = 14;  // outer levels: up to 2^14 blocks of 32 (k <= 524288)
 
 template <typename T>
@@ -389,81 +392,67 @@ __device__ __forceinline__ T total(const Carry<T> &t, uint32_t count) {
     return tot;
 }
 
+// Halving butterfly over 32 values per lane.  `valid` marks the lane's leaf
+// as present (lanes holding leaves past the end of k are absent: the tree of
+// a prefix).  Returns the lane's block sum; `col` = the column it belongs to.
+template <typename T, bool FULL>
+__device__ __forceinline__ T block_butterfly(T (&v)[TN], int lane, bool valid, int &col) {
+    col = 0;
+    bool vs = valid;
+#pragma unroll
+    for (int cnt = TN, off = 1; cnt > 1; cnt >>= 1, off <<= 1) {
+        const bool bit = (lane & off) != 0;
+        const bool vp = FULL ? true : (__shfl_xor_sync(0xffffffffu, vs ? 1 : 0, off) != 0);
+#pragma unroll
+        for (int j = 0; j < cnt / 2; ++j) {
+            const T send = bit ? v[j] : v[j + cnt / 2];
+            const T keep = bit ? v[j + cnt / 2] : v[j];
+            const T recv = __shfl_xor_sync(0xffffffffu, send, off);
+            v[j] = FULL ? add_rn(keep, recv) : tree_pair(keep, vs, recv, vp);
+        }
+        vs = vs || vp;
+        if (bit) col += cnt / 2;
+    }
+    return v[0];
+}
+
 template <typename T>
 __global__ void __launch_bounds__(THREADS)
     gemm_exact_kernel(int64_t m, int64_t n, int64_t k, const T *__restrict__ a, int64_t sa_r,
                       int64_t sa_k, int64_t sa_b, const T *__restrict__ b, int64_t sb_k,
                       int64_t sb_c, int64_t sb_b, T *__restrict__ c, int64_t ldc,
                       int64_t sc_b) {
-    __shared__ T as[TM][TK + 1];
     __shared__ T bs[TK][TN + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t bb = blockIdx.z;
-    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * TM;
+    const int64_t row = static_cast<int64_t>(blockIdx.y) * RW + warp;
     const int64_t c0 = static_cast<int64_t>(blockIdx.x) * TN;
-    const int tr = threadIdx.x / 8;       // 0..31 row in tile
-    const int tc = (threadIdx.x % 8) * 4;  // 0..28 first of 4 columns
     a += bb * sa_b;
     b += bb * sb_b;
-    Carry<T> tree[4];
+    Carry<T> tree;
     uint32_t blocks = 0;
+    int col = lane;
     for (int64_t k0 = 0; k0 < k; k0 += TK) {
-        for (int i = threadIdx.x; i < TM * TK; i += THREADS) {
-            int rr = i / TK, kk = i % TK;
-            int64_t gr = r0 + rr, gk = k0 + kk;
-            as[rr][kk] = (gr < m && gk < k) ? a[gr * sa_r + gk * sa_k] : T(0);
-        }
         for (int i = threadIdx.x; i < TK * TN; i += THREADS) {
-            int kk = i / TN, cc = i % TN;
-            int64_t gk = k0 + kk, gc = c0 + cc;
+            const int kk = i / TN, cc = i % TN;
+            const int64_t gk = k0 + kk, gc = c0 + cc;
             bs[kk][cc] = (gc < n && gk < k) ? b[gk * sb_k + gc * sb_c] : T(0);
         }
         __syncthreads();
         const int64_t valid = (k - k0) < TK ? (k - k0) : TK;
+        const bool lv = lane < valid;
+        const T av = (row < m && lv) ? a[row * sa_r + (k0 + lane) * sa_k] : T(0);
+        T v[TN];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            // streaming carry tree over the `valid` leaves of this block; a
-            // full block (valid == 32) reduces to the perfect 32-leaf subtree
-            T lv[6];
-            uint32_t cnt = 0;
-            for (int kk = 0; kk < valid; ++kk) {
-                T carry = mul_rn(as[tr][kk], bs[kk][tc + j]);
-                bool active = true;
-#pragma unroll
-                for (int d = 0; d < 6; ++d) {
-                    const bool bit = (cnt >> d) & 1u;
-                    if (active) {
-                        if (bit) {
-                            carry = add_rn(lv[d], carry);
-                        } else {
-                            lv[d] = carry;
-                            active = false;
-                        }
-                    }
-                }
-                ++cnt;
-            }
-            T bsum = T(0);
-            bool found = false;
-#pragma unroll
-            for (int d = 0; d < 6; ++d) {
-                if ((cnt >> d) & 1u) {
-                    bsum = found ? add_rn(lv[d], bsum) : lv[d];
-                    found = true;
-                }
-            }
-            push(tree[j], blocks, bsum);
-        }
+        for (int j = 0; j < TN; ++j) v[j] = mul_rn(av, bs[lane][j]);
+        const T s = (valid == TK) ? block_butterfly<T, true>(v, lane, lv, col)
+                                  : block_butterfly<T, false>(v, lane, lv, col);
+        push(tree, blocks, s);
         ++blocks;
         __syncthreads();
     }
-    const int64_t gr = r0 + tr;
-    if (gr < m) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int64_t gc = c0 + tc + j;
-            if (gc < n) c[bb * sc_b + gr * ldc + gc] = k > 0 ? total(tree[j], blocks) : T(0);
-        }
-    }
+    const int64_t gc = c0 + col;
+    if (row < m && gc < n) c[bb * sc_b + row * ldc + gc] = k > 0 ? total(tree, blocks) : T(0);
 }
 
 }  // namespace exact
@@ -472,10 +461,13 @@ template <typename T>
 int launch_exact_gemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const T *a,
                       int64_t lda, int64_t stride_a, const T *b, int64_t ldb, int64_t stride_b,
                       T *c, int64_t ldc, int64_t stride_c, int64_t batch, cudaStream_t s) {
+    if (k > static_cast<int64_t>(exact::TK) << exact::MAXD)
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "exact-tree matmul admits k <= %lld",
+                         static_cast<long long>(exact::TK) << exact::MAXD);
     int64_t sa_r = trans_a ? 1 : lda, sa_k = trans_a ? lda : 1;
     int64_t sb_k = trans_b ? 1 : ldb, sb_c = trans_b ? ldb : 1;
     dim3 grid(static_cast<unsigned>((n + exact::TN - 1) / exact::TN),
-              static_cast<unsigned>((m + exact::TM - 1) / exact::TM),
+              static_cast<unsigned>((m + exact::RW - 1) / exact::RW),
               static_cast<unsigned>(batch));
     exact::gemm_exact_kernel<T><<<grid, exact::THREADS, 0, s>>>(
         m, n, k, a, sa_r, sa_k, stride_a, b, sb_k, sb_c, stride_b, c, ldc, stride_c);

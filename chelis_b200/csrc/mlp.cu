@@ -49,8 +49,7 @@ __global__ void relu_adjoint_kernel(const float *__restrict__ pre, float *__rest
 // dz = softmax adjoint of g = (onehot * (-1/B)) / s.
 __global__ void ce_rows_kernel(float *__restrict__ z, const float *__restrict__ b2,
                                const int64_t *__restrict__ labels, int64_t rows, int classes,
-                               float dsel, float *__restrict__ nl, float *__restrict__ dz,
-                               int *__restrict__ bad_label) {
+                               float dsel, float *__restrict__ nl, float *__restrict__ dz) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (row >= rows) return;
@@ -68,7 +67,9 @@ __global__ void ce_rows_kernel(float *__restrict__ z, const float *__restrict__ 
     const float s = __fdiv_rn(e, zsum);
     const int64_t label = labels[row];
     if (label < 0 || label >= classes) {
-        if (lane == 0) atomicExch(bad_label, 1);
+        // [05-OP-52] out-of-range gather index: recorded in the device error
+        // word and reported by chelis_cuda_device_status (no host sync here)
+        if (lane == 0) report_device_error(DEVERR_BAD_INDEX);
         return;
     }
     const float s_label = __shfl_sync(0xffffffffu, s, static_cast<int>(label));
@@ -103,6 +104,74 @@ __global__ void mean_kernel(const float *__restrict__ nl, int64_t n, float *__re
     *loss = __fdiv_rn(total, static_cast<float>(n));
 }
 
+// Column sums of a small [rows, cols] matrix, one warp per column: lane l
+// takes row k0 + l of each aligned 32-row block (a subtree of the canonical
+// tree over rows), the block sums go through lane 0's carry tree.  With
+// `divide`, the total is divided by rows (the mean lowering).
+__global__ void col_tree_warp_kernel(const float *__restrict__ x, int64_t rows, int64_t cols,
+                                     float *__restrict__ out, bool divide) {
+    const int lane = threadIdx.x & 31;
+    const int64_t col = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (col >= cols) return;
+    float level[40];
+    int64_t count = 0;
+    for (int64_t r0 = 0; r0 < rows; r0 += 32) {
+        bool valid = r0 + lane < rows;
+        float v = valid ? x[(r0 + lane) * cols + col] : 0.0f;
+        v = warp_tree(v, valid);
+        if (lane == 0) {
+            float carry = v;
+            int depth = 0;
+            for (int64_t pending = count; pending & 1; pending >>= 1, ++depth)
+                carry = __fadd_rn(level[depth], carry);
+            level[depth] = carry;
+        }
+        ++count;
+    }
+    if (lane == 0) {
+        float total = 0.0f;
+        bool found = false;
+        int depth = 0;
+        for (int64_t remaining = count; remaining; remaining >>= 1, ++depth)
+            if (remaining & 1) {
+                total = found ? __fadd_rn(level[depth], total) : level[depth];
+                found = true;
+            }
+        out[col] = divide ? __fdiv_rn(total, static_cast<float>(rows)) : total;
+    }
+}
+
+// pre = tree over `nk` k-chunk partial sums (each an aligned power-of-two
+// block of the contraction, so a subtree of the canonical tree) + bias;
+// h = relu(pre).
+__global__ void combine_bias_relu_kernel(const float *__restrict__ part, int nk, int64_t mn,
+                                         const float *__restrict__ bias, int64_t cols,
+                                         float *__restrict__ pre, float *__restrict__ h) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < mn;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float level[8];
+        int count = 0;
+        for (int c = 0; c < nk; ++c) {
+            float carry = part[c * mn + i];
+            int depth = 0;
+            for (int pending = count++; pending & 1; pending >>= 1, ++depth)
+                carry = __fadd_rn(level[depth], carry);
+            level[depth] = carry;
+        }
+        float total = 0.0f;
+        bool found = false;
+        int depth = 0;
+        for (int remaining = count; remaining; remaining >>= 1, ++depth)
+            if (remaining & 1) {
+                total = found ? __fadd_rn(level[depth], total) : level[depth];
+                found = true;
+            }
+        const float v = __fadd_rn(total, bias[i % cols]);
+        pre[i] = v;
+        h[i] = (v < 0.0f) ? 0.0f : v;
+    }
+}
+
 }  // namespace mlp
 }  // namespace chelis
 
@@ -118,45 +187,64 @@ extern "C" int chelis_cuda_mlp_step(const float *x, const int64_t *labels, const
     if (dout > 32)
         return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "cross_entropy kernel admits <= 32 classes");
     cudaStream_t s = current_stream();
-    // scratch: pre, h, dh [batch, dh]; z, dz [batch, dout]; nl [batch]; flag
+    // The first product (k = din) is split along k into aligned chunks of
+    // KC leaves computed in parallel; every chunk is a subtree of the
+    // canonical tree, so combining the chunk sums pass by pass gives the
+    // same bits as one tree over k.
+    constexpr int64_t KC = 256;
+    const int64_t nk = (din + KC - 1) / KC;
+    if (nk > 255)
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "mlp input width beyond %lld", 255 * KC);
+    // scratch: k-chunk partials; pre, h, dh [batch, dh]; z, dz [batch, dout]; nl [batch]
     const size_t bh = static_cast<size_t>(batch * dh), bo = static_cast<size_t>(batch * dout);
-    const size_t bytes = (3 * bh + 2 * bo + batch) * sizeof(float) + 16;
+    const size_t bytes = (nk * bh + 3 * bh + 2 * bo + batch) * sizeof(float) + 16;
     void *scratch = nullptr;
     CHELIS_TRY(scratch_alloc(&scratch, bytes, s));
-    float *pre = static_cast<float *>(scratch);
+    float *part = static_cast<float *>(scratch);
+    float *pre = part + nk * bh;
     float *h = pre + bh;
     float *dhid = h + bh;
     float *z = dhid + bh;
     float *dz = z + bo;
     float *nl = dz + bo;
-    int *bad = reinterpret_cast<int *>(nl + batch);
     int st = CHELIS_CUDA_OK;
     auto launch_blocks = [](int64_t n) {
         int64_t b = (n + 255) / 256;
         return static_cast<unsigned>(b > 148 * 8 ? 148 * 8 : (b < 1 ? 1 : b));
     };
     do {
-        st = check_cuda(cudaMemsetAsync(bad, 0, sizeof(int), s), "memset");
-        if (st) break;
-        // forward
-        st = launch_exact_gemm<float>(0, 0, batch, dh, din, x, din, 0, w1, dh, 0, pre, dh, 0, 1, s);
-        if (st) break;
-        mlp::bias_relu_kernel<<<launch_blocks(bh), 256, 0, s>>>(pre, h, b1, batch, dh);
+        // forward: full chunks as one batched launch, the ragged tail apart
+        const int64_t full = din / KC, tail = din - full * KC;
+        if (full > 0) {
+            st = launch_exact_gemm<float>(0, 0, batch, dh, KC, x, din, KC, w1, dh, KC * dh, part,
+                                          dh, static_cast<int64_t>(bh), full, s);
+            if (st) break;
+        }
+        if (tail > 0) {
+            st = launch_exact_gemm<float>(0, 0, batch, dh, tail, x + full * KC, din, 0,
+                                          w1 + full * KC * dh, dh, 0, part + full * bh, dh, 0, 1, s);
+            if (st) break;
+        }
+        mlp::combine_bias_relu_kernel<<<launch_blocks(bh), 256, 0, s>>>(
+            part, static_cast<int>(nk), static_cast<int64_t>(bh), b1, dh, pre, h);
         g_launches++;
-        if ((st = check_cuda(cudaGetLastError(), "bias_relu_kernel"))) break;
+        if ((st = check_cuda(cudaGetLastError(), "combine_bias_relu_kernel"))) break;
         st = launch_exact_gemm<float>(0, 0, batch, dout, dh, h, dh, 0, w2, dout, 0, z, dout, 0, 1, s);
         if (st) break;
         const float bf = static_cast<float>(batch);
         const float dnl = 1.0f / bf;
         mlp::ce_rows_kernel<<<static_cast<unsigned>((batch * 32 + 255) / 256), 256, 0, s>>>(
-            z, b2, labels, batch, static_cast<int>(dout), -dnl, nl, dz, bad);
+            z, b2, labels, batch, static_cast<int>(dout), -dnl, nl, dz);
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "ce_rows_kernel"))) break;
-        mlp::mean_kernel<<<1, 32, 0, s>>>(nl, batch, loss);
+        mlp::col_tree_warp_kernel<<<1, 32, 0, s>>>(nl, batch, 1, loss, true);
         g_launches++;
-        if ((st = check_cuda(cudaGetLastError(), "mean_kernel"))) break;
-        // adjoint
-        if ((st = col_sum_into(dz, batch, dout, db2, s))) break;
+        if ((st = check_cuda(cudaGetLastError(), "col_tree_warp_kernel"))) break;
+        // adjoint; the bias gradients are column trees over the batch
+        const unsigned cbo = static_cast<unsigned>((dout * 32 + 255) / 256);
+        mlp::col_tree_warp_kernel<<<cbo, 256, 0, s>>>(dz, batch, dout, db2, false);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "col_tree_warp_kernel"))) break;
         st = launch_exact_gemm<float>(1, 0, dh, dout, batch, h, dh, 0, dz, dout, 0, dw2, dout, 0, 1, s);
         if (st) break;
         st = launch_exact_gemm<float>(0, 1, batch, dh, dout, dz, dout, 0, w2, dout, 0, dhid, dh, 0, 1, s);
@@ -164,15 +252,12 @@ extern "C" int chelis_cuda_mlp_step(const float *x, const int64_t *labels, const
         mlp::relu_adjoint_kernel<<<launch_blocks(bh), 256, 0, s>>>(pre, dhid, bh);
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "relu_adjoint_kernel"))) break;
-        if ((st = col_sum_into(dhid, batch, dh, db1, s))) break;
+        const unsigned cbh = static_cast<unsigned>((dh * 32 + 255) / 256);
+        mlp::col_tree_warp_kernel<<<cbh, 256, 0, s>>>(dhid, batch, dh, db1, false);
+        g_launches++;
+        if ((st = check_cuda(cudaGetLastError(), "col_tree_warp_kernel"))) break;
         st = launch_exact_gemm<float>(1, 0, din, dh, batch, x, din, 0, dhid, dh, 0, dw1, dh, 0, 1, s);
         if (st) break;
-        int flag = 0;
-        st = check_cuda(cudaMemcpyAsync(&flag, bad, sizeof(int), cudaMemcpyDeviceToHost, s), "copy flag");
-        if (st) break;
-        st = check_cuda(cudaStreamSynchronize(s), "sync");
-        if (st) break;
-        if (flag) st = set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in gather at i64");
     } while (0);
     scratch_free(scratch, s);
     return st;

@@ -265,8 +265,10 @@ int chelis_cuda_device_status(void) {
     if (word) {
         CHELIS_TRY(check_cuda(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)),
                               "clear device error word"));
-        return set_error(CHELIS_CUDA_ERR_TIMEOUT,
-                         "a bounded device wait gave up (error word 0x%x)", word);
+        if (word & DEVERR_TIMEOUTS)
+            return set_error(CHELIS_CUDA_ERR_TIMEOUT,
+                             "a bounded device wait gave up (error word 0x%x)", word);
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in gather at i64");
     }
     return CHELIS_CUDA_OK;
 }

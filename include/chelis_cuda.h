@@ -100,8 +100,9 @@ int chelis_cuda_init(int32_t device);
 int chelis_cuda_set_stream(void *cuda_stream);
 void *chelis_cuda_get_stream(void);
 int chelis_cuda_synchronize(void);
-/* Read-and-clear the device error word (bounded-wait timeouts); returns
- * CHELIS_CUDA_ERR_TIMEOUT if any kernel gave up since the last call.
+/* Read-and-clear the device error word: CHELIS_CUDA_ERR_TIMEOUT if a bounded
+ * device wait gave up, CHELIS_CUDA_ERR_DOMAIN if an index operand was out of
+ * range ([05-OP-52]), since the last call.
  * Synchronises the stream.  Replaces the debug failure flag readback of
  * chelis_hip_runtime.h:487-524. */
 int chelis_cuda_device_status(void);
@@ -294,7 +295,10 @@ int chelis_cuda_portfolio_f64(const double *r, const double *w, int64_t count, i
                               int64_t a, double *sigma, double *risk, double *cum);
 
 /* 2-layer MLP forward + adjoint (matmul, add, relu, softmax cross-entropy,
- * mean; grads w.r.t. w1, b1, w2, b2).  labels are i64 class ids. */
+ * mean; grads w.r.t. w1, b1, w2, b2).  labels are i64 class ids.  The call
+ * does not synchronise: a label outside [0, dout) is recorded on the device
+ * and reported as CHELIS_CUDA_ERR_DOMAIN ("numeric trap: domain in gather")
+ * by the next chelis_cuda_device_status(). */
 int chelis_cuda_mlp_step(const float *x, const int64_t *labels, const float *w1,
                          const float *b1, const float *w2, const float *b2, int64_t batch,
                          int64_t din, int64_t dh, int64_t dout, float *loss, float *dw1,

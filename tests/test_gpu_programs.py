@@ -66,8 +66,10 @@ def test_mlp_step_matches_oracle(cuda, orc, shape):
 def test_mlp_rejects_out_of_range_label(cuda):
     x, labels, w1, b1, w2, b2 = W.mlp_inputs(batch=4, din=8, dh=8, dout=3)
     labels[2] = 3
+    cuda.mlp_step(t(x), t(labels), t(w1), t(b1), t(w2), t(b2))  # asynchronous
     with pytest.raises(L.ChelisCudaError, match="gather"):
-        cuda.mlp_step(t(x), t(labels), t(w1), t(b1), t(w2), t(b2))
+        cuda.device_status()
+    cuda.device_status()  # read-and-clear: the next check is clean
 
 
 def _owner_from(tensor, keep):
