@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(THREADS, 2)
     portfolio_kernel(const double *__restrict__ r_all, const double *__restrict__ w_all,
                      int64_t count, int t_len, double *__restrict__ sigma_all,
                      double *__restrict__ risk_all, double *__restrict__ cum_all) {
-    __shared__ __align__(16) double tile[CH * A];   // staged chunk (raw or centred)
+    extern __shared__ __align__(16) double tiles[];  // 2 x [CH * A]: staged chunks
+    double *tile = tiles;                           // pass 1, Sigma.w: buffer 0
     __shared__ double wv[A];
     __shared__ double mean[A];
     __shared__ double colsum[4][A];                 // per-chunk column subtree sums
@@ -194,36 +195,46 @@ __global__ void __launch_bounds__(THREADS, 2)
             const int e = tid + j * CT;
             nxt[j] = (e < CH * A && e / A < t_len) ? __ldg(R + e) : 0.0;
         }
-        for (int q = 0; q < nchunks; ++q) {
+        // centred chunk q into buffer q & 1 (rows past the end are zeros, so
+        // the k loop can always run all CH / 4 steps: they add exact zeros)
+        auto stage = [&](int q) {
             const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
+            double *buf = tiles + (q & 1) * CH * A;
 #pragma unroll
             for (int j = 0; j < PER_T; ++j) {
                 const int e = tid + j * CT;
                 if (e < CH * A) {
                     const int k = e / A, a = e % A;
-                    tile[sw(k, a)] = k < rows ? __dsub_rn(nxt[j], mean[a]) : 0.0;
+                    buf[sw(k, a)] = k < rows ? __dsub_rn(nxt[j], mean[a]) : 0.0;
                 }
             }
-            compute_sync();
-            if (q + 1 < nchunks) {
-                const double *src = R + static_cast<int64_t>(q + 1) * CH * A;
-                const int rows2 = (t_len - (q + 1) * CH) < CH ? (t_len - (q + 1) * CH) : CH;
+        };
+        auto fetch = [&](int q) {
+            const double *src = R + static_cast<int64_t>(q) * CH * A;
+            const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
 #pragma unroll
-                for (int j = 0; j < PER_T; ++j) {
-                    const int e = tid + j * CT;
-                    nxt[j] = (e < CH * A && e / A < rows2) ? __ldg(src + e) : 0.0;
-                }
+            for (int j = 0; j < PER_T; ++j) {
+                const int e = tid + j * CT;
+                nxt[j] = (e < CH * A && e / A < rows) ? __ldg(src + e) : 0.0;
             }
-            const int ksteps = (rows + 3) / 4;
-            for (int ks = 0; ks < ksteps; ++ks) {
+        };
+        stage(0);
+        compute_sync();
+        for (int q = 0; q < nchunks; ++q) {
+            if (q + 1 < nchunks) fetch(q + 1);
+            const double *buf = tiles + (q & 1) * CH * A;
+#pragma unroll
+            for (int ks = 0; ks < CH / 4; ++ks) {
                 const int k = ks * 4 + tq;
-                const double a0 = tile[sw(k, mi * 16 + g)];
-                const double a1 = tile[sw(k, mi * 16 + g + 8)];
-                const double b0 = tile[sw(k, nj * 8 + g)];
-                const double b1 = tile[sw(k, (nj + 1) * 8 + g)];
+                const double a0 = buf[sw(k, mi * 16 + g)];
+                const double a1 = buf[sw(k, mi * 16 + g + 8)];
+                const double b0 = buf[sw(k, nj * 8 + g)];
+                const double b1 = buf[sw(k, (nj + 1) * 8 + g)];
                 dmma(acc[0], a0, a1, b0);
                 dmma(acc[1], a0, a1, b1);
             }
+            // the other buffer was last read before the previous barrier
+            if (q + 1 < nchunks) stage(q + 1);
             compute_sync();
         }
         // Sigma / (T-1) for the upper entries (row <= col), mirrored
@@ -282,7 +293,11 @@ extern "C" int chelis_cuda_portfolio_f64(const double *r, const double *w, int64
     cudaStream_t s = current_stream();
     int64_t grid = static_cast<int64_t>(sm_count()) * 2;
     if (grid > count) grid = count;
-    portfolio::portfolio_kernel<<<static_cast<unsigned>(grid), portfolio::THREADS, 0, s>>>(
+    constexpr int smem = 2 * portfolio::CH * portfolio::A * sizeof(double);
+    CHELIS_TRY(check_cuda(cudaFuncSetAttribute(portfolio::portfolio_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                          "cudaFuncSetAttribute(portfolio_kernel)"));
+    portfolio::portfolio_kernel<<<static_cast<unsigned>(grid), portfolio::THREADS, smem, s>>>(
         r, w, count, static_cast<int>(t), sigma, risk, cum);
     g_launches++;
     CHELIS_LAUNCH_CHECK("portfolio_kernel");

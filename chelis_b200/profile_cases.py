@@ -1,0 +1,49 @@
+"""Small single-launch cases of each hot kernel, for profiler captures.
+
+    python -m chelis_b200.profile_cases gemm        # 8192^3 f32 3xTF32 (split + main kernel)
+    python -m chelis_b200.profile_cases dgemm       # 4096^3 f64 DMMA
+    python -m chelis_b200.profile_cases chain       # config 3 forward (saving state) + adjoint
+    python -m chelis_b200.profile_cases portfolio   # config 5, 4096 portfolios
+    python -m chelis_b200.profile_cases block       # config 4 step, batch 1
+
+Each case builds its inputs on the device, runs the hot path once and
+synchronises; inputs exceed the 126 MB L2 except where the case is smaller
+by construction (MLP-sized work is not profiled this way).
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from . import ops
+from . import workloads as W
+
+
+def run(case: str) -> None:
+    torch.cuda.set_device(0)
+    if case == "gemm":
+        a, b = W.torch_gemm_inputs(8192, 8192, 8192, torch.float32, seed=1)
+        ops.matmul(a, b)
+    elif case == "dgemm":
+        a, b = W.torch_gemm_inputs(4096, 4096, 4096, torch.float64, seed=1)
+        ops.matmul(a, b)
+    elif case == "chain":
+        x, g, be = W.torch_chain_inputs()
+        _, saved = ops.chain_fwd_save(x, g, be, 1e-5, 42, 0.1)
+        ops.chain_bwd_saved(x, g, be, 1e-5, 0.1, saved)
+    elif case == "portfolio":
+        r, w = W.torch_portfolio_inputs(count=4096)
+        ops.portfolio(r, w)
+    elif case == "block":
+        x, dy, w = W.torch_block_inputs(**dict(W.BLOCK_SHAPE, batch=1))
+        ops.block_step(x, w, W.BLOCK_SHAPE["heads"], 1e-5, dy)
+    else:
+        raise SystemExit(f"unknown case {case!r}")
+    torch.cuda.synchronize()
+    ops.device_status()
+    print("done", case)
+
+
+if __name__ == "__main__":
+    run(sys.argv[1] if len(sys.argv) > 1 else "gemm")
