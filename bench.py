@@ -201,16 +201,17 @@ def bench_gemm_headline(args, world, rank, peaks):
     ops.device_status()
     value = world * flops * args.steps / (ms * 1e-3) / 1e12
 
-    # roofline: the tcgen05 main kernel alone on pre-split operands
+    # roofline: the tcgen05 main kernel alone on pre-split operands (A K-major,
+    # row-major B MN-major: the layouts matmul itself picks)
     kp = (n + 31) // 32 * 32
     ahi = torch.empty((n, kp), dtype=torch.float32, device="cuda")
     alo, bhi, blo = torch.empty_like(ahi), torch.empty_like(ahi), torch.empty_like(ahi)
-    L.call("chelis_cuda_tf32x3_split", 0, n, n, a.data_ptr(), n, 0, 1, ahi.data_ptr(), alo.data_ptr())
-    L.call("chelis_cuda_tf32x3_split", 1, n, n, b.data_ptr(), n, 0, 1, bhi.data_ptr(), blo.data_ptr())
+    L.call("chelis_cuda_tf32x3_split", 0, 0, n, n, a.data_ptr(), n, 0, 1, ahi.data_ptr(), alo.data_ptr())
+    L.call("chelis_cuda_tf32x3_split", 1, 1, n, n, b.data_ptr(), n, 0, 1, bhi.data_ptr(), blo.data_ptr())
 
     def main_only():
-        L.call("chelis_cuda_sgemm_tf32x3_presplit", n, n, n, 1, ahi.data_ptr(), alo.data_ptr(),
-               bhi.data_ptr(), blo.data_ptr(), c.data_ptr(), n, 0)
+        L.call("chelis_cuda_sgemm_tf32x3_presplit", n, n, n, 1, 0, ahi.data_ptr(), alo.data_ptr(),
+               1, bhi.data_ptr(), blo.data_ptr(), c.data_ptr(), n, 0)
 
     for _ in range(3):
         main_only()

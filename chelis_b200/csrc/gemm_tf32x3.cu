@@ -8,9 +8,13 @@
 // lo = RN_tf32(x - hi) (x - hi is exact in f32).  The product a.b is then
 // accumulated as a_lo.b_hi + a_hi.b_lo + a_hi.b_hi in the f32 accumulator
 // of tcgen05.mma kind::tf32; the dropped a_lo.b_lo term is below 2^-22
-// relative.  The split runs as a pre-pass that also lays both operands out
-// K-major ([rows][Kp], Kp = K rounded up to 32, zero padded), so the main
-// kernel streams four K-major tiles per stage with TMA (128-byte swizzle).
+// relative.  The split runs as a pre-pass in the operand's own orientation
+// (one streaming read, two writes): a K-contiguous operand becomes K-major
+// [rows][Kp] (Kp = K rounded up to 32), an MN-contiguous one (row-major B,
+// transposed A) MN-major [K][MNp] (MNp = MN rounded up to 4), both zero
+// padded; only operands with neither stride 1 go through a transposing
+// tile kernel.  The main kernel streams four tiles per stage with TMA
+// (128-byte swizzle) and tells tcgen05.mma each operand's major-ness.
 //
 // Main kernel (one 128 x 256 output tile per CTA, 192 threads):
 //   warp 0      TMA producer (one elected lane)
@@ -44,15 +48,67 @@ constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 256;
+constexpr int MN_BOX = 32;                  // MN-major TMA box: 32 (MN) x 32 (K) f32
+constexpr int MN_BOX_BYTES = MN_BOX * BK * 4;  // 4 KiB
 
 struct Params {
     int64_t m, n;
-    int32_t num_kb;       // Kp / BK
-    int64_t a_rows_per_batch, b_rows_per_batch;  // rows of the split buffers per batch item
+    int32_t num_kb;       // ceil(K / BK)
+    int64_t a_rows_per_batch, b_rows_per_batch;  // K-major split buffers: rows per batch item
     float *c;
     int64_t ldc, stride_c;
 };
 
+// Operand layouts in shared memory (both written by TMA):
+//  K-major  (operand stored [rows][K]): one box of `rows` x 32 K, 128-byte
+//           swizzle of 16-byte chunks; 128-byte rows along K, 8-row atoms
+//           1024 B apart; an MMA K-step of 8 moves the start 32 B along the
+//           swizzled row.
+//  MN-major (operand stored [K][rows]): rows/32 boxes of 32 (MN) x 32 (K),
+//           4 KiB apart; inside a box one 128-byte row along MN per k.  For
+//           32-bit operands tcgen05 reads MN-major data only in the
+//           "128-byte span, 32-byte chunk" swizzle (descriptor layout 1,
+//           TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B), whose atom is 4 rows
+//           (512 B).  LBO = 4096 (next 32 MN), SBO = 512 (next 4 k); an MMA
+//           K-step of 8 moves the start 1024 B.
+__device__ __forceinline__ uint64_t sw128a32_mnmajor_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(MN_BOX_BYTES >> 4) << 16;  // leading byte offset
+    d |= static_cast<uint64_t>(512u >> 4) << 32;          // stride byte offset
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(1u) << 61;                 // 128B swizzle, 32B atoms
+    return d;
+}
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int kk) {
+    return MN ? sw128a32_mnmajor_desc(tile + kk * 1024) : sw128_kmajor_desc(tile + kk * 32);
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// Load one operand's tile for k-block `kb` into `dst`.
+template <bool MN, int ROWS>
+__device__ __forceinline__ void load_operand(unsigned char *dst, const CUtensorMap *map,
+                                             uint64_t *bar, int kb, int32_t row0, int32_t y_kmaj,
+                                             int32_t batch) {
+    if (MN) {
+#pragma unroll
+        for (int j = 0; j < ROWS / MN_BOX; ++j)
+            tma_load_3d(dst + j * MN_BOX_BYTES, map, bar, row0 + j * MN_BOX, kb * BK, batch);
+    } else {
+        tma_load_2d(dst, map, bar, kb * BK, y_kmaj);
+    }
+}
+
+template <bool AMN, bool BMN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_ahi,
                 const __grid_constant__ CUtensorMap map_alo,
@@ -106,6 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             const int32_t ya = static_cast<int32_t>(batch * p.a_rows_per_batch + m0);
             const int32_t yb = static_cast<int32_t>(batch * p.b_rows_per_batch + n0);
+            const int32_t z = static_cast<int32_t>(batch);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int s = kb % STAGES;
                 const uint32_t phase = (kb / STAGES) & 1;
@@ -115,24 +172,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 unsigned char *st = smem + s * STAGE_BYTES;
                 mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                const int32_t x = kb * BK;
-                tma_load_2d(st, &map_ahi, &full[s], x, ya);
-                tma_load_2d(st + A_TILE_BYTES, &map_alo, &full[s], x, ya);
-                tma_load_2d(st + 2 * A_TILE_BYTES, &map_bhi, &full[s], x, yb);
-                tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &map_blo, &full[s], x, yb);
+                load_operand<AMN, BM>(st, &map_ahi, &full[s], kb, static_cast<int32_t>(m0), ya, z);
+                load_operand<AMN, BM>(st + A_TILE_BYTES, &map_alo, &full[s], kb,
+                                      static_cast<int32_t>(m0), ya, z);
+                load_operand<BMN, BN>(st + 2 * A_TILE_BYTES, &map_bhi, &full[s], kb,
+                                      static_cast<int32_t>(n0), yb, z);
+                load_operand<BMN, BN>(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &map_blo, &full[s],
+                                      kb, static_cast<int32_t>(n0), yb, z);
                 issued = kb + 1;
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(BM, BN);
-            bool ok = true;
+            constexpr uint32_t idesc = idesc_tf32(BM, BN) | (AMN ? (1u << 15) : 0u) |
+                                       (BMN ? (1u << 16) : 0u);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int s = kb % STAGES;
                 const uint32_t phase = (kb / STAGES) & 1;
                 if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
-                    ok = false;
                     *abort_flag = 1;
                     break;
                 }
@@ -143,20 +201,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t blo = bhi + B_TILE_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
                     const uint32_t acc = (kb | kk) ? 1u : 0u;
-                    mma_tf32_ss(tmem_base, sw128_kmajor_desc(alo + off),
-                                sw128_kmajor_desc(bhi + off), idesc, acc);
-                    mma_tf32_ss(tmem_base, sw128_kmajor_desc(ahi + off),
-                                sw128_kmajor_desc(blo + off), idesc, 1u);
-                    mma_tf32_ss(tmem_base, sw128_kmajor_desc(ahi + off),
-                                sw128_kmajor_desc(bhi + off), idesc, 1u);
+                    mma_tf32_ss(tmem_base, operand_desc<AMN>(alo, kk), operand_desc<BMN>(bhi, kk),
+                                idesc, acc);
+                    mma_tf32_ss(tmem_base, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(blo, kk),
+                                idesc, 1u);
+                    mma_tf32_ss(tmem_base, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(bhi, kk),
+                                idesc, 1u);
                 }
                 mma_commit(&empty[s]);
                 *consumed = kb + 1;
             }
             // Signal the epilogue either way; on abort it skips the stores.
-            (void)ok;
             mma_commit(accum_full);
         }
     } else {
@@ -210,10 +266,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// split pre-pass: src element (r, k) at src[b*sb + r*sr + k*sk] ->
-// hi/lo[b][r][k] (K-major, row stride kp), zero for k >= K.
-// A 32 x 32 tile goes through shared memory so that both the read (along the
-// unit-stride axis of the source) and the write (along k) are coalesced.
+// split pre-pass kernels.  hi = RN_tf32(x), lo = RN_tf32(x - hi) (x - hi is
+// exact in f32); non-finite x gets lo = 0.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float rna_tf32(float x) {
     uint32_t r;
@@ -221,6 +275,9 @@ __device__ __forceinline__ float rna_tf32(float x) {
     return __uint_as_float(r);
 }
 
+// General strides: element (r, kk) at src[b*sb + r*sr + kk*sk] ->
+// hi/lo[b][r][kk] (K-major, row stride kp), zero for kk >= K.  A 32 x 32
+// tile goes through shared memory so both the read and the write coalesce.
 __global__ void split_kernel(const float *__restrict__ src, int64_t rows, int64_t k,
                              int64_t sr, int64_t sk, int64_t sb, int64_t kp,
                              float *__restrict__ hi, float *__restrict__ lo) {
@@ -231,13 +288,11 @@ __global__ void split_kernel(const float *__restrict__ src, int64_t rows, int64_
     const float *s = src + b * sb;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     if (sk == 1) {
-        // rows contiguous along k: read row-wise
         for (int i = ty; i < 32; i += 8) {
             int64_t r = r0 + i, kk = k0 + tx;
             tile[i][tx] = (r < rows && kk < k) ? s[r * sr + kk] : 0.0f;
         }
     } else {
-        // contiguous along rows (a transposed operand): read column-wise
         for (int i = ty; i < 32; i += 8) {
             int64_t r = r0 + tx, kk = k0 + i;
             tile[tx][i] = (r < rows && kk < k) ? s[r * sr + kk * sk] : 0.0f;
@@ -258,27 +313,30 @@ __global__ void split_kernel(const float *__restrict__ src, int64_t rows, int64_
     }
 }
 
-// Row-contiguous source (sk == 1): a plain streaming split, one float4 in
-// and two float4 out per thread step; columns [k, kp) are written as zeros.
-__global__ void split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t k,
-                                  int64_t sr, int64_t sb, int64_t kp, float *__restrict__ hi,
+// Row-contiguous source: the split streams, one float4 in and two float4
+// out per step; row r of `rows` has `cols` valid entries at src[b*sb +
+// r*sr + c] and the output row stride is `cp` (columns [cols, cp) zero).
+// Used for both layouts: K-major (rows = MN, cols = K) and MN-major
+// (rows = K, cols = MN).
+__global__ void split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                  int64_t sr, int64_t sb, int64_t cp, float *__restrict__ hi,
                                   float *__restrict__ lo) {
     const int64_t b = blockIdx.y;
     const float *s = src + b * sb;
-    float *h = hi + b * rows * kp;
-    float *l = lo + b * rows * kp;
-    const int64_t q = kp / 4;  // float4 per output row
-    const bool vec = (k % 4 == 0) && (sr % 4 == 0) && ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
+    float *h = hi + b * rows * cp;
+    float *l = lo + b * rows * cp;
+    const int64_t q = cp / 4;  // float4 per output row
+    const bool vec = (cols % 4 == 0) && (sr % 4 == 0) && ((reinterpret_cast<uintptr_t>(s) & 15) == 0);
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * q;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t r = i / q, c0 = (i % q) * 4;
         float x[4];
-        if (vec && c0 + 3 < k) {
+        if (vec && c0 + 3 < cols) {
             const float4 v = __ldcs(reinterpret_cast<const float4 *>(s + r * sr + c0));
             x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
         } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) x[j] = (c0 + j < k) ? s[r * sr + c0 + j] : 0.0f;
+            for (int j = 0; j < 4; ++j) x[j] = (c0 + j < cols) ? s[r * sr + c0 + j] : 0.0f;
         }
         float xh[4], xl[4];
 #pragma unroll
@@ -286,8 +344,8 @@ __global__ void split_rows_kernel(const float *__restrict__ src, int64_t rows, i
             xh[j] = rna_tf32(x[j]);
             xl[j] = isfinite(x[j]) ? rna_tf32(__fsub_rn(x[j], xh[j])) : 0.0f;
         }
-        *reinterpret_cast<float4 *>(h + r * kp + c0) = make_float4(xh[0], xh[1], xh[2], xh[3]);
-        *reinterpret_cast<float4 *>(l + r * kp + c0) = make_float4(xl[0], xl[1], xl[2], xl[3]);
+        *reinterpret_cast<float4 *>(h + r * cp + c0) = make_float4(xh[0], xh[1], xh[2], xh[3]);
+        *reinterpret_cast<float4 *>(l + r * cp + c0) = make_float4(xl[0], xl[1], xl[2], xl[3]);
     }
 }
 
@@ -309,6 +367,7 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// K-major split buffer [total_rows][kp] -> box 32 (K) x box_rows
 int make_kmajor_map(CUtensorMap *map, const float *base, int64_t rows, int64_t kp, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -322,6 +381,26 @@ int make_kmajor_map(CUtensorMap *map, const float *base, int64_t rows, int64_t k
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CHELIS_CUDA_OK;
+}
+
+// MN-major split buffer [batch][k][mnp] -> box 32 (MN) x 32 (K) x 1; rows
+// past k and columns past mn read as zeros (per batch item: 3-D map)
+int make_mnmajor_map(CUtensorMap *map, const float *base, int64_t mn, int64_t mnp, int64_t k,
+                     int64_t batch) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(mn), static_cast<cuuint64_t>(k),
+                          static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(mnp) * 4, static_cast<cuuint64_t>(mnp * k) * 4};
+    cuuint32_t box[3] = {MN_BOX, BK, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled(3d) failed (%d)", (int)r);
     return CHELIS_CUDA_OK;
 }
 
@@ -482,65 +561,101 @@ template int launch_exact_gemm<double>(int, int, int64_t, int64_t, int64_t, cons
                                        int64_t, int64_t, const double *, int64_t, int64_t,
                                        double *, int64_t, int64_t, int64_t, cudaStream_t);
 
-// Split rows x k of a source (element (r, kk) at src[b*sb + r*sr + kk*sk])
-// into K-major hi / lo copies of kp columns per row.
-int launch_split(const float *src, int64_t rows, int64_t k, int64_t sr, int64_t sk, int64_t sb,
-                 int64_t batch, int64_t kp, float *hi, float *lo, cudaStream_t s) {
+// ---------------------------------------------------------------------------
+// operand plans: how one operand of op(A) . op(B) is split and loaded
+// ---------------------------------------------------------------------------
+// The operand is viewed as `rows` x k (rows = m for A, n for B) with element
+// (r, kk) at src[b*sb + r*sr + kk*sk].  K-contiguous sources (sk == 1) split
+// K-major; MN-contiguous ones (sr == 1) split MN-major; anything else goes
+// through the transposing tile kernel into K-major.
+struct OperandPlan {
+    bool mn;             // MN-major layout
+    int64_t rows, k;
+    int64_t cp;          // padded inner extent of the split buffer
+    int64_t floats;      // floats of one of hi / lo, all batch items
+};
+
+OperandPlan plan_operand(int64_t rows, int64_t k, int64_t sr, int64_t sk, int64_t batch) {
     using namespace tf32x3;
-    if (sk == 1) {
-        int64_t blocks = (rows * (kp / 4) + 255) / 256;
-        const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    OperandPlan p;
+    p.rows = rows;
+    p.k = k;
+    p.mn = (sk != 1) && (sr == 1);
+    if (p.mn) {
+        p.cp = (rows + 3) / 4 * 4;
+        p.floats = batch * k * p.cp;
+    } else {
+        p.cp = (k + BK - 1) / BK * BK;
+        p.floats = batch * rows * p.cp;
+    }
+    return p;
+}
+
+int launch_split_plan(const OperandPlan &p, const float *src, int64_t sr, int64_t sk, int64_t sb,
+                      int64_t batch, float *hi, float *lo, cudaStream_t s) {
+    using namespace tf32x3;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    if (p.mn || sk == 1) {
+        // streaming: MN-major rows are k (stride sk), K-major rows are `rows` (stride sr)
+        const int64_t out_rows = p.mn ? p.k : p.rows;
+        const int64_t cols = p.mn ? p.rows : p.k;
+        const int64_t row_stride = p.mn ? sk : sr;
+        int64_t blocks = (out_rows * (p.cp / 4) + 255) / 256;
         if (blocks > cap) blocks = cap;
+        if (blocks < 1) blocks = 1;
         split_rows_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batch)), 256,
-                            0, s>>>(src, rows, k, sr, sb, kp, hi, lo);
+                            0, s>>>(src, out_rows, cols, row_stride, sb, p.cp, hi, lo);
         g_launches++;
         CHELIS_LAUNCH_CHECK("split_rows_kernel");
         return CHELIS_CUDA_OK;
     }
-    dim3 grid(static_cast<unsigned>(kp / 32), static_cast<unsigned>((rows + 31) / 32),
+    dim3 grid(static_cast<unsigned>(p.cp / 32), static_cast<unsigned>((p.rows + 31) / 32),
               static_cast<unsigned>(batch));
-    split_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, k, sr, sk, sb, kp, hi, lo);
+    split_kernel<<<grid, dim3(32, 8), 0, s>>>(src, p.rows, p.k, sr, sk, sb, p.cp, hi, lo);
     g_launches++;
     CHELIS_LAUNCH_CHECK("split_kernel");
     return CHELIS_CUDA_OK;
 }
 
-// Split both operands into caller-provided scratch and run the tcgen05
-// kernel.  `scratch` must hold 2 * (m + n) * kp floats per batch item.
-int sgemm_3xtf32_with_scratch(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
-                              const float *a, int64_t lda, int64_t stride_a, const float *b,
-                              int64_t ldb, int64_t stride_b, float *c, int64_t ldc,
-                              int64_t stride_c, int64_t batch, float *scratch, cudaStream_t s) {
+int make_operand_map(CUtensorMap *map, const OperandPlan &p, const float *buf, int64_t batch,
+                     int box_rows) {
+    if (p.mn) return tf32x3::make_mnmajor_map(map, buf, p.rows, p.cp, p.k, batch);
+    return tf32x3::make_kmajor_map(map, buf, batch * p.rows, p.cp, box_rows);
+}
+
+template <bool AMN, bool BMN>
+int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMap &bhi,
+                const CUtensorMap &blo, const tf32x3::Params &p, dim3 grid, cudaStream_t s) {
     using namespace tf32x3;
-    const int64_t kp = (k + BK - 1) / BK * BK;
-    float *ahi = scratch;
-    float *alo = ahi + batch * m * kp;
-    float *bhi = alo + batch * m * kp;
-    float *blo = bhi + batch * n * kp;
-    // op(A)[i, kk] = a[i*lda + kk] (no trans) or a[kk*lda + i] (trans)
-    CHELIS_TRY(launch_split(a, m, k, trans_a ? 1 : lda, trans_a ? lda : 1, stride_a, batch, kp,
-                            ahi, alo, s));
-    // op(B)[kk, j] -> K-major rows j: element (j, kk) = b[kk*ldb + j] (no
-    // trans) or b[j*ldb + kk] (trans)
-    CHELIS_TRY(launch_split(b, n, k, trans_b ? ldb : 1, trans_b ? 1 : ldb, stride_b, batch, kp,
-                            bhi, blo, s));
-    CUtensorMap mahi, malo, mbhi, mblo;
-    CHELIS_TRY(make_kmajor_map(&mahi, ahi, batch * m, kp, BM));
-    CHELIS_TRY(make_kmajor_map(&malo, alo, batch * m, kp, BM));
-    CHELIS_TRY(make_kmajor_map(&mbhi, bhi, batch * n, kp, BN));
-    CHELIS_TRY(make_kmajor_map(&mblo, blo, batch * n, kp, BN));
     static bool attr_set = false;
     if (!attr_set) {
-        CHELIS_TRY(check_cuda(cudaFuncSetAttribute(gemm_kernel,
+        CHELIS_TRY(check_cuda(cudaFuncSetAttribute(gemm_kernel<AMN, BMN>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    SMEM_BYTES),
                               "cudaFuncSetAttribute(gemm_kernel)"));
         attr_set = true;
     }
+    gemm_kernel<AMN, BMN><<<grid, THREADS, SMEM_BYTES, s>>>(ahi, alo, bhi, blo, p);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("gemm_kernel(3xtf32)");
+    return CHELIS_CUDA_OK;
+}
+
+// Main kernel on split operands.
+int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
+                      const OperandPlan &pb, const float *bhi, const float *blo, int64_t m,
+                      int64_t n, int64_t k, float *c, int64_t ldc, int64_t stride_c, int64_t batch,
+                      cudaStream_t s) {
+    using namespace tf32x3;
+    CUtensorMap mahi, malo, mbhi, mblo;
+    CHELIS_TRY(make_operand_map(&mahi, pa, ahi, batch, BM));
+    CHELIS_TRY(make_operand_map(&malo, pa, alo, batch, BM));
+    CHELIS_TRY(make_operand_map(&mbhi, pb, bhi, batch, BN));
+    CHELIS_TRY(make_operand_map(&mblo, pb, blo, batch, BN));
     Params p;
     p.m = m;
     p.n = n;
-    p.num_kb = static_cast<int32_t>(kp / BK);
+    p.num_kb = static_cast<int32_t>((k + BK - 1) / BK);
     p.a_rows_per_batch = m;
     p.b_rows_per_batch = n;
     p.c = c;
@@ -548,15 +663,49 @@ int sgemm_3xtf32_with_scratch(int trans_a, int trans_b, int64_t m, int64_t n, in
     p.stride_c = stride_c;
     dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>((m + BM - 1) / BM),
               static_cast<unsigned>(batch));
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mahi, malo, mbhi, mblo, p);
-    g_launches++;
-    CHELIS_LAUNCH_CHECK("gemm_kernel(3xtf32)");
-    return CHELIS_CUDA_OK;
+    if (pa.mn) {
+        if (pb.mn) return launch_main<true, true>(mahi, malo, mbhi, mblo, p, grid, s);
+        return launch_main<true, false>(mahi, malo, mbhi, mblo, p, grid, s);
+    }
+    if (pb.mn) return launch_main<false, true>(mahi, malo, mbhi, mblo, p, grid, s);
+    return launch_main<false, false>(mahi, malo, mbhi, mblo, p, grid, s);
 }
 
-size_t sgemm_3xtf32_scratch_bytes(int64_t m, int64_t n, int64_t k, int64_t batch) {
-    const int64_t kp = (k + tf32x3::BK - 1) / tf32x3::BK * tf32x3::BK;
-    return static_cast<size_t>(2 * (m + n) * kp * batch) * sizeof(float);
+struct GemmPlan {
+    OperandPlan a, b;
+    int64_t sar, sak, sbr, sbk;
+    size_t bytes() const { return static_cast<size_t>(2 * (a.floats + b.floats)) * sizeof(float); }
+};
+
+GemmPlan plan_gemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, int64_t lda,
+                   int64_t ldb, int64_t batch) {
+    GemmPlan g;
+    // op(A)[i, kk] = a[i*lda + kk] (no trans) or a[kk*lda + i] (trans)
+    g.sar = trans_a ? 1 : lda;
+    g.sak = trans_a ? lda : 1;
+    // op(B)[kk, j] as the n x k operand: element (j, kk) = b[kk*ldb + j] (no
+    // trans) or b[j*ldb + kk] (trans)
+    g.sbr = trans_b ? ldb : 1;
+    g.sbk = trans_b ? 1 : ldb;
+    g.a = plan_operand(m, k, g.sar, g.sak, batch);
+    g.b = plan_operand(n, k, g.sbr, g.sbk, batch);
+    return g;
+}
+
+// Split both operands into caller-provided scratch (GemmPlan::bytes()) and
+// run the tcgen05 kernel.
+int sgemm_3xtf32_with_scratch(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                              const float *a, int64_t lda, int64_t stride_a, const float *b,
+                              int64_t ldb, int64_t stride_b, float *c, int64_t ldc,
+                              int64_t stride_c, int64_t batch, float *scratch, cudaStream_t s) {
+    const GemmPlan g = plan_gemm(trans_a, trans_b, m, n, k, lda, ldb, batch);
+    float *ahi = scratch;
+    float *alo = ahi + g.a.floats;
+    float *bhi = alo + g.a.floats;
+    float *blo = bhi + g.b.floats;
+    CHELIS_TRY(launch_split_plan(g.a, a, g.sar, g.sak, stride_a, batch, ahi, alo, s));
+    CHELIS_TRY(launch_split_plan(g.b, b, g.sbr, g.sbk, stride_b, batch, bhi, blo, s));
+    return sgemm_3xtf32_main(g.a, ahi, alo, g.b, bhi, blo, m, n, k, c, ldc, stride_c, batch, s);
 }
 
 int validate_gemm_args(int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
@@ -575,51 +724,36 @@ int validate_gemm_args(int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb
 
 using namespace chelis;
 
-extern "C" int chelis_cuda_tf32x3_split(int trans, int64_t rows, int64_t k, const float *src,
-                                        int64_t ld, int64_t stride, int64_t batch, float *hi,
-                                        float *lo) {
-    if (rows < 0 || k < 0 || batch < 0)
+extern "C" int chelis_cuda_tf32x3_split(int trans, int layout, int64_t rows, int64_t k,
+                                        const float *src, int64_t ld, int64_t stride,
+                                        int64_t batch, float *hi, float *lo) {
+    if (rows < 0 || k < 0 || batch < 0 || (layout & ~1))
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
-    if (rows == 0 || batch == 0) return CHELIS_CUDA_OK;
-    const int64_t kp = (k + tf32x3::BK - 1) / tf32x3::BK * tf32x3::BK;
-    if (kp == 0) return CHELIS_CUDA_OK;
-    return launch_split(src, rows, k, trans ? 1 : ld, trans ? ld : 1, stride, batch, kp, hi, lo,
-                        current_stream());
+    const int64_t sr = trans ? 1 : ld, sk = trans ? ld : 1;
+    OperandPlan p = plan_operand(rows, k, sr, sk, batch);
+    if (layout == 1 && !p.mn)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN,
+                         "MN-major split needs an MN-contiguous source (trans = 1)");
+    if (layout == 0 && p.mn) {  // force K-major through the transposing kernel
+        p.mn = false;
+        p.cp = (k + tf32x3::BK - 1) / tf32x3::BK * tf32x3::BK;
+    }
+    if (rows == 0 || batch == 0 || k == 0) return CHELIS_CUDA_OK;
+    return launch_split_plan(p, src, sr, sk, stride, batch, hi, lo, current_stream());
 }
 
 extern "C" int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t batch,
-                                                 const float *a_hi, const float *a_lo,
+                                                 int a_layout, const float *a_hi,
+                                                 const float *a_lo, int b_layout,
                                                  const float *b_hi, const float *b_lo, float *c,
                                                  int64_t ldc, int64_t stride_c) {
-    using namespace tf32x3;
-    if (m < 0 || n < 0 || k <= 0 || batch < 0 || ldc < n)
+    if (m < 0 || n < 0 || k <= 0 || batch < 0 || ldc < n || (a_layout & ~1) || (b_layout & ~1))
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
     if (m == 0 || n == 0 || batch == 0) return CHELIS_CUDA_OK;
-    const int64_t kp = (k + BK - 1) / BK * BK;
-    CUtensorMap mahi, malo, mbhi, mblo;
-    CHELIS_TRY(make_kmajor_map(&mahi, a_hi, batch * m, kp, BM));
-    CHELIS_TRY(make_kmajor_map(&malo, a_lo, batch * m, kp, BM));
-    CHELIS_TRY(make_kmajor_map(&mbhi, b_hi, batch * n, kp, BN));
-    CHELIS_TRY(make_kmajor_map(&mblo, b_lo, batch * n, kp, BN));
-    CHELIS_TRY(check_cuda(cudaFuncSetAttribute(gemm_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               SMEM_BYTES),
-                          "cudaFuncSetAttribute(gemm_kernel)"));
-    Params p;
-    p.m = m;
-    p.n = n;
-    p.num_kb = static_cast<int32_t>(kp / BK);
-    p.a_rows_per_batch = m;
-    p.b_rows_per_batch = n;
-    p.c = c;
-    p.ldc = ldc;
-    p.stride_c = stride_c;
-    dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>((m + BM - 1) / BM),
-              static_cast<unsigned>(batch));
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, current_stream()>>>(mahi, malo, mbhi, mblo, p);
-    g_launches++;
-    CHELIS_LAUNCH_CHECK("gemm_kernel(3xtf32)");
-    return CHELIS_CUDA_OK;
+    OperandPlan pa = plan_operand(m, k, a_layout ? 1 : 2, a_layout ? 2 : 1, batch);
+    OperandPlan pb = plan_operand(n, k, b_layout ? 1 : 2, b_layout ? 2 : 1, batch);
+    return sgemm_3xtf32_main(pa, a_hi, a_lo, pb, b_hi, b_lo, m, n, k, c, ldc, stride_c, batch,
+                             current_stream());
 }
 
 extern "C" int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
@@ -642,8 +776,9 @@ extern "C" int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n,
                                         stride_b, c, ldc, stride_c, batch, s);
     if (batch * (m > n ? m : n) > INT32_MAX)
         return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "batched matmul rows beyond 2^31");
+    const GemmPlan g = plan_gemm(trans_a, trans_b, m, n, k, lda, ldb, batch);
     void *scratch = nullptr;
-    CHELIS_TRY(scratch_alloc(&scratch, sgemm_3xtf32_scratch_bytes(m, n, k, batch), s));
+    CHELIS_TRY(scratch_alloc(&scratch, g.bytes(), s));
     int st = sgemm_3xtf32_with_scratch(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb,
                                        stride_b, c, ldc, stride_c, batch,
                                        static_cast<float *>(scratch), s);

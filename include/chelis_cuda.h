@@ -193,18 +193,24 @@ int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
 int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
                       int64_t lda, int64_t stride_a, const double *b, int64_t ldb,
                       int64_t stride_b, double *c, int64_t ldc, int64_t stride_c, int64_t batch);
-/* 3xTF32 in two halves, for operands reused across many products (weights):
- * split op(X) (rows x k, op = transpose when trans != 0) into K-major hi/lo
- * copies of rows x kp floats per batch item (kp = k rounded up to 32, zero
- * padded), then multiply pre-split operands: C[b] = A[b] . B[b]^T where A is
- * m x kp and B is n x kp (B split from op(B)^T, i.e. with the transposed
- * flag of the row-major product).  No reference counterpart: hipBLAS has no
- * split form (chelis_hip_runtime.h:48-78 is the single-call slot). */
-int chelis_cuda_tf32x3_split(int trans, int64_t rows, int64_t k, const float *src, int64_t ld,
-                             int64_t stride, int64_t batch, float *hi, float *lo);
+/* 3xTF32 in two halves, for operands reused across many products (weights).
+ * chelis_cuda_tf32x3_split splits op(X) (rows x k, op = transpose when
+ * trans != 0, element (r, kk) at src[r*ld + kk], or src[kk*ld + r] when
+ * transposed) into hi/lo copies in one of two layouts:
+ *   layout 0 (K-major):  [batch][rows][kp], kp = k rounded up to 32;
+ *   layout 1 (MN-major): [batch][k][rp],    rp = rows rounded up to 4
+ *                        (needs trans != 0: the source is already [k][rows]).
+ * Padding is zero.  chelis_cuda_sgemm_tf32x3_presplit then computes
+ * C[b] = A[b] . B[b]^T for pre-split A (m x k) and B (n x k) in the layouts
+ * named by a_layout / b_layout; a row-major right operand B (k x n) is split
+ * with trans = 1, layout = 1.  No reference counterpart: hipBLAS has no split
+ * form (chelis_hip_runtime.h:48-78 is the single-call slot). */
+int chelis_cuda_tf32x3_split(int trans, int layout, int64_t rows, int64_t k, const float *src,
+                             int64_t ld, int64_t stride, int64_t batch, float *hi, float *lo);
 int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t batch,
-                                      const float *a_hi, const float *a_lo, const float *b_hi,
-                                      const float *b_lo, float *c, int64_t ldc, int64_t stride_c);
+                                      int a_layout, const float *a_hi, const float *a_lo,
+                                      int b_layout, const float *b_hi, const float *b_lo,
+                                      float *c, int64_t ldc, int64_t stride_c);
 
 /* =========================================================================
  * Fused elementwise / reduction groups and their adjoints.

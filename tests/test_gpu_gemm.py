@@ -141,3 +141,70 @@ def test_row_major_helper_abi(cuda, orc):
     bad = desc(tb)
     bad.strides = (ctypes.c_int64 * 2)(1, k)
     assert L.load().chelis_cuda_sgemm_row_major(ctypes.byref(da), ctypes.byref(bad), ctypes.byref(dc), m, n, k) == 1
+
+
+@pytest.mark.parametrize("a_layout,b_layout", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_presplit_layouts(cuda, orc, a_layout, b_layout):
+    """chelis_cuda_tf32x3_split + chelis_cuda_sgemm_tf32x3_presplit with each
+    operand K-major (layout 0) or MN-major (layout 1), batched, ragged
+    extents (m, n not multiples of 4 or of the tile; k not of 32)."""
+    import torch
+    m, n, k, batch = 131, 301, 97, 3
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=21, batch=batch)
+    ta = torch.from_numpy(a).cuda()                       # [batch][m][k]
+    tbt = torch.from_numpy(b).cuda()                      # [batch][k][n]
+    # A as m x k: layout 0 from the row-major copy, layout 1 from A^T ([k][m])
+    at = ta.transpose(1, 2).contiguous()
+    bt = tbt.transpose(1, 2).contiguous()                 # [batch][n][k]
+
+    def split(src, trans, layout, rows):
+        if layout == 0:
+            shape = (batch, rows, (k + 31) // 32 * 32)
+        else:
+            shape = (batch, k, (rows + 3) // 4 * 4)
+        hi = torch.full(shape, float("nan"), dtype=torch.float32, device="cuda")
+        lo = torch.full(shape, float("nan"), dtype=torch.float32, device="cuda")
+        ld = src.shape[2]
+        cuda._prepare(src)
+        L.call("chelis_cuda_tf32x3_split", trans, layout, rows, k, src.data_ptr(), ld,
+               src.shape[1] * src.shape[2], batch, hi.data_ptr(), lo.data_ptr())
+        return hi, lo
+
+    # layout 0 for A: row-major A (trans 0); layout 1: A^T source (trans 1)
+    ahi, alo = split(ta, 0, 0, m) if a_layout == 0 else split(at, 1, 1, m)
+    # B as n x k: layout 0 from B^T rows (trans 0); layout 1 from row-major B (trans 1)
+    bhi, blo = split(bt, 0, 0, n) if b_layout == 0 else split(tbt, 1, 1, n)
+    c = torch.full((batch, m, n), float("nan"), dtype=torch.float32, device="cuda")
+    L.call("chelis_cuda_sgemm_tf32x3_presplit", m, n, k, batch, a_layout, ahi.data_ptr(),
+           alo.data_ptr(), b_layout, bhi.data_ptr(), blo.data_ptr(), c.data_ptr(), n, m * n)
+    torch.cuda.synchronize()
+    cuda.device_status()
+    got = c.cpu().numpy()
+    for i in range(batch):
+        assert _rel_err(got[i], orc.gemm(a[i], b[i]), a[i], b[i]) <= 1e-5, i
+
+
+def test_split_forced_kmajor_from_transposed_source(cuda, orc):
+    """layout 0 on a transposed source goes through the tile-transposing
+    split; MN-major from a row-contiguous source is rejected."""
+    import torch
+    m, n, k = 70, 90, 45
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=22)
+    at = torch.from_numpy(a.T.copy()).cuda()              # [k][m]
+    tb = torch.from_numpy(b).cuda()                       # [k][n]
+    kp = (k + 31) // 32 * 32
+    ahi = torch.empty((m, kp), dtype=torch.float32, device="cuda")
+    alo = torch.empty_like(ahi)
+    bhi = torch.empty((n, kp), dtype=torch.float32, device="cuda")
+    blo = torch.empty_like(bhi)
+    cuda._prepare(at)
+    L.call("chelis_cuda_tf32x3_split", 1, 0, m, k, at.data_ptr(), m, 0, 1, ahi.data_ptr(), alo.data_ptr())
+    L.call("chelis_cuda_tf32x3_split", 1, 0, n, k, tb.data_ptr(), n, 0, 1, bhi.data_ptr(), blo.data_ptr())
+    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    L.call("chelis_cuda_sgemm_tf32x3_presplit", m, n, k, 1, 0, ahi.data_ptr(), alo.data_ptr(),
+           0, bhi.data_ptr(), blo.data_ptr(), c.data_ptr(), n, 0)
+    torch.cuda.synchronize()
+    assert _rel_err(c.cpu().numpy(), orc.gemm(a, b), a, b) <= 1e-5
+    lib = L.load()
+    assert lib.chelis_cuda_tf32x3_split(0, 1, m, k, at.data_ptr(), k, 0, 1, ahi.data_ptr(),
+                                        alo.data_ptr()) == 1  # CHELIS_CUDA_ERR_DOMAIN
