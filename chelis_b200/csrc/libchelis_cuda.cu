@@ -4,6 +4,7 @@
 #include "runtime.cu"
 #include "gemm_tf32x3.cu"
 #include "gemm_f64.cu"
+#include "host_gemm.cu"
 #include "rows.cu"
 #include "chain.cu"
 #include "portfolio.cu"

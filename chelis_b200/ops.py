@@ -98,6 +98,43 @@ def matmul(a: torch.Tensor, b: torch.Tensor, trans_a: bool = False, trans_b: boo
     return out
 
 
+def matmul_host(a: torch.Tensor, b: torch.Tensor, trans_a: bool = False, trans_b: bool = False,
+                out: torch.Tensor | None = None, device: int | None = None) -> torch.Tensor:
+    """op(A).op(B) for host (CPU) tensors through chelis_cuda_[sd]gemm_host:
+    uploads, GEMM panels and read-back overlap on the GPU's copy engines.
+    Returns once the result is in `out` (pinned output memory is allocated
+    when `out` is None and `a` is pinned)."""
+    if a.device.type != "cpu" or b.device.type != "cpu":
+        raise ValueError("matmul_host takes host tensors")
+    if a.dtype != b.dtype or a.dtype not in (torch.float32, torch.float64):
+        raise ValueError("matmul_host takes two f32 or two f64 tensors")
+    if not (a.is_contiguous() and b.is_contiguous()):
+        raise ValueError("matmul_host takes contiguous tensors")
+    batched = a.dim() == 3
+    if batched != (b.dim() == 3) or a.dim() not in (2, 3):
+        raise ValueError("matmul_host takes rank-2 or rank-3 operands of equal rank")
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    with torch.cuda.device(dev):
+        _prepare()
+        ar, ac = a.shape[-2:]
+        br, bc = b.shape[-2:]
+        m, k = (ac, ar) if trans_a else (ar, ac)
+        k2, n = (bc, br) if trans_b else (br, bc)
+        if k != k2:
+            raise ValueError(f"contraction extents differ: {k} vs {k2}")
+        batch = a.shape[0] if batched else 1
+        shape = (batch, m, n) if batched else (m, n)
+        if out is None:
+            out = torch.empty(shape, dtype=a.dtype, pin_memory=a.is_pinned())
+        elif out.device.type != "cpu" or not out.is_contiguous() or tuple(out.shape) != shape:
+            raise ValueError("out must be a contiguous host tensor of the product's shape")
+        name = "chelis_cuda_sgemm_host" if a.dtype == torch.float32 else "chelis_cuda_dgemm_host"
+        L.call(name, int(trans_a), int(trans_b), m, n, k, a.data_ptr(), ac, ar * ac,
+               b.data_ptr(), bc, br * bc, out.data_ptr(), n, m * n, batch)
+        torch.cuda.current_stream(dev).synchronize()
+    return out
+
+
 # ---------------------------------------------------------------- rows
 
 def row_sum(x: torch.Tensor) -> torch.Tensor:

@@ -193,6 +193,22 @@ int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
 int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
                       int64_t lda, int64_t stride_a, const double *b, int64_t ldb,
                       int64_t stride_b, double *c, int64_t ldc, int64_t stride_c, int64_t batch);
+/* [05-OP-30] matmul on HOST buffers (row-major, same argument meaning as
+ * chelis_cuda_sgemm / chelis_cuda_dgemm, all pointers host pointers).  The
+ * reference uploads both operands, runs hipBLAS and downloads C in sequence
+ * (chelis_hip_runtime.h:48-78 plus its buffer copies); here the uploads of A
+ * panels, the GEMM of earlier panels and the read-back of finished panels
+ * overlap on three streams.  Stream-ordered on the thread's stream: C is
+ * complete once that stream is synchronised.  Page-locked host memory lets
+ * the copies run asynchronously. */
+int chelis_cuda_sgemm_host(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                           const float *a, int64_t lda, int64_t stride_a, const float *b,
+                           int64_t ldb, int64_t stride_b, float *c, int64_t ldc,
+                           int64_t stride_c, int64_t batch);
+int chelis_cuda_dgemm_host(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                           const double *a, int64_t lda, int64_t stride_a, const double *b,
+                           int64_t ldb, int64_t stride_b, double *c, int64_t ldc,
+                           int64_t stride_c, int64_t batch);
 /* 3xTF32 in two halves, for operands reused across many products (weights).
  * chelis_cuda_tf32x3_split splits op(X) (rows x k, op = transpose when
  * trans != 0, element (r, kk) at src[r*ld + kk], or src[kk*ld + r] when
