@@ -35,6 +35,9 @@ namespace chelis {
 
 extern std::atomic<uint64_t> g_launches;
 int gemm_mode();
+// 1: 3xTF32 products with more than 128 rows run on CTA pairs (default);
+// 0: one CTA per 128 x 256 tile everywhere
+std::atomic<int> g_pair_tiles{1};
 
 namespace tf32x3 {
 
@@ -52,7 +55,7 @@ constexpr int MN_BOX = 32;                  // MN-major TMA box: 32 (MN) x 32 (K
 constexpr int MN_BOX_BYTES = MN_BOX * BK * 4;  // 4 KiB
 
 struct Params {
-    int64_t m, n;
+    int64_t m, n, batch;
     int32_t num_kb;       // ceil(K / BK)
     int64_t a_rows_per_batch, b_rows_per_batch;  // K-major split buffers: rows per batch item
     float *c;
@@ -262,6 +265,213 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair main kernel: one 256 x 256 output tile per cluster of 2 CTAs
+// (tcgen05 cta_group::2, M = 256).  Each CTA stages its 128 rows of A and
+// its 128 rows of B^T (half of the tile's columns), so one pair MMA reads
+// 8 KiB of operands per SM per K-step of 8 instead of 12 KiB: the shared
+// memory port stays below its limit with the TMA writes included, and the
+// tensor pipe, not shared memory, bounds the main loop.  Rank 0 issues the
+// MMAs; both CTAs' TMA loads report to rank 0's `full` barriers; the MMA
+// commits release both CTAs' `empty` barriers and both accumulators.
+// ---------------------------------------------------------------------------
+constexpr int P_STAGES = 3;
+constexpr int P_ROWS = 128;  // A rows and B rows per CTA
+constexpr int P_TILE_BYTES = P_ROWS * BK * 4;   // 16 KiB
+constexpr int P_STAGE_BYTES = 4 * P_TILE_BYTES;  // A hi, A lo, B hi, B lo
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr uint64_t P_DRAIN_NS = 200000;  // bounded drain of an aborted rank 1
+
+template <bool MN>
+__device__ __forceinline__ void load_operand_pair(unsigned char *dst, const CUtensorMap *map,
+                                                  uint32_t bar, int kb, int32_t row0,
+                                                  int32_t y_kmaj, int32_t batch) {
+    if (MN) {
+#pragma unroll
+        for (int j = 0; j < P_ROWS / MN_BOX; ++j)
+            tma_load_3d_pair(dst + j * MN_BOX_BYTES, map, bar, row0 + j * MN_BOX, kb * BK, batch);
+    } else {
+        tma_load_2d_pair(dst, map, bar, kb * BK, y_kmaj);
+    }
+}
+
+// Epilogue of one CTA: its 128 accumulator rows (TMEM lanes) x 256 columns
+// to C.  Warps 2..5 each own the TMEM lane quadrant (warp & 3).
+__device__ __forceinline__ void store_accumulator(uint32_t tmem_base, int warp, int lane,
+                                                  int64_t m0, int64_t n0, int64_t batch,
+                                                  const Params &p) {
+    const int quad = warp & 3;
+    const int64_t row = m0 + quad * 32 + lane;
+    float *crow = p.c + batch * p.stride_c + row * p.ldc;
+    const bool row_ok = row < p.m;
+    const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
+                        ((p.stride_c & 3) == 0);
+#pragma unroll 1
+    for (int cb = 0; cb < BN / 32; ++cb) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + cb * 32, r);
+        tmem_wait_ld();
+        const int64_t col0 = n0 + cb * 32;
+        if (!row_ok) continue;
+        if (vec_ok && col0 + 32 <= p.n) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4 *>(crow + col0 + j) =
+                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.n) crow[col0 + j] = __uint_as_float(r[j]);
+        }
+    }
+}
+
+template <bool AMN, bool BMN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_ahi,
+                     const __grid_constant__ CUtensorMap map_alo,
+                     const __grid_constant__ CUtensorMap map_bhi,
+                     const __grid_constant__ CUtensorMap map_blo, Params p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // The dynamic shared window starts at the same offset in both CTAs, so
+    // the aligned tiles and barriers below do too (the pair MMA and the
+    // multicast commits address the peer by offset).
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+    uint64_t *empty = full + P_STAGES;
+    uint64_t *accum_full = empty + P_STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+    volatile uint32_t *abort_flag = tmem_slot + 1;
+    volatile int32_t *consumed = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
+    int32_t issued = 0;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x >> 1) * (2 * P_ROWS) + rank * P_ROWS;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.y) * BN;
+    const int64_t nb0 = n0 + rank * P_ROWS;  // this CTA's half of the columns (rows of B^T)
+    const int64_t batch = blockIdx.z;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum_full, 1);
+        *abort_flag = 0;
+        *consumed = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&map_ahi);
+        prefetch_tensormap(&map_alo);
+        prefetch_tensormap(&map_bhi);
+        prefetch_tensormap(&map_blo);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    // barrier inits of both CTAs are visible cluster-wide before any remote
+    // arrival (TMA bytes from rank 1, multicast commits from rank 0)
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            const int32_t ya = static_cast<int32_t>(batch * p.a_rows_per_batch + m0);
+            const int32_t yb = static_cast<int32_t>(batch * p.b_rows_per_batch + nb0);
+            const int32_t z = static_cast<int32_t>(batch);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % P_STAGES;
+                const uint32_t phase = (kb / P_STAGES) & 1;
+                if (!mbar_wait_bounded(&empty[s], phase ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+                if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE_BYTES);
+                unsigned char *st = smem + s * P_STAGE_BYTES;
+                load_operand_pair<AMN>(st, &map_ahi, bar, kb, static_cast<int32_t>(m0), ya, z);
+                load_operand_pair<AMN>(st + P_TILE_BYTES, &map_alo, bar, kb,
+                                       static_cast<int32_t>(m0), ya, z);
+                load_operand_pair<BMN>(st + 2 * P_TILE_BYTES, &map_bhi, bar, kb,
+                                       static_cast<int32_t>(nb0), yb, z);
+                load_operand_pair<BMN>(st + 3 * P_TILE_BYTES, &map_blo, bar, kb,
+                                       static_cast<int32_t>(nb0), yb, z);
+                issued = kb + 1;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (rank 0 only) ----------------
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_tf32(2 * P_ROWS, BN) | (AMN ? (1u << 15) : 0u) |
+                                       (BMN ? (1u << 16) : 0u);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % P_STAGES;
+                const uint32_t phase = (kb / P_STAGES) & 1;
+                if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + s * P_STAGE_BYTES);
+                const uint32_t ahi = st, alo = st + P_TILE_BYTES;
+                const uint32_t bhi = st + 2 * P_TILE_BYTES, blo = st + 3 * P_TILE_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint32_t acc = (kb | kk) ? 1u : 0u;
+                    mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(alo, kk),
+                                     operand_desc<BMN>(bhi, kk), idesc, acc);
+                    mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(ahi, kk),
+                                     operand_desc<BMN>(blo, kk), idesc, 1u);
+                    mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(ahi, kk),
+                                     operand_desc<BMN>(bhi, kk), idesc, 1u);
+                }
+                mma_commit_pair(&empty[s], 0x3);
+                *consumed = kb + 1;
+            }
+            // both epilogues proceed either way; on abort rank 0 skips its stores
+            mma_commit_pair(accum_full, 0x3);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+        const bool ok = mbar_wait_bounded(accum_full, 0, DEVERR_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        if (ok && !*abort_flag) store_accumulator(tmem_base, warp, lane, m0, n0, batch, p);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && lane == 0 && *abort_flag) {
+        if (rank == 0) {
+            // loads this CTA issued land on its own `full` barriers
+            for (int kb = *consumed; kb < issued; ++kb)
+                mbar_wait_bounded(&full[kb % P_STAGES], (kb / P_STAGES) & 1,
+                                  DEVERR_TIMEOUT_PRODUCER);
+        } else if (issued > 0) {
+            // rank 1's loads report to rank 0's barriers: give any still in
+            // flight a bounded time to land before the pair retires
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < P_DRAIN_NS) __nanosleep(1000);
+        }
+    }
+    // neither CTA frees TMEM or exits while the other may still read its
+    // shared memory or TMEM
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -623,52 +833,91 @@ int make_operand_map(CUtensorMap *map, const OperandPlan &p, const float *buf, i
     return tf32x3::make_kmajor_map(map, buf, batch * p.rows, p.cp, box_rows);
 }
 
+// Large dynamic shared memory is a per-device function attribute: set it
+// once per (kernel, device).
+int ensure_smem_attr(const void *fn, int bytes, uint64_t *done_mask, const char *what) {
+    int d = 0;
+    CHELIS_TRY(current_device_checked(&d));
+    const uint64_t bit = 1ull << (d & 63);
+    if (*done_mask & bit) return CHELIS_CUDA_OK;
+    CHELIS_TRY(check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               bytes),
+                          what));
+    *done_mask |= bit;
+    return CHELIS_CUDA_OK;
+}
+
 template <bool AMN, bool BMN>
 int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMap &bhi,
-                const CUtensorMap &blo, const tf32x3::Params &p, dim3 grid, cudaStream_t s) {
+                const CUtensorMap &blo, const tf32x3::Params &p, bool pair, cudaStream_t s) {
     using namespace tf32x3;
-    static bool attr_set = false;
-    if (!attr_set) {
-        CHELIS_TRY(check_cuda(cudaFuncSetAttribute(gemm_kernel<AMN, BMN>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   SMEM_BYTES),
-                              "cudaFuncSetAttribute(gemm_kernel)"));
-        attr_set = true;
+    if (pair) {
+        static uint64_t done = 0;
+        CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(gemm_pair_kernel<AMN, BMN>),
+                                    P_SMEM_BYTES, &done, "cudaFuncSetAttribute(gemm_pair_kernel)"));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * ((p.m + 2 * P_ROWS - 1) / (2 * P_ROWS))),
+                           static_cast<unsigned>((p.n + BN - 1) / BN),
+                           static_cast<unsigned>(p.batch));
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CHELIS_TRY(check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<AMN, BMN>, ahi, alo, bhi,
+                                                 blo, p),
+                              "cudaLaunchKernelEx(gemm_pair_kernel)"));
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("gemm_pair_kernel(3xtf32)");
+        return CHELIS_CUDA_OK;
     }
+    static uint64_t done = 0;
+    CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(gemm_kernel<AMN, BMN>), SMEM_BYTES,
+                                &done, "cudaFuncSetAttribute(gemm_kernel)"));
+    dim3 grid(static_cast<unsigned>((p.n + BN - 1) / BN), static_cast<unsigned>((p.m + BM - 1) / BM),
+              static_cast<unsigned>(p.batch));
     gemm_kernel<AMN, BMN><<<grid, THREADS, SMEM_BYTES, s>>>(ahi, alo, bhi, blo, p);
     g_launches++;
     CHELIS_LAUNCH_CHECK("gemm_kernel(3xtf32)");
     return CHELIS_CUDA_OK;
 }
 
-// Main kernel on split operands.
+// Main kernel on split operands.  CTA pairs (256-row tiles) whenever the
+// product has more than one 128-row tile; a single CTA per 128 x 256 tile
+// otherwise.
 int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
                       const OperandPlan &pb, const float *bhi, const float *blo, int64_t m,
                       int64_t n, int64_t k, float *c, int64_t ldc, int64_t stride_c, int64_t batch,
                       cudaStream_t s) {
     using namespace tf32x3;
+    const bool pair = m > BM && g_pair_tiles.load();
+    const int b_box = pair ? P_ROWS : BN;
     CUtensorMap mahi, malo, mbhi, mblo;
     CHELIS_TRY(make_operand_map(&mahi, pa, ahi, batch, BM));
     CHELIS_TRY(make_operand_map(&malo, pa, alo, batch, BM));
-    CHELIS_TRY(make_operand_map(&mbhi, pb, bhi, batch, BN));
-    CHELIS_TRY(make_operand_map(&mblo, pb, blo, batch, BN));
+    CHELIS_TRY(make_operand_map(&mbhi, pb, bhi, batch, b_box));
+    CHELIS_TRY(make_operand_map(&mblo, pb, blo, batch, b_box));
     Params p;
     p.m = m;
     p.n = n;
+    p.batch = batch;
     p.num_kb = static_cast<int32_t>((k + BK - 1) / BK);
     p.a_rows_per_batch = m;
     p.b_rows_per_batch = n;
     p.c = c;
     p.ldc = ldc;
     p.stride_c = stride_c;
-    dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>((m + BM - 1) / BM),
-              static_cast<unsigned>(batch));
     if (pa.mn) {
-        if (pb.mn) return launch_main<true, true>(mahi, malo, mbhi, mblo, p, grid, s);
-        return launch_main<true, false>(mahi, malo, mbhi, mblo, p, grid, s);
+        if (pb.mn) return launch_main<true, true>(mahi, malo, mbhi, mblo, p, pair, s);
+        return launch_main<true, false>(mahi, malo, mbhi, mblo, p, pair, s);
     }
-    if (pb.mn) return launch_main<false, true>(mahi, malo, mbhi, mblo, p, grid, s);
-    return launch_main<false, false>(mahi, malo, mbhi, mblo, p, grid, s);
+    if (pb.mn) return launch_main<false, true>(mahi, malo, mbhi, mblo, p, pair, s);
+    return launch_main<false, false>(mahi, malo, mbhi, mblo, p, pair, s);
 }
 
 struct GemmPlan {
@@ -785,3 +1034,12 @@ extern "C" int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n,
     scratch_free(scratch, s);
     return st;
 }
+
+extern "C" int chelis_cuda_set_gemm_pairs(int enable) {
+    if (enable != 0 && enable != 1)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "gemm pair mode must be 0 or 1");
+    g_pair_tiles.store(enable);
+    return CHELIS_CUDA_OK;
+}
+
+extern "C" int chelis_cuda_get_gemm_pairs(void) { return g_pair_tiles.load(); }

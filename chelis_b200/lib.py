@@ -92,6 +92,8 @@ SIGNATURES = {
     "chelis_cuda_dgemm_strided_batched_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
     "chelis_cuda_sgemm": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
     "chelis_cuda_dgemm": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    "chelis_cuda_set_gemm_pairs": (c_int, [c_int]),
+    "chelis_cuda_get_gemm_pairs": (c_int, []),
     "chelis_cuda_sgemm_host": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
     "chelis_cuda_dgemm_host": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
     "chelis_cuda_tf32x3_split": (c_int, [c_int, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),

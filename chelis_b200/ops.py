@@ -51,6 +51,19 @@ def gemm_mode(mode: int):
 
 
 @contextlib.contextmanager
+def gemm_pairs(enable: bool):
+    """3xTF32 main kernel on CTA pairs (256 x 256 tiles, the default) or on
+    single CTAs (128 x 256 tiles)."""
+    lib = L.load()
+    old = lib.chelis_cuda_get_gemm_pairs()
+    L.call("chelis_cuda_set_gemm_pairs", int(enable))
+    try:
+        yield
+    finally:
+        L.call("chelis_cuda_set_gemm_pairs", old)
+
+
+@contextlib.contextmanager
 def rows_mode(mode: int):
     lib = L.load()
     old = lib.chelis_cuda_get_rows_mode()

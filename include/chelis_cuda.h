@@ -193,6 +193,12 @@ int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
 int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
                       int64_t lda, int64_t stride_a, const double *b, int64_t ldb,
                       int64_t stride_b, double *c, int64_t ldc, int64_t stride_c, int64_t batch);
+/* Tile shape of the 3xTF32 main kernel: 1 (default) = 256 x 256 tiles on
+ * CTA pairs (tcgen05 cta_group::2) for products with more than 128 rows,
+ * 0 = 128 x 256 tiles on single CTAs.  Results are identical in both modes
+ * up to the f32 accumulation order inside the tensor core.  Process-wide. */
+int chelis_cuda_set_gemm_pairs(int enable);
+int chelis_cuda_get_gemm_pairs(void);
 /* [05-OP-30] matmul on HOST buffers (row-major, same argument meaning as
  * chelis_cuda_sgemm / chelis_cuda_dgemm, all pointers host pointers).  The
  * reference uploads both operands, runs hipBLAS and downloads C in sequence

@@ -208,3 +208,29 @@ def test_split_forced_kmajor_from_transposed_source(cuda, orc):
     lib = L.load()
     assert lib.chelis_cuda_tf32x3_split(0, 1, m, k, at.data_ptr(), k, 0, 1, ahi.data_ptr(),
                                         alo.data_ptr()) == 1  # CHELIS_CUDA_ERR_DOMAIN
+
+
+@pytest.mark.parametrize("pairs", [True, False])
+@pytest.mark.parametrize("m,n,k,ta,tb,batch", [
+    (300, 500, 700, False, False, 1),     # ragged pair: rows 300..383 of the second pair idle
+    (256, 256, 32, False, False, 1),      # exactly one pair tile, one k-block
+    (513, 129, 1000, True, False, 1),     # MN-major A on pairs
+    (384, 300, 257, True, True, 2),       # MN-major A, K-major B, batched
+    (1024, 768, 96, False, True, 3),      # K-major both, batched
+])
+def test_sgemm_pair_and_single_cta_tiles(cuda, orc, pairs, m, n, k, ta, tb, batch):
+    """The CTA-pair (cta_group::2, 256 x 256) and single-CTA (128 x 256) main
+    kernels against the oracle, over both operand majors and batches."""
+    import torch
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=m + n + k + batch, batch=batch)
+    sw = (lambda x: np.ascontiguousarray(np.swapaxes(x, -1, -2)))
+    at = sw(a) if ta else a
+    bt = sw(b) if tb else b
+    with cuda.gemm_pairs(pairs):
+        c = cuda.matmul(torch.from_numpy(at).cuda(), torch.from_numpy(bt).cuda(), ta, tb)
+        torch.cuda.synchronize()
+    cuda.device_status()
+    got = c.cpu().numpy().reshape(batch, m, n)
+    a3, b3 = a.reshape(batch, m, k), b.reshape(batch, k, n)
+    for i in range(batch):
+        assert _rel_err(got[i], orc.gemm(a3[i], b3[i]), a3[i], b3[i]) <= 1e-5, i
