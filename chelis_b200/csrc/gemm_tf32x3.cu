@@ -56,6 +56,7 @@ constexpr int MN_BOX_BYTES = MN_BOX * BK * 4;  // 4 KiB
 
 struct Params {
     int64_t m, n, batch;
+    int64_t pairs_m, tiles_n;  // pair kernel: 256-row tile count, 256-column tile count
     int32_t num_kb;       // ceil(K / BK)
     int64_t a_rows_per_batch, b_rows_per_batch;  // K-major split buffers: rows per batch item
     float *c;
@@ -284,6 +285,7 @@ constexpr int P_TILE_BYTES = P_ROWS * BK * 4;   // 16 KiB
 constexpr int P_STAGE_BYTES = 4 * P_TILE_BYTES;  // A hi, A lo, B hi, B lo
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr uint64_t P_DRAIN_NS = 200000;  // bounded drain of an aborted rank 1
+constexpr int P_GROUP = 8;                // pair-rows per group of the tile order
 
 template <bool MN>
 __device__ __forceinline__ void load_operand_pair(unsigned char *dst, const CUtensorMap *map,
@@ -353,8 +355,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
-    const int64_t m0 = static_cast<int64_t>(blockIdx.x >> 1) * (2 * P_ROWS) + rank * P_ROWS;
-    const int64_t n0 = static_cast<int64_t>(blockIdx.y) * BN;
+    // Grouped tile order: consecutive pairs walk P_GROUP pair-rows down one
+    // column of tiles before moving right, so the ~74 pairs in flight share
+    // a few A and B panels in L2 instead of streaming all of A.
+    int64_t pm, pn;
+    {
+        const int64_t pid = blockIdx.x >> 1;
+        const int64_t per_group = static_cast<int64_t>(P_GROUP) * p.tiles_n;
+        const int64_t first = (pid / per_group) * P_GROUP;
+        const int64_t rem = p.pairs_m - first;
+        const int64_t gsize = rem < P_GROUP ? rem : P_GROUP;
+        const int64_t in = pid % per_group;
+        pm = first + in % gsize;
+        pn = in / gsize;
+    }
+    const int64_t m0 = pm * (2 * P_ROWS) + rank * P_ROWS;
+    const int64_t n0 = pn * BN;
     const int64_t nb0 = n0 + rank * P_ROWS;  // this CTA's half of the columns (rows of B^T)
     const int64_t batch = blockIdx.z;
 
@@ -856,8 +872,12 @@ int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMa
         CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(gemm_pair_kernel<AMN, BMN>),
                                     P_SMEM_BYTES, &done, "cudaFuncSetAttribute(gemm_pair_kernel)"));
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * ((p.m + 2 * P_ROWS - 1) / (2 * P_ROWS))),
-                           static_cast<unsigned>((p.n + BN - 1) / BN),
+        Params q = p;
+        q.pairs_m = (p.m + 2 * P_ROWS - 1) / (2 * P_ROWS);
+        q.tiles_n = (p.n + BN - 1) / BN;
+        if (2 * q.pairs_m * q.tiles_n > INT32_MAX)
+            return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "matmul tile count beyond 2^31");
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * q.pairs_m * q.tiles_n), 1,
                            static_cast<unsigned>(p.batch));
         cfg.blockDim = dim3(THREADS);
         cfg.dynamicSmemBytes = P_SMEM_BYTES;
@@ -870,7 +890,7 @@ int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMa
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         CHELIS_TRY(check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<AMN, BMN>, ahi, alo, bhi,
-                                                 blo, p),
+                                                 blo, q),
                               "cudaLaunchKernelEx(gemm_pair_kernel)"));
         g_launches++;
         CHELIS_LAUNCH_CHECK("gemm_pair_kernel(3xtf32)");
@@ -906,6 +926,8 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     p.m = m;
     p.n = n;
     p.batch = batch;
+    p.pairs_m = 0;
+    p.tiles_n = 0;
     p.num_kb = static_cast<int32_t>((k + BK - 1) / BK);
     p.a_rows_per_batch = m;
     p.b_rows_per_batch = n;

@@ -217,6 +217,7 @@ def test_split_forced_kmajor_from_transposed_source(cuda, orc):
     (513, 129, 1000, True, False, 1),     # MN-major A on pairs
     (384, 300, 257, True, True, 2),       # MN-major A, K-major B, batched
     (1024, 768, 96, False, True, 3),      # K-major both, batched
+    (2404, 600, 64, False, False, 1),     # 10 pair-rows: two tile-order groups, ragged last
 ])
 def test_sgemm_pair_and_single_cta_tiles(cuda, orc, pairs, m, n, k, ta, tb, batch):
     """The CTA-pair (cta_group::2, 256 x 256) and single-CTA (128 x 256) main
