@@ -1,0 +1,557 @@
+// attention.cu -- causal softmax attention without the [S, S] scores in HBM.
+//
+// The reference evaluates attention as its graph spells it: scores
+// (q.k^T)*scale, where(causal, ., -inf), softmax over the last axis, then
+// probabilities . v (spec 05 section 4.7; tier2.rs attention lowering), every
+// step a separate tensor.  Here one kernel keeps a 128-row query tile's
+// scores, probabilities and output accumulator in tensor memory and streams
+// the keys and values through shared memory in blocks of 64, combining the
+// blocks with the running-maximum form of softmax:
+//
+//   m_j = max(m_{j-1}, rowmax(s_j)),  p_j = exp(s_j - m_j),
+//   l_j = l_{j-1} exp(m_{j-1} - m_j) + rowsum(p_j),
+//   o_j = o_{j-1} exp(m_{j-1} - m_j) + p_j . v_j,   out = o_J / l_J.
+//
+// Every product is 3xTF32 on tcgen05 (hi/lo split of both operands, three
+// MMAs), so the f32 result carries f32-level error like the rest of the
+// block; the query tile and the probabilities are the MMA's A operand
+// straight from tensor memory, the keys and values the B operand from
+// shared memory (TMA, 128-byte swizzle).
+//
+// Roles (192 threads): warp 0 loads key/value blocks with TMA, warp 1 issues
+// the MMAs, warps 2-5 own one query row per thread (TMEM lane = row).
+// Every wait is bounded; a timeout sets the device error word and the CTA
+// winds down.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "common.cuh"
+
+namespace chelis {
+
+extern std::atomic<uint64_t> g_launches;
+
+namespace attn {
+
+constexpr int BQ = 128;      // query rows per CTA (TMEM lanes)
+constexpr int BKV = 64;      // keys per block
+constexpr int THREADS = 192;
+constexpr int MN_BOX_BYTES = 32 * 32 * 4;  // MN-major TMA box 32 x 32 f32
+
+template <int DH>
+struct Fwd {
+    static_assert(DH == 32 || DH == 64, "flash attention path covers head dims 32 and 64");
+    static constexpr int KCH = DH / 32;                 // 128-byte chunks along the head dim
+    static constexpr int K_TILE = BKV * DH * 4;          // one of hi / lo
+    static constexpr int V_TILE = BKV * DH * 4;
+    static constexpr int STAGE = 2 * K_TILE + 2 * V_TILE;
+    static constexpr int STAGES = 2;
+    // at least ~116 KiB so that one CTA (holding all 512 TMEM columns) runs per SM
+    static constexpr int SMEM_USED = STAGES * STAGE + 1024 + 512;
+    static constexpr int SMEM = SMEM_USED > 118784 ? SMEM_USED : 118784;
+    // tensor-memory columns
+    static constexpr uint32_t C_QHI = 0, C_QLO = DH;
+    static constexpr uint32_t C_S0 = 2 * DH, C_S1 = 2 * DH + BKV;
+    static constexpr uint32_t C_PHI = 2 * DH + 2 * BKV, C_PLO = C_PHI + BKV;
+    static constexpr uint32_t C_O0 = C_PLO + BKV, C_O1 = C_O0 + DH;
+    static constexpr uint32_t COLS = 512;
+    static_assert(C_O1 + DH <= COLS, "tensor memory budget");
+};
+
+struct FwdParams {
+    const float *q;                  // f32 query rows (split in the kernel)
+    int64_t q_row, q_b, q_h;         // element strides: row, batch item, head
+    float *o;                        // output rows
+    int64_t o_row, o_b, o_h;
+    float *lse;                      // [BH][S] log-sum-exp of the scaled scores (may be null)
+    int heads, seq;
+    float scale;
+    int n_qblocks;
+};
+
+__device__ __forceinline__ float rna_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t &hi, uint32_t &lo) {
+    const float h = rna_tf32(x);
+    hi = __float_as_uint(h);
+    lo = __float_as_uint(isfinite(x) ? rna_tf32(__fsub_rn(x, h)) : 0.0f);
+}
+
+// K-major 128-byte-swizzle operand (rows x 32-float chunks), K-step kk of 8
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int rows, int kk) {
+    return sw128_kmajor_desc(tile + (kk >> 2) * rows * 128 + (kk & 3) * 32);
+}
+// MN-major 128-byte / 32-byte-atom operand made of 32 x 32 boxes laid out
+// [k-chunk][mn-chunk]; K-step kk of 8 (LBO 4 KiB to the next 32 of MN,
+// SBO 512 B to the next 4 k)
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int mn_chunks, int kk) {
+    const uint32_t a = tile + (kk >> 2) * mn_chunks * MN_BOX_BYTES + (kk & 3) * 1024;
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((a >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(MN_BOX_BYTES >> 4) << 16;
+    d |= static_cast<uint64_t>(512u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(1u) << 61;
+    return d;
+}
+
+template <int DH>
+__global__ void __launch_bounds__(THREADS, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap map_khi,
+               const __grid_constant__ CUtensorMap map_klo,
+               const __grid_constant__ CUtensorMap map_vhi,
+               const __grid_constant__ CUtensorMap map_vlo, FwdParams p) {
+    using C = Fwd<DH>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE);
+    uint64_t *k_full = bars;          // [2]
+    uint64_t *v_full = bars + 2;      // [2]
+    uint64_t *kv_empty = bars + 4;    // [2]
+    uint64_t *s_full = bars + 6;      // [2]
+    uint64_t *s_free = bars + 8;      // [2]
+    uint64_t *o_full = bars + 10;     // [2]
+    uint64_t *o_free = bars + 12;     // [2]
+    uint64_t *p_full = bars + 14;
+    uint64_t *p_free = bars + 15;
+    uint64_t *q_ready = bars + 16;
+    uint64_t *mma_done = bars + 17;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 18);
+    volatile uint32_t *abort_flag = tmem_slot + 1;
+    volatile int32_t *k_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
+    volatile int32_t *v_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 3);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.x);  // longest rows first
+    const int q0 = qb * BQ;
+    int last_key = q0 + BQ - 1;
+    if (last_key > p.seq - 1) last_key = p.seq - 1;
+    const int nkb = last_key / BKV + 1;  // key blocks up to the diagonal
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 4);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&o_free[i], 4);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(p_free, 1);
+        mbar_init(q_ready, 4);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        *k_used = 0;
+        *v_used = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&map_khi);
+        prefetch_tensormap(&map_klo);
+        prefetch_tensormap(&map_vhi);
+        prefetch_tensormap(&map_vlo);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = *tmem_slot;
+    int32_t issued = 0;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int j = 0; j < nkb; ++j) {
+                const int s = j & 1;
+                if (*abort_flag ||
+                    !mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                unsigned char *st = smem + s * C::STAGE;
+                mbar_arrive_expect_tx(&k_full[s], 2 * C::K_TILE);
+#pragma unroll
+                for (int c = 0; c < C::KCH; ++c) {
+                    tma_load_3d(st + c * BKV * 128, &map_khi, &k_full[s], c * 32, j * BKV, bh);
+                    tma_load_3d(st + C::K_TILE + c * BKV * 128, &map_klo, &k_full[s], c * 32,
+                                j * BKV, bh);
+                }
+                unsigned char *sv = st + 2 * C::K_TILE;
+                mbar_arrive_expect_tx(&v_full[s], 2 * C::V_TILE);
+#pragma unroll
+                for (int kc = 0; kc < BKV / 32; ++kc)
+#pragma unroll
+                    for (int dc = 0; dc < C::KCH; ++dc) {
+                        const int off = (kc * C::KCH + dc) * MN_BOX_BYTES;
+                        tma_load_3d(sv + off, &map_vhi, &v_full[s], dc * 32, j * BKV + kc * 32, bh);
+                        tma_load_3d(sv + C::V_TILE + off, &map_vlo, &v_full[s], dc * 32,
+                                    j * BKV + kc * 32, bh);
+                    }
+                issued = j + 1;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_tf32(BQ, BKV);
+            constexpr uint32_t idesc_o = idesc_tf32(BQ, DH) | (1u << 16);  // B (values) MN-major
+            bool ok = mbar_wait_bounded(q_ready, 0, DEVERR_TIMEOUT_MMA);
+            if (!ok) *abort_flag = 1;
+            for (int j = 0; ok && j <= nkb; ++j) {
+                if (j < nkb) {
+                    const int s = j & 1;
+                    if (*abort_flag ||
+                        !mbar_wait_bounded(&k_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
+                        !mbar_wait_bounded(&s_free[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    *k_used = j + 1;
+                    tc_fence_after();
+                    const uint32_t kt = smem_u32(smem + s * C::STAGE);
+                    const uint32_t d = tm + (s ? C::C_S1 : C::C_S0);
+#pragma unroll
+                    for (int kk = 0; kk < DH / 8; ++kk) {
+                        const uint64_t bhi = kmajor_desc(kt, BKV, kk);
+                        const uint64_t blo = kmajor_desc(kt + C::K_TILE, BKV, kk);
+                        mma_tf32_ts(d, tm + C::C_QLO + 8 * kk, bhi, idesc_s, kk ? 1u : 0u);
+                        mma_tf32_ts(d, tm + C::C_QHI + 8 * kk, blo, idesc_s, 1u);
+                        mma_tf32_ts(d, tm + C::C_QHI + 8 * kk, bhi, idesc_s, 1u);
+                    }
+                    mma_commit(&s_full[s]);
+                }
+                if (j >= 1) {
+                    const int jj = j - 1, s = jj & 1;
+                    if (*abort_flag || !mbar_wait_bounded(p_full, jj & 1, DEVERR_TIMEOUT_MMA) ||
+                        !mbar_wait_bounded(&v_full[s], (jj >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
+                        !mbar_wait_bounded(&o_free[s], ((jj >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    *v_used = jj + 1;
+                    tc_fence_after();
+                    const uint32_t vt = smem_u32(smem + s * C::STAGE + 2 * C::K_TILE);
+                    const uint32_t d = tm + (s ? C::C_O1 : C::C_O0);
+#pragma unroll
+                    for (int kk = 0; kk < BKV / 8; ++kk) {
+                        const uint64_t bhi = mnmajor_desc(vt, C::KCH, kk);
+                        const uint64_t blo = mnmajor_desc(vt + C::V_TILE, C::KCH, kk);
+                        mma_tf32_ts(d, tm + C::C_PLO + 8 * kk, bhi, idesc_o, kk ? 1u : 0u);
+                        mma_tf32_ts(d, tm + C::C_PHI + 8 * kk, blo, idesc_o, 1u);
+                        mma_tf32_ts(d, tm + C::C_PHI + 8 * kk, bhi, idesc_o, 1u);
+                    }
+                    mma_commit(&o_full[s]);
+                    mma_commit(p_free);
+                    mma_commit(&kv_empty[s]);
+                }
+            }
+            // no MMA may still run when tensor memory is released
+            mma_commit(mma_done);
+            mbar_wait_bounded(mma_done, 0, DEVERR_TIMEOUT_MMA);
+        }
+    } else {
+        // ---------------- rows: one query row per thread ----------------
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int qrow = q0 + r;
+        const bool live = qrow < p.seq;
+        const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+        const int b = bh / p.heads, h = bh % p.heads;
+        // query row -> hi / lo in tensor memory
+        {
+            const float *qr = p.q + b * p.q_b + h * p.q_h + static_cast<int64_t>(qrow) * p.q_row;
+#pragma unroll
+            for (int c = 0; c < C::KCH; ++c) {
+                uint32_t hi[32], lo[32];
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (live) v = *reinterpret_cast<const float4 *>(qr + c * 32 + i);
+                    split_tf32(v.x, hi[i], lo[i]);
+                    split_tf32(v.y, hi[i + 1], lo[i + 1]);
+                    split_tf32(v.z, hi[i + 2], lo[i + 2]);
+                    split_tf32(v.w, hi[i + 3], lo[i + 3]);
+                }
+                tmem_st_32x32b_x32(tm + lane_base + C::C_QHI + c * 32, hi);
+                tmem_st_32x32b_x32(tm + lane_base + C::C_QLO + c * 32, lo);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_ready);
+        }
+        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        float acc[DH];
+#pragma unroll
+        for (int i = 0; i < DH; ++i) acc[i] = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nkb; ++j) {
+            const int s = j & 1;
+            if (*abort_flag || !mbar_wait_bounded(&s_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[BKV];
+            tmem_ld_32x32b_x32(tm + lane_base + (s ? C::C_S1 : C::C_S0),
+                               *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+            tmem_ld_32x32b_x32(tm + lane_base + (s ? C::C_S1 : C::C_S0) + 32,
+                               *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[s]);
+            // scale, causal mask, running maximum
+            const int key0 = j * BKV;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) {
+                const int key = key0 + c;
+                const float x = (key <= qrow && key < p.seq)
+                                    ? __fmul_rn(__uint_as_float(sr[c]), p.scale)
+                                    : -INFINITY;
+                sr[c] = __float_as_uint(x);
+                mx = fmaxf(mx, x);
+            }
+            const float m_new = fmaxf(m, mx);
+            const float alpha = __expf(__fsub_rn(m, m_new));
+            // probabilities -> tensor memory once the previous block's P . V is done
+            if (j >= 1 && (*abort_flag || !mbar_wait_bounded(p_free, (j - 1) & 1, DEVERR_TIMEOUT_EPILOGUE))) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float rs = 0.0f;
+#pragma unroll
+            for (int h32 = 0; h32 < BKV / 32; ++h32) {
+                uint32_t phi[32], plo[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float e = __expf(__fsub_rn(__uint_as_float(sr[h32 * 32 + c]), m_new));
+                    rs = __fadd_rn(rs, e);
+                    split_tf32(e, phi[c], plo[c]);
+                }
+                tmem_st_32x32b_x32(tm + lane_base + C::C_PHI + h32 * 32, phi);
+                tmem_st_32x32b_x32(tm + lane_base + C::C_PLO + h32 * 32, plo);
+            }
+            l = __fadd_rn(__fmul_rn(l, alpha), rs);
+            m = m_new;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            // fold in the previous block's P . V
+            if (j >= 1) {
+                const int jj = j - 1, so = jj & 1;
+                if (*abort_flag || !mbar_wait_bounded(&o_full[so], (jj >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < C::KCH; ++c) {
+                    uint32_t ov[32];
+                    tmem_ld_32x32b_x32(tm + lane_base + (so ? C::C_O1 : C::C_O0) + c * 32, ov);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        acc[c * 32 + i] = __fadd_rn(__fmul_rn(acc[c * 32 + i], alpha_prev),
+                                                    __uint_as_float(ov[i]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_free[so]);
+            }
+            alpha_prev = alpha;
+        }
+        if (ok) {
+            const int jj = nkb - 1, so = jj & 1;
+            if (!*abort_flag && mbar_wait_bounded(&o_full[so], (jj >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < C::KCH; ++c) {
+                    uint32_t ov[32];
+                    tmem_ld_32x32b_x32(tm + lane_base + (so ? C::C_O1 : C::C_O0) + c * 32, ov);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        acc[c * 32 + i] = __fadd_rn(__fmul_rn(acc[c * 32 + i], alpha_prev),
+                                                    __uint_as_float(ov[i]));
+                }
+                if (live) {
+                    float *orow = p.o + b * p.o_b + h * p.o_h + static_cast<int64_t>(qrow) * p.o_row;
+#pragma unroll
+                    for (int i = 0; i < DH; i += 4)
+                        *reinterpret_cast<float4 *>(orow + i) =
+                            make_float4(__fdiv_rn(acc[i], l), __fdiv_rn(acc[i + 1], l),
+                                        __fdiv_rn(acc[i + 2], l), __fdiv_rn(acc[i + 3], l));
+                    if (p.lse) p.lse[static_cast<int64_t>(bh) * p.seq + qrow] = __fadd_rn(m, logf(l));
+                }
+            } else {
+                *abort_flag = 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && lane == 0 && *abort_flag) {
+        // let issued key / value loads land before the CTA retires
+        for (int j = *k_used; j < issued; ++j)
+            mbar_wait_bounded(&k_full[j & 1], (j >> 1) & 1, DEVERR_TIMEOUT_PRODUCER);
+        for (int j = *v_used; j < issued; ++j)
+            mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1, DEVERR_TIMEOUT_PRODUCER);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tm, C::COLS);
+    }
+}
+
+// hi / lo of a flat f32 array (a [BH][S][DH] head tensor with DH a multiple
+// of 32 is its own K-major split layout)
+__global__ void split_flat_kernel(const float *__restrict__ x, float *__restrict__ hi,
+                                  float *__restrict__ lo, int64_t n4) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4 *>(x)[i];
+        uint32_t h[4], l[4];
+        split_tf32(v.x, h[0], l[0]);
+        split_tf32(v.y, h[1], l[1]);
+        split_tf32(v.z, h[2], l[2]);
+        split_tf32(v.w, h[3], l[3]);
+        reinterpret_cast<uint4 *>(hi)[i] = make_uint4(h[0], h[1], h[2], h[3]);
+        reinterpret_cast<uint4 *>(lo)[i] = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+}  // namespace attn
+
+namespace {
+
+typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                             const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                             const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// [BH][S][DH] head tensor -> 3-D map {DH, S, BH}; box {32, rows, 1}.  Rows
+// past S read as zeros (per head).
+int head_map(CUtensorMap *map, const float *base, int64_t bh, int64_t s, int dh, int box_rows,
+             bool mn_major) {
+    EncodeFn fn = reinterpret_cast<EncodeFn>(tf32x3::encode_fn());
+    if (!fn) return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(dh), static_cast<cuuint64_t>(s),
+                          static_cast<cuuint64_t>(bh)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(dh) * 4, static_cast<cuuint64_t>(s * dh) * 4};
+    cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled(head) failed (%d)", (int)r);
+    return CHELIS_CUDA_OK;
+}
+
+}  // namespace
+
+bool flash_attention_supported(int64_t dh) { return dh == 32 || dh == 64; }
+
+int split_flat(const float *x, float *hi, float *lo, int64_t n, cudaStream_t s) {
+    const int64_t n4 = n / 4;
+    int64_t blocks = (n4 + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    attn::split_flat_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, hi, lo, n4);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("split_flat_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+// Causal attention forward on split keys / values ([BH][S][DH] hi / lo,
+// contiguous) and f32 queries addressed by strides; output rows addressed
+// the same way; lse [BH][S] optional.
+int flash_fwd(int64_t bh, int64_t heads, int64_t seq, int64_t dh, float scale, const float *q,
+              int64_t q_row, int64_t q_b, int64_t q_h, const float *k_hi, const float *k_lo,
+              const float *v_hi, const float *v_lo, float *o, int64_t o_row, int64_t o_b,
+              int64_t o_h, float *lse, cudaStream_t s) {
+    if (!flash_attention_supported(dh))
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "flash attention covers head dims 32, 64");
+    if (bh > 65535 || seq > (1 << 24))
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "attention extents beyond the grid");
+    CUtensorMap mkh, mkl, mvh, mvl;
+    CHELIS_TRY(head_map(&mkh, k_hi, bh, seq, static_cast<int>(dh), attn::BKV, false));
+    CHELIS_TRY(head_map(&mkl, k_lo, bh, seq, static_cast<int>(dh), attn::BKV, false));
+    CHELIS_TRY(head_map(&mvh, v_hi, bh, seq, static_cast<int>(dh), 32, true));
+    CHELIS_TRY(head_map(&mvl, v_lo, bh, seq, static_cast<int>(dh), 32, true));
+    attn::FwdParams p;
+    p.q = q;
+    p.q_row = q_row;
+    p.q_b = q_b;
+    p.q_h = q_h;
+    p.o = o;
+    p.o_row = o_row;
+    p.o_b = o_b;
+    p.o_h = o_h;
+    p.lse = lse;
+    p.heads = static_cast<int>(heads);
+    p.seq = static_cast<int>(seq);
+    p.scale = scale;
+    p.n_qblocks = static_cast<int>((seq + attn::BQ - 1) / attn::BQ);
+    dim3 grid(static_cast<unsigned>(p.n_qblocks), static_cast<unsigned>(bh));
+    auto launch = [&](auto kern, int smem) -> int {
+        static uint64_t done[2] = {0, 0};
+        CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(kern), smem,
+                                    &done[dh == 64 ? 1 : 0], "cudaFuncSetAttribute(attn fwd)"));
+        kern<<<grid, attn::THREADS, smem, s>>>(mkh, mkl, mvh, mvl, p);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("attn::fwd_kernel");
+        return CHELIS_CUDA_OK;
+    };
+    if (dh == 64) return launch(attn::fwd_kernel<64>, attn::Fwd<64>::SMEM);
+    return launch(attn::fwd_kernel<32>, attn::Fwd<32>::SMEM);
+}
+
+}  // namespace chelis
+
+using namespace chelis;
+
+extern "C" int chelis_cuda_attention_causal_fwd(int64_t bh, int64_t seq, int64_t dh, float scale,
+                                                const float *q, const float *k, const float *v,
+                                                float *o, float *lse) {
+    if (bh < 0 || seq < 0 || dh <= 0)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in attention at i64");
+    if (bh == 0 || seq == 0) return CHELIS_CUDA_OK;
+    if (!flash_attention_supported(dh))
+        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "flash attention covers head dims 32, 64");
+    cudaStream_t s = current_stream();
+    const int64_t n = bh * seq * dh;
+    void *buf = nullptr;
+    CHELIS_TRY(scratch_alloc(&buf, 4 * n * sizeof(float), s));
+    float *khi = static_cast<float *>(buf), *klo = khi + n, *vhi = klo + n, *vlo = vhi + n;
+    int st = split_flat(k, khi, klo, n, s);
+    if (st == CHELIS_CUDA_OK) st = split_flat(v, vhi, vlo, n, s);
+    if (st == CHELIS_CUDA_OK)
+        st = flash_fwd(bh, 1, seq, dh, scale, q, dh, seq * dh, 0, khi, klo, vhi, vlo, o, dh,
+                       seq * dh, 0, lse, s);
+    scratch_free(buf, s);
+    return st;
+}

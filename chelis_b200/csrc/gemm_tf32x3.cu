@@ -89,15 +89,6 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int kk) {
     return MN ? sw128a32_mnmajor_desc(tile + kk * 1024) : sw128_kmajor_desc(tile + kk * 32);
 }
 
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int32_t x, int32_t y, int32_t z) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-        : "memory");
-}
-
 // Load one operand's tile for k-block `kb` into `dst`.
 template <bool MN, int ROWS>
 __device__ __forceinline__ void load_operand(unsigned char *dst, const CUtensorMap *map,

@@ -9,6 +9,7 @@
 #include "chain.cu"
 #include "portfolio.cu"
 #include "mlp.cu"
+#include "attention.cu"
 #include "block.cu"
 #include "abi.cu"
 #include "chain_noalloc.cu"

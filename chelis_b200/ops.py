@@ -148,6 +148,22 @@ def matmul_host(a: torch.Tensor, b: torch.Tensor, trans_a: bool = False, trans_b
     return out
 
 
+def attention_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                     with_lse: bool = False):
+    """softmax(where(causal, (q.k^T)*scale, -inf)).v for f32 [..., seq, dh]
+    heads (flattened to [bh, seq, dh]); head dims 32 and 64."""
+    if not (q.dtype == k.dtype == v.dtype == torch.float32) or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("attention_causal takes three f32 tensors of one shape")
+    _prepare(q, k, v)
+    seq, dh = q.shape[-2:]
+    bh = q.numel() // (seq * dh) if q.numel() else 0
+    o = torch.empty_like(q)
+    lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=q.device) if with_lse else None
+    L.call("chelis_cuda_attention_causal_fwd", bh, seq, dh, float(scale), q.data_ptr(),
+           k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if with_lse else None)
+    return (o, lse) if with_lse else o
+
+
 # ---------------------------------------------------------------- rows
 
 def row_sum(x: torch.Tensor) -> torch.Tensor:

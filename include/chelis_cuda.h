@@ -234,6 +234,17 @@ int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t b
                                       int b_layout, const float *b_hi, const float *b_lo,
                                       float *c, int64_t ldc, int64_t stride_c);
 
+/* [05-OP-30..33] causal softmax attention per head, the block's attention
+ * step (spec 05 section 4.7): o = softmax(where(causal, (q.k^T)*scale,
+ * -inf)) . v for bh independent heads, q, k, v, o f32 [bh][seq][dh]
+ * contiguous, lse [bh][seq] (optional, may be NULL) = max + log(sum) of each
+ * row's scaled scores.  The reference materialises the [seq, seq] scores
+ * (tier2.rs attention lowering); this keeps them in tensor memory.  Head dims
+ * 32 and 64 (else CHELIS_CUDA_ERR_UNSUPPORTED). */
+int chelis_cuda_attention_causal_fwd(int64_t bh, int64_t seq, int64_t dh, float scale,
+                                     const float *q, const float *k, const float *v, float *o,
+                                     float *lse);
+
 /* =========================================================================
  * Fused elementwise / reduction groups and their adjoints.
  * The reference JIT-compiles per-DAG kernel strings (kernels.rs:2175-2468,
