@@ -18,8 +18,10 @@
 // straight from tensor memory, the keys and values the B operand from
 // shared memory (TMA, 128-byte swizzle).
 //
-// Roles (192 threads): warp 0 loads key/value blocks with TMA, warp 1 issues
-// the MMAs, warps 2-5 own one query row per thread (TMEM lane = row).
+// Roles (384 threads): warps 0 / 11 load key / value blocks with TMA, warp 1
+// issues the score MMAs and warp 10 the output MMAs (independent streams, so
+// neither waits behind the other), warps 2-9 own the query rows (two
+// threads per TMEM lane, each half of the columns).
 // Every wait is bounded; a timeout sets the device error word and the CTA
 // winds down.
 #include <cuda.h>
@@ -37,7 +39,7 @@ namespace attn {
 
 constexpr int BQ = 128;      // query rows per CTA (TMEM lanes)
 constexpr int BKV = 64;      // keys per block
-constexpr int THREADS = 192;
+constexpr int THREADS = 384;  // 0 key TMA, 1 score MMA, 2-9 rows, 10 output MMA, 11 value TMA
 constexpr int MN_BOX_BYTES = 32 * 32 * 4;  // MN-major TMA box 32 x 32 f32
 
 template <int DH>
@@ -49,7 +51,7 @@ struct Fwd {
     static constexpr int STAGE = 2 * K_TILE + 2 * V_TILE;
     static constexpr int STAGES = 2;
     // at least ~116 KiB so that one CTA (holding all 512 TMEM columns) runs per SM
-    static constexpr int SMEM_USED = STAGES * STAGE + 1024 + 512;
+    static constexpr int SMEM_USED = STAGES * STAGE + 1024 + 256 + 10 * BQ * 4;
     static constexpr int SMEM = SMEM_USED > 118784 ? SMEM_USED : 118784;
     // tensor-memory columns
     static constexpr uint32_t C_QHI = 0, C_QLO = DH;
@@ -71,15 +73,52 @@ struct FwdParams {
     int n_qblocks;
 };
 
-__device__ __forceinline__ float rna_tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
+// Round a finite f32 to the nearest tf32 (ties away from zero), the value
+// cvt.rna.tf32.f32 gives, with two integer ops instead of a conversion-pipe
+// instruction: add half an ulp of the 10-bit mantissa to the magnitude bits
+// and clear the 13 dropped bits (a carry into the exponent is the correct
+// rounding up).
+__device__ __forceinline__ uint32_t rna_tf32_bits(uint32_t b) { return (b + 0x1000u) & 0xFFFFE000u; }
+// hi = RN_tf32(x), lo = RN_tf32(x - hi) (x - hi is exact); non-finite x
+// passes through as hi with lo = 0.
 __device__ __forceinline__ void split_tf32(float x, uint32_t &hi, uint32_t &lo) {
-    const float h = rna_tf32(x);
-    hi = __float_as_uint(h);
-    lo = __float_as_uint(isfinite(x) ? rna_tf32(__fsub_rn(x, h)) : 0.0f);
+    if (isfinite(x)) {
+        hi = rna_tf32_bits(__float_as_uint(x));
+        lo = rna_tf32_bits(__float_as_uint(__fsub_rn(x, __uint_as_float(hi))));
+    } else {
+        hi = __float_as_uint(x);
+        lo = 0u;
+    }
+}
+
+// 2^x (MUFU), flushing subnormal results; x <= 0 here, ex2(-inf) = +0
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// acc = acc * alpha + O, O the OH accumulator columns at `taddr`
+template <int OH>
+__device__ __forceinline__ void fold_o(float (&acc)[OH], uint32_t taddr, float alpha) {
+    if constexpr (OH >= 32) {
+#pragma unroll
+        for (int c = 0; c < OH / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(taddr + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(acc[c * 32 + i], alpha, __uint_as_float(ov[i]));
+        }
+    } else {
+        uint32_t ov[16];
+        tmem_ld_32x32b_x16(taddr, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(acc[i], alpha, __uint_as_float(ov[i]));
+    }
 }
 
 // K-major 128-byte-swizzle operand (rows x 32-float chunks), K-step kk of 8
@@ -113,7 +152,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE);
     uint64_t *k_full = bars;          // [2]
     uint64_t *v_full = bars + 2;      // [2]
-    uint64_t *kv_empty = bars + 4;    // [2]
+    uint64_t *k_empty = bars + 4;     // [2]
     uint64_t *s_full = bars + 6;      // [2]
     uint64_t *s_free = bars + 8;      // [2]
     uint64_t *o_full = bars + 10;     // [2]
@@ -121,11 +160,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *p_full = bars + 14;
     uint64_t *p_free = bars + 15;
     uint64_t *q_ready = bars + 16;
-    uint64_t *mma_done = bars + 17;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 18);
+    uint64_t *s_done = bars + 17;
+    uint64_t *v_empty = bars + 18;    // [2]
+    uint64_t *pv_done = bars + 20;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 21);
     volatile uint32_t *abort_flag = tmem_slot + 1;
     volatile int32_t *k_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
     volatile int32_t *v_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 3);
+    float *red = reinterpret_cast<float *>(tmem_slot + 8);  // [6][BQ] row-half maxima / sums
+    volatile int *stop = reinterpret_cast<volatile int *>(red + 6 * BQ);  // [4][BQ] stop flags
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -139,16 +182,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&v_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
+            mbar_init(&s_free[i], 8);
             mbar_init(&o_full[i], 1);
-            mbar_init(&o_free[i], 4);
+            mbar_init(&o_free[i], 8);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, 8);
         mbar_init(p_free, 1);
-        mbar_init(q_ready, 4);
-        mbar_init(mma_done, 1);
+        mbar_init(q_ready, 8);
+        mbar_init(s_done, 1);
+        mbar_init(pv_done, 1);
         *abort_flag = 0;
         *k_used = 0;
         *v_used = 0;
@@ -170,110 +215,130 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tm = *tmem_slot;
     int32_t issued = 0;
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
+    if (warp == 0 || warp == 11) {
+        // ---------------- TMA producers: warp 0 keys, warp 11 values ----------------
         if (lane == 0) {
+            const bool keys = warp == 0;
+            uint64_t *full = keys ? k_full : v_full;
+            uint64_t *empty = keys ? k_empty : v_empty;
             for (int j = 0; j < nkb; ++j) {
                 const int s = j & 1;
                 if (*abort_flag ||
-                    !mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
+                    !mbar_wait_bounded(&empty[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
                     *abort_flag = 1;
                     break;
                 }
                 unsigned char *st = smem + s * C::STAGE;
-                mbar_arrive_expect_tx(&k_full[s], 2 * C::K_TILE);
+                if (keys) {
+                    mbar_arrive_expect_tx(&full[s], 2 * C::K_TILE);
 #pragma unroll
-                for (int c = 0; c < C::KCH; ++c) {
-                    tma_load_3d(st + c * BKV * 128, &map_khi, &k_full[s], c * 32, j * BKV, bh);
-                    tma_load_3d(st + C::K_TILE + c * BKV * 128, &map_klo, &k_full[s], c * 32,
-                                j * BKV, bh);
-                }
-                unsigned char *sv = st + 2 * C::K_TILE;
-                mbar_arrive_expect_tx(&v_full[s], 2 * C::V_TILE);
-#pragma unroll
-                for (int kc = 0; kc < BKV / 32; ++kc)
-#pragma unroll
-                    for (int dc = 0; dc < C::KCH; ++dc) {
-                        const int off = (kc * C::KCH + dc) * MN_BOX_BYTES;
-                        tma_load_3d(sv + off, &map_vhi, &v_full[s], dc * 32, j * BKV + kc * 32, bh);
-                        tma_load_3d(sv + C::V_TILE + off, &map_vlo, &v_full[s], dc * 32,
-                                    j * BKV + kc * 32, bh);
+                    for (int c = 0; c < C::KCH; ++c) {
+                        tma_load_3d(st + c * BKV * 128, &map_khi, &full[s], c * 32, j * BKV, bh);
+                        tma_load_3d(st + C::K_TILE + c * BKV * 128, &map_klo, &full[s], c * 32,
+                                    j * BKV, bh);
                     }
+                } else {
+                    unsigned char *sv = st + 2 * C::K_TILE;
+                    mbar_arrive_expect_tx(&full[s], 2 * C::V_TILE);
+#pragma unroll
+                    for (int kc = 0; kc < BKV / 32; ++kc)
+#pragma unroll
+                        for (int dc = 0; dc < C::KCH; ++dc) {
+                            const int off = (kc * C::KCH + dc) * MN_BOX_BYTES;
+                            tma_load_3d(sv + off, &map_vhi, &full[s], dc * 32, j * BKV + kc * 32, bh);
+                            tma_load_3d(sv + C::V_TILE + off, &map_vlo, &full[s], dc * 32,
+                                        j * BKV + kc * 32, bh);
+                        }
+                }
                 issued = j + 1;
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- score MMAs: S_j = Q . K_j^T ----------------
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_tf32(BQ, BKV);
-            constexpr uint32_t idesc_o = idesc_tf32(BQ, DH) | (1u << 16);  // B (values) MN-major
             bool ok = mbar_wait_bounded(q_ready, 0, DEVERR_TIMEOUT_MMA);
             if (!ok) *abort_flag = 1;
-            for (int j = 0; ok && j <= nkb; ++j) {
-                if (j < nkb) {
-                    const int s = j & 1;
-                    if (*abort_flag ||
-                        !mbar_wait_bounded(&k_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
-                        !mbar_wait_bounded(&s_free[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
-                        *abort_flag = 1;
-                        break;
-                    }
-                    *k_used = j + 1;
-                    tc_fence_after();
-                    const uint32_t kt = smem_u32(smem + s * C::STAGE);
-                    const uint32_t d = tm + (s ? C::C_S1 : C::C_S0);
-#pragma unroll
-                    for (int kk = 0; kk < DH / 8; ++kk) {
-                        const uint64_t bhi = kmajor_desc(kt, BKV, kk);
-                        const uint64_t blo = kmajor_desc(kt + C::K_TILE, BKV, kk);
-                        mma_tf32_ts(d, tm + C::C_QLO + 8 * kk, bhi, idesc_s, kk ? 1u : 0u);
-                        mma_tf32_ts(d, tm + C::C_QHI + 8 * kk, blo, idesc_s, 1u);
-                        mma_tf32_ts(d, tm + C::C_QHI + 8 * kk, bhi, idesc_s, 1u);
-                    }
-                    mma_commit(&s_full[s]);
+            for (int j = 0; ok && j < nkb; ++j) {
+                const int s = j & 1;
+                if (*abort_flag || !mbar_wait_bounded(&k_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
+                    !mbar_wait_bounded(&s_free[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
+                    *abort_flag = 1;
+                    break;
                 }
-                if (j >= 1) {
-                    const int jj = j - 1, s = jj & 1;
-                    if (*abort_flag || !mbar_wait_bounded(p_full, jj & 1, DEVERR_TIMEOUT_MMA) ||
-                        !mbar_wait_bounded(&v_full[s], (jj >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
-                        !mbar_wait_bounded(&o_free[s], ((jj >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
-                        *abort_flag = 1;
-                        break;
-                    }
-                    *v_used = jj + 1;
-                    tc_fence_after();
-                    const uint32_t vt = smem_u32(smem + s * C::STAGE + 2 * C::K_TILE);
-                    const uint32_t d = tm + (s ? C::C_O1 : C::C_O0);
+                *k_used = j + 1;
+                tc_fence_after();
+                const uint32_t kt = smem_u32(smem + s * C::STAGE);
+                const uint32_t d = tm + (s ? C::C_S1 : C::C_S0);
 #pragma unroll
-                    for (int kk = 0; kk < BKV / 8; ++kk) {
-                        const uint64_t bhi = mnmajor_desc(vt, C::KCH, kk);
-                        const uint64_t blo = mnmajor_desc(vt + C::V_TILE, C::KCH, kk);
-                        mma_tf32_ts(d, tm + C::C_PLO + 8 * kk, bhi, idesc_o, kk ? 1u : 0u);
-                        mma_tf32_ts(d, tm + C::C_PHI + 8 * kk, blo, idesc_o, 1u);
-                        mma_tf32_ts(d, tm + C::C_PHI + 8 * kk, bhi, idesc_o, 1u);
-                    }
-                    mma_commit(&o_full[s]);
-                    mma_commit(p_free);
-                    mma_commit(&kv_empty[s]);
+                for (int kk = 0; kk < DH / 8; ++kk) {
+                    const uint64_t bhi = kmajor_desc(kt, BKV, kk);
+                    const uint64_t blo = kmajor_desc(kt + C::K_TILE, BKV, kk);
+                    mma_tf32_ts(d, tm + C::C_QLO + 8 * kk, bhi, idesc_s, kk ? 1u : 0u);
+                    mma_tf32_ts(d, tm + C::C_QHI + 8 * kk, blo, idesc_s, 1u);
+                    mma_tf32_ts(d, tm + C::C_QHI + 8 * kk, bhi, idesc_s, 1u);
                 }
+                mma_commit(&s_full[s]);
+                mma_commit(&k_empty[s]);
             }
-            // no MMA may still run when tensor memory is released
-            mma_commit(mma_done);
-            mbar_wait_bounded(mma_done, 0, DEVERR_TIMEOUT_MMA);
+            // no MMA of this thread may still run when tensor memory is released
+            mma_commit(s_done);
+            mbar_wait_bounded(s_done, 0, DEVERR_TIMEOUT_MMA);
+        }
+    } else if (warp == 10) {
+        // ---------------- output MMAs: O_j = P_j . V_j ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_o = idesc_tf32(BQ, DH) | (1u << 16);  // B (values) MN-major
+            for (int j = 0; j < nkb; ++j) {
+                const int s = j & 1;
+                if (*abort_flag || !mbar_wait_bounded(p_full, j & 1, DEVERR_TIMEOUT_MMA) ||
+                    !mbar_wait_bounded(&v_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
+                    !mbar_wait_bounded(&o_free[s], ((j >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                *v_used = j + 1;
+                tc_fence_after();
+                const uint32_t vt = smem_u32(smem + s * C::STAGE + 2 * C::K_TILE);
+                const uint32_t d = tm + (s ? C::C_O1 : C::C_O0);
+#pragma unroll
+                for (int kk = 0; kk < BKV / 8; ++kk) {
+                    const uint64_t bhi = mnmajor_desc(vt, C::KCH, kk);
+                    const uint64_t blo = mnmajor_desc(vt + C::V_TILE, C::KCH, kk);
+                    mma_tf32_ts(d, tm + C::C_PLO + 8 * kk, bhi, idesc_o, kk ? 1u : 0u);
+                    mma_tf32_ts(d, tm + C::C_PHI + 8 * kk, blo, idesc_o, 1u);
+                    mma_tf32_ts(d, tm + C::C_PHI + 8 * kk, bhi, idesc_o, 1u);
+                }
+                mma_commit(&o_full[s]);
+                mma_commit(p_free);
+                mma_commit(&v_empty[s]);
+            }
+            mma_commit(pv_done);
+            mbar_wait_bounded(pv_done, 0, DEVERR_TIMEOUT_MMA);
         }
     } else {
-        // ---------------- rows: one query row per thread ----------------
+        // ---------------- rows: 8 warps, two per TMEM lane quadrant ----------------
+        // Thread (half, r) owns query row r = quad * 32 + lane and columns
+        // [half * 32, half * 32 + 32) of each score block and
+        // [half * DH / 2, (half + 1) * DH / 2) of the output.  The two halves
+        // of a row exchange their block maxima through shared memory; their
+        // partial row sums combine once at the end.
         const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int qrow = q0 + r;
         const bool live = qrow < p.seq;
         const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
         const int b = bh / p.heads, h = bh % p.heads;
-        // query row -> hi / lo in tensor memory
+        constexpr int OH = DH / 2;  // output columns per thread
+        // scores are kept in the base-2 domain: x = s * scale * log2(e)
+        const float c2 = __fmul_rn(p.scale, 1.4426950408889634f);
+        // query row half -> hi / lo in tensor memory
         {
-            const float *qr = p.q + b * p.q_b + h * p.q_h + static_cast<int64_t>(qrow) * p.q_row;
+            const float *qr = p.q + b * p.q_b + h * p.q_h + static_cast<int64_t>(qrow) * p.q_row +
+                              half * OH;
 #pragma unroll
-            for (int c = 0; c < C::KCH; ++c) {
+            for (int c = 0; c < OH / 32; ++c) {  // DH = 64: one 32-column chunk per half
                 uint32_t hi[32], lo[32];
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
@@ -284,8 +349,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                     split_tf32(v.z, hi[i + 2], lo[i + 2]);
                     split_tf32(v.w, hi[i + 3], lo[i + 3]);
                 }
-                tmem_st_32x32b_x32(tm + lane_base + C::C_QHI + c * 32, hi);
-                tmem_st_32x32b_x32(tm + lane_base + C::C_QLO + c * 32, lo);
+                tmem_st_32x32b_x32(tm + lane_base + C::C_QHI + half * OH + c * 32, hi);
+                tmem_st_32x32b_x32(tm + lane_base + C::C_QLO + half * OH + c * 32, lo);
+            }
+            if constexpr (OH < 32) {
+                // DH = 32: 16 columns per half
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int i = 0; i < 16; i += 4) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (live) v = *reinterpret_cast<const float4 *>(qr + i);
+                    split_tf32(v.x, hi[i], lo[i]);
+                    split_tf32(v.y, hi[i + 1], lo[i + 1]);
+                    split_tf32(v.z, hi[i + 2], lo[i + 2]);
+                    split_tf32(v.w, hi[i + 3], lo[i + 3]);
+                }
+                tmem_st_32x32b_x16(tm + lane_base + C::C_QHI + half * OH, hi);
+                tmem_st_32x32b_x16(tm + lane_base + C::C_QLO + half * OH, lo);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -293,114 +373,117 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) mbar_arrive(q_ready);
         }
         float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
-        float acc[DH];
+        float acc[OH];
 #pragma unroll
-        for (int i = 0; i < DH; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < OH; ++i) acc[i] = 0.0f;
         bool ok = true;
+        // The two halves of a row pass the exchange barrier below the same
+        // number of times: a failed wait only clears `ok`, and the loop ends
+        // at the exchange when either half has stopped.
         for (int j = 0; j < nkb; ++j) {
             const int s = j & 1;
-            if (*abort_flag || !mbar_wait_bounded(&s_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+            if (ok && (*abort_flag ||
+                       !mbar_wait_bounded(&s_full[s], (j >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE))) {
                 *abort_flag = 1;
                 ok = false;
-                break;
             }
-            tc_fence_after();
-            uint32_t sr[BKV];
-            tmem_ld_32x32b_x32(tm + lane_base + (s ? C::C_S1 : C::C_S0),
-                               *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-            tmem_ld_32x32b_x32(tm + lane_base + (s ? C::C_S1 : C::C_S0) + 32,
-                               *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[s]);
-            // scale, causal mask, running maximum
-            const int key0 = j * BKV;
+            uint32_t sr[32];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld_32x32b_x32(tm + lane_base + (s ? C::C_S1 : C::C_S0) + half * 32, sr);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[s]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) sr[c] = 0u;
+            }
+            // scale into the base-2 domain, causal mask, running maximum
+            const int key0 = j * BKV + half * 32;
+            const bool full_block = key0 + 31 <= q0 && key0 + 31 < p.seq;
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BKV; ++c) {
+            for (int c = 0; c < 32; ++c) {
                 const int key = key0 + c;
-                const float x = (key <= qrow && key < p.seq)
-                                    ? __fmul_rn(__uint_as_float(sr[c]), p.scale)
-                                    : -INFINITY;
+                float x = __fmul_rn(__uint_as_float(sr[c]), c2);
+                if (!full_block && !(key <= qrow && key < p.seq)) x = -INFINITY;
                 sr[c] = __float_as_uint(x);
                 mx = fmaxf(mx, x);
             }
-            const float m_new = fmaxf(m, mx);
-            const float alpha = __expf(__fsub_rn(m, m_new));
-            // probabilities -> tensor memory once the previous block's P . V is done
-            if (j >= 1 && (*abort_flag || !mbar_wait_bounded(p_free, (j - 1) & 1, DEVERR_TIMEOUT_EPILOGUE))) {
-                *abort_flag = 1;
+            const int slot = (j & 1) * 2;
+            red[(slot + half) * BQ + r] = mx;
+            stop[(slot + half) * BQ + r] = (!ok || *abort_flag) ? 1 : 0;
+            named_bar_sync(1 + quad, 64);
+            if (stop[(slot + half) * BQ + r] | stop[(slot + (half ^ 1)) * BQ + r]) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            float rs = 0.0f;
-#pragma unroll
-            for (int h32 = 0; h32 < BKV / 32; ++h32) {
+            mx = fmaxf(mx, red[(slot + (half ^ 1)) * BQ + r]);
+            const float m_new = fmaxf(m, mx);
+            const float alpha = ex2_approx(__fsub_rn(m, m_new));
+            // probabilities -> tensor memory once the previous block's P . V is done
+            if (j >= 1 && !mbar_wait_bounded(p_free, (j - 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+                *abort_flag = 1;
+                ok = false;
+            }
+            if (ok) {
+                tc_fence_after();
+                float rs = 0.0f;
                 uint32_t phi[32], plo[32];
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
-                    const float e = __expf(__fsub_rn(__uint_as_float(sr[h32 * 32 + c]), m_new));
+                    // e in [0, 1]: finite, so the split needs no special cases
+                    const float e = ex2_approx(__fsub_rn(__uint_as_float(sr[c]), m_new));
                     rs = __fadd_rn(rs, e);
-                    split_tf32(e, phi[c], plo[c]);
+                    phi[c] = rna_tf32_bits(__float_as_uint(e));
+                    plo[c] = rna_tf32_bits(__float_as_uint(__fsub_rn(e, __uint_as_float(phi[c]))));
                 }
-                tmem_st_32x32b_x32(tm + lane_base + C::C_PHI + h32 * 32, phi);
-                tmem_st_32x32b_x32(tm + lane_base + C::C_PLO + h32 * 32, plo);
-            }
-            l = __fadd_rn(__fmul_rn(l, alpha), rs);
-            m = m_new;
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            // fold in the previous block's P . V
-            if (j >= 1) {
-                const int jj = j - 1, so = jj & 1;
-                if (*abort_flag || !mbar_wait_bounded(&o_full[so], (jj >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
-                    *abort_flag = 1;
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < C::KCH; ++c) {
-                    uint32_t ov[32];
-                    tmem_ld_32x32b_x32(tm + lane_base + (so ? C::C_O1 : C::C_O0) + c * 32, ov);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        acc[c * 32 + i] = __fadd_rn(__fmul_rn(acc[c * 32 + i], alpha_prev),
-                                                    __uint_as_float(ov[i]));
-                }
+                tmem_st_32x32b_x32(tm + lane_base + C::C_PHI + half * 32, phi);
+                tmem_st_32x32b_x32(tm + lane_base + C::C_PLO + half * 32, plo);
+                l = fmaf(l, alpha, rs);
+                m = m_new;
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&o_free[so]);
+                if (lane == 0) mbar_arrive(p_full);
+            }
+            // fold in the previous block's P . V
+            if (ok && j >= 1) {
+                const int jj = j - 1, so = jj & 1;
+                if (!mbar_wait_bounded(&o_full[so], (jj >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+                    *abort_flag = 1;
+                    ok = false;
+                } else {
+                    tc_fence_after();
+                    fold_o<OH>(acc, tm + lane_base + (so ? C::C_O1 : C::C_O0) + half * OH, alpha_prev);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&o_free[so]);
+                }
             }
             alpha_prev = alpha;
         }
+        // partial row sums of the two halves
+        red[(4 + half) * BQ + r] = l;
+        named_bar_sync(1 + quad, 64);
+        l = __fadd_rn(red[(4 + half) * BQ + r], red[(4 + (half ^ 1)) * BQ + r]);
         if (ok) {
             const int jj = nkb - 1, so = jj & 1;
             if (!*abort_flag && mbar_wait_bounded(&o_full[so], (jj >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
                 tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < C::KCH; ++c) {
-                    uint32_t ov[32];
-                    tmem_ld_32x32b_x32(tm + lane_base + (so ? C::C_O1 : C::C_O0) + c * 32, ov);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        acc[c * 32 + i] = __fadd_rn(__fmul_rn(acc[c * 32 + i], alpha_prev),
-                                                    __uint_as_float(ov[i]));
-                }
+                fold_o<OH>(acc, tm + lane_base + (so ? C::C_O1 : C::C_O0) + half * OH, alpha_prev);
                 if (live) {
-                    float *orow = p.o + b * p.o_b + h * p.o_h + static_cast<int64_t>(qrow) * p.o_row;
+                    float *orow = p.o + b * p.o_b + h * p.o_h + static_cast<int64_t>(qrow) * p.o_row +
+                                  half * OH;
 #pragma unroll
-                    for (int i = 0; i < DH; i += 4)
+                    for (int i = 0; i < OH; i += 4)
                         *reinterpret_cast<float4 *>(orow + i) =
                             make_float4(__fdiv_rn(acc[i], l), __fdiv_rn(acc[i + 1], l),
                                         __fdiv_rn(acc[i + 2], l), __fdiv_rn(acc[i + 3], l));
-                    if (p.lse) p.lse[static_cast<int64_t>(bh) * p.seq + qrow] = __fadd_rn(m, logf(l));
+                    if (p.lse && half == 0)
+                        p.lse[static_cast<int64_t>(bh) * p.seq + qrow] =
+                            __fadd_rn(__fmul_rn(m, 0.6931471805599453f), logf(l));
                 }
             } else {
                 *abort_flag = 1;
@@ -410,12 +493,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 0 && lane == 0 && *abort_flag) {
+    if ((warp == 0 || warp == 11) && lane == 0 && *abort_flag) {
         // let issued key / value loads land before the CTA retires
-        for (int j = *k_used; j < issued; ++j)
-            mbar_wait_bounded(&k_full[j & 1], (j >> 1) & 1, DEVERR_TIMEOUT_PRODUCER);
-        for (int j = *v_used; j < issued; ++j)
-            mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1, DEVERR_TIMEOUT_PRODUCER);
+        uint64_t *full = warp == 0 ? k_full : v_full;
+        for (int j = warp == 0 ? *k_used : *v_used; j < issued; ++j)
+            mbar_wait_bounded(&full[j & 1], (j >> 1) & 1, DEVERR_TIMEOUT_PRODUCER);
     }
     __syncthreads();
     if (warp == 1) {
