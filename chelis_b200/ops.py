@@ -164,6 +164,18 @@ def attention_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: f
     return (o, lse) if with_lse else o
 
 
+def attention_causal_bwd(q, k, v, o, lse, dout, scale: float):
+    """(dq, dk, dv) of attention_causal given its output o and lse."""
+    _prepare(q, k, v, o, lse, dout)
+    seq, dh = q.shape[-2:]
+    bh = q.numel() // (seq * dh) if q.numel() else 0
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    L.call("chelis_cuda_attention_causal_bwd", bh, seq, dh, float(scale), q.data_ptr(),
+           k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), dout.data_ptr(),
+           dq.data_ptr(), dk.data_ptr(), dv.data_ptr())
+    return dq, dk, dv
+
+
 # ---------------------------------------------------------------- rows
 
 def row_sum(x: torch.Tensor) -> torch.Tensor:

@@ -244,6 +244,14 @@ int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k, int64_t b
 int chelis_cuda_attention_causal_fwd(int64_t bh, int64_t seq, int64_t dh, float scale,
                                      const float *q, const float *k, const float *v, float *o,
                                      float *lse);
+/* Reverse mode of the same: given o and lse from the forward and the
+ * cotangent dout ([bh][seq][dh]), dq, dk, dv ([bh][seq][dh]).  The reference
+ * differentiates the materialised graph (grad.rs softmax / matmul adjoints);
+ * this recomputes the scores blockwise from lse (no [seq, seq] tensor). */
+int chelis_cuda_attention_causal_bwd(int64_t bh, int64_t seq, int64_t dh, float scale,
+                                     const float *q, const float *k, const float *v,
+                                     const float *o, const float *lse, const float *dout,
+                                     float *dq, float *dk, float *dv);
 
 /* =========================================================================
  * Fused elementwise / reduction groups and their adjoints.
