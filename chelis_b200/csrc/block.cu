@@ -13,8 +13,11 @@
 // the matmul adjoint is a matmul with a transposed operand, [05-OP-51]).
 //
 // Every matmul runs on the tcgen05 3xTF32 kernel (chelis_cuda_sgemm); the
-// row work runs on the kernels below.  Attention is materialised per head
-// ([B*H, S, S] scores), the unfused form of the reference graph.
+// row work runs on the kernels below.  Attention runs on the fused kernels
+// of attention.cu (scores kept in tensor memory, reverse mode recomputed
+// from the saved log-sum-exp) for head dims 32 and 64 in the FAST rows
+// mode; otherwise (EXACT rows mode, other head dims) it is materialised per
+// head ([B*H, S, S] scores), the unfused form of the reference graph.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -341,6 +344,59 @@ __global__ void qkv_permute_kernel(float *__restrict__ qkv, float *__restrict__ 
     }
 }
 
+// [B, S, 3, H, D] -> q, k, v [B, H, S, D] f32 plus hi / lo (tf32 split) of
+// each, the operand copies the fused attention kernels stream with TMA
+__global__ void qkv_heads_split_kernel(const float *__restrict__ qkv, float *__restrict__ q,
+                                       float *__restrict__ k, float *__restrict__ v,
+                                       float *__restrict__ hl, int64_t act, int b_, int s_, int h_,
+                                       int d4) {
+    const int64_t total = static_cast<int64_t>(b_) * s_ * 3 * h_ * d4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t t = i;
+        const int dd = static_cast<int>(t % d4); t /= d4;
+        const int hh = static_cast<int>(t % h_); t /= h_;
+        const int w = static_cast<int>(t % 3); t /= 3;
+        const int ss = static_cast<int>(t % s_); t /= s_;
+        const int bb = static_cast<int>(t);
+        const int64_t o = ((static_cast<int64_t>(bb) * h_ + hh) * s_ + ss) * d4 + dd;
+        const float4 x = reinterpret_cast<const float4 *>(qkv)[i];
+        reinterpret_cast<float4 *>(w == 0 ? q : w == 1 ? k : v)[o] = x;
+        uint32_t hi[4], lo[4];
+        attn::split_tf32(x.x, hi[0], lo[0]);
+        attn::split_tf32(x.y, hi[1], lo[1]);
+        attn::split_tf32(x.z, hi[2], lo[2]);
+        attn::split_tf32(x.w, hi[3], lo[3]);
+        // hl: [q_hi, q_lo, k_hi, k_lo, v_hi, v_lo], act floats each
+        float *base = hl + 2 * w * act;
+        reinterpret_cast<uint4 *>(base)[o] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        reinterpret_cast<uint4 *>(base + act)[o] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// [B, S, H, D] -> hi / lo in [B, H, S, D]
+__global__ void rows_heads_split_kernel(const float *__restrict__ x, float *__restrict__ hi,
+                                        float *__restrict__ lo, int b_, int s_, int h_, int d4) {
+    const int64_t total = static_cast<int64_t>(b_) * s_ * h_ * d4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t t = i;
+        const int dd = static_cast<int>(t % d4); t /= d4;
+        const int hh = static_cast<int>(t % h_); t /= h_;
+        const int ss = static_cast<int>(t % s_); t /= s_;
+        const int bb = static_cast<int>(t);
+        const int64_t o = ((static_cast<int64_t>(bb) * h_ + hh) * s_ + ss) * d4 + dd;
+        const float4 v = reinterpret_cast<const float4 *>(x)[i];
+        uint32_t h4[4], l4[4];
+        attn::split_tf32(v.x, h4[0], l4[0]);
+        attn::split_tf32(v.y, h4[1], l4[1]);
+        attn::split_tf32(v.z, h4[2], l4[2]);
+        attn::split_tf32(v.w, h4[3], l4[3]);
+        reinterpret_cast<uint4 *>(hi)[o] = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+        reinterpret_cast<uint4 *>(lo)[o] = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+    }
+}
+
 // [B, H, S, D] <-> [B, S, H, D]; dir 0: heads -> rows, 1: rows -> heads
 __global__ void heads_permute_kernel(float *__restrict__ hsd, float *__restrict__ shd, int b_,
                                      int s_, int h_, int d4, int dir) {
@@ -388,9 +444,12 @@ int block_dims(const chelis_block_params *p, BlockDims &d) {
 }
 
 // workspace layout in floats
+// (P, dP: [B*H, S, S] of the materialised attention path, taken from the
+// pool by chelis_cuda_block_step only when that path runs; hl: hi / lo
+// copies of q, k, v, dO for the fused path; lse, dsum: [B*H, S].)
 struct Ws {
     float *h1, *qkv, *q, *k, *v, *P, *oh, *o, *x2, *h2, *u, *g, *dg, *dh2, *dx2, *dO, *doh, *dP,
-        *dq, *dk, *dv, *dqkv, *dh1, *part;
+        *dq, *dk, *dv, *dqkv, *dh1, *part, *hl, *lse, *dsum;
     float2 *st1, *st2;
     int64_t total;
 };
@@ -405,12 +464,13 @@ Ws carve(const BlockDims &d, float *base) {
         off += (n + 63) / 64 * 64;
         return p;
     };
-    const int64_t act = d.BS * d.D, big = d.BH * d.S * d.S, ff = d.BS * d.F;
+    const int64_t act = d.BS * d.D, ff = d.BS * d.F;
     w.h1 = take(act); w.qkv = take(3 * act); w.q = take(act); w.k = take(act); w.v = take(act);
-    w.P = take(big); w.oh = take(act); w.o = take(act); w.x2 = take(act); w.h2 = take(act);
+    w.oh = take(act); w.o = take(act); w.x2 = take(act); w.h2 = take(act);
     w.u = take(ff); w.g = take(ff); w.dg = take(ff); w.dh2 = take(act); w.dx2 = take(act);
-    w.dO = take(act); w.doh = take(act); w.dP = take(big); w.dq = take(act); w.dk = take(act);
+    w.dO = take(act); w.doh = take(act); w.dq = take(act); w.dk = take(act);
     w.dv = take(act); w.dqkv = take(3 * act); w.dh1 = take(act);
+    w.hl = take(8 * act); w.lse = take(d.BH * d.S); w.dsum = take(d.BH * d.S);
     w.part = take(2 * static_cast<int64_t>(ln_grid()) * d.D);
     w.st1 = reinterpret_cast<float2 *>(take(2 * d.BS));
     w.st2 = reinterpret_cast<float2 *>(take(2 * d.BS));
@@ -536,32 +596,59 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
     BlockDims d;
     CHELIS_TRY(block_dims(p, d));
     cudaStream_t s = current_stream();
-    void *owned = nullptr;
+    const bool fused = rows_mode() == CHELIS_CUDA_ROWS_FAST && flash_attention_supported(d.Dh);
+    const int64_t big = d.BH * d.S * d.S;
+    void *owned = nullptr, *owned_big = nullptr;
     float *base = static_cast<float *>(workspace);
     if (!base) {
         CHELIS_TRY(scratch_alloc(&owned, carve(d, nullptr).total * sizeof(float), s));
         base = static_cast<float *>(owned);
     }
     Ws w = carve(d, base);
+    if (!fused) {
+        int st0 = scratch_alloc(&owned_big, 2 * big * sizeof(float), s);
+        if (st0 != CHELIS_CUDA_OK) {
+            if (owned) scratch_free(owned, s);
+            return st0;
+        }
+        w.P = static_cast<float *>(owned_big);
+        w.dP = w.P + big;
+    }
     const float scale = 1.0f / sqrtf(static_cast<float>(d.Dh));
-    const int64_t D = d.D, S = d.S, Dh = d.Dh, F = d.F, BS = d.BS, BH = d.BH;
+    const int64_t D = d.D, S = d.S, Dh = d.Dh, F = d.F, BS = d.BS, BH = d.BH, H = d.H;
+    const int64_t act = BS * D;
     const int d4 = static_cast<int>(Dh / 4);
+    // split copies for the fused path: [q_hi, q_lo, k_hi, k_lo, v_hi, v_lo, dO_hi, dO_lo]
+    float *hl = w.hl;
     int st = CHELIS_CUDA_OK;
     do {
         // ---------------- forward ----------------
         if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, w.h1, w.st1, BS, D, s))) break;
         if ((st = mm(0, 0, BS, 3 * D, D, w.h1, D, p->w_qkv, 3 * D, w.qkv, 3 * D))) break;
-        block::qkv_permute_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
-            w.qkv, w.q, w.k, w.v, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 0);
-        g_launches++;
-        if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
-        if ((st = mm(0, 1, S, S, Dh, w.q, Dh, w.k, Dh, w.P, S, BH, S * Dh, S * Dh, S * S))) break;
-        if ((st = softmax_causal(w.P, BH * S, S, scale, s))) break;
-        if ((st = mm(0, 0, S, Dh, S, w.P, S, w.v, Dh, w.oh, Dh, BH, S * S, S * Dh, S * Dh))) break;
-        block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
-            w.oh, w.o, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 0);
-        g_launches++;
-        if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
+        if (fused) {
+            block::qkv_heads_split_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
+                w.qkv, w.q, w.k, w.v, hl, act, static_cast<int>(d.B), static_cast<int>(S),
+                static_cast<int>(H), d4);
+            g_launches++;
+            if ((st = check_cuda(cudaGetLastError(), "qkv_heads_split_kernel"))) break;
+            // o straight into the [B, S, H, Dh] rows layout the projection reads
+            if ((st = flash_fwd(BH, H, S, Dh, scale, w.q, Dh, H * S * Dh, S * Dh, hl + 2 * act,
+                                hl + 3 * act, hl + 4 * act, hl + 5 * act, w.o, D, S * D, Dh, w.lse,
+                                s)))
+                break;
+        } else {
+            block::qkv_permute_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
+                w.qkv, w.q, w.k, w.v, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(H), d4, 0);
+            g_launches++;
+            if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
+            if ((st = mm(0, 1, S, S, Dh, w.q, Dh, w.k, Dh, w.P, S, BH, S * Dh, S * Dh, S * S))) break;
+            if ((st = softmax_causal(w.P, BH * S, S, scale, s))) break;
+            if ((st = mm(0, 0, S, Dh, S, w.P, S, w.v, Dh, w.oh, Dh, BH, S * S, S * Dh, S * Dh))) break;
+            block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
+                w.oh, w.o, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(H), d4, 0);
+            g_launches++;
+            if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
+        }
         if ((st = mm(0, 0, BS, D, D, w.o, D, p->w_o, D, w.x2, D))) break;
         if ((st = add(p->x, w.x2, w.x2, BS * D, s))) break;
         if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) break;
@@ -585,24 +672,39 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
                          p->dln2_beta, BS, D, s))) break;
         if ((st = mm(1, 0, D, D, BS, w.o, D, w.dx2, D, p->dw_o, D))) break;
         if ((st = mm(0, 1, BS, D, D, w.dx2, D, p->w_o, D, w.dO, D))) break;
-        block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
-            w.doh, w.dO, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 1);
-        g_launches++;
-        if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
-        if ((st = mm(0, 1, S, S, Dh, w.doh, Dh, w.v, Dh, w.dP, S, BH, S * Dh, S * Dh, S * S))) break;
-        if ((st = mm(1, 0, S, Dh, S, w.P, S, w.doh, Dh, w.dv, Dh, BH, S * S, S * Dh, S * Dh))) break;
-        if ((st = softmax_bwd_scaled(w.P, w.dP, BH * S, S, scale, s))) break;
-        if ((st = mm(0, 0, S, Dh, S, w.dP, S, w.k, Dh, w.dq, Dh, BH, S * S, S * Dh, S * Dh))) break;
-        if ((st = mm(1, 0, S, Dh, S, w.dP, S, w.q, Dh, w.dk, Dh, BH, S * S, S * Dh, S * Dh))) break;
-        block::qkv_permute_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
-            w.dqkv, w.dq, w.dk, w.dv, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(d.H), d4, 1);
-        g_launches++;
-        if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
+        if (fused) {
+            block::rows_heads_split_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
+                w.dO, hl + 6 * act, hl + 7 * act, static_cast<int>(d.B), static_cast<int>(S),
+                static_cast<int>(H), d4);
+            g_launches++;
+            if ((st = check_cuda(cudaGetLastError(), "rows_heads_split_kernel"))) break;
+            // dq, dk, dv straight into the [B, S, 3, H, Dh] layout of dqkv
+            if ((st = flash_bwd(BH, H, S, Dh, scale, w.q, w.k, w.v, Dh, H * S * Dh, S * Dh, w.dO, D,
+                                S * D, Dh, w.o, D, S * D, Dh, w.lse, hl, hl + act, hl + 2 * act,
+                                hl + 3 * act, hl + 4 * act, hl + 5 * act, hl + 6 * act, hl + 7 * act,
+                                w.dsum, w.dqkv, w.dqkv + D, w.dqkv + 2 * D, 3 * D, S * 3 * D, Dh, s)))
+                break;
+        } else {
+            block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
+                w.doh, w.dO, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(H), d4, 1);
+            g_launches++;
+            if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
+            if ((st = mm(0, 1, S, S, Dh, w.doh, Dh, w.v, Dh, w.dP, S, BH, S * Dh, S * Dh, S * S))) break;
+            if ((st = mm(1, 0, S, Dh, S, w.P, S, w.doh, Dh, w.dv, Dh, BH, S * S, S * Dh, S * Dh))) break;
+            if ((st = softmax_bwd_scaled(w.P, w.dP, BH * S, S, scale, s))) break;
+            if ((st = mm(0, 0, S, Dh, S, w.dP, S, w.k, Dh, w.dq, Dh, BH, S * S, S * Dh, S * Dh))) break;
+            if ((st = mm(1, 0, S, Dh, S, w.dP, S, w.q, Dh, w.dk, Dh, BH, S * S, S * Dh, S * Dh))) break;
+            block::qkv_permute_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
+                w.dqkv, w.dq, w.dk, w.dv, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(H), d4, 1);
+            g_launches++;
+            if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
+        }
         if ((st = mm(1, 0, D, 3 * D, BS, w.h1, D, w.dqkv, 3 * D, p->dw_qkv, 3 * D))) break;
         if ((st = mm(0, 1, BS, D, 3 * D, w.dqkv, 3 * D, p->w_qkv, 3 * D, w.dh1, D))) break;
         if ((st = ln_bwd(p->x, w.dh1, w.st1, p->ln1_gamma, w.dx2, p->dx, w.part, p->dln1_gamma,
                          p->dln1_beta, BS, D, s))) break;
     } while (0);
+    if (owned_big) scratch_free(owned_big, s);
     if (owned) scratch_free(owned, s);
     return st;
 }
