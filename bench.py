@@ -241,7 +241,7 @@ def bench_gemm_headline(args, world, rank, peaks):
         roofline={"bound": "tensor", "achieved": round(pipe, 2), "peak": tf32_peak,
                   "unit": "TFLOP/s", "frac": round(pipe / tf32_peak, 4),
                   "traffic": load_traffic("gemm_tf32x3_8192"),
-                  "kernel": "tf32x3::gemm_kernel (tcgen05.mma kind::tf32, 3 MMAs per product term)",
+                  "kernel": "tf32x3::gemm_pair_kernel (tcgen05.mma cta_group::2 kind::tf32, 3 MMAs per product term)",
                   "kernel_ms": round(kms, 4),
                   "peak_source": f"{peaks['source']} dense bf16 / 2 (tf32 issues at half the f16 rate)"},
         e2e={"value": round(e2e_value, 2), "unit": "TFLOP/s",

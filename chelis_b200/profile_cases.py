@@ -5,6 +5,8 @@
     python -m chelis_b200.profile_cases chain       # config 3 forward (saving state) + adjoint
     python -m chelis_b200.profile_cases portfolio   # config 5, 4096 portfolios
     python -m chelis_b200.profile_cases block       # config 4 step, batch 1
+    python -m chelis_b200.profile_cases attention   # config 4 attention, 8 x 16 heads x 2048 x 64,
+                                                    # fused forward + reverse mode
 
 Each case builds its inputs on the device, runs the hot path once and
 synchronises; inputs exceed the 126 MB L2 except where the case is smaller
@@ -38,6 +40,11 @@ def run(case: str) -> None:
     elif case == "block":
         x, dy, w = W.torch_block_inputs(**dict(W.BLOCK_SHAPE, batch=1))
         ops.block_step(x, w, W.BLOCK_SHAPE["heads"], 1e-5, dy)
+    elif case == "attention":
+        g = torch.Generator(device="cuda").manual_seed(3)
+        q, k, v, do = (torch.randn(128, 2048, 64, device="cuda", generator=g) for _ in range(4))
+        o, lse = ops.attention_causal(q, k, v, 0.125, with_lse=True)
+        ops.attention_causal_bwd(q, k, v, o, lse, do, 0.125)
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
