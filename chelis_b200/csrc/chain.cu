@@ -44,6 +44,13 @@ __device__ __forceinline__ float quad(float a, float b, float c, float d, int cn
     return tree_pair(s01, cnt > 0, s23, cnt > 2);
 }
 
+// Leaves of chunk c this thread holds (4 unless the row ends inside its
+// quad); FULL rows (hidden == NC * 4 * T) need no bounds arithmetic.
+template <bool FULL, int T>
+__device__ __forceinline__ int lanes_left(int n, int c) {
+    return FULL ? 4 : n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x));
+}
+
 // Two reduction scratch areas used alternately: a reduction writes its warp
 // partials into one area, synchronises once and reads them back; the next
 // reduction uses the other area, so no thread can overwrite partials that a
@@ -162,16 +169,16 @@ __device__ __forceinline__ float tree_parts(const float (&part)[NC], int n, Red<
     return chunk[0];
 }
 
-template <int T, int NC>
+template <int T, int NC, bool FULL = false>
 __device__ __forceinline__ float tree4(const float (&v)[NC][4], int n, Red<T, NC> &rs) {
     float part[NC];
 #pragma unroll
     for (int c = 0; c < NC; ++c)
-        part[c] = quad(v[c][0], v[c][1], v[c][2], v[c][3], n - (c * 4 * T + 4 * threadIdx.x));
-    return tree_parts<T, NC>(part, n, rs);
+        part[c] = quad(v[c][0], v[c][1], v[c][2], v[c][3], lanes_left<FULL, T>(n, c));
+    return tree_parts<T, NC>(part, FULL ? NC * 4 * T : n, rs);
 }
 
-template <int T, int NC>
+template <int T, int NC, bool FULL = false>
 __device__ __forceinline__ float row_max(const float (&v)[NC][4], int n, Red<T, NC> &rs) {
     constexpr int W = T / 32;
     float *red = rs.next();
@@ -182,7 +189,7 @@ __device__ __forceinline__ float row_max(const float (&v)[NC][4], int n, Red<T, 
     for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            if (c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n) {
+            if (FULL || c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n) {
                 m = fmaxf(m, v[c][i]);
                 nan |= isnan(v[c][i]);
             }
@@ -257,16 +264,51 @@ __device__ __forceinline__ float at(const float4 &q, int i) {
     return i == 0 ? q.x : i == 1 ? q.y : i == 2 ? q.z : q.w;
 }
 
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`
+// (addresses 16-byte aligned, size a multiple of 16; no multicast)
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Ring of RING row slots in shared memory, each [x row: L floats][keep
+// words][stats: 4 floats], filled by bulk copies that thread 0 issues RING
+// rows ahead, so a CTA's next rows stream in while it works on this one.
+template <int T, int NC>
+struct RowRing {
+    static constexpr int RING = 2;
+    static constexpr int L = NC * 4 * T;
+    static constexpr int WORDS = NC * T / 8;
+    static constexpr int SLOT = L + WORDS + 4;  // floats
+    static constexpr size_t bytes() { return RING * SLOT * sizeof(float) + 2 * RING * sizeof(uint64_t); }
+    float *base;
+    uint64_t *full;
+    __device__ float *slot(int i) const { return base + i * SLOT; }
+    __device__ void issue(int i, const Params &p, int64_t r) const {
+        const int n = p.hidden;
+        const uint32_t xb = static_cast<uint32_t>(n) * 4u;
+        const uint32_t kb = static_cast<uint32_t>(p.words_per_row) * 4u;
+        mbar_arrive_expect_tx(&full[i], xb + kb + 16u);
+        float *d = slot(i);
+        bulk_load(d, p.x + r * n, xb, &full[i]);
+        bulk_load(d + L, p.keep_in + r * p.words_per_row, kb, &full[i]);
+        bulk_load(d + L + WORDS, p.stats_in + 4 * r, 16u, &full[i]);
+    }
+};
+
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
-template <int T, int NC, bool EXACT>
+template <int T, int NC, bool EXACT, bool FULL>
 __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
     extern __shared__ __align__(16) float smem[];
     float *sg = smem;                 // gamma
     float *sb = sg + NC * 4 * T;      // beta
     Red<T, NC> rs{sb + NC * 4 * T};
-    const int n = p.hidden;
+    const int n = FULL ? NC * 4 * T : p.hidden;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
     stage<NC, T>(sg, p.gamma, n);
@@ -296,7 +338,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
                     if (lane == 0) kw[(c * (T / 32) + warp) * 4 + i] = bits;
                 }
         }
-        const float s1 = tree4<T, NC>(v, n, rs);
+        const float s1 = tree4<T, NC, FULL>(v, n, rs);
         const float mean = div_<EXACT>(s1, p.hf, p.rh);
         float part[NC];
 #pragma unroll
@@ -305,7 +347,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
             for (int i = 0; i < 4; ++i) v[c][i] = __fsub_rn(v[c][i], mean);
             part[c] = quad(__fmul_rn(v[c][0], v[c][0]), __fmul_rn(v[c][1], v[c][1]),
                            __fmul_rn(v[c][2], v[c][2]), __fmul_rn(v[c][3], v[c][3]),
-                           n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+                           lanes_left<FULL, T>(n, c));
         }
         const float s2 = tree_parts<T, NC>(part, n, rs);
         const float var = div_<EXACT>(s2, p.hf, p.rh);
@@ -318,12 +360,12 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
             for (int i = 0; i < 4; ++i)
                 v[c][i] = __fadd_rn(__fmul_rn(div_<EXACT>(v[c][i], d, rd), at(g4, i)), at(b4, i));
         }
-        const float mx = row_max<T, NC>(v, n, rs);
+        const float mx = row_max<T, NC, FULL>(v, n, rs);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = exp_<EXACT>(__fsub_rn(v[c][i], mx));
-        const float z = tree4<T, NC>(v, n, rs);
+        const float z = tree4<T, NC, FULL>(v, n, rs);
         const float rz = __fdiv_rn(1.0f, z);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
@@ -332,7 +374,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
                 const float s = div_<EXACT>(v[c][i], z, rz);
                 v[c][i] = ((keepm >> (c * 4 + i)) & 1u) ? div_<EXACT>(s, p.den, p.rden) : 0.0f;
             }
-        const float rsum = tree4<T, NC>(v, n, rs);
+        const float rsum = tree4<T, NC, FULL>(v, n, rs);
         if (threadIdx.x == 0) {
             p.rowsum[r] = canon(rsum);
             if (p.stats)
@@ -344,8 +386,8 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
 // ---------------------------------------------------------------------------
 // adjoint
 // ---------------------------------------------------------------------------
-template <int T, int NC, bool EXACT>
-__global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
+template <int T, int NC, bool EXACT, bool FULL>
+__global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
     extern __shared__ __align__(16) float smem[];
     constexpr int L = NC * 4 * T;
     float *sg = smem;          // gamma
@@ -353,24 +395,66 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
     float *pg = sb + L;        // dgamma partial of this CTA
     float *pb = pg + L;        // dbeta partial of this CTA
     Red<T, NC> rs{pb + L};
-    const int n = p.hidden;
+    const int n = FULL ? NC * 4 * T : p.hidden;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(p.dx) & 15) == 0);
+    // saved-state adjoint: stream x, keep bits and statistics through the ring
+    const bool ring = vec && p.keep_in && p.stats_in &&
+                      ((reinterpret_cast<uintptr_t>(p.keep_in) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(p.stats_in) & 15) == 0);
+    RowRing<T, NC> rr;
+    rr.base = pb + L + 2 * (NC * (T / 32) + 8);
+    rr.full = reinterpret_cast<uint64_t *>(rr.base + RowRing<T, NC>::RING * RowRing<T, NC>::SLOT);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(rr.full + 2 * RowRing<T, NC>::RING);
+    const int64_t r_begin = static_cast<int64_t>(blockIdx.x) * p.rows_per_cta;
+    int64_t r_end = r_begin + p.rows_per_cta;
+    if (r_end > p.rows) r_end = p.rows;
+    if (ring && threadIdx.x == 0) {
+        for (int i = 0; i < RowRing<T, NC>::RING; ++i) mbar_init(&rr.full[i], 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        for (int i = 0; i < RowRing<T, NC>::RING && r_begin + i < r_end; ++i) rr.issue(i, p, r_begin + i);
+    }
     stage<NC, T>(sg, p.gamma, n);
     stage<NC, T>(sb, p.beta, n);
     stage<NC, T>(pg, nullptr, n);
     stage<NC, T>(pb, nullptr, n);
     __syncthreads();
-    const int64_t r_begin = static_cast<int64_t>(blockIdx.x) * p.rows_per_cta;
-    int64_t r_end = r_begin + p.rows_per_cta;
-    if (r_end > p.rows) r_end = p.rows;
+    int64_t issued = r_begin + RowRing<T, NC>::RING;  // next row to stream (thread 0)
+    // this CTA's dgamma / dbeta partials for the columns this thread owns,
+    // summed over its rows in row order (registers: the thread holds the
+    // same columns for every row)
+    float4 acc_g[NC], acc_b[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc_g[c] = acc_b[c] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int64_t r = r_begin; r < r_end; ++r) {
         float c_[NC][4];
-        load4<NC, T>(c_, p.x + r * n, n, vec);
         uint32_t keepm = 0;  // bit (c*4+i): element kept
+        const int li = static_cast<int>(r - r_begin);
+        const float *slot = nullptr;
+        if (ring) {
+            const int si = li % RowRing<T, NC>::RING;
+            if (!mbar_wait_bounded(&rr.full[si], (li / RowRing<T, NC>::RING) & 1, DEVERR_TIMEOUT_PRODUCER))
+                *abort_flag = 1;
+            slot = rr.slot(si);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int e0 = c * 4 * T + 4 * threadIdx.x;
+                if (e0 + 3 < n) {
+                    const float4 q = reinterpret_cast<const float4 *>(slot)[c * T + threadIdx.x];
+                    c_[c][0] = q.x; c_[c][1] = q.y; c_[c][2] = q.z; c_[c][3] = q.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) c_[c][i] = (e0 + i < n) ? slot[e0 + i] : 0.0f;
+                }
+            }
+        } else {
+            load4<NC, T>(c_, p.x + r * n, n, vec);
+        }
         if (p.keep_in) {
-            const uint32_t *kw = p.keep_in + r * p.words_per_row;
+            const uint32_t *kw = ring ? reinterpret_cast<const uint32_t *>(slot + L)
+                                      : p.keep_in + r * p.words_per_row;
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const uint4 w = reinterpret_cast<const uint4 *>(kw)[c * (T / 32) + warp];
@@ -392,10 +476,11 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
         }
         float mean, d, mx, z;
         if (p.stats_in) {
-            const float4 st = *reinterpret_cast<const float4 *>(p.stats_in + 4 * r);
+            const float4 st = ring ? *reinterpret_cast<const float4 *>(slot + L + RowRing<T, NC>::WORDS)
+                                   : *reinterpret_cast<const float4 *>(p.stats_in + 4 * r);
             mean = st.x; d = st.y; mx = st.z; z = st.w;
         } else {
-            mean = div_<EXACT>(tree4<T, NC>(c_, n, rs), p.hf, p.rh);
+            mean = div_<EXACT>(tree4<T, NC, FULL>(c_, n, rs), p.hf, p.rh);
             float part[NC];
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
@@ -405,7 +490,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
                     const float cc = __fsub_rn(c_[c][i], mean);
                     q[i] = __fmul_rn(cc, cc);
                 }
-                part[c] = quad(q[0], q[1], q[2], q[3], n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+                part[c] = quad(q[0], q[1], q[2], q[3], lanes_left<FULL, T>(n, c));
             }
             const float var = div_<EXACT>(tree_parts<T, NC>(part, n, rs), p.hf, p.rh);
             d = __fsqrt_rn(__fadd_rn(var, p.eps));
@@ -418,12 +503,12 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
                 for (int i = 0; i < 4; ++i)
                     y[c][i] = __fadd_rn(__fmul_rn(div_<EXACT>(__fsub_rn(c_[c][i], mean), d, rd0), at(g4, i)), at(b4, i));
             }
-            mx = row_max<T, NC>(y, n, rs);
+            mx = row_max<T, NC, FULL>(y, n, rs);
 #pragma unroll
             for (int c = 0; c < NC; ++c)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) y[c][i] = exp_<EXACT>(__fsub_rn(y[c][i], mx));
-            z = tree4<T, NC>(y, n, rs);
+            z = tree4<T, NC, FULL>(y, n, rs);
         }
         const float rd = __fdiv_rn(1.0f, d);
         const float rz = __fdiv_rn(1.0f, z);
@@ -444,15 +529,24 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
                 s[c][i] = div_<EXACT>(exp_<EXACT>(__fsub_rn(y, mx)), z, rz);
                 gy[i] = ((keepm >> (c * 4 + i)) & 1u) ? __fmul_rn(p.one_over_den, s[c][i]) : 0.0f;
             }
-            part[c] = quad(gy[0], gy[1], gy[2], gy[3], n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+            part[c] = quad(gy[0], gy[1], gy[2], gy[3], lanes_left<FULL, T>(n, c));
         }
         const float q = tree_parts<T, NC>(part, n, rs);
+        if (ring) {
+            // every thread has read its slot (the reduction above synchronised
+            // the CTA): refill it with the row RING ahead
+            if (*abort_flag) break;
+            if (threadIdx.x == 0 && issued < r_end) {
+                rr.issue(li % RowRing<T, NC>::RING, p, issued);
+                ++issued;
+            }
+        }
         // dy = s*(ds - q); dgamma += dy*nn; dbeta += dy; dn = dy*gamma;
         // dt = -((dn*nn)/d)/(2d); s becomes dn
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const float4 g4 = ld4<T>(sg, c);
-            float4 pg4 = ld4<T>(pg, c), pb4 = ld4<T>(pb, c);
+            float4 &pg4 = acc_g[c], &pb4 = acc_b[c];
             float dt[4], dys[4], dyn[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -471,9 +565,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
             pg4.z = __fadd_rn(pg4.z, dyn[2]); pg4.w = __fadd_rn(pg4.w, dyn[3]);
             pb4.x = __fadd_rn(pb4.x, dys[0]); pb4.y = __fadd_rn(pb4.y, dys[1]);
             pb4.z = __fadd_rn(pb4.z, dys[2]); pb4.w = __fadd_rn(pb4.w, dys[3]);
-            reinterpret_cast<float4 *>(pg)[c * T + threadIdx.x] = pg4;
-            reinterpret_cast<float4 *>(pb)[c * T + threadIdx.x] = pb4;
-            part[c] = quad(dt[0], dt[1], dt[2], dt[3], n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+            part[c] = quad(dt[0], dt[1], dt[2], dt[3], lanes_left<FULL, T>(n, c));
         }
         const float dvar = tree_parts<T, NC>(part, n, rs);
         const float ds2 = div_<EXACT>(dvar, p.hf, p.rh);
@@ -488,7 +580,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
                 s[c][i] = dc;
                 m4[i] = -dc;
             }
-            part[c] = quad(m4[0], m4[1], m4[2], m4[3], n - (c * 4 * T + 4 * static_cast<int>(threadIdx.x)));
+            part[c] = quad(m4[0], m4[1], m4[2], m4[3], lanes_left<FULL, T>(n, c));
         }
         const float dm = tree_parts<T, NC>(part, n, rs);
         const float ds1 = div_<EXACT>(dm, p.hf, p.rh);
@@ -507,6 +599,19 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) bwd_kernel(Params p) {
                     if (e0 + i < n) dxr[e0 + i] = o[i];
             }
         }
+    }
+    if (ring && threadIdx.x == 0 && *abort_flag) {
+        // bulk copies issued for rows this CTA no longer reads land before it retires
+        for (int64_t r = r_begin; r < issued && r < r_end; ++r) {
+            const int li = static_cast<int>(r - r_begin);
+            mbar_wait_bounded(&rr.full[li % RowRing<T, NC>::RING], (li / RowRing<T, NC>::RING) & 1,
+                              DEVERR_TIMEOUT_PRODUCER);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        reinterpret_cast<float4 *>(pg)[c * T + threadIdx.x] = acc_g[c];
+        reinterpret_cast<float4 *>(pb)[c * T + threadIdx.x] = acc_b[c];
     }
     __syncthreads();
     float *og = p.dgamma_part + static_cast<int64_t>(blockIdx.x) * n;
@@ -586,13 +691,14 @@ int launch_chain_fwd(const ChainParams &p, cudaStream_t s) {
         int64_t g = static_cast<int64_t>(sm_count()) * 3 * 8;
         if (g > p.rows) g = p.rows;
         const unsigned grid = static_cast<unsigned>(g);
-        if (exact) {
-            CHELIS_TRY(set_smem(chain::fwd_kernel<T, NC, true>, smem));
-            chain::fwd_kernel<T, NC, true><<<grid, T, smem, s>>>(p);
-        } else {
-            CHELIS_TRY(set_smem(chain::fwd_kernel<T, NC, false>, smem));
-            chain::fwd_kernel<T, NC, false><<<grid, T, smem, s>>>(p);
-        }
+        const bool full = p.hidden == NC * 4 * T;
+        auto go = [&](auto kern) -> int {
+            CHELIS_TRY(set_smem(kern, smem));
+            kern<<<grid, T, smem, s>>>(p);
+            return CHELIS_CUDA_OK;
+        };
+        if (exact) CHELIS_TRY(full ? go(chain::fwd_kernel<T, NC, true, true>) : go(chain::fwd_kernel<T, NC, true, false>));
+        else CHELIS_TRY(full ? go(chain::fwd_kernel<T, NC, false, true>) : go(chain::fwd_kernel<T, NC, false, false>));
         g_launches++;
         CHELIS_LAUNCH_CHECK("chain::fwd_kernel");
         return CHELIS_CUDA_OK;
@@ -604,14 +710,16 @@ int launch_chain_bwd(const ChainParams &p, int grid, cudaStream_t s) {
     const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
     return with_nc(p.hidden, [&](auto ncv) -> int {
         constexpr int NC = decltype(ncv)::value;
-        const size_t smem = 4 * NC * 4 * T * sizeof(float) + red_bytes<T, NC>();
-        if (exact) {
-            CHELIS_TRY(set_smem(chain::bwd_kernel<T, NC, true>, smem));
-            chain::bwd_kernel<T, NC, true><<<grid, T, smem, s>>>(p);
-        } else {
-            CHELIS_TRY(set_smem(chain::bwd_kernel<T, NC, false>, smem));
-            chain::bwd_kernel<T, NC, false><<<grid, T, smem, s>>>(p);
-        }
+        const size_t smem = 4 * NC * 4 * T * sizeof(float) + red_bytes<T, NC>() +
+                            chain::RowRing<T, NC>::bytes() + 16;
+        const bool full = p.hidden == NC * 4 * T;
+        auto go = [&](auto kern) -> int {
+            CHELIS_TRY(set_smem(kern, smem));
+            kern<<<grid, T, smem, s>>>(p);
+            return CHELIS_CUDA_OK;
+        };
+        if (exact) CHELIS_TRY(full ? go(chain::bwd_kernel<T, NC, true, true>) : go(chain::bwd_kernel<T, NC, true, false>));
+        else CHELIS_TRY(full ? go(chain::bwd_kernel<T, NC, false, true>) : go(chain::bwd_kernel<T, NC, false, false>));
         g_launches++;
         CHELIS_LAUNCH_CHECK("chain::bwd_kernel");
         return CHELIS_CUDA_OK;
@@ -621,7 +729,9 @@ int launch_chain_bwd(const ChainParams &p, int grid, cudaStream_t s) {
 }  // namespace
 
 int chain_bwd_grid(int64_t rows) {
-    int64_t g = static_cast<int64_t>(sm_count()) * 3;
+    // two resident CTAs per SM (shared memory: gamma, beta, two partials and
+    // the row ring), each owning a contiguous run of rows
+    int64_t g = static_cast<int64_t>(sm_count()) * 2;
     return static_cast<int>(rows < g ? (rows < 1 ? 1 : rows) : g);
 }
 
