@@ -166,6 +166,135 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// Row-major fast path: both operands contiguous along their tile rows (A
+// along k, B along n), even extents and leading dimensions, 16-byte aligned
+// bases.  Slabs stream global -> shared memory with cp.async (16-byte
+// chunks, zero-filled past the matrix edge) through a 4-deep ring, so three
+// slabs are in flight while the DMMAs consume the fourth; no registers are
+// spent on staging.  Same tile, swizzle and fragment code as dgemm_kernel.
+// ---------------------------------------------------------------------------
+constexpr int ASTAGES = 4;
+constexpr int ASYNC_SMEM_BYTES = ASTAGES * (BM * BK + BK * BN) * 8;  // 128 KiB
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    dgemm_async_kernel(int64_t m, int64_t n, int64_t k, const double *__restrict__ a, int64_t lda,
+                       int64_t sa_b, const double *__restrict__ b, int64_t ldb, int64_t sb_b,
+                       double *__restrict__ c, int64_t ldc, int64_t sc_b) {
+    extern __shared__ __align__(16) double dsmem[];
+    double *As = dsmem;                          // [ASTAGES][BM * BK]
+    double *Bs = dsmem + ASTAGES * BM * BK;      // [ASTAGES][BK * BN]
+
+    const int64_t bz = blockIdx.z;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+    a += bz * sa_b;
+    b += bz * sb_b;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int wm = warp >> 2, wn = warp & 3;
+    const int g = lane >> 2, t = lane & 3;
+
+    // 16-byte chunks per slab: A 128 rows x 8 chunks, B 16 rows x 64 chunks
+    auto issue = [&](int64_t slab, int buf) {
+        const int64_t k0 = slab * BK;
+        double *as = As + buf * BM * BK;
+        double *bs = Bs + buf * BK * BN;
+#pragma unroll
+        for (int j = 0; j < (BM * BK / 2) / THREADS; ++j) {
+            const int e = tid + j * THREADS;
+            const int r = e >> 3, kk = (e & 7) * 2;
+            const int64_t gr = m0 + r, gk = k0 + kk;
+            const bool ok = gr < m && gk < k;
+            cp_async16(as + a_off(r, kk), ok ? a + gr * lda + gk : a, ok);
+        }
+#pragma unroll
+        for (int j = 0; j < (BK * BN / 2) / THREADS; ++j) {
+            const int e = tid + j * THREADS;
+            const int kk = e >> 6, nn = (e & 63) * 2;
+            const int64_t gk = k0 + kk, gn = n0 + nn;
+            const bool ok = gk < k && gn < n;
+            cp_async16(bs + b_off(kk, nn), ok ? b + gk * ldb + gn : b, ok);
+        }
+    };
+
+    double acc[4][4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.0;
+
+    const int64_t nslab = (k + BK - 1) / BK;
+#pragma unroll
+    for (int s = 0; s < ASTAGES - 1; ++s) {
+        if (s < nslab) issue(s, s);
+        cp_async_commit();
+    }
+    for (int64_t s = 0; s < nslab; ++s) {
+        cp_async_wait<ASTAGES - 2>();  // slab s has landed (this thread's chunks)
+        __syncthreads();               // ... everyone's; and slab s - 1 is consumed
+        if (s + ASTAGES - 1 < nslab) issue(s + ASTAGES - 1, static_cast<int>((s + ASTAGES - 1) % ASTAGES));
+        cp_async_commit();
+        const int buf = static_cast<int>(s % ASTAGES);
+        const double *Ab = As + buf * BM * BK;
+        const double *Bb = Bs + buf * BK * BN;
+#pragma unroll
+        for (int kk = 0; kk < BK; kk += 4) {
+            double af[4][2], bf[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = wm * 64 + i * 16 + g;
+                af[i][0] = Ab[a_off(r, kk + t)];
+                af[i][1] = Ab[a_off(r + 8, kk + t)];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bf[j] = Bb[b_off(kk + t, wn * 32 + j * 8 + g)];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_16x8x4(acc[i][j], af[i][0], af[i][1], bf[j]);
+        }
+    }
+    cp_async_wait<0>();
+
+    double *cb = c + bz * sc_b;
+    const bool vec = ((ldc & 1) == 0) && ((reinterpret_cast<uintptr_t>(cb) & 15) == 0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t col = n0 + wn * 32 + j * 8 + 2 * t;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int64_t row = m0 + wm * 64 + i * 16 + g + h * 8;
+                if (row >= m) continue;
+                double *dst = cb + row * ldc + col;
+                const double v0 = acc[i][j][2 * h], v1 = acc[i][j][2 * h + 1];
+                if (vec && col + 1 < n) {
+                    *reinterpret_cast<double2 *>(dst) = make_double2(v0, v1);
+                } else {
+                    if (col < n) dst[0] = v0;
+                    if (col + 1 < n) dst[1] = v1;
+                }
+            }
+        }
+    }
+}
+
 }  // namespace dmma
 
 int launch_dgemm_dmma(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
@@ -177,14 +306,24 @@ int launch_dgemm_dmma(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
     dim3 grid(static_cast<unsigned>((n + dmma::BN - 1) / dmma::BN),
               static_cast<unsigned>((m + dmma::BM - 1) / dmma::BM),
               static_cast<unsigned>(batch));
-    static bool attr_set = false;
-    if (!attr_set) {
-        CHELIS_TRY(check_cuda(cudaFuncSetAttribute(dmma::dgemm_kernel,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   dmma::SMEM_BYTES),
-                              "cudaFuncSetAttribute(dgemm_kernel)"));
-        attr_set = true;
+    const bool fast = !trans_a && !trans_b && (k % 2 == 0) && (n % 2 == 0) && (lda % 2 == 0) &&
+                      (ldb % 2 == 0) && (batch == 1 || (stride_a % 2 == 0 && stride_b % 2 == 0)) &&
+                      (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+    if (fast) {
+        static uint64_t done = 0;
+        CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(dmma::dgemm_async_kernel),
+                                    dmma::ASYNC_SMEM_BYTES, &done,
+                                    "cudaFuncSetAttribute(dgemm_async_kernel)"));
+        dmma::dgemm_async_kernel<<<grid, dmma::THREADS, dmma::ASYNC_SMEM_BYTES, s>>>(
+            m, n, k, a, lda, stride_a, b, ldb, stride_b, c, ldc, stride_c);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("dgemm_async_kernel(dmma)");
+        return CHELIS_CUDA_OK;
     }
+    static uint64_t done_sync = 0;
+    CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(dmma::dgemm_kernel), dmma::SMEM_BYTES,
+                                &done_sync, "cudaFuncSetAttribute(dgemm_kernel)"));
     dmma::dgemm_kernel<<<grid, dmma::THREADS, dmma::SMEM_BYTES, s>>>(m, n, k, a, sa_r, sa_k, stride_a, b, sb_k,
                                                        sb_n, stride_b, c, ldc, stride_c);
     g_launches++;
