@@ -619,16 +619,18 @@ struct Dkv {
     static constexpr int O_QK = 0, O_DOK = 2 * T, O_QM = 4 * T, O_DOM = 6 * T;
     static constexpr int STAGE = 8 * T;
     static constexpr int STAGES = 2;
-    static constexpr int SMEM_USED = STAGES * STAGE + 1024 + 256;
+    static constexpr int VT = BQ * DH * 4;          // the CTA's values, hi or lo (32 KiB at DH 64)
+    static constexpr int O_V = STAGES * STAGE;      // values hi, then lo (K-major A operand)
+    static constexpr int SMEM_USED = O_V + 2 * VT + 1024 + 256;
     static constexpr int SMEM = SMEM_USED > 118784 ? SMEM_USED : 118784;
-    // TMEM: K, V (A operands), dK, dV accumulators, then one block's S^T (->
-    // P^T hi), dP^T (-> dS^T hi), P^T lo, dS^T lo
-    static constexpr uint32_t C_KHI = 0, C_KLO = DH, C_VHI = 2 * DH, C_VLO = 3 * DH;
-    static constexpr uint32_t C_DK = 4 * DH, C_DV = 5 * DH;
-    static constexpr uint32_t C_ST = 6 * DH, C_DPT = C_ST + BQ2, C_PLO = C_DPT + BQ2,
-                              C_DSLO = C_PLO + BQ2;
+    // TMEM: K (A operand of S^T), dK and dV of one block, then two score
+    // buffers, each S^T (-> P^T hi), dP^T (-> dS^T hi), P^T lo, dS^T lo
+    static constexpr uint32_t C_KHI = 0, C_KLO = DH, C_DK = 2 * DH, C_DV = 3 * DH;
+    static constexpr uint32_t C_BUF = 4 * DH, BUF = 4 * BQ2;
+    static constexpr uint32_t O_ST = 0, O_DPT = BQ2, O_PLO = 2 * BQ2, O_DSLO = 3 * BQ2;
     static constexpr uint32_t COLS = 512;
-    static_assert(C_DSLO + BQ2 <= COLS, "tensor memory budget");
+    static_assert(C_BUF + 2 * BUF <= COLS, "tensor memory budget");
+    static_assert(SMEM_USED <= 232448, "shared memory budget");
 };
 
 template <int DH>
@@ -637,18 +639,20 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
                const __grid_constant__ CUtensorMap m_dhi, const __grid_constant__ CUtensorMap m_dlo,
                const __grid_constant__ CUtensorMap n_qhi, const __grid_constant__ CUtensorMap n_qlo,
                const __grid_constant__ CUtensorMap n_dhi, const __grid_constant__ CUtensorMap n_dlo,
+               const __grid_constant__ CUtensorMap m_vhi, const __grid_constant__ CUtensorMap m_vlo,
                BwdParams p) {
     using C = Dkv<DH>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE);
-    uint64_t *t_full = bars, *t_empty = bars + 2;  // [2] query tiles
-    uint64_t *kv_ready = bars + 4, *s_full = bars + 5, *p_full = bars + 6, *s_free = bars + 7;
-    uint64_t *acc_done = bars + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::O_V + 2 * C::VT);
+    uint64_t *t_full = bars, *t_empty = bars + 2;   // [2] query tiles
+    uint64_t *s_full = bars + 4, *p_full = bars + 6, *s_free = bars + 8;  // [2] score buffers
+    uint64_t *kv_ready = bars + 10, *v_full = bars + 11, *acc_full = bars + 12, *acc_done = bars + 13;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
     volatile uint32_t *abort_flag = tmem_slot + 1;
     volatile int32_t *t_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
+    volatile int32_t *v_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 3);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -662,14 +666,17 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&t_full[i], 1);
             mbar_init(&t_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 8);
+            mbar_init(&s_free[i], 1);
         }
         mbar_init(kv_ready, 8);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 8);
-        mbar_init(s_free, 1);
+        mbar_init(v_full, 1);
+        mbar_init(acc_full, 1);
         mbar_init(acc_done, 1);
         *abort_flag = 0;
         *t_used = 0;
+        *v_used = 0;
         fence_mbarrier_init();
     }
     if (warp == 1) {
@@ -684,6 +691,13 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
 
     if (warp == 0) {
         if (lane == 0) {
+            // the CTA's values (A operand of dP^T), once
+            mbar_arrive_expect_tx(v_full, 2 * C::VT);
+#pragma unroll
+            for (int c = 0; c < C::KCH; ++c) {
+                tma_load_3d(smem + C::O_V + c * BQ * 128, &m_vhi, v_full, c * 32, k0, bh);
+                tma_load_3d(smem + C::O_V + C::VT + c * BQ * 128, &m_vlo, v_full, c * 32, k0, bh);
+            }
             for (int n = 0; n < nblk; ++n) {
                 const int s = n & 1, q0 = (i0 + n) * BQ2;
                 if (*abort_flag ||
@@ -713,38 +727,55 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_tf32(BQ, BQ2);                 // S^T, dP^T
             constexpr uint32_t idesc_g = idesc_tf32(BQ, DH) | (1u << 16);     // dV, dK (B MN-major)
-            bool ok = mbar_wait_bounded(kv_ready, 0, DEVERR_TIMEOUT_MMA);
+            const uint32_t vt = smem_u32(smem + C::O_V);
+            bool ok = mbar_wait_bounded(kv_ready, 0, DEVERR_TIMEOUT_MMA) &&
+                      mbar_wait_bounded(v_full, 0, DEVERR_TIMEOUT_MMA);
             if (!ok) *abort_flag = 1;
-            for (int n = 0; ok && n < nblk; ++n) {
+            if (ok) *v_used = 1;
+            // scores of block n (S^T = K . Q^T, dP^T = V . dO^T) into buffer n % 2
+            auto scores = [&](int n) -> bool {
                 const int s = n & 1;
                 if (*abort_flag || !mbar_wait_bounded(&t_full[s], (n >> 1) & 1, DEVERR_TIMEOUT_MMA) ||
-                    !mbar_wait_bounded(s_free, (n & 1) ^ 1, DEVERR_TIMEOUT_MMA)) {
-                    *abort_flag = 1;
-                    break;
-                }
+                    !mbar_wait_bounded(&s_free[s], ((n >> 1) & 1) ^ 1, DEVERR_TIMEOUT_MMA))
+                    return false;
                 *t_used = n + 1;
                 tc_fence_after();
                 const uint32_t st = smem_u32(smem + s * C::STAGE);
+                const uint32_t buf = tm + C::C_BUF + s * C::BUF;
 #pragma unroll
                 for (int kk = 0; kk < DH / 8; ++kk) {
                     const uint64_t qh = kmajor_desc(st + C::O_QK, BQ2, kk);
                     const uint64_t ql = kmajor_desc(st + C::O_QK + C::T, BQ2, kk);
                     const uint64_t dh = kmajor_desc(st + C::O_DOK, BQ2, kk);
                     const uint64_t dl = kmajor_desc(st + C::O_DOK + C::T, BQ2, kk);
+                    const uint64_t vh = kmajor_desc(vt, BQ, kk);
+                    const uint64_t vl = kmajor_desc(vt + C::VT, BQ, kk);
                     const uint32_t a = 8 * kk, acc = kk ? 1u : 0u;
-                    mma_tf32_ts(tm + C::C_ST, tm + C::C_KLO + a, qh, idesc_s, acc);
-                    mma_tf32_ts(tm + C::C_ST, tm + C::C_KHI + a, ql, idesc_s, 1u);
-                    mma_tf32_ts(tm + C::C_ST, tm + C::C_KHI + a, qh, idesc_s, 1u);
-                    mma_tf32_ts(tm + C::C_DPT, tm + C::C_VLO + a, dh, idesc_s, acc);
-                    mma_tf32_ts(tm + C::C_DPT, tm + C::C_VHI + a, dl, idesc_s, 1u);
-                    mma_tf32_ts(tm + C::C_DPT, tm + C::C_VHI + a, dh, idesc_s, 1u);
+                    mma_tf32_ts(buf + C::O_ST, tm + C::C_KLO + a, qh, idesc_s, acc);
+                    mma_tf32_ts(buf + C::O_ST, tm + C::C_KHI + a, ql, idesc_s, 1u);
+                    mma_tf32_ts(buf + C::O_ST, tm + C::C_KHI + a, qh, idesc_s, 1u);
+                    mma_tf32_ss(buf + C::O_DPT, vl, dh, idesc_s, acc);
+                    mma_tf32_ss(buf + C::O_DPT, vh, dl, idesc_s, 1u);
+                    mma_tf32_ss(buf + C::O_DPT, vh, dh, idesc_s, 1u);
                 }
-                mma_commit(s_full);
-                if (!mbar_wait_bounded(p_full, n & 1, DEVERR_TIMEOUT_MMA)) {
-                    *abort_flag = 1;
+                mma_commit(&s_full[s]);
+                return true;
+            };
+            if (ok && nblk > 0) ok = scores(0);
+            for (int n = 0; ok && n < nblk; ++n) {
+                const int s = n & 1;
+                // the next block's scores run while the rows work on this one
+                if (n + 1 < nblk && !scores(n + 1)) {
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait_bounded(&p_full[s], (n >> 1) & 1, DEVERR_TIMEOUT_MMA)) {
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t st = smem_u32(smem + s * C::STAGE);
+                const uint32_t buf = tm + C::C_BUF + s * C::BUF;
 #pragma unroll
                 for (int kk = 0; kk < BQ2 / 8; ++kk) {
                     const uint64_t dh = mnmajor_desc(st + C::O_DOM, C::KCH, kk);
@@ -752,16 +783,18 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
                     const uint64_t qh = mnmajor_desc(st + C::O_QM, C::KCH, kk);
                     const uint64_t ql = mnmajor_desc(st + C::O_QM + C::T, C::KCH, kk);
                     const uint32_t a = 8 * kk, acc = kk ? 1u : 0u;  // fresh per block
-                    mma_tf32_ts(tm + C::C_DV, tm + C::C_PLO + a, dh, idesc_g, acc);
-                    mma_tf32_ts(tm + C::C_DV, tm + C::C_ST + a, dl, idesc_g, 1u);
-                    mma_tf32_ts(tm + C::C_DV, tm + C::C_ST + a, dh, idesc_g, 1u);
-                    mma_tf32_ts(tm + C::C_DK, tm + C::C_DSLO + a, qh, idesc_g, acc);
-                    mma_tf32_ts(tm + C::C_DK, tm + C::C_DPT + a, ql, idesc_g, 1u);
-                    mma_tf32_ts(tm + C::C_DK, tm + C::C_DPT + a, qh, idesc_g, 1u);
+                    mma_tf32_ts(tm + C::C_DV, buf + C::O_PLO + a, dh, idesc_g, acc);
+                    mma_tf32_ts(tm + C::C_DV, buf + C::O_ST + a, dl, idesc_g, 1u);
+                    mma_tf32_ts(tm + C::C_DV, buf + C::O_ST + a, dh, idesc_g, 1u);
+                    mma_tf32_ts(tm + C::C_DK, buf + C::O_DSLO + a, qh, idesc_g, acc);
+                    mma_tf32_ts(tm + C::C_DK, buf + C::O_DPT + a, ql, idesc_g, 1u);
+                    mma_tf32_ts(tm + C::C_DK, buf + C::O_DPT + a, qh, idesc_g, 1u);
                 }
-                mma_commit(s_free);
-                mma_commit(&t_empty[s]);
+                mma_commit(acc_full);       // this block's dK, dV ready to fold
+                mma_commit(&s_free[s]);     // score buffer s reusable for block n + 2
+                mma_commit(&t_empty[s]);    // query tiles of stage s reusable
             }
+            if (!ok) *abort_flag = 1;
             mma_commit(acc_done);
             mbar_wait_bounded(acc_done, 0, DEVERR_TIMEOUT_MMA);
         }
@@ -777,9 +810,6 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
         stage_row_split<DH>(p.k + row_off + half * (DH / 2), live,
                             tm + lane_base + C::C_KHI + half * (DH / 2),
                             tm + lane_base + C::C_KLO + half * (DH / 2));
-        stage_row_split<DH>(p.v + row_off + half * (DH / 2), live,
-                            tm + lane_base + C::C_VHI + half * (DH / 2),
-                            tm + lane_base + C::C_VLO + half * (DH / 2));
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -792,15 +822,17 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
         for (int i = 0; i < DH / 2; ++i) dk_acc[i] = dv_acc[i] = 0.0f;
         bool ok = true;
         for (int n = 0; n < nblk; ++n) {
-            if (*abort_flag || !mbar_wait_bounded(s_full, n & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+            const int s = n & 1;
+            const uint32_t buf = tm + lane_base + C::C_BUF + s * C::BUF;
+            if (*abort_flag || !mbar_wait_bounded(&s_full[s], (n >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
                 *abort_flag = 1;
                 ok = false;
                 break;
             }
             tc_fence_after();
             uint32_t sv[16], dv[16];
-            tmem_ld_32x32b_x16(tm + lane_base + C::C_ST + half * 16, sv);
-            tmem_ld_32x32b_x16(tm + lane_base + C::C_DPT + half * 16, dv);
+            tmem_ld_32x32b_x16(buf + C::O_ST + half * 16, sv);
+            tmem_ld_32x32b_x16(buf + C::O_DPT + half * 16, dv);
             tmem_wait_ld();
             const int qb0 = (i0 + n) * BQ2 + half * 16;
             uint32_t ph[16], pl[16], dh[16], dl[16];
@@ -815,17 +847,19 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
                 split_tf32(pr, ph[c], pl[c]);
                 split_tf32(ds, dh[c], dl[c]);
             }
-            tmem_st_32x32b_x16(tm + lane_base + C::C_ST + half * 16, ph);
-            tmem_st_32x32b_x16(tm + lane_base + C::C_PLO + half * 16, pl);
-            tmem_st_32x32b_x16(tm + lane_base + C::C_DPT + half * 16, dh);
-            tmem_st_32x32b_x16(tm + lane_base + C::C_DSLO + half * 16, dl);
+            tmem_st_32x32b_x16(buf + C::O_ST + half * 16, ph);
+            tmem_st_32x32b_x16(buf + C::O_PLO + half * 16, pl);
+            tmem_st_32x32b_x16(buf + C::O_DPT + half * 16, dh);
+            tmem_st_32x32b_x16(buf + C::O_DSLO + half * 16, dl);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[s]);
             // this block's dK, dV contributions -> f32 registers (rounded
-            // additions; the block itself is 12 tensor-core accumulations)
-            if (!mbar_wait_bounded(s_free, n & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+            // additions; the block itself is 12 tensor-core accumulations).
+            // The next block's dK / dV MMAs wait for this thread's next
+            // p_full arrival, so the accumulators are read before reuse.
+            if (!mbar_wait_bounded(acc_full, n & 1, DEVERR_TIMEOUT_EPILOGUE)) {
                 *abort_flag = 1;
                 ok = false;
                 break;
@@ -845,9 +879,11 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 0 && lane == 0 && *abort_flag)
+    if (warp == 0 && lane == 0 && *abort_flag) {
         for (int n = *t_used; n < issued; ++n)
             mbar_wait_bounded(&t_full[n & 1], (n >> 1) & 1, DEVERR_TIMEOUT_PRODUCER);
+        if (!*v_used) mbar_wait_bounded(v_full, 0, DEVERR_TIMEOUT_PRODUCER);
+    }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -1258,12 +1294,15 @@ int flash_bwd(int64_t bh, int64_t heads, int64_t seq, int64_t dh, float scale, c
         CHELIS_TRY(head_map(&nq[1], q_lo, bh, seq, d, 32, true));
         CHELIS_TRY(head_map(&nd[0], do_hi, bh, seq, d, 32, true));
         CHELIS_TRY(head_map(&nd[1], do_lo, bh, seq, d, 32, true));
+        CUtensorMap mvv[2];
+        CHELIS_TRY(head_map(&mvv[0], v_hi, bh, seq, d, attn::BQ, false));
+        CHELIS_TRY(head_map(&mvv[1], v_lo, bh, seq, d, attn::BQ, false));
         auto launch = [&](auto kern, int smem) -> int {
             static uint64_t done[2] = {0, 0};
             CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(kern), smem,
                                         &done[d == 64 ? 1 : 0], "cudaFuncSetAttribute(attn dkv)"));
             kern<<<grid, attn::THREADS_BWD, smem, s>>>(mq[0], mq[1], md[0], md[1], nq[0], nq[1],
-                                                       nd[0], nd[1], p);
+                                                       nd[0], nd[1], mvv[0], mvv[1], p);
             g_launches++;
             CHELIS_LAUNCH_CHECK("attn::dkv_kernel");
             return CHELIS_CUDA_OK;
