@@ -61,6 +61,11 @@ struct Params {
     int64_t a_rows_per_batch, b_rows_per_batch;  // K-major split buffers: rows per batch item
     float *c;
     int64_t ldc, stride_c;
+    // pair kernel split-K: blockIdx.z = batch * splits + split; split s covers
+    // k-blocks [s * kb_per_split, (s + 1) * kb_per_split) and writes its
+    // partial product to part[blockIdx.z] ([m][n], dense) when splits > 1
+    int32_t splits, kb_per_split;
+    float *part;
 };
 
 // Operand layouts in shared memory (both written by TMA):
@@ -363,7 +368,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t m0 = pm * (2 * P_ROWS) + rank * P_ROWS;
     const int64_t n0 = pn * BN;
     const int64_t nb0 = n0 + rank * P_ROWS;  // this CTA's half of the columns (rows of B^T)
-    const int64_t batch = blockIdx.z;
+    const int64_t zz = blockIdx.z;
+    const int split = static_cast<int>(zz % p.splits);
+    const int64_t batch = zz / p.splits;
+    const int kb_lo = split * p.kb_per_split;
+    const int nk = (p.num_kb - kb_lo < p.kb_per_split) ? p.num_kb - kb_lo : p.kb_per_split;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
@@ -398,9 +407,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int32_t ya = static_cast<int32_t>(batch * p.a_rows_per_batch + m0);
             const int32_t yb = static_cast<int32_t>(batch * p.b_rows_per_batch + nb0);
             const int32_t z = static_cast<int32_t>(batch);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % P_STAGES;
-                const uint32_t phase = (kb / P_STAGES) & 1;
+            for (int i = 0; i < nk; ++i) {
+                const int kb = kb_lo + i;
+                const int s = i % P_STAGES;
+                const uint32_t phase = (i / P_STAGES) & 1;
                 if (!mbar_wait_bounded(&empty[s], phase ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
                     *abort_flag = 1;
                     break;
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                        static_cast<int32_t>(nb0), yb, z);
                 load_operand_pair<BMN>(st + 3 * P_TILE_BYTES, &map_blo, bar, kb,
                                        static_cast<int32_t>(nb0), yb, z);
-                issued = kb + 1;
+                issued = i + 1;
             }
         }
     } else if (warp == 1) {
@@ -423,9 +433,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && rank == 0) {
             constexpr uint32_t idesc = idesc_tf32(2 * P_ROWS, BN) | (AMN ? (1u << 15) : 0u) |
                                        (BMN ? (1u << 16) : 0u);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % P_STAGES;
-                const uint32_t phase = (kb / P_STAGES) & 1;
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % P_STAGES;
+                const uint32_t phase = (i / P_STAGES) & 1;
                 if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
                     *abort_flag = 1;
                     break;
@@ -436,7 +446,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t bhi = st + 2 * P_TILE_BYTES, blo = st + 3 * P_TILE_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t acc = (kb | kk) ? 1u : 0u;
+                    const uint32_t acc = (i | kk) ? 1u : 0u;
                     mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(alo, kk),
                                      operand_desc<BMN>(bhi, kk), idesc, acc);
                     mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(ahi, kk),
@@ -445,7 +455,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                      operand_desc<BMN>(bhi, kk), idesc, 1u);
                 }
                 mma_commit_pair(&empty[s], 0x3);
-                *consumed = kb + 1;
+                *consumed = i + 1;
             }
             // both epilogues proceed either way; on abort rank 0 skips its stores
             mma_commit_pair(accum_full, 0x3);
@@ -454,7 +464,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- epilogue (warps 2..5, both CTAs) ----------------
         const bool ok = mbar_wait_bounded(accum_full, 0, DEVERR_TIMEOUT_EPILOGUE);
         tc_fence_after();
-        if (ok && !*abort_flag) store_accumulator(tmem_base, warp, lane, m0, n0, batch, p);
+        if (ok && !*abort_flag) {
+            if (p.splits > 1) {
+                Params q = p;
+                q.c = p.part;
+                q.ldc = p.n;
+                q.stride_c = p.m * p.n;
+                store_accumulator(tmem_base, warp, lane, m0, n0, zz, q);
+            } else {
+                store_accumulator(tmem_base, warp, lane, m0, n0, batch, p);
+            }
+        }
     }
 
     tc_fence_before();
@@ -479,6 +499,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
+// C[b][i][j] = sum over s of part[b * splits + s][i][j], in split order
+__global__ void splitk_reduce_kernel(const float *__restrict__ part, int splits, int64_t m,
+                                     int64_t n, int64_t batch, float *__restrict__ c, int64_t ldc,
+                                     int64_t stride_c) {
+    const int64_t mn = m * n, total = batch * mn;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / mn, e = i % mn, row = e / n, col = e % n;
+        const float *src = part + b * splits * mn + e;
+        float acc = src[0];
+        for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, src[s * mn]);
+        c[b * stride_c + row * ldc + col] = acc;
     }
 }
 
@@ -869,7 +904,7 @@ int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMa
         if (2 * q.pairs_m * q.tiles_n > INT32_MAX)
             return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "matmul tile count beyond 2^31");
         cfg.gridDim = dim3(static_cast<unsigned>(2 * q.pairs_m * q.tiles_n), 1,
-                           static_cast<unsigned>(p.batch));
+                           static_cast<unsigned>(p.batch * p.splits));
         cfg.blockDim = dim3(THREADS);
         cfg.dynamicSmemBytes = P_SMEM_BYTES;
         cfg.stream = s;
@@ -925,12 +960,59 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     p.c = c;
     p.ldc = ldc;
     p.stride_c = stride_c;
-    if (pa.mn) {
-        if (pb.mn) return launch_main<true, true>(mahi, malo, mbhi, mblo, p, pair, s);
-        return launch_main<true, false>(mahi, malo, mbhi, mblo, p, pair, s);
+    p.splits = 1;
+    p.kb_per_split = p.num_kb;
+    p.part = nullptr;
+    // Split-K when the tile grid fills the GPU poorly (long-K weight
+    // gradients, mid-size squares): pick the split count whose CTA total
+    // wastes the fewest SM slots of its last wave (a small penalty per extra
+    // split for the partial traffic), each split keeping >= 4 k-blocks.
+    if (pair) {
+        const int64_t sms = sm_count();
+        const int64_t ctas = 2 * ((m + 2 * P_ROWS - 1) / (2 * P_ROWS)) * ((n + BN - 1) / BN) * batch;
+        if (ctas < 2 * sms && p.num_kb >= 8) {
+            double best = -1.0;
+            int best_s = 1;
+            for (int sp = 1; sp <= 16 && p.num_kb / sp >= 4; ++sp) {
+                const int64_t tot = ctas * sp;
+                const double eff = static_cast<double>(tot) /
+                                   static_cast<double>(((tot + sms - 1) / sms) * sms);
+                const double score = eff - 0.02 * (sp - 1);
+                if (score > best + 1e-9) {
+                    best = score;
+                    best_s = sp;
+                }
+            }
+            if (best_s > 1) {
+                p.kb_per_split = (p.num_kb + best_s - 1) / best_s;
+                p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+            }
+        }
     }
-    if (pb.mn) return launch_main<false, true>(mahi, malo, mbhi, mblo, p, pair, s);
-    return launch_main<false, false>(mahi, malo, mbhi, mblo, p, pair, s);
+    void *part = nullptr;
+    if (p.splits > 1) {
+        CHELIS_TRY(scratch_alloc(&part, static_cast<size_t>(p.splits * batch * m * n) * sizeof(float), s));
+        p.part = static_cast<float *>(part);
+    }
+    int st;
+    if (pa.mn) {
+        if (pb.mn) st = launch_main<true, true>(mahi, malo, mbhi, mblo, p, pair, s);
+        else st = launch_main<true, false>(mahi, malo, mbhi, mblo, p, pair, s);
+    } else {
+        if (pb.mn) st = launch_main<false, true>(mahi, malo, mbhi, mblo, p, pair, s);
+        else st = launch_main<false, false>(mahi, malo, mbhi, mblo, p, pair, s);
+    }
+    if (st == CHELIS_CUDA_OK && p.splits > 1) {
+        int64_t blocks = (batch * m * n + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+        if (blocks > cap) blocks = cap;
+        splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+            p.part, p.splits, m, n, batch, c, ldc, stride_c);
+        g_launches++;
+        st = check_cuda(cudaGetLastError(), "splitk_reduce_kernel");
+    }
+    if (part) scratch_free(part, s);
+    return st;
 }
 
 struct GemmPlan {
