@@ -304,40 +304,51 @@ def bench_extras(args, peaks):
 
 def bench_sharded(args, world, rank, peaks):
     """The configurations that shard across GPUs, at every N (max over ranks):
-    config 4 data-parallel (per-rank batch shard of 8, one NCCL all-reduce of
-    the flat gradient buffer per step), config 5 and the batched GEMM of
-    config 2 along their vmap axis (no collective)."""
+    config 4 data-parallel (one NCCL all-reduce of the flat gradient buffer
+    per step), both as the global batch of 8 split across ranks (strong) and
+    as 8 samples per rank (weak), config 5 and the batched GEMM of config 2
+    along their vmap axis (no collective)."""
     import torch
     from chelis_b200 import dp, ops, workloads as W
     out = {}
-    # config 4: transformer block fwd + VJP, DP over the global batch of 8
     shape = dict(W.BLOCK_SHAPE)
-    a, b = dp.shard(shape["batch"], world, rank)
-    local = dict(shape, batch=b - a)
-    x, dy, w = W.torch_block_inputs(seed=3 + rank, **local)
-    names = list(ops.BLOCK_WEIGHTS)
-    grads = dp.FlatGrads({"d" + k: tuple(w[k].shape) for k in names}, "cuda")
-    res = {"y": torch.empty_like(x), "dx": torch.empty_like(x)}
-    res.update({k: grads[k] for k in grads.views})
-    ws = ops.block_workspace(x, w, shape["heads"])
-
-    def step():
-        ops.block_step(x, w, shape["heads"], 1e-5, dy, workspace=ws, out=res)
-        dp.allreduce_sum(grads.flat, world)
-
-    for _ in range(3):
-        step()
-    steps = 5
-    ms = time_region(step, steps, world) / steps
     S, D, F = shape["seq"], shape["d_model"], shape["d_ff"]
     per_sample = 3 * (2 * S * 3 * D * D + 2 * S * S * D + 2 * S * D * D + 4 * S * D * F)
-    out["block_dp"] = {"samples_per_s": round(shape["batch"] / ms * 1e3, 1),
-                       "ms_per_step": round(ms, 3), "per_rank_batch": b - a,
-                       "tflops": round(shape["batch"] * per_sample / ms / 1e9, 1),
-                       "flop_per_sample": per_sample,
-                       "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1),
-                       "scaling": "strong (global batch 8)"}
-    del x, dy, w, grads, res, ws
+
+    def block_dp(local_batch, global_batch):
+        # config 4: transformer block fwd + VJP on this rank's samples, then one
+        # NCCL all-reduce of the flat gradient buffer
+        local = dict(shape, batch=local_batch)
+        x, dy, w = W.torch_block_inputs(seed=3 + rank, **local)
+        names = list(ops.BLOCK_WEIGHTS)
+        grads = dp.FlatGrads({"d" + k: tuple(w[k].shape) for k in names}, "cuda")
+        res = {"y": torch.empty_like(x), "dx": torch.empty_like(x)}
+        res.update({k: grads[k] for k in grads.views})
+        ws = ops.block_workspace(x, w, shape["heads"])
+
+        def step():
+            ops.block_step(x, w, shape["heads"], 1e-5, dy, workspace=ws, out=res)
+            dp.allreduce_sum(grads.flat, world)
+
+        for _ in range(3):
+            step()
+        steps = 5
+        ms = time_region(step, steps, world) / steps
+        return {"samples_per_s": round(global_batch / ms * 1e3, 1), "ms_per_step": round(ms, 3),
+                "per_rank_batch": local_batch,
+                "tflops": round(global_batch * per_sample / ms / 1e9, 1),
+                "flop_per_sample": per_sample,
+                "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1)}
+
+    # strong: the global batch of 8 split across ranks
+    a, b = dp.shard(shape["batch"], world, rank)
+    out["block_dp"] = dict(block_dp(b - a, shape["batch"]), scaling="strong (global batch 8)")
+    # weak: 8 samples per rank (global batch 8 N)
+    if world == 1:
+        out["block_dp_weak"] = dict(out["block_dp"], scaling="weak (8 samples per rank)")
+    else:
+        out["block_dp_weak"] = dict(block_dp(shape["batch"], shape["batch"] * world),
+                                    scaling="weak (8 samples per rank)")
     # config 5: covariance / risk, 65536 portfolios split across ranks
     cnt = W.PORTFOLIO_SHAPE["count"]
     a, b = dp.shard(cnt, world, rank)
