@@ -294,7 +294,26 @@ def bench_extras(args, peaks):
                         "frac_hbm": round(fbytes / fms / 1e6 / hbm, 3)}
     out["chain_bwd"] = {"gbs": round(bbytes / bms / 1e6, 1), "ms": round(bms, 4),
                         "frac_hbm": round(bbytes / bms / 1e6 / hbm, 3)}
-    del x, g, be, state
+    # the fused groups one at a time on the same [16384, 4096] f32 matrix
+    # (algorithmic bytes: each input read once, each output written once)
+    y = torch.softmax(x, -1)
+    nb = rows * hidden * 4
+    groups = {
+        "layer_norm": (lambda: ops.layer_norm(x, g, be, 1e-5), 2 * nb),
+        "softmax": (lambda: ops.softmax_rows(x), 2 * nb),
+        "softmax_bwd": (lambda: ops.softmax_rows_bwd(y, x), 3 * nb),
+        "row_sum": (lambda: ops.row_sum(x), nb + rows * 4),
+        "col_sum": (lambda: ops.col_sum(x), nb + hidden * 4),
+        "row_max": (lambda: ops.row_max(x), nb + rows * 4),
+        "dropout": (lambda: ops.dropout(x, 42, 0.1), 2 * nb),
+    }
+    fused = {}
+    for name, (fn, nbytes) in groups.items():
+        ms_g = timed(fn, 10)
+        fused[name] = {"ms": round(ms_g, 4), "gbs": round(nbytes / ms_g / 1e6, 1),
+                       "frac_hbm": round(nbytes / ms_g / 1e6 / hbm, 3)}
+    out["fused_groups_16384x4096"] = fused
+    del x, g, be, state, y
     # MLP step
     x, labels, w1, b1, w2, b2 = W.torch_mlp_inputs()
     ms = timed(lambda: ops.mlp_step(x, labels, w1, b1, w2, b2), 20)

@@ -189,9 +189,17 @@ __global__ void __launch_bounds__(T)
     float g[NC][4], b[NC][4];
     load_row<NC, T>(g, gamma, n, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && n % 4 == 0);
     load_row<NC, T>(b, beta, n, (reinterpret_cast<uintptr_t>(beta) & 15) == 0 && n % 4 == 0);
+    // the next row's loads are issued before this row's reductions, so each
+    // CTA keeps two rows in flight
+    float nxt[NC][4];
+    if (blockIdx.x < rows) load_row<NC, T>(nxt, xin + blockIdx.x * static_cast<int64_t>(n), n, vec);
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         float v[NC][4], c2[NC][4];
-        load_row<NC, T>(v, xin + r * n, n, vec);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
+        if (r + gridDim.x < rows) load_row<NC, T>(nxt, xin + (r + gridDim.x) * n, n, vec);
         const float s1 = block_tree<T, NC>(v, n, red);
         const float mean = EXACT ? __fdiv_rn(s1, hf) : __fmul_rn(s1, rh);
 #pragma unroll
@@ -222,9 +230,15 @@ __global__ void __launch_bounds__(T)
     __shared__ float red[NC * (T / 32) + 8];
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(xin) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(yout) & 15) == 0);
+    float nxt[NC][4];
+    if (blockIdx.x < rows) load_row<NC, T>(nxt, xin + blockIdx.x * static_cast<int64_t>(n), n, vec);
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         float v[NC][4];
-        load_row<NC, T>(v, xin + r * n, n, vec);
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
+        if (r + gridDim.x < rows) load_row<NC, T>(nxt, xin + (r + gridDim.x) * n, n, vec);
         const float mx = block_max<T, NC>(v, n, red);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
@@ -263,6 +277,28 @@ __global__ void __launch_bounds__(T)
 #pragma unroll
             for (int i = 0; i < 4; ++i) gy[c][i] = canon(__fmul_rn(y[c][i], __fsub_rn(g[c][i], q)));
         store_row<NC, T>(gy, dx + r * n, n, vec);
+    }
+}
+
+// Row sum of a row that fits one CTA's registers (width <= NC * 4T): the
+// canonical tree of block_tree (the same value as the chunked carry form
+// below), float4 loads, next row prefetched.
+template <int T, int NC>
+__global__ void __launch_bounds__(T)
+    row_sum_nc_kernel(const float *__restrict__ x, int64_t rows, int n, float *__restrict__ out) {
+    __shared__ float red[NC * (T / 32) + 8];
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    float nxt[NC][4];
+    if (blockIdx.x < rows) load_row<NC, T>(nxt, x + blockIdx.x * static_cast<int64_t>(n), n, vec);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float v[NC][4];
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
+        if (r + gridDim.x < rows) load_row<NC, T>(nxt, x + (r + gridDim.x) * n, n, vec);
+        const float s = block_tree<T, NC>(v, n, red);
+        if (threadIdx.x == 0) out[r] = canon(s);
     }
 }
 
@@ -381,6 +417,35 @@ __global__ void col_block_kernel(const float *__restrict__ x, int64_t rows, int6
     out[blk * cols + col] = total;
 }
 
+// Full aligned blocks of COL_RB = 64 rows, four columns per thread: the
+// canonical tree over 64 leaves is the balanced binary tree, taken here as
+// four 16-row subtrees reduced pairwise in registers ((s0 + s1) + (s2 + s3)),
+// so the loads are float4 and independent.  Same values as col_block_kernel.
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                       __fadd_rn(a.w, b.w));
+}
+__global__ void col_block4_kernel(const float *__restrict__ x, int64_t cols, float *__restrict__ out) {
+    const int64_t c4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // float4 column
+    if (c4 * 4 >= cols) return;
+    const int64_t blk = blockIdx.y;
+    const float4 *src = reinterpret_cast<const float4 *>(x + blk * COL_RB * cols) + c4;
+    const int64_t stride = cols / 4;
+    float4 sub[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __ldcs(src + (q * 16 + i) * stride);
+#pragma unroll
+        for (int width = 1; width < 16; width <<= 1)
+#pragma unroll
+            for (int i = 0; i + width < 16; i += 2 * width) v[i] = add4(v[i], v[i + width]);
+        sub[q] = v[0];
+    }
+    reinterpret_cast<float4 *>(out + blk * cols)[c4] = add4(add4(sub[0], sub[1]), add4(sub[2], sub[3]));
+}
+
 // ---------------------------------------------------------------------------
 // dropout, count, cumsum
 // ---------------------------------------------------------------------------
@@ -390,6 +455,24 @@ __global__ void dropout_kernel(const float *__restrict__ x, float *__restrict__ 
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const bool keep = dropout_keep(key, static_cast<uint64_t>(index_base + i), threshold);
         y[i] = keep ? canon(__fdiv_rn(x[i], den)) : 0.0f;
+    }
+}
+
+// Four consecutive elements per thread step (float4 in and out, four
+// independent keyed-RNG chains in flight); elements past the last full
+// quad go through dropout_kernel.
+__global__ void dropout4_kernel(const float4 *__restrict__ x, float4 *__restrict__ y, int64_t n4,
+                                uint64_t key, uint64_t threshold, float den, int64_t index_base) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 v = __ldcs(x + i);
+        const uint64_t e = static_cast<uint64_t>(index_base + 4 * i);
+        const bool k0 = dropout_keep(key, e, threshold), k1 = dropout_keep(key, e + 1, threshold);
+        const bool k2 = dropout_keep(key, e + 2, threshold), k3 = dropout_keep(key, e + 3, threshold);
+        __stcs(y + i, make_float4(k0 ? canon(__fdiv_rn(v.x, den)) : 0.0f,
+                                  k1 ? canon(__fdiv_rn(v.y, den)) : 0.0f,
+                                  k2 ? canon(__fdiv_rn(v.z, den)) : 0.0f,
+                                  k3 ? canon(__fdiv_rn(v.w, den)) : 0.0f));
     }
 }
 
@@ -526,10 +609,28 @@ int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStr
     const int64_t nb = (rows + COL_RB - 1) / COL_RB;
     void *tmp = nullptr;
     CHELIS_TRY(scratch_alloc(&tmp, static_cast<size_t>(nb * cols) * sizeof(float), s));
-    col_block_kernel<<<dim3(cb, static_cast<unsigned>(nb)), 128, 0, s>>>(x, rows, cols, COL_RB,
-                                                                        static_cast<float *>(tmp));
-    g_launches++;
-    int st = check_cuda(cudaGetLastError(), "col_block_kernel");
+    float *blk = static_cast<float *>(tmp);
+    int st;
+    const int64_t nfull = rows / COL_RB;
+    if (cols % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && nfull > 0 && nfull <= 65535) {
+        // full blocks with float4 columns, the ragged last block (if any) below
+        const unsigned cb4 = static_cast<unsigned>((cols / 4 + 127) / 128);
+        col_block4_kernel<<<dim3(cb4, static_cast<unsigned>(nfull)), 128, 0, s>>>(x, cols, blk);
+        g_launches++;
+        st = check_cuda(cudaGetLastError(), "col_block4_kernel");
+        if (st == CHELIS_CUDA_OK && nb > nfull) {
+            col_block_kernel<<<dim3(cb, 1), 128, 0, s>>>(x + nfull * COL_RB * cols,
+                                                         rows - nfull * COL_RB, cols, COL_RB,
+                                                         blk + nfull * cols);
+            g_launches++;
+            st = check_cuda(cudaGetLastError(), "col_block_kernel");
+        }
+    } else {
+        col_block_kernel<<<dim3(cb, static_cast<unsigned>(nb)), 128, 0, s>>>(x, rows, cols, COL_RB,
+                                                                            blk);
+        g_launches++;
+        st = check_cuda(cudaGetLastError(), "col_block_kernel");
+    }
     if (st == CHELIS_CUDA_OK) st = col_sum_into(static_cast<float *>(tmp), nb, cols, out, s);
     scratch_free(tmp, s);
     return st;
@@ -610,6 +711,16 @@ int chelis_cuda_row_sum_f32(const float *x, int64_t rows, int64_t cols, float *o
     cudaStream_t s = current_stream();
     if (cols == 0) return check_cuda(cudaMemsetAsync(out, 0, rows * sizeof(float), s), "memset");
     const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
+    if (cols <= 8 * 4 * kRowThreads) {
+        const int n = static_cast<int>(cols);
+        return dispatch_nc(n, kRowThreads, [&](auto ncv) -> int {
+            constexpr int NC = decltype(ncv)::value;
+            row_sum_nc_kernel<kRowThreads, NC><<<grid, kRowThreads, 0, s>>>(x, rows, n, out);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("row_sum_nc_kernel");
+            return CHELIS_CUDA_OK;
+        });
+    }
     row_sum_kernel<256><<<grid, 256, 0, s>>>(x, rows, cols, out);
     g_launches++;
     CHELIS_LAUNCH_CHECK("row_sum_kernel");
@@ -656,13 +767,29 @@ int chelis_cuda_dropout_f32(const float *x, float *y, int64_t n, uint64_t key, f
     cudaStream_t s = current_stream();
     volatile float one = 1.0f;
     const float den = one - rate;
-    int64_t blocks = (n + 255) / 256;
-    if (blocks > 148 * 32) blocks = 148 * 32;
-    dropout_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, y, n, key,
-                                                               dropout_threshold(rate), den,
-                                                               index_base);
-    g_launches++;
-    CHELIS_LAUNCH_CHECK("dropout_kernel");
+    const uint64_t thr = dropout_threshold(rate);
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
+    int64_t done = 0;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+        n >= 4) {
+        const int64_t n4 = n / 4;
+        int64_t blocks = (n4 + 255) / 256;
+        if (blocks > cap) blocks = cap;
+        dropout4_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+            reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), n4, key, thr, den,
+            index_base);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("dropout4_kernel");
+        done = 4 * n4;
+    }
+    if (done < n) {
+        int64_t blocks = (n - done + 255) / 256;
+        if (blocks > cap) blocks = cap;
+        dropout_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x + done, y + done, n - done, key,
+                                                                   thr, den, index_base + done);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("dropout_kernel");
+    }
     return CHELIS_CUDA_OK;
 }
 
