@@ -37,8 +37,10 @@ namespace rows {
 // Reduce v[c][0..3] (thread t's 4 leaves of chunk c, valid when the element
 // index is < n) to the canonical tree total over all n leaves.  `red` is
 // shared scratch of at least NC * (T/32) floats.  Every thread returns the
-// total.  Ends with a __syncthreads so `red` can be reused.
-template <int T, int NC>
+// total.  Ends with a __syncthreads so `red` can be reused (TRAIL = false
+// leaves it out: the caller alternates two scratch areas, so the next
+// reduction's barrier already orders this one's reads before any rewrite).
+template <int T, int NC, bool TRAIL = true>
 __device__ __forceinline__ float block_tree(const float (&v)[NC][4], int n, float *red) {
     constexpr int W = T / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,14 +100,14 @@ __device__ __forceinline__ float block_tree(const float (&v)[NC][4], int n, floa
             chunk[i] = tree_pair(chunk[i], lv, chunk[i + width], rv);
         }
     }
-    __syncthreads();
+    if (TRAIL) __syncthreads();
     return chunk[0];
 }
 
 // Row maximum (order-free except for NaN, which fmaxf would drop: a NaN
 // anywhere makes the result NaN, as the first-NaN rule of [05-OP-12] does
 // for softmax, where only NaN-ness matters downstream).
-template <int T, int NC>
+template <int T, int NC, bool TRAIL = true>
 __device__ __forceinline__ float block_max(const float (&v)[NC][4], int n, float *red) {
     constexpr int W = T / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,7 +133,7 @@ __device__ __forceinline__ float block_max(const float (&v)[NC][4], int n, float
         const float o = red[i];
         r = (isnan(r) || isnan(o)) ? __int_as_float(0x7fc00000) : fmaxf(r, o);
     }
-    __syncthreads();
+    if (TRAIL) __syncthreads();
     return r;
 }
 
@@ -178,17 +180,30 @@ __device__ __forceinline__ float canon(float x) {
 // standalone row ops
 // ---------------------------------------------------------------------------
 template <int T, int NC, bool EXACT>
-__global__ void __launch_bounds__(T)
+__global__ void __launch_bounds__(T, NC <= 4 ? 3 : 1)
     layer_norm_kernel(const float *__restrict__ xin, const float *__restrict__ gamma,
                       const float *__restrict__ beta, float eps, float *__restrict__ yout,
                       int64_t rows, int n) {
-    __shared__ float red[NC * (T / 32) + 8];
+    __shared__ float red[2][NC * (T / 32) + 8];
     const float hf = static_cast<float>(n), rh = __fdiv_rn(1.0f, hf);
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(xin) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(yout) & 15) == 0);
-    float g[NC][4], b[NC][4];
-    load_row<NC, T>(g, gamma, n, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && n % 4 == 0);
-    load_row<NC, T>(b, beta, n, (reinterpret_cast<uintptr_t>(beta) & 15) == 0 && n % 4 == 0);
+    // gamma / beta in shared memory in the row layout (thread t's float4 of
+    // chunk c at [c * T + t]), read back as conflict-free float4; rows of
+    // 8 chunks keep them in registers (static shared memory is 48 KiB)
+    constexpr bool SMEM_GB = NC <= 4;
+    __shared__ float4 sg[SMEM_GB ? NC * T : 1], sb[SMEM_GB ? NC * T : 1];
+    float g[SMEM_GB ? 1 : NC][4], b[SMEM_GB ? 1 : NC][4];
+    if constexpr (SMEM_GB) {
+        for (int e = threadIdx.x; e < NC * 4 * T; e += T) {
+            reinterpret_cast<float *>(sg)[e] = e < n ? gamma[e] : 0.0f;
+            reinterpret_cast<float *>(sb)[e] = e < n ? beta[e] : 0.0f;
+        }
+        __syncthreads();
+    } else {
+        load_row<NC, T>(g, gamma, n, (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && n % 4 == 0);
+        load_row<NC, T>(b, beta, n, (reinterpret_cast<uintptr_t>(beta) & 15) == 0 && n % 4 == 0);
+    }
     // the next row's loads are issued before this row's reductions, so each
     // CTA keeps two rows in flight
     float nxt[NC][4];
@@ -200,7 +215,7 @@ __global__ void __launch_bounds__(T)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
         if (r + gridDim.x < rows) load_row<NC, T>(nxt, xin + (r + gridDim.x) * n, n, vec);
-        const float s1 = block_tree<T, NC>(v, n, red);
+        const float s1 = block_tree<T, NC, false>(v, n, red[0]);
         const float mean = EXACT ? __fdiv_rn(s1, hf) : __fmul_rn(s1, rh);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
@@ -209,17 +224,27 @@ __global__ void __launch_bounds__(T)
                 v[c][i] = __fsub_rn(v[c][i], mean);
                 c2[c][i] = __fmul_rn(v[c][i], v[c][i]);
             }
-        const float s2 = block_tree<T, NC>(c2, n, red);
+        const float s2 = block_tree<T, NC, false>(c2, n, red[1]);
         const float var = EXACT ? __fdiv_rn(s2, hf) : __fmul_rn(s2, rh);
         const float d = __fsqrt_rn(__fadd_rn(var, eps));
         const float rd = __fdiv_rn(1.0f, d);
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
+        for (int c = 0; c < NC; ++c) {
+            float gg[4], bb[4];
+            if constexpr (SMEM_GB) {
+                const float4 g4 = sg[c * T + threadIdx.x], b4 = sb[c * T + threadIdx.x];
+                gg[0] = g4.x; gg[1] = g4.y; gg[2] = g4.z; gg[3] = g4.w;
+                bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) { gg[i] = g[SMEM_GB ? 0 : c][i]; bb[i] = b[SMEM_GB ? 0 : c][i]; }
+            }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const float nn = EXACT ? __fdiv_rn(v[c][i], d) : __fmul_rn(v[c][i], rd);
-                v[c][i] = canon(__fadd_rn(__fmul_rn(nn, g[c][i]), b[c][i]));
+                v[c][i] = canon(__fadd_rn(__fmul_rn(nn, gg[i]), bb[i]));
             }
+        }
         store_row<NC, T>(v, yout + r * n, n, vec);
     }
 }
@@ -227,7 +252,7 @@ __global__ void __launch_bounds__(T)
 template <int T, int NC, bool EXACT>
 __global__ void __launch_bounds__(T)
     softmax_kernel(const float *__restrict__ xin, float *__restrict__ yout, int64_t rows, int n) {
-    __shared__ float red[NC * (T / 32) + 8];
+    __shared__ float red[2][NC * (T / 32) + 8];
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(xin) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(yout) & 15) == 0);
     float nxt[NC][4];
@@ -239,12 +264,12 @@ __global__ void __launch_bounds__(T)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
         if (r + gridDim.x < rows) load_row<NC, T>(nxt, xin + (r + gridDim.x) * n, n, vec);
-        const float mx = block_max<T, NC>(v, n, red);
+        const float mx = block_max<T, NC, false>(v, n, red[0]);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = expf(__fsub_rn(v[c][i], mx));
-        const float z = block_tree<T, NC>(v, n, red);
+        const float z = block_tree<T, NC, false>(v, n, red[1]);
         const float rz = __fdiv_rn(1.0f, z);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
@@ -286,7 +311,7 @@ __global__ void __launch_bounds__(T)
 template <int T, int NC>
 __global__ void __launch_bounds__(T)
     row_sum_nc_kernel(const float *__restrict__ x, int64_t rows, int n, float *__restrict__ out) {
-    __shared__ float red[NC * (T / 32) + 8];
+    __shared__ float red[2][NC * (T / 32) + 8];
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
     float nxt[NC][4];
     if (blockIdx.x < rows) load_row<NC, T>(nxt, x + blockIdx.x * static_cast<int64_t>(n), n, vec);
@@ -297,7 +322,7 @@ __global__ void __launch_bounds__(T)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
         if (r + gridDim.x < rows) load_row<NC, T>(nxt, x + (r + gridDim.x) * n, n, vec);
-        const float s = block_tree<T, NC>(v, n, red);
+        const float s = block_tree<T, NC, false>(v, n, red[((r - blockIdx.x) / gridDim.x) & 1]);
         if (threadIdx.x == 0) out[r] = canon(s);
     }
 }
