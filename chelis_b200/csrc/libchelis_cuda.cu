@@ -13,3 +13,4 @@
 #include "block.cu"
 #include "abi.cu"
 #include "chain_noalloc.cu"
+#include "fused.cu"

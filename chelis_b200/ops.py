@@ -9,6 +9,7 @@ tensors.  Names and argument meanings follow the reference's operations
 from __future__ import annotations
 
 import contextlib
+import ctypes
 
 import torch
 
@@ -376,3 +377,60 @@ def mlp_step(x, labels, w1, b1, w2, b2):
            b1.data_ptr(), w2.data_ptr(), b2.data_ptr(), batch, din, dh, dout, loss.data_ptr(),
            dw1.data_ptr(), db1.data_ptr(), dw2.data_ptr(), db2.data_ptr())
     return loss, dw1, db1, dw2, db2
+
+
+def _fused_args(steps, inputs, shape):
+    from . import fused as F
+    if not steps:
+        raise ValueError("a fused group has at least one step")
+    dtypes = {t.dtype for t in inputs}
+    if len(dtypes) > 1:
+        raise ValueError("fused group inputs share one dtype")
+    dtype = dtypes.pop() if dtypes else torch.float32
+    if dtype not in (torch.float32, torch.float64):
+        raise ValueError("fused groups compute in f32 or f64")
+    for t in inputs:
+        if not t.is_cuda:
+            raise ValueError("chelis_b200 ops take CUDA tensors (device memory)")
+    shape = tuple(torch.broadcast_shapes(*(t.shape for t in inputs))) if shape is None else tuple(shape)
+    rank = len(shape)
+    strides = []
+    for t in inputs:
+        strides.extend(t.expand(shape).stride() if rank else ())
+    c_i64 = ctypes.c_int64
+    arrays = dict(
+        steps=F.encode(steps),
+        ptrs=(ctypes.c_void_p * max(len(inputs), 1))(*[t.data_ptr() for t in inputs]),
+        strides=(c_i64 * max(len(strides), 1))(*strides),
+        shape=(c_i64 * max(rank, 1))(*shape),
+    )
+    dt = L.DTYPE_F32 if dtype == torch.float32 else L.DTYPE_F64
+    return dt, dtype, shape, arrays
+
+
+def fused_elementwise(steps, inputs, shape=None) -> torch.Tensor:
+    """Evaluate a FusedElem chain (a list of chelis_b200.fused.FusedStep)
+    over `inputs` broadcast to `shape` (default: their broadcast shape)."""
+    dt, dtype, shape, a = _fused_args(steps, inputs, shape)
+    device = inputs[0].device if inputs else torch.device("cuda", torch.cuda.current_device())
+    out = torch.empty(shape, dtype=dtype, device=device)
+    _prepare(out)
+    L.call("chelis_cuda_fused_elementwise", dt, a["steps"], len(steps), a["ptrs"], a["strides"],
+           len(inputs), a["shape"], len(shape), out.data_ptr())
+    return out
+
+
+def fused_reduce(steps, inputs, axis: int, kind: str = "sum", shape=None) -> torch.Tensor:
+    """The chain reduced along `axis` ("sum" or "max", emit_fused_reduce):
+    the result has the iteration shape without `axis`."""
+    from . import fused as F
+    dt, dtype, shape, a = _fused_args(steps, inputs, shape)
+    if not shape:
+        raise ValueError("fused_reduce needs rank >= 1")
+    axis = axis % len(shape)
+    device = inputs[0].device if inputs else torch.device("cuda", torch.cuda.current_device())
+    out = torch.empty(shape[:axis] + shape[axis + 1:], dtype=dtype, device=device)
+    _prepare(out)
+    L.call("chelis_cuda_fused_reduce", dt, a["steps"], len(steps), a["ptrs"], a["strides"],
+           len(inputs), a["shape"], len(shape), axis, F.REDUCE_KIND[kind], out.data_ptr())
+    return out

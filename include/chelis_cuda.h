@@ -259,6 +259,64 @@ int chelis_cuda_attention_causal_bwd(int64_t bh, int64_t seq, int64_t dh, float 
  * fused_elementwise / reduce_fused; row reductions :1703-2014) and rejects
  * Softmax, sqrt and Dropout on HIP (emit.rs:1572-1583, 2763-2775).
  * ========================================================================= */
+/* A FusedElem group (dag.rs:1323-1325): a chain of steps, each one
+ * FusedStepOp (dag.rs:494-526, same order and numbering) over operands that
+ * are FusedInputs (dag.rs:673-678): a >= 0 is External(a), an input; a < 0
+ * is PreviousStep(-1 - a), an earlier step.  Unary steps ignore b.  The
+ * group's value is its last step. */
+typedef enum {
+    CHELIS_FUSED_ADD = 0,
+    CHELIS_FUSED_SUB = 1,
+    CHELIS_FUSED_MUL = 2,
+    CHELIS_FUSED_DIV = 3,
+    CHELIS_FUSED_POW = 4,
+    CHELIS_FUSED_FLOOR_DIV = 5,
+    CHELIS_FUSED_TRUNC_DIV = 6, /* integer-only: rejected on a float chain */
+    CHELIS_FUSED_MAX_ELEM = 7,
+    CHELIS_FUSED_MIN_ELEM = 8,
+    CHELIS_FUSED_NEG = 9,
+    CHELIS_FUSED_RECIP = 10,
+    CHELIS_FUSED_EXP = 11,
+    CHELIS_FUSED_LOG = 12,
+    CHELIS_FUSED_SIN = 13,
+    CHELIS_FUSED_SQRT = 14,
+    CHELIS_FUSED_COS = 15,
+    CHELIS_FUSED_TAN = 16,
+    CHELIS_FUSED_ATAN = 17,
+    CHELIS_FUSED_TANH = 18,
+    CHELIS_FUSED_ERF = 19,
+    CHELIS_FUSED_ERFC = 20,
+    CHELIS_FUSED_ABS = 21,
+    CHELIS_FUSED_FLOOR = 22,
+    CHELIS_FUSED_CEIL = 23,
+    CHELIS_FUSED_ROUND = 24
+} chelis_fused_op;
+typedef struct {
+    int32_t op; /* chelis_fused_op */
+    int32_t a, b;
+} chelis_fused_step;
+typedef enum { CHELIS_FUSED_REDUCE_SUM = 0, CHELIS_FUSED_REDUCE_MAX = 1 } chelis_fused_reduce_kind;
+/* Evaluate the group over `shape` (rank <= 6) into the dense `out`.  Input k
+ * is read at sum(coord[d] * strides[k * rank + d]) elements: stride 0 on a
+ * dimension broadcasts it (the HIP lane's per-input strides, kernels.rs
+ * fused_elementwise :2391-2468; the C lane's full-or-scalar inputs,
+ * emit.rs:6984-7100, are the strides 1..., and 0...).  dtype F32 or F64;
+ * <= 32 steps, <= 8 inputs.  Step results follow the C lane
+ * (emit.rs:6744-6905 with fp_env.rs:213-241): canonical NaN after every step
+ * but MaxElem / MinElem; transcendentals within a few ulp of its correctly
+ * rounded CORE-MATH calls. */
+int chelis_cuda_fused_elementwise(int32_t dtype, const chelis_fused_step *steps, int32_t n_steps,
+                                  const void *const *inputs, const int64_t *strides,
+                                  int32_t n_inputs, const int64_t *shape, int32_t rank, void *out);
+/* The group reduced along `axis` of `shape` (emit_fused_reduce,
+ * emit.rs:9580-9860; reduce_fused kernels.rs:2175-2390): Sum by the
+ * canonical pair tree, Max folding chelis_fmax_propnan_f32 from -inf.  `out`
+ * is dense over shape without `axis`.  An empty Max axis is the Domain trap
+ * "max_reduce"; an empty Sum axis writes zeros. */
+int chelis_cuda_fused_reduce(int32_t dtype, const chelis_fused_step *steps, int32_t n_steps,
+                             const void *const *inputs, const int64_t *strides, int32_t n_inputs,
+                             const int64_t *shape, int32_t rank, int32_t axis, int32_t kind,
+                             void *out);
 /* [05-OP-30] sum over the last axis / first axis of a [rows, cols] f32 tensor,
  * canonical adjacent-pair tree (kernels.rs:1703-1755 left-folds instead). */
 int chelis_cuda_row_sum_f32(const float *x, int64_t rows, int64_t cols, float *out);

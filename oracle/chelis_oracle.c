@@ -674,3 +674,159 @@ float orc_add_f32(float a, float b) { return canon_f32(a + b); }
 float orc_mul_f32(float a, float b) { return canon_f32(a * b); }
 float orc_div_f32(float a, float b) { return canon_f32(a / b); }
 float orc_sqrt_f32(float a) { return canon_f32(sqrtf(a)); }
+
+/* ------------------------------------------------------------------------ */
+/* FusedElem groups: the chain of FusedStepOps (crates/chelis-dag-core/src/ */
+/* dag.rs:494-526) evaluated per element as the C lane emits it             */
+/* (crates/chelis-backend-c/src/emit.rs scalar_step_raw_expr :6744-6905,    */
+/* each step finalized by fp_env.rs fused_step_nan_finalization :213-241:   */
+/* canonical NaN after every op but MaxElem / MinElem), and reduced along   */
+/* one axis as emit_fused_reduce does (emit.rs:9580-9860: Sum by the carry  */
+/* tree, finalized once; Max folding chelis_fmax_propnan_f32 from -inf,     */
+/* crates/chelis-runtime/include/chelis_simd.h:66-69).  Transcendentals     */
+/* are the reference's CORE-MATH (chelis_cr_* -> crmath_ffi.c).             */
+/* ------------------------------------------------------------------------ */
+float chelis_crmath_ffi_sinf(float);
+float chelis_crmath_ffi_cosf(float);
+float chelis_crmath_ffi_tanf(float);
+float chelis_crmath_ffi_atanf(float);
+float chelis_crmath_ffi_tanhf(float);
+float chelis_crmath_ffi_erff(float);
+float chelis_crmath_ffi_powf(float, float);
+double chelis_crmath_ffi_log(double);
+double chelis_crmath_ffi_sin(double);
+double chelis_crmath_ffi_cos(double);
+double chelis_crmath_ffi_tan(double);
+double chelis_crmath_ffi_atan(double);
+double chelis_crmath_ffi_tanh(double);
+double chelis_crmath_ffi_erf(double);
+double chelis_crmath_ffi_erfc(double);
+double chelis_crmath_ffi_pow(double, double);
+
+enum {
+    F_ADD, F_SUB, F_MUL, F_DIV, F_POW, F_FLOOR_DIV, F_TRUNC_DIV, F_MAX, F_MIN, F_NEG, F_RECIP,
+    F_EXP, F_LOG, F_SIN, F_SQRT, F_COS, F_TAN, F_ATAN, F_TANH, F_ERF, F_ERFC, F_ABS, F_FLOOR,
+    F_CEIL, F_ROUND
+};
+
+#define DEFINE_FUSED(T, SUFFIX, CANON, CR, FLOOR, CEIL, RINT, FABS, SQRT)                      \
+    static T fused_step_##SUFFIX(int op, T x, T y) {                                           \
+        switch (op) {                                                                          \
+            case F_ADD: return CANON(x + y);                                                   \
+            case F_SUB: return CANON((x) - (y));                                               \
+            case F_MUL: return CANON(x * y);                                                   \
+            case F_DIV: return CANON(x / y);                                                   \
+            case F_POW: return CANON(CR(pow)(x, y));                                           \
+            case F_FLOOR_DIV: return CANON(FLOOR(x / y));                                      \
+            case F_MAX: return (isnan(x) || (!isnan(y) && x >= y)) ? x : y;                    \
+            case F_MIN: return (isnan(x) || (!isnan(y) && x <= y)) ? x : y;                    \
+            case F_NEG: return CANON(-x);                                                      \
+            case F_RECIP: return CANON((T)1 / x);                                              \
+            case F_EXP: return CANON(CR(exp)(x));                                              \
+            case F_LOG: return CANON(CR(log)(x));                                              \
+            case F_SIN: return CANON(CR(sin)(x));                                              \
+            case F_SQRT: return CANON(SQRT(x));                                                \
+            case F_COS: return CANON(CR(cos)(x));                                              \
+            case F_TAN: return CANON(CR(tan)(x));                                              \
+            case F_ATAN: return CANON(CR(atan)(x));                                            \
+            case F_TANH: return CANON(CR(tanh)(x));                                            \
+            case F_ERF: return CANON(CR(erf)(x));                                              \
+            case F_ERFC: return CANON(CR(erfc)(x));                                            \
+            case F_ABS: return CANON(FABS(x));                                                 \
+            case F_FLOOR: return CANON(FLOOR(x));                                              \
+            case F_CEIL: return CANON(CEIL(x));                                                \
+            case F_ROUND: return CANON(RINT(x));                                               \
+            default: abort();                                                                  \
+        }                                                                                      \
+    }                                                                                          \
+    /* value of the chain at the element with coordinates `coord` */                          \
+    static T fused_eval_##SUFFIX(const int32_t *steps, int n_steps, const T *const *in,         \
+                                 const int64_t *strides, int n_in, const int64_t *coord,       \
+                                 int rank, T *v) {                                             \
+        T ext[8];                                                                              \
+        for (int k = 0; k < n_in; ++k) {                                                       \
+            int64_t off = 0;                                                                   \
+            for (int d = 0; d < rank; ++d) off += coord[d] * strides[k * rank + d];            \
+            ext[k] = in[k][off];                                                               \
+        }                                                                                      \
+        for (int s = 0; s < n_steps; ++s) {                                                    \
+            int op = steps[3 * s], a = steps[3 * s + 1], b = steps[3 * s + 2];                 \
+            T x = a >= 0 ? ext[a] : v[-1 - a];                                                 \
+            T y = x;                                                                           \
+            if (op <= F_MIN) y = b >= 0 ? ext[b] : v[-1 - b];                                  \
+            v[s] = fused_step_##SUFFIX(op, x, y);                                              \
+        }                                                                                      \
+        return v[n_steps - 1];                                                                 \
+    }                                                                                          \
+    void orc_fused_elementwise_##SUFFIX(const int32_t *steps, int32_t n_steps,                 \
+                                        const T *const *in, const int64_t *strides,            \
+                                        int32_t n_in, const int64_t *shape, int32_t rank,      \
+                                        T *out) {                                              \
+        int64_t total = 1;                                                                     \
+        for (int d = 0; d < rank; ++d) total *= shape[d];                                      \
+        _Pragma("omp parallel for schedule(static)")                                           \
+        for (int64_t i = 0; i < total; ++i) {                                                  \
+            int64_t coord[8], rem = i;                                                         \
+            T v[32];                                                                           \
+            for (int d = rank - 1; d >= 0; --d) {                                              \
+                coord[d] = rem % shape[d];                                                     \
+                rem /= shape[d];                                                               \
+            }                                                                                  \
+            out[i] = fused_eval_##SUFFIX(steps, n_steps, in, strides, n_in, coord, rank, v);   \
+        }                                                                                      \
+    }                                                                                          \
+    /* kind 0 = Sum, 1 = Max; out is dense over shape without `axis` */                       \
+    void orc_fused_reduce_##SUFFIX(const int32_t *steps, int32_t n_steps, const T *const *in,  \
+                                   const int64_t *strides, int32_t n_in, const int64_t *shape, \
+                                   int32_t rank, int32_t axis, int32_t kind, T *out) {         \
+        int64_t outputs = 1, len = shape[axis];                                                \
+        for (int d = 0; d < rank; ++d)                                                         \
+            if (d != axis) outputs *= shape[d];                                                \
+        _Pragma("omp parallel for schedule(static)")                                           \
+        for (int64_t o = 0; o < outputs; ++o) {                                                \
+            int64_t coord[8], rem = o;                                                         \
+            T v[32];                                                                           \
+            for (int d = rank - 1; d >= 0; --d) {                                              \
+                if (d == axis) continue;                                                       \
+                coord[d] = rem % shape[d];                                                     \
+                rem /= shape[d];                                                               \
+            }                                                                                  \
+            if (kind == 0) {                                                                   \
+                T level[64];                                                                   \
+                int64_t count = 0;                                                             \
+                for (int64_t j = 0; j < len; ++j) {                                            \
+                    coord[axis] = j;                                                           \
+                    T carry = fused_eval_##SUFFIX(steps, n_steps, in, strides, n_in, coord,    \
+                                                  rank, v);                                    \
+                    int depth = 0;                                                             \
+                    for (int64_t pending = count++; pending & 1; pending >>= 1, ++depth)       \
+                        carry = level[depth] + carry;                                          \
+                    level[depth] = carry;                                                      \
+                }                                                                              \
+                T total = (T)0;                                                                \
+                int found = 0, depth = 0;                                                      \
+                for (int64_t remaining = count; remaining; remaining >>= 1, ++depth)           \
+                    if (remaining & 1) {                                                       \
+                        total = found ? level[depth] + total : level[depth];                   \
+                        found = 1;                                                             \
+                    }                                                                          \
+                out[o] = CANON(total);                                                         \
+            } else {                                                                           \
+                T acc = -INFINITY;                                                             \
+                for (int64_t j = 0; j < len; ++j) {                                            \
+                    coord[axis] = j;                                                           \
+                    T x = fused_eval_##SUFFIX(steps, n_steps, in, strides, n_in, coord, rank,  \
+                                              v);                                              \
+                    /* chelis_fmax_propnan_f32(acc, x) */                                      \
+                    acc = (acc != acc || x != x) ? CANON((T)NAN) : (acc > x ? acc : x);        \
+                }                                                                              \
+                out[o] = acc;                                                                  \
+            }                                                                                  \
+        }                                                                                      \
+    }
+
+#define CR_F32(name) chelis_crmath_ffi_##name##f
+#define CR_F64(name) chelis_crmath_ffi_##name
+static inline float cr_sqrtf(float x) { return sqrtf(x); }
+DEFINE_FUSED(float, f32, canon_f32, CR_F32, floorf, ceilf, rintf, fabsf, cr_sqrtf)
+DEFINE_FUSED(double, f64, canon_f64, CR_F64, floor, ceil, rint, fabs, sqrt)

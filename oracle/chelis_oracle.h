@@ -99,6 +99,25 @@ float orc_erfcf(float x);
 double orc_exp(double x);
 double orc_sqrt(double x);
 
+
+/* ---- FusedElem groups (emit.rs:6744-6905, 9580-9860) ----
+ * steps: n_steps triplets (op, a, b), op the FusedStepOp index
+ * (dag.rs:494-526), operand >= 0 an input, < 0 step -1 - operand.
+ * Input k is read at sum(coord[d] * strides[k * rank + d]).  Reduce kind
+ * 0 = Sum, 1 = Max; its output is dense over shape without `axis`. */
+void orc_fused_elementwise_f32(const int32_t *steps, int32_t n_steps, const float *const *in,
+                               const int64_t *strides, int32_t n_in, const int64_t *shape,
+                               int32_t rank, float *out);
+void orc_fused_elementwise_f64(const int32_t *steps, int32_t n_steps, const double *const *in,
+                               const int64_t *strides, int32_t n_in, const int64_t *shape,
+                               int32_t rank, double *out);
+void orc_fused_reduce_f32(const int32_t *steps, int32_t n_steps, const float *const *in,
+                          const int64_t *strides, int32_t n_in, const int64_t *shape, int32_t rank,
+                          int32_t axis, int32_t kind, float *out);
+void orc_fused_reduce_f64(const int32_t *steps, int32_t n_steps, const double *const *in,
+                          const int64_t *strides, int32_t n_in, const int64_t *shape, int32_t rank,
+                          int32_t axis, int32_t kind, double *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -286,3 +286,48 @@ def expf(x: float) -> float:
 
 def logf(x: float) -> float:
     return lib().orc_logf(x)
+
+
+def _fused_call(name, triplets, inputs, shape, extra):
+    inputs = [np.asarray(x) for x in inputs]
+    dtypes = {x.dtype for x in inputs} or {np.dtype(np.float32)}
+    assert len(dtypes) == 1, "fused inputs share one dtype"
+    dt = dtypes.pop()
+    assert dt in (np.float32, np.float64)
+    shape = tuple(np.broadcast_shapes(*(x.shape for x in inputs))) if shape is None else tuple(shape)
+    rank = len(shape)
+    keep = [x if x.flags.c_contiguous else x.copy(order="C") for x in inputs]  # rank 0 stays rank 0
+    strides = []
+    for k in keep:  # element strides of each (contiguous) input over the shape
+        strides.extend(s // k.itemsize for s in np.broadcast_to(k, shape).strides)
+    steps = np.ascontiguousarray(np.asarray(triplets, dtype=np.int32).reshape(-1))
+    ptrs = (ctypes.c_void_p * max(len(keep), 1))(*[k.ctypes.data for k in keep])
+    st = np.ascontiguousarray(np.asarray(strides if strides else [0], dtype=np.int64))
+    sh = np.ascontiguousarray(np.asarray(shape if shape else [1], dtype=np.int64))
+    fn = getattr(lib(), name + ("_f32" if dt == np.float32 else "_f64"))
+    fn.restype = None
+    out_shape, args = extra(shape)
+    out = np.empty(out_shape, dtype=dt)
+    fn(steps.ctypes.data_as(ctypes.c_void_p), ctypes.c_int32(len(triplets)), ptrs,
+       st.ctypes.data_as(ctypes.c_void_p), ctypes.c_int32(len(keep)),
+       sh.ctypes.data_as(ctypes.c_void_p), ctypes.c_int32(rank), *args,
+       out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
+def fused_elementwise(triplets, inputs, shape=None) -> np.ndarray:
+    """FusedElem chain of (op, a, b) triplets (op the FusedStepOp index; an
+    operand >= 0 an input, < 0 the step -1 - operand) over the inputs
+    broadcast to `shape`; C-lane step semantics with CORE-MATH."""
+    return _fused_call("orc_fused_elementwise", triplets, inputs, shape, lambda s: (s, ()))
+
+
+def fused_reduce(triplets, inputs, axis: int, kind: str = "sum", shape=None) -> np.ndarray:
+    """The chain reduced along `axis`: "sum" (carry tree) or "max"
+    (chelis_fmax_propnan fold from -inf)."""
+    k = {"sum": 0, "max": 1}[kind]
+
+    def extra(s):
+        ax = axis % len(s)
+        return s[:ax] + s[ax + 1:], (ctypes.c_int32(ax), ctypes.c_int32(k))
+    return _fused_call("orc_fused_reduce", triplets, inputs, shape, extra)

@@ -11,6 +11,11 @@ tree at run time.
   crates/chelis-crmath/tests/fixtures/profile_obligations.txt: primitive,
   expected bits, operand bits.  They pin the oracle's finalized arithmetic
   (round to nearest even, subnormals kept, canonical NaN).
+* fused_steps.txt -- one row per single-step FusedElem chain: step op, width
+  (f32 / f64), expected bits, operand bits.  The add / sub / mul / div / sqrt
+  / pow rows of profile_obligations.txt, every canary.txt row (exp, log, sin,
+  cos, tan, atan, tanh, erf, erfc) and the pow_worst_cases.txt sample; they
+  pin the fused oracle's steps and bound the CUDA steps.
 """
 import os
 import sys
@@ -44,7 +49,17 @@ def main():
         f.write("# primitive expected-bits operand-bits... (from the reference profile obligations)\n")
         for p in ieee:
             f.write(" ".join([p[0]] + p[2:]) + "\n")
-    print(len(canary), len(ieee))
+    steps = [[p[0], p[1], p[2], *p[3:]] for p in rows(
+        os.path.join(FIX, "profile_obligations.txt"),
+        lambda p: p[0] in ("add", "sub", "mul", "div", "sqrt", "pow"))]
+    steps += [[p[0], p[1], p[3], p[2]] for p in rows(os.path.join(FIX, "canary.txt"), lambda p: True)]
+    steps += [[p[0], p[1], p[4], p[2], p[3]]
+              for p in rows(os.path.join(FIX, "pow_worst_cases.txt"), lambda p: True)]
+    with open(os.path.join(OUT, "fused_steps.txt"), "w") as f:
+        f.write("# op width expected-bits operand-bits... (reference CORE-MATH / profile fixtures)\n")
+        for p in steps:
+            f.write(" ".join(p) + "\n")
+    print(len(canary), len(ieee), len(steps))
 
 
 if __name__ == "__main__":
