@@ -47,7 +47,7 @@ namespace fused {
 
 constexpr int MAX_STEPS = 32, MAX_INPUTS = 8, MAX_RANK = 6, THREADS = 128;
 enum Mode { DENSE = 0, STRIDED32 = 1, STRIDED64 = 2 };
-enum StepFlag { A_PREV = 1, B_PREV = 2, STORE = 4 };
+enum StepFlag { A_PREV = 1, B_PREV = 2, STORE = 4, HEAVY = 8 };
 
 struct Program {
     uint8_t op[MAX_STEPS];
@@ -55,7 +55,7 @@ struct Program {
     uint8_t flags[MAX_STEPS];            // A_PREV / B_PREV: operand is the step before; STORE: a later step reads the row
     uint8_t row[MAX_STEPS];              // table row of a STORE step
     int32_t n_steps, n_inputs, rank;
-    int32_t n_rows;                       // inputs, then the STORE steps
+    int32_t n_rows;                       // inputs, then the STORE steps (a scratch row follows)
     int32_t vec_mask;                     // input k may be read E elements at a time (aligned, unit stride)
     const void *in[MAX_INPUTS];
     int64_t stride[MAX_INPUTS][MAX_RANK];  // element strides over the iteration shape
@@ -122,21 +122,20 @@ __device__ __forceinline__ T m_pow(T x, T y) {
     else return ::pow(x, y);
 }
 
-// One step over E elements: x, y in, r out.  The opcode is uniform across
-// the grid, so the switch is taken once per step for all E elements.
+// The light steps over E elements (all but pow, sin, cos, tan): x, y in, r out.  The opcode is uniform
+// across the grid, so the switch is taken once per step for all E elements.
 template <typename T, int E>
-__device__ __forceinline__ void apply(int op, const T (&x)[E], const T (&y)[E], T (&r)[E]) {
-#define CHELIS_FUSED_EACH(expr)                  \
-    {                                            \
-        _Pragma("unroll") for (int e = 0; e < E; ++e) r[e] = (expr); \
-    }                                            \
+__device__ __forceinline__ void apply_light(int op, const T (&x)[E], const T (&y)[E], T (&r)[E]) {
+#define CHELIS_FUSED_EACH(expr)                                          \
+    {                                                                    \
+        _Pragma("unroll") for (int e = 0; e < E; ++e) r[e] = (expr);     \
+    }                                                                    \
     break;
     switch (op) {
         case CHELIS_FUSED_ADD: CHELIS_FUSED_EACH(canon_nan(m_add(x[e], y[e])))
         case CHELIS_FUSED_SUB: CHELIS_FUSED_EACH(canon_nan(m_sub(x[e], y[e])))
         case CHELIS_FUSED_MUL: CHELIS_FUSED_EACH(canon_nan(m_mul(x[e], y[e])))
         case CHELIS_FUSED_DIV: CHELIS_FUSED_EACH(canon_nan(m_div(x[e], y[e])))
-        case CHELIS_FUSED_POW: CHELIS_FUSED_EACH(canon_nan(m_pow(x[e], y[e])))
         case CHELIS_FUSED_FLOOR_DIV: CHELIS_FUSED_EACH(canon_nan(m_floor(m_div(x[e], y[e]))))
         case CHELIS_FUSED_MAX_ELEM:
             CHELIS_FUSED_EACH((isnan(x[e]) || (!isnan(y[e]) && x[e] >= y[e])) ? x[e] : y[e])
@@ -144,51 +143,84 @@ __device__ __forceinline__ void apply(int op, const T (&x)[E], const T (&y)[E], 
             CHELIS_FUSED_EACH((isnan(x[e]) || (!isnan(y[e]) && x[e] <= y[e])) ? x[e] : y[e])
         case CHELIS_FUSED_NEG: CHELIS_FUSED_EACH(canon_nan(-x[e]))
         case CHELIS_FUSED_RECIP: CHELIS_FUSED_EACH(canon_nan(m_div(T(1), x[e])))
-        case CHELIS_FUSED_EXP: CHELIS_FUSED_EACH(canon_nan(m_exp(x[e])))
-        case CHELIS_FUSED_LOG: CHELIS_FUSED_EACH(canon_nan(m_log(x[e])))
-        case CHELIS_FUSED_SIN: CHELIS_FUSED_EACH(canon_nan(m_sin(x[e])))
         case CHELIS_FUSED_SQRT: CHELIS_FUSED_EACH(canon_nan(m_sqrt(x[e])))
-        case CHELIS_FUSED_COS: CHELIS_FUSED_EACH(canon_nan(m_cos(x[e])))
-        case CHELIS_FUSED_TAN: CHELIS_FUSED_EACH(canon_nan(m_tan(x[e])))
-        case CHELIS_FUSED_ATAN: CHELIS_FUSED_EACH(canon_nan(m_atan(x[e])))
-        case CHELIS_FUSED_TANH: CHELIS_FUSED_EACH(canon_nan(m_tanh(x[e])))
-        case CHELIS_FUSED_ERF: CHELIS_FUSED_EACH(canon_nan(m_erf(x[e])))
-        case CHELIS_FUSED_ERFC: CHELIS_FUSED_EACH(canon_nan(m_erfc(x[e])))
         case CHELIS_FUSED_ABS: CHELIS_FUSED_EACH(canon_nan(m_abs(x[e])))
         case CHELIS_FUSED_FLOOR: CHELIS_FUSED_EACH(canon_nan(m_floor(x[e])))
         case CHELIS_FUSED_CEIL: CHELIS_FUSED_EACH(canon_nan(m_ceil(x[e])))
         case CHELIS_FUSED_ROUND: CHELIS_FUSED_EACH(canon_nan(m_rint(x[e])))
-        default: CHELIS_FUSED_EACH(x[e])  // rejected on the host
+        case CHELIS_FUSED_EXP: CHELIS_FUSED_EACH(canon_nan(m_exp(x[e])))
+        case CHELIS_FUSED_LOG: CHELIS_FUSED_EACH(canon_nan(m_log(x[e])))
+        case CHELIS_FUSED_ATAN: CHELIS_FUSED_EACH(canon_nan(m_atan(x[e])))
+        case CHELIS_FUSED_TANH: CHELIS_FUSED_EACH(canon_nan(m_tanh(x[e])))
+        case CHELIS_FUSED_ERF: CHELIS_FUSED_EACH(canon_nan(m_erf(x[e])))
+        case CHELIS_FUSED_ERFC: CHELIS_FUSED_EACH(canon_nan(m_erfc(x[e])))
+        default: CHELIS_FUSED_EACH(x[e])  // heavy steps take run_steps' other path
     }
 #undef CHELIS_FUSED_EACH
+}
+
+// The heavy steps (pow, sin, cos, tan: libm calls whose slow paths hold
+// many registers or a local array), one element at a time.
+template <typename T>
+__device__ __forceinline__ T apply_heavy(int op, T x, T y) {
+    switch (op) {
+        case CHELIS_FUSED_POW: return canon_nan(m_pow(x, y));
+        case CHELIS_FUSED_EXP: return canon_nan(m_exp(x));
+        case CHELIS_FUSED_LOG: return canon_nan(m_log(x));
+        case CHELIS_FUSED_SIN: return canon_nan(m_sin(x));
+        case CHELIS_FUSED_COS: return canon_nan(m_cos(x));
+        case CHELIS_FUSED_TAN: return canon_nan(m_tan(x));
+        case CHELIS_FUSED_ATAN: return canon_nan(m_atan(x));
+        case CHELIS_FUSED_TANH: return canon_nan(m_tanh(x));
+        case CHELIS_FUSED_ERF: return canon_nan(m_erf(x));
+        case CHELIS_FUSED_ERFC: return canon_nan(m_erfc(x));
+        default: return x;
+    }
 }
 
 // Table cell of row `row`, element e: tab[(row * E + e) * THREADS].  The
 // step before stays in registers (`last`): an operand that names it is not
 // re-read, and a step's row is written only when a later step, not the next
-// one, reads it.
+// one, reads it.  A heavy step runs its E elements in a loop (one libm
+// call's registers, not E of them) through the table's scratch row.
 template <typename T, int E>
 __device__ __forceinline__ void run_steps(const Program &p, T *tab, T (&last)[E]) {
+    T *scratch = tab + p.n_rows * (E * THREADS);
     for (int s = 0; s < p.n_steps; ++s) {
         const int f = p.flags[s];
-        T x[E], y[E];
-        if (f & A_PREV) {
+        if (f & HEAVY) {
+            if (f & (A_PREV | B_PREV)) {
 #pragma unroll
-            for (int e = 0; e < E; ++e) x[e] = last[e];
+                for (int e = 0; e < E; ++e) scratch[e * THREADS] = last[e];
+            }
+            const T *ra = (f & A_PREV) ? scratch : tab + p.a[s] * (E * THREADS);
+            const T *rb = (f & B_PREV) ? scratch : tab + p.b[s] * (E * THREADS);
+            const int op = p.op[s];
+#pragma unroll 1
+            for (int e = 0; e < E; ++e)
+                scratch[e * THREADS] = apply_heavy<T>(op, ra[e * THREADS], rb[e * THREADS]);
+#pragma unroll
+            for (int e = 0; e < E; ++e) last[e] = scratch[e * THREADS];
         } else {
-            const T *ra = tab + p.a[s] * (E * THREADS);
+            T x[E], y[E];
+            if (f & A_PREV) {
 #pragma unroll
-            for (int e = 0; e < E; ++e) x[e] = ra[e * THREADS];
+                for (int e = 0; e < E; ++e) x[e] = last[e];
+            } else {
+                const T *ra = tab + p.a[s] * (E * THREADS);
+#pragma unroll
+                for (int e = 0; e < E; ++e) x[e] = ra[e * THREADS];
+            }
+            if (f & B_PREV) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) y[e] = last[e];
+            } else {
+                const T *rb = tab + p.b[s] * (E * THREADS);
+#pragma unroll
+                for (int e = 0; e < E; ++e) y[e] = rb[e * THREADS];
+            }
+            apply_light<T, E>(p.op[s], x, y, last);
         }
-        if (f & B_PREV) {
-#pragma unroll
-            for (int e = 0; e < E; ++e) y[e] = last[e];
-        } else {
-            const T *rb = tab + p.b[s] * (E * THREADS);
-#pragma unroll
-            for (int e = 0; e < E; ++e) y[e] = rb[e * THREADS];
-        }
-        apply<T, E>(p.op[s], x, y, last);
         if (f & STORE) {
             T *rr = tab + p.row[s] * (E * THREADS);
 #pragma unroll
@@ -245,38 +277,44 @@ __device__ __forceinline__ void decode(const Program &p, int64_t i, Off<MODE> (&
     }
 }
 
-// Load E elements of every input, then run the chain; `last` receives the
-// group's value at the E elements.  Input k's elements sit at off[k] +
-// e * stride[k][axis] (e * dense_step when MODE is dense).  VEC: inputs in
-// vec_mask are read as aligned 16-byte vectors (unit stride).
-template <typename T, int E, bool VEC, int MODE>
-__device__ __forceinline__ void load_run(const Program &p, const Off<MODE> (&off)[MAX_INPUTS],
-                                         int axis, Off<MODE> dense_step, T *tab, T (&last)[E]) {
+// Load G groups of W elements of every input, then run the chain; `last`
+// receives the group's value at the G*W elements (group g's element e at
+// g*W + e).  Input k's group g starts at off[g][k], its elements e *
+// stride[k][axis] apart (e * dense_step when MODE is dense).  VEC: inputs in
+// vec_mask read a group as one aligned 16-byte vector (W*sizeof(T) == 16).
+template <typename T, int G, int W, bool VEC, int MODE>
+__device__ __forceinline__ void load_run(const Program &p, const Off<MODE> (&off)[G][MAX_INPUTS],
+                                         int axis, Off<MODE> dense_step, T *tab, T (&last)[G * W]) {
+    constexpr int E = G * W;
 #pragma unroll
     for (int k = 0; k < MAX_INPUTS; ++k) {
         if (k >= p.n_inputs) break;
-        const T *src = static_cast<const T *>(p.in[k]) + off[k];
         const Off<MODE> st = MODE == DENSE ? dense_step : static_cast<Off<MODE>>(p.stride[k][axis]);
+        constexpr int Q = W * sizeof(T) / 16;  // 16-byte vectors per group
+        const bool vec = VEC && Q > 0 && ((p.vec_mask >> k) & 1);
         T v[E];
-        if constexpr (VEC && E * sizeof(T) >= 16) {
-            if ((p.vec_mask >> k) & 1) {
 #pragma unroll
-                for (int q = 0; q < E * static_cast<int>(sizeof(T)) / 16; ++q) {
-                    if constexpr (sizeof(T) == 4) {
-                        const float4 w = __ldg(reinterpret_cast<const float4 *>(src) + q);
-                        v[4 * q] = w.x, v[4 * q + 1] = w.y, v[4 * q + 2] = w.z, v[4 * q + 3] = w.w;
-                    } else {
-                        const double2 w = __ldg(reinterpret_cast<const double2 *>(src) + q);
-                        v[2 * q] = w.x, v[2 * q + 1] = w.y;
+        for (int g = 0; g < G; ++g) {
+            const T *src = static_cast<const T *>(p.in[k]) + off[g][k];
+            if constexpr (VEC && Q > 0 && W * sizeof(T) == Q * 16) {
+                if (vec) {
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) {
+                        if constexpr (sizeof(T) == 4) {
+                            const float4 w = __ldg(reinterpret_cast<const float4 *>(src) + q);
+                            T *d = v + g * W + 4 * q;
+                            d[0] = w.x, d[1] = w.y, d[2] = w.z, d[3] = w.w;
+                        } else {
+                            const double2 w = __ldg(reinterpret_cast<const double2 *>(src) + q);
+                            T *d = v + g * W + 2 * q;
+                            d[0] = w.x, d[1] = w.y;
+                        }
                     }
+                    continue;
                 }
-            } else {
-#pragma unroll
-                for (int e = 0; e < E; ++e) v[e] = __ldg(src + e * st);
             }
-        } else {
 #pragma unroll
-            for (int e = 0; e < E; ++e) v[e] = __ldg(src + e * st);
+            for (int e = 0; e < W; ++e) v[g * W + e] = __ldg(src + e * st);
         }
         T *row = tab + k * (E * THREADS);
 #pragma unroll
@@ -285,43 +323,66 @@ __device__ __forceinline__ void load_run(const Program &p, const Off<MODE> (&off
     run_steps<T, E>(p, tab, last);
 }
 
-// Elementwise: thread t takes the chunk of E consecutive flat indices
-// starting at E*t (E divides the innermost extent when MODE is strided, so a
-// chunk never crosses a row); the ragged end (dense only) one by one.
-template <typename T, int MODE, int E>
+template <typename T, int W>
+__device__ __forceinline__ void store_group(T *dst, const T *r) {
+    if constexpr (W * sizeof(T) % 16 == 0) {
+#pragma unroll
+        for (int q = 0; q < static_cast<int>(W * sizeof(T) / 16); ++q) {
+            if constexpr (sizeof(T) == 4)
+                reinterpret_cast<float4 *>(dst)[q] = make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            else
+                reinterpret_cast<double2 *>(dst)[q] = make_double2(r[2 * q], r[2 * q + 1]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < W; ++e) dst[e] = r[e];
+    }
+}
+
+// Elementwise.  W = 16 bytes of elements (W = 1: one element at a time).
+// A warp takes 32*G consecutive W-element vectors at once, lane l the
+// vectors l, l+32, ...: each load instruction of the warp reads 512
+// contiguous bytes, and G loads per input are in flight per thread.  When
+// MODE is strided, W divides the innermost extent, so a vector never
+// crosses a row.  Leftover vectors go one per thread, then (dense only) the
+// ragged end element by element.
+template <typename T, int MODE, int G, int W>
 __global__ void __launch_bounds__(THREADS) elementwise_kernel(Program p, T *__restrict__ out) {
     extern __shared__ __align__(16) unsigned char fused_smem[];
     T *tab = reinterpret_cast<T *>(fused_smem) + threadIdx.x;
-    const int axis = p.rank > 0 ? p.rank - 1 : 0;  // a chunk runs along the innermost axis
-    const int64_t chunks = p.total / E;
-    const int64_t gstride = static_cast<int64_t>(gridDim.x) * THREADS;
+    const int axis = p.rank > 0 ? p.rank - 1 : 0;  // a vector runs along the innermost axis
+    const int lane = threadIdx.x & 31;
+    const int64_t n_vec = p.total / W;
+    const int64_t n_wc = n_vec / (32 * G);
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (THREADS / 32);
+    const int64_t gwarp = static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + (threadIdx.x >> 5);
+    for (int64_t wc = gwarp; wc < n_wc; wc += warps) {
+        Off<MODE> off[G][MAX_INPUTS];
+#pragma unroll
+        for (int g = 0; g < G; ++g) decode<MODE>(p, (wc * (32 * G) + g * 32 + lane) * W, off[g]);
+        T r[G * W];
+        load_run<T, G, W, true, MODE>(p, off, axis, 1, tab, r);
+#pragma unroll
+        for (int g = 0; g < G; ++g) store_group<T, W>(out + (wc * (32 * G) + g * 32 + lane) * W, r + g * W);
+    }
     const int64_t gtid = static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x;
-    for (int64_t c = gtid; c < chunks; c += gstride) {
-        Off<MODE> off[MAX_INPUTS];
-        decode<MODE>(p, c * E, off);
-        T r[E];
-        load_run<T, E, true, MODE>(p, off, axis, 1, tab, r);
-        if constexpr (E * sizeof(T) >= 16) {
-#pragma unroll
-            for (int q = 0; q < E * static_cast<int>(sizeof(T)) / 16; ++q) {
-                if constexpr (sizeof(T) == 4)
-                    reinterpret_cast<float4 *>(out + c * E)[q] =
-                        make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-                else
-                    reinterpret_cast<double2 *>(out + c * E)[q] = make_double2(r[2 * q], r[2 * q + 1]);
-            }
-        } else {
-#pragma unroll
-            for (int e = 0; e < E; ++e) out[c * E + e] = r[e];
+    {
+        const int64_t v = n_wc * (32 * G) + gtid;
+        if (v < n_vec) {
+            Off<MODE> off[1][MAX_INPUTS];
+            decode<MODE>(p, v * W, off[0]);
+            T r[W];
+            load_run<T, 1, W, true, MODE>(p, off, axis, 1, tab, r);
+            store_group<T, W>(out + v * W, r);
         }
     }
-    if (E > 1) {
-        const int64_t i = chunks * E + gtid;
+    if (W > 1) {
+        const int64_t i = n_vec * W + gtid;
         if (i < p.total) {
-            Off<MODE> off[MAX_INPUTS];
-            decode<MODE>(p, i, off);
+            Off<MODE> off[1][MAX_INPUTS];
+            decode<MODE>(p, i, off[0]);
             T r[1];
-            load_run<T, 1, false, MODE>(p, off, axis, 1, tab, r);
+            load_run<T, 1, 1, false, MODE>(p, off, axis, 1, tab, r);
             out[i] = r[0];
         }
     }
@@ -334,16 +395,16 @@ struct Span {
 // Carry-tree push of one leaf (emit.rs emit_carry_tree_push :8129): leaf
 // `count` first combines with the completed subtrees its trailing one bits
 // name, the earlier subtree on the left.
-template <typename T>
-__device__ __forceinline__ void carry_push(T (&level)[48], int64_t &count, T leaf) {
+template <typename T, int N>
+__device__ __forceinline__ void carry_push(T (&level)[N], int64_t &count, T leaf) {
     int depth = 0;
     for (int64_t pending = count++; pending & 1; pending >>= 1, ++depth) leaf = level[depth] + leaf;
     level[depth] = leaf;
 }
 // Carry-tree total (emit_carry_tree_total :8179) started from `total`
 // (valid when `found`): the levels from the lowest up, each on the left.
-template <typename T>
-__device__ __forceinline__ T carry_total(const T (&level)[48], int64_t count, T total, bool found) {
+template <typename T, int N>
+__device__ __forceinline__ T carry_total(const T (&level)[N], int64_t count, T total, bool found) {
     int depth = 0;
     for (int64_t remaining = count; remaining; remaining >>= 1, ++depth)
         if (remaining & 1) {
@@ -359,108 +420,145 @@ __device__ __forceinline__ void max_push(T &best, bool &nan, T v) {
     if (isnan(v)) nan = true;
     else if (!(best > v)) best = v;
 }
+// Pair tree over n aligned leaves held in registers (n a power of two).
+template <typename T, int N>
+__device__ __forceinline__ T reg_tree(T (&r)[N]) {
+#pragma unroll
+    for (int width = 1; width < N; width <<= 1)
+#pragma unroll
+        for (int i = 0; i + width < N; i += 2 * width) r[i] = r[i] + r[i + width];
+    return r[0];
+}
 
 // Reduction over the last axis (inner extent 1, so the axis's leaves are
-// consecutive flat indices): one warp per span.  A pass
-// covers 32*E consecutive leaves, lane l the aligned group [l*E, l*E + E),
-// whose pair tree and then the warp's butterfly give one aligned subtree of
-// 32*E leaves, pushed as a leaf of the carry tree above it; a ragged last
-// pass is the tree's lowest part and starts the total.  Max keeps, per
-// lane, the maximum and the last index holding it.
-template <typename T, int MODE, int E>
+// consecutive flat indices): one warp per span.  A pass covers 32*W
+// consecutive leaves, lane l the aligned group [l*W, l*W + W): its pair
+// tree, then the warp's butterfly, give the aligned subtree of the pass.
+// G passes are loaded together and their subtrees paired in registers into
+// one aligned subtree of G*32*W leaves, a leaf of the span's carry tree.
+// What remains after the last such block, fewer than G*32*W leaves, is the
+// tree's lowest part: its own passes (a small carry tree, then a ragged
+// pass) give the value the total starts from.  Max keeps, per lane, the
+// maximum and the last index holding it.
+template <typename T, int MODE, int G, int W>
 __global__ void __launch_bounds__(THREADS)
     reduce_last_kernel(Program p, int axis, int kind, Span sp, int64_t spans, T *__restrict__ out) {
     extern __shared__ __align__(16) unsigned char fused_smem[];
     T *tab = reinterpret_cast<T *>(fused_smem) + threadIdx.x;
     const int lane = threadIdx.x & 31;
+    constexpr int PASS = 32 * W, BLOCK = G * PASS;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (THREADS / 32);
     for (int64_t w = static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + (threadIdx.x >> 5); w < spans;
          w += warps) {
-        const int64_t o = w / sp.nseg, g = w % sp.nseg;
-        const int64_t j0 = g * sp.seg;
+        const int64_t o = w / sp.nseg, g0 = w % sp.nseg;
+        const int64_t j0 = g0 * sp.seg;
         const int64_t n = (sp.len - j0) < sp.seg ? (sp.len - j0) : sp.seg;
         Off<MODE> base[MAX_INPUTS];
         decode<MODE>(p, o * sp.len + j0, base);
-        auto leaves_at = [&](int64_t j, auto &r) {  // evaluate the leaves from j on
-            constexpr int EE = sizeof(r) / sizeof(T);
-            Off<MODE> off[MAX_INPUTS];
+        // the group of W leaves from leaf j of the span, for each input
+        auto group_off = [&](int64_t j, Off<MODE> (&off)[MAX_INPUTS]) {
 #pragma unroll
             for (int k = 0; k < MAX_INPUTS; ++k)
                 off[k] = base[k] + static_cast<Off<MODE>>(j) *
                                        (MODE == DENSE ? 1 : static_cast<Off<MODE>>(p.stride[k][axis]));
-            load_run<T, EE, false, MODE>(p, off, axis, 1, tab, r);
         };
         T result;
         if (kind == CHELIS_FUSED_REDUCE_SUM) {
             T level[48];
             int64_t count = 0;
+            int64_t c0 = 0;
+            for (; c0 + BLOCK <= n; c0 += BLOCK) {
+                Off<MODE> off[G][MAX_INPUTS];
+#pragma unroll
+                for (int g = 0; g < G; ++g) group_off(c0 + g * PASS + lane * W, off[g]);
+                T r[G * W];
+                load_run<T, G, W, true, MODE>(p, off, axis, 1, tab, r);
+                T pass[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    T q[W];
+#pragma unroll
+                    for (int e = 0; e < W; ++e) q[e] = r[g * W + e];
+                    pass[g] = warp_tree_full(reg_tree(q));
+                }
+                carry_push(level, count, reg_tree(pass));
+            }
+            // the lowest part: full passes into a small carry tree, then a ragged pass
+            T low[8];
+            int64_t low_count = 0;
             T tail = T(0);
             bool has_tail = false;
-            for (int64_t c0 = 0; c0 < n; c0 += 32 * E) {
+            for (; c0 < n; c0 += PASS) {
                 const int64_t left = n - c0;
-                const int64_t mine = left - lane * E;  // this lane's valid leaves, clamped below
-                T s;
+                const int64_t mine = left - lane * W;  // this lane's valid leaves
+                T q[W];
                 bool valid;
-                if (left >= 32 * E) {
-                    T r[E];
-                    leaves_at(c0 + lane * E, r);
-#pragma unroll
-                    for (int width = 1; width < E; width <<= 1)
-#pragma unroll
-                        for (int i = 0; i + width < E; i += 2 * width) r[i] = r[i] + r[i + width];
-                    s = r[0];
+                if (left >= PASS) {
+                    Off<MODE> off[1][MAX_INPUTS];
+                    group_off(c0 + lane * W, off[0]);
+                    load_run<T, 1, W, true, MODE>(p, off, axis, 1, tab, q);
+                    reg_tree(q);
                     valid = true;
                 } else {
-                    T r[E];
 #pragma unroll
-                    for (int e = 0; e < E; ++e) {
-                        r[e] = T(0);
+                    for (int e = 0; e < W; ++e) {
+                        q[e] = T(0);
                         if (e < mine) {
+                            Off<MODE> off[1][MAX_INPUTS];
+                            group_off(c0 + lane * W + e, off[0]);
                             T one[1];
-                            leaves_at(c0 + lane * E + e, one);
-                            r[e] = one[0];
+                            load_run<T, 1, 1, false, MODE>(p, off, axis, 1, tab, one);
+                            q[e] = one[0];
                         }
                     }
 #pragma unroll
-                    for (int width = 1; width < E; width <<= 1)
+                    for (int width = 1; width < W; width <<= 1)
 #pragma unroll
-                        for (int i = 0; i + width < E; i += 2 * width)
-                            r[i] = tree_pair(r[i], i < mine, r[i + width], i + width < mine);
-                    s = r[0];
+                        for (int i = 0; i + width < W; i += 2 * width)
+                            q[i] = tree_pair(q[i], i < mine, q[i + width], i + width < mine);
                     valid = mine > 0;
                 }
-                const bool full = left >= 32 * E;
-                s = warp_tree(s, valid);
+                T s = warp_tree(q[0], valid);
                 s = __shfl_sync(0xffffffffu, s, 0);
-                if (full) {
-                    carry_push(level, count, s);
+                if (left >= PASS) {
+                    carry_push(low, low_count, s);
                 } else {
                     tail = s;
                     has_tail = true;
                 }
             }
-            result = carry_total(level, count, tail, has_tail);
+            const bool has_low = low_count > 0 || has_tail;
+            const T low_total = carry_total(low, low_count, tail, has_tail);
+            result = carry_total(level, count, low_total, has_low);
             if (sp.nseg == 1) result = canon_nan(result);
         } else {
             T best = -INFINITY;
             int64_t at = -1;
             bool nan = false;
-            for (int64_t c0 = 0; c0 < n; c0 += 32 * E) {
-                const int64_t mine = n - c0 - lane * E;
-                if (mine >= E) {
-                    T r[E];
-                    leaves_at(c0 + lane * E, r);
+            auto take = [&](T v, int64_t j) {
+                if (isnan(v)) nan = true;
+                else if (!(best > v)) { best = v; at = j; }
+            };
+            int64_t c0 = 0;
+            for (; c0 + BLOCK <= n; c0 += BLOCK) {
+                Off<MODE> off[G][MAX_INPUTS];
 #pragma unroll
-                    for (int e = 0; e < E; ++e)
-                        if (isnan(r[e])) nan = true;
-                        else if (!(best > r[e])) { best = r[e]; at = c0 + lane * E + e; }
-                } else {
-                    for (int e = 0; e < mine; ++e) {
-                        T one[1];
-                        leaves_at(c0 + lane * E + e, one);
-                        if (isnan(one[0])) nan = true;
-                        else if (!(best > one[0])) { best = one[0]; at = c0 + lane * E + e; }
-                    }
+                for (int g = 0; g < G; ++g) group_off(c0 + g * PASS + lane * W, off[g]);
+                T r[G * W];
+                load_run<T, G, W, true, MODE>(p, off, axis, 1, tab, r);
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+#pragma unroll
+                    for (int e = 0; e < W; ++e) take(r[g * W + e], c0 + g * PASS + lane * W + e);
+            }
+            for (; c0 < n; c0 += PASS) {
+                const int64_t mine = n - c0 - lane * W;
+                for (int e = 0; e < W && e < mine; ++e) {
+                    Off<MODE> off[1][MAX_INPUTS];
+                    group_off(c0 + lane * W + e, off[0]);
+                    T one[1];
+                    load_run<T, 1, 1, false, MODE>(p, off, axis, 1, tab, one);
+                    take(one[0], c0 + lane * W + e);
                 }
             }
             nan = __any_sync(0xffffffffu, nan);
@@ -479,6 +577,9 @@ __global__ void __launch_bounds__(THREADS)
 // Reduction over a leading axis (inner extent > 1): one thread per span,
 // walking its leaves in order, E at a time (E loads in flight); neighbouring
 // threads take neighbouring inner indices, so each load is a coalesced row.
+// A span starts at an aligned leaf, so each E leaves form an aligned
+// subtree, paired in registers and pushed as one carry-tree leaf; the last
+// n mod E leaves are the tree's lowest part.
 template <typename T, int MODE, int E>
 __global__ void __launch_bounds__(THREADS)
     reduce_inner_kernel(Program p, int axis, int kind, Span sp, int64_t spans, T *__restrict__ out) {
@@ -507,27 +608,39 @@ __global__ void __launch_bounds__(THREADS)
         bool nan = false;
         int64_t j = 0;
         for (; j + E <= n; j += E) {
-            Off<MODE> off[MAX_INPUTS];
-            at(j, off);
+            Off<MODE> off[1][MAX_INPUTS];
+            at(j, off[0]);
             T r[E];
-            load_run<T, E, false, MODE>(p, off, axis, dense_step, tab, r);
+            load_run<T, 1, E, false, MODE>(p, off, axis, dense_step, tab, r);
+            if (kind == CHELIS_FUSED_REDUCE_SUM) {
+                carry_push(level, count, reg_tree(r));
+            } else {
 #pragma unroll
-            for (int e = 0; e < E; ++e) {
-                if (kind == CHELIS_FUSED_REDUCE_SUM) carry_push(level, count, r[e]);
-                else max_push(best, nan, r[e]);
+                for (int e = 0; e < E; ++e) max_push(best, nan, r[e]);
             }
         }
-        for (; j < n; ++j) {
-            Off<MODE> off[MAX_INPUTS];
-            at(j, off);
-            T r[1];
-            load_run<T, 1, false, MODE>(p, off, axis, dense_step, tab, r);
-            if (kind == CHELIS_FUSED_REDUCE_SUM) carry_push(level, count, r[0]);
-            else max_push(best, nan, r[0]);
+        T r[E];
+        const int rest = static_cast<int>(n - j);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            r[e] = T(0);
+            if (e < rest) {
+                Off<MODE> off[1][MAX_INPUTS];
+                at(j + e, off[0]);
+                T one[1];
+                load_run<T, 1, 1, false, MODE>(p, off, axis, dense_step, tab, one);
+                r[e] = one[0];
+                if (kind != CHELIS_FUSED_REDUCE_SUM) max_push(best, nan, one[0]);
+            }
         }
         T result;
         if (kind == CHELIS_FUSED_REDUCE_SUM) {
-            result = carry_total(level, count, T(0), false);
+#pragma unroll
+            for (int width = 1; width < E; width <<= 1)
+#pragma unroll
+                for (int i = 0; i + width < E; i += 2 * width)
+                    r[i] = tree_pair(r[i], i < rest, r[i + width], i + width < rest);
+            result = carry_total(level, count, r[0], rest > 0);
             if (sp.nseg == 1) result = canon_nan(result);
         } else {
             result = nan ? canon_nan(T(NAN)) : best;
@@ -536,28 +649,80 @@ __global__ void __launch_bounds__(THREADS)
     }
 }
 
-// Combine the segment results of each output in segment order: full
-// segments are carry-tree leaves at the segment's level, a ragged last
-// segment is the tree's lowest part; Max folds chelis_fmax_propnan.
+// Combine the segment results of each output: one CTA per output.  The
+// segments are aligned subtrees of the output's tree (a ragged last one is
+// its lowest part), so Sum is the canonical pair tree over the segment
+// values: thread t folds the aligned run of c segments from t*c through a
+// carry tree, then the runs pair up across lanes and warps.  Max folds
+// chelis_fmax_propnan in segment order (the later of equal values wins).
+constexpr int FINISH_THREADS = 256;
 template <typename T>
-__global__ void finish_kernel(const T *__restrict__ part, int kind, Span sp, int64_t outputs,
-                              T *__restrict__ out) {
-    for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < outputs;
-         o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const T *seg = part + o * sp.nseg;
+__global__ void __launch_bounds__(FINISH_THREADS)
+    finish_kernel(const T *__restrict__ part, int kind, Span sp, int64_t outputs, T *__restrict__ out) {
+    __shared__ T red_v[FINISH_THREADS / 32];
+    __shared__ long long red_i[FINISH_THREADS / 32];
+    __shared__ int red_f[FINISH_THREADS / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t n = sp.nseg;
+    int64_t c = 1;
+    while (c * FINISH_THREADS < n) c <<= 1;
+    for (int64_t o = blockIdx.x; o < outputs; o += gridDim.x) {
+        const T *seg = part + o * n;
+        const int64_t lo = threadIdx.x * c, hi = lo + c < n ? lo + c : n;
         if (kind == CHELIS_FUSED_REDUCE_SUM) {
-            const bool ragged = (sp.len % sp.seg) != 0;
-            const int64_t full = ragged ? sp.nseg - 1 : sp.nseg;
             T level[48];
             int64_t count = 0;
-            for (int64_t g = 0; g < full; ++g) carry_push(level, count, seg[g]);
-            out[o] = canon_nan(carry_total(level, count, ragged ? seg[full] : T(0), ragged));
+            for (int64_t g = lo; g < hi; ++g) carry_push(level, count, seg[g]);
+            bool valid = lo < n;
+            T v = warp_tree(carry_total(level, count, T(0), false), valid);
+            if (lane == 0) {
+                red_v[warp] = v;
+                red_f[warp] = valid;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                bool wv = lane < FINISH_THREADS / 32 && red_f[lane];
+                T w = wv ? red_v[lane] : T(0);
+                w = warp_tree(w, wv);
+                if (lane == 0) out[o] = canon_nan(w);
+            }
         } else {
-            T acc = -INFINITY;
+            T best = -INFINITY;
+            long long at = -1;
             bool nan = false;
-            for (int64_t g = 0; g < sp.nseg; ++g) max_push(acc, nan, seg[g]);
-            out[o] = nan ? canon_nan(T(NAN)) : acc;
+            for (int64_t g = lo; g < hi; ++g) {
+                const T v = seg[g];
+                if (isnan(v)) nan = true;
+                else if (!(best > v)) { best = v; at = g; }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const T ob = __shfl_xor_sync(0xffffffffu, best, off);
+                const long long oa = __shfl_xor_sync(0xffffffffu, at, off);
+                if (ob > best || (ob == best && oa > at)) { best = ob; at = oa; }
+            }
+            nan = __any_sync(0xffffffffu, nan);
+            if (lane == 0) {
+                red_v[warp] = best;
+                red_i[warp] = at;
+                red_f[warp] = nan;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                const bool in = lane < FINISH_THREADS / 32;
+                T b = in ? red_v[lane] : T(-INFINITY);
+                long long i = in ? red_i[lane] : -1;
+                const bool any_nan = __any_sync(0xffffffffu, in && red_f[lane]);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const T ob = __shfl_xor_sync(0xffffffffu, b, off);
+                    const long long oi = __shfl_xor_sync(0xffffffffu, i, off);
+                    if (ob > b || (ob == b && oi > i)) { b = ob; i = oi; }
+                }
+                if (lane == 0) out[o] = any_nan ? canon_nan(T(NAN)) : b;
+            }
         }
+        __syncthreads();
     }
 }
 
@@ -613,6 +778,12 @@ int build_program(fused::Program &p, int &mode, const chelis_fused_step *steps, 
         if (!valid(steps[s].a) || (binary && !valid(steps[s].b)))
             return set_error(CHELIS_CUDA_ERR_DOMAIN, "fused step %d: operand out of range", s);
         p.op[s] = static_cast<uint8_t>(op);
+        switch (op) {  // libm calls with a large register or local-memory footprint
+            case CHELIS_FUSED_POW: case CHELIS_FUSED_SIN: case CHELIS_FUSED_COS: case CHELIS_FUSED_TAN:
+                p.flags[s] |= HEAVY;
+                break;
+            default: break;
+        }
     }
     // Operands: an input's row is its index; the step just before is
     // forwarded in registers; any other step is read from its row, which only
@@ -645,17 +816,13 @@ int build_program(fused::Program &p, int &mode, const chelis_fused_step *steps, 
             return set_error(CHELIS_CUDA_ERR_DOMAIN, "fused input %d is misaligned", k);
         p.in[k] = inputs[k];
         int64_t expect = 1, span = 0;
-        bool vec = (reinterpret_cast<uintptr_t>(inputs[k]) % 16) == 0 && rank > 0 &&
-                   (shape[rank - 1] == 1 || strides[k * rank + rank - 1] == 1);
         for (int d = rank - 1; d >= 0; --d) {
             const int64_t st = strides[k * rank + d];
             p.stride[k][d] = st;
             if (shape[d] > 1 && st != expect) dense = false;
             if (shape[d] > 0) span += (st < 0 ? -st : st) * (shape[d] - 1);
-            if (d < rank - 1 && shape[d] > 1 && st % 4 != 0) vec = false;
             expect *= shape[d];
         }
-        if (vec) p.vec_mask |= 1 << k;
         if (span > reach) reach = span;
     }
     const int64_t lim = int64_t(1) << 31;
@@ -674,84 +841,109 @@ unsigned grid_of(int64_t units, int per_block) {
 // Shared-memory table for E elements per thread; E = 4 when it fits the
 // default 48 KiB, else 1.
 size_t table_bytes(const fused::Program &p, size_t elem, int e) {
-    return static_cast<size_t>(p.n_rows) * e * fused::THREADS * elem;
+    return static_cast<size_t>(p.n_rows + 1) * e * fused::THREADS * elem;  // + the scratch row
 }
 bool table_fits(const fused::Program &p, size_t elem, int e) { return table_bytes(p, elem, e) <= 48 * 1024; }
-int pick_e(const fused::Program &p, size_t elem) { return table_fits(p, elem, 4) ? 4 : 1; }
 
-template <typename T, int MODE, int E>
+// Inputs that may be read as aligned 16-byte vectors of W elements running
+// along `axis` (unit stride there, every other stride a multiple of W, base
+// aligned): a vector then never straddles a row of another axis.
+int32_t vector_inputs(const fused::Program &p, int mode, int axis, int w) {
+    int32_t mask = 0;
+    for (int k = 0; k < p.n_inputs; ++k) {
+        bool ok = reinterpret_cast<uintptr_t>(p.in[k]) % 16 == 0 && p.rank > 0;
+        if (mode == fused::DENSE) {
+            int64_t inner = 1;  // elements from one axis step to the next
+            for (int d = axis + 1; d < p.rank; ++d) inner *= p.shape[d];
+            ok = ok && inner == 1;
+        } else {
+            ok = ok && p.stride[k][axis] == 1;
+            for (int d = 0; d < p.rank; ++d)
+                if (d != axis && p.shape[d] > 1 && p.stride[k][d] % w != 0) ok = false;
+        }
+        if (ok) mask |= 1 << k;
+    }
+    return mask;
+}
+
+template <typename T, int MODE, int G, int W>
 void launch_ew(const fused::Program &p, T *out, cudaStream_t s) {
-    const size_t smem = table_bytes(p, sizeof(T), E);
-    fused::elementwise_kernel<T, MODE, E>
-        <<<grid_of((p.total + E - 1) / E, fused::THREADS), fused::THREADS, smem, s>>>(p, out);
+    const size_t smem = table_bytes(p, sizeof(T), G * W);
+    const int64_t units = p.total / W / (32 * G) * 32 + 128;  // threads of the main loop + leftovers
+    fused::elementwise_kernel<T, MODE, G, W>
+        <<<grid_of(units, fused::THREADS), fused::THREADS, smem, s>>>(p, out);
+}
+
+template <typename T, int G, int W>
+void launch_ew_mode(const fused::Program &p, int mode, T *out, cudaStream_t s) {
+    using namespace fused;
+    if (mode == DENSE) launch_ew<T, DENSE, G, W>(p, out, s);
+    else if (mode == STRIDED32) launch_ew<T, STRIDED32, G, W>(p, out, s);
+    else launch_ew<T, STRIDED64, G, W>(p, out, s);
 }
 
 template <typename T>
 int launch_elementwise(fused::Program &p, int mode, T *out, cudaStream_t s) {
     using namespace fused;
-    // 32 bytes of every input per thread and chunk (E = 8 f32 / 4 f64) when
-    // the table fits; a strided chunk must not cross a row of the iteration
-    // shape, and the vector store wants an aligned output
-    int e = 1;
-    for (int cand : {static_cast<int>(32 / sizeof(T)), 4}) {
-        if (e == 1 && table_fits(p, sizeof(T), cand) &&
-            (mode == DENSE || (p.rank > 0 && p.shape[p.rank - 1] % cand == 0)))
-            e = cand;
-    }
-    if (reinterpret_cast<uintptr_t>(out) % 16 != 0) e = 1;
-    if (mode == DENSE && e > 1) {
-        for (int k = 0; k < p.n_inputs; ++k)  // dense inputs: vector reads when aligned
-            if (reinterpret_cast<uintptr_t>(p.in[k]) % 16 == 0) p.vec_mask |= 1 << k;
-            else p.vec_mask &= ~(1 << k);
-    }
-    if (e == 8) {
-        if constexpr (sizeof(T) == 4) {
-            if (mode == DENSE) launch_ew<T, DENSE, 8>(p, out, s);
-            else if (mode == STRIDED32) launch_ew<T, STRIDED32, 8>(p, out, s);
-            else launch_ew<T, STRIDED64, 8>(p, out, s);
-        }
-    } else if (e == 4) {
-        if (mode == DENSE) launch_ew<T, DENSE, 4>(p, out, s);
-        else if (mode == STRIDED32) launch_ew<T, STRIDED32, 4>(p, out, s);
-        else launch_ew<T, STRIDED64, 4>(p, out, s);
-    } else {
-        if (mode == DENSE) launch_ew<T, DENSE, 1>(p, out, s);
-        else if (mode == STRIDED32) launch_ew<T, STRIDED32, 1>(p, out, s);
-        else launch_ew<T, STRIDED64, 1>(p, out, s);
-    }
+    // 16-byte vectors of W elements along the innermost axis (a strided
+    // vector must not cross a row), two per thread when the table fits
+    constexpr int W = 16 / sizeof(T);
+    const bool vec_ok = reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                        (mode == DENSE || (p.rank > 0 && p.shape[p.rank - 1] % W == 0));
+    p.vec_mask = vec_ok ? vector_inputs(p, mode, p.rank > 0 ? p.rank - 1 : 0, W) : 0;
+    if (vec_ok && table_fits(p, sizeof(T), 2 * W)) launch_ew_mode<T, 2, W>(p, mode, out, s);
+    else if (vec_ok && table_fits(p, sizeof(T), W)) launch_ew_mode<T, 1, W>(p, mode, out, s);
+    else launch_ew_mode<T, 1, 1>(p, mode, out, s);
     g_launches++;
     CHELIS_LAUNCH_CHECK("fused::elementwise_kernel");
     return CHELIS_CUDA_OK;
 }
 
-template <typename T, int MODE, int E>
-void launch_red(const fused::Program &p, int axis, int kind, fused::Span sp, int64_t spans, T *dst,
-                cudaStream_t s) {
+template <typename T, int MODE, int G, int W>
+void launch_last(const fused::Program &p, int axis, int kind, fused::Span sp, int64_t spans, T *dst,
+                 cudaStream_t s) {
     using namespace fused;
-    const size_t smem = table_bytes(p, sizeof(T), E);
-    if (sp.inner == 1)
-        reduce_last_kernel<T, MODE, E>
-            <<<grid_of(spans, THREADS / 32), THREADS, smem, s>>>(p, axis, kind, sp, spans, dst);
-    else
-        reduce_inner_kernel<T, MODE, E>
-            <<<grid_of(spans, THREADS), THREADS, smem, s>>>(p, axis, kind, sp, spans, dst);
+    reduce_last_kernel<T, MODE, G, W><<<grid_of(spans, THREADS / 32), THREADS,
+                                        table_bytes(p, sizeof(T), G * W), s>>>(p, axis, kind, sp, spans,
+                                                                               dst);
+}
+
+template <typename T, int MODE, int E>
+void launch_inner(const fused::Program &p, int axis, int kind, fused::Span sp, int64_t spans, T *dst,
+                  cudaStream_t s) {
+    using namespace fused;
+    reduce_inner_kernel<T, MODE, E><<<grid_of(spans, THREADS), THREADS, table_bytes(p, sizeof(T), E),
+                                      s>>>(p, axis, kind, sp, spans, dst);
+}
+
+template <typename T, int MODE>
+void launch_red(fused::Program &p, int axis, int kind, fused::Span sp, int64_t spans, T *dst,
+                cudaStream_t s) {
+    constexpr int W = 16 / sizeof(T);
+    if (sp.inner == 1) {
+        // groups of W leaves along the axis; vectors where the axis has unit
+        // stride and the rows start aligned
+        const bool rows_aligned = MODE != fused::DENSE || sp.len % W == 0;
+        p.vec_mask = rows_aligned ? vector_inputs(p, MODE, axis, W) : 0;
+        if (table_fits(p, sizeof(T), 4 * W)) launch_last<T, MODE, 4, W>(p, axis, kind, sp, spans, dst, s);
+        else if (table_fits(p, sizeof(T), W)) launch_last<T, MODE, 1, W>(p, axis, kind, sp, spans, dst, s);
+        else launch_last<T, MODE, 1, 1>(p, axis, kind, sp, spans, dst, s);
+    } else {
+        p.vec_mask = 0;
+        constexpr int E = 32 / sizeof(T);  // leaves in flight per thread
+        if (table_fits(p, sizeof(T), E)) launch_inner<T, MODE, E>(p, axis, kind, sp, spans, dst, s);
+        else launch_inner<T, MODE, 1>(p, axis, kind, sp, spans, dst, s);
+    }
 }
 
 template <typename T>
-int launch_reduce(const fused::Program &p, int mode, int axis, int kind, fused::Span sp,
-                  int64_t outputs, T *dst, cudaStream_t s) {
+int launch_reduce(fused::Program p, int mode, int axis, int kind, fused::Span sp, int64_t outputs,
+                  T *dst, cudaStream_t s) {
     using namespace fused;
     const int64_t spans = outputs * sp.nseg;
-    const int e = pick_e(p, sizeof(T));
-    if (e == 4) {
-        if (mode == DENSE) launch_red<T, DENSE, 4>(p, axis, kind, sp, spans, dst, s);
-        else if (mode == STRIDED32) launch_red<T, STRIDED32, 4>(p, axis, kind, sp, spans, dst, s);
-        else launch_red<T, STRIDED64, 4>(p, axis, kind, sp, spans, dst, s);
-    } else {
-        if (mode == DENSE) launch_red<T, DENSE, 1>(p, axis, kind, sp, spans, dst, s);
-        else if (mode == STRIDED32) launch_red<T, STRIDED32, 1>(p, axis, kind, sp, spans, dst, s);
-        else launch_red<T, STRIDED64, 1>(p, axis, kind, sp, spans, dst, s);
-    }
+    if (mode == DENSE) launch_red<T, DENSE>(p, axis, kind, sp, spans, dst, s);
+    else if (mode == STRIDED32) launch_red<T, STRIDED32>(p, axis, kind, sp, spans, dst, s);
+    else launch_red<T, STRIDED64>(p, axis, kind, sp, spans, dst, s);
     g_launches++;
     CHELIS_LAUNCH_CHECK(sp.inner == 1 ? "fused::reduce_last_kernel" : "fused::reduce_inner_kernel");
     return CHELIS_CUDA_OK;
@@ -786,8 +978,9 @@ int fused_reduce_t(const fused::Program &p, int mode, int kind, int axis, int64_
     CHELIS_TRY(scratch_alloc(&part, static_cast<size_t>(outputs * sp.nseg) * sizeof(T), s));
     int rc = launch_reduce<T>(p, mode, axis, kind, sp, outputs, static_cast<T *>(part), s);
     if (rc == CHELIS_CUDA_OK) {
-        finish_kernel<T><<<grid_of(outputs, 256), 256, 0, s>>>(static_cast<const T *>(part), kind, sp,
-                                                               outputs, out);
+        const int64_t blocks = outputs < 65535 ? outputs : 65535;
+        finish_kernel<T><<<static_cast<unsigned>(blocks), FINISH_THREADS, 0, s>>>(
+            static_cast<const T *>(part), kind, sp, outputs, out);
         g_launches++;
         rc = check_cuda(cudaGetLastError(), "fused::finish_kernel");
     }
