@@ -313,7 +313,34 @@ def bench_extras(args, peaks):
         fused[name] = {"ms": round(ms_g, 4), "gbs": round(nbytes / ms_g / 1e6, 1),
                        "frac_hbm": round(nbytes / ms_g / 1e6 / hbm, 3)}
     out["fused_groups_16384x4096"] = fused
-    del x, g, be, state, y
+    # generic FusedElem groups (chelis_cuda_fused_elementwise / _reduce) on
+    # the same matrix: broadcast affine, a unary chain, a GELU-like chain of
+    # 9 steps, and square-sums along each axis and over the whole tensor
+    from chelis_b200 import fused as F
+    consts = [torch.tensor(v, device="cuda") for v in (0.044715, 0.7978845608, 0.5, 1.0)]
+    gelu = ("mul x0 x0; mul v0 x0; mul v1 x1; add v2 x0; mul v3 x2; tanh v4; "
+            "add v5 x4; mul v6 x0; mul v7 x3")
+    flat = x.reshape(-1)
+    elem = {
+        "affine": (lambda c=F.parse("mul x0 x1; add v0 x2"): ops.fused_elementwise(c, [x, g, be]),
+                   2 * nb),
+        "exp": (lambda c=F.parse("exp x0"): ops.fused_elementwise(c, [x]), 2 * nb),
+        "gelu": (lambda c=F.parse(gelu): ops.fused_elementwise(c, [x, *consts]), 2 * nb),
+        "sum_sq_rows": (lambda c=F.parse("mul x0 x0"): ops.fused_reduce(c, [x], axis=1),
+                        nb + rows * 4),
+        "sum_sq_cols": (lambda c=F.parse("mul x0 x0"): ops.fused_reduce(c, [x], axis=0),
+                        nb + hidden * 4),
+        "max_abs_rows": (lambda c=F.parse("abs x0"): ops.fused_reduce(c, [x], axis=1, kind="max"),
+                         nb + rows * 4),
+        "sum_sq_all": (lambda c=F.parse("mul x0 x0"): ops.fused_reduce(c, [flat], axis=0), nb + 4),
+    }
+    generic = {}
+    for name, (fn, nbytes) in elem.items():
+        ms_g = timed(fn, 10)
+        generic[name] = {"ms": round(ms_g, 4), "gbs": round(nbytes / ms_g / 1e6, 1),
+                         "frac_hbm": round(nbytes / ms_g / 1e6 / hbm, 3)}
+    out["fused_elem_16384x4096"] = generic
+    del x, g, be, state, y, flat
     # MLP step
     x, labels, w1, b1, w2, b2 = W.torch_mlp_inputs()
     ms = timed(lambda: ops.mlp_step(x, labels, w1, b1, w2, b2), 20)
