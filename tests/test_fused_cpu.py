@@ -105,16 +105,6 @@ def test_oracle_step_nan_rules(orc):
     assert fd.tolist() == [3.0, -4.0, -4.0]
 
 
-def _program(rng, n_inputs, n_steps, ops):
-    steps = []
-    for s in range(n_steps):
-        op = ops[rng.integers(len(ops))]
-        pick = lambda: (F.External(int(rng.integers(n_inputs))) if s == 0 or rng.random() < 0.4
-                        else F.PreviousStep(int(rng.integers(s))))
-        steps.append(F.FusedStep(op, pick(), pick()) if op in F.BINARY else F.FusedStep(op, pick()))
-    return steps
-
-
 def test_oracle_reduce_orders_match_pinned_trees(orc):
     """Sum along the last / first axis is the canonical tree the pinned
     row_sum / col_sum use; Max is chelis_fmax_propnan folded from -inf."""
@@ -195,3 +185,16 @@ def test_fused_abi_rejects_bad_programs_without_device():
     # empty elementwise work is a successful no-op
     assert lib.chelis_cuda_fused_elementwise(L.DTYPE_F32, steps, 1, ptrs, strides, 1, zero, 1,
                                              None) == 0
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_oracle_inlined_product_equals_matmul_tree(orc, dtype):
+    """fuse.rs:483-560: a Sum over k of Mul(Expand(a), Expand(b)) keeps the
+    materialised graph's bits -- the C lane's matmul tree (emit.rs:8431-8640)."""
+    rng = np.random.default_rng(9)
+    a = rng.standard_normal((19, 77)).astype(dtype)
+    b = rng.standard_normal((77, 23)).astype(dtype)
+    got = orc.fused_reduce(F.triplets(F.parse("mul x0 x1")), [a[:, :, None], b[None, :, :]],
+                           axis=1, shape=(19, 77, 23))
+    ref = orc.gemm(a, b)
+    assert (got == ref).all()

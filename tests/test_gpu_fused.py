@@ -230,3 +230,22 @@ def test_errors(cuda):
         cuda.fused_elementwise(F.parse("add x0 x1"), [t(np.ones(3, np.float32)),
                                                       t(np.ones(3, np.float64))])
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("mkn", [(33, 70, 17), (8, 1000, 64)])
+def test_inlined_product_is_the_c_lane_matmul(cuda, orc, mkn, dtype):
+    """Sum(Mul(Expand(a), Expand(b))) along k -- the reduction-inlined product
+    of fuse.rs:483-560 (an einsum contraction) -- as one fused reduction over
+    the broadcast [m, k, n] iteration shape: bit for bit the C lane's matmul
+    (fl(a*b) leaves, canonical tree over k, emit.rs:8431-8640)."""
+    m, k, n = mkn
+    rng = np.random.default_rng(m * k + n)
+    a = rng.standard_normal((m, k)).astype(dtype)
+    b = rng.standard_normal((k, n)).astype(dtype)
+    A, B = t(a), t(b)
+    got = cuda.fused_reduce(F.parse("mul x0 x1"), [A[:, :, None], B[None, :, :]], axis=1,
+                            shape=(m, k, n)).cpu().numpy()
+    ref = orc.gemm(a, b)
+    width = "f32" if dtype == np.float32 else "f64"
+    assert (got.view(UINT[width]) == ref.view(UINT[width])).all()
