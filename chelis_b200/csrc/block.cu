@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(T) ln_fwd_kernel(const float *__restrict__ x,
         const float var = div_<EXACT>(tree_parts<T, NC>(part, n, rs), hf, rh);
         const float d = __fsqrt_rn(__fadd_rn(var, eps));
         const float rd = __fdiv_rn(1.0f, d);
+        if (threadIdx.x == 0) stats[r] = make_float2(mean, d);
+        if (y == nullptr) continue;  // statistics only (the standalone layer_norm adjoint)
         float *yr = y + r * n;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
@@ -91,7 +93,6 @@ __global__ void __launch_bounds__(T) ln_fwd_kernel(const float *__restrict__ x,
                 for (int i = 0; i < 4; ++i)
                     if (e0 + i < n) yr[e0 + i] = o[i];
         }
-        if (threadIdx.x == 0) stats[r] = make_float2(mean, d);
     }
 }
 
@@ -267,9 +268,9 @@ __global__ void __launch_bounds__(T) softmax_scaled_bwd_kernel(const float *__re
 // gelu = m(x) * Phi(x) with the compensated Phi graph of spec 05 section 3.3
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float phi_graph(float x) {
-    const float c = 0.70710677f;          // RN_f32(1/sqrt(2))
-    const float cl = 1.2101671e-08f;      // RN_f32(1/sqrt(2) - c)
-    const float k = 1.1283792f;           // RN_f32(2/sqrt(pi))
+    const float c = 0x1.6a09e6p-1f;       // RN_f32(1/sqrt(2))
+    const float cl = 0x1.9fcef4p-27f;     // RN_f32(1/sqrt(2) - c)
+    const float k = 0x1.20dd76p+0f;       // RN_f32(2/sqrt(pi))
     const float sp = 4097.0f;             // Veltkamp splitter for f32
     const float e = erfcf(__fmul_rn(-x, c));
     const float z = (fabsf(x) < 64.0f) ? x : 0.0f;

@@ -14,3 +14,4 @@
 #include "abi.cu"
 #include "chain_noalloc.cu"
 #include "fused.cu"
+#include "activations.cu"

@@ -666,9 +666,10 @@ int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStr
 namespace {
 constexpr int kRowThreads = 256;
 
-int check_rows_args(const void *x, int64_t rows, int64_t hidden) {
+// wide_ok: the op has a path for rows wider than the register-resident kernels
+int check_rows_args(const void *x, int64_t rows, int64_t hidden, bool wide_ok = false) {
     if (rows < 0 || hidden < 0) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in rows at i64");
-    if (hidden > 8 * 4 * kRowThreads || hidden > INT32_MAX)
+    if ((!wide_ok && hidden > 8 * 4 * kRowThreads) || hidden > INT32_MAX)
         return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "row width %lld beyond %d",
                          static_cast<long long>(hidden), 8 * 4 * kRowThreads);
     (void)x;
@@ -697,10 +698,67 @@ int chelis_cuda_layer_norm_f32(const float *x, const float *gamma, const float *
     });
 }
 
+}  // extern "C"
+
+namespace chelis {
+namespace {
+
+// Rows wider than the register-resident kernels take (8192): the softmax
+// lowering (max -> sub -> exp -> sum -> div, tier2.rs:1079-1180) and its
+// adjoint y * (g - sum(g * y)) as FusedElem groups over the row, with the
+// per-row max / sums broadcast back (stride 0 along the row).
+int softmax_rows_wide(const float *x, const float *g, float *out, int64_t rows, int64_t cols,
+                      cudaStream_t s) {
+    void *scratch = nullptr;
+    CHELIS_TRY(scratch_alloc(&scratch, 2 * static_cast<size_t>(rows) * sizeof(float), s));
+    float *r1 = static_cast<float *>(scratch), *r2 = r1 + rows;
+    const int64_t shape[2] = {rows, cols};
+    const int64_t dense[2] = {cols, 1};
+    int rc;
+    if (!g) {  // forward: out = softmax(x)
+        const chelis_fused_step ident[1] = {{CHELIS_FUSED_MAX_ELEM, 0, 0}};
+        const chelis_fused_step shift_exp[2] = {{CHELIS_FUSED_SUB, 0, 1}, {CHELIS_FUSED_EXP, -1, -1}};
+        const chelis_fused_step divide[1] = {{CHELIS_FUSED_DIV, 0, 1}};
+        const void *in_x[1] = {x};
+        rc = chelis_cuda_fused_reduce(CHELIS_DTYPE_F32, ident, 1, in_x, dense, 1, shape, 2, 1,
+                                      CHELIS_FUSED_REDUCE_MAX, r1);
+        const void *in_xm[2] = {x, r1};
+        const int64_t st_xm[4] = {cols, 1, 1, 0};
+        if (rc == CHELIS_CUDA_OK)
+            rc = chelis_cuda_fused_elementwise(CHELIS_DTYPE_F32, shift_exp, 2, in_xm, st_xm, 2, shape, 2, out);
+        const void *in_e[1] = {out};
+        if (rc == CHELIS_CUDA_OK)
+            rc = chelis_cuda_fused_reduce(CHELIS_DTYPE_F32, ident, 1, in_e, dense, 1, shape, 2, 1,
+                                          CHELIS_FUSED_REDUCE_SUM, r2);
+        const void *in_ez[2] = {out, r2};
+        if (rc == CHELIS_CUDA_OK)
+            rc = chelis_cuda_fused_elementwise(CHELIS_DTYPE_F32, divide, 1, in_ez, st_xm, 2, shape, 2, out);
+    } else {  // adjoint: out = x * (g - sum(g * x)), x the softmax output
+        const chelis_fused_step prod[1] = {{CHELIS_FUSED_MUL, 0, 1}};
+        const chelis_fused_step grad[2] = {{CHELIS_FUSED_SUB, 0, 2}, {CHELIS_FUSED_MUL, 1, -1}};
+        const void *in_gy[2] = {g, x};
+        const int64_t st_gy[4] = {cols, 1, cols, 1};
+        rc = chelis_cuda_fused_reduce(CHELIS_DTYPE_F32, prod, 1, in_gy, st_gy, 2, shape, 2, 1,
+                                      CHELIS_FUSED_REDUCE_SUM, r1);
+        const void *in_gyq[3] = {g, x, r1};
+        const int64_t st_gyq[6] = {cols, 1, cols, 1, 1, 0};
+        if (rc == CHELIS_CUDA_OK)
+            rc = chelis_cuda_fused_elementwise(CHELIS_DTYPE_F32, grad, 2, in_gyq, st_gyq, 3, shape, 2, out);
+    }
+    scratch_free(scratch, s);
+    return rc;
+}
+
+}  // namespace
+}  // namespace chelis
+
+extern "C" {
+
 int chelis_cuda_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols) {
-    CHELIS_TRY(check_rows_args(x, rows, cols));
+    CHELIS_TRY(check_rows_args(x, rows, cols, true));
     if (rows == 0 || cols == 0) return CHELIS_CUDA_OK;
     cudaStream_t s = current_stream();
+    if (cols > 8 * 4 * kRowThreads) return softmax_rows_wide(x, nullptr, y, rows, cols, s);
     const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
     const int n = static_cast<int>(cols);
     const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
@@ -716,9 +774,10 @@ int chelis_cuda_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t
 
 int chelis_cuda_softmax_rows_bwd_f32(const float *y, const float *g, float *dx, int64_t rows,
                                      int64_t cols) {
-    CHELIS_TRY(check_rows_args(y, rows, cols));
+    CHELIS_TRY(check_rows_args(y, rows, cols, true));
     if (rows == 0 || cols == 0) return CHELIS_CUDA_OK;
     cudaStream_t s = current_stream();
+    if (cols > 8 * 4 * kRowThreads) return softmax_rows_wide(y, g, dx, rows, cols, s);
     const int n = static_cast<int>(cols);
     const unsigned grid = static_cast<unsigned>(rows_grid(rows, 8));
     return dispatch_nc(n, kRowThreads, [&](auto ncv) -> int {

@@ -123,6 +123,12 @@ SIGNATURES = {
     "chelis_cuda_block_step": (c_int, [ctypes.POINTER(BlockParams), c_vp]),
     "chelis_cuda_fused_elementwise": (c_int, [c_i32, c_vp, c_i32, _PP, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_i64), c_i32, c_vp]),
     "chelis_cuda_fused_reduce": (c_int, [c_i32, c_vp, c_i32, _PP, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_i64), c_i32, c_i32, c_i32, c_vp]),
+    "chelis_cuda_relu": (c_int, [c_i32, c_vp, c_vp, c_i64]),
+    "chelis_cuda_relu_adjoint": (c_int, [c_i32, c_vp, c_vp, c_vp, c_i64]),
+    "chelis_cuda_gelu_f32": (c_int, [c_vp, c_vp, c_i64]),
+    "chelis_cuda_gelu_adjoint_f32": (c_int, [c_vp, c_vp, c_vp, c_i64]),
+    "chelis_cuda_layer_norm_bwd_f32": (c_int, [c_vp, c_vp, c_f32, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "chelis_cuda_cross_entropy_f32": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
     "chelis_chain_fwd_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_chain_grad_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_portfolio_device": (c_int, [_PP, c_i32, _PP, c_i32]),

@@ -434,3 +434,61 @@ def fused_reduce(steps, inputs, axis: int, kind: str = "sum", shape=None) -> tor
     L.call("chelis_cuda_fused_reduce", dt, a["steps"], len(steps), a["ptrs"], a["strides"],
            len(inputs), a["shape"], len(shape), axis, F.REDUCE_KIND[kind], out.data_ptr())
     return out
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return L.DTYPE_F32
+    if t.dtype == torch.float64:
+        return L.DTYPE_F64
+    raise ValueError("f32 or f64 tensors")
+
+
+def relu(x: torch.Tensor) -> torch.Tensor:
+    _prepare(x)
+    y = torch.empty_like(x)
+    L.call("chelis_cuda_relu", _dt(x), x.data_ptr(), y.data_ptr(), x.numel())
+    return y
+
+
+def relu_adjoint(x: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    _prepare(x, g)
+    dx = torch.empty_like(g)
+    L.call("chelis_cuda_relu_adjoint", _dt(x), x.data_ptr(), g.data_ptr(), dx.data_ptr(), x.numel())
+    return dx
+
+
+def gelu(x: torch.Tensor) -> torch.Tensor:
+    _prepare(x)
+    y = torch.empty_like(x)
+    L.call("chelis_cuda_gelu_f32", x.data_ptr(), y.data_ptr(), x.numel())
+    return y
+
+
+def gelu_adjoint(x: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    _prepare(x, g)
+    dx = torch.empty_like(g)
+    L.call("chelis_cuda_gelu_adjoint_f32", x.data_ptr(), g.data_ptr(), dx.data_ptr(), x.numel())
+    return dx
+
+
+def layer_norm_bwd(x, gamma, eps: float, dy):
+    _prepare(x, gamma, dy)
+    rows, hidden = x.shape
+    dx = torch.empty_like(x)
+    dg = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    db = torch.empty(hidden, dtype=torch.float32, device=x.device)
+    L.call("chelis_cuda_layer_norm_bwd_f32", x.data_ptr(), gamma.data_ptr(), eps, dy.data_ptr(),
+           rows, hidden, dx.data_ptr(), dg.data_ptr(), db.data_ptr())
+    return dx, dg, db
+
+
+def cross_entropy(logits, labels, want_grad: bool = True):
+    """Mean cross-entropy of row softmax at int64 labels; returns (loss, dlogits)."""
+    _prepare(logits, labels)
+    rows, classes = logits.shape
+    loss = torch.empty((), dtype=torch.float32, device=logits.device)
+    dz = torch.empty_like(logits) if want_grad else None
+    L.call("chelis_cuda_cross_entropy_f32", logits.data_ptr(), labels.data_ptr(), rows, classes,
+           loss.data_ptr(), _ptr(dz))
+    return loss, dz

@@ -340,6 +340,30 @@ int chelis_cuda_layer_norm_f32(const float *x, const float *gamma, const float *
 int chelis_cuda_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols);
 int chelis_cuda_softmax_rows_bwd_f32(const float *y, const float *g, float *dx, int64_t rows,
                                      int64_t cols);
+/* [05-OP-43] relu = max_elem(x, +0) (a NaN keeps its bits, -0 stays -0) and
+ * ReluAdjoint: g's bits where 0 < x, exact +0 elsewhere (dag.rs:957,965,
+ * grad.rs:2281-2294).  f32 or f64, n elements, bit-exact. */
+int chelis_cuda_relu(int32_t dtype, const void *x, void *y, int64_t n);
+int chelis_cuda_relu_adjoint(int32_t dtype, const void *x, const void *g, void *dx, int64_t n);
+/* gelu = m(x) * Phi(x), Phi the compensated standard normal CDF graph of
+ * spec 05 section 3.3 (tier2.rs lower_gelu), and its adjoint
+ * dx = g * (Phi(x) + x * phi(x)).  f32; CUDA erfc / exp stand in for
+ * CORE-MATH's. */
+int chelis_cuda_gelu_f32(const float *x, float *y, int64_t n);
+int chelis_cuda_gelu_adjoint_f32(const float *x, const float *g, float *dx, int64_t n);
+/* Adjoint of y = layer_norm(x, gamma, beta, eps) over the last axis
+ * (tier2.rs:1248-1375 through grad.rs): dx [rows, hidden] and the complete
+ * dgamma, dbeta [hidden] from dy.  hidden <= 8192. */
+int chelis_cuda_layer_norm_bwd_f32(const float *x, const float *gamma, float eps, const float *dy,
+                                   int64_t rows, int64_t hidden, float *dx, float *dgamma,
+                                   float *dbeta);
+/* Cross-entropy of spec 05 section 4.3: loss = mean_r(-log softmax(z_r)[label_r])
+ * written to the device scalar *loss; with dlogits non-NULL also d loss / d z
+ * (the AD graph through mean, neg, gather, log and softmax).  labels int64 in
+ * [0, classes): another value is the gather's Domain trap, reported by
+ * chelis_cuda_device_status. */
+int chelis_cuda_cross_entropy_f32(const float *logits, const int64_t *labels, int64_t rows,
+                                  int64_t classes, float *loss, float *dlogits);
 /* The fused chain layer_norm -> softmax -> dropout -> row sum over a
  * [rows, hidden] f32 tensor.  `row_stats` (optional, 4 floats per row:
  * mean, sqrt(var+eps), softmax max, softmax denominator) is written for the

@@ -830,3 +830,134 @@ enum {
 static inline float cr_sqrtf(float x) { return sqrtf(x); }
 DEFINE_FUSED(float, f32, canon_f32, CR_F32, floorf, ceilf, rintf, fabsf, cr_sqrtf)
 DEFINE_FUSED(double, f64, canon_f64, CR_F64, floor, ceil, rint, fabs, sqrt)
+
+/* ------------------------------------------------------------------------ */
+/* activations, layer_norm adjoint, cross-entropy                           */
+/* ------------------------------------------------------------------------ */
+/* [05-OP-43] relu = max_elem(x, +0) (spec/05-risc-primitives.md:1439-1452):
+ * a NaN keeps its bits, -0 stays -0 (first operand on ties). */
+void orc_relu_f32(const float *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = (isnan(x[i]) || x[i] >= 0.0f) ? x[i] : 0.0f;
+}
+void orc_relu_f64(const double *x, double *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) y[i] = (isnan(x[i]) || x[i] >= 0.0) ? x[i] : 0.0;
+}
+/* ReluAdjoint: g where cmplt(0, x), exact +0 otherwise (grad.rs:2281-2294). */
+void orc_relu_adjoint_f32(const float *x, const float *g, float *dx, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) dx[i] = (0.0f < x[i]) ? g[i] : 0.0f;
+}
+void orc_relu_adjoint_f64(const double *x, const double *g, double *dx, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) dx[i] = (0.0 < x[i]) ? g[i] : 0.0;
+}
+
+/* gelu(x) = mul(m(x), Phi(x)) with the compensated Phi graph of
+ * spec/05-risc-primitives.md:1353-1400 at f32 (tier2.rs lower_gelu); every
+ * step one finalized f32 operation, erfc and exp CORE-MATH. */
+static float phi_graph_f32(float x) {
+    const float c = 0x1.6a09e6p-1f, cl = 0x1.9fcef4p-27f, k = 0x1.20dd76p+0f, s = 4097.0f;
+    float e = canon_f32(chelis_crmath_ffi_erfcf(canon_f32(canon_f32(-x) * c)));
+    float z = (fabsf(x) < 64.0f) ? x : 0.0f;
+    float a = canon_f32(-z);
+    float th = canon_f32(a * c);
+    float ta = canon_f32(s * a);
+    float ah = canon_f32(ta - canon_f32(ta - a));
+    float al = canon_f32(a - ah);
+    float tc = canon_f32(s * c);
+    float ch = canon_f32(tc - canon_f32(tc - c));
+    float cr = canon_f32(c - ch);
+    float tl = canon_f32(canon_f32(ah * ch) - th);
+    tl = canon_f32(tl + canon_f32(ah * cr));
+    tl = canon_f32(tl + canon_f32(al * ch));
+    tl = canon_f32(tl + canon_f32(al * cr));
+    tl = canon_f32(tl + canon_f32(a * cl));
+    float ex = canon_f32(chelis_crmath_ffi_expf(canon_f32(-canon_f32(th * th))));
+    float corr = canon_f32(canon_f32(k * ex) * tl);
+    return canon_f32(0.5f * canon_f32(e - corr));
+}
+void orc_gelu_f32(const float *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        float m = (x[i] < -0x1.fffffep+127f) ? -0.0f : x[i]; /* the multiplicand guard m(x) */
+        y[i] = canon_f32(m * phi_graph_f32(x[i]));
+    }
+}
+
+/* Adjoint of layer_norm over the last axis given dy: the LN part of
+ * orc_chain_bwd on its own (the AD of tier2.rs:1248-1375; dgamma, dbeta by
+ * the canonical tree over rows). */
+void orc_layer_norm_bwd_f32(const float *x, const float *gamma, float eps, const float *dy_all,
+                            int64_t rows, int64_t hidden, float *dx, float *dgamma, float *dbeta) {
+    float hf = (float)hidden;
+    float *dyn_rows = (float *)malloc(sizeof(float) * (size_t)(rows * hidden));
+#pragma omp parallel
+    {
+        float *c = (float *)malloc(sizeof(float) * (size_t)hidden);
+        float *n = (float *)malloc(sizeof(float) * (size_t)hidden);
+        float *y = (float *)malloc(sizeof(float) * (size_t)hidden);
+        float *ds = (float *)malloc(sizeof(float) * (size_t)hidden);
+        float *tmp = (float *)malloc(sizeof(float) * (size_t)hidden);
+#pragma omp for schedule(static)
+        for (int64_t r = 0; r < rows; ++r) {
+            const float *xr = x + r * hidden;
+            const float *dy = dy_all + r * hidden;
+            ln_row lr = ln_row_fwd(xr, gamma, gamma, eps, hidden, c, n, y);
+            float *dyn = dyn_rows + r * hidden;
+            for (int64_t j = 0; j < hidden; ++j) dyn[j] = dy[j] * n[j];
+            for (int64_t j = 0; j < hidden; ++j) {
+                float dn = dy[j] * gamma[j];
+                float q = (dn * n[j]) / lr.d;
+                float dd = -q;
+                float two_d = 2.0f * lr.d;
+                tmp[j] = dd / two_d;
+                ds[j] = dn / lr.d;
+            }
+            float dS2 = orc_tree_sum_f32(tmp, hidden, 1) / hf;
+            for (int64_t j = 0; j < hidden; ++j) {
+                float p = dS2 * c[j];
+                ds[j] = (p + p) + ds[j];
+                tmp[j] = -ds[j];
+            }
+            float dS1 = orc_tree_sum_f32(tmp, hidden, 1) / hf;
+            float *dxr = dx + r * hidden;
+            for (int64_t j = 0; j < hidden; ++j) dxr[j] = canon_f32(dS1 + ds[j]);
+        }
+        free(c);
+        free(n);
+        free(y);
+        free(ds);
+        free(tmp);
+    }
+    orc_col_sum_f32(dyn_rows, rows, hidden, dgamma);
+    orc_col_sum_f32(dy_all, rows, hidden, dbeta);
+    free(dyn_rows);
+}
+
+/* Cross-entropy (spec/05-risc-primitives.md:5044-5063): loss =
+ * mean_r(-log softmax(z_r)[label_r]) and, when dz is non-NULL, its adjoint
+ * through mean, neg, gather, log and softmax -- the loss head of
+ * orc_mlp_step on its own.  Returns 1 on an out-of-range label. */
+int orc_cross_entropy_f32(const float *z, const int64_t *labels, int64_t rows, int64_t classes,
+                          float *loss, float *dz) {
+    for (int64_t i = 0; i < rows; ++i)
+        if (labels[i] < 0 || labels[i] >= classes) return 1;
+    float *s = (float *)malloc(sizeof(float) * (size_t)(rows * classes));
+    float *nl = (float *)malloc(sizeof(float) * (size_t)rows);
+    float *g = (float *)malloc(sizeof(float) * (size_t)classes);
+    float *tmp = (float *)malloc(sizeof(float) * (size_t)classes);
+    orc_softmax_rows_f32(z, s, rows, classes);
+    for (int64_t i = 0; i < rows; ++i) nl[i] = -orc_logf(s[i * classes + labels[i]]);
+    float bf = (float)rows;
+    *loss = canon_f32(orc_tree_sum_f32(nl, rows, 1) / bf);
+    if (dz) {
+        float dsel = -(1.0f / bf);
+        for (int64_t i = 0; i < rows; ++i) {
+            const float *si = s + i * classes;
+            for (int64_t j = 0; j < classes; ++j) g[j] = ((j == labels[i]) ? dsel : 0.0f) / si[j];
+            softmax_row_bwd(si, g, dz + i * classes, tmp, classes);
+        }
+    }
+    free(s);
+    free(nl);
+    free(g);
+    free(tmp);
+    return 0;
+}

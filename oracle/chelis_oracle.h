@@ -118,6 +118,18 @@ void orc_fused_reduce_f64(const int32_t *steps, int32_t n_steps, const double *c
                           const int64_t *strides, int32_t n_in, const int64_t *shape, int32_t rank,
                           int32_t axis, int32_t kind, double *out);
 
+
+/* ---- activations, layer_norm adjoint, cross-entropy ---- */
+void orc_relu_f32(const float *x, float *y, int64_t n);
+void orc_relu_f64(const double *x, double *y, int64_t n);
+void orc_relu_adjoint_f32(const float *x, const float *g, float *dx, int64_t n);
+void orc_relu_adjoint_f64(const double *x, const double *g, double *dx, int64_t n);
+void orc_gelu_f32(const float *x, float *y, int64_t n);
+void orc_layer_norm_bwd_f32(const float *x, const float *gamma, float eps, const float *dy,
+                            int64_t rows, int64_t hidden, float *dx, float *dgamma, float *dbeta);
+int orc_cross_entropy_f32(const float *z, const int64_t *labels, int64_t rows, int64_t classes,
+                          float *loss, float *dz);
+
 #ifdef __cplusplus
 }
 #endif

@@ -331,3 +331,59 @@ def fused_reduce(triplets, inputs, axis: int, kind: str = "sum", shape=None) -> 
         ax = axis % len(s)
         return s[:ax] + s[ax + 1:], (ctypes.c_int32(ax), ctypes.c_int32(k))
     return _fused_call("orc_fused_reduce", triplets, inputs, shape, extra)
+
+
+def relu(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    y = np.empty_like(x)
+    fn = lib().orc_relu_f32 if x.dtype == np.float32 else lib().orc_relu_f64
+    fn.restype = None
+    fn(x.ctypes.data_as(ctypes.c_void_p), y.ctypes.data_as(ctypes.c_void_p), _i64(x.size))
+    return y
+
+
+def relu_adjoint(x: np.ndarray, g: np.ndarray) -> np.ndarray:
+    x, g = np.ascontiguousarray(x), np.ascontiguousarray(g)
+    dx = np.empty_like(g)
+    fn = lib().orc_relu_adjoint_f32 if x.dtype == np.float32 else lib().orc_relu_adjoint_f64
+    fn.restype = None
+    fn(x.ctypes.data_as(ctypes.c_void_p), g.ctypes.data_as(ctypes.c_void_p),
+       dx.ctypes.data_as(ctypes.c_void_p), _i64(x.size))
+    return dx
+
+
+def gelu(x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    fn = lib().orc_gelu_f32
+    fn.restype = None
+    fn(x.ctypes.data_as(ctypes.c_void_p), y.ctypes.data_as(ctypes.c_void_p), _i64(x.size))
+    return y
+
+
+def layer_norm_bwd(x, gamma, eps, dy):
+    x, gamma, dy = _c(x, np.float32), _c(gamma, np.float32), _c(dy, np.float32)
+    rows, hidden = x.shape
+    dx = np.empty_like(x)
+    dg = np.empty(hidden, np.float32)
+    db = np.empty(hidden, np.float32)
+    fn = lib().orc_layer_norm_bwd_f32
+    fn.restype = None
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    fn(p(x), p(gamma), ctypes.c_float(eps), p(dy), _i64(rows), _i64(hidden), p(dx), p(dg), p(db))
+    return dx, dg, db
+
+
+def cross_entropy(z, labels):
+    """(loss, dz) of the mean cross-entropy at int64 labels."""
+    z = _c(z, np.float32)
+    labels = np.ascontiguousarray(labels, dtype=np.int64)
+    rows, classes = z.shape
+    loss = np.zeros(1, np.float32)
+    dz = np.empty_like(z)
+    fn = lib().orc_cross_entropy_f32
+    fn.restype = ctypes.c_int
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    if fn(p(z), p(labels), _i64(rows), _i64(classes), p(loss), p(dz)) != 0:
+        raise ValueError("label out of range")
+    return loss[0], dz
