@@ -351,7 +351,8 @@ def bench_extras(args, peaks):
 def bench_sharded(args, world, rank, peaks):
     """The configurations that shard across GPUs, at every N (max over ranks):
     config 4 data-parallel (one NCCL all-reduce of the flat gradient buffer
-    per step), both as the global batch of 8 split across ranks (strong) and
+    per step, through the library's own communicator, chelis_cuda_dp_*),
+    both as the global batch of 8 split across ranks (strong) and
     as 8 samples per rank (weak), config 5 and the batched GEMM of config 2
     along their vmap axis (no collective)."""
     import torch
@@ -386,6 +387,8 @@ def bench_sharded(args, world, rank, peaks):
                 "flop_per_sample": per_sample,
                 "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1)}
 
+    if world > 1:
+        dp.native_init(world, rank)
     # strong: the global batch of 8 split across ranks
     a, b = dp.shard(shape["batch"], world, rank)
     out["block_dp"] = dict(block_dp(b - a, shape["batch"]), scaling="strong (global batch 8)")
@@ -395,6 +398,8 @@ def bench_sharded(args, world, rank, peaks):
     else:
         out["block_dp_weak"] = dict(block_dp(shape["batch"], shape["batch"] * world),
                                     scaling="weak (8 samples per rank)")
+        torch.cuda.synchronize()
+        dp.native_finalize()
     # config 5: covariance / risk, 65536 portfolios split across ranks
     cnt = W.PORTFOLIO_SHAPE["count"]
     a, b = dp.shard(cnt, world, rank)

@@ -15,3 +15,4 @@
 #include "chain_noalloc.cu"
 #include "fused.cu"
 #include "activations.cu"
+#include "dp.cu"

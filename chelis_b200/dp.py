@@ -15,7 +15,13 @@ spec/design/chelis_project_plan.md:1188-1192):
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
+
+from . import lib as L
+
+_native = [False]
 
 
 def shard(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -47,7 +53,39 @@ class FlatGrads:
         return self.views[name]
 
 
+def native_init(world: int, rank: int) -> None:
+    """Open the library's own NCCL communicator (chelis_cuda_dp_init) over the
+    ranks of the running torch.distributed group: rank 0 makes the id, the
+    group's broadcast hands it to the others."""
+    import torch.distributed as dist
+    buf = (ctypes.c_uint8 * 128)()
+    if rank == 0:
+        L.call("chelis_cuda_dp_unique_id", buf)
+    obj = [bytes(buf)]
+    dist.broadcast_object_list(obj, src=0)
+    ctypes.memmove(buf, obj[0], 128)
+    L.call("chelis_cuda_dp_init", world, rank, buf)
+    _native[0] = True
+
+
+def native_finalize(abort: bool = False) -> None:
+    if _native[0]:
+        _native[0] = False
+        L.call("chelis_cuda_dp_finalize", 1 if abort else 0)
+
+
 def allreduce_sum(flat: torch.Tensor, world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
-        dist.all_reduce(flat, op=dist.ReduceOp.SUM)
+    """Sum `flat` over the ranks, in place, on the current stream: through the
+    library's communicator when native_init opened one, else through
+    torch.distributed (gloo on CPU)."""
+    if world <= 1:
+        return
+    if _native[0] and flat.is_cuda:
+        from . import ops
+        ops._prepare(flat)
+        dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64,
+              torch.int64: L.DTYPE_I64, torch.int32: L.DTYPE_I32}[flat.dtype]
+        L.call("chelis_cuda_dp_allreduce_sum", dt, flat.data_ptr(), flat.numel())
+        return
+    import torch.distributed as dist
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM)

@@ -129,6 +129,12 @@ SIGNATURES = {
     "chelis_cuda_gelu_adjoint_f32": (c_int, [c_vp, c_vp, c_vp, c_i64]),
     "chelis_cuda_layer_norm_bwd_f32": (c_int, [c_vp, c_vp, c_f32, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "chelis_cuda_cross_entropy_f32": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
+    "chelis_cuda_dp_shard": (c_int, [c_i64, c_i32, c_i32, ctypes.POINTER(c_i64), ctypes.POINTER(c_i64)]),
+    "chelis_cuda_dp_unique_id": (c_int, [c_vp]),
+    "chelis_cuda_dp_init": (c_int, [c_i32, c_i32, c_vp]),
+    "chelis_cuda_dp_allreduce_sum": (c_int, [c_i32, c_vp, c_i64]),
+    "chelis_cuda_dp_world": (c_int, [ctypes.POINTER(c_i32), ctypes.POINTER(c_i32)]),
+    "chelis_cuda_dp_finalize": (c_int, [c_i32]),
     "chelis_chain_fwd_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_chain_grad_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_portfolio_device": (c_int, [_PP, c_i32, _PP, c_i32]),

@@ -459,6 +459,30 @@ int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p);
 int chelis_cuda_block_step(const chelis_block_params *p, void *workspace);
 
 /* =========================================================================
+ * Data parallel across the GPUs of one node (new: the reference has no
+ * multi-GPU lane).  One process per GPU; NCCL is opened at run time
+ * (libnccl.so.2), without it these return CHELIS_CUDA_ERR_UNSUPPORTED.
+ * ========================================================================= */
+/* Contiguous [start, stop) of n batch items for `rank`: shard sizes differ by
+ * at most one and tile [0, n) in rank order (the vmap axis,
+ * crates/chelis-ir-core/src/vmap.rs:9-56). */
+int chelis_cuda_dp_shard(int64_t n, int32_t nranks, int32_t rank, int64_t *start, int64_t *stop);
+/* 128 bytes identifying a new communicator; rank 0 makes it, every rank
+ * passes the same bytes to chelis_cuda_dp_init. */
+int chelis_cuda_dp_unique_id(uint8_t *id);
+/* Join the communicator on the current device (every rank calls it). */
+int chelis_cuda_dp_init(int32_t nranks, int32_t rank, const uint8_t *id);
+/* In-place sum over ranks of count elements (f32, f64, i32, i64), enqueued
+ * on the calling thread's stream: the gradient all-reduce of a data-parallel
+ * step.  Every rank calls it in the same order. */
+int chelis_cuda_dp_allreduce_sum(int32_t dtype, void *buf, int64_t count);
+/* nranks / rank of the open communicator (1 / 0 without one). */
+int chelis_cuda_dp_world(int32_t *nranks, int32_t *rank);
+/* Close the communicator; abort != 0 abandons collectives in flight (a rank
+ * that learned of a failed peer on the host). */
+int chelis_cuda_dp_finalize(int32_t abort);
+
+/* =========================================================================
  * Generated-entry device ABI (emit.rs:838-958, `f_device`): inputs borrowed,
  * outputs newly allocated owners the caller releases.  One entry per program
  * this backend ships whole.

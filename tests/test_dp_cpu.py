@@ -68,3 +68,23 @@ def test_two_rank_gradient_allreduce_equals_full_batch():
         assert p.exitcode == 0
     e1, e2 = q.get(timeout=10)
     assert e1 < 1e-12 and e2 < 1e-12
+
+
+def test_c_abi_shard_matches_host_rule():
+    import ctypes
+    from chelis_b200 import lib as L
+    lib = L.load()
+    a, b = ctypes.c_int64(), ctypes.c_int64()
+    for n in (0, 1, 7, 65536, 1000003):
+        for world in (1, 2, 3, 8):
+            for r in range(world):
+                assert lib.chelis_cuda_dp_shard(n, world, r, ctypes.byref(a), ctypes.byref(b)) == 0
+                assert (a.value, b.value) == dp.shard(n, world, r)
+    assert lib.chelis_cuda_dp_shard(5, 2, 2, ctypes.byref(a), ctypes.byref(b)) == 1
+    # no communicator: the all-reduce refuses, the world is one rank
+    w, r = ctypes.c_int32(), ctypes.c_int32()
+    assert lib.chelis_cuda_dp_world(ctypes.byref(w), ctypes.byref(r)) == 0 and (w.value, r.value) == (1, 0)
+    assert lib.chelis_cuda_dp_allreduce_sum(L.DTYPE_F32, None, 4) == 1
+    assert "dp_init" in L.last_error()
+    assert lib.chelis_cuda_dp_allreduce_sum(L.DTYPE_BOOL, None, 4) == 4
+    assert lib.chelis_cuda_dp_finalize(0) == 0
