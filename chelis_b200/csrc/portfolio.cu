@@ -8,18 +8,20 @@
 //   risk     = sqrt(matmul(w, matmul(Sigma, w)))
 //   cum[t]   = cumsum_t(matmul(R, w))         ([05-OP-53])
 //
-// One CTA owns one portfolio at a time: 10 "compute" warps and 1 "serial"
-// warp.  Pass 1 streams R in 64-row chunks (coalesced loads, the next
-// chunk prefetched into registers while the current one is reduced) to form
-// the column sums (canonical tree over t: aligned 64-row chunks are
-// subtrees) and the row dot products R.w (canonical tree over a).  Pass 2
-// re-streams R (an L2 hit: the CTA read the same 129 KiB moments before),
-// centres each chunk into shared memory and accumulates C^T C on the FP64
-// tensor path (mma.sync m16n8k4 .f64).  Sigma is symmetric, so only the 20
-// m16n8 tiles that touch the upper triangle are computed (two per compute
-// warp, sharing their A fragment) and mirrored: 37.5 % fewer DMMAs.  The
-// serial warp runs the sequential cumsum of R.w concurrently with pass 2;
-// the compute warps synchronise among themselves with a named barrier.
+// One CTA carries two portfolios at a time on two warp groups.  The 4
+// "stream" warps run pass 1 of portfolio p+1: the column sums (one thread per
+// asset, 16 rows at a time from HBM, each aligned 16-row run a subtree of the
+// canonical tree over t, pushed through a carry tree), the row dot products
+// R.w (one warp per row, canonical tree over a) and then the sequential
+// cumsum of R.w ([05-OP-53]).  Meanwhile the 10 "tensor" warps run pass 2 of
+// portfolio p: they re-stream R (an L2 hit: pass 1 read it one portfolio
+// earlier), centre each 64-row chunk into shared memory and accumulate C^T C
+// on the FP64 tensor path (mma.sync m16n8k4 .f64).  Sigma is symmetric, so
+// only the 20 m16n8 tiles that touch the upper triangle are computed (two per
+// tensor warp, sharing their A fragment) and mirrored: 37.5 % fewer DMMAs.
+// The groups meet once per portfolio (__syncthreads); the tensor warps
+// synchronise among themselves with named barrier 1, the stream warps with
+// named barrier 2.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -34,10 +36,11 @@ namespace portfolio {
 
 constexpr int A = 64;         // assets (the kernel is specialised to 64)
 constexpr int CH = 64;        // rows of R per chunk
-constexpr int CW = 10;        // compute warps
-constexpr int CT = CW * 32;   // compute threads
-constexpr int THREADS = CT + 32;
-constexpr int PER_T = (CH * A + CT - 1) / CT;  // 13 doubles per compute thread per chunk
+constexpr int CW = 10;        // tensor warps
+constexpr int CT = CW * 32;   // tensor threads
+constexpr int SW = 4;         // stream warps
+constexpr int THREADS = CT + SW * 32;
+constexpr int PER_T = (CH * A + CT - 1) / CT;  // 13 doubles per tensor thread per chunk
 
 __device__ __forceinline__ int sw(int k, int a) { return k * A + (a ^ ((k & 3) << 2)); }
 
@@ -53,10 +56,9 @@ __device__ __forceinline__ double canon(double x) {
     return isnan(x) ? __longlong_as_double(0x7ff8000000000000ll) : x;
 }
 
-// barrier among the compute warps only (named barrier 1)
-__device__ __forceinline__ void compute_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
-}
+// barriers among the tensor warps only (1) and among the stream warps only (2)
+__device__ __forceinline__ void tensor_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
+__device__ __forceinline__ void stream_sync() { asm volatile("bar.sync 2, %0;" ::"n"(SW * 32) : "memory"); }
 
 // The upper-triangle tiles: warp w owns tiles (mi, nj) and (mi, nj + 1).
 __device__ __forceinline__ void warp_tiles(int w, int &mi, int &nj) {
@@ -67,122 +69,168 @@ __device__ __forceinline__ void warp_tiles(int w, int &mi, int &nj) {
     else { mi = 3; nj = 6; }
 }
 
+constexpr int BR = 16;  // rows of a stream block
+
+struct Shared {
+    double mean[2][A];   // per portfolio slot (portfolio i uses slot i & 1)
+    double wv[2][A];
+    double rw[2][256];   // R.w halves of the portfolio in pass 1: assets [0, 32) and [32, 64)
+    double colpart[A];   // column sums of rows [128, t)
+    double u[A];
+    double ring[2][2][BR * A];  // [half][stage]: blocks of R in flight for pass 1
+};
+
+// barriers of one half of the stream warps (ids 3 and 4, 64 threads)
+__device__ __forceinline__ void half_sync(int half) {
+    if (half) asm volatile("bar.sync 4, 64;" ::: "memory");
+    else asm volatile("bar.sync 3, 64;" ::: "memory");
+}
+
+// Pass 1 of portfolio p on the stream warps: mean, w, R.w and its cumsum.
+// Threads st and st + 64 take asset a = st & 63; the first 64 threads rows
+// [0, 128), the others rows [128, t) -- the aligned 128-leaf subtree of the
+// canonical tree over t and the rest of the tree -- 16 rows at a time,
+// copied into shared memory asynchronously (cp.async) one block ahead.  The
+// same rows give R.w: the products of row t over a warp's 32 assets pair up
+// by the xor butterfly (aligned subtrees of the tree over a), and the two
+// warps' halves meet in the cumsum.
+__device__ __forceinline__ void stream_pass(const double *__restrict__ R, const double *__restrict__ w,
+                                            int t_len, double *__restrict__ cum, Shared &sh, int slot,
+                                            int st) {
+    const int lane = st & 31, a = st & (A - 1), half = st >> 6, wa = a >> 5, hs = st & 63;
+    if (st < A) sh.wv[slot][st] = w[st];
+    stream_sync();  // wv visible
+    const double wa_v = sh.wv[slot][a];
+    const int split = t_len > 128 ? 128 : t_len;
+    const int r0 = half ? split : 0, r1 = half ? t_len : split;
+    // copy rows [t0, t0 + BR) (those below r1) into ring stage `stg`: 16-byte
+    // pieces, 8 per thread of the half
+    auto copy = [&](int t0, int stg) {
+        double *dst = sh.ring[half][stg];
+#pragma unroll
+        for (int j = 0; j < BR * A / 2 / 64; ++j) {
+            const int e = hs + j * 64;           // 16-byte piece
+            const int row = e / (A / 2), col = (e % (A / 2)) * 2;
+            const bool ok = t0 + row < r1;
+            dmma::cp_async16(dst + row * A + col, ok ? R + (t0 + row) * A + col : R, ok);
+        }
+        dmma::cp_async_commit();
+    };
+    double level[8];
+    int64_t count = 0;
+    double tail = 0.0;
+    bool has_tail = false;
+    if (r0 < r1) copy(r0, 0);
+    for (int t0 = r0, stg = 0; t0 < r1; t0 += BR, stg ^= 1) {
+        const int nv = (r1 - t0) < BR ? (r1 - t0) : BR;
+        dmma::cp_async_wait<0>();
+        half_sync(half);  // block t0 landed for every thread; stage stg ^ 1 is free
+        if (t0 + BR < r1) copy(t0 + BR, stg ^ 1);
+        const double *blk = sh.ring[half][stg];
+        double v[BR];
+#pragma unroll
+        for (int i = 0; i < BR; ++i) v[i] = blk[i * A + a];
+        // R.w of rows t0 .. t0 + BR: this warp's 32 products per row, tree
+        // over a by recursive halving -- at level L a lane keeps BR >> L rows
+        // and adds its partner's (lane ^ 2^(L-1)) aligned 2^L-lane subtree
+        // of them; after four levels lane l holds row l & 15, and one more
+        // xor-16 step completes the 32-lane subtree.
+        {
+            double q[BR];
+#pragma unroll
+            for (int i = 0; i < BR; ++i) q[i] = __dmul_rn(v[i], wa_v);
+#pragma unroll
+            for (int lvl = 0; lvl < 4; ++lvl) {
+                const int off = 1 << lvl, n = BR >> (lvl + 1);  // rows kept after this level
+                const bool upper = (lane & off) != 0;          // keeps the upper half of its rows
+#pragma unroll
+                for (int i = 0; i < n; ++i) {
+                    const double send = upper ? q[i] : q[i + n];
+                    const double mine = upper ? q[i + n] : q[i];
+                    q[i] = __dadd_rn(mine, __shfl_xor_sync(0xffffffffu, send, off));
+                }
+            }
+            const double s = __dadd_rn(q[0], __shfl_xor_sync(0xffffffffu, q[0], 16));
+            // lane l now holds the row whose index bits are lane bits 0..3
+            // (each level kept the half named by that lane bit)
+            const int row = ((lane & 1) << 3) | ((lane & 2) << 1) | ((lane & 4) >> 1) | ((lane & 8) >> 3);
+            if (lane < 16 && row < nv) sh.rw[wa][t0 + row] = s;
+        }
+        // column subtree of these rows (pairwise, absent rows pass through)
+#pragma unroll
+        for (int width = 1; width < BR; width <<= 1)
+#pragma unroll
+            for (int i = 0; i + width < BR; i += 2 * width)
+                v[i] = tree_pair(v[i], i < nv, v[i + width], i + width < nv);
+        if (nv == BR) {
+            double carry = v[0];
+            int depth = 0;
+            for (int64_t pending = count++; pending & 1; pending >>= 1, ++depth)
+                carry = __dadd_rn(level[depth], carry);
+            level[depth] = carry;
+        } else {
+            tail = v[0];
+            has_tail = true;
+        }
+    }
+    double total = tail;
+    bool found = has_tail;
+    int depth = 0;
+    for (int64_t remaining = count; remaining; remaining >>= 1, ++depth)
+        if (remaining & 1) {
+            total = found ? __dadd_rn(level[depth], total) : level[depth];
+            found = true;
+        }
+    if (half) sh.colpart[a] = total;
+    stream_sync();  // colpart and both R.w halves complete; the ring is idle
+    if (half == 0) {
+        // rows [0, 128) are a complete subtree when t > 128: on the left
+        const double s = t_len > 128 ? __dadd_rn(total, sh.colpart[a]) : total;
+        sh.mean[slot][a] = __ddiv_rn(s, static_cast<double>(t_len));
+    } else if (hs == 0) {
+        // sequential prefix of R.w = (assets [0,32) + assets [32,64)) per row
+        double acc = __dadd_rn(sh.rw[0][0], sh.rw[1][0]);
+        cum[0] = canon(acc);
+        for (int k = 1; k < t_len; ++k) {
+            acc = __dadd_rn(acc, __dadd_rn(sh.rw[0][k], sh.rw[1][k]));
+            cum[k] = canon(acc);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(THREADS, 2)
     portfolio_kernel(const double *__restrict__ r_all, const double *__restrict__ w_all,
                      int64_t count, int t_len, double *__restrict__ sigma_all,
                      double *__restrict__ risk_all, double *__restrict__ cum_all) {
-    extern __shared__ __align__(16) double tiles[];  // 2 x [CH * A]: staged chunks
-    double *tile = tiles;                           // pass 1, Sigma.w: buffer 0
-    __shared__ double wv[A];
-    __shared__ double mean[A];
-    __shared__ double colsum[4][A];                 // per-chunk column subtree sums
-    __shared__ double segsum[4][A];                 // 16-row segment sums of a chunk
-    __shared__ bool segvalid[4][A];
-    __shared__ double rw[256 + 4];                  // R.w per t (t_len <= 256)
-    __shared__ double u[A];
+    extern __shared__ __align__(16) double tiles[];  // 2 x [CH * A]: staged centred chunks
+    __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool serial = warp == CW;
+    const bool tensor = warp < CW;
     const int g = lane >> 2, tq = lane & 3;
     const int nchunks = (t_len + CH - 1) / CH;
-    const double tf = static_cast<double>(t_len), tm1 = static_cast<double>(t_len - 1);
+    const double tm1 = static_cast<double>(t_len - 1);
     int mi = 0, nj = 0;
-    if (!serial) warp_tiles(warp, mi, nj);
+    if (tensor) warp_tiles(warp, mi, nj);
+    const int64_t stride = gridDim.x;
 
-    for (int64_t p = blockIdx.x; p < count; p += gridDim.x) {
+    // portfolio i of this CTA is blockIdx.x + i * gridDim.x; pass 1 of
+    // portfolio i + 1 overlaps pass 2 of portfolio i
+    int64_t p = blockIdx.x;
+    if (!tensor && p < count)
+        stream_pass(r_all + p * t_len * A, w_all + p * A, t_len, cum_all + p * t_len, sh, 0, tid - CT);
+    __syncthreads();
+    for (int slot = 0; p < count; p += stride, slot ^= 1) {
+        if (!tensor) {
+            const int64_t pn = p + stride;
+            if (pn < count)
+                stream_pass(r_all + pn * t_len * A, w_all + pn * A, t_len, cum_all + pn * t_len, sh,
+                            slot ^ 1, tid - CT);
+            __syncthreads();
+            continue;
+        }
         const double *R = r_all + p * t_len * A;
-        __syncthreads();  // all warps: the previous portfolio is finished
-        if (tid < A) wv[tid] = w_all[p * A + tid];  // read after pass 1's first barrier
-
-        if (!serial) {
-            // ---------------- pass 1: column sums and R.w ----------------
-            double nxt[PER_T];
-#pragma unroll
-            for (int j = 0; j < PER_T; ++j) {
-                const int e = tid + j * CT;
-                nxt[j] = (e < CH * A && e / A < t_len) ? __ldcs(R + e) : 0.0;
-            }
-            for (int q = 0; q < nchunks; ++q) {
-                const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
-#pragma unroll
-                for (int j = 0; j < PER_T; ++j) {
-                    const int e = tid + j * CT;
-                    if (e < CH * A) tile[e] = nxt[j];
-                }
-                compute_sync();
-                if (q + 1 < nchunks) {
-                    const double *src = R + static_cast<int64_t>(q + 1) * CH * A;
-                    const int rows2 = (t_len - (q + 1) * CH) < CH ? (t_len - (q + 1) * CH) : CH;
-#pragma unroll
-                    for (int j = 0; j < PER_T; ++j) {
-                        const int e = tid + j * CT;
-                        nxt[j] = (e < CH * A && e / A < rows2) ? __ldcs(src + e) : 0.0;
-                    }
-                }
-                if (tid < 4 * A) {
-                    // column a, rows [16*seg, 16*seg + 16): an aligned 16-leaf
-                    // subtree of the chunk's canonical tree, reduced pairwise
-                    // (rows past the chunk end are absent leaves)
-                    const int a = tid & (A - 1), seg = tid >> 6;
-                    double v[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) v[i] = tile[(seg * 16 + i) * A + a];
-                    const int nv = rows - seg * 16;  // valid leaves of this segment
-#pragma unroll
-                    for (int width = 1; width < 16; width <<= 1)
-#pragma unroll
-                        for (int i = 0; i + width < 16; i += 2 * width)
-                            v[i] = tree_pair(v[i], i < nv, v[i + width], i + width < nv);
-                    segsum[seg][a] = v[0];
-                    segvalid[seg][a] = nv > 0;
-                }
-                compute_sync();
-                if (tid < A) {
-                    double s4[4];
-                    bool v4[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) { s4[i] = segsum[i][tid]; v4[i] = segvalid[i][tid]; }
-                    const double lo = tree_pair(s4[0], v4[0], s4[1], v4[1]);
-                    const double hi = tree_pair(s4[2], v4[2], s4[3], v4[3]);
-                    colsum[q][tid] = tree_pair(lo, v4[0], hi, v4[2]);
-                }
-                // R.w for each row of the chunk: lane l holds a = 2l, 2l+1
-                for (int k = warp; k < rows; k += CW) {
-                    const double p0 = __dmul_rn(tile[k * A + 2 * lane], wv[2 * lane]);
-                    const double p1 = __dmul_rn(tile[k * A + 2 * lane + 1], wv[2 * lane + 1]);
-                    const double s = warp_tree_full(__dadd_rn(p0, p1));
-                    if (lane == 0) rw[q * CH + k] = s;
-                }
-                compute_sync();
-            }
-            if (tid < A) {
-                double c[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) c[q] = q < nchunks ? colsum[q][tid] : 0.0;
-#pragma unroll
-                for (int width = 1; width < 4; width <<= 1)
-#pragma unroll
-                    for (int i = 0; i + width < 4; i += 2 * width)
-                        c[i] = tree_pair(c[i], i < nchunks, c[i + width], i + width < nchunks);
-                mean[tid] = __ddiv_rn(c[0], tf);
-            }
-        }
-        __syncthreads();  // rw and mean complete
-
-        if (serial) {
-            // sequential prefix ([05-OP-53]): the first input is the first
-            // prefix; runs while the compute warps do pass 2
-            if (lane == 0) {
-                double acc = rw[0];
-                double *cum = cum_all + p * t_len;
-                cum[0] = canon(acc);
-                for (int k = 1; k < t_len; ++k) {
-                    acc = __dadd_rn(acc, rw[k]);
-                    cum[k] = canon(acc);
-                }
-            }
-            continue;  // joins the next portfolio's first __syncthreads
-        }
-
+        const double *mean = sh.mean[slot];
+        const double *wv = sh.wv[slot];
         // ---------------- pass 2: upper tiles of Sigma = C^T C ----------------
         double acc[2][4];
 #pragma unroll
@@ -190,11 +238,15 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[j][q] = 0.0;
         double nxt[PER_T];
+        auto fetch = [&](int q) {
+            const double *src = R + static_cast<int64_t>(q) * CH * A;
+            const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
 #pragma unroll
-        for (int j = 0; j < PER_T; ++j) {
-            const int e = tid + j * CT;
-            nxt[j] = (e < CH * A && e / A < t_len) ? __ldg(R + e) : 0.0;
-        }
+            for (int j = 0; j < PER_T; ++j) {
+                const int e = tid + j * CT;
+                nxt[j] = (e < CH * A && e / A < rows) ? __ldg(src + e) : 0.0;
+            }
+        };
         // centred chunk q into buffer q & 1 (rows past the end are zeros, so
         // the k loop can always run all CH / 4 steps: they add exact zeros)
         auto stage = [&](int q) {
@@ -209,17 +261,9 @@ __global__ void __launch_bounds__(THREADS, 2)
                 }
             }
         };
-        auto fetch = [&](int q) {
-            const double *src = R + static_cast<int64_t>(q) * CH * A;
-            const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
-#pragma unroll
-            for (int j = 0; j < PER_T; ++j) {
-                const int e = tid + j * CT;
-                nxt[j] = (e < CH * A && e / A < rows) ? __ldg(src + e) : 0.0;
-            }
-        };
+        fetch(0);
         stage(0);
-        compute_sync();
+        tensor_sync();
         for (int q = 0; q < nchunks; ++q) {
             if (q + 1 < nchunks) fetch(q + 1);
             const double *buf = tiles + (q & 1) * CH * A;
@@ -235,10 +279,11 @@ __global__ void __launch_bounds__(THREADS, 2)
             }
             // the other buffer was last read before the previous barrier
             if (q + 1 < nchunks) stage(q + 1);
-            compute_sync();
+            tensor_sync();
         }
         // Sigma / (T-1) for the upper entries (row <= col), mirrored
         double *S = sigma_all + p * A * A;
+        double *tile = tiles;  // Sigma, for Sigma.w (buffer 0 is free after the barrier)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
 #pragma unroll
@@ -257,21 +302,22 @@ __global__ void __launch_bounds__(THREADS, 2)
                 }
             }
         }
-        compute_sync();
+        tensor_sync();
         // u = Sigma.w (tree over j), then w.u (tree over i), risk = sqrt
         for (int i = warp; i < A; i += CW) {
             const double p0 = __dmul_rn(tile[i * A + 2 * lane], wv[2 * lane]);
             const double p1 = __dmul_rn(tile[i * A + 2 * lane + 1], wv[2 * lane + 1]);
             const double s = warp_tree_full(__dadd_rn(p0, p1));
-            if (lane == 0) u[i] = s;
+            if (lane == 0) sh.u[i] = s;
         }
-        compute_sync();
+        tensor_sync();
         if (warp == 0) {
-            const double p0 = __dmul_rn(wv[2 * lane], u[2 * lane]);
-            const double p1 = __dmul_rn(wv[2 * lane + 1], u[2 * lane + 1]);
+            const double p0 = __dmul_rn(wv[2 * lane], sh.u[2 * lane]);
+            const double p1 = __dmul_rn(wv[2 * lane + 1], sh.u[2 * lane + 1]);
             const double s = warp_tree_full(__dadd_rn(p0, p1));
             if (lane == 0) risk_all[p] = canon(__dsqrt_rn(s));
         }
+        __syncthreads();  // both groups: portfolio p done, p + stride's pass 1 done
     }
 }
 
