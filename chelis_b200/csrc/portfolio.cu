@@ -35,13 +35,12 @@ extern std::atomic<uint64_t> g_launches;
 namespace portfolio {
 
 constexpr int A = 64;         // assets (the kernel is specialised to 64)
-constexpr int CH = 64;        // rows of R per chunk
+constexpr int CH = 32;        // rows of R per ring slot
+constexpr int NST = 4;        // ring slots (CH * A doubles each)
 constexpr int CW = 10;        // tensor warps
 constexpr int CT = CW * 32;   // tensor threads
 constexpr int SW = 4;         // stream warps
 constexpr int THREADS = CT + SW * 32;
-constexpr int PER_T = (CH * A + CT - 1) / CT;  // 13 doubles per tensor thread per chunk
-
 __device__ __forceinline__ int sw(int k, int a) { return k * A + (a ^ ((k & 3) << 2)); }
 
 __device__ __forceinline__ void dmma(double (&d)[4], double a0, double a1, double b0) {
@@ -202,7 +201,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     portfolio_kernel(const double *__restrict__ r_all, const double *__restrict__ w_all,
                      int64_t count, int t_len, double *__restrict__ sigma_all,
                      double *__restrict__ risk_all, double *__restrict__ cum_all) {
-    extern __shared__ __align__(16) double tiles[];  // 2 x [CH * A]: staged centred chunks
+    extern __shared__ __align__(16) double tiles[];  // NST x [CH * A]: the pass-2 ring
     __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool tensor = warp < CW;
@@ -232,58 +231,60 @@ __global__ void __launch_bounds__(THREADS, 2)
         const double *mean = sh.mean[slot];
         const double *wv = sh.wv[slot];
         // ---------------- pass 2: upper tiles of Sigma = C^T C ----------------
+        // R streams through a ring of NST chunks of CH rows in shared memory
+        // by cp.async (an L2 hit: pass 1 read it one portfolio earlier), NST - 1
+        // chunks in flight; the fragments are centred as they are read
+        // (C = R - mean, the same one rounding as a centred copy), rows past
+        // t are exact zeros.
         double acc[2][4];
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[j][q] = 0.0;
-        double nxt[PER_T];
-        auto fetch = [&](int q) {
-            const double *src = R + static_cast<int64_t>(q) * CH * A;
-            const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
+        const int ca0 = mi * 16 + g, ca1 = ca0 + 8, cb0 = nj * 8 + g, cb1 = cb0 + 8;
+        const double m0 = mean[ca0], m1 = mean[ca1], n0 = mean[cb0], n1 = mean[cb1];
+        auto copy = [&](int q) {  // chunk q into ring slot q % NST (empty group past the end)
+            if (q < nchunks) {
+                double *dst = tiles + (q % NST) * CH * A;
+                const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
+                const double *src = R + static_cast<int64_t>(q) * CH * A;
 #pragma unroll
-            for (int j = 0; j < PER_T; ++j) {
-                const int e = tid + j * CT;
-                nxt[j] = (e < CH * A && e / A < rows) ? __ldg(src + e) : 0.0;
-            }
-        };
-        // centred chunk q into buffer q & 1 (rows past the end are zeros, so
-        // the k loop can always run all CH / 4 steps: they add exact zeros)
-        auto stage = [&](int q) {
-            const int rows = (t_len - q * CH) < CH ? (t_len - q * CH) : CH;
-            double *buf = tiles + (q & 1) * CH * A;
-#pragma unroll
-            for (int j = 0; j < PER_T; ++j) {
-                const int e = tid + j * CT;
-                if (e < CH * A) {
-                    const int k = e / A, a = e % A;
-                    buf[sw(k, a)] = k < rows ? __dsub_rn(nxt[j], mean[a]) : 0.0;
+                for (int j = 0; j < (CH * A / 2 + CT - 1) / CT; ++j) {
+                    const int e = tid + j * CT;  // 16-byte piece
+                    if (e < CH * A / 2) {
+                        const int k = e / (A / 2), c = (e % (A / 2)) * 2;
+                        const bool ok = k < rows;
+                        dmma::cp_async16(dst + sw(k, c), ok ? src + k * A + c : src, ok);
+                    }
                 }
             }
+            dmma::cp_async_commit();
         };
-        fetch(0);
-        stage(0);
-        tensor_sync();
+#pragma unroll
+        for (int q = 0; q < NST - 1; ++q) copy(q);
         for (int q = 0; q < nchunks; ++q) {
-            if (q + 1 < nchunks) fetch(q + 1);
-            const double *buf = tiles + (q & 1) * CH * A;
+            dmma::cp_async_wait<NST - 2>();
+            tensor_sync();  // chunk q landed for all; slot (q - 1) % NST is free
+            copy(q + NST - 1);
+            const double *buf = tiles + (q % NST) * CH * A;
+            const int k0 = q * CH;
 #pragma unroll
             for (int ks = 0; ks < CH / 4; ++ks) {
                 const int k = ks * 4 + tq;
-                const double a0 = buf[sw(k, mi * 16 + g)];
-                const double a1 = buf[sw(k, mi * 16 + g + 8)];
-                const double b0 = buf[sw(k, nj * 8 + g)];
-                const double b1 = buf[sw(k, (nj + 1) * 8 + g)];
+                const bool in = k0 + k < t_len;
+                const double a0 = in ? __dsub_rn(buf[sw(k, ca0)], m0) : 0.0;
+                const double a1 = in ? __dsub_rn(buf[sw(k, ca1)], m1) : 0.0;
+                const double b0 = in ? __dsub_rn(buf[sw(k, cb0)], n0) : 0.0;
+                const double b1 = in ? __dsub_rn(buf[sw(k, cb1)], n1) : 0.0;
                 dmma(acc[0], a0, a1, b0);
                 dmma(acc[1], a0, a1, b1);
             }
-            // the other buffer was last read before the previous barrier
-            if (q + 1 < nchunks) stage(q + 1);
-            tensor_sync();
         }
+        dmma::cp_async_wait<0>();
+        tensor_sync();  // every warp is done with the ring: Sigma may take slots 0 and 1
         // Sigma / (T-1) for the upper entries (row <= col), mirrored
         double *S = sigma_all + p * A * A;
-        double *tile = tiles;  // Sigma, for Sigma.w (buffer 0 is free after the barrier)
+        double *tile = tiles;  // Sigma, for Sigma.w (ring slots 0 and 1)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
 #pragma unroll
@@ -339,7 +340,7 @@ extern "C" int chelis_cuda_portfolio_f64(const double *r, const double *w, int64
     cudaStream_t s = current_stream();
     int64_t grid = static_cast<int64_t>(sm_count()) * 2;
     if (grid > count) grid = count;
-    constexpr int smem = 2 * portfolio::CH * portfolio::A * sizeof(double);
+    constexpr int smem = portfolio::NST * portfolio::CH * portfolio::A * sizeof(double);
     CHELIS_TRY(check_cuda(cudaFuncSetAttribute(portfolio::portfolio_kernel,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                           "cudaFuncSetAttribute(portfolio_kernel)"));

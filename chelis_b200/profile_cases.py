@@ -7,6 +7,8 @@
     python -m chelis_b200.profile_cases block       # config 4 step, batch 1
     python -m chelis_b200.profile_cases attention   # config 4 attention, 8 x 16 heads x 2048 x 64,
                                                     # fused forward + reverse mode
+    python -m chelis_b200.profile_cases fused       # generic FusedElem groups on 16384 x 4096 f32:
+                                                    # x*gamma+beta, then sum of squares per row
 
 Each case builds its inputs on the device, runs the hot path once and
 synchronises; inputs exceed the 126 MB L2 except where the case is smaller
@@ -45,6 +47,11 @@ def run(case: str) -> None:
         q, k, v, do = (torch.randn(128, 2048, 64, device="cuda", generator=g) for _ in range(4))
         o, lse = ops.attention_causal(q, k, v, 0.125, with_lse=True)
         ops.attention_causal_bwd(q, k, v, o, lse, do, 0.125)
+    elif case == "fused":
+        from . import fused as F
+        x, g, be = W.torch_chain_inputs()
+        ops.fused_elementwise(F.parse("mul x0 x1; add v0 x2"), [x, g, be])
+        ops.fused_reduce(F.parse("mul x0 x0"), [x], axis=1)
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
