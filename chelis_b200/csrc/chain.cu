@@ -7,8 +7,8 @@
 // balanced_adjoint_sum (:1713-1745).
 //
 // One CTA of T threads owns one row at a time (the rows.cu layout: chunks of
-// 4T elements, thread t holds [4t, 4t+4) of each).  All row sums are the
-// canonical adjacent-pair tree, bit for bit.  The forward can save, per row,
+// 4T elements, thread t holds [4t, 4t+4) of each).  In EXACT mode every row
+// sum is the canonical adjacent-pair tree, bit for bit.  The forward can save, per row,
 // its statistics (mean, sqrt(var+eps), softmax max and denominator) and the
 // keyed-dropout keep bits (one bit per element, warp-ballot packed), so the
 // adjoint re-derives nothing that needs a reduction or the RNG.
@@ -19,8 +19,12 @@
 // so each costs one barrier.
 //
 // Modes: EXACT divides where the C lane divides (IEEE __fdiv_rn) and uses
-// CUDA's expf; FAST multiplies by per-row reciprocals and uses __expf
-// (ex2.approx); both stay within f32 rel 1e-5 of the oracle.
+// CUDA's expf, following the adjoint graph step by step; FAST multiplies by
+// per-row reciprocals, uses __expf (ex2.approx), reduces in butterfly order,
+// folds the row sum into the softmax denominator's reduction (four block
+// reductions per forward row instead of five) and runs the adjoint in its
+// closed form (two reductions instead of three); both stay within f32 rel
+// 1e-5 of the oracle.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -300,6 +304,123 @@ struct RowRing {
 };
 
 // ---------------------------------------------------------------------------
+// FAST-mode row statistics.  Four block reductions per row -- sum (mean), sum
+// of squared deviations (variance), max, and one joint reduction of the
+// softmax denominator z with its kept part ks = sum of exp(y - max) over the
+// elements dropout keeps -- where the EXACT form needs five: the forward's
+// row sum of dropout(softmax(y)) is ks / z / (1 - rate), so neither the
+// per-element division by z nor a reduction of the dropped-out probabilities
+// is needed.  Sums run in butterfly order with contraction allowed; every
+// result stays within f32 rel 1e-5 of the C lane's canonical trees.  The
+// forward and the adjoint's recomputing path both call fast_stats, so saved
+// and recomputed statistics are bit-identical.
+// ---------------------------------------------------------------------------
+template <int T, int NV>
+__device__ __forceinline__ void block_sums(float *a, float *red) {
+    constexpr int W = T / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int j = 0; j < NV; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], off);
+    if (lane == 0)
+#pragma unroll
+        for (int j = 0; j < NV; ++j) red[j * W + warp] = a[j];
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        float w[W];
+#pragma unroll
+        for (int i = 0; i < W; i += 4) {
+            const float4 q = *reinterpret_cast<const float4 *>(red + j * W + i);
+            w[i] = q.x; w[i + 1] = q.y; w[i + 2] = q.z; w[i + 3] = q.w;
+        }
+#pragma unroll
+        for (int width = 1; width < W; width <<= 1)
+#pragma unroll
+            for (int i = 0; i + width < W; i += 2 * width) w[i] += w[i + width];
+        a[j] = w[0];
+    }
+}
+
+template <int T>
+__device__ __forceinline__ float block_max_fast(float m, float *red) {
+    constexpr int W = T / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int i = 1; i < W; ++i) r = fmaxf(r, red[i]);
+    return r;
+}
+
+struct RowStats {
+    float mean, d, mx, z, ks;
+};
+
+// x: the row in the chunk layout (zeros past the row end); keepm: bit
+// (c*4+i) set where dropout keeps the element.  A NaN anywhere in the row
+// makes mean, and with it every later statistic but mx, NaN.
+template <int T, int NC, bool FULL>
+__device__ __forceinline__ RowStats fast_stats(const float (&x)[NC][4], uint32_t keepm, int n,
+                                               const float *sg, const float *sb, float eps,
+                                               float rh, Red<T, NC> &rs) {
+    RowStats st;
+    float a[2];
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) s += (x[c][0] + x[c][1]) + (x[c][2] + x[c][3]);
+    a[0] = s;
+    block_sums<T, 1>(a, rs.next());
+    st.mean = a[0] * rh;
+    float q = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float cc = x[c][i] - st.mean;
+            const bool valid = FULL || c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n;
+            q = valid ? fmaf(cc, cc, q) : q;
+        }
+    a[0] = q;
+    block_sums<T, 1>(a, rs.next());
+    st.d = __fsqrt_rn(a[0] * rh + eps);
+    const float rd = __frcp_rn(st.d);
+    float y[NC][4];
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const float4 g4 = ld4<T>(sg, c), b4 = ld4<T>(sb, c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const bool valid = FULL || c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n;
+            const float v = fmaf((x[c][i] - st.mean) * rd, at(g4, i), at(b4, i));
+            y[c][i] = valid ? v : -INFINITY;
+            m = fmaxf(m, y[c][i]);
+        }
+    }
+    st.mx = block_max_fast<T>(m, rs.next());
+    float z = 0.0f, ks = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float e = __expf(y[c][i] - st.mx);
+            z += e;
+            ks += ((keepm >> (c * 4 + i)) & 1u) ? e : 0.0f;
+        }
+    a[0] = z;
+    a[1] = ks;
+    block_sums<T, 2>(a, rs.next());
+    st.z = a[0];
+    st.ks = a[1];
+    return st;
+}
+
+// ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
 template <int T, int NC, bool EXACT, bool FULL>
@@ -337,6 +458,15 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 3) fwd_kernel(Params p) {
                     const uint32_t bits = __ballot_sync(0xffffffffu, (keepm >> (c * 4 + i)) & 1u);
                     if (lane == 0) kw[(c * (T / 32) + warp) * 4 + i] = bits;
                 }
+        }
+        if constexpr (!EXACT) {
+            const RowStats st = fast_stats<T, NC, FULL>(v, keepm, n, sg, sb, p.eps, p.rh, rs);
+            if (threadIdx.x == 0) {
+                p.rowsum[r] = canon(__fmul_rn(__fdiv_rn(st.ks, st.z), p.rden));
+                if (p.stats)
+                    *reinterpret_cast<float4 *>(p.stats + 4 * r) = make_float4(st.mean, st.d, st.mx, st.z);
+            }
+            continue;
         }
         const float s1 = tree4<T, NC, FULL>(v, n, rs);
         const float mean = div_<EXACT>(s1, p.hf, p.rh);
@@ -479,6 +609,9 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
             const float4 st = ring ? *reinterpret_cast<const float4 *>(slot + L + RowRing<T, NC>::WORDS)
                                    : *reinterpret_cast<const float4 *>(p.stats_in + 4 * r);
             mean = st.x; d = st.y; mx = st.z; z = st.w;
+        } else if constexpr (!EXACT) {
+            const RowStats st = fast_stats<T, NC, FULL>(c_, keepm, n, sg, sb, p.eps, p.rh, rs);
+            mean = st.mean; d = st.d; mx = st.mx; z = st.z;
         } else {
             mean = div_<EXACT>(tree4<T, NC, FULL>(c_, n, rs), p.hf, p.rh);
             float part[NC];
@@ -509,6 +642,82 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) y[c][i] = exp_<EXACT>(__fsub_rn(y[c][i], mx));
             z = tree4<T, NC, FULL>(y, n, rs);
+        }
+        if constexpr (!EXACT) {
+            // Closed form of the same adjoint: with s = softmax(y), g the
+            // replayed dropout cotangent (1/(1-rate) where kept, else 0) and
+            // q = sum(g s), dy = s (g - q); dgamma += dy nn, dbeta += dy;
+            // dn = dy gamma and dx = (dn - mean(dn) - nn mean(dn nn)) / d.
+            // Two block reductions (q, then mean(dn) with mean(dn nn)) where
+            // the graph's literal form takes three.
+            const float rd = __frcp_rn(d), rz = __frcp_rn(z);
+            float s[NC][4], nn[NC][4];
+            float red2[2];
+            float qp = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const float4 g4 = ld4<T>(sg, c), b4 = ld4<T>(sb, c);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const bool valid = FULL || c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n;
+                    nn[c][i] = (c_[c][i] - mean) * rd;
+                    const float y = fmaf(nn[c][i], at(g4, i), at(b4, i));
+                    s[c][i] = valid ? __expf(y - mx) * rz : 0.0f;
+                    qp += ((keepm >> (c * 4 + i)) & 1u) ? s[c][i] : 0.0f;
+                }
+            }
+            red2[0] = qp;
+            block_sums<T, 1>(red2, rs.next());
+            const float q = red2[0] * p.one_over_den;
+            if (ring) {
+                // every thread has read its slot (the reduction synchronised
+                // the CTA): refill it with the row RING ahead
+                if (*abort_flag) break;
+                if (threadIdx.x == 0 && issued < r_end) {
+                    rr.issue(li % RowRing<T, NC>::RING, p, issued);
+                    ++issued;
+                }
+            }
+            float sdn = 0.0f, sdnn = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const float4 g4 = ld4<T>(sg, c);
+                float dy[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float ds = ((keepm >> (c * 4 + i)) & 1u) ? p.one_over_den : 0.0f;
+                    dy[i] = s[c][i] * (ds - q);
+                    const float dn = dy[i] * at(g4, i);
+                    s[c][i] = dn;
+                    sdn += dn;
+                    sdnn = fmaf(dn, nn[c][i], sdnn);
+                }
+                acc_b[c].x += dy[0]; acc_b[c].y += dy[1]; acc_b[c].z += dy[2]; acc_b[c].w += dy[3];
+                acc_g[c].x = fmaf(dy[0], nn[c][0], acc_g[c].x);
+                acc_g[c].y = fmaf(dy[1], nn[c][1], acc_g[c].y);
+                acc_g[c].z = fmaf(dy[2], nn[c][2], acc_g[c].z);
+                acc_g[c].w = fmaf(dy[3], nn[c][3], acc_g[c].w);
+            }
+            red2[0] = sdn;
+            red2[1] = sdnn;
+            block_sums<T, 2>(red2, rs.next());
+            const float m1 = red2[0] * p.rh, m2 = red2[1] * p.rh;
+            float *dxr = p.dx + r * n;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int e0 = c * 4 * T + 4 * threadIdx.x;
+                float o[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = canon(rd * (fmaf(-nn[c][i], m2, s[c][i]) - m1));
+                if (vec && e0 + 3 < n) {
+                    __stcs(reinterpret_cast<float4 *>(dxr + e0), make_float4(o[0], o[1], o[2], o[3]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (e0 + i < n) dxr[e0 + i] = o[i];
+                }
+            }
+            continue;
         }
         const float rd = __fdiv_rn(1.0f, d);
         const float rz = __fdiv_rn(1.0f, z);

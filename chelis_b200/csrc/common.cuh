@@ -95,6 +95,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that acquires at cluster scope: pairs with arrivals that other
+// CTAs of the cluster make with release.cluster (mbar_arrive_cluster).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+// Arrive (release, cluster scope) on an mbarrier given by its
+// shared::cluster address, in this CTA or another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
 // Bounded wait: at most kMaxTries probes of at most ~1 us each (a few
 // seconds), far beyond any legal stall of these kernels (a whole CTA tile
 // main loop is well under 100 ms even at k = 10^6).  On timeout the error bit
@@ -105,6 +124,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
                                                   unsigned int err_code) {
     for (uint32_t i = 0; i < kMaxTries; ++i)
         if (mbar_try_wait(bar, parity)) return true;
+    report_device_error(err_code);
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity,
+                                                          unsigned int err_code) {
+    for (uint32_t i = 0; i < kMaxTries; ++i)
+        if (mbar_try_wait_cluster(bar, parity)) return true;
     report_device_error(err_code);
     return false;
 }
@@ -410,8 +436,34 @@ __host__ __device__ __forceinline__ uint64_t rng_word(uint64_t key, uint64_t ind
 // the test is (w >> 11) >= threshold with threshold the least 53-bit integer
 // whose f32 rounding reaches rate * 2^53 (computed exactly on the host by
 // dropout_threshold()).
-__device__ __forceinline__ bool dropout_keep(uint64_t key, uint64_t index, uint64_t threshold) {
-    return (rng_word(key, index) >> 11) >= threshold;
+//
+// (w >> 11) >= threshold  <=>  w >= lim = threshold << 11 (threshold < 2^53).
+// The last splitmix64 step is w = z ^ (z >> 31) with z = u * C2 mod 2^64, so
+// the top 32 bits of w are zh ^ (zh >> 31), zh = hi32(z) =
+// umulhi(lo(u), lo(C2)) + lo(u) hi(C2) + hi(u) lo(C2) mod 2^32.  Those bits
+// decide the comparison unless they equal the top 32 bits of lim (once in
+// 2^32 draws), when the full word is formed.
+__host__ __device__ __forceinline__ uint32_t mulhi_u32(uint32_t a, uint32_t b) {
+#ifdef __CUDA_ARCH__
+    return __umulhi(a, b);
+#else
+    return static_cast<uint32_t>((static_cast<uint64_t>(a) * b) >> 32);
+#endif
+}
+__host__ __device__ __forceinline__ bool dropout_keep(uint64_t key, uint64_t index, uint64_t threshold) {
+    constexpr uint64_t C2 = 0x94d049bb133111ebull;
+    constexpr uint32_t C2L = static_cast<uint32_t>(C2), C2H = static_cast<uint32_t>(C2 >> 32);
+    const uint64_t s = splitmix64(index);
+    uint64_t v = (key ^ ((s << 41) | (s >> 23))) + 0x9e3779b97f4a7c15ull;
+    v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+    v ^= v >> 27;
+    const uint64_t lim = threshold << 11;
+    const uint32_t ul = static_cast<uint32_t>(v), uh = static_cast<uint32_t>(v >> 32);
+    const uint32_t zh = mulhi_u32(ul, C2L) + ul * C2H + uh * C2L;
+    const uint32_t wh = zh ^ (zh >> 31), lh = static_cast<uint32_t>(lim >> 32);
+    if (wh != lh) return wh > lh;
+    const uint64_t z = v * C2;
+    return (z ^ (z >> 31)) >= lim;
 }
 
 }  // namespace chelis

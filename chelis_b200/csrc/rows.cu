@@ -408,6 +408,75 @@ __global__ void row_max_kernel(const float *__restrict__ x, int64_t rows, int64_
     }
 }
 
+// The same selection with float4 loads and 32-bit indices, for rows whose
+// width is a multiple of 4 (< 2^31) in a 16-byte aligned matrix: lane l scans
+// the quads l, l + 32, l + 64, ... of its row, so indices still increase
+// along a lane, with four quads in flight.  Within a lane an element
+// replaces the candidate iff the candidate is not NaN and the element is NaN
+// or strictly greater (the first NaN, else the first of equal maxima, stays);
+// lanes merge by the rule of row_max_kernel.
+__device__ __forceinline__ void max_take(float v, int j, float &best, int &bi) {
+    const bool take = !isnan(best) && (isnan(v) || v > best);
+    best = take ? v : best;
+    bi = take ? j : bi;
+}
+__global__ void row_max4_kernel(const float *__restrict__ x, int64_t rows, int cols,
+                                float *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int nq = cols >> 2;
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += warps) {
+        const float4 *row = reinterpret_cast<const float4 *>(x + r * cols);
+        float best = 0.0f;
+        int bi = INT_MAX;
+        int k = lane;
+        if (k < nq) {
+            const float4 a = __ldcs(row + k);
+            best = a.x;
+            bi = 4 * k;
+            max_take(a.y, 4 * k + 1, best, bi);
+            max_take(a.z, 4 * k + 2, best, bi);
+            max_take(a.w, 4 * k + 3, best, bi);
+            k += 32;
+        }
+        for (; k + 96 < nq; k += 128) {
+            float4 a[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) a[u] = __ldcs(row + k + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = 4 * (k + 32 * u);
+                max_take(a[u].x, j, best, bi);
+                max_take(a[u].y, j + 1, best, bi);
+                max_take(a[u].z, j + 2, best, bi);
+                max_take(a[u].w, j + 3, best, bi);
+            }
+        }
+        for (; k < nq; k += 32) {
+            const float4 a = __ldcs(row + k);
+            max_take(a.x, 4 * k, best, bi);
+            max_take(a.y, 4 * k + 1, best, bi);
+            max_take(a.z, 4 * k + 2, best, bi);
+            max_take(a.w, 4 * k + 3, best, bi);
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            bool take;
+            if (oi == INT_MAX) take = false;
+            else if (bi == INT_MAX) take = true;
+            else if (isnan(best) || isnan(ob)) {
+                take = isnan(ob) && (!isnan(best) || oi < bi);
+            } else if (ob > best) take = true;
+            else if (ob == best) take = oi < bi;
+            else take = false;
+            if (take) { best = ob; bi = oi; }
+        }
+        if (lane == 0) out[r] = best;
+    }
+}
+
 // Column sums (axis 0) of [rows, cols]: aligned row blocks of RB leaves
 // (complete subtrees of the canonical tree over rows) reduced per column
 // with a register carry tree, then the block sums reduced the same way by a
@@ -823,6 +892,12 @@ int chelis_cuda_row_max_f32(const float *x, int64_t rows, int64_t cols, float *o
     cudaStream_t s = current_stream();
     int64_t blocks = (rows * 32 + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
+    if (cols % 4 == 0 && cols < INT_MAX && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        row_max4_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, static_cast<int>(cols), out);
+        g_launches++;
+        CHELIS_LAUNCH_CHECK("row_max4_kernel");
+        return CHELIS_CUDA_OK;
+    }
     row_max_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, cols, out);
     g_launches++;
     CHELIS_LAUNCH_CHECK("row_max_kernel");

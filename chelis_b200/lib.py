@@ -94,6 +94,8 @@ SIGNATURES = {
     "chelis_cuda_dgemm": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
     "chelis_cuda_set_gemm_pairs": (c_int, [c_int]),
     "chelis_cuda_get_gemm_pairs": (c_int, []),
+    "chelis_cuda_set_gemm_split": (c_int, [c_int]),
+    "chelis_cuda_get_gemm_split": (c_int, []),
     "chelis_cuda_attention_causal_fwd": (c_int, [c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "chelis_cuda_attention_causal_bwd": (c_int, [c_i64, c_i64, c_i64, c_f32] + [c_vp] * 9),
     "chelis_cuda_sgemm_host": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),

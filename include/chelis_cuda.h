@@ -199,6 +199,14 @@ int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
  * up to the f32 accumulation order inside the tensor core.  Process-wide. */
 int chelis_cuda_set_gemm_pairs(int enable);
 int chelis_cuda_get_gemm_pairs(void);
+/* Where the 3xTF32 split happens for row-major products on CTA pairs
+ * (trans_a = trans_b = 0, more than 128 rows, lda / ldb and batch strides
+ * multiples of 4 floats, 16-byte aligned A and B): 1 = inside the main
+ * kernel, on the tiles staged in shared memory; 0 = the split pre-pass into
+ * scratch.  Results are bit-identical in both modes.  Process-wide.  No
+ * reference counterpart (hipBLAS has no split). */
+int chelis_cuda_set_gemm_split(int in_kernel);
+int chelis_cuda_get_gemm_split(void);
 /* [05-OP-30] matmul on HOST buffers (row-major, same argument meaning as
  * chelis_cuda_sgemm / chelis_cuda_dgemm, all pointers host pointers).  The
  * reference uploads both operands, runs hipBLAS and downloads C in sequence

@@ -250,3 +250,45 @@ def test_sgemm_split_k_matches_oracle(cuda, orc, m, n, k, batch):
         rows = slice(0, min(m, 64))
         ref = orc.gemm(a3[i][rows], b3[i])
         assert _rel_err(c3[i][rows], ref, a3[i][rows], b3[i]) <= 1e-5, i
+
+
+@pytest.mark.parametrize("m,n,k,batch,ld_pad", [
+    (300, 500, 700, 1, 0),       # ragged in m, n and k (zero fill past every edge)
+    (256, 256, 32, 1, 0),        # one pair tile, one k-block
+    (2404, 600, 64, 1, 0),       # tile-order groups, ragged last pair-row
+    (1024, 768, 96, 3, 0),       # batched
+    (256, 256, 8192, 1, 0),      # split-K (partials reduced in split order)
+    (520, 260, 333, 2, 12),      # leading dimensions wider than the rows
+])
+def test_sgemm_split_in_kernel_bit_identical(cuda, orc, m, n, k, batch, ld_pad):
+    """Row-major products split inside the CTA-pair kernel (tiles in shared
+    memory) give the same bits as the split pre-pass, and stay within the
+    3xTF32 bound of the oracle."""
+    import torch
+    a, b = W.gemm_inputs(m, n, k, np.float32, seed=m + 3 * n + k, batch=batch)
+    a3, b3 = a.reshape(batch, m, k), b.reshape(batch, k, n)
+    A = torch.zeros(batch, m, k + ld_pad, device="cuda")
+    B = torch.zeros(batch, k, n + ld_pad, device="cuda")
+    A[:, :, :k] = torch.from_numpy(a3).cuda()
+    B[:, :, :n] = torch.from_numpy(b3).cuda()
+    lda, ldb = k + ld_pad, n + ld_pad
+
+    def run():
+        c = torch.empty(batch, m, n, device="cuda")
+        L.call("chelis_cuda_sgemm", 0, 0, m, n, k, A.data_ptr(), lda, m * lda, B.data_ptr(), ldb,
+               k * ldb, c.data_ptr(), n, m * n, batch)
+        torch.cuda.synchronize()
+        return c
+
+    with cuda.gemm_split(True):
+        c1 = run()
+    with cuda.gemm_split(False):
+        c0 = run()
+    cuda.device_status()
+    g1 = c1.cpu().numpy().reshape(batch, m, n)
+    g0 = c0.cpu().numpy().reshape(batch, m, n)
+    assert (g1.view(np.uint32) == g0.view(np.uint32)).all()
+    rows = slice(0, min(m, 96))
+    for i in range(batch):
+        ref = orc.gemm(a3[i][rows], b3[i])
+        assert _rel_err(g1[i][rows], ref, a3[i][rows], b3[i]) <= 1e-5, i

@@ -67,6 +67,30 @@ def test_row_max_first_nan_and_ties(cuda, orc):
     assert bits_equal(cuda.row_max(t(x)).cpu().numpy(), orc.row_max(x))
 
 
+@pytest.mark.parametrize("rows,cols", [(9, 4), (9, 5), (12, 128), (12, 644), (10, 4096), (9, 4099)])
+def test_row_max_selection_rules(cuda, orc, rows, cols):
+    """First NaN (payload kept) wins, else the first of equal maxima (+0 / -0
+    order kept); vectorised rows (width % 4 == 0) and ragged ones."""
+    rng = np.random.default_rng(cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    nan1 = np.array([0x7fc00123], np.uint32).view(np.float32)[0]
+    nan2 = np.array([0xffc00456], np.uint32).view(np.float32)[0]
+    x[0, cols - 1] = nan1
+    x[1, :] = -np.inf
+    x[2, :] = 0.0
+    x[2, cols // 2] = -0.0
+    x[3, :] = -0.0
+    x[3, cols - 1] = 0.0
+    x[4, cols // 3] = nan2
+    x[4, cols - 1] = nan1
+    x[5, :] = nan2
+    x[6, :] = 7.0
+    x[7, 0] = np.inf
+    x[7, cols - 1] = np.inf
+    x[8, cols - 1] = 1e30
+    assert bits_equal(cuda.row_max(t(x)).cpu().numpy(), orc.row_max(x))
+
+
 def test_count_exact(cuda, orc):
     x = (np.random.default_rng(4).random(1_000_003) < 0.37).astype(np.uint8)
     assert cuda.count(t(x)) == orc.count(x)
