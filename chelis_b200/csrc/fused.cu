@@ -993,6 +993,13 @@ int fused_reduce_t(const fused::Program &p, int mode, int kind, int axis, int64_
 
 using namespace chelis;
 
+namespace chelis {
+namespace fusedjit {
+int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
+                    int mode, void *out, cudaStream_t s);
+}  // namespace fusedjit
+}  // namespace chelis
+
 extern "C" int chelis_cuda_fused_elementwise(int32_t dtype, const chelis_fused_step *steps,
                                              int32_t n_steps, const void *const *inputs,
                                              const int64_t *strides, int32_t n_inputs,
@@ -1008,6 +1015,9 @@ extern "C" int chelis_cuda_fused_elementwise(int32_t dtype, const chelis_fused_s
     if (reinterpret_cast<uintptr_t>(out) % elem != 0)
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "fused output is misaligned");
     cudaStream_t s = current_stream();
+    // the chain compiled for itself (fused_jit.cu) where it fits that form
+    const int jit = fusedjit::try_elementwise(dtype == CHELIS_DTYPE_F32, steps, n_steps, p, mode, out, s);
+    if (jit >= 0) return jit;
     return dtype == CHELIS_DTYPE_F32 ? launch_elementwise<float>(p, mode, static_cast<float *>(out), s)
                                      : launch_elementwise<double>(p, mode, static_cast<double *>(out), s);
 }

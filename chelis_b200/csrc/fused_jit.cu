@@ -1,0 +1,375 @@
+// fused_jit.cu -- FusedElem elementwise groups compiled per chain at run time.
+//
+// The reference's GPU lane JIT-compiles one kernel string per fused chain
+// (crates/chelis-backend-hip/src/kernels.rs fused_elementwise :2391, built
+// with hiprtc on every call, runtime/chelis_hip_runtime.h:409-453).  Here the
+// chain's steps become straight-line CUDA in one kernel, compiled once with
+// NVRTC for sm_100a and kept in a per-device cache keyed by the kernel text
+// (dtype, rank, which inputs run along the innermost axis, the steps): shapes
+// and strides are kernel arguments, so every tensor size of a given chain
+// shares one compiled kernel.  The interpreter in fused.cu stays the path for
+// groups this form does not cover (an innermost extent that is not a whole
+// number of 16-byte vectors, an input that is neither unit-stride nor
+// broadcast along the innermost axis, misaligned bases) and when NVRTC is
+// absent.
+//
+// Layout: a thread takes one 16-byte vector of the output (4 f32 / 2 f64
+// consecutive elements of one innermost row); every input with unit
+// innermost stride is read as the matching aligned vector, a broadcast input
+// (innermost stride 0) as one element.  Element offsets come from the flat
+// index by the division-by-invariant-integer decode of fused.cu.
+//
+// Step semantics are those of fused.cu apply_light / apply_heavy, written
+// out per opcode below: IEEE + - * / and sqrt through the _rn intrinsics (no
+// contraction), the canonical quiet NaN after every step but MaxElem /
+// MinElem, CUDA's libm for the transcendental steps, pow's signaling-NaN rule.
+// The kernel is compiled with the library's own floating-point flags, so the
+// JIT and the interpreter give the same bits (tested for every opcode).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nvrtc.h>
+
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace chelis {
+namespace fusedjit {
+
+constexpr int THREADS = 256;
+
+// Kernel argument block; the generated source declares the same struct.
+struct Args {
+    const void *in[fused::MAX_INPUTS];
+    void *out;
+    long long stride[fused::MAX_INPUTS][fused::MAX_RANK];
+    long long shape[fused::MAX_RANK];
+    unsigned div_mul[fused::MAX_RANK];
+    unsigned div_shr[fused::MAX_RANK];
+    long long nvec;
+};
+
+const char *kPrelude = R"SRC(
+struct Args {
+    const void *in[8];
+    void *out;
+    long long stride[8][6];
+    long long shape[6];
+    unsigned div_mul[6];
+    unsigned div_shr[6];
+    long long nvec;
+};
+__device__ __forceinline__ float cn(float x) { return isnan(x) ? __int_as_float(0x7fc00000) : x; }
+__device__ __forceinline__ double cn(double x) { return isnan(x) ? __longlong_as_double(0x7ff8000000000000ll) : x; }
+__device__ __forceinline__ bool snan(float x) { return isnan(x) && !(__float_as_uint(x) & 0x00400000u); }
+__device__ __forceinline__ bool snan(double x) {
+    return isnan(x) && !(static_cast<unsigned long long>(__double_as_longlong(x)) & 0x0008000000000000ull);
+}
+__device__ __forceinline__ float pw(float x, float y) { return (snan(x) || snan(y)) ? cn(x + y) : cn(powf(x, y)); }
+__device__ __forceinline__ double pw(double x, double y) { return (snan(x) || snan(y)) ? cn(x + y) : cn(pow(x, y)); }
+template <typename T> __device__ __forceinline__ T mx(T x, T y) { return (isnan(x) || (!isnan(y) && x >= y)) ? x : y; }
+template <typename T> __device__ __forceinline__ T mn(T x, T y) { return (isnan(x) || (!isnan(y) && x <= y)) ? x : y; }
+)SRC";
+
+// One step's expression over operands `a` (and `b`), in the dtype's spelling.
+std::string step_expr(int op, bool f32, const std::string &a, const std::string &b) {
+    auto fn = [&](const char *f, const char *d) { return std::string(f32 ? f : d); };
+    auto un = [&](const char *f, const char *d) { return "cn(" + fn(f, d) + "(" + a + "))"; };
+    switch (op) {
+        case CHELIS_FUSED_ADD: return "cn(" + fn("__fadd_rn", "__dadd_rn") + "(" + a + ", " + b + "))";
+        case CHELIS_FUSED_SUB: return "cn(" + fn("__fsub_rn", "__dsub_rn") + "(" + a + ", " + b + "))";
+        case CHELIS_FUSED_MUL: return "cn(" + fn("__fmul_rn", "__dmul_rn") + "(" + a + ", " + b + "))";
+        case CHELIS_FUSED_DIV: return "cn(" + fn("__fdiv_rn", "__ddiv_rn") + "(" + a + ", " + b + "))";
+        case CHELIS_FUSED_POW: return "pw(" + a + ", " + b + ")";
+        case CHELIS_FUSED_FLOOR_DIV:
+            return "cn(" + fn("floorf", "floor") + "(" + fn("__fdiv_rn", "__ddiv_rn") + "(" + a + ", " + b + ")))";
+        case CHELIS_FUSED_MAX_ELEM: return "mx(" + a + ", " + b + ")";
+        case CHELIS_FUSED_MIN_ELEM: return "mn(" + a + ", " + b + ")";
+        case CHELIS_FUSED_NEG: return "cn(-(" + a + "))";
+        case CHELIS_FUSED_RECIP:
+            return "cn(" + fn("__fdiv_rn(1.0f, ", "__ddiv_rn(1.0, ") + a + "))";
+        case CHELIS_FUSED_EXP: return un("expf", "exp");
+        case CHELIS_FUSED_LOG: return un("logf", "log");
+        case CHELIS_FUSED_SIN: return un("sinf", "sin");
+        case CHELIS_FUSED_SQRT: return un("__fsqrt_rn", "__dsqrt_rn");
+        case CHELIS_FUSED_COS: return un("cosf", "cos");
+        case CHELIS_FUSED_TAN: return un("tanf", "tan");
+        case CHELIS_FUSED_ATAN: return un("atanf", "atan");
+        case CHELIS_FUSED_TANH: return un("tanhf", "tanh");
+        case CHELIS_FUSED_ERF: return un("erff", "erf");
+        case CHELIS_FUSED_ERFC: return un("erfcf", "erfc");
+        case CHELIS_FUSED_ABS: return un("fabsf", "fabs");
+        case CHELIS_FUSED_FLOOR: return un("floorf", "floor");
+        case CHELIS_FUSED_CEIL: return un("ceilf", "ceil");
+        case CHELIS_FUSED_ROUND: return un("rintf", "rint");
+        default: return "";
+    }
+}
+
+// Kernel text for the chain; empty when the chain uses an op this form does
+// not spell (none today beyond the integer-only trunc_div, which
+// build_program rejects).
+std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps, int n_inputs,
+                          int rank, uint32_t unit_inner, bool i32) {
+    const int V = f32 ? 4 : 2;
+    const std::string T = f32 ? "float" : "double";
+    const std::string VT = f32 ? "float4" : "double2";
+    const char *lanes[4] = {"x", "y", "z", "w"};
+    std::string s = kPrelude;
+    s += "extern \"C\" __global__ void __launch_bounds__(256) chelis_fused_jit(Args a) {\n";
+    s += "  const long long step = (long long)gridDim.x * 256;\n";
+    s += "  for (long long q = (long long)blockIdx.x * 256 + threadIdx.x; q < a.nvec; q += step) {\n";
+    // decode the vector's first element into per-input offsets
+    if (i32) {
+        s += "    unsigned rem = (unsigned)(q * " + std::to_string(V) + ");\n";
+        for (int k = 0; k < n_inputs; ++k) s += "    int o" + std::to_string(k) + " = 0;\n";
+        for (int d = rank - 1; d >= 0; --d) {
+            const std::string D = std::to_string(d);
+            if (d > 0) {
+                s += "    { const unsigned qd = a.div_mul[" + D + "] ? (__umulhi(rem, a.div_mul[" + D +
+                     "]) >> a.div_shr[" + D + "]) : rem;\n";
+                s += "      const int c = (int)(rem - qd * (unsigned)a.shape[" + D + "]); rem = qd;\n";
+            } else {
+                s += "    { const int c = (int)rem;\n";
+            }
+            for (int k = 0; k < n_inputs; ++k)
+                s += "      o" + std::to_string(k) + " += c * (int)a.stride[" + std::to_string(k) + "][" + D + "];\n";
+            s += "    }\n";
+        }
+    } else {
+        s += "    long long rem = q * " + std::to_string(V) + ";\n";
+        for (int k = 0; k < n_inputs; ++k) s += "    long long o" + std::to_string(k) + " = 0;\n";
+        for (int d = rank - 1; d >= 0; --d) {
+            const std::string D = std::to_string(d);
+            s += "    { long long c = rem;";
+            if (d > 0) s += " c = rem % a.shape[" + D + "]; rem /= a.shape[" + D + "];";
+            s += "\n";
+            for (int k = 0; k < n_inputs; ++k)
+                s += "      o" + std::to_string(k) + " += c * a.stride[" + std::to_string(k) + "][" + D + "];\n";
+            s += "    }\n";
+        }
+    }
+    // loads: unit-stride inputs as one vector, broadcast ones as one element
+    for (int k = 0; k < n_inputs; ++k) {
+        const std::string K = std::to_string(k);
+        if ((unit_inner >> k) & 1) {
+            s += "    const " + VT + " v" + K + " = __ldg(reinterpret_cast<const " + VT +
+                 " *>(static_cast<const " + T + " *>(a.in[" + K + "]) + o" + K + "));\n";
+        } else {
+            s += "    const " + T + " b" + K + " = __ldg(static_cast<const " + T + " *>(a.in[" + K +
+                 "]) + o" + K + ");\n";
+        }
+    }
+    // the steps, element by element
+    for (int e = 0; e < V; ++e) {
+        const std::string E = std::to_string(e);
+        auto operand = [&](int32_t v) -> std::string {
+            if (v >= 0) return ((unit_inner >> v) & 1) ? "v" + std::to_string(v) + "." + lanes[e]
+                                                       : "b" + std::to_string(v);
+            return "s" + std::to_string(-1 - v) + "_" + E;
+        };
+        for (int j = 0; j < n_steps; ++j) {
+            const int op = steps[j].op;
+            const bool binary = op <= CHELIS_FUSED_MIN_ELEM;
+            const std::string ex = step_expr(op, f32, operand(steps[j].a), binary ? operand(steps[j].b) : "");
+            if (ex.empty()) return "";
+            s += "    const " + T + " s" + std::to_string(j) + "_" + E + " = " + ex + ";\n";
+        }
+    }
+    const std::string last = "s" + std::to_string(n_steps - 1) + "_";
+    s += "    reinterpret_cast<" + VT + " *>(static_cast<" + T + " *>(a.out))[q] = make_" + VT + "(";
+    for (int e = 0; e < V; ++e) s += (e ? ", " : "") + last + std::to_string(e);
+    s += ");\n  }\n}\n";
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// NVRTC (opened at run time: the library links no NVRTC) and the cache
+// ---------------------------------------------------------------------------
+struct Nvrtc {
+    decltype(&nvrtcCreateProgram) create = nullptr;
+    decltype(&nvrtcCompileProgram) compile = nullptr;
+    decltype(&nvrtcGetProgramLogSize) log_size = nullptr;
+    decltype(&nvrtcGetProgramLog) log = nullptr;
+    decltype(&nvrtcGetCUBINSize) cubin_size = nullptr;
+    decltype(&nvrtcGetCUBIN) cubin = nullptr;
+    decltype(&nvrtcDestroyProgram) destroy = nullptr;
+    bool ok = false;
+};
+
+const Nvrtc &nvrtc() {
+    static Nvrtc n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnvrtc.so.12", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnvrtc.so", RTLD_NOW | RTLD_LOCAL);
+        if (!h) return;
+        n.create = reinterpret_cast<decltype(n.create)>(dlsym(h, "nvrtcCreateProgram"));
+        n.compile = reinterpret_cast<decltype(n.compile)>(dlsym(h, "nvrtcCompileProgram"));
+        n.log_size = reinterpret_cast<decltype(n.log_size)>(dlsym(h, "nvrtcGetProgramLogSize"));
+        n.log = reinterpret_cast<decltype(n.log)>(dlsym(h, "nvrtcGetProgramLog"));
+        n.cubin_size = reinterpret_cast<decltype(n.cubin_size)>(dlsym(h, "nvrtcGetCUBINSize"));
+        n.cubin = reinterpret_cast<decltype(n.cubin)>(dlsym(h, "nvrtcGetCUBIN"));
+        n.destroy = reinterpret_cast<decltype(n.destroy)>(dlsym(h, "nvrtcDestroyProgram"));
+        n.ok = n.create && n.compile && n.log_size && n.log && n.cubin_size && n.cubin && n.destroy;
+    });
+    return n;
+}
+
+// Driver entry points through the runtime (the library links no libcuda, so
+// it loads on hosts without a driver).
+struct Driver {
+    decltype(&cuModuleLoadData) load = nullptr;
+    decltype(&cuModuleGetFunction) get = nullptr;
+    decltype(&cuLaunchKernel) launch = nullptr;
+    bool ok = false;
+};
+
+const Driver &driver() {
+    static Driver d;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        auto entry = [](const char *name) -> void * {
+            void *ptr = nullptr;
+            cudaDriverEntryPointQueryResult q{};
+            if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+                q != cudaDriverEntryPointSuccess)
+                return nullptr;
+            return ptr;
+        };
+        d.load = reinterpret_cast<decltype(d.load)>(entry("cuModuleLoadData"));
+        d.get = reinterpret_cast<decltype(d.get)>(entry("cuModuleGetFunction"));
+        d.launch = reinterpret_cast<decltype(d.launch)>(entry("cuLaunchKernel"));
+        d.ok = d.load && d.get && d.launch;
+    });
+    return d;
+}
+
+std::mutex g_mu;
+std::unordered_map<std::string, CUfunction> g_cache;  // key: device id + kernel text
+std::atomic<int> g_enabled{1};
+std::atomic<uint64_t> g_jit_launches{0};
+std::atomic<uint64_t> g_compiles{0};
+
+// Compiled kernel for `src` on the current device (compiling it on first use).
+int get_kernel(const std::string &src, CUfunction *fn) {
+    int dev = 0;
+    CHELIS_TRY(current_device_checked(&dev));
+    const std::string key = std::to_string(dev) + "\n" + src;
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+        *fn = it->second;
+        return CHELIS_CUDA_OK;
+    }
+    const Nvrtc &n = nvrtc();
+    if (!n.ok) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "NVRTC is not available");
+    nvrtcProgram prog;
+    if (n.create(&prog, src.c_str(), "chelis_fused_jit.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "nvrtcCreateProgram failed");
+    const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "-ftz=false", "-prec-div=true",
+                          "-prec-sqrt=true", "-default-device"};
+    const nvrtcResult cr = n.compile(prog, 6, opts);
+    if (cr != NVRTC_SUCCESS) {
+        size_t ls = 0;
+        n.log_size(prog, &ls);
+        std::string log(ls, '\0');
+        if (ls) n.log(prog, &log[0]);
+        n.destroy(&prog);
+        return set_error(CHELIS_CUDA_ERR_CUDA, "fused JIT compile failed: %.400s", log.c_str());
+    }
+    size_t bytes = 0;
+    n.cubin_size(prog, &bytes);
+    std::string cubin(bytes, '\0');
+    n.cubin(prog, &cubin[0]);
+    n.destroy(&prog);
+    CHELIS_TRY(check_cuda(cudaFree(nullptr), "cudaFree(0) (context)"));
+    const Driver &drv = driver();
+    if (!drv.ok) return set_error(CHELIS_CUDA_ERR_CUDA, "driver module entry points unavailable");
+    CUmodule mod;
+    if (drv.load(&mod, cubin.data()) != CUDA_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "cuModuleLoadData(fused JIT) failed");
+    if (drv.get(fn, mod, "chelis_fused_jit") != CUDA_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "cuModuleGetFunction(fused JIT) failed");
+    g_cache.emplace(key, *fn);
+    g_compiles++;
+    return CHELIS_CUDA_OK;
+}
+
+// Runs the chain through a compiled kernel.  Returns -1 (nothing launched)
+// when the group is outside this form or JIT is switched off / unavailable,
+// so the caller takes the interpreter; otherwise a status.
+int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
+                    int mode, void *out, cudaStream_t s) {
+    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || p.total <= 0) return -1;
+    const int V = f32 ? 4 : 2;
+    const int64_t inner = p.shape[p.rank - 1];
+    if (inner % V != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0) return -1;
+    uint32_t unit = 0;
+    for (int k = 0; k < p.n_inputs; ++k) {
+        const int64_t st = inner > 1 ? p.stride[k][p.rank - 1] : 0;
+        if (st == 1) {
+            if (reinterpret_cast<uintptr_t>(p.in[k]) % 16 != 0) return -1;
+            for (int d = 0; d < p.rank - 1; ++d)
+                if (p.shape[d] > 1 && p.stride[k][d] % V != 0) return -1;
+            unit |= 1u << k;
+        } else if (st != 0) {
+            return -1;
+        }
+    }
+    const bool i32 = mode != fused::STRIDED64 && p.total < (int64_t(1) << 31);
+    const std::string src = kernel_source(f32, steps, n_steps, p.n_inputs, p.rank, unit, i32);
+    if (src.empty()) return -1;
+    CUfunction fn;
+    CHELIS_TRY(get_kernel(src, &fn));
+    Args a{};
+    for (int k = 0; k < p.n_inputs; ++k) {
+        a.in[k] = p.in[k];
+        for (int d = 0; d < p.rank; ++d) a.stride[k][d] = p.stride[k][d];
+    }
+    a.out = out;
+    for (int d = 0; d < p.rank; ++d) {
+        a.shape[d] = p.shape[d];
+        uint32_t mul = 0, shr = 0;
+        if (i32 && p.shape[d] > 1) {
+            int c = 0;
+            while ((uint64_t(1) << c) < static_cast<uint64_t>(p.shape[d])) ++c;
+            mul = static_cast<uint32_t>(((uint64_t(1) << (31 + c)) + p.shape[d] - 1) / p.shape[d]);
+            shr = static_cast<uint32_t>(c - 1);
+        }
+        a.div_mul[d] = mul;
+        a.div_shr[d] = shr;
+    }
+    a.nvec = p.total / V;
+    int64_t grid = (a.nvec + THREADS - 1) / THREADS;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    if (grid > cap) grid = cap;
+    void *params[] = {&a};
+    if (driver().launch(fn, static_cast<unsigned>(grid), 1, 1, THREADS, 1, 1, 0, s, params, nullptr) !=
+        CUDA_SUCCESS)
+        return set_error(CHELIS_CUDA_ERR_CUDA, "cuLaunchKernel(fused JIT) failed");
+    g_launches++;
+    g_jit_launches++;
+    return CHELIS_CUDA_OK;
+}
+
+}  // namespace fusedjit
+}  // namespace chelis
+
+extern "C" int chelis_cuda_set_fused_jit(int enable) {
+    if (enable != 0 && enable != 1)
+        return chelis::set_error(CHELIS_CUDA_ERR_DOMAIN, "fused JIT mode must be 0 or 1");
+    chelis::fusedjit::g_enabled.store(enable);
+    return CHELIS_CUDA_OK;
+}
+
+extern "C" int chelis_cuda_get_fused_jit(void) { return chelis::fusedjit::g_enabled.load(); }
+
+extern "C" int64_t chelis_cuda_fused_jit_launches(void) {
+    return static_cast<int64_t>(chelis::fusedjit::g_jit_launches.load());
+}

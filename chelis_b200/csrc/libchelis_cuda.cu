@@ -14,5 +14,6 @@
 #include "abi.cu"
 #include "chain_noalloc.cu"
 #include "fused.cu"
+#include "fused_jit.cu"
 #include "activations.cu"
 #include "dp.cu"

@@ -124,6 +124,9 @@ SIGNATURES = {
     "chelis_cuda_block_workspace_bytes": (c_i64, [ctypes.POINTER(BlockParams)]),
     "chelis_cuda_block_step": (c_int, [ctypes.POINTER(BlockParams), c_vp]),
     "chelis_cuda_fused_elementwise": (c_int, [c_i32, c_vp, c_i32, _PP, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_i64), c_i32, c_vp]),
+    "chelis_cuda_set_fused_jit": (c_int, [c_int]),
+    "chelis_cuda_get_fused_jit": (c_int, []),
+    "chelis_cuda_fused_jit_launches": (c_i64, []),
     "chelis_cuda_fused_reduce": (c_int, [c_i32, c_vp, c_i32, _PP, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_i64), c_i32, c_i32, c_i32, c_vp]),
     "chelis_cuda_relu": (c_int, [c_i32, c_vp, c_vp, c_i64]),
     "chelis_cuda_relu_adjoint": (c_int, [c_i32, c_vp, c_vp, c_vp, c_i64]),

@@ -78,6 +78,19 @@ def gemm_split(in_kernel: bool):
 
 
 @contextlib.contextmanager
+def fused_jit(enable: bool):
+    """FusedElem elementwise groups through per-chain compiled kernels (the
+    default) or the ahead-of-time interpreter; the same bits either way."""
+    lib = L.load()
+    old = lib.chelis_cuda_get_fused_jit()
+    L.call("chelis_cuda_set_fused_jit", int(enable))
+    try:
+        yield
+    finally:
+        L.call("chelis_cuda_set_fused_jit", old)
+
+
+@contextlib.contextmanager
 def rows_mode(mode: int):
     lib = L.load()
     old = lib.chelis_cuda_get_rows_mode()

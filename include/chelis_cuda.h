@@ -316,6 +316,19 @@ typedef enum { CHELIS_FUSED_REDUCE_SUM = 0, CHELIS_FUSED_REDUCE_MAX = 1 } chelis
 int chelis_cuda_fused_elementwise(int32_t dtype, const chelis_fused_step *steps, int32_t n_steps,
                                   const void *const *inputs, const int64_t *strides,
                                   int32_t n_inputs, const int64_t *shape, int32_t rank, void *out);
+/* Compiled chains for chelis_cuda_fused_elementwise: 1 (default) = a group
+ * whose innermost extent is a whole number of 16-byte vectors, and whose
+ * inputs are unit-stride (16-byte aligned) or broadcast along that axis, runs
+ * as one kernel generated for its chain.  That kernel is compiled at run time
+ * with NVRTC for sm_100a and cached per device and chain, the counterpart of
+ * the HIP lane's per-chain kernel strings compiled with hiprtc
+ * (kernels.rs:2391, chelis_hip_runtime.h:409-453).  Other groups, and every
+ * group when NVRTC is absent, use the ahead-of-time interpreter.  0 = always
+ * the interpreter.  Both give the same bits.  Process-wide.
+ * chelis_cuda_fused_jit_launches counts the compiled-chain launches so far. */
+int chelis_cuda_set_fused_jit(int enable);
+int chelis_cuda_get_fused_jit(void);
+int64_t chelis_cuda_fused_jit_launches(void);
 /* The group reduced along `axis` of `shape` (emit_fused_reduce,
  * emit.rs:9580-9860; reduce_fused kernels.rs:2175-2390): Sum by the
  * canonical pair tree, Max folding chelis_fmax_propnan_f32 from -inf.  `out`

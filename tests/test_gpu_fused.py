@@ -249,3 +249,55 @@ def test_inlined_product_is_the_c_lane_matmul(cuda, orc, mkn, dtype):
     ref = orc.gemm(a, b)
     width = "f32" if dtype == np.float32 else "f64"
     assert (got.view(UINT[width]) == ref.view(UINT[width])).all()
+
+
+def _special_mix(rng, shape, dtype):
+    x = (rng.standard_normal(shape) * 3).astype(dtype)
+    flat = x.reshape(-1)
+    specials = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-40, -1e-40, 0.5, -2.5, 1e30],
+                        dtype=dtype)
+    flat[: len(specials)] = specials
+    return x
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("op", [o for o in F.OPS if o != "trunc_div"])
+def test_compiled_chain_matches_interpreter(cuda, op, dtype):
+    """Every step op through the per-chain compiled kernel (NVRTC) and through
+    the interpreter gives the same bits, with a full-size operand, a row
+    vector broadcast along the rows and a column broadcast along the
+    innermost axis; and the compiled path is the one that ran."""
+    import torch
+    rng = np.random.default_rng(F.OP_CODE[op] + (0 if dtype == np.float32 else 100))
+    rows, cols = 37, 96
+    x = _special_mix(rng, (rows, cols), dtype)
+    row = _special_mix(rng, (1, cols), dtype)        # broadcast over rows, unit inner stride
+    col = (rng.standard_normal((rows, 1)) * 2).astype(dtype)  # broadcast along the inner axis
+    second = "x1" if op in F.BINARY else ""
+    chain = F.parse(f"{op} x0 {second}".strip() + "; mul v0 x2; " + (f"{op} v1 x1" if op in F.BINARY else f"{op} v1"))
+    ins = [t(x), t(row), t(col)]
+    before = L.load().chelis_cuda_fused_jit_launches()
+    with cuda.fused_jit(True):
+        jit = cuda.fused_elementwise(chain, ins).cpu().numpy()
+    after = L.load().chelis_cuda_fused_jit_launches()
+    with cuda.fused_jit(False):
+        ref = cuda.fused_elementwise(chain, ins).cpu().numpy()
+    torch.cuda.synchronize()
+    assert after == before + 1
+    w = UINT["f32" if dtype == np.float32 else "f64"]
+    assert (jit.view(w) == ref.view(w)).all(), op
+
+
+def test_compiled_chain_affine_large(cuda, orc):
+    """The affine chain x * gamma + beta at 4096 x 4096 through the compiled
+    kernel matches the oracle bit for bit."""
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((4096, 4096)).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, (1, 4096)).astype(np.float32)
+    b = (rng.standard_normal((1, 4096)) * 0.1).astype(np.float32)
+    chain = F.parse("mul x0 x1; add v0 x2")
+    before = L.load().chelis_cuda_fused_jit_launches()
+    got = cuda.fused_elementwise(chain, [t(x), t(g), t(b)]).cpu().numpy()
+    assert L.load().chelis_cuda_fused_jit_launches() == before + 1
+    ref = (x * g).astype(np.float32) + b
+    assert (got.view(np.uint32) == ref.astype(np.float32).view(np.uint32)).all()
