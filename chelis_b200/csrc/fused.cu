@@ -997,6 +997,8 @@ namespace chelis {
 namespace fusedjit {
 int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
                     int mode, void *out, cudaStream_t s);
+int try_reduce(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
+               int mode, int axis, int kind, int64_t outputs, void *out, cudaStream_t s);
 }  // namespace fusedjit
 }  // namespace chelis
 
@@ -1052,6 +1054,9 @@ extern "C" int chelis_cuda_fused_reduce(int32_t dtype, const chelis_fused_step *
     if (p.shape[axis] == 0)  // an empty Sum is zero (the C lane's zero fill)
         return check_cuda(cudaMemsetAsync(out, 0, static_cast<size_t>(outputs) * elem, s),
                           "cudaMemsetAsync(fused_reduce)");
+    const int jit = fusedjit::try_reduce(dtype == CHELIS_DTYPE_F32, steps, n_steps, p, mode, axis, kind,
+                                         outputs, out, s);
+    if (jit >= 0) return jit;
     return dtype == CHELIS_DTYPE_F32
                ? fused_reduce_t<float>(p, mode, kind, axis, outputs, static_cast<float *>(out), s)
                : fused_reduce_t<double>(p, mode, kind, axis, outputs, static_cast<double *>(out), s);

@@ -52,6 +52,7 @@ struct Args {
     unsigned div_mul[fused::MAX_RANK];
     unsigned div_shr[fused::MAX_RANK];
     long long nvec;
+    long long len;
 };
 
 const char *kPrelude = R"SRC(
@@ -63,6 +64,7 @@ struct Args {
     unsigned div_mul[6];
     unsigned div_shr[6];
     long long nvec;
+    long long len;
 };
 __device__ __forceinline__ float cn(float x) { return isnan(x) ? __int_as_float(0x7fc00000) : x; }
 __device__ __forceinline__ double cn(double x) { return isnan(x) ? __longlong_as_double(0x7ff8000000000000ll) : x; }
@@ -111,22 +113,20 @@ std::string step_expr(int op, bool f32, const std::string &a, const std::string 
     }
 }
 
-// Kernel text for the chain; empty when the chain uses an op this form does
-// not spell (none today beyond the integer-only trunc_div, which
-// build_program rejects).
-std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps, int n_inputs,
-                          int rank, uint32_t unit_inner, bool i32) {
+// Code that evaluates the chain on the V consecutive elements starting at
+// flat index `first` (an expression of type long long): their offsets in
+// every input, the loads (unit-stride inputs as one vector, broadcast ones as
+// one element) and the steps, leaving element e's result in s<last>_<e>.
+// Empty when a step has no spelling here.
+std::string vector_body(bool f32, const chelis_fused_step *steps, int n_steps, int n_inputs,
+                        int rank, uint32_t unit_inner, bool i32, const std::string &first) {
     const int V = f32 ? 4 : 2;
     const std::string T = f32 ? "float" : "double";
     const std::string VT = f32 ? "float4" : "double2";
     const char *lanes[4] = {"x", "y", "z", "w"};
-    std::string s = kPrelude;
-    s += "extern \"C\" __global__ void __launch_bounds__(256) chelis_fused_jit(Args a) {\n";
-    s += "  const long long step = (long long)gridDim.x * 256;\n";
-    s += "  for (long long q = (long long)blockIdx.x * 256 + threadIdx.x; q < a.nvec; q += step) {\n";
-    // decode the vector's first element into per-input offsets
+    std::string s;
     if (i32) {
-        s += "    unsigned rem = (unsigned)(q * " + std::to_string(V) + ");\n";
+        s += "    unsigned rem = (unsigned)(" + first + ");\n";
         for (int k = 0; k < n_inputs; ++k) s += "    int o" + std::to_string(k) + " = 0;\n";
         for (int d = rank - 1; d >= 0; --d) {
             const std::string D = std::to_string(d);
@@ -142,7 +142,7 @@ std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps,
             s += "    }\n";
         }
     } else {
-        s += "    long long rem = q * " + std::to_string(V) + ";\n";
+        s += "    long long rem = " + first + ";\n";
         for (int k = 0; k < n_inputs; ++k) s += "    long long o" + std::to_string(k) + " = 0;\n";
         for (int d = rank - 1; d >= 0; --d) {
             const std::string D = std::to_string(d);
@@ -154,7 +154,6 @@ std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps,
             s += "    }\n";
         }
     }
-    // loads: unit-stride inputs as one vector, broadcast ones as one element
     for (int k = 0; k < n_inputs; ++k) {
         const std::string K = std::to_string(k);
         if ((unit_inner >> k) & 1) {
@@ -165,7 +164,6 @@ std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps,
                  "]) + o" + K + ");\n";
         }
     }
-    // the steps, element by element
     for (int e = 0; e < V; ++e) {
         const std::string E = std::to_string(e);
         auto operand = [&](int32_t v) -> std::string {
@@ -181,10 +179,97 @@ std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps,
             s += "    const " + T + " s" + std::to_string(j) + "_" + E + " = " + ex + ";\n";
         }
     }
+    return s;
+}
+
+// Elementwise kernel: thread q writes output vector q.
+std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps, int n_inputs,
+                          int rank, uint32_t unit_inner, bool i32) {
+    const int V = f32 ? 4 : 2;
+    const std::string T = f32 ? "float" : "double";
+    const std::string VT = f32 ? "float4" : "double2";
+    const std::string body = vector_body(f32, steps, n_steps, n_inputs, rank, unit_inner, i32,
+                                         "q * " + std::to_string(V));
+    if (body.empty()) return "";
+    std::string s = kPrelude;
+    s += "extern \"C\" __global__ void __launch_bounds__(256) chelis_fused_jit(Args a) {\n";
+    s += "  const long long step = (long long)gridDim.x * 256;\n";
+    s += "  for (long long q = (long long)blockIdx.x * 256 + threadIdx.x; q < a.nvec; q += step) {\n";
+    s += body;
     const std::string last = "s" + std::to_string(n_steps - 1) + "_";
     s += "    reinterpret_cast<" + VT + " *>(static_cast<" + T + " *>(a.out))[q] = make_" + VT + "(";
     for (int e = 0; e < V; ++e) s += (e ? ", " : "") + last + std::to_string(e);
     s += ");\n  }\n}\n";
+    return s;
+}
+
+// Reduction over the last axis (length a.len, a multiple of 32 V): one warp
+// per output w (a.nvec outputs), the leaves of row w at flat indices
+// [w * len, (w + 1) * len).  A pass covers 32 V consecutive leaves, lane l
+// the aligned group [l V, l V + V): its pair tree, then the warp butterfly
+// (adjacent lanes first), give the pass's aligned subtree, pushed onto the
+// carry tree (emit.rs emit_carry_tree_push :8129); the carry tree's total is
+// the canonical adjacent-pair tree over the row, canonicalised once.  Max
+// keeps per lane the maximum and the last index holding it (NaN anywhere
+// gives the canonical NaN); lanes merge by value, later index on ties.  The
+// same trees, in the same order, as fused.cu reduce_last_kernel.
+std::string reduce_source(bool f32, const chelis_fused_step *steps, int n_steps, int n_inputs,
+                          int rank, uint32_t unit_inner, bool i32, bool sum) {
+    const int V = f32 ? 4 : 2;
+    const std::string T = f32 ? "float" : "double";
+    const std::string add = f32 ? "__fadd_rn" : "__dadd_rn";
+    const std::string body = vector_body(f32, steps, n_steps, n_inputs, rank, unit_inner, i32,
+                                         "w * a.len + c0 + lane * " + std::to_string(V));
+    if (body.empty()) return "";
+    const std::string last = "s" + std::to_string(n_steps - 1) + "_";
+    std::string s = kPrelude;
+    s += "extern \"C\" __global__ void __launch_bounds__(256) chelis_fused_jit(Args a) {\n";
+    s += "  const int lane = threadIdx.x & 31;\n";
+    s += "  const long long warps = (long long)gridDim.x * 8;\n";
+    s += "  for (long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); w < a.nvec; w += warps) {\n";
+    if (sum) {
+        s += "  " + T + " level[48]; long long count = 0;\n";
+    } else {
+        s += "  " + T + " best = " + (f32 ? std::string("__int_as_float(0xff800000)")
+                                         : std::string("__longlong_as_double(0xfff0000000000000ll)")) +
+             "; long long at = -1; bool nan = false;\n";
+    }
+    s += "  for (long long c0 = 0; c0 < a.len; c0 += " + std::to_string(32 * V) + ") {\n";
+    s += body;
+    if (sum) {
+        if (V == 4)
+            s += "    " + T + " t = " + add + "(" + add + "(" + last + "0, " + last + "1), " + add + "(" +
+                 last + "2, " + last + "3));\n";
+        else
+            s += "    " + T + " t = " + add + "(" + last + "0, " + last + "1);\n";
+        s += "    for (int off = 1; off < 32; off <<= 1) t = " + add + "(t, __shfl_xor_sync(0xffffffffu, t, off));\n";
+        s += "    { int depth = 0; for (long long pending = count++; pending & 1; pending >>= 1, ++depth) t = " +
+             add + "(level[depth], t); level[depth] = t; }\n";
+    } else {
+        for (int e = 0; e < V; ++e) {
+            const std::string v = last + std::to_string(e);
+            s += "    if (isnan(" + v + ")) nan = true; else if (!(best > " + v + ")) { best = " + v +
+                 "; at = c0 + lane * " + std::to_string(V) + " + " + std::to_string(e) + "; }\n";
+        }
+    }
+    s += "  }\n";
+    if (sum) {
+        s += "  " + T + " total = 0; bool found = false; int depth = 0;\n";
+        s += "  for (long long remaining = count; remaining; remaining >>= 1, ++depth)\n";
+        s += "    if (remaining & 1) { total = found ? " + add + "(level[depth], total) : level[depth]; found = true; }\n";
+        s += "  if (lane == 0) static_cast<" + T + " *>(a.out)[w] = cn(found ? total : (" + T + ")0);\n";
+    } else {
+        s += "  nan = __any_sync(0xffffffffu, nan);\n";
+        s += "  for (int off = 16; off > 0; off >>= 1) {\n";
+        s += "    const " + T + " ob = __shfl_xor_sync(0xffffffffu, best, off);\n";
+        s += "    const long long oa = __shfl_xor_sync(0xffffffffu, at, off);\n";
+        s += "    if (ob > best || (ob == best && oa > at)) { best = ob; at = oa; }\n";
+        s += "  }\n";
+        s += "  if (lane == 0) static_cast<" + T + " *>(a.out)[w] = nan ? " +
+             (f32 ? std::string("__int_as_float(0x7fc00000)") : std::string("__longlong_as_double(0x7ff8000000000000ll)")) +
+             " : best;\n";
+    }
+    s += "  }\n}\n";
     return s;
 }
 
@@ -301,33 +386,28 @@ int get_kernel(const std::string &src, CUfunction *fn) {
     return CHELIS_CUDA_OK;
 }
 
-// Runs the chain through a compiled kernel.  Returns -1 (nothing launched)
-// when the group is outside this form or JIT is switched off / unavailable,
-// so the caller takes the interpreter; otherwise a status.
-int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
-                    int mode, void *out, cudaStream_t s) {
-    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || p.total <= 0) return -1;
-    const int V = f32 ? 4 : 2;
+// Inputs that run along the innermost axis with unit stride (bit k set), or
+// false when some input is neither unit-stride nor broadcast there, or a
+// unit-stride input cannot be read as aligned V-element vectors.
+bool unit_inputs(const fused::Program &p, int V, uint32_t *unit) {
     const int64_t inner = p.shape[p.rank - 1];
-    if (inner % V != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0) return -1;
-    uint32_t unit = 0;
+    *unit = 0;
     for (int k = 0; k < p.n_inputs; ++k) {
         const int64_t st = inner > 1 ? p.stride[k][p.rank - 1] : 0;
         if (st == 1) {
-            if (reinterpret_cast<uintptr_t>(p.in[k]) % 16 != 0) return -1;
+            if (reinterpret_cast<uintptr_t>(p.in[k]) % 16 != 0) return false;
             for (int d = 0; d < p.rank - 1; ++d)
-                if (p.shape[d] > 1 && p.stride[k][d] % V != 0) return -1;
-            unit |= 1u << k;
+                if (p.shape[d] > 1 && p.stride[k][d] % V != 0) return false;
+            *unit |= 1u << k;
         } else if (st != 0) {
-            return -1;
+            return false;
         }
     }
-    const bool i32 = mode != fused::STRIDED64 && p.total < (int64_t(1) << 31);
-    const std::string src = kernel_source(f32, steps, n_steps, p.n_inputs, p.rank, unit, i32);
-    if (src.empty()) return -1;
-    CUfunction fn;
-    CHELIS_TRY(get_kernel(src, &fn));
-    Args a{};
+    return true;
+}
+
+void fill_args(Args &a, const fused::Program &p, void *out, bool i32) {
+    a = Args{};
     for (int k = 0; k < p.n_inputs; ++k) {
         a.in[k] = p.in[k];
         for (int d = 0; d < p.rank; ++d) a.stride[k][d] = p.stride[k][d];
@@ -336,7 +416,7 @@ int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const
     for (int d = 0; d < p.rank; ++d) {
         a.shape[d] = p.shape[d];
         uint32_t mul = 0, shr = 0;
-        if (i32 && p.shape[d] > 1) {
+        if (i32 && p.shape[d] > 1) {  // fused.cu fast_divisor
             int c = 0;
             while ((uint64_t(1) << c) < static_cast<uint64_t>(p.shape[d])) ++c;
             mul = static_cast<uint32_t>(((uint64_t(1) << (31 + c)) + p.shape[d] - 1) / p.shape[d]);
@@ -345,17 +425,63 @@ int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const
         a.div_mul[d] = mul;
         a.div_shr[d] = shr;
     }
-    a.nvec = p.total / V;
-    int64_t grid = (a.nvec + THREADS - 1) / THREADS;
+}
+
+int launch(CUfunction fn, Args &a, int64_t blocks, cudaStream_t s) {
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
-    if (grid > cap) grid = cap;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
     void *params[] = {&a};
-    if (driver().launch(fn, static_cast<unsigned>(grid), 1, 1, THREADS, 1, 1, 0, s, params, nullptr) !=
+    if (driver().launch(fn, static_cast<unsigned>(blocks), 1, 1, THREADS, 1, 1, 0, s, params, nullptr) !=
         CUDA_SUCCESS)
         return set_error(CHELIS_CUDA_ERR_CUDA, "cuLaunchKernel(fused JIT) failed");
     g_launches++;
     g_jit_launches++;
     return CHELIS_CUDA_OK;
+}
+
+// Runs the chain through a compiled kernel.  Returns -1 (nothing launched)
+// when the group is outside this form or JIT is switched off / unavailable,
+// so the caller takes the interpreter; otherwise a status.
+int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
+                    int mode, void *out, cudaStream_t s) {
+    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || p.total <= 0) return -1;
+    const int V = f32 ? 4 : 2;
+    uint32_t unit = 0;
+    if (p.shape[p.rank - 1] % V != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0 ||
+        !unit_inputs(p, V, &unit))
+        return -1;
+    const bool i32 = mode != fused::STRIDED64 && p.total < (int64_t(1) << 31);
+    const std::string src = kernel_source(f32, steps, n_steps, p.n_inputs, p.rank, unit, i32);
+    if (src.empty()) return -1;
+    CUfunction fn;
+    CHELIS_TRY(get_kernel(src, &fn));
+    Args a;
+    fill_args(a, p, out, i32);
+    a.nvec = p.total / V;
+    return launch(fn, a, (a.nvec + THREADS - 1) / THREADS, s);
+}
+
+// The chain reduced (Sum or Max) along the last axis, when that axis is a
+// whole number of 32-lane passes of V-element vectors; -1 as above.
+int try_reduce(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
+               int mode, int axis, int kind, int64_t outputs, void *out, cudaStream_t s) {
+    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || axis != p.rank - 1 || outputs <= 0) return -1;
+    const int V = f32 ? 4 : 2;
+    const int64_t len = p.shape[axis];
+    uint32_t unit = 0;
+    if (len <= 0 || len % (32 * V) != 0 || !unit_inputs(p, V, &unit)) return -1;
+    const bool i32 = mode != fused::STRIDED64 && p.total < (int64_t(1) << 31);
+    const std::string src = reduce_source(f32, steps, n_steps, p.n_inputs, p.rank, unit, i32,
+                                          kind == CHELIS_FUSED_REDUCE_SUM);
+    if (src.empty()) return -1;
+    CUfunction fn;
+    CHELIS_TRY(get_kernel(src, &fn));
+    Args a;
+    fill_args(a, p, out, i32);
+    a.nvec = outputs;
+    a.len = len;
+    return launch(fn, a, (outputs + THREADS / 32 - 1) / (THREADS / 32), s);
 }
 
 }  // namespace fusedjit
