@@ -463,10 +463,14 @@ int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const
 }
 
 // The chain reduced (Sum or Max) along the last axis, when that axis is a
-// whole number of 32-lane passes of V-element vectors; -1 as above.
+// whole number of 32-lane passes of V-element vectors and there are enough
+// outputs to give every SM eight warps (one warp per output; fewer, longer
+// rows go to the interpreter, which splits a row into segments); -1 as above.
 int try_reduce(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
                int mode, int axis, int kind, int64_t outputs, void *out, cudaStream_t s) {
-    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || axis != p.rank - 1 || outputs <= 0) return -1;
+    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || axis != p.rank - 1 ||
+        outputs < static_cast<int64_t>(sm_count()) * 8)
+        return -1;
     const int V = f32 ? 4 : 2;
     const int64_t len = p.shape[axis];
     uint32_t unit = 0;

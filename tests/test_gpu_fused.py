@@ -314,7 +314,9 @@ def test_compiled_last_axis_reduction_matches_interpreter(cuda, dtype, kind, cha
     import torch
     rng = np.random.default_rng(len(chain_text) * 7 + (kind == "max"))
     v = 4 if dtype == np.float32 else 2
-    for rows, passes in ((3, 1), (17, 5), (40, 32)):
+    # one warp per output: the compiled form takes row counts that fill the
+    # GPU (>= 8 warps per SM)
+    for rows, passes in ((1250, 1), (1250, 5), (1250, 32)):
         cols = 32 * v * passes
         x = _special_mix(rng, (rows, cols), dtype)
         x[1, :] = 0.0
@@ -336,3 +338,13 @@ def test_compiled_last_axis_reduction_matches_interpreter(cuda, dtype, kind, cha
         assert after == before + 1
         w = UINT["f32" if dtype == np.float32 else "f64"]
         assert (jit.view(w) == ref.view(w)).all(), (rows, passes)
+
+
+def test_few_long_rows_stay_on_the_segmented_interpreter(cuda):
+    """A whole-tensor sum (one output) is not given to the one-warp-per-output
+    compiled form: the interpreter splits the row into segments."""
+    x = np.random.default_rng(3).standard_normal(1 << 20).astype(np.float32)
+    before = L.load().chelis_cuda_fused_jit_launches()
+    got = cuda.fused_reduce(F.parse("mul x0 x0"), [t(x)], axis=0, kind="sum").cpu().numpy()
+    assert L.load().chelis_cuda_fused_jit_launches() == before
+    assert abs(float(got) - float((x.astype(np.float64) ** 2).sum())) <= 1e-5 * float((x.astype(np.float64) ** 2).sum())
