@@ -519,15 +519,19 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
                        __fadd_rn(a.w, b.w));
 }
+// RB = 32 takes two 16-row subtrees: twice the blocks for the same matrix,
+// so the last wave of the grid leaves fewer SMs idle.
+template <int RB>
 __global__ void col_block4_kernel(const float *__restrict__ x, int64_t cols, float *__restrict__ out) {
+    constexpr int Q = RB / 16;
     const int64_t c4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // float4 column
     if (c4 * 4 >= cols) return;
     const int64_t blk = blockIdx.y;
-    const float4 *src = reinterpret_cast<const float4 *>(x + blk * COL_RB * cols) + c4;
+    const float4 *src = reinterpret_cast<const float4 *>(x + blk * RB * cols) + c4;
     const int64_t stride = cols / 4;
-    float4 sub[4];
+    float4 sub[Q];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < Q; ++q) {
         float4 v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __ldcs(src + (q * 16 + i) * stride);
@@ -537,7 +541,10 @@ __global__ void col_block4_kernel(const float *__restrict__ x, int64_t cols, flo
             for (int i = 0; i + width < 16; i += 2 * width) v[i] = add4(v[i], v[i + width]);
         sub[q] = v[0];
     }
-    reinterpret_cast<float4 *>(out + blk * cols)[c4] = add4(add4(sub[0], sub[1]), add4(sub[2], sub[3]));
+    if constexpr (Q == 4)
+        reinterpret_cast<float4 *>(out + blk * cols)[c4] = add4(add4(sub[0], sub[1]), add4(sub[2], sub[3]));
+    else
+        reinterpret_cast<float4 *>(out + blk * cols)[c4] = add4(sub[0], sub[1]);
 }
 
 // ---------------------------------------------------------------------------
@@ -686,9 +693,9 @@ using namespace chelis::rows;
 
 namespace chelis {
 
-// Canonical column sums of a [rows, cols] matrix into out[cols] (two-level
-// aligned-block scheme; one scratch buffer of ceil(rows/64) * cols floats
-// when rows > 64).
+// Canonical column sums of a [rows, cols] matrix into out[cols] (aligned
+// row blocks reduced level by level; one scratch buffer of ceil(rows/rb) *
+// cols floats per level when rows > 64).
 int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStream_t s) {
     if (cols == 0) return CHELIS_CUDA_OK;
     if (rows == 0)
@@ -700,28 +707,30 @@ int col_sum_into(const float *x, int64_t rows, int64_t cols, float *out, cudaStr
         CHELIS_LAUNCH_CHECK("col_block_kernel");
         return CHELIS_CUDA_OK;
     }
-    const int64_t nb = (rows + COL_RB - 1) / COL_RB;
+    // aligned row blocks of rb rows (any aligned power-of-two block is a
+    // subtree of the canonical tree): 32 on the float4 path, 64 otherwise
+    const bool v4 = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const int64_t rb = v4 ? 32 : COL_RB;
+    const int64_t nb = (rows + rb - 1) / rb;
     void *tmp = nullptr;
     CHELIS_TRY(scratch_alloc(&tmp, static_cast<size_t>(nb * cols) * sizeof(float), s));
     float *blk = static_cast<float *>(tmp);
     int st;
-    const int64_t nfull = rows / COL_RB;
-    if (cols % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && nfull > 0 && nfull <= 65535) {
+    const int64_t nfull = rows / rb;
+    if (v4 && nfull > 0 && nfull <= 65535) {
         // full blocks with float4 columns, the ragged last block (if any) below
         const unsigned cb4 = static_cast<unsigned>((cols / 4 + 127) / 128);
-        col_block4_kernel<<<dim3(cb4, static_cast<unsigned>(nfull)), 128, 0, s>>>(x, cols, blk);
+        col_block4_kernel<32><<<dim3(cb4, static_cast<unsigned>(nfull)), 128, 0, s>>>(x, cols, blk);
         g_launches++;
         st = check_cuda(cudaGetLastError(), "col_block4_kernel");
         if (st == CHELIS_CUDA_OK && nb > nfull) {
-            col_block_kernel<<<dim3(cb, 1), 128, 0, s>>>(x + nfull * COL_RB * cols,
-                                                         rows - nfull * COL_RB, cols, COL_RB,
-                                                         blk + nfull * cols);
+            col_block_kernel<<<dim3(cb, 1), 128, 0, s>>>(x + nfull * rb * cols, rows - nfull * rb,
+                                                         cols, rb, blk + nfull * cols);
             g_launches++;
             st = check_cuda(cudaGetLastError(), "col_block_kernel");
         }
     } else {
-        col_block_kernel<<<dim3(cb, static_cast<unsigned>(nb)), 128, 0, s>>>(x, rows, cols, COL_RB,
-                                                                            blk);
+        col_block_kernel<<<dim3(cb, static_cast<unsigned>(nb)), 128, 0, s>>>(x, rows, cols, rb, blk);
         g_launches++;
         st = check_cuda(cudaGetLastError(), "col_block_kernel");
     }

@@ -52,7 +52,8 @@ def test_row_sum_bit_exact(cuda, orc, rows, cols):
     assert bits_equal(cuda.row_sum(t(x)).cpu().numpy(), orc.row_sum(x))
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 3), (64, 5), (65, 130), (4097, 33), (16384, 64)])
+@pytest.mark.parametrize("rows,cols", [(1, 3), (64, 5), (65, 130), (4097, 33), (16384, 64),
+                                       (1000, 4096), (4129, 128), (96, 8)])
 def test_col_sum_bit_exact(cuda, orc, rows, cols):
     x = np.random.default_rng(rows + cols).standard_normal((rows, cols)).astype(np.float32)
     assert bits_equal(cuda.col_sum(t(x)).cpu().numpy(), orc.col_sum(x))
