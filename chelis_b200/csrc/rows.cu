@@ -179,6 +179,27 @@ __device__ __forceinline__ float canon(float x) {
 // ---------------------------------------------------------------------------
 // standalone row ops
 // ---------------------------------------------------------------------------
+// FAST-mode block sum: each thread's partial, one warp butterfly, then the
+// warp partials (every thread reads them back; the caller alternates two
+// scratch areas, so one barrier suffices).  Butterfly order, not the
+// canonical tree: within f32 rel 1e-5 of it.
+template <int T>
+__device__ __forceinline__ float block_sum_fast(float v, float *red) {
+    constexpr int W = T / 32;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float w[W];
+#pragma unroll
+    for (int i = 0; i < W; ++i) w[i] = red[i];
+#pragma unroll
+    for (int width = 1; width < W; width <<= 1)
+#pragma unroll
+        for (int i = 0; i + width < W; i += 2 * width) w[i] += w[i + width];
+    return w[0];
+}
+
 template <int T, int NC, bool EXACT>
 __global__ void __launch_bounds__(T, NC <= 4 ? 3 : 1)
     layer_norm_kernel(const float *__restrict__ xin, const float *__restrict__ gamma,
@@ -215,16 +236,37 @@ __global__ void __launch_bounds__(T, NC <= 4 ? 3 : 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = nxt[c][i];
         if (r + gridDim.x < rows) load_row<NC, T>(nxt, xin + (r + gridDim.x) * n, n, vec);
-        const float s1 = block_tree<T, NC, false>(v, n, red[0]);
-        const float mean = EXACT ? __fdiv_rn(s1, hf) : __fmul_rn(s1, rh);
+        float s1, s2, mean;
+        if constexpr (EXACT) {
+            s1 = block_tree<T, NC, false>(v, n, red[0]);
+            mean = __fdiv_rn(s1, hf);
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
+            for (int c = 0; c < NC; ++c)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                v[c][i] = __fsub_rn(v[c][i], mean);
-                c2[c][i] = __fmul_rn(v[c][i], v[c][i]);
-            }
-        const float s2 = block_tree<T, NC, false>(c2, n, red[1]);
+                for (int i = 0; i < 4; ++i) {
+                    v[c][i] = __fsub_rn(v[c][i], mean);
+                    c2[c][i] = __fmul_rn(v[c][i], v[c][i]);
+                }
+            s2 = block_tree<T, NC, false>(c2, n, red[1]);
+        } else {
+            // zeros past the row end (load_row) add nothing to the sum; the
+            // squared deviations are masked to the row
+            float t = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) t += (v[c][0] + v[c][1]) + (v[c][2] + v[c][3]);
+            s1 = block_sum_fast<T>(t, red[0]);
+            mean = __fmul_rn(s1, rh);
+            float q = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    v[c][i] = __fsub_rn(v[c][i], mean);
+                    const bool valid = c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n;
+                    q = valid ? fmaf(v[c][i], v[c][i], q) : q;
+                }
+            s2 = block_sum_fast<T>(q, red[1]);
+        }
         const float var = EXACT ? __fdiv_rn(s2, hf) : __fmul_rn(s2, rh);
         const float d = __fsqrt_rn(__fadd_rn(var, eps));
         const float rd = __fdiv_rn(1.0f, d);
