@@ -311,7 +311,18 @@ __global__ void __launch_bounds__(T)
         for (int c = 0; c < NC; ++c)
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[c][i] = expf(__fsub_rn(v[c][i], mx));
-        const float z = block_tree<T, NC, false>(v, n, red[1]);
+        float z;
+        if constexpr (EXACT) {
+            z = block_tree<T, NC, false>(v, n, red[1]);
+        } else {
+            float t = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (c * 4 * T + 4 * static_cast<int>(threadIdx.x) + i < n) t += v[c][i];
+            z = block_sum_fast<T>(t, red[1]);
+        }
         const float rz = __fdiv_rn(1.0f, z);
 #pragma unroll
         for (int c = 0; c < NC; ++c)
