@@ -468,13 +468,50 @@ int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const
 // rows go to the interpreter, which splits a row into segments); -1 as above.
 int try_reduce(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
                int mode, int axis, int kind, int64_t outputs, void *out, cudaStream_t s) {
-    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || axis != p.rank - 1 ||
-        outputs < static_cast<int64_t>(sm_count()) * 8)
-        return -1;
+    if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || axis != p.rank - 1 || outputs < 1) return -1;
     const int V = f32 ? 4 : 2;
     const int64_t len = p.shape[axis];
+    const int64_t want = static_cast<int64_t>(sm_count()) * 8;
     uint32_t unit = 0;
     if (len <= 0 || len % (32 * V) != 0 || !unit_inputs(p, V, &unit)) return -1;
+    if (outputs < want) {
+        // Few, long rows: cut each row into aligned segments of seg leaves
+        // (a power-of-two share of the row, a whole number of passes: every
+        // segment is a subtree of the canonical tree), reduce the segments
+        // one warp each into partials, then the partials of each row, in
+        // order, by the same group kind through an identity step (max_elem
+        // of a value with itself keeps its bits).
+        // (segments enough for 64 warps per SM, as many rows do; far fewer
+        // and longer ones leave the warps latency-bound: measured)
+        int64_t seg = len;
+        while (outputs * (len / seg) < 8 * want && seg % 2 == 0 && (seg / 2) % (32 * V) == 0) seg /= 2;
+        if (outputs * (len / seg) < want) return -1;
+        const int64_t nseg = len / seg;
+        const bool i32 = mode != fused::STRIDED64 && p.total < (int64_t(1) << 31);
+        const std::string src = reduce_source(f32, steps, n_steps, p.n_inputs, p.rank, unit, i32,
+                                              kind == CHELIS_FUSED_REDUCE_SUM);
+        if (src.empty()) return -1;
+        CUfunction fn;
+        CHELIS_TRY(get_kernel(src, &fn));
+        const size_t elem = f32 ? 4 : 8;
+        void *part = nullptr;
+        CHELIS_TRY(scratch_alloc(&part, static_cast<size_t>(outputs * nseg) * elem, s));
+        Args a;
+        fill_args(a, p, part, i32);
+        a.nvec = outputs * nseg;  // segment w covers flat leaves [w * seg, (w + 1) * seg)
+        a.len = seg;
+        int st = launch(fn, a, (a.nvec + THREADS / 32 - 1) / (THREADS / 32), s);
+        if (st == CHELIS_CUDA_OK) {
+            const chelis_fused_step id{CHELIS_FUSED_MAX_ELEM, 0, 0};
+            const void *ins[1] = {part};
+            const int64_t strides[2] = {nseg, 1};
+            const int64_t shape[2] = {outputs, nseg};
+            st = chelis_cuda_fused_reduce(f32 ? CHELIS_DTYPE_F32 : CHELIS_DTYPE_F64, &id, 1, ins, strides,
+                                          1, shape, 2, 1, kind, out);
+        }
+        scratch_free(part, s);
+        return st;
+    }
     const bool i32 = mode != fused::STRIDED64 && p.total < (int64_t(1) << 31);
     const std::string src = reduce_source(f32, steps, n_steps, p.n_inputs, p.rank, unit, i32,
                                           kind == CHELIS_FUSED_REDUCE_SUM);

@@ -340,11 +340,30 @@ def test_compiled_last_axis_reduction_matches_interpreter(cuda, dtype, kind, cha
         assert (jit.view(w) == ref.view(w)).all(), (rows, passes)
 
 
-def test_few_long_rows_stay_on_the_segmented_interpreter(cuda):
-    """A whole-tensor sum (one output) is not given to the one-warp-per-output
-    compiled form: the interpreter splits the row into segments."""
-    x = np.random.default_rng(3).standard_normal(1 << 20).astype(np.float32)
-    before = L.load().chelis_cuda_fused_jit_launches()
-    got = cuda.fused_reduce(F.parse("mul x0 x0"), [t(x)], axis=0, kind="sum").cpu().numpy()
-    assert L.load().chelis_cuda_fused_jit_launches() == before
-    assert abs(float(got) - float((x.astype(np.float64) ** 2).sum())) <= 1e-5 * float((x.astype(np.float64) ** 2).sum())
+@pytest.mark.parametrize("kind", ["sum", "max"])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_few_long_rows_reduce_in_segments(cuda, kind, dtype):
+    """A whole-tensor reduction (one output) runs as aligned segments, one
+    warp each through the compiled kernel, then the segment partials in
+    order; the bits equal the interpreter's single canonical tree (Sum) and
+    first-NaN / later-zero rule (Max)."""
+    import torch
+    rng = np.random.default_rng(3)
+    for n, finite in ((1 << 20, True), (3 << 18, True), (1 << 20, False)):
+        x = _special_mix(rng, (n,), dtype)
+        if finite:
+            x = np.nan_to_num(x, nan=0.5, posinf=2.0, neginf=-2.0)
+        x[n // 3] = 0.0
+        x[n // 2] = -0.0
+        for chain_text in ("mul x0 x0", "abs x0; neg v0"):
+            chain = F.parse(chain_text)
+            before = L.load().chelis_cuda_fused_jit_launches()
+            with cuda.fused_jit(True):
+                jit = cuda.fused_reduce(chain, [t(x)], axis=0, kind=kind).cpu().numpy()
+            after = L.load().chelis_cuda_fused_jit_launches()
+            with cuda.fused_jit(False):
+                ref = cuda.fused_reduce(chain, [t(x)], axis=0, kind=kind).cpu().numpy()
+            torch.cuda.synchronize()
+            assert after == before + 1
+            w = UINT["f32" if dtype == np.float32 else "f64"]
+            assert (jit.view(w) == ref.view(w)).all(), (n, chain_text)
