@@ -1,6 +1,8 @@
 """Build libchelis_cuda.so in-tree for sm_100a (nvcc cross-compiles; no GPU
 needed).  The shared library is what travels to the GPU box and what
-chelis_b200 loads; nothing is JIT-compiled at run time."""
+chelis_b200 loads.  One part compiles at run time: the per-chain FusedElem
+kernels of csrc/fused_jit.cu, generated and compiled with NVRTC for sm_100a
+at first use and cached per device; every other kernel is in this library."""
 from __future__ import annotations
 
 import os

@@ -268,3 +268,30 @@ int chelis_matmul_device(const chelis_device_tensor_owner *const *inputs, chelis
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// bounded-wait self-test: a consumer waits on an mbarrier for a producer
+// thread's arrival through the same mbar_wait_bounded every pipeline uses
+// ---------------------------------------------------------------------------
+namespace chelis {
+namespace selftest {
+__global__ void bounded_wait_probe_kernel(int skip_arrival) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 32 && !skip_arrival) mbar_arrive(&bar);  // the producer warp
+    if (threadIdx.x == 0) (void)mbar_wait_bounded(&bar, 0, DEVERR_TIMEOUT_PRODUCER);
+    __syncthreads();
+}
+}  // namespace selftest
+}  // namespace chelis
+
+extern "C" int chelis_cuda_selftest_bounded_wait(int skip_arrival) {
+    selftest::bounded_wait_probe_kernel<<<1, 64, 0, current_stream()>>>(skip_arrival);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("bounded_wait_probe_kernel");
+    return CHELIS_CUDA_OK;
+}

@@ -119,17 +119,23 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 // main loop is well under 100 ms even at k = 10^6).  On timeout the error bit
 // is recorded and false is returned: the caller skips its remaining work and
 // proceeds to teardown.
+// The limit is a device variable (default kMaxTries) that the host may
+// lower with chelis_cuda_set_wait_limit, so a test can make a wait run out
+// in about a millisecond and check the reported status.
 constexpr uint32_t kMaxTries = 1u << 22;
+__device__ uint32_t g_wait_tries = kMaxTries;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   unsigned int err_code) {
-    for (uint32_t i = 0; i < kMaxTries; ++i)
+    const uint32_t tries = *static_cast<volatile uint32_t *>(&g_wait_tries);
+    for (uint32_t i = 0; i < tries; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     report_device_error(err_code);
     return false;
 }
 __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity,
                                                           unsigned int err_code) {
-    for (uint32_t i = 0; i < kMaxTries; ++i)
+    const uint32_t tries = *static_cast<volatile uint32_t *>(&g_wait_tries);
+    for (uint32_t i = 0; i < tries; ++i)
         if (mbar_try_wait_cluster(bar, parity)) return true;
     report_device_error(err_code);
     return false;

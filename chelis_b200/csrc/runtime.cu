@@ -275,6 +275,17 @@ int chelis_cuda_device_status(void) {
 
 uint64_t chelis_cuda_launch_count(void) { return g_launches.load(); }
 
+int chelis_cuda_set_wait_limit(uint32_t tries) {
+    const uint32_t v = tries ? tries : kMaxTries;
+    return check_cuda(cudaMemcpyToSymbol(g_wait_tries, &v, sizeof(v)), "set wait limit");
+}
+
+uint32_t chelis_cuda_get_wait_limit(void) {
+    uint32_t v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_wait_tries, sizeof(v)) != cudaSuccess) return 0;
+    return v;
+}
+
 int chelis_cuda_set_gemm_mode(int mode) {
     if (mode != CHELIS_CUDA_GEMM_3XTF32 && mode != CHELIS_CUDA_GEMM_EXACT_TREE)
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown GEMM mode %d", mode);

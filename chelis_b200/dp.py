@@ -75,12 +75,17 @@ def native_finalize(abort: bool = False) -> None:
 
 
 def allreduce_sum(flat: torch.Tensor, world: int) -> None:
-    """Sum `flat` over the ranks, in place, on the current stream: through the
-    library's communicator when native_init opened one, else through
-    torch.distributed (gloo on CPU)."""
+    """Sum `flat` over the ranks, in place, on the current stream.  Device
+    tensors go through the library's communicator (native_init must have
+    opened it; otherwise this raises: there is no library-free path for
+    GPU data).  Host tensors, the CPU (gloo) form of the same host logic,
+    go through torch.distributed."""
     if world <= 1:
         return
-    if _native[0] and flat.is_cuda:
+    if flat.is_cuda:
+        if not _native[0]:
+            raise RuntimeError("dp.allreduce_sum on a CUDA tensor needs native_init "
+                               "(the library's NCCL communicator)")
         from . import ops
         ops._prepare(flat)
         dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64,

@@ -71,6 +71,9 @@ SIGNATURES = {
     "chelis_cuda_synchronize": (c_int, []),
     "chelis_cuda_device_status": (c_int, []),
     "chelis_cuda_launch_count": (c_u64, []),
+    "chelis_cuda_set_wait_limit": (c_int, [ctypes.c_uint32]),
+    "chelis_cuda_get_wait_limit": (ctypes.c_uint32, []),
+    "chelis_cuda_selftest_bounded_wait": (c_int, [c_int]),
     "chelis_cuda_set_gemm_mode": (c_int, [c_int]),
     "chelis_cuda_get_gemm_mode": (c_int, []),
     "chelis_cuda_set_rows_mode": (c_int, [c_int]),

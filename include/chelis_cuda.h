@@ -108,6 +108,18 @@ int chelis_cuda_synchronize(void);
 int chelis_cuda_device_status(void);
 /* Number of kernels this library launched since process start (all threads). */
 uint64_t chelis_cuda_launch_count(void);
+/* Probes every bounded device wait makes before it gives up and reports
+ * CHELIS_CUDA_ERR_TIMEOUT (about 1 us each; 0 restores the default of
+ * 2^22, a few seconds).  Device-wide for this process; for tests of the
+ * timeout path.  No counterpart in the reference (its waits are unbounded). */
+int chelis_cuda_set_wait_limit(uint32_t tries);
+uint32_t chelis_cuda_get_wait_limit(void);
+/* Self-test of the bounded wait: one CTA whose consumer thread waits on an
+ * mbarrier for a producer thread's arrival; skip_arrival != 0 tells the
+ * producer not to arrive, so the wait runs out after the wait limit and the
+ * next chelis_cuda_device_status returns CHELIS_CUDA_ERR_TIMEOUT.  The
+ * kernel always returns. */
+int chelis_cuda_selftest_bounded_wait(int skip_arrival);
 int chelis_cuda_set_gemm_mode(int mode);
 int chelis_cuda_get_gemm_mode(void);
 int chelis_cuda_set_rows_mode(int mode);
@@ -422,9 +434,11 @@ int chelis_cuda_chain_bwd_saved(const float *x, const float *gamma, const float 
  * CHELIS_CUDA_ERR_UNSUPPORTED).  Calls that overlap on the GPU share that
  * array and race; order them.  The first call on a device resolves the
  * array's address with that device current: make it before any stream
- * capture.  dgamma / dbeta use a different CTA grouping than
- * chelis_cuda_chain_bwd, so they agree with it within tolerance, dx bit for
- * bit. */
+ * capture; a device reset invalidates that address (do not call it on a
+ * device after resetting it).  The grid is two CTAs per SM, at most 296 (the
+ * array's capacity): dx is bit for bit chelis_cuda_chain_bwd's on any GPU,
+ * and on a 148-SM B200 so are dgamma / dbeta; on a GPU with more SMs they
+ * group rows differently and agree within f32 rounding. */
 int chelis_cuda_chain_bwd_noalloc(const float *x, const float *gamma, const float *beta,
                                   float eps, uint64_t key, float rate, int64_t rows,
                                   int64_t hidden, int64_t index_base, const float *row_stats,

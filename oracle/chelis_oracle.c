@@ -191,60 +191,133 @@ int64_t orc_count_bool(const uint8_t *x, int64_t n) {
 /* ------------------------------------------------------------------------ */
 
 
+/*
+ * The C lane streams every output's tree over k through a carry tree, in
+ * lane blocks of output columns that share one leaf schedule (emit.rs:
+ * 8113-8176).  The restatement does the same with blocks of 64 columns
+ * and one more step that leaves every value unchanged: an aligned run of 8
+ * leaves is a complete subtree of the canonical tree, so the first
+ * k - k % 8 leaves enter in groups, each group's subtree
+ * ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7)) formed in registers and pushed at
+ * depth 3; the carry tree then sees exactly the sums it would have built
+ * leaf by leaf.  The last k % 8 leaves enter one at a time.  Lanes are
+ * independent IEEE operations (GCC vector extensions; no reassociation, no
+ * contraction), so the values equal the scalar tree's bit for bit
+ * (tests/test_oracle.py checks this against orc_tree_sum_f32).
+ */
+#define VL 8 /* vector lanes per vector */
+#define NV (LANES / VL)
+typedef float v8f __attribute__((vector_size(VL * sizeof(float))));
+typedef double v8d __attribute__((vector_size(VL * sizeof(double))));
+
+#define DEFINE_GEMM_ROWS(T, V, SUFFIX, CANON)                                                  \
+    __attribute__((target_clones("avx2", "default"))) static void gemm_block_##SUFFIX(          \
+        const T *arow, int64_t sa1, const T *b, int64_t ldb, T *crow, int64_t k) {             \
+        V lv[64][NV];                                                                          \
+        V leaf[NV];                                                                            \
+        int64_t count = 0;                                                                     \
+        const int64_t kb_end = k & ~(int64_t)7;                                                \
+        for (int64_t kk = 0; kk < kb_end; kk += 8) {                                           \
+            const T a0 = arow[(kk + 0) * sa1], a1 = arow[(kk + 1) * sa1];                      \
+            const T a2 = arow[(kk + 2) * sa1], a3 = arow[(kk + 3) * sa1];                      \
+            const T a4 = arow[(kk + 4) * sa1], a5 = arow[(kk + 5) * sa1];                      \
+            const T a6 = arow[(kk + 6) * sa1], a7 = arow[(kk + 7) * sa1];                      \
+            const T *bp = b + kk * ldb;                                                        \
+            for (int v = 0; v < NV; ++v) {                                                     \
+                V b0, b1, b2, b3, b4, b5, b6, b7;                                              \
+                memcpy(&b0, bp + 0 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b1, bp + 1 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b2, bp + 2 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b3, bp + 3 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b4, bp + 4 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b5, bp + 5 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b6, bp + 6 * ldb + v * VL, sizeof(V));                                 \
+                memcpy(&b7, bp + 7 * ldb + v * VL, sizeof(V));                                 \
+                V p01 = (a0 * b0) + (a1 * b1), p23 = (a2 * b2) + (a3 * b3);                    \
+                V p45 = (a4 * b4) + (a5 * b5), p67 = (a6 * b6) + (a7 * b7);                    \
+                leaf[v] = (p01 + p23) + (p45 + p67);                                           \
+            }                                                                                  \
+            int depth = 3;                                                                     \
+            for (int64_t pending = count >> 3; pending & 1; pending >>= 1, ++depth)            \
+                for (int v = 0; v < NV; ++v) leaf[v] = lv[depth][v] + leaf[v];                 \
+            for (int v = 0; v < NV; ++v) lv[depth][v] = leaf[v];                               \
+            count += 8;                                                                        \
+        }                                                                                      \
+        for (int64_t kk = kb_end; kk < k; ++kk) {                                              \
+            const T av = arow[kk * sa1];                                                       \
+            for (int v = 0; v < NV; ++v) {                                                     \
+                V bv;                                                                          \
+                memcpy(&bv, b + kk * ldb + v * VL, sizeof(V));                                 \
+                leaf[v] = av * bv;                                                             \
+            }                                                                                  \
+            int depth = 0;                                                                     \
+            for (int64_t pending = count++; pending & 1; pending >>= 1, ++depth)               \
+                for (int v = 0; v < NV; ++v) leaf[v] = lv[depth][v] + leaf[v];                 \
+            for (int v = 0; v < NV; ++v) lv[depth][v] = leaf[v];                               \
+        }                                                                                      \
+        int found = 0, depth = 0;                                                              \
+        for (int v = 0; v < NV; ++v) leaf[v] = (V){0};                                         \
+        for (int64_t remaining = count; remaining; remaining >>= 1, ++depth) {                 \
+            if (remaining & 1) {                                                               \
+                for (int v = 0; v < NV; ++v) leaf[v] = found ? lv[depth][v] + leaf[v] : lv[depth][v]; \
+                found = 1;                                                                     \
+            }                                                                                  \
+        }                                                                                      \
+        for (int v = 0; v < NV; ++v)                                                           \
+            for (int l = 0; l < VL; ++l) crow[v * VL + l] = CANON(leaf[v][l]);                 \
+    }                                                                                          \
+    static void gemm_rows_##SUFFIX(const T *a, int64_t sa0, int64_t sa1, const T *b0,          \
+                                   int64_t sb0, int64_t sb1, T *c, int64_t ldc, int64_t n,     \
+                                   int64_t k, int64_t row_begin, int64_t row_end) {            \
+        /* a B that is not row-contiguous is first copied to row-major [k, n] */               \
+        T *bt = NULL;                                                                          \
+        const T *b = b0;                                                                       \
+        int64_t ldb = sb0;                                                                     \
+        if (sb1 != 1 && k > 0 && n > 0) {                                                      \
+            bt = (T *)malloc(sizeof(T) * (size_t)(k * n));                                     \
+            _Pragma("omp parallel for schedule(static)")                                       \
+            for (int64_t kk = 0; kk < k; ++kk)                                                 \
+                for (int64_t j = 0; j < n; ++j) bt[kk * n + j] = b0[kk * sb0 + j * sb1];       \
+            b = bt;                                                                            \
+            ldb = n;                                                                           \
+        }                                                                                      \
+        int64_t blocks = (n + LANES - 1) / LANES;                                              \
+        _Pragma("omp parallel for schedule(dynamic, 1) collapse(2)")                           \
+        for (int64_t i = row_begin; i < row_end; ++i) {                                        \
+            for (int64_t bj = 0; bj < blocks; ++bj) {                                          \
+                int64_t j0 = bj * LANES;                                                       \
+                int lanes = (int)((n - j0) < LANES ? (n - j0) : LANES);                        \
+                if (lanes == LANES) {                                                          \
+                    gemm_block_##SUFFIX(a + i * sa0, sa1, b + j0, ldb, c + i * ldc + j0, k);   \
+                    continue;                                                                  \
+                }                                                                              \
+                laned_##SUFFIX t;                                                              \
+                t.count = 0;                                                                   \
+                T leafs[LANES];                                                                \
+                for (int64_t kk = 0; kk < k; ++kk) {                                           \
+                    T av = a[i * sa0 + kk * sa1];                                              \
+                    const T *brow = b + kk * ldb + j0;                                         \
+                    for (int l = 0; l < lanes; ++l) leafs[l] = av * brow[l];                   \
+                    laned_push_##SUFFIX(&t, leafs, lanes);                                     \
+                }                                                                              \
+                laned_total_##SUFFIX(&t, leafs, lanes);                                        \
+                for (int l = 0; l < lanes; ++l) c[i * ldc + j0 + l] = CANON(leafs[l]);         \
+            }                                                                                  \
+        }                                                                                      \
+        free(bt);                                                                              \
+    }
+DEFINE_GEMM_ROWS(float, v8f, f32, canon_f32)
+DEFINE_GEMM_ROWS(double, v8d, f64, canon_f64)
+
 static void sgemm_rows(const float *a, int64_t sa0, int64_t sa1, const float *b, int64_t sb0,
                        int64_t sb1, float *c, int64_t ldc, int64_t n, int64_t k,
                        int64_t row_begin, int64_t row_end) {
-    int64_t blocks = (n + LANES - 1) / LANES;
-#pragma omp parallel for schedule(dynamic, 1) collapse(2)
-    for (int64_t i = row_begin; i < row_end; ++i) {
-        for (int64_t bj = 0; bj < blocks; ++bj) {
-            laned_f32 t;
-            t.count = 0;
-            float leaf[LANES];
-            int64_t j0 = bj * LANES;
-            int lanes = (int)((n - j0) < LANES ? (n - j0) : LANES);
-            for (int64_t kk = 0; kk < k; ++kk) {
-                float av = a[i * sa0 + kk * sa1];
-                const float *brow = b + kk * sb0 + j0 * sb1;
-                if (sb1 == 1) {
-                    for (int l = 0; l < lanes; ++l) leaf[l] = av * brow[l];
-                } else {
-                    for (int l = 0; l < lanes; ++l) leaf[l] = av * brow[l * sb1];
-                }
-                laned_push_f32(&t, leaf, lanes);
-            }
-            laned_total_f32(&t, leaf, lanes);
-            for (int l = 0; l < lanes; ++l) c[i * ldc + j0 + l] = canon_f32(leaf[l]);
-        }
-    }
+    gemm_rows_f32(a, sa0, sa1, b, sb0, sb1, c, ldc, n, k, row_begin, row_end);
 }
-
 static void dgemm_rows(const double *a, int64_t sa0, int64_t sa1, const double *b, int64_t sb0,
                        int64_t sb1, double *c, int64_t ldc, int64_t n, int64_t k,
                        int64_t row_begin, int64_t row_end) {
-    int64_t blocks = (n + LANES - 1) / LANES;
-#pragma omp parallel for schedule(dynamic, 1) collapse(2)
-    for (int64_t i = row_begin; i < row_end; ++i) {
-        for (int64_t bj = 0; bj < blocks; ++bj) {
-            laned_f64 t;
-            t.count = 0;
-            double leaf[LANES];
-            int64_t j0 = bj * LANES;
-            int lanes = (int)((n - j0) < LANES ? (n - j0) : LANES);
-            for (int64_t kk = 0; kk < k; ++kk) {
-                double av = a[i * sa0 + kk * sa1];
-                const double *brow = b + kk * sb0 + j0 * sb1;
-                if (sb1 == 1) {
-                    for (int l = 0; l < lanes; ++l) leaf[l] = av * brow[l];
-                } else {
-                    for (int l = 0; l < lanes; ++l) leaf[l] = av * brow[l * sb1];
-                }
-                laned_push_f64(&t, leaf, lanes);
-            }
-            laned_total_f64(&t, leaf, lanes);
-            for (int l = 0; l < lanes; ++l) c[i * ldc + j0 + l] = canon_f64(leaf[l]);
-        }
-    }
+    gemm_rows_f64(a, sa0, sa1, b, sb0, sb1, c, ldc, n, k, row_begin, row_end);
 }
 
 /* Row-major C[m,n] = A[m,k] . B[k,n]; only rows [row_begin, row_end) are
@@ -875,6 +948,7 @@ static float phi_graph_f32(float x) {
     return canon_f32(0.5f * canon_f32(e - corr));
 }
 void orc_gelu_f32(const float *x, float *y, int64_t n) {
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; ++i) {
         float m = (x[i] < -0x1.fffffep+127f) ? -0.0f : x[i]; /* the multiplicand guard m(x) */
         y[i] = canon_f32(m * phi_graph_f32(x[i]));
@@ -960,4 +1034,322 @@ int orc_cross_entropy_f32(const float *z, const int64_t *labels, int64_t rows, i
     free(g);
     free(tmp);
     return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* GELU adjoint: reverse mode through the Phi graph above                   */
+/* ------------------------------------------------------------------------ */
+/*
+ * The adjoint graph of gelu = mul(m(x), Phi(x)) node by node, with the
+ * rules of crates/chelis-dag-core/src/grad.rs: mul gives (g*b, g*a), sub
+ * gives (g, neg(g)), neg gives neg(g), exp gives g*exp(x), erfc gives
+ * neg(g*(k*exp(neg(x*x)))) with k = 2/sqrt(pi) rounded once to f32
+ * ([05-OP-46], grad.rs:2408-2425), where gives g on the chosen side and
+ * +0 on the other.  A node with several consumers sums their cotangents
+ * with the adjacent-pair tree in consumer order (balanced_adjoint_sum,
+ * grad.rs:1713-1745).  The constants ch, cr (the split of c) carry no
+ * cotangent.
+ */
+static float gelu_adjoint_one(float x, float g) {
+    const float c = 0x1.6a09e6p-1f, cl = 0x1.9fcef4p-27f, k = 0x1.20dd76p+0f, s = 4097.0f;
+    const float k2 = (float)1.12837916709551257390; /* 2/sqrt(pi) rounded to f32 */
+    /* forward values */
+    float n1 = canon_f32(-x);
+    float n2 = canon_f32(n1 * c);
+    float e = canon_f32(chelis_crmath_ffi_erfcf(n2));
+    int zc = fabsf(x) < 64.0f;
+    float z = zc ? x : 0.0f;
+    float a = canon_f32(-z);
+    float th = canon_f32(a * c);
+    float ta = canon_f32(s * a);
+    float t1 = canon_f32(ta - a);
+    float ah = canon_f32(ta - t1);
+    float al = canon_f32(a - ah);
+    float tc = canon_f32(s * c);
+    float ch = canon_f32(tc - canon_f32(tc - c));
+    float cr = canon_f32(c - ch);
+    float tl0 = canon_f32(canon_f32(ah * ch) - th);
+    float tl1 = canon_f32(tl0 + canon_f32(ah * cr));
+    float tl2 = canon_f32(tl1 + canon_f32(al * ch));
+    float tl3 = canon_f32(tl2 + canon_f32(al * cr));
+    float tl = canon_f32(tl3 + canon_f32(a * cl));
+    float sq = canon_f32(th * th);
+    float ex = canon_f32(chelis_crmath_ffi_expf(canon_f32(-sq)));
+    float kx = canon_f32(k * ex);
+    float corr = canon_f32(kx * tl);
+    float phi = canon_f32(0.5f * canon_f32(e - corr));
+    int mc = x < -0x1.fffffep+127f;
+    float m = mc ? -0.0f : x;
+    (void)tl2;
+    (void)tl3;
+    (void)tl1;
+    /* reverse sweep */
+    float g_m = canon_f32(g * phi);
+    float g_phi = canon_f32(g * m);
+    float g_df = canon_f32(g_phi * 0.5f);
+    float g_e = g_df;
+    float g_corr = canon_f32(-g_df);
+    float g_kx = canon_f32(g_corr * tl);
+    float g_tl = canon_f32(g_corr * kx);
+    float g_ex = canon_f32(g_kx * k);
+    float g_nsq = canon_f32(g_ex * ex);
+    float g_sq = canon_f32(-g_nsq);
+    /* tl = ((((ah*ch - th) + ah*cr) + al*ch) + al*cr) + a*cl */
+    float g_p1 = g_tl, g_p2 = g_tl, g_p3 = g_tl, g_p4 = g_tl, g_p5 = g_tl;
+    float g_th_tl = canon_f32(-g_tl);
+    /* th feeds tl0 (slot 1), then sq (slots 0 and 1) */
+    float g_th = canon_f32(canon_f32(g_th_tl + canon_f32(g_sq * th)) + canon_f32(g_sq * th));
+    /* al feeds p3 (al*ch), then p4 (al*cr) */
+    float g_al = canon_f32(canon_f32(g_p3 * ch) + canon_f32(g_p4 * cr));
+    /* ah feeds al = a - ah (slot 1), then p1, then p2 */
+    float g_ah = canon_f32(canon_f32(canon_f32(-g_al) + canon_f32(g_p1 * ch)) + canon_f32(g_p2 * cr));
+    /* t1 = ta - a feeds ah = ta - t1 (slot 1) */
+    float g_t1 = canon_f32(-g_ah);
+    /* ta feeds t1 (slot 0), then ah (slot 0) */
+    float g_ta = canon_f32(g_t1 + g_ah);
+    /* a feeds th, ta, t1 (slot 1), al (slot 0), p5: five cotangents */
+    float ga0 = canon_f32(g_th * c), ga1 = canon_f32(g_ta * s), ga2 = canon_f32(-g_t1);
+    float ga3 = g_al, ga4 = canon_f32(g_p5 * cl);
+    float g_a = canon_f32(canon_f32(canon_f32(ga0 + ga1) + canon_f32(ga2 + ga3)) + ga4);
+    float g_z = canon_f32(-g_a);
+    /* erfc adjoint, then n2 = n1 * c, n1 = neg(x) */
+    float dens = canon_f32(chelis_crmath_ffi_expf(canon_f32(-canon_f32(n2 * n2))));
+    float g_n2 = canon_f32(-canon_f32(g_e * canon_f32(k2 * dens)));
+    float g_n1 = canon_f32(g_n2 * c);
+    float gx0 = canon_f32(-g_n1);
+    float gx1 = zc ? g_z : 0.0f;
+    float gx2 = mc ? 0.0f : g_m;
+    return canon_f32(canon_f32(gx0 + gx1) + gx2);
+}
+
+void orc_gelu_adjoint_f32(const float *x, const float *g, float *dx, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) dx[i] = gelu_adjoint_one(x[i], g[i]);
+}
+
+/* ------------------------------------------------------------------------ */
+/* transformer block: pre-LN, causal multi-head attention, GELU MLP         */
+/* ------------------------------------------------------------------------ */
+/*
+ * Per sample (the batch is the vmap axis, crates/chelis-ir-core/src/
+ * vmap.rs:9-56):
+ *   h1 = layer_norm(x; g1, b1)                      tier2.rs:1248-1375
+ *   [q k v] = h1 . Wqkv                             [S, 3D], row-major
+ *   per head h (columns h*Dh .. h*Dh+Dh of q, k, v), spec/05-risc-
+ *   primitives.md:5146-5181:
+ *     raw = q_h . k_h^T; scores = raw * scale; masked = where(j <= i,
+ *     scores, -inf); p = softmax(masked, last axis); o_h = p . v_h
+ *   x2 = x + o . Wo
+ *   h2 = layer_norm(x2; g2, b2)
+ *   u = h2 . W1;  y = x2 + gelu(u) . W2
+ * with scale = 1/sqrtf(Dh) at f32.  Every matmul is the tree over its
+ * contracted axis in increasing order (emit.rs:8431-8640), the masked
+ * entries included (their probabilities are +0).
+ *
+ * Reverse mode for an upstream cotangent dy (grad.rs adjoint graphs): the
+ * matmul adjoint is a matmul with a transposed operand ([05-OP-51]); the
+ * softmax adjoint p*(g - sum(g*p)) (grad.rs:2248-2280); where passes the
+ * cotangent on the chosen side, +0 on the other; mul by the scale gives
+ * g*scale; layer_norm's adjoint is orc_layer_norm_bwd_f32's graph; a node
+ * with several consumers sums their cotangents in consumer order (x2: its
+ * layer_norm, then the residual add; x: likewise).  A weight is broadcast
+ * along the batch axis, so its gradient is the per-sample gradient (tree
+ * over the sequence) summed over samples by the canonical tree (the Expand
+ * adjoint, grad.rs Sum over the broadcast axis).
+ */
+
+/* Streaming canonical tree over equally sized arrays (one leaf per sample). */
+typedef struct {
+    float *level[64];
+    int64_t count, n;
+} array_tree;
+
+static void array_tree_push(array_tree *t, float *leaf) {
+    /* leaf is consumed: it becomes a level array or is freed */
+    int depth = 0;
+    for (int64_t pending = t->count++; pending & 1; pending >>= 1, ++depth) {
+        float *lv = t->level[depth];
+        for (int64_t i = 0; i < t->n; ++i) leaf[i] = lv[i] + leaf[i];
+        free(lv);
+        t->level[depth] = NULL;
+    }
+    t->level[depth] = leaf;
+}
+
+static void array_tree_total(array_tree *t, float *out) {
+    int found = 0, depth = 0;
+    for (int64_t remaining = t->count; remaining; remaining >>= 1, ++depth) {
+        if (remaining & 1) {
+            float *lv = t->level[depth];
+            if (found)
+                for (int64_t i = 0; i < t->n; ++i) out[i] = lv[i] + out[i];
+            else
+                memcpy(out, lv, sizeof(float) * (size_t)t->n);
+            found = 1;
+            free(lv);
+            t->level[depth] = NULL;
+        }
+    }
+    if (!found) memset(out, 0, sizeof(float) * (size_t)t->n);
+    for (int64_t i = 0; i < t->n; ++i) out[i] = canon_f32(out[i]);
+}
+
+static float *falloc(int64_t n) { return (float *)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1)); }
+
+/* Causal attention of one head, forward: p [S,S] and o_h (ldo stride). */
+static void attn_head_fwd(const float *q, const float *k, const float *v, int64_t ld, int64_t S,
+                          int64_t Dh, float scale, float *p, float *o, int64_t ldo) {
+    /* raw = q . k^T: A = q (rows of ld), B[kk][j] = k[j][kk] */
+    sgemm_rows(q, ld, 1, k, 1, ld, p, S, S, Dh, 0, S);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < S; ++i) {
+        float *pr = p + i * S;
+        for (int64_t j = 0; j < S; ++j) pr[j] = (j <= i) ? canon_f32(pr[j] * scale) : -INFINITY;
+        softmax_row(pr, pr, S);
+    }
+    /* o_h = p . v_h */
+    sgemm_rows(p, S, 1, v, ld, 1, o, ldo, Dh, S, 0, S);
+}
+
+/* Reverse of one head: dq, dk, dv into dqkv columns (ld), given p and do_h. */
+static void attn_head_bwd(const float *q, const float *k, const float *v, int64_t ld,
+                          const float *p, const float *dout, int64_t lddo, int64_t S, int64_t Dh,
+                          float scale, float *dp, float *dq, float *dk, float *dv) {
+    /* dv = p^T . do_h */
+    sgemm_rows(p, 1, S, dout, lddo, 1, dv, ld, Dh, S, 0, S);
+    /* dp = do_h . v_h^T */
+    sgemm_rows(dout, lddo, 1, v, 1, ld, dp, S, S, Dh, 0, S);
+#pragma omp parallel
+    {
+        float *tmp = falloc(S);
+#pragma omp for schedule(static)
+        for (int64_t i = 0; i < S; ++i) {
+            const float *pr = p + i * S;
+            float *dr = dp + i * S;
+            softmax_row_bwd(pr, dr, dr, tmp, S);
+            for (int64_t j = 0; j < S; ++j) dr[j] = (j <= i) ? canon_f32(dr[j] * scale) : 0.0f;
+        }
+        free(tmp);
+    }
+    /* dq = ds . k_h; dk = ds^T . q_h */
+    sgemm_rows(dp, S, 1, k, ld, 1, dq, ld, Dh, S, 0, S);
+    sgemm_rows(dp, 1, S, q, ld, 1, dk, ld, Dh, S, 0, S);
+}
+
+int orc_block_step(const float *x, const float *dy, int64_t batch, int64_t S, int64_t D,
+                   int64_t H, int64_t F, float eps, const float *w_qkv, const float *w_o,
+                   const float *w_1, const float *w_2, const float *g1, const float *b1,
+                   const float *g2, const float *b2, float *y, float *dx, float *dw_qkv,
+                   float *dw_o, float *dw_1, float *dw_2, float *dg1, float *db1, float *dg2,
+                   float *db2) {
+    if (batch < 0 || S <= 0 || D <= 0 || H <= 0 || F <= 0 || D % H) return 1;
+    const int64_t Dh = D / H, D3 = 3 * D, SD = S * D;
+    const float scale = 1.0f / sqrtf((float)Dh);
+    float *h1 = falloc(SD), *qkv = falloc(S * D3), *o = falloc(SD), *x2 = falloc(SD);
+    float *h2 = falloc(SD), *u = falloc(S * F), *act = falloc(S * F), *ps = falloc(H * S * S);
+    float *c = falloc(D), *nn = falloc(D);
+    /* reverse scratch */
+    float *da = falloc(S * F), *du = falloc(S * F), *dh2 = falloc(SD), *dx2 = falloc(SD);
+    float *dln = falloc(SD), *dout = falloc(SD), *dqkv = falloc(S * D3), *dh1 = falloc(SD);
+    float *dp = falloc(S * S);
+    array_tree tw[8];
+    const int64_t wn[8] = {D * D3, D * D, D * F, F * D, D, D, D, D};
+    for (int t = 0; t < 8; ++t) {
+        memset(&tw[t], 0, sizeof(tw[t]));
+        tw[t].n = wn[t];
+    }
+    for (int64_t b = 0; b < batch; ++b) {
+        const float *xb = x + b * SD;
+        float *yb = y + b * SD;
+        /* ---- forward ---- */
+        orc_layer_norm_f32(xb, g1, b1, eps, h1, S, D);
+        sgemm_rows(h1, D, 1, w_qkv, D3, 1, qkv, D3, D3, D, 0, S);
+        for (int64_t h = 0; h < H; ++h)
+            attn_head_fwd(qkv + h * Dh, qkv + D + h * Dh, qkv + 2 * D + h * Dh, D3, S, Dh, scale,
+                          ps + h * S * S, o + h * Dh, D);
+        sgemm_rows(o, D, 1, w_o, D, 1, x2, D, D, D, 0, S);
+        for (int64_t i = 0; i < SD; ++i) x2[i] = canon_f32(xb[i] + x2[i]);
+        orc_layer_norm_f32(x2, g2, b2, eps, h2, S, D);
+        sgemm_rows(h2, D, 1, w_1, F, 1, u, F, F, D, 0, S);
+        orc_gelu_f32(u, act, S * F);
+        sgemm_rows(act, F, 1, w_2, D, 1, yb, D, D, F, 0, S);
+        for (int64_t i = 0; i < SD; ++i) yb[i] = canon_f32(x2[i] + yb[i]);
+        if (!dy) continue;
+        /* ---- reverse ---- */
+        const float *dyb = dy + b * SD;
+        float *dw2b = falloc(F * D), *dw1b = falloc(D * F), *dwob = falloc(D * D);
+        float *dwqkvb = falloc(D * D3);
+        float *dg2b = falloc(D), *db2b = falloc(D), *dg1b = falloc(D), *db1b = falloc(D);
+        /* y = x2 + act . W2 */
+        sgemm_rows(act, 1, F, dyb, D, 1, dw2b, D, D, S, 0, F);   /* dW2 = act^T dy */
+        sgemm_rows(dyb, D, 1, w_2, 1, D, da, F, F, D, 0, S);     /* da = dy W2^T */
+        orc_gelu_adjoint_f32(u, da, du, S * F);
+        sgemm_rows(h2, 1, D, du, F, 1, dw1b, F, F, S, 0, D);     /* dW1 = h2^T du */
+        sgemm_rows(du, F, 1, w_1, 1, F, dh2, D, D, F, 0, S);     /* dh2 = du W1^T */
+        orc_layer_norm_bwd_f32(x2, g2, eps, dh2, S, D, dln, dg2b, db2b);
+        for (int64_t i = 0; i < SD; ++i) dx2[i] = canon_f32(dln[i] + dyb[i]);
+        /* x2 = x + o . Wo */
+        sgemm_rows(o, 1, D, dx2, D, 1, dwob, D, D, S, 0, D);     /* dWo = o^T dx2 */
+        sgemm_rows(dx2, D, 1, w_o, 1, D, dout, D, D, D, 0, S);   /* do = dx2 Wo^T */
+        for (int64_t h = 0; h < H; ++h)
+            attn_head_bwd(qkv + h * Dh, qkv + D + h * Dh, qkv + 2 * D + h * Dh, D3,
+                          ps + h * S * S, dout + h * Dh, D, S, Dh, scale, dp, dqkv + h * Dh,
+                          dqkv + D + h * Dh, dqkv + 2 * D + h * Dh);
+        sgemm_rows(h1, 1, D, dqkv, D3, 1, dwqkvb, D3, D3, S, 0, D); /* dWqkv = h1^T dqkv */
+        sgemm_rows(dqkv, D3, 1, w_qkv, 1, D3, dh1, D, D, D3, 0, S); /* dh1 = dqkv Wqkv^T */
+        orc_layer_norm_bwd_f32(xb, g1, eps, dh1, S, D, dln, dg1b, db1b);
+        float *dxb = dx + b * SD;
+        for (int64_t i = 0; i < SD; ++i) dxb[i] = canon_f32(dln[i] + dx2[i]);
+        array_tree_push(&tw[0], dwqkvb);
+        array_tree_push(&tw[1], dwob);
+        array_tree_push(&tw[2], dw1b);
+        array_tree_push(&tw[3], dw2b);
+        array_tree_push(&tw[4], dg1b);
+        array_tree_push(&tw[5], db1b);
+        array_tree_push(&tw[6], dg2b);
+        array_tree_push(&tw[7], db2b);
+    }
+    if (dy) {
+        float *outs[8] = {dw_qkv, dw_o, dw_1, dw_2, dg1, db1, dg2, db2};
+        for (int t = 0; t < 8; ++t) array_tree_total(&tw[t], outs[t]);
+    }
+    (void)c;
+    (void)nn;
+    free(h1); free(qkv); free(o); free(x2); free(h2); free(u); free(act); free(ps);
+    free(c); free(nn); free(da); free(du); free(dh2); free(dx2); free(dln); free(dout);
+    free(dqkv); free(dh1); free(dp);
+    return 0;
+}
+
+/* The causal attention of one [S, Dh] head set on its own (q, k, v of shape
+ * [bh, S, Dh]), forward and, with dout, reverse: the head loop of
+ * orc_block_step. */
+void orc_attention_causal(const float *q, const float *k, const float *v, const float *dout,
+                          int64_t bh, int64_t S, int64_t Dh, float scale, float *o, float *dq,
+                          float *dk, float *dv) {
+    float *p = falloc(S * S), *dp = falloc(S * S);
+    for (int64_t h = 0; h < bh; ++h) {
+        const int64_t off = h * S * Dh;
+        attn_head_fwd(q + off, k + off, v + off, Dh, S, Dh, scale, p, o + off, Dh);
+        if (!dout) continue;
+        /* dq, dk, dv share one leading dimension (Dh) in this layout */
+        sgemm_rows(p, 1, S, dout + off, Dh, 1, dv + off, Dh, Dh, S, 0, S);
+        sgemm_rows(dout + off, Dh, 1, v + off, 1, Dh, dp, S, S, Dh, 0, S);
+#pragma omp parallel
+        {
+            float *tmp = falloc(S);
+#pragma omp for schedule(static)
+            for (int64_t i = 0; i < S; ++i) {
+                const float *pr = p + i * S;
+                float *dr = dp + i * S;
+                softmax_row_bwd(pr, dr, dr, tmp, S);
+                for (int64_t j = 0; j < S; ++j) dr[j] = (j <= i) ? canon_f32(dr[j] * scale) : 0.0f;
+            }
+            free(tmp);
+        }
+        sgemm_rows(dp, S, 1, k + off, Dh, 1, dq + off, Dh, Dh, S, 0, S);
+        sgemm_rows(dp, 1, S, q + off, Dh, 1, dk + off, Dh, Dh, S, 0, S);
+    }
+    free(p);
+    free(dp);
 }

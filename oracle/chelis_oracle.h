@@ -130,6 +130,24 @@ void orc_layer_norm_bwd_f32(const float *x, const float *gamma, float eps, const
 int orc_cross_entropy_f32(const float *z, const int64_t *labels, int64_t rows, int64_t classes,
                           float *loss, float *dz);
 
+/* ---- GELU adjoint: reverse mode through the Phi graph (grad.rs rules) ---- */
+void orc_gelu_adjoint_f32(const float *x, const float *g, float *dx, int64_t n);
+
+/* ---- transformer block (config 4): pre-LN, causal attention (spec/05-risc-
+ * primitives.md:5146-5181), GELU MLP; forward and, when dy is non-NULL, the
+ * vector-Jacobian product.  x, dy, y, dx are [batch, S, D]; w_qkv [D, 3D],
+ * w_o [D, D], w_1 [D, F], w_2 [F, D]; returns 1 on a shape it does not admit. */
+int orc_block_step(const float *x, const float *dy, int64_t batch, int64_t S, int64_t D,
+                   int64_t H, int64_t F, float eps, const float *w_qkv, const float *w_o,
+                   const float *w_1, const float *w_2, const float *g1, const float *b1,
+                   const float *g2, const float *b2, float *y, float *dx, float *dw_qkv,
+                   float *dw_o, float *dw_1, float *dw_2, float *dg1, float *db1, float *dg2,
+                   float *db2);
+/* causal attention per head, q/k/v/o [bh, S, Dh]; reverse when dout != NULL */
+void orc_attention_causal(const float *q, const float *k, const float *v, const float *dout,
+                          int64_t bh, int64_t S, int64_t Dh, float scale, float *o, float *dq,
+                          float *dk, float *dv);
+
 #ifdef __cplusplus
 }
 #endif

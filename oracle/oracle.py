@@ -387,3 +387,54 @@ def cross_entropy(z, labels):
     if fn(p(z), p(labels), _i64(rows), _i64(classes), p(loss), p(dz)) != 0:
         raise ValueError("label out of range")
     return loss[0], dz
+
+
+BLOCK_WEIGHTS = ("w_qkv", "w_o", "w_1", "w_2", "ln1_gamma", "ln1_beta", "ln2_gamma", "ln2_beta")
+
+
+def gelu_adjoint(x: np.ndarray, g: np.ndarray) -> np.ndarray:
+    x, g = _c(x, np.float32), _c(g, np.float32)
+    dx = np.empty_like(x)
+    fn = lib().orc_gelu_adjoint_f32
+    fn.restype = None
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    fn(p(x), p(g), p(dx), _i64(x.size))
+    return dx
+
+
+def block_step(x, w: dict, heads: int, eps: float, dy=None):
+    """Transformer block forward (+ VJP when dy is given), orc_block_step.
+    Returns (y, grads) with grads keyed "dx" and "d<weight>" (None without dy)."""
+    x = _c(x, np.float32)
+    batch, seq, d = x.shape
+    dff = w["w_1"].shape[1]
+    ws = [_c(w[k], np.float32) for k in BLOCK_WEIGHTS]
+    y = np.empty_like(x)
+    grads = None
+    p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+    if dy is not None:
+        dy = _c(dy, np.float32)
+        grads = {"dx": np.empty_like(x)}
+        grads.update({"d" + k: np.empty_like(a) for k, a in zip(BLOCK_WEIGHTS, ws)})
+    outs = [None] * 9 if grads is None else [grads["dx"]] + [grads["d" + k] for k in BLOCK_WEIGHTS]
+    fn = lib().orc_block_step
+    fn.restype = ctypes.c_int
+    rc = fn(p(x), p(dy), _i64(batch), _i64(seq), _i64(d), _i64(heads), _i64(dff),
+            ctypes.c_float(eps), *[p(a) for a in ws], p(y), *[p(a) for a in outs])
+    if rc:
+        raise ValueError("orc_block_step: shape not admitted")
+    return y, grads
+
+
+def attention_causal(q, k, v, scale: float, dout=None):
+    """Causal attention per head on [bh, S, Dh]: o, and (dq, dk, dv) with dout."""
+    q, k, v = (_c(t, np.float32) for t in (q, k, v))
+    bh, seq, dh = q.shape
+    o = np.empty_like(q)
+    g = [np.empty_like(q) for _ in range(3)] if dout is not None else [None] * 3
+    p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+    fn = lib().orc_attention_causal
+    fn.restype = None
+    fn(p(q), p(k), p(v), p(None if dout is None else _c(dout, np.float32)), _i64(bh), _i64(seq),
+       _i64(dh), ctypes.c_float(scale), p(o), *[p(a) for a in g])
+    return (o, tuple(g)) if dout is not None else o

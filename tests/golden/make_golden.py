@@ -1,8 +1,8 @@
 """Regenerate the golden fixtures under tests/golden/ from the reference tree.
 
-Run in a container where the reference is mounted (default /root/reference,
-or pass its path).  The outputs are committed; tests never read the reference
-tree at run time.
+Usage: python tests/golden/make_golden.py <reference-root> (or set
+CHELIS_REFERENCE to the reference checkout).  The outputs are committed;
+tests never read the reference tree at run time.
 
 * crmath_f32.txt -- the f32 exp / log / erfc rows of the reference's CORE-MATH
   canary fixture (crates/chelis-crmath/tests/fixtures/canary.txt): function,
@@ -20,7 +20,9 @@ tree at run time.
 import os
 import sys
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CHELIS_REFERENCE", "")
+if not REF or not os.path.isdir(REF):
+    sys.exit("usage: make_golden.py <reference-root> (or CHELIS_REFERENCE=<reference-root>)")
 FIX = os.path.join(REF, "crates/chelis-crmath/tests/fixtures")
 OUT = os.path.dirname(os.path.abspath(__file__))
 

@@ -32,7 +32,7 @@ def _normwise(got, ref):
 
 
 @pytest.mark.parametrize("bh,seq,dh", [(1, 1, 64), (2, 64, 64), (3, 200, 64), (2, 384, 32),
-                                       (4, 1000, 64), (1, 129, 32)])
+                                       (4, 1000, 64), (1, 129, 32), (2, 2048, 64), (1, 2048, 32)])
 def test_attention_causal_matches_float64(cuda, bh, seq, dh):
     import torch
     rng = np.random.default_rng(bh * 1000 + seq + dh)
@@ -71,7 +71,8 @@ def _reference_grads(q, k, v, dout, scale, dtype):
 
 
 @pytest.mark.parametrize("bh,seq,dh", [(1, 1, 64), (2, 64, 64), (3, 200, 64), (2, 384, 32),
-                                       (2, 1000, 64), (1, 129, 32), (1, 300, 64)])
+                                       (2, 1000, 64), (1, 129, 32), (1, 300, 64), (2, 2048, 64),
+                                       (1, 2048, 32)])
 def test_attention_causal_bwd_matches_float64(cuda, bh, seq, dh):
     """dq, dk, dv from the blockwise recomputation against float64 autograd;
     each within max(1e-5, 3 x the float32 autograd error), normwise."""
@@ -90,3 +91,24 @@ def test_attention_causal_bwd_matches_float64(cuda, bh, seq, dh):
         bound = max(1e-5, 3.0 * _normwise(g32, g64))
         err = _normwise(got.cpu().numpy(), g64)
         assert err <= bound, (name, err, bound)
+
+
+@pytest.mark.parametrize("bh,seq,dh", [(2, 2048, 64), (1, 777, 64)])
+def test_attention_causal_matches_oracle(cuda, orc, bh, seq, dh):
+    """Forward and reverse against the oracle's per-head restatement of the
+    reference graph (scores materialised, canonical trees): o, dq, dk, dv
+    within normwise f32 rel 1e-5."""
+    import torch
+    rng = np.random.default_rng(bh + seq)
+    q, k, v, do = (rng.standard_normal((bh, seq, dh)).astype(np.float32) for _ in range(4))
+    scale = float(np.float32(1.0 / np.sqrt(dh)))
+    tq, tk, tv, tdo = (torch.from_numpy(t).cuda() for t in (q, k, v, do))
+    o, lse = cuda.attention_causal(tq, tk, tv, scale, with_lse=True)
+    dq, dk, dv = cuda.attention_causal_bwd(tq, tk, tv, o, lse, tdo, scale)
+    torch.cuda.synchronize()
+    cuda.device_status()
+    o_ref, (dq_ref, dk_ref, dv_ref) = orc.attention_causal(q, k, v, scale, do)
+    for name, got, ref in (("o", o, o_ref), ("dq", dq, dq_ref), ("dk", dk, dk_ref),
+                           ("dv", dv, dv_ref)):
+        err = _normwise(got.cpu().numpy(), ref.astype(np.float64))
+        assert err <= 1e-5, (name, err)

@@ -13,45 +13,9 @@ import numpy as np
 import pytest
 
 from chelis_b200 import workloads as W
+from _block_ref import normwise, reference
 
 pytestmark = pytest.mark.gpu
-
-
-def reference(x, dy, w, heads, eps, dtype=None):
-    import torch
-    dtype = dtype or torch.float64
-    T = {k: torch.tensor(v, dtype=dtype, requires_grad=True) for k, v in w.items()}
-    X = torch.tensor(x, dtype=dtype, requires_grad=True)
-    B, S, D = x.shape
-    Dh = D // heads
-
-    def ln(v, g, b):
-        m = v.mean(-1, keepdim=True)
-        c = v - m
-        var = (c * c).mean(-1, keepdim=True)
-        return c / torch.sqrt(var + eps) * g + b
-
-    h1 = ln(X, T["ln1_gamma"], T["ln1_beta"])
-    qkv = h1 @ T["w_qkv"]
-    q, k, v = qkv.split(D, dim=-1)
-    q = q.view(B, S, heads, Dh).transpose(1, 2)
-    k = k.view(B, S, heads, Dh).transpose(1, 2)
-    v = v.view(B, S, heads, Dh).transpose(1, 2)
-    s = (q @ k.transpose(-1, -2)) * (1.0 / np.sqrt(Dh))
-    mask = torch.ones(S, S, dtype=torch.bool).tril()
-    s = torch.where(mask, s, torch.tensor(-float("inf"), dtype=dtype))
-    o = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B, S, D)
-    x2 = X + o @ T["w_o"]
-    h2 = ln(x2, T["ln2_gamma"], T["ln2_beta"])
-    y = x2 + torch.nn.functional.gelu(h2 @ T["w_1"]) @ T["w_2"]
-    y.backward(torch.tensor(dy, dtype=dtype))
-    grads = {"d" + k: t.grad.double().numpy() for k, t in T.items()}
-    grads["dx"] = X.grad.double().numpy()
-    return y.detach().double().numpy(), grads
-
-
-def normwise(got, ref):
-    return float(np.abs(got.astype(np.float64) - ref).max() / np.abs(ref).max())
 
 
 @pytest.mark.parametrize("shape", [
@@ -87,3 +51,46 @@ def test_block_workspace_entry_matches_pool_entry(cuda):
     b = cuda.block_step(X, wt, 2, 1e-5, DY, workspace=ws)
     for k in a:
         assert torch.equal(a[k], b[k]), k
+
+
+def _oracle_bound_check(out, y_ref, g_ref, tol):
+    errs = {"y": normwise(out["y"].cpu().numpy(), y_ref)}
+    errs.update({k: normwise(out[k].cpu().numpy(), v) for k, v in g_ref.items()})
+    bad = {k: e for k, e in errs.items() if not e <= tol}
+    assert not bad, (bad, errs)
+    return errs
+
+
+@pytest.mark.parametrize("shape", [
+    dict(batch=2, seq=64, d_model=128, heads=2, d_ff=512),
+    dict(batch=1, seq=300, d_model=256, heads=4, d_ff=1024),
+])
+def test_block_matches_oracle_small(cuda, orc, shape):
+    """The CUDA block against the oracle's restatement of the reference graph
+    (orc_block_step): every output within normwise f32 rel 1e-5."""
+    import torch
+    x, dy, w = W.block_inputs(seed=11, **shape)
+    wt = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    out = cuda.block_step(torch.from_numpy(x).cuda(), wt, shape["heads"], 1e-5,
+                          torch.from_numpy(dy).cuda())
+    torch.cuda.synchronize()
+    cuda.device_status()
+    y_ref, g_ref = orc.block_step(x, w, shape["heads"], 1e-5, dy)
+    _oracle_bound_check(out, y_ref, g_ref, 1e-5)
+
+
+def test_block_config4_shape_matches_oracle(cuda, orc):
+    """Config 4 at its own shape (S 2048, d_model 1024, 16 heads of 64, d_ff
+    4096; one sample of the batch of 8, seed 3) against the oracle: y, dx and
+    all eight parameter gradients within normwise f32 rel 1e-5."""
+    import torch
+    shape = dict(W.BLOCK_SHAPE, batch=1)
+    x, dy, w = W.block_inputs(seed=3, **shape)
+    wt = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    out = cuda.block_step(torch.from_numpy(x).cuda(), wt, shape["heads"], 1e-5,
+                          torch.from_numpy(dy).cuda())
+    torch.cuda.synchronize()
+    cuda.device_status()
+    y_ref, g_ref = orc.block_step(x, w, shape["heads"], 1e-5, dy)
+    errs = _oracle_bound_check(out, y_ref, g_ref, 1e-5)
+    print("config-4 normwise errors vs oracle:", {k: f"{v:.2e}" for k, v in errs.items()})

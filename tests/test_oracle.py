@@ -189,6 +189,30 @@ def test_oracle_gemm_matches_tree_per_output(orc):
     assert (ct.view(np.uint32) == c.view(np.uint32)).all()
 
 
+@pytest.mark.parametrize("k", [0, 1, 7, 8, 9, 64, 100, 263, 1024])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_oracle_gemm_grouped_leaves_equal_the_carry_tree(orc, k, dtype):
+    """Full 64-column blocks take 8-leaf groups (each an aligned subtree) into
+    the carry tree; the values must equal the leaf-by-leaf tree bit for bit,
+    with specials among the operands, for plain and transposed operands."""
+    rng = np.random.default_rng(k + 11)
+    m, n = 3, 150  # two full 64-column blocks and a ragged one
+    a = (rng.standard_normal((m, k)) * 10 ** rng.uniform(-4, 4, (m, k))).astype(dtype)
+    b = (rng.standard_normal((k, n)) * 10 ** rng.uniform(-4, 4, (k, n))).astype(dtype)
+    if k > 9:
+        a[1, 5] = np.inf
+        b[7, 3] = np.nan
+        b[2, 70] = -np.inf
+    c = orc.gemm(a, b)
+    view = np.uint32 if dtype == np.float32 else np.uint64
+    for i in range(m):
+        for j in (0, 3, 63, 64, 70, 127, 128, 149):
+            leaves = (a[i, :] * b[:, j]).astype(dtype)
+            assert c[i, j].view(view) == np.asarray(orc.tree_sum(leaves), dtype).view(view), (i, j)
+    ct = orc.gemm_t(a.T.copy(), b.T.copy(), True, True)
+    assert (ct.view(view) == c.view(view)).all()
+
+
 # ---------------------------------------------------------------- CORE-MATH and IEEE pins
 
 def _golden(name):
@@ -286,3 +310,62 @@ def test_cumsum_first_prefix_is_first_input(orc):
     assert np.signbit(y[0, 0]) and y[0, 2] == 3.0
     yr = orc.cumsum(x, reverse=True)
     assert yr[0].tolist() == [3.0, 3.0, 2.0]
+
+
+# ---------------------------------------------------------------- transformer block (config 4)
+
+@pytest.mark.parametrize("shape", [
+    dict(batch=2, seq=64, d_model=128, heads=2, d_ff=512),
+    dict(batch=1, seq=200, d_model=128, heads=4, d_ff=384),
+    dict(batch=3, seq=17, d_model=64, heads=2, d_ff=96),
+])
+def test_oracle_block_step_matches_float64_autograd(orc, shape):
+    """orc_block_step (the reference graph restated: tree matmuls, masked
+    softmax, Phi-graph GELU and the AD graphs) against torch float64 autograd
+    of the same block: every output within normwise 2e-6 and no further
+    from float64 than a plain float32 evaluation is."""
+    import torch
+    from _block_ref import normwise, reference
+    from chelis_b200 import workloads as W
+    x, dy, w = W.block_inputs(seed=5, **shape)
+    y, g = orc.block_step(x, w, shape["heads"], 1e-5, dy)
+    y64, g64 = reference(x, dy, w, shape["heads"], 1e-5)
+    y32, g32 = reference(x, dy, w, shape["heads"], 1e-5, torch.float32)
+    assert normwise(y, y64) <= max(2e-6, normwise(y32, y64))
+    for k in g64:
+        assert normwise(g[k], g64[k]) <= max(2e-6, normwise(g32[k], g64[k])), k
+    y_only, none = orc.block_step(x, w, shape["heads"], 1e-5)
+    assert none is None and np.array_equal(y_only, y)
+
+
+def test_oracle_attention_matches_block_heads_and_float64(orc):
+    import torch
+    rng = np.random.default_rng(4)
+    bh, seq, dh = 3, 150, 32
+    q, k, v, do = (rng.standard_normal((bh, seq, dh)).astype(np.float32) for _ in range(4))
+    scale = float(np.float32(1.0 / np.sqrt(dh)))
+    o, (dq, dk, dv) = orc.attention_causal(q, k, v, scale, do)
+    Q, K, V = (torch.tensor(t, dtype=torch.float64, requires_grad=True) for t in (q, k, v))
+    s = (Q @ K.transpose(-1, -2)) * scale
+    s = torch.where(torch.ones(seq, seq, dtype=torch.bool).tril(), s,
+                    torch.tensor(-float("inf"), dtype=torch.float64))
+    out = torch.softmax(s, -1) @ V
+    out.backward(torch.tensor(do, dtype=torch.float64))
+    for got, ref in ((o, out), (dq, Q.grad), (dk, K.grad), (dv, V.grad)):
+        ref = ref.detach().numpy()
+        assert np.abs(got - ref).max() / np.abs(ref).max() <= 2e-6
+
+
+def test_oracle_gelu_adjoint_is_the_derivative(orc):
+    """The reverse sweep through the Phi graph equals g * (Phi(x) + x phi(x))
+    to a few f32 ulps; at the guard values it follows the graph's selects."""
+    from math import erfc, exp, pi, sqrt
+    rng = np.random.default_rng(8)
+    x = np.concatenate([rng.standard_normal(4000) * 3, [0.0, -0.0, 1e-30, -9.0, 9.0, 63.9, -63.9,
+                                                        70.0, -70.0]]).astype(np.float32)
+    g = rng.standard_normal(x.size).astype(np.float32)
+    dx = orc.gelu_adjoint(x, g)
+    for xi, gi, di in zip(x.astype(np.float64), g.astype(np.float64), dx.astype(np.float64)):
+        der = 0.5 * erfc(-xi / sqrt(2.0)) + xi * exp(-0.5 * xi * xi) / sqrt(2.0 * pi)
+        ref = gi * der
+        assert abs(di - ref) <= 4e-7 * max(abs(gi), 1e-30) + 1e-37, (xi, gi, di, ref)
