@@ -587,6 +587,33 @@ int mm(int ta, int tb, int64_t m, int64_t n, int64_t k, const float *a, int64_t 
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Optional phase timing of chelis_cuda_block_step: CUDA events recorded on
+// the call's stream at the boundaries of its phases, read back after the
+// step.  A diagnostic for one host thread at a time (the events are
+// process-wide); off by default, and then no event is recorded.
+// ---------------------------------------------------------------------------
+namespace block_timing {
+constexpr int kPhases = 16;
+const char *const kNames[kPhases] = {
+    "ln1",          "gemm_qkv",     "attention_fwd", "gemm_o_residual", "ln2",
+    "gemm_mlp_up",  "gelu",         "gemm_mlp_down_residual", "gemm_dw2_da", "gelu_bwd",
+    "gemm_dw1_dh2", "ln2_bwd",      "gemm_dwo_do",   "attention_bwd",   "gemm_dwqkv_dh1",
+    "ln1_bwd"};
+bool g_on = false;
+int g_dev = -1;
+cudaEvent_t g_ev[kPhases + 1] = {};
+bool g_rec[kPhases + 1] = {};
+
+inline void mark(int i, cudaStream_t s) {
+    if (!g_on) return;
+    g_rec[i] = cudaEventRecord(g_ev[i], s) == cudaSuccess;
+}
+inline void reset() {
+    for (bool &r : g_rec) r = false;
+}
+}  // namespace block_timing
+
 extern "C" int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p) {
     BlockDims d;
     if (block_dims(p, d) != CHELIS_CUDA_OK) return -1;
@@ -622,10 +649,15 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
     // split copies for the fused path: [q_hi, q_lo, k_hi, k_lo, v_hi, v_lo, dO_hi, dO_lo]
     float *hl = w.hl;
     int st = CHELIS_CUDA_OK;
+    using block_timing::mark;
+    block_timing::reset();
     do {
         // ---------------- forward ----------------
+        mark(0, s);
         if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, w.h1, w.st1, BS, D, s))) break;
+        mark(1, s);
         if ((st = mm(0, 0, BS, 3 * D, D, w.h1, D, p->w_qkv, 3 * D, w.qkv, 3 * D))) break;
+        mark(2, s);
         if (fused) {
             block::qkv_heads_split_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
                 w.qkv, w.q, w.k, w.v, hl, act, static_cast<int>(d.B), static_cast<int>(S),
@@ -650,29 +682,40 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
             g_launches++;
             if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
         }
+        mark(3, s);
         if ((st = mm(0, 0, BS, D, D, w.o, D, p->w_o, D, w.x2, D))) break;
         if ((st = add(p->x, w.x2, w.x2, BS * D, s))) break;
+        mark(4, s);
         if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) break;
+        mark(5, s);
         if ((st = mm(0, 0, BS, F, D, w.h2, D, p->w_1, F, w.u, F))) break;
+        mark(6, s);
         block::gelu_fwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.g, BS * F);
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_fwd_kernel"))) break;
+        mark(7, s);
         if ((st = mm(0, 0, BS, D, F, w.g, F, p->w_2, D, p->y, D))) break;
         if ((st = add(w.x2, p->y, p->y, BS * D, s))) break;
+        mark(8, s);
         if (!p->dy) break;
         // ---------------- reverse mode ----------------
         const float *dy = p->dy;
         if ((st = mm(1, 0, F, D, BS, w.g, F, dy, D, p->dw_2, D))) break;
         if ((st = mm(0, 1, BS, F, D, dy, D, p->w_2, D, w.dg, F))) break;
+        mark(9, s);
         block::gelu_bwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.dg, BS * F);
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_bwd_kernel"))) break;
+        mark(10, s);
         if ((st = mm(1, 0, D, F, BS, w.h2, D, w.dg, F, p->dw_1, F))) break;
         if ((st = mm(0, 1, BS, D, F, w.dg, F, p->w_1, F, w.dh2, D))) break;
+        mark(11, s);
         if ((st = ln_bwd(w.x2, w.dh2, w.st2, p->ln2_gamma, dy, w.dx2, w.part, p->dln2_gamma,
                          p->dln2_beta, BS, D, s))) break;
+        mark(12, s);
         if ((st = mm(1, 0, D, D, BS, w.o, D, w.dx2, D, p->dw_o, D))) break;
         if ((st = mm(0, 1, BS, D, D, w.dx2, D, p->w_o, D, w.dO, D))) break;
+        mark(13, s);
         if (fused) {
             block::rows_heads_split_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
                 w.dO, hl + 6 * act, hl + 7 * act, static_cast<int>(d.B), static_cast<int>(S),
@@ -700,12 +743,58 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
             g_launches++;
             if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
         }
+        mark(14, s);
         if ((st = mm(1, 0, D, 3 * D, BS, w.h1, D, w.dqkv, 3 * D, p->dw_qkv, 3 * D))) break;
         if ((st = mm(0, 1, BS, D, 3 * D, w.dqkv, 3 * D, p->w_qkv, 3 * D, w.dh1, D))) break;
+        mark(15, s);
         if ((st = ln_bwd(p->x, w.dh1, w.st1, p->ln1_gamma, w.dx2, p->dx, w.part, p->dln1_gamma,
                          p->dln1_beta, BS, D, s))) break;
+        mark(16, s);
     } while (0);
     if (owned_big) scratch_free(owned_big, s);
     if (owned) scratch_free(owned, s);
     return st;
+}
+
+extern "C" int chelis_cuda_block_timing(int enable) {
+    using namespace block_timing;
+    int dev = 0;
+    CHELIS_TRY(current_device_checked(&dev));
+    if (g_dev >= 0 && (!enable || g_dev != dev)) {
+        for (cudaEvent_t &e : g_ev) {
+            if (e) cudaEventDestroy(e);
+            e = nullptr;
+        }
+        g_dev = -1;
+    }
+    g_on = false;
+    reset();
+    if (!enable) return CHELIS_CUDA_OK;
+    for (cudaEvent_t &e : g_ev)
+        CHELIS_TRY(check_cuda(cudaEventCreate(&e), "cudaEventCreate(block timing)"));
+    g_dev = dev;
+    g_on = true;
+    return CHELIS_CUDA_OK;
+}
+
+extern "C" int chelis_cuda_block_phase_ms(float *ms, int32_t n) {
+    using namespace block_timing;
+    if (!ms || n < kPhases)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "block_phase_ms needs room for %d phases", kPhases);
+    if (!g_on) return set_error(CHELIS_CUDA_ERR_DOMAIN, "block timing is off");
+    for (int i = 0; i < kPhases; ++i) ms[i] = 0.0f;
+    for (int i = kPhases; i >= 0; --i)
+        if (g_rec[i]) {
+            CHELIS_TRY(check_cuda(cudaEventSynchronize(g_ev[i]), "cudaEventSynchronize"));
+            break;
+        }
+    for (int i = 0; i < kPhases; ++i)
+        if (g_rec[i] && g_rec[i + 1])
+            CHELIS_TRY(check_cuda(cudaEventElapsedTime(&ms[i], g_ev[i], g_ev[i + 1]),
+                                  "cudaEventElapsedTime"));
+    return CHELIS_CUDA_OK;
+}
+
+extern "C" const char *chelis_cuda_block_phase_name(int32_t i) {
+    return (i >= 0 && i < block_timing::kPhases) ? block_timing::kNames[i] : nullptr;
 }

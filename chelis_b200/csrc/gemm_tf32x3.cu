@@ -16,11 +16,22 @@
 // tile kernel.  The main kernel streams four tiles per stage with TMA
 // (128-byte swizzle) and tells tcgen05.mma each operand's major-ness.
 //
-// Main kernel (one 128 x 256 output tile per CTA, 192 threads):
+// Main kernel (one 128 x 256 output tile per CTA, or 256 x 256 per CTA
+// pair, 320 threads per CTA):
 //   warp 0      TMA producer (one elected lane)
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
-//   warps 2-5   epilogue: tcgen05.ld of the 128 x 256 f32 accumulator
-//               (TMEM lanes = rows, 256 columns) and stores to C
+//   warps 2-9   epilogue: fold the accumulator chunks (below) into f32
+//               registers, then store the 128 x 256 tile rows to C
+//
+// Chunked accumulation.  The tensor core's f32 accumulator does not add like
+// a chain of IEEE additions: kept over a long K in one TMEM accumulator, the
+// error grows linearly with K (measured against float64: normwise 2e-6 at
+// K = 256, 5.8e-5 at K = 8192, 16x cuBLAS's FFMA GEMM there).  So every
+// accumulator covers CHUNK_KB k-blocks (128 of K) from a fresh start,
+// alternating between two 256-column TMEM buffers, and the eight epilogue
+// warps fold each finished chunk into f32 registers with IEEE additions
+// (two warps per TMEM lane quadrant, 128 columns each) while the MMAs fill
+// the other buffer.  Error then grows like an f32 sum of K/128 terms.
 // Every mbarrier wait is bounded (common.cuh) so a fault in the pipeline
 // reports CHELIS_CUDA_ERR_TIMEOUT instead of hanging the GPU.
 #include <cuda.h>
@@ -38,9 +49,6 @@ int gemm_mode();
 // 1: 3xTF32 products with more than 128 rows run on CTA pairs (default);
 // 0: one CTA per 128 x 256 tile everywhere
 std::atomic<int> g_pair_tiles{1};
-// 1: row-major products on CTA pairs split their operands inside the main
-// kernel; 0 (default): always through the split pre-pass
-std::atomic<int> g_split_in_kernel{0};
 
 namespace tf32x3 {
 
@@ -52,8 +60,14 @@ constexpr int A_TILE_BYTES = BM * BK * 4;  // 16 KiB
 constexpr int B_TILE_BYTES = BN * BK * 4;  // 32 KiB
 constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr int EPI_WARPS = 8;                 // warps 2..9
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // 320
+// k-blocks per fresh accumulator.  Measured at 8192^3 (normwise error vs
+// float64, main kernel ms): 2 -> 8.6e-7, 4.53; 4 -> 9.9e-7, 4.20; 8 ->
+// 1.8e-6, 4.58; 16 -> 3.9e-6, 4.48; one accumulator -> 6.5e-5, 4.36.
+constexpr int CHUNK_KB = 4;
+constexpr uint32_t ACC_COLS = 256;            // one 128 x 256 f32 accumulator
+constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;  // two, alternating by chunk
 constexpr int MN_BOX = 32;                  // MN-major TMA box: 32 (MN) x 32 (K) f32
 constexpr int MN_BOX_BYTES = MN_BOX * BK * 4;  // 4 KiB
 
@@ -69,6 +83,7 @@ struct Params {
     // partial product to part[blockIdx.z] ([m][n], dense) when splits > 1
     int32_t splits, kb_per_split;
     float *part;
+    int32_t chunk_kb;  // k-blocks per fresh accumulator (CHUNK_KB)
 };
 
 // Operand layouts in shared memory (both written by TMA):
@@ -111,6 +126,75 @@ __device__ __forceinline__ void load_operand(unsigned char *dst, const CUtensorM
     }
 }
 
+// Epilogue warps (2..9): fold the tile's accumulator chunks, chunk c in TMEM
+// buffer c & 1, into `run` (this thread's row, this warp's 128 columns),
+// releasing each buffer to the MMA issuer once read.  In a CTA pair the
+// release goes to rank 0's barrier (the issuer's), from both CTAs.  False
+// on a timeout or an aborted pipeline.
+template <bool PAIR>
+__device__ __forceinline__ bool fold_chunks(uint32_t tmem_base, int nchunks, uint64_t *chunk_full,
+                                            uint64_t *chunk_empty, int warp, int lane,
+                                            float (&run)[128], volatile uint32_t *abort_flag) {
+    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;   // warps 2-5: columns 0..127, 6-9: 128..255
+    const uint32_t lanes = static_cast<uint32_t>(quad * 32) << 16;
+    for (int c = 0; c < nchunks; ++c) {
+        const int b = c & 1;
+        if (!mbar_wait_bounded(&chunk_full[b], (c >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+            *abort_flag = 1;
+            return false;
+        }
+        tc_fence_after();
+        if (*abort_flag) return false;
+        const uint32_t base = tmem_base + lanes + static_cast<uint32_t>(b) * ACC_COLS +
+                              static_cast<uint32_t>(half * 128);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(base + j * 32, r);
+            tmem_wait_ld();
+            if (c == 0) {
+#pragma unroll
+                for (int t = 0; t < 32; ++t) run[j * 32 + t] = __uint_as_float(r[t]);
+            } else {
+#pragma unroll
+                for (int t = 0; t < 32; ++t)
+                    run[j * 32 + t] = __fadd_rn(run[j * 32 + t], __uint_as_float(r[t]));
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            if (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&chunk_empty[b]), 0));
+            else mbar_arrive(&chunk_empty[b]);
+        }
+    }
+    return true;
+}
+
+// This thread's row (m0 + lane quadrant row), this warp's 128 columns, to C.
+__device__ __forceinline__ void store_run(const float (&run)[128], int warp, int lane, int64_t m0,
+                                          int64_t n0, int64_t batch, const Params &p) {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int64_t row = m0 + quad * 32 + lane;
+    if (row >= p.m) return;
+    float *crow = p.c + batch * p.stride_c + row * p.ldc;
+    const int64_t col0 = n0 + half * 128;
+    const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
+                        ((p.stride_c & 3) == 0);
+    if (vec_ok && col0 + 128 <= p.n) {
+#pragma unroll
+        for (int j = 0; j < 128; j += 4)
+            *reinterpret_cast<float4 *>(crow + col0 + j) =
+                make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 128; ++j)
+            if (col0 + j < p.n) crow[col0 + j] = run[j];
+    }
+}
+
 template <bool AMN, bool BMN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_ahi,
@@ -123,8 +207,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
     uint64_t *empty = full + STAGES;
-    uint64_t *accum_full = empty + STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+    uint64_t *chunk_full = empty + STAGES;   // [2]: MMA commit of a chunk
+    uint64_t *chunk_empty = chunk_full + 2;  // [2]: epilogue warps have read it
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(chunk_empty + 2);
     volatile uint32_t *abort_flag = tmem_slot + 1;
     volatile int32_t *consumed = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
     int32_t issued = 0;
@@ -134,13 +219,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
     const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
     const int64_t batch = blockIdx.z;
+    const int nchunks = (p.num_kb + p.chunk_kb - 1) / p.chunk_kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&chunk_full[b], 1);
+            mbar_init(&chunk_empty[b], EPI_WARPS);
+        }
         *abort_flag = 0;
         *consumed = 0;
         fence_mbarrier_init();
@@ -190,7 +279,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN) | (AMN ? (1u << 15) : 0u) |
                                        (BMN ? (1u << 16) : 0u);
+            int cur = 0;  // accumulator buffer of the chunk in progress
             for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int c = kb / p.chunk_kb;
+                const bool first = (kb % p.chunk_kb) == 0;
+                cur = c & 1;
+                // buffer `cur` last held chunk c - 2: wait until it was folded
+                if (first && c >= 2) {
+                    if (!mbar_wait_bounded(&chunk_empty[cur], ((c >> 1) - 1) & 1,
+                                           DEVERR_TIMEOUT_MMA)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                }
                 const int s = kb % STAGES;
                 const uint32_t phase = (kb / STAGES) & 1;
                 if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
@@ -202,56 +304,33 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t ahi = st, alo = st + A_TILE_BYTES;
                 const uint32_t bhi = st + 2 * A_TILE_BYTES;
                 const uint32_t blo = bhi + B_TILE_BYTES;
+                const uint32_t d = tmem_base + static_cast<uint32_t>(cur) * ACC_COLS;
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t acc = (kb | kk) ? 1u : 0u;
-                    mma_tf32_ss(tmem_base, operand_desc<AMN>(alo, kk), operand_desc<BMN>(bhi, kk),
-                                idesc, acc);
-                    mma_tf32_ss(tmem_base, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(blo, kk),
-                                idesc, 1u);
-                    mma_tf32_ss(tmem_base, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(bhi, kk),
-                                idesc, 1u);
+                    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+                    mma_tf32_ss(d, operand_desc<AMN>(alo, kk), operand_desc<BMN>(bhi, kk), idesc,
+                                acc);
+                    mma_tf32_ss(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(blo, kk), idesc,
+                                1u);
+                    mma_tf32_ss(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(bhi, kk), idesc,
+                                1u);
                 }
                 mma_commit(&empty[s]);
                 *consumed = kb + 1;
+                if ((kb % p.chunk_kb) == p.chunk_kb - 1 || kb == p.num_kb - 1)
+                    mma_commit(&chunk_full[cur]);
             }
-            // Signal the epilogue either way; on abort it skips the stores.
-            mma_commit(accum_full);
+            // on abort, release the epilogue waiting for the unfinished chunk
+            if (*abort_flag) mma_commit(&chunk_full[cur]);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-        const bool ok = mbar_wait_bounded(accum_full, 0, DEVERR_TIMEOUT_EPILOGUE);
-        tc_fence_after();
-        if (ok && !*abort_flag) {
-            const int64_t row = m0 + quad * 32 + lane;
-            float *crow = p.c + batch * p.stride_c + row * p.ldc;
-            const bool row_ok = row < p.m;
-            const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
-                                ((p.stride_c & 3) == 0);
-#pragma unroll 1
-            for (int cb = 0; cb < BN / 32; ++cb) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + cb * 32, r);
-                tmem_wait_ld();
-                const int64_t col0 = n0 + cb * 32;
-                if (row_ok) {
-                    if (vec_ok && col0 + 32 <= p.n) {
+        // ---------------- epilogue (warps 2..9) ----------------
+        float run[128];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                   __uint_as_float(r[j + 2]),
-                                                   __uint_as_float(r[j + 3]));
-                            *reinterpret_cast<float4 *>(crow + col0 + j) = v;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.n) crow[col0 + j] = __uint_as_float(r[j]);
-                    }
-                }
-            }
-        }
+        for (int j = 0; j < 128; ++j) run[j] = 0.0f;  // K = 0: the empty sum
+        if (fold_chunks<false>(tmem_base, nchunks, chunk_full, chunk_empty, warp, lane, run,
+                               abort_flag))
+            store_run(run, warp, lane, m0, n0, batch, p);
     }
 
     tc_fence_before();
@@ -299,38 +378,6 @@ __device__ __forceinline__ void load_operand_pair(unsigned char *dst, const CUte
     }
 }
 
-// Epilogue of one CTA: its 128 accumulator rows (TMEM lanes) x 256 columns
-// to C.  Warps 2..5 each own the TMEM lane quadrant (warp & 3).
-__device__ __forceinline__ void store_accumulator(uint32_t tmem_base, int warp, int lane,
-                                                  int64_t m0, int64_t n0, int64_t batch,
-                                                  const Params &p) {
-    const int quad = warp & 3;
-    const int64_t row = m0 + quad * 32 + lane;
-    float *crow = p.c + batch * p.stride_c + row * p.ldc;
-    const bool row_ok = row < p.m;
-    const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
-                        ((p.stride_c & 3) == 0);
-#pragma unroll 1
-    for (int cb = 0; cb < BN / 32; ++cb) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + cb * 32, r);
-        tmem_wait_ld();
-        const int64_t col0 = n0 + cb * 32;
-        if (!row_ok) continue;
-        if (vec_ok && col0 + 32 <= p.n) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4 *>(crow + col0 + j) =
-                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.n) crow[col0 + j] = __uint_as_float(r[j]);
-        }
-    }
-}
-
 template <bool AMN, bool BMN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_ahi,
@@ -345,8 +392,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
     uint64_t *empty = full + P_STAGES;
-    uint64_t *accum_full = empty + P_STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+    uint64_t *chunk_full = empty + P_STAGES;  // [2]: MMA commit of a chunk (both CTAs)
+    uint64_t *chunk_empty = chunk_full + 2;   // [2]: rank 0's; both CTAs' epilogues arrive
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(chunk_empty + 2);
     volatile uint32_t *abort_flag = tmem_slot + 1;
     volatile int32_t *consumed = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
     int32_t issued = 0;
@@ -376,13 +424,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t batch = zz / p.splits;
     const int kb_lo = split * p.kb_per_split;
     const int nk = (p.num_kb - kb_lo < p.kb_per_split) ? p.num_kb - kb_lo : p.kb_per_split;
+    const int nchunks = (nk + p.chunk_kb - 1) / p.chunk_kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&chunk_full[b], 1);
+            mbar_init(&chunk_empty[b], 2 * EPI_WARPS);
+        }
         *abort_flag = 0;
         *consumed = 0;
         fence_mbarrier_init();
@@ -398,7 +450,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_relinquish_pair();
     }
     // barrier inits of both CTAs are visible cluster-wide before any remote
-    // arrival (TMA bytes from rank 1, multicast commits from rank 0)
+    // arrival (TMA bytes from rank 1, multicast commits from rank 0, chunk
+    // releases from rank 1's epilogue)
     tc_fence_before();
     cluster_sync_all();
     tc_fence_after();
@@ -436,7 +489,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && rank == 0) {
             constexpr uint32_t idesc = idesc_tf32(2 * P_ROWS, BN) | (AMN ? (1u << 15) : 0u) |
                                        (BMN ? (1u << 16) : 0u);
+            int cur = 0;  // accumulator buffer of the chunk in progress
             for (int i = 0; i < nk; ++i) {
+                const int c = i / p.chunk_kb;
+                const bool first = (i % p.chunk_kb) == 0;
+                cur = c & 1;
+                // buffer `cur` last held chunk c - 2: wait until both CTAs
+                // have folded it (their epilogues arrive at cluster scope)
+                if (first && c >= 2) {
+                    if (!mbar_wait_cluster_bounded(&chunk_empty[cur], ((c >> 1) - 1) & 1,
+                                                   DEVERR_TIMEOUT_MMA)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                }
                 const int s = i % P_STAGES;
                 const uint32_t phase = (i / P_STAGES) & 1;
                 if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
@@ -447,35 +514,41 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t st = smem_u32(smem + s * P_STAGE_BYTES);
                 const uint32_t ahi = st, alo = st + P_TILE_BYTES;
                 const uint32_t bhi = st + 2 * P_TILE_BYTES, blo = st + 3 * P_TILE_BYTES;
+                const uint32_t d = tmem_base + static_cast<uint32_t>(cur) * ACC_COLS;
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t acc = (i | kk) ? 1u : 0u;
-                    mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(alo, kk),
-                                     operand_desc<BMN>(bhi, kk), idesc, acc);
-                    mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(ahi, kk),
-                                     operand_desc<BMN>(blo, kk), idesc, 1u);
-                    mma_tf32_ss_pair(tmem_base, operand_desc<AMN>(ahi, kk),
-                                     operand_desc<BMN>(bhi, kk), idesc, 1u);
+                    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+                    mma_tf32_ss_pair(d, operand_desc<AMN>(alo, kk), operand_desc<BMN>(bhi, kk),
+                                     idesc, acc);
+                    mma_tf32_ss_pair(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(blo, kk),
+                                     idesc, 1u);
+                    mma_tf32_ss_pair(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(bhi, kk),
+                                     idesc, 1u);
                 }
                 mma_commit_pair(&empty[s], 0x3);
                 *consumed = i + 1;
+                if ((i % p.chunk_kb) == p.chunk_kb - 1 || i == nk - 1)
+                    mma_commit_pair(&chunk_full[cur], 0x3);
             }
-            // both epilogues proceed either way; on abort rank 0 skips its stores
-            mma_commit_pair(accum_full, 0x3);
+            // on abort, release both epilogues waiting for the unfinished
+            // chunk; rank 0 skips its stores
+            if (*abort_flag) mma_commit_pair(&chunk_full[cur], 0x3);
         }
     } else {
-        // ---------------- epilogue (warps 2..5, both CTAs) ----------------
-        const bool ok = mbar_wait_bounded(accum_full, 0, DEVERR_TIMEOUT_EPILOGUE);
-        tc_fence_after();
-        if (ok && !*abort_flag) {
+        // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+        float run[128];
+#pragma unroll
+        for (int j = 0; j < 128; ++j) run[j] = 0.0f;  // K = 0: the empty sum
+        if (fold_chunks<true>(tmem_base, nchunks, chunk_full, chunk_empty, warp, lane, run,
+                              abort_flag)) {
             if (p.splits > 1) {
                 Params q = p;
                 q.c = p.part;
                 q.ldc = p.n;
                 q.stride_c = p.m * p.n;
-                store_accumulator(tmem_base, warp, lane, m0, n0, zz, q);
+                store_run(run, warp, lane, m0, n0, zz, q);
             } else {
-                store_accumulator(tmem_base, warp, lane, m0, n0, batch, p);
+                store_run(run, warp, lane, m0, n0, batch, p);
             }
         }
     }
@@ -604,204 +677,6 @@ __global__ void split_rows_kernel(const float *__restrict__ src, int64_t rows, i
     }
 }
 
-// ---------------------------------------------------------------------------
-// CTA-pair kernel with the split in shared memory, for row-major A and B
-// (A K-major, B MN-major, both read straight from the caller's tensors).
-// TMA stages the raw f32 tiles; in each CTA the four epilogue warps split
-// every staged tile before the MMAs read it -- hi = RN_tf32(x) written back
-// in place, lo = RN_tf32(x - hi) into the stage's lo slot, the values the
-// split pre-pass would have produced -- and afterwards run the epilogue.  The
-// MMAs, their operands and order are those of gemm_pair_kernel<0, 1>, so the
-// product is bit-identical to the pre-split path, without the pre-pass's HBM
-// round trip (read x, write hi and lo, read both back) and its launches.
-//
-// Barriers per stage s: full[s] (each CTA, its own TMA bytes), conv[s]
-// (rank 0, one arrival per converting warp of both CTAs, release / acquire
-// at cluster scope after a proxy fence, so the tensor core sees the split
-// tiles), empty[s] (both CTAs, the MMA commit).  Every wait is bounded.
-// ---------------------------------------------------------------------------
-constexpr int F_CONV_THREADS = THREADS - 64;   // warps 2..5
-constexpr int F_CONV_WARPS = F_CONV_THREADS / 32;
-
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_pair_split_kernel(const __grid_constant__ CUtensorMap map_a,
-                           const __grid_constant__ CUtensorMap map_b, Params p) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
-    uint64_t *conv = full + P_STAGES;
-    uint64_t *empty = conv + P_STAGES;
-    uint64_t *accum_full = empty + P_STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
-    volatile uint32_t *abort_flag = tmem_slot + 1;
-    volatile int32_t *converted = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
-    int32_t issued = 0;
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();
-    int64_t pm, pn;
-    {
-        const int64_t pid = blockIdx.x >> 1;
-        const int64_t per_group = static_cast<int64_t>(P_GROUP) * p.tiles_n;
-        const int64_t first = (pid / per_group) * P_GROUP;
-        const int64_t rem = p.pairs_m - first;
-        const int64_t gsize = rem < P_GROUP ? rem : P_GROUP;
-        const int64_t in = pid % per_group;
-        pm = first + in % gsize;
-        pn = in / gsize;
-    }
-    const int64_t m0 = pm * (2 * P_ROWS) + rank * P_ROWS;
-    const int64_t n0 = pn * BN;
-    const int64_t nb0 = n0 + rank * P_ROWS;
-    const int64_t zz = blockIdx.z;
-    const int split = static_cast<int>(zz % p.splits);
-    const int64_t batch = zz / p.splits;
-    const int kb_lo = split * p.kb_per_split;
-    const int nk = (p.num_kb - kb_lo < p.kb_per_split) ? p.num_kb - kb_lo : p.kb_per_split;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < P_STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&conv[s], 2 * F_CONV_WARPS);
-            mbar_init(&empty[s], 1);
-        }
-        mbar_init(accum_full, 1);
-        *abort_flag = 0;
-        *converted = 0;
-        fence_mbarrier_init();
-    }
-    if (warp == 0 && lane == 0) {
-        prefetch_tensormap(&map_a);
-        prefetch_tensormap(&map_b);
-    }
-    if (warp == 1) {
-        tmem_alloc_pair(tmem_slot, TMEM_COLS);
-        tmem_relinquish_pair();
-    }
-    tc_fence_before();
-    cluster_sync_all();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-
-    if (warp == 0) {
-        // ---------------- TMA producer (both CTAs, own barriers) ----------------
-        if (lane == 0) {
-            const int32_t z = static_cast<int32_t>(batch);
-            for (int i = 0; i < nk; ++i) {
-                const int kb = kb_lo + i;
-                const int s = i % P_STAGES;
-                const uint32_t phase = (i / P_STAGES) & 1;
-                if (!mbar_wait_bounded(&empty[s], phase ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(&full[s], 2 * P_TILE_BYTES);
-                unsigned char *st = smem + s * P_STAGE_BYTES;
-                tma_load_3d(st, &map_a, &full[s], kb * BK, static_cast<int32_t>(m0), z);
-#pragma unroll
-                for (int j = 0; j < P_ROWS / MN_BOX; ++j)
-                    tma_load_3d(st + 2 * P_TILE_BYTES + j * MN_BOX_BYTES, &map_b, &full[s],
-                                static_cast<int32_t>(nb0) + j * MN_BOX, kb * BK, z);
-                issued = i + 1;
-            }
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer (rank 0 only) ----------------
-        if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_tf32(2 * P_ROWS, BN) | (1u << 16);  // B MN-major
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % P_STAGES;
-                const uint32_t phase = (i / P_STAGES) & 1;
-                if (!mbar_wait_cluster_bounded(&conv[s], phase, DEVERR_TIMEOUT_MMA)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t st = smem_u32(smem + s * P_STAGE_BYTES);
-                const uint32_t ahi = st, alo = st + P_TILE_BYTES;
-                const uint32_t bhi = st + 2 * P_TILE_BYTES, blo = st + 3 * P_TILE_BYTES;
-#pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t acc = (i | kk) ? 1u : 0u;
-                    mma_tf32_ss_pair(tmem_base, operand_desc<false>(alo, kk),
-                                     operand_desc<true>(bhi, kk), idesc, acc);
-                    mma_tf32_ss_pair(tmem_base, operand_desc<false>(ahi, kk),
-                                     operand_desc<true>(blo, kk), idesc, 1u);
-                    mma_tf32_ss_pair(tmem_base, operand_desc<false>(ahi, kk),
-                                     operand_desc<true>(bhi, kk), idesc, 1u);
-                }
-                mma_commit_pair(&empty[s], 0x3);
-            }
-            mma_commit_pair(accum_full, 0x3);
-        }
-    } else {
-        // ---------------- split (warps 2..5, both CTAs), then epilogue ----------------
-        const int t = threadIdx.x - 64;
-        bool ok = true;
-        for (int i = 0; i < nk; ++i) {
-            const int s = i % P_STAGES;
-            const uint32_t phase = (i / P_STAGES) & 1;
-            if (*abort_flag || !mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_EPILOGUE)) {
-                *abort_flag = 1;
-                ok = false;
-                break;
-            }
-            if (t == 0) *converted = i + 1;
-            unsigned char *st = smem + s * P_STAGE_BYTES;
-            // the A tile (stage offset 0) and the B tile (2 tiles in), 16-byte
-            // chunks; a chunk's lo lands one tile further on
-#pragma unroll 4
-            for (int j = 0; j < 2 * P_TILE_BYTES / 16 / F_CONV_THREADS; ++j) {
-                const int idx = t + j * F_CONV_THREADS;
-                const int region = idx / (P_TILE_BYTES / 16);
-                float4 *x4 = reinterpret_cast<float4 *>(st + region * 2 * P_TILE_BYTES +
-                                                        (idx % (P_TILE_BYTES / 16)) * 16);
-                const float4 v = *x4;
-                const float h0 = rna_tf32(v.x), h1 = rna_tf32(v.y), h2 = rna_tf32(v.z),
-                            h3 = rna_tf32(v.w);
-                const float4 lo = make_float4(isfinite(v.x) ? rna_tf32(__fsub_rn(v.x, h0)) : 0.0f,
-                                              isfinite(v.y) ? rna_tf32(__fsub_rn(v.y, h1)) : 0.0f,
-                                              isfinite(v.z) ? rna_tf32(__fsub_rn(v.z, h2)) : 0.0f,
-                                              isfinite(v.w) ? rna_tf32(__fsub_rn(v.w, h3)) : 0.0f);
-                *x4 = make_float4(h0, h1, h2, h3);
-                *reinterpret_cast<float4 *>(reinterpret_cast<unsigned char *>(x4) + P_TILE_BYTES) = lo;
-            }
-            // the split tiles are read by the tensor core (async proxy) of rank 0
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&conv[s]), 0));
-        }
-        ok = mbar_wait_bounded(accum_full, 0, DEVERR_TIMEOUT_EPILOGUE) && ok;
-        tc_fence_after();
-        if (ok && !*abort_flag) {
-            if (p.splits > 1) {
-                Params q = p;
-                q.c = p.part;
-                q.ldc = p.n;
-                q.stride_c = p.m * p.n;
-                store_accumulator(tmem_base, warp, lane, m0, n0, zz, q);
-            } else {
-                store_accumulator(tmem_base, warp, lane, m0, n0, batch, p);
-            }
-        }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0 && lane == 0 && *abort_flag) {
-        // loads this CTA issued land on its own `full` barriers
-        for (int kb = *converted; kb < issued; ++kb)
-            mbar_wait_bounded(&full[kb % P_STAGES], (kb / P_STAGES) & 1, DEVERR_TIMEOUT_PRODUCER);
-    }
-    tc_fence_before();
-    cluster_sync_all();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem_base, TMEM_COLS);
-    }
-}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
@@ -855,47 +730,6 @@ int make_mnmajor_map(CUtensorMap *map, const float *base, int64_t mn, int64_t mn
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled(3d) failed (%d)", (int)r);
-    return CHELIS_CUDA_OK;
-}
-
-// Row-major A itself ([batch][m][lda]) as the K-major operand of the
-// in-kernel split: box 32 (K) x 128 (rows) x 1, rows past m and columns past
-// k read as zeros.  lda, the batch stride and the base are 16-byte aligned.
-int make_raw_kmajor_map(CUtensorMap *map, const float *base, int64_t rows, int64_t k, int64_t ld,
-                        int64_t stride, int64_t batch) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
-                          static_cast<cuuint64_t>(batch)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(stride) * 4};
-    cuuint32_t box[3] = {BK, static_cast<cuuint32_t>(P_ROWS), 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled(raw A) failed (%d)", (int)r);
-    return CHELIS_CUDA_OK;
-}
-
-// Row-major B itself ([batch][k][ldb]) as the MN-major operand: box 32 (MN)
-// x 32 (K) x 1, columns past n and rows past k read as zeros.
-int make_raw_mnmajor_map(CUtensorMap *map, const float *base, int64_t mn, int64_t k, int64_t ld,
-                         int64_t stride, int64_t batch) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[3] = {static_cast<cuuint64_t>(mn), static_cast<cuuint64_t>(k),
-                          static_cast<cuuint64_t>(batch)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(stride) * 4};
-    cuuint32_t box[3] = {MN_BOX, BK, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(CHELIS_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled(raw B) failed (%d)", (int)r);
     return CHELIS_CUDA_OK;
 }
 
@@ -1206,6 +1040,7 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     p.splits = 1;
     p.kb_per_split = p.num_kb;
     p.part = nullptr;
+    p.chunk_kb = CHUNK_KB;
     // Split-K when the tile grid fills the GPU poorly (long-K weight
     // gradients, mid-size squares): pick the split count whose CTA total
     // wastes the fewest SM slots of its last wave (a small penalty per extra
@@ -1258,109 +1093,6 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     return st;
 }
 
-// Row-major A . B on CTA pairs with the split done in shared memory
-// (gemm_pair_split_kernel): no split pre-pass and no scratch but the split-K
-// partials.  Caller checks eligible_split_in_kernel().
-bool eligible_split_in_kernel(int trans_a, int trans_b, int64_t m, const float *a, int64_t lda,
-                              int64_t stride_a, const float *b, int64_t ldb, int64_t stride_b,
-                              int64_t batch) {
-    using namespace tf32x3;
-    if (!g_split_in_kernel.load() || !g_pair_tiles.load() || trans_a || trans_b || m <= BM)
-        return false;
-    if ((lda & 3) || (ldb & 3)) return false;
-    if (batch > 1 && ((stride_a & 3) || (stride_b & 3))) return false;
-    return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
-}
-
-int sgemm_3xtf32_split_in_kernel(int64_t m, int64_t n, int64_t k, const float *a, int64_t lda,
-                                 int64_t stride_a, const float *b, int64_t ldb, int64_t stride_b,
-                                 float *c, int64_t ldc, int64_t stride_c, int64_t batch,
-                                 cudaStream_t s) {
-    using namespace tf32x3;
-    CUtensorMap ma, mb;
-    CHELIS_TRY(make_raw_kmajor_map(&ma, a, m, k, lda, batch > 1 ? stride_a : m * lda, batch));
-    CHELIS_TRY(make_raw_mnmajor_map(&mb, b, n, k, ldb, batch > 1 ? stride_b : k * ldb, batch));
-    Params p;
-    p.m = m;
-    p.n = n;
-    p.batch = batch;
-    p.pairs_m = (m + 2 * P_ROWS - 1) / (2 * P_ROWS);
-    p.tiles_n = (n + BN - 1) / BN;
-    p.num_kb = static_cast<int32_t>((k + BK - 1) / BK);
-    p.a_rows_per_batch = m;
-    p.b_rows_per_batch = n;
-    p.c = c;
-    p.ldc = ldc;
-    p.stride_c = stride_c;
-    p.splits = 1;
-    p.kb_per_split = p.num_kb;
-    p.part = nullptr;
-    if (2 * p.pairs_m * p.tiles_n > INT32_MAX)
-        return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "matmul tile count beyond 2^31");
-    // split-K by the rule of sgemm_3xtf32_main
-    {
-        const int64_t sms = sm_count();
-        const int64_t ctas = 2 * p.pairs_m * p.tiles_n * batch;
-        if (ctas < 2 * sms && p.num_kb >= 8) {
-            double best = -1.0;
-            int best_s = 1;
-            for (int sp = 1; sp <= 16 && p.num_kb / sp >= 4; ++sp) {
-                const int64_t tot = ctas * sp;
-                const double eff = static_cast<double>(tot) /
-                                   static_cast<double>(((tot + sms - 1) / sms) * sms);
-                const double score = eff - 0.02 * (sp - 1);
-                if (score > best + 1e-9) {
-                    best = score;
-                    best_s = sp;
-                }
-            }
-            if (best_s > 1) {
-                p.kb_per_split = (p.num_kb + best_s - 1) / best_s;
-                p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
-            }
-        }
-    }
-    void *part = nullptr;
-    if (p.splits > 1) {
-        CHELIS_TRY(scratch_alloc(&part, static_cast<size_t>(p.splits * batch * m * n) * sizeof(float), s));
-        p.part = static_cast<float *>(part);
-    }
-    static uint64_t done = 0;
-    int st = ensure_smem_attr(reinterpret_cast<const void *>(gemm_pair_split_kernel), P_SMEM_BYTES,
-                              &done, "cudaFuncSetAttribute(gemm_pair_split_kernel)");
-    if (st == CHELIS_CUDA_OK) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * p.pairs_m * p.tiles_n), 1,
-                           static_cast<unsigned>(batch * p.splits));
-        cfg.blockDim = dim3(THREADS);
-        cfg.dynamicSmemBytes = P_SMEM_BYTES;
-        cfg.stream = s;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        st = check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_split_kernel, ma, mb, p),
-                        "cudaLaunchKernelEx(gemm_pair_split_kernel)");
-        if (st == CHELIS_CUDA_OK) {
-            g_launches++;
-            st = check_cuda(cudaGetLastError(), "gemm_pair_split_kernel");
-        }
-    }
-    if (st == CHELIS_CUDA_OK && p.splits > 1) {
-        int64_t blocks = (batch * m * n + 255) / 256;
-        const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
-        if (blocks > cap) blocks = cap;
-        splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-            p.part, p.splits, m, n, batch, c, ldc, stride_c);
-        g_launches++;
-        st = check_cuda(cudaGetLastError(), "splitk_reduce_kernel");
-    }
-    if (part) scratch_free(part, s);
-    return st;
-}
 
 struct GemmPlan {
     OperandPlan a, b;
@@ -1467,9 +1199,6 @@ extern "C" int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n,
                                         stride_b, c, ldc, stride_c, batch, s);
     if (batch * (m > n ? m : n) > INT32_MAX)
         return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "batched matmul rows beyond 2^31");
-    if (eligible_split_in_kernel(trans_a, trans_b, m, a, lda, stride_a, b, ldb, stride_b, batch))
-        return sgemm_3xtf32_split_in_kernel(m, n, k, a, lda, stride_a, b, ldb, stride_b, c, ldc,
-                                            stride_c, batch, s);
     const GemmPlan g = plan_gemm(trans_a, trans_b, m, n, k, lda, ldb, batch);
     void *scratch = nullptr;
     CHELIS_TRY(scratch_alloc(&scratch, g.bytes(), s));
@@ -1489,11 +1218,3 @@ extern "C" int chelis_cuda_set_gemm_pairs(int enable) {
 
 extern "C" int chelis_cuda_get_gemm_pairs(void) { return g_pair_tiles.load(); }
 
-extern "C" int chelis_cuda_set_gemm_split(int in_kernel) {
-    if (in_kernel != 0 && in_kernel != 1)
-        return set_error(CHELIS_CUDA_ERR_DOMAIN, "gemm split mode must be 0 or 1");
-    g_split_in_kernel.store(in_kernel);
-    return CHELIS_CUDA_OK;
-}
-
-extern "C" int chelis_cuda_get_gemm_split(void) { return g_split_in_kernel.load(); }

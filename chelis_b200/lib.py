@@ -97,8 +97,6 @@ SIGNATURES = {
     "chelis_cuda_dgemm": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
     "chelis_cuda_set_gemm_pairs": (c_int, [c_int]),
     "chelis_cuda_get_gemm_pairs": (c_int, []),
-    "chelis_cuda_set_gemm_split": (c_int, [c_int]),
-    "chelis_cuda_get_gemm_split": (c_int, []),
     "chelis_cuda_attention_causal_fwd": (c_int, [c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "chelis_cuda_attention_causal_bwd": (c_int, [c_i64, c_i64, c_i64, c_f32] + [c_vp] * 9),
     "chelis_cuda_sgemm_host": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
@@ -126,6 +124,9 @@ SIGNATURES = {
     "chelis_cuda_mlp_step": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "chelis_cuda_block_workspace_bytes": (c_i64, [ctypes.POINTER(BlockParams)]),
     "chelis_cuda_block_step": (c_int, [ctypes.POINTER(BlockParams), c_vp]),
+    "chelis_cuda_block_timing": (c_int, [c_int]),
+    "chelis_cuda_block_phase_ms": (c_int, [ctypes.POINTER(c_f32), c_i32]),
+    "chelis_cuda_block_phase_name": (ctypes.c_char_p, [c_i32]),
     "chelis_cuda_fused_elementwise": (c_int, [c_i32, c_vp, c_i32, _PP, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_i64), c_i32, c_vp]),
     "chelis_cuda_set_fused_jit": (c_int, [c_int]),
     "chelis_cuda_get_fused_jit": (c_int, []),

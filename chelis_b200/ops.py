@@ -65,19 +65,6 @@ def gemm_pairs(enable: bool):
 
 
 @contextlib.contextmanager
-def gemm_split(in_kernel: bool):
-    """3xTF32 split of row-major operands inside the CTA-pair main kernel or
-    through the split pre-pass; bit-identical results."""
-    lib = L.load()
-    old = lib.chelis_cuda_get_gemm_split()
-    L.call("chelis_cuda_set_gemm_split", int(in_kernel))
-    try:
-        yield
-    finally:
-        L.call("chelis_cuda_set_gemm_split", old)
-
-
-@contextlib.contextmanager
 def fused_jit(enable: bool):
     """FusedElem elementwise groups through per-chain compiled kernels (the
     default) or the ahead-of-time interpreter; the same bits either way."""

@@ -211,14 +211,6 @@ int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
  * up to the f32 accumulation order inside the tensor core.  Process-wide. */
 int chelis_cuda_set_gemm_pairs(int enable);
 int chelis_cuda_get_gemm_pairs(void);
-/* Where the 3xTF32 split happens for row-major products on CTA pairs
- * (trans_a = trans_b = 0, more than 128 rows, lda / ldb and batch strides
- * multiples of 4 floats, 16-byte aligned A and B): 1 = inside the main
- * kernel, on the tiles staged in shared memory; 0 = the split pre-pass into
- * scratch.  Results are bit-identical in both modes.  Process-wide.  No
- * reference counterpart (hipBLAS has no split). */
-int chelis_cuda_set_gemm_split(int in_kernel);
-int chelis_cuda_get_gemm_split(void);
 /* [05-OP-30] matmul on HOST buffers (row-major, same argument meaning as
  * chelis_cuda_sgemm / chelis_cuda_dgemm, all pointers host pointers).  The
  * reference uploads both operands, runs hipBLAS and downloads C in sequence
@@ -492,6 +484,16 @@ int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p);
 /* workspace: device memory of chelis_cuda_block_workspace_bytes bytes, or
  * NULL to take it from the library's stream-ordered pool for the call. */
 int chelis_cuda_block_step(const chelis_block_params *p, void *workspace);
+/* Phase timing of chelis_cuda_block_step (a diagnostic; no counterpart in the
+ * reference).  enable != 0 creates CUDA events on the current device; every
+ * later block step records them on its stream at its 16 phase boundaries
+ * (layer norms, each matmul pair, attention forward and reverse, GELU).
+ * chelis_cuda_block_phase_ms waits for the last step and writes each phase's
+ * milliseconds (0 for phases that step did not run) into ms[0..15] (n >= 16).
+ * Process-wide: use from one host thread at a time. */
+int chelis_cuda_block_timing(int enable);
+int chelis_cuda_block_phase_ms(float *ms, int32_t n);
+const char *chelis_cuda_block_phase_name(int32_t i);
 
 /* =========================================================================
  * Data parallel across the GPUs of one node (new: the reference has no

@@ -252,43 +252,34 @@ def test_sgemm_split_k_matches_oracle(cuda, orc, m, n, k, batch):
         assert _rel_err(c3[i][rows], ref, a3[i][rows], b3[i]) <= 1e-5, i
 
 
-@pytest.mark.parametrize("m,n,k,batch,ld_pad", [
-    (300, 500, 700, 1, 0),       # ragged in m, n and k (zero fill past every edge)
-    (256, 256, 32, 1, 0),        # one pair tile, one k-block
-    (2404, 600, 64, 1, 0),       # tile-order groups, ragged last pair-row
-    (1024, 768, 96, 3, 0),       # batched
-    (256, 256, 8192, 1, 0),      # split-K (partials reduced in split order)
-    (520, 260, 333, 2, 12),      # leading dimensions wider than the rows
+@pytest.mark.parametrize("m,n,k,ta,tb", [
+    (128, 256, 8192, 0, 0),      # single-CTA tiles, 64 accumulator chunks
+    (512, 512, 8192, 0, 0),      # CTA pairs, split-K
+    (8192, 8192, 8192, 0, 0),    # the headline product (sampled rows)
+    (8192, 1024, 4096, 0, 1),    # A . B^T (activation gradients)
+    (1024, 4096, 2048, 1, 0),    # A^T . B (weight gradients, long K)
+    (1000, 700, 3001, 0, 0),     # ragged everywhere, last chunk partial
 ])
-def test_sgemm_split_in_kernel_bit_identical(cuda, orc, m, n, k, batch, ld_pad):
-    """Row-major products split inside the CTA-pair kernel (tiles in shared
-    memory) give the same bits as the split pre-pass, and stay within the
-    3xTF32 bound of the oracle."""
+def test_sgemm_error_grows_like_an_f32_sum(cuda, orc, m, n, k, ta, tb):
+    """The tensor core's accumulator loses accuracy linearly in K when one
+    accumulator spans the whole product (normwise 5.8e-5 at K = 8192).  With
+    fresh 128-deep accumulator chunks folded in f32, the error must stay
+    within normwise 1e-5 of the oracle's tree and within 3x the error of a
+    float32 BLAS product (numpy) on the same rows."""
     import torch
-    a, b = W.gemm_inputs(m, n, k, np.float32, seed=m + 3 * n + k, batch=batch)
-    a3, b3 = a.reshape(batch, m, k), b.reshape(batch, k, n)
-    A = torch.zeros(batch, m, k + ld_pad, device="cuda")
-    B = torch.zeros(batch, k, n + ld_pad, device="cuda")
-    A[:, :, :k] = torch.from_numpy(a3).cuda()
-    B[:, :, :n] = torch.from_numpy(b3).cuda()
-    lda, ldb = k + ld_pad, n + ld_pad
-
-    def run():
-        c = torch.empty(batch, m, n, device="cuda")
-        L.call("chelis_cuda_sgemm", 0, 0, m, n, k, A.data_ptr(), lda, m * lda, B.data_ptr(), ldb,
-               k * ldb, c.data_ptr(), n, m * n, batch)
-        torch.cuda.synchronize()
-        return c
-
-    with cuda.gemm_split(True):
-        c1 = run()
-    with cuda.gemm_split(False):
-        c0 = run()
+    rng = np.random.default_rng(m + n + k)
+    a = (rng.random((k, m) if ta else (m, k), dtype=np.float32) * 2 - 1)
+    b = (rng.random((n, k) if tb else (k, n), dtype=np.float32) * 2 - 1)
+    c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), ta, tb)
+    torch.cuda.synchronize()
     cuda.device_status()
-    g1 = c1.cpu().numpy().reshape(batch, m, n)
-    g0 = c0.cpu().numpy().reshape(batch, m, n)
-    assert (g1.view(np.uint32) == g0.view(np.uint32)).all()
-    rows = slice(0, min(m, 96))
-    for i in range(batch):
-        ref = orc.gemm(a3[i][rows], b3[i])
-        assert _rel_err(g1[i][rows], ref, a3[i][rows], b3[i]) <= 1e-5, i
+    rows = np.arange(m) if m <= 1024 else np.linspace(0, m - 1, 96).astype(np.int64)
+    A = np.ascontiguousarray(a.T if ta else a)[rows]
+    B = np.ascontiguousarray(b.T if tb else b)
+    ref = orc.gemm(A, B).astype(np.float64)
+    got = c.cpu().numpy()[rows].astype(np.float64)
+    blas = (A @ B).astype(np.float64)
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    err_blas = np.abs(blas - ref).max() / np.abs(ref).max()
+    assert err <= 1e-5, (err, err_blas)
+    assert err <= max(3.0 * err_blas, 2e-6), (err, err_blas)
