@@ -1,29 +1,36 @@
 """Benchmark of the Chelis B200 backend (one JSON line on rank 0).
 
-Headline workload (its largest size): C = A.B, row-major,
-M = N = K = 8192, f32, A and B ~ U(-1, 1) (seed 1), through the library's
-matmul entry (3xTF32 on tcgen05: split pre-pass + tensor-core main kernel).
-Metric: TFLOP/s of useful work (2 N^3 per product), whole job.
+Headline workload: the pre-LN transformer block, forward
+and reverse mode, f32 -- batch 8, sequence 2048, d_model 1024, 16 heads of
+64, causal softmax attention, GELU MLP 1024 -> 4096 -> 1024, weights
+Xavier-uniform and activations N(0, 1) from seed 3 -- data-parallel over
+the batch: with --gpus N the global batch of 8 is split across the N ranks
+(strong scaling) and the weight gradients (12.6 M f32, 50.3 MB) are summed
+across ranks by the library's NCCL communicator (chelis_cuda_dp_*) every
+step.  Metric: samples per second of the whole job.
 
   value     device-resident inputs, CUDA-event timed over exactly --steps
-            products after --warmup untimed ones (inputs of 512 MiB exceed
-            the 126 MB L2, so no flush is needed), max over ranks.
-  e2e       the same product from pinned host buffers through
-            chelis_cuda_sgemm_host (ops.matmul_host): H2D of A and B, the
-            product and D2H of C inside every timed step, the copies
-            overlapped with the GEMM panels on separate streams.
-  roofline  the tensor-core main kernel alone on pre-split operands, timed
-            with CUDA events on its stream: pipe FLOPs (3 tf32 MMAs per
-            product term) per launch / mean launch time, against the tf32
-            tensor peak = measured dense bf16 / 2.
-  extra     the other configurations (f64 GEMM, batched GEMM, fused chain
-            forward / adjoint, vmap covariance, MLP step) at one GPU.
-  --gpus N  (torchrun) every rank multiplies its own 8192^3 pair: replicas,
-            weak scaling; there is no collective on this path.
+            steps after --warmup untimed ones, max over ranks.  The working
+            set (weights, gradients and the per-rank activations) exceeds the
+            126 MB L2, so no flush is needed.
+  e2e       the same step from pinned host buffers: this rank's x and dy
+            copied to the device, the block step, the all-reduce, and the
+            reduced gradients plus dx copied back, inside every timed step.
+  roofline  the phase group that takes the most time in the step (the
+            library's phase timer: CUDA events inside chelis_cuda_block_step),
+            its algorithmic FLOPs (useful f32 FLOPs; each runs as 3 tf32 MMA
+            terms) over its measured time, against the measured tf32 tensor
+            peak / 3 (cuBLAS TF32 GEMM timed in this run).
+  cpu_baseline  the oracle (the reference C lane's algorithm restated in C,
+            -O2 -ffp-contract=off, OpenMP on every host core) on one sample
+            of the batch.
+  extra     the other configurations: f32 / f64 GEMM sweeps with pipe
+            fractions, the fused chain (config 3), the fused groups, the MLP
+            step (config 1), the covariance vmap (config 5), the batched
+            GEMM (2b), each with a roofline and, at one GPU, a CPU baseline.
 
-`--impl reference` times the reference C lane's algorithm (the oracle port:
-canonical tree over k, -O2 -ffp-contract=off, OpenMP on every host core) on
-a bounded sample of output rows of the same product.
+`--impl reference` times the reference C lane's algorithm (the oracle) on
+the same workload, one sample of the batch per step, with every host core.
 """
 from __future__ import annotations
 
@@ -39,9 +46,12 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_HEADLINE = 8192
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
+METRIC = "block_fwd_bwd_samples_per_s"
+UNIT = "samples/s"
+GLOBAL_BATCH = 8
+DATA = "synthetic (Xavier-uniform weights, N(0,1) activations and cotangent, seed 3)"
 
 
 def load_peaks():
@@ -61,6 +71,30 @@ def load_traffic(name):
             return json.load(f).get(name)
     except Exception:
         return None
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def use_all_host_cores():
+    """OpenMP threads for the oracle: every host core this process may use
+    (set outright: torchrun sets OMP_NUM_THREADS=1 for its ranks)."""
+    n = host_cores()
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    return n
+
+
+def block_config(world):
+    """The workload description both arms print (identical dicts)."""
+    return {"workload": "config 4: transformer block fwd+bwd f32 (pre-LN, causal softmax "
+                        "attention, GELU MLP), data-parallel over the batch",
+            "global_batch": GLOBAL_BATCH, "seq_len": 2048, "d_model": 1024, "heads": 16,
+            "head_dim": 64, "d_ff": 4096, "parallelism": f"dp{world}",
+            "l2": "working set > 126 MB L2 (weights + gradients 100.6 MB + activations), no flush"}
 
 
 # ---------------------------------------------------------------- clocks
@@ -173,26 +207,122 @@ def time_region(fn, steps, world):
     return max_over_ranks(start.elapsed_time(stop), world)
 
 
-# ---------------------------------------------------------------- workloads
+def timed(fn, steps, warm=3):
+    for _ in range(warm):
+        fn()
+    return time_region(fn, steps, 1) / steps
 
-def bench_gemm_headline(args, world, rank, peaks):
+
+def measure_pipe_peaks():
+    """Denominators for the tensor and FP64 pipes, measured in this run with
+    cuBLAS through torch (8192^3, best of a few): tf32 tensor GEMM, f64 GEMM
+    (DMMA), and f32 GEMM with tf32 off."""
     import torch
+    n = 8192
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for name, dt, tf32, reps in (("tf32_tflops", torch.float32, True, 5),
+                                 ("fp32_tflops", torch.float32, False, 3),
+                                 ("fp64_tflops", torch.float64, False, 3)):
+        a = torch.rand((n, n), generator=g, device="cuda", dtype=dt)
+        b = torch.rand((n, n), generator=g, device="cuda", dtype=dt)
+        old = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+        try:
+            for _ in range(2):
+                torch.matmul(a, b)
+            best = None
+            for _ in range(reps):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                torch.matmul(a, b)
+                e.record()
+                torch.cuda.synchronize()
+                ms = s.elapsed_time(e)
+                best = ms if best is None else min(best, ms)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = old
+        out[name] = round(2 * n ** 3 / best / 1e9, 1)
+        del a, b
+    torch.cuda.empty_cache()
+    out["how"] = "cuBLAS via torch.matmul 8192^3, best of 3-5 (CUDA events), this run"
+    return out
+
+
+# ---------------------------------------------------------------- config 4 (headline)
+
+def block_flops(local_batch, S=2048, D=1024, H=16, F=4096):
+    """Useful FLOPs of one block step (forward + VJP) on `local_batch`
+    samples, by phase group: matmuls 3 x (2 S D (4D + 2F)) per sample; causal
+    attention 2 S^2 D forward, 4 S^2 D reverse."""
+    Dh = D // H
+    gemm = 3 * 2 * local_batch * S * D * (4 * D + 2 * F)
+    att_f = local_batch * H * 2 * S * S * Dh
+    att_b = local_batch * H * 4 * S * S * Dh
+    return {"gemm": gemm, "attention_fwd": att_f, "attention_bwd": att_b,
+            "total": gemm + att_f + att_b}
+
+
+def phase_group(name):
+    if name.startswith("gemm"):
+        return "gemm"
+    if name.startswith("attention"):
+        return name
+    return "rows"
+
+
+def block_phases(step, steps=3):
+    """Per-phase ms of the block step (library phase timer), mean of `steps`."""
+    import ctypes
     from chelis_b200 import lib as L
-    from chelis_b200 import ops, workloads as W
-    n = args.n
-    a, b = W.torch_gemm_inputs(n, n, n, torch.float32, seed=1 + rank)
-    c = torch.empty((n, n), dtype=torch.float32, device="cuda")
-    flops = 2.0 * n ** 3
+    lib = L.load()
+    L.call("chelis_cuda_block_timing", 1)
+    acc = [0.0] * 16
+    try:
+        for _ in range(steps):
+            step()
+            ms = (ctypes.c_float * 16)()
+            L.call("chelis_cuda_block_phase_ms", ms, 16)
+            for i in range(16):
+                acc[i] += ms[i] / steps
+    finally:
+        L.call("chelis_cuda_block_timing", 0)
+    names = [lib.chelis_cuda_block_phase_name(i).decode() for i in range(16)]
+    phases = {n: round(v, 4) for n, v in zip(names, acc)}
+    groups = {}
+    for n, v in zip(names, acc):
+        g = phase_group(n)
+        groups[g] = round(groups.get(g, 0.0) + v, 4)
+    return phases, groups
+
+
+def bench_block_headline(args, world, rank, peaks, pipes):
+    import torch
+    from chelis_b200 import dp, ops, workloads as W
+    shape = dict(W.BLOCK_SHAPE)
+    heads = shape["heads"]
+    a, b = dp.shard(GLOBAL_BATCH, world, rank)
+    local = b - a
+    x_all, dy_all, w = W.torch_block_inputs(seed=3, **shape)
+    x = x_all[a:b].contiguous()
+    dy = dy_all[a:b].contiguous()
+    del x_all, dy_all
+    names = list(ops.BLOCK_WEIGHTS)
+    grads = dp.FlatGrads({"d" + k: tuple(w[k].shape) for k in names}, "cuda")
+    res = {"y": torch.empty_like(x), "dx": torch.empty_like(x)}
+    res.update({k: grads[k] for k in grads.views})
+    ws = ops.block_workspace(x, w, heads)
 
     def step():
-        ops.matmul(a, b, out=c)
+        ops.block_step(x, w, heads, 1e-5, dy, workspace=ws, out=res)
+        dp.allreduce_sum(grads.flat, world)
 
     for _ in range(args.warmup):
         step()
     ops.device_status()
     with ClockSampler(torch.cuda.current_device()) as clk:
         # the sampler needs ~1 s to start; keep the GPU busy with untimed
-        # products until it reports, then time exactly args.steps
+        # steps until it reports, then time exactly args.steps
         t0 = time.time()
         while not clk.lines and time.time() - t0 < 5.0:
             step()
@@ -201,13 +331,131 @@ def bench_gemm_headline(args, world, rank, peaks):
         ms = time_region(step, args.steps, world)
         launches = ops.launch_count() - l0
     ops.device_status()
-    value = world * flops * args.steps / (ms * 1e-3) / 1e12
+    ms_step = ms / args.steps
+    value = GLOBAL_BATCH * args.steps / (ms * 1e-3)
 
-    # roofline: the tcgen05 main kernel alone on pre-split operands (A K-major,
-    # row-major B MN-major: the layouts matmul itself picks)
+    # where the step's time goes (phase timer; compute only) and the
+    # gradient all-reduce alone
+    phases, groups = block_phases(lambda: ops.block_step(x, w, heads, 1e-5, dy, workspace=ws,
+                                                         out=res))
+    ar_ms = 0.0
+    if world > 1:
+        for _ in range(3):
+            dp.allreduce_sum(grads.flat, world)
+        ar_ms = time_region(lambda: dp.allreduce_sum(grads.flat, world), 10, world) / 10
+    fl = block_flops(local)
+    dom = max(("gemm", "attention_fwd", "attention_bwd"), key=lambda g: groups.get(g, 0.0))
+    dom_ms = groups[dom]
+    achieved = fl[dom] / (dom_ms * 1e-3) / 1e12
+    f32_peak = pipes["tf32_tflops"] / 3.0
+    roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(f32_peak, 2),
+                "unit": "TFLOP/s", "frac": round(achieved / f32_peak, 4),
+                "traffic": load_traffic("block_" + dom),
+                "kernel": {"gemm": "tf32x3 matmuls of the step (split pre-pass + "
+                                   "tf32x3::gemm_pair_kernel, tcgen05 cta_group::2)",
+                           "attention_fwd": "attn::fwd_kernel (tcgen05, scores in TMEM)",
+                           "attention_bwd": "attn::dkv_kernel + attn::dq_kernel"}[dom],
+                "group_ms_per_step": dom_ms, "algorithmic_flop_per_step": fl[dom],
+                "peak_source": "measured cuBLAS TF32 GEMM in this run / 3 (an f32 product "
+                               "term is 3 tf32 MMA terms)"}
+    step_frac = fl["total"] / (ms_step * 1e-3) / 1e12 / f32_peak
+
+    # e2e: pinned host buffers every step
+    hx = x.cpu().pin_memory()
+    hdy = dy.cpu().pin_memory()
+    hg = torch.empty(grads.flat.numel(), dtype=torch.float32).pin_memory()
+    hdx = torch.empty(x.shape, dtype=torch.float32).pin_memory()
+    xd, dyd = torch.empty_like(x), torch.empty_like(dy)
+
+    def e2e_step():
+        xd.copy_(hx, non_blocking=True)
+        dyd.copy_(hdy, non_blocking=True)
+        ops.block_step(xd, w, heads, 1e-5, dyd, workspace=ws, out=res)
+        dp.allreduce_sum(grads.flat, world)
+        hg.copy_(grads.flat, non_blocking=True)
+        hdx.copy_(res["dx"], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e_steps = max(3, args.steps // 2)
+    ems = time_region(e2e_step, e_steps, world)
+    e2e = {"value": round(GLOBAL_BATCH * e_steps / (ems * 1e-3), 2), "unit": UNIT,
+           "h2d_bytes_per_step": 2 * x.numel() * 4,
+           "d2h_bytes_per_step": grads.flat.numel() * 4 + x.numel() * 4,
+           "what": "per rank: x and dy shard H2D; block step; gradient all-reduce; reduced "
+                   "gradients and dx D2H"}
+    return dict(value=value, ms_per_step=ms_step, launches=launches, clocks=clk.summary(),
+                roofline=roofline, e2e=e2e,
+                breakdown={"phase_ms": phases, "group_ms": groups,
+                           "compute_ms": round(sum(groups.values()), 4),
+                           "allreduce_alone_ms": round(ar_ms, 4),
+                           "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1),
+                           "per_rank_batch": local,
+                           "step_useful_tflops": round(fl["total"] / (ms_step * 1e-3) / 1e12, 1),
+                           "step_frac_of_f32_tensor_peak": round(step_frac, 4)})
+
+
+def cpu_block_sample():
+    """Oracle block step (forward + VJP) on one sample; (samples/s, s, cores)."""
+    import numpy as np
+    from chelis_b200 import workloads as W
+    cores = use_all_host_cores()
+    from oracle import oracle as O
+    O.lib()
+    shape = dict(W.BLOCK_SHAPE, batch=1)
+    x, dy, w = W.block_inputs(seed=3, **shape)
+    t0 = time.perf_counter()
+    O.block_step(x, w, shape["heads"], np.float32(1e-5), dy)
+    dt = time.perf_counter() - t0
+    return 1.0 / dt, dt, cores
+
+
+# ---------------------------------------------------------------- extras
+
+def cpu_gemm_sample(n, budget_s, seed=1):
+    """Oracle on a bounded sample of output rows of the n^3 f32 product;
+    returns (TFLOP/s, rows, seconds, threads)."""
+    import numpy as np
+    from chelis_b200 import workloads as W
+    threads = use_all_host_cores()
+    from oracle import oracle as O
+    a, b = W.gemm_inputs(n, n, n, np.float32, seed=seed)
+    O.lib()
+    t0 = time.perf_counter()
+    O.gemm(a[:threads], b)
+    dt = time.perf_counter() - t0
+    per_row = dt / threads
+    rows = int(max(threads, min(n, budget_s / max(per_row, 1e-9))))
+    rows = (rows // threads) * threads or threads
+    t0 = time.perf_counter()
+    O.gemm(a[:rows], b)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * n * n / dt / 1e12, rows, dt, threads
+
+
+def bench_gemm(args, peaks, pipes, with_cpu):
+    """Config 2: the f32 sweep (3xTF32) incl. 8192^3 with its main-kernel
+    roofline and host-buffer e2e, and the f64 sweep (DMMA)."""
+    import torch
+    from chelis_b200 import lib as L
+    from chelis_b200 import ops, workloads as W
+    out = {}
+    f32_peak = pipes["tf32_tflops"] / 3.0
+    sweep = {}
+    for n in (512, 1024, 2048, 4096, 8192):
+        a, b = W.torch_gemm_inputs(n, n, n, torch.float32, seed=1)
+        c = torch.empty((n, n), dtype=torch.float32, device="cuda")
+        ms = timed(lambda: ops.matmul(a, b, out=c), 20 if n < 8192 else 10)
+        t = 2 * n ** 3 / ms / 1e9
+        sweep[str(n)] = {"tflops": round(t, 2), "ms": round(ms, 4),
+                         "frac_f32_tensor_peak": round(t / f32_peak, 4)}
+    out["gemm_f32_sweep"] = sweep
+    n = 8192
+    # roofline of the main kernel alone on pre-split operands
     kp = (n + 31) // 32 * 32
     ahi = torch.empty((n, kp), dtype=torch.float32, device="cuda")
     alo, bhi, blo = torch.empty_like(ahi), torch.empty_like(ahi), torch.empty_like(ahi)
+    ops._prepare(a)
     L.call("chelis_cuda_tf32x3_split", 0, 0, n, n, a.data_ptr(), n, 0, 1, ahi.data_ptr(), alo.data_ptr())
     L.call("chelis_cuda_tf32x3_split", 1, 1, n, n, b.data_ptr(), n, 0, 1, bhi.data_ptr(), blo.data_ptr())
 
@@ -215,69 +463,51 @@ def bench_gemm_headline(args, world, rank, peaks):
         L.call("chelis_cuda_sgemm_tf32x3_presplit", n, n, n, 1, 0, ahi.data_ptr(), alo.data_ptr(),
                1, bhi.data_ptr(), blo.data_ptr(), c.data_ptr(), n, 0)
 
-    for _ in range(3):
-        main_only()
-    kms = time_region(main_only, args.steps, 1) / args.steps
-    pipe = 3.0 * flops / (kms * 1e-3) / 1e12
-    tf32_peak = peaks["bf16"] / 2.0
+    kms = timed(main_only, 10)
+    ach = 2 * n ** 3 / (kms * 1e-3) / 1e12
     del ahi, alo, bhi, blo
-
-    # e2e: pinned host buffers through chelis_cuda_sgemm_host every step
-    ha = a.cpu().pin_memory()
-    hb = b.cpu().pin_memory()
+    ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
     hc = torch.empty((n, n), dtype=torch.float32).pin_memory()
+    ems = timed(lambda: ops.matmul_host(ha, hb, out=hc), 3, 1)
+    out["gemm_f32_8192"] = {
+        "tflops": sweep["8192"]["tflops"], "ms": sweep["8192"]["ms"],
+        "roofline": {"bound": "tensor", "achieved": round(ach, 2), "peak": round(f32_peak, 2),
+                     "unit": "TFLOP/s", "frac": round(ach / f32_peak, 4),
+                     "traffic": load_traffic("gemm_tf32x3_8192"), "kernel_ms": round(kms, 4),
+                     "kernel": "tf32x3::gemm_pair_kernel (tcgen05 cta_group::2 kind::tf32)",
+                     "peak_source": "measured cuBLAS TF32 / 3"},
+        "e2e": {"value": round(2 * n ** 3 / ems / 1e9, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 2 * n * n * 4, "d2h_bytes_per_step": n * n * 4}}
+    del a, b, c, ha, hb, hc
+    torch.cuda.empty_cache()
+    if with_cpu:
+        v, rows, dt, threads = cpu_gemm_sample(n, 8.0)
+        out["gemm_f32_8192"]["cpu_baseline"] = {
+            "value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {n} output rows of the {n}^3 f32 product ({dt:.1f} s)"}
+    f64 = {}
+    for n in (512, 1024, 2048, 4096, 8192):
+        a, b = W.torch_gemm_inputs(n, n, n, torch.float64, seed=1)
+        c = torch.empty((n, n), dtype=torch.float64, device="cuda")
+        ms = timed(lambda: ops.matmul(a, b, out=c), 10 if n < 8192 else 3, 2)
+        t = 2 * n ** 3 / ms / 1e9
+        f64[str(n)] = {"tflops": round(t, 2), "ms": round(ms, 4),
+                       "frac_fp64_peak": round(t / pipes["fp64_tflops"], 4)}
+        del a, b, c
+    out["gemm_f64_sweep"] = dict(f64, peak_source="measured cuBLAS DGEMM 8192^3 in this run",
+                                 kernel="dmma::dgemm_async_kernel (mma.sync m16n8k4 f64)")
+    torch.cuda.empty_cache()
+    return out
 
-    def e2e_step():
-        # the user-facing host-buffer call: uploads, GEMM panels and
-        # read-back overlap inside it; returns with C in host memory
-        ops.matmul_host(ha, hb, out=hc)
 
-    for _ in range(2):
-        e2e_step()
-    ems = time_region(e2e_step, max(2, args.steps // 2), world)
-    e2e_value = world * flops * max(2, args.steps // 2) / (ems * 1e-3) / 1e12
-    return dict(
-        value=value, ms_per_step=ms / args.steps, launches=launches, clocks=clk.summary(),
-        roofline={"bound": "tensor", "achieved": round(pipe, 2), "peak": tf32_peak,
-                  "unit": "TFLOP/s", "frac": round(pipe / tf32_peak, 4),
-                  "traffic": load_traffic("gemm_tf32x3_8192"),
-                  "kernel": "tf32x3::gemm_pair_kernel (tcgen05.mma cta_group::2 kind::tf32, 3 MMAs per product term)",
-                  "kernel_ms": round(kms, 4),
-                  "peak_source": f"{peaks['source']} dense bf16 / 2 (tf32 issues at half the f16 rate)"},
-        e2e={"value": round(e2e_value, 2), "unit": "TFLOP/s",
-             "h2d_bytes_per_step": 2 * n * n * 4, "d2h_bytes_per_step": n * n * 4},
-    )
-
-
-def bench_extras(args, peaks):
-    """The other configurations, one GPU, short timed loops (CUDA events)."""
+def bench_rows(args, peaks, with_cpu):
+    """Config 3 (fused chain fwd / adjoint), the fused groups alone and
+    generic FusedElem groups on [16384, 4096] f32; config 1 (MLP step)."""
+    import numpy as np
     import torch
     from chelis_b200 import ops, workloads as W
     out = {}
     hbm = peaks["hbm"]
-
-    def timed(fn, steps, warm=3):
-        for _ in range(warm):
-            fn()
-        return time_region(fn, steps, 1) / steps
-
-    # f64 GEMM 8192^3 on DMMA
-    n = 8192
-    a, b = W.torch_gemm_inputs(n, n, n, torch.float64, seed=1)
-    c = torch.empty((n, n), dtype=torch.float64, device="cuda")
-    ms = timed(lambda: ops.matmul(a, b, out=c), 3, 1)
-    out["gemm_f64_8192"] = {"tflops": round(2 * n ** 3 / ms / 1e9, 2), "ms": round(ms, 3)}
-    del a, b, c
-    # f32 GEMM sweep (smaller sizes)
-    sweep = {}
-    for n in (512, 1024, 2048, 4096):
-        a, b = W.torch_gemm_inputs(n, n, n, torch.float32, seed=1)
-        c = torch.empty((n, n), dtype=torch.float32, device="cuda")
-        ms = timed(lambda: ops.matmul(a, b, out=c), 10)
-        sweep[str(n)] = round(2 * n ** 3 / ms / 1e9, 2)
-    out["gemm_f32_sweep_tflops"] = sweep
-    del a, b, c
-    # fused chain fwd / adjoint
     x, g, be = W.torch_chain_inputs()
     rows, hidden = x.shape
     state = {}
@@ -288,14 +518,41 @@ def bench_extras(args, peaks):
     fms = timed(fwd, 10)
     bms = timed(lambda: ops.chain_bwd_saved(x, g, be, 1e-5, 0.1, state["saved"]), 10)
     saved = state["saved"].numel() * 4
+    # algorithmic bytes: X read + gamma, beta + row sums (forward); X read, dX
+    # written, dgamma / dbeta (adjoint); the saved state both ways
     fbytes = rows * hidden * 4 + 2 * hidden * 4 + rows * 4 + saved
     bbytes = 2 * rows * hidden * 4 + 4 * hidden * 4 + saved
-    out["chain_fwd"] = {"gbs": round(fbytes / fms / 1e6, 1), "ms": round(fms, 4),
-                        "frac_hbm": round(fbytes / fms / 1e6 / hbm, 3)}
-    out["chain_bwd"] = {"gbs": round(bbytes / bms / 1e6, 1), "ms": round(bms, 4),
-                        "frac_hbm": round(bbytes / bms / 1e6 / hbm, 3)}
-    # the fused groups one at a time on the same [16384, 4096] f32 matrix
-    # (algorithmic bytes: each input read once, each output written once)
+    chain = {"fwd": {"gbs": round(fbytes / fms / 1e6, 1), "ms": round(fms, 4),
+                     "roofline": {"bound": "hbm", "achieved": round(fbytes / fms / 1e6, 1),
+                                  "peak": hbm, "unit": "GB/s",
+                                  "frac": round(fbytes / fms / 1e6 / hbm, 4),
+                                  "traffic": load_traffic("chain_fwd_16384x4096")}},
+             "bwd": {"gbs": round(bbytes / bms / 1e6, 1), "ms": round(bms, 4),
+                     "roofline": {"bound": "hbm", "achieved": round(bbytes / bms / 1e6, 1),
+                                  "peak": hbm, "unit": "GB/s",
+                                  "frac": round(bbytes / bms / 1e6 / hbm, 4),
+                                  "traffic": load_traffic("chain_bwd_16384x4096")}}}
+    if with_cpu:
+        cores = use_all_host_cores()
+        from oracle import oracle as O
+        O.lib()
+        xs, gs, bs = (np.ascontiguousarray(t[:512].cpu().numpy()) if t.dim() == 2 else
+                      t.cpu().numpy() for t in (x, g, be))
+        t0 = time.perf_counter()
+        O.chain_fwd(xs, gs, bs, np.float32(1e-5), 42, np.float32(0.1))
+        dt = time.perf_counter() - t0
+        sb = 512 * hidden * 4 + 2 * hidden * 4 + 512 * 4
+        chain["fwd"]["cpu_baseline"] = {"value": round(sb / dt / 1e9, 3), "unit": "GB/s",
+                                        "cores": cores, "kind": "port",
+                                        "sample": f"512 of {rows} rows ({dt:.2f} s)"}
+        t0 = time.perf_counter()
+        O.chain_bwd(xs, gs, bs, np.float32(1e-5), 42, np.float32(0.1))
+        dt = time.perf_counter() - t0
+        sb = 2 * 512 * hidden * 4 + 4 * hidden * 4
+        chain["bwd"]["cpu_baseline"] = {"value": round(sb / dt / 1e9, 3), "unit": "GB/s",
+                                        "cores": cores, "kind": "port",
+                                        "sample": f"512 of {rows} rows ({dt:.2f} s)"}
+    out["chain_16384x4096"] = chain
     y = torch.softmax(x, -1)
     nb = rows * hidden * 4
     groups = {
@@ -313,9 +570,6 @@ def bench_extras(args, peaks):
         fused[name] = {"ms": round(ms_g, 4), "gbs": round(nbytes / ms_g / 1e6, 1),
                        "frac_hbm": round(nbytes / ms_g / 1e6 / hbm, 3)}
     out["fused_groups_16384x4096"] = fused
-    # generic FusedElem groups (chelis_cuda_fused_elementwise / _reduce) on
-    # the same matrix: broadcast affine, a unary chain, a GELU-like chain of
-    # 9 steps, and square-sums along each axis and over the whole tensor
     from chelis_b200 import fused as F
     consts = [torch.tensor(v, device="cuda") for v in (0.044715, 0.7978845608, 0.5, 1.0)]
     gelu = ("mul x0 x0; mul v0 x0; mul v1 x1; add v2 x0; mul v3 x2; tanh v4; "
@@ -341,32 +595,46 @@ def bench_extras(args, peaks):
                          "frac_hbm": round(nbytes / ms_g / 1e6 / hbm, 3)}
     out["fused_elem_16384x4096"] = generic
     del x, g, be, state, y, flat
-    # MLP step
+    # config 1: MLP step (latency-bound: 1.05e8 FLOP in a handful of launches)
     x, labels, w1, b1, w2, b2 = W.torch_mlp_inputs()
-    ms = timed(lambda: ops.mlp_step(x, labels, w1, b1, w2, b2), 20)
-    out["mlp_step"] = {"us_per_step": round(ms * 1e3, 1)}
+    l0 = ops.launch_count()
+    ops.mlp_step(x, labels, w1, b1, w2, b2)
+    launches = ops.launch_count() - l0
+    ms = timed(lambda: ops.mlp_step(x, labels, w1, b1, w2, b2), 50)
+    flop = 2 * 128 * (784 * 256 + 256 * 10) + 2 * 128 * (784 * 256 + 2 * 256 * 10)
+    mlp = {"us_per_step": round(ms * 1e3, 1), "launches_per_step": launches,
+           "roofline": {"bound": "latency", "achieved": round(flop / (ms * 1e-3) / 1e12, 3),
+                        "unit": "TFLOP/s", "flop_per_step": flop,
+                        "note": "1.05e8 FLOP over launches_per_step dependent kernels"}}
+    if with_cpu:
+        cores = use_all_host_cores()
+        from oracle import oracle as O
+        xs, ls, a1, c1, a2, c2 = (t.cpu().numpy() for t in (x, labels, w1, b1, w2, b2))
+        O.mlp_step(xs, ls, a1, c1, a2, c2)
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            O.mlp_step(xs, ls, a1, c1, a2, c2)
+        dt = (time.perf_counter() - t0) / reps
+        mlp["cpu_baseline"] = {"value": round(dt * 1e6, 1), "unit": "us/step", "cores": cores,
+                               "kind": "port", "sample": f"the full step, mean of {reps}"}
+    out["mlp_step"] = mlp
     return out
 
 
-def bench_sharded(args, world, rank, peaks):
-    """The configurations that shard across GPUs, at every N (max over ranks):
-    config 4 data-parallel (one NCCL all-reduce of the flat gradient buffer
-    per step, through the library's own communicator, chelis_cuda_dp_*),
-    both as the global batch of 8 split across ranks (strong) and
-    as 8 samples per rank (weak), config 5 and the batched GEMM of config 2
+def bench_sharded(args, world, rank, peaks, pipes, with_cpu):
+    """Configs that shard across GPUs, at every N (max over ranks): config 4
+    weak (8 samples per rank), config 5 and the batched GEMM of config 2
     along their vmap axis (no collective)."""
+    import numpy as np
     import torch
     from chelis_b200 import dp, ops, workloads as W
     out = {}
     shape = dict(W.BLOCK_SHAPE)
     S, D, F = shape["seq"], shape["d_model"], shape["d_ff"]
-    per_sample = 3 * (2 * S * 3 * D * D + 2 * S * S * D + 2 * S * D * D + 4 * S * D * F)
-
-    def block_dp(local_batch, global_batch):
-        # config 4: transformer block fwd + VJP on this rank's samples, then one
-        # NCCL all-reduce of the flat gradient buffer
-        local = dict(shape, batch=local_batch)
-        x, dy, w = W.torch_block_inputs(seed=3 + rank, **local)
+    per_sample = block_flops(1, S, D, shape["heads"], F)["total"]
+    if world > 1:
+        x, dy, w = W.torch_block_inputs(seed=3 + rank, **shape)
         names = list(ops.BLOCK_WEIGHTS)
         grads = dp.FlatGrads({"d" + k: tuple(w[k].shape) for k in names}, "cuda")
         res = {"y": torch.empty_like(x), "dx": torch.empty_like(x)}
@@ -379,96 +647,99 @@ def bench_sharded(args, world, rank, peaks):
 
         for _ in range(3):
             step()
-        steps = 5
-        ms = time_region(step, steps, world) / steps
-        return {"samples_per_s": round(global_batch / ms * 1e3, 1), "ms_per_step": round(ms, 3),
-                "per_rank_batch": local_batch,
-                "tflops": round(global_batch * per_sample / ms / 1e9, 1),
-                "flop_per_sample": per_sample,
-                "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1)}
-
-    if world > 1:
-        dp.native_init(world, rank)
-    # strong: the global batch of 8 split across ranks
-    a, b = dp.shard(shape["batch"], world, rank)
-    out["block_dp"] = dict(block_dp(b - a, shape["batch"]), scaling="strong (global batch 8)")
-    # weak: 8 samples per rank (global batch 8 N)
-    if world == 1:
-        out["block_dp_weak"] = dict(out["block_dp"], scaling="weak (8 samples per rank)")
-    else:
-        out["block_dp_weak"] = dict(block_dp(shape["batch"], shape["batch"] * world),
-                                    scaling="weak (8 samples per rank)")
-        torch.cuda.synchronize()
-        dp.native_finalize()
+        ms = time_region(step, 5, world) / 5
+        out["block_dp_weak"] = {"samples_per_s": round(8 * world / ms * 1e3, 1),
+                                "ms_per_step": round(ms, 3), "per_rank_batch": 8,
+                                "scaling": "weak (8 samples per rank)",
+                                "tflops": round(8 * world * per_sample / ms / 1e9, 1)}
+        del x, dy, w, grads, res, ws
+        torch.cuda.empty_cache()
     # config 5: covariance / risk, 65536 portfolios split across ranks
-    cnt = W.PORTFOLIO_SHAPE["count"]
-    a, b = dp.shard(cnt, world, rank)
-    r, wv = W.torch_portfolio_inputs(count=b - a, seed=4 + rank)
+    cnt, T, A = (W.PORTFOLIO_SHAPE[k] for k in ("count", "t", "a"))
+    lo, hi = dp.shard(cnt, world, rank)
+    r, wv = W.torch_portfolio_inputs(count=hi - lo, seed=4 + rank)
     for _ in range(2):
         ops.portfolio(r, wv)
     ms = time_region(lambda: ops.portfolio(r, wv), 3, world) / 3
-    out["portfolio_vmap"] = {"portfolios_per_s": round(cnt / ms * 1e3, 1), "ms": round(ms, 3),
-                             "fp64_tflops": round(cnt * 2.10e6 / ms / 1e9, 2),
-                             "scaling": "strong (65536 portfolios)"}
+    flop = cnt * 2.10e6
+    nbytes = cnt * (T * A * 8 + A * 8 + A * A * 8 + 8 + T * 8)
+    fp64 = flop / ms / 1e9
+    gbs = nbytes / ms / 1e6
+    port = {"portfolios_per_s": round(cnt / ms * 1e3, 1), "ms": round(ms, 3),
+            "fp64_tflops": round(fp64, 2), "scaling": "strong (65536 portfolios)",
+            "roofline": {"bound": "fp64", "achieved": round(fp64, 2),
+                         "peak": pipes["fp64_tflops"], "unit": "TFLOP/s",
+                         "frac": round(fp64 / pipes["fp64_tflops"], 4),
+                         "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm"], 4),
+                         "traffic": load_traffic("portfolio_4096"),
+                         "algorithmic": "2.10 MFLOP and 164 KB per portfolio"}}
+    if with_cpu and world == 1:
+        cores = use_all_host_cores()
+        from oracle import oracle as O
+        rs, wsn = W.portfolio_inputs(count=512, seed=4)
+        O.lib()
+        t0 = time.perf_counter()
+        O.portfolio(rs, wsn)
+        dt = time.perf_counter() - t0
+        port["cpu_baseline"] = {"value": round(512 / dt, 1), "unit": "portfolios/s",
+                                "cores": cores, "kind": "port",
+                                "sample": f"512 of {cnt} portfolios ({dt:.2f} s)"}
+    out["portfolio_vmap"] = port
     del r, wv
     # config 2b: 256 x [512 x 512] . [512 x 512] f32, batch split across ranks
-    a, b = dp.shard(256, world, rank)
-    A, B = W.torch_gemm_inputs(512, 512, 512, torch.float32, seed=1 + rank, batch=b - a)
-    C = torch.empty((b - a, 512, 512), dtype=torch.float32, device="cuda")
+    lo, hi = dp.shard(256, world, rank)
+    A_, B_ = W.torch_gemm_inputs(512, 512, 512, torch.float32, seed=1 + rank, batch=hi - lo)
+    C_ = torch.empty((hi - lo, 512, 512), dtype=torch.float32, device="cuda")
     for _ in range(3):
-        ops.matmul(A, B, out=C)
-    ms = time_region(lambda: ops.matmul(A, B, out=C), 10, world) / 10
-    out["gemm_batched_vmap"] = {"tflops": round(256 * 2 * 512 ** 3 / ms / 1e9, 2),
-                                "ms": round(ms, 3), "scaling": "strong (batch 256)"}
+        ops.matmul(A_, B_, out=C_)
+    ms = time_region(lambda: ops.matmul(A_, B_, out=C_), 10, world) / 10
+    t = 256 * 2 * 512 ** 3 / ms / 1e9
+    f32_peak = pipes["tf32_tflops"] / 3.0
+    out["gemm_batched_vmap"] = {"tflops": round(t, 2), "ms": round(ms, 3),
+                                "scaling": "strong (batch 256)",
+                                "roofline": {"bound": "tensor", "achieved": round(t, 2),
+                                             "peak": round(f32_peak, 2), "unit": "TFLOP/s",
+                                             "frac": round(t / f32_peak, 4)}}
+    del A_, B_, C_
+    _ = np
     return out
 
 
 # ---------------------------------------------------------------- reference arm
 
-def cpu_gemm_sample(n, budget_s, seed=1):
-    """Oracle (reference C lane algorithm) on a bounded sample of output rows
-    of the n^3 f32 product; returns (TFLOP/s, rows, seconds, threads)."""
-    import numpy as np
-    from chelis_b200 import workloads as W
-    from oracle import oracle as O
-    a, b = W.gemm_inputs(n, n, n, np.float32, seed=seed)
-    O.lib()
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    t0 = time.perf_counter()
-    O.gemm(a[:threads], b)
-    dt = time.perf_counter() - t0
-    per_row = dt / threads
-    rows = int(max(threads, min(n, budget_s / max(per_row, 1e-9))))
-    rows = (rows // threads) * threads or threads
-    t0 = time.perf_counter()
-    O.gemm(a[:rows], b)
-    dt = time.perf_counter() - t0
-    return 2.0 * rows * n * n / dt / 1e12, rows, dt, threads
-
-
 def run_reference(args, world, rank):
+    """The reference C lane's algorithm (the oracle) on the headline
+    workload: each step is the block forward + VJP of one sample of the
+    global batch (sample i mod 8), on every host core."""
     if rank != 0:
         return
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-    n = args.n
-    vals = []
+    import numpy as np
+    from chelis_b200 import workloads as W
+    cores = use_all_host_cores()
+    from oracle import oracle as O
+    O.lib()
+    shape = dict(W.BLOCK_SHAPE)
+    x, dy, w = W.block_inputs(seed=3, **shape)
+    times = []
     for i in range(args.warmup + args.steps):
-        v, rows, dt, threads = cpu_gemm_sample(n, args.ref_budget / max(1, args.steps))
+        j = i % GLOBAL_BATCH
+        t0 = time.perf_counter()
+        O.block_step(x[j:j + 1], w, shape["heads"], np.float32(1e-5), dy[j:j + 1])
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            vals.append((v, rows, dt))
-    value = statistics.median(v for v, _, _ in vals)
-    rows = vals[-1][1]
+            times.append(dt)
+    per_sample = statistics.median(times)
+    value = 1.0 / per_sample
     line = {
-        "impl": "reference", "metric": "gemm_f32_tflops", "value": value, "unit": "TFLOP/s",
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": statistics.median(dt for _, _, dt in vals) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic U(-1,1) seed 1",
-        "config": {"workload": f"gemm_f32 row-major {n}x{n}x{n} (config 2)",
-                   "sample": f"{rows} of {n} output rows per step"},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows x {n} cols of C, k = {n}, canonical tree over k"},
-        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "ms_per_step": per_sample * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": DATA,
+        "config": block_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "one sample of the global batch per step (block forward + "
+                                   "VJP at S 2048, d 1024), oracle restatement of the C lane"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -478,13 +749,11 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="chelis", choices=["chelis", "reference"])
-    ap.add_argument("--n", type=int, default=N_HEADLINE)
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--ref-budget", type=float, default=60.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -497,37 +766,45 @@ def main():
     import torch
     world, rank, local = dist_setup(args)
     peaks = load_peaks()
-    res = bench_gemm_headline(args, world, rank, peaks)
-    extras = None
+    if world > 1:
+        from chelis_b200 import dp
+        dp.native_init(world, rank)
+    pipes = measure_pipe_peaks()
+    res = bench_block_headline(args, world, rank, peaks, pipes)
+    with_cpu = rank == 0 and world == 1 and not args.no_cpu
+    extras = {}
     if not args.no_extras:
-        extras = bench_extras(args, peaks) if world == 1 else {}
-        extras.update(bench_sharded(args, world, rank, peaks))
+        if world == 1:
+            extras.update(bench_gemm(args, peaks, pipes, with_cpu))
+            extras.update(bench_rows(args, peaks, with_cpu))
+        extras.update(bench_sharded(args, world, rank, peaks, pipes, with_cpu))
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-        v, rows, dt, threads = cpu_gemm_sample(args.n, 15.0)
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": f"{rows} of {args.n} output rows of the {args.n}^3 f32 product "
-                         f"({dt:.1f} s), oracle restatement of the C lane"}
+    if with_cpu:
+        v, dt, cores = cpu_block_sample()
+        cpu = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"one sample of the batch: block forward + VJP at S 2048, d 1024 "
+                         f"({dt:.2f} s), oracle restatement of the C lane"}
     if rank == 0:
         line = {
-            "metric": "gemm_f32_tflops", "value": round(res["value"], 2), "unit": "TFLOP/s",
+            "metric": METRIC, "value": round(res["value"], 2), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(res["ms_per_step"], 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic U(-1,1) seed 1 (per-rank seed offset)",
-            "config": {"workload": f"gemm_f32 row-major {args.n}x{args.n}x{args.n} (config 2, 3xTF32)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs 512 MiB > L2, no flush"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": DATA,
+            "config": block_config(world),
             "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
             "gpu_launches": res["launches"], "clocks": res["clocks"],
+            "breakdown": res["breakdown"], "pipe_peaks": pipes,
         }
-        if extras is not None:
+        if extras:
             line["extra"] = extras
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        from chelis_b200 import dp
+        torch.cuda.synchronize()
         dist.barrier()
+        dp.native_finalize()
         dist.destroy_process_group()
 
 
