@@ -6,8 +6,10 @@ and reverse mode, f32 -- batch 8, sequence 2048, d_model 1024, 16 heads of
 Xavier-uniform and activations N(0, 1) from seed 3 -- data-parallel over
 the batch: with --gpus N the global batch of 8 is split across the N ranks
 (strong scaling) and the weight gradients (12.6 M f32, 50.3 MB) are summed
-across ranks by the library's NCCL communicator (chelis_cuda_dp_*) every
-step.  Metric: samples per second of the whole job.
+across ranks by the library's NCCL communicator every step, each gradient
+as soon as the reverse pass has written it, overlapped with the rest of the
+pass (chelis_cuda_block_step_dp).  Metric: samples per second of the whole
+job.
 
   value     device-resident inputs, CUDA-event timed over exactly --steps
             steps after --warmup untimed ones, max over ranks.  The working
@@ -167,7 +169,7 @@ def dist_setup(args):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
@@ -205,6 +207,26 @@ def time_region(fn, steps, world):
     torch.cuda.synchronize()
     barrier(world)
     return max_over_ranks(start.elapsed_time(stop), world)
+
+
+def warm_until_sampling(step, clk, world, limit_s=5.0):
+    """Run untimed steps until the clock sampler of every rank has reported
+    (or limit_s has passed on every rank).  The stop decision is a MIN
+    all-reduce over the ranks after each step, so every rank runs the same
+    number of steps."""
+    import torch
+    t0 = time.time()
+    while True:
+        step()
+        torch.cuda.synchronize()
+        done = 1.0 if (clk.lines or time.time() - t0 > limit_s) else 0.0
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([done], dtype=torch.float32, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            done = float(t.item())
+        if done:
+            return
 
 
 def timed(fn, steps, warm=3):
@@ -314,19 +336,19 @@ def bench_block_headline(args, world, rank, peaks, pipes):
     ws = ops.block_workspace(x, w, heads)
 
     def step():
-        ops.block_step(x, w, heads, 1e-5, dy, workspace=ws, out=res)
-        dp.allreduce_sum(grads.flat, world)
+        # each weight gradient is summed across the ranks as soon as the
+        # reverse pass has written it, overlapped with the rest of the pass
+        ops.block_step(x, w, heads, 1e-5, dy, workspace=ws, out=res, reduce_grads=True)
 
     for _ in range(args.warmup):
         step()
     ops.device_status()
     with ClockSampler(torch.cuda.current_device()) as clk:
         # the sampler needs ~1 s to start; keep the GPU busy with untimed
-        # steps until it reports, then time exactly args.steps
-        t0 = time.time()
-        while not clk.lines and time.time() - t0 < 5.0:
-            step()
-            torch.cuda.synchronize()
+        # steps until every rank's sampler reports (a collective decision, so
+        # all ranks run the same number of steps and collectives), then time
+        # exactly args.steps
+        warm_until_sampling(step, clk, world)
         l0 = ops.launch_count()
         ms = time_region(step, args.steps, world)
         launches = ops.launch_count() - l0
@@ -338,11 +360,19 @@ def bench_block_headline(args, world, rank, peaks, pipes):
     # gradient all-reduce alone
     phases, groups = block_phases(lambda: ops.block_step(x, w, heads, 1e-5, dy, workspace=ws,
                                                          out=res))
-    ar_ms = 0.0
+    ar_ms = serial_ms = 0.0
     if world > 1:
         for _ in range(3):
             dp.allreduce_sum(grads.flat, world)
         ar_ms = time_region(lambda: dp.allreduce_sum(grads.flat, world), 10, world) / 10
+
+        def serial_step():
+            ops.block_step(x, w, heads, 1e-5, dy, workspace=ws, out=res)
+            dp.allreduce_sum(grads.flat, world)
+
+        for _ in range(2):
+            serial_step()
+        serial_ms = time_region(serial_step, 5, world) / 5
     fl = block_flops(local)
     dom = max(("gemm", "attention_fwd", "attention_bwd"), key=lambda g: groups.get(g, 0.0))
     dom_ms = groups[dom]
@@ -370,8 +400,7 @@ def bench_block_headline(args, world, rank, peaks, pipes):
     def e2e_step():
         xd.copy_(hx, non_blocking=True)
         dyd.copy_(hdy, non_blocking=True)
-        ops.block_step(xd, w, heads, 1e-5, dyd, workspace=ws, out=res)
-        dp.allreduce_sum(grads.flat, world)
+        ops.block_step(xd, w, heads, 1e-5, dyd, workspace=ws, out=res, reduce_grads=True)
         hg.copy_(grads.flat, non_blocking=True)
         hdx.copy_(res["dx"], non_blocking=True)
 
@@ -389,6 +418,8 @@ def bench_block_headline(args, world, rank, peaks, pipes):
                 breakdown={"phase_ms": phases, "group_ms": groups,
                            "compute_ms": round(sum(groups.values()), 4),
                            "allreduce_alone_ms": round(ar_ms, 4),
+                           "allreduce_overlapped": world > 1,
+                           "step_ms_allreduce_after_step": round(serial_ms, 4),
                            "allreduce_mb": round(grads.flat.numel() * 4 / 1e6, 1),
                            "per_rank_batch": local,
                            "step_useful_tflops": round(fl["total"] / (ms_step * 1e-3) / 1e12, 1),

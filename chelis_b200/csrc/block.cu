@@ -620,7 +620,62 @@ extern "C" int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *
     return carve(d, nullptr).total * static_cast<int64_t>(sizeof(float));
 }
 
-extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *workspace) {
+// ---------------------------------------------------------------------------
+// Gradient reduction overlapped with the reverse pass: each parameter
+// gradient is summed across the data-parallel ranks as soon as the reverse
+// pass has written it, on the library's communication stream, while the
+// reverse pass goes on; the caller's stream waits for all of them at the
+// end of the step.  Events are created once per device (one host thread per
+// device at a time drives a communicator).
+// ---------------------------------------------------------------------------
+namespace grad_reduce {
+constexpr int kMax = 8;
+cudaEvent_t g_ev[64][kMax + 1] = {};
+
+struct Overlap {
+    bool on = false;
+    int dev = 0, n = 0;
+    cudaStream_t comm = nullptr;
+    int begin(cudaStream_t) {
+        if (dp_nranks() <= 1) return CHELIS_CUDA_OK;
+        CHELIS_TRY(current_device_checked(&dev));
+        if (dev >= 64) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "device index %d", dev);
+        CHELIS_TRY(dp_comm_stream(&comm));
+        for (cudaEvent_t &e : g_ev[dev])
+            if (!e)
+                CHELIS_TRY(check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming),
+                                      "cudaEventCreate(grad reduce)"));
+        on = true;
+        return CHELIS_CUDA_OK;
+    }
+    // sum `count` floats at `buf` across ranks once the work queued on `s`
+    // so far (which wrote them) is done
+    int reduce(float *buf, int64_t count, cudaStream_t s) {
+        if (!on) return CHELIS_CUDA_OK;
+        if (n >= kMax) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "too many gradient buckets");
+        cudaEvent_t e = g_ev[dev][n++];
+        CHELIS_TRY(check_cuda(cudaEventRecord(e, s), "cudaEventRecord(grad ready)"));
+        CHELIS_TRY(check_cuda(cudaStreamWaitEvent(comm, e, 0), "cudaStreamWaitEvent(comm)"));
+        return dp_allreduce_f32_on(buf, count, comm);
+    }
+    // two gradients in one reduction when the caller laid them out back to back
+    int reduce_pair(float *a, float *b, int64_t count, cudaStream_t s) {
+        if (b == a + count) return reduce(a, 2 * count, s);
+        CHELIS_TRY(reduce(a, count, s));
+        return reduce(b, count, s);
+    }
+    // the caller's stream waits for every reduction issued
+    int join(cudaStream_t s) {
+        if (!on) return CHELIS_CUDA_OK;
+        cudaEvent_t e = g_ev[dev][kMax];
+        CHELIS_TRY(check_cuda(cudaEventRecord(e, comm), "cudaEventRecord(grads reduced)"));
+        return check_cuda(cudaStreamWaitEvent(s, e, 0), "cudaStreamWaitEvent(grads reduced)");
+    }
+};
+}  // namespace grad_reduce
+
+namespace {
+int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_grads) {
     BlockDims d;
     CHELIS_TRY(block_dims(p, d));
     cudaStream_t s = current_stream();
@@ -649,6 +704,12 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
     // split copies for the fused path: [q_hi, q_lo, k_hi, k_lo, v_hi, v_lo, dO_hi, dO_lo]
     float *hl = w.hl;
     int st = CHELIS_CUDA_OK;
+    grad_reduce::Overlap gr;
+    if (reduce_grads && p->dy && (st = gr.begin(s))) {
+        if (owned_big) scratch_free(owned_big, s);
+        if (owned) scratch_free(owned, s);
+        return st;
+    }
     using block_timing::mark;
     block_timing::reset();
     do {
@@ -701,6 +762,7 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
         // ---------------- reverse mode ----------------
         const float *dy = p->dy;
         if ((st = mm(1, 0, F, D, BS, w.g, F, dy, D, p->dw_2, D))) break;
+        if ((st = gr.reduce(p->dw_2, F * D, s))) break;
         if ((st = mm(0, 1, BS, F, D, dy, D, p->w_2, D, w.dg, F))) break;
         mark(9, s);
         block::gelu_bwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.dg, BS * F);
@@ -708,12 +770,15 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
         if ((st = check_cuda(cudaGetLastError(), "gelu_bwd_kernel"))) break;
         mark(10, s);
         if ((st = mm(1, 0, D, F, BS, w.h2, D, w.dg, F, p->dw_1, F))) break;
+        if ((st = gr.reduce(p->dw_1, D * F, s))) break;
         if ((st = mm(0, 1, BS, D, F, w.dg, F, p->w_1, F, w.dh2, D))) break;
         mark(11, s);
         if ((st = ln_bwd(w.x2, w.dh2, w.st2, p->ln2_gamma, dy, w.dx2, w.part, p->dln2_gamma,
                          p->dln2_beta, BS, D, s))) break;
+        if ((st = gr.reduce_pair(p->dln2_gamma, p->dln2_beta, D, s))) break;
         mark(12, s);
         if ((st = mm(1, 0, D, D, BS, w.o, D, w.dx2, D, p->dw_o, D))) break;
+        if ((st = gr.reduce(p->dw_o, D * D, s))) break;
         if ((st = mm(0, 1, BS, D, D, w.dx2, D, p->w_o, D, w.dO, D))) break;
         mark(13, s);
         if (fused) {
@@ -745,15 +810,31 @@ extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *worksp
         }
         mark(14, s);
         if ((st = mm(1, 0, D, 3 * D, BS, w.h1, D, w.dqkv, 3 * D, p->dw_qkv, 3 * D))) break;
+        if ((st = gr.reduce(p->dw_qkv, D * 3 * D, s))) break;
         if ((st = mm(0, 1, BS, D, 3 * D, w.dqkv, 3 * D, p->w_qkv, 3 * D, w.dh1, D))) break;
         mark(15, s);
         if ((st = ln_bwd(p->x, w.dh1, w.st1, p->ln1_gamma, w.dx2, p->dx, w.part, p->dln1_gamma,
                          p->dln1_beta, BS, D, s))) break;
         mark(16, s);
+        if ((st = gr.reduce_pair(p->dln1_gamma, p->dln1_beta, D, s))) break;
     } while (0);
+    // the caller's stream waits for the reductions issued, also after an error
+    if (gr.on) {
+        const int js = gr.join(s);
+        if (st == CHELIS_CUDA_OK) st = js;
+    }
     if (owned_big) scratch_free(owned_big, s);
     if (owned) scratch_free(owned, s);
     return st;
+}
+}  // namespace
+
+extern "C" int chelis_cuda_block_step(const chelis_block_params *p, void *workspace) {
+    return block_step_impl(p, workspace, false);
+}
+
+extern "C" int chelis_cuda_block_step_dp(const chelis_block_params *p, void *workspace) {
+    return block_step_impl(p, workspace, true);
 }
 
 extern "C" int chelis_cuda_block_timing(int enable) {

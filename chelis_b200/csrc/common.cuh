@@ -27,6 +27,11 @@ int current_device_checked(int *device);
 int scratch_alloc(void **ptr, size_t bytes, cudaStream_t stream);
 void scratch_free(void *ptr, cudaStream_t stream);
 int sm_count();
+// data-parallel communicator (dp.cu): its size (1 when none is open), the
+// library's communication stream, an f32 sum all-reduce on a given stream
+int dp_nranks();
+int dp_comm_stream(cudaStream_t *out);
+int dp_allreduce_f32_on(float *buf, int64_t count, cudaStream_t s);
 
 #define CHELIS_TRY(expr)                   \
     do {                                   \

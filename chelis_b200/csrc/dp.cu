@@ -64,6 +64,45 @@ int nccl_check(ncclResult_t r, const char *what) {
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Library-internal entry points for programs that reduce their gradients as
+// they produce them (chelis_cuda_block_step_dp): the communicator's size and
+// an f32 sum all-reduce on a given stream.  The communication stream is
+// created once per process, on the communicator's device, non-blocking with
+// respect to the legacy default stream.
+// ---------------------------------------------------------------------------
+cudaStream_t g_comm_stream = nullptr;
+
+int dp_nranks() {
+    std::lock_guard<std::mutex> lock(g_dp_mu);
+    return g_nccl.comm ? g_nccl.nranks : 1;
+}
+
+int dp_comm_stream(cudaStream_t *out) {
+    std::lock_guard<std::mutex> lock(g_dp_mu);
+    if (!g_nccl.comm) return set_error(CHELIS_CUDA_ERR_DOMAIN, "dp: no communicator (dp_init)");
+    if (!g_comm_stream) {
+        int prio_lo = 0, prio_hi = 0;
+        CHELIS_TRY(check_cuda(cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi),
+                              "cudaDeviceGetStreamPriorityRange"));
+        CHELIS_TRY(check_cuda(cudaStreamCreateWithPriority(&g_comm_stream, cudaStreamNonBlocking,
+                                                           prio_hi),
+                              "cudaStreamCreateWithPriority(dp comm)"));
+    }
+    *out = g_comm_stream;
+    return CHELIS_CUDA_OK;
+}
+
+int dp_allreduce_f32_on(float *buf, int64_t count, cudaStream_t s) {
+    std::lock_guard<std::mutex> lock(g_dp_mu);
+    if (!g_nccl.comm) return set_error(CHELIS_CUDA_ERR_DOMAIN, "dp_allreduce: no communicator (dp_init)");
+    if (count <= 0) return CHELIS_CUDA_OK;
+    return nccl_check(g_nccl.all_reduce(buf, buf, static_cast<size_t>(count), ncclFloat32, ncclSum,
+                                        g_nccl.comm, s),
+                      "ncclAllReduce");
+}
+
 }  // namespace chelis
 
 using namespace chelis;
@@ -141,6 +180,11 @@ extern "C" int chelis_cuda_dp_finalize(int32_t abort) {
     g_nccl.comm = nullptr;
     g_nccl.nranks = 0;
     g_nccl.rank = -1;
+    if (g_comm_stream) {
+        cudaStreamSynchronize(g_comm_stream);
+        cudaStreamDestroy(g_comm_stream);
+        g_comm_stream = nullptr;
+    }
     return nccl_check(abort ? g_nccl.comm_abort(comm) : g_nccl.comm_destroy(comm),
                       abort ? "ncclCommAbort" : "ncclCommDestroy");
 }

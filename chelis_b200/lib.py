@@ -124,6 +124,7 @@ SIGNATURES = {
     "chelis_cuda_mlp_step": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "chelis_cuda_block_workspace_bytes": (c_i64, [ctypes.POINTER(BlockParams)]),
     "chelis_cuda_block_step": (c_int, [ctypes.POINTER(BlockParams), c_vp]),
+    "chelis_cuda_block_step_dp": (c_int, [ctypes.POINTER(BlockParams), c_vp]),
     "chelis_cuda_block_timing": (c_int, [c_int]),
     "chelis_cuda_block_phase_ms": (c_int, [ctypes.POINTER(c_f32), c_i32]),
     "chelis_cuda_block_phase_name": (ctypes.c_char_p, [c_i32]),

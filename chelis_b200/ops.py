@@ -332,9 +332,12 @@ BLOCK_WEIGHTS = ("w_qkv", "w_o", "w_1", "w_2", "ln1_gamma", "ln1_beta", "ln2_gam
 
 
 def block_step(x, weights: dict, heads: int, eps: float = 1e-5, dy=None, workspace=None,
-               out: dict | None = None):
+               out: dict | None = None, reduce_grads: bool = False):
     """Transformer block forward (+ vector-Jacobian product when dy is given).
-    Returns a dict with y and, with dy, dx and d<weight> for every weight."""
+    Returns a dict with y and, with dy, dx and d<weight> for every weight.
+    reduce_grads: one rank of a data-parallel step (chelis_cuda_block_step_dp):
+    every weight gradient is summed across the ranks of the library's
+    communicator while the reverse pass runs."""
     import ctypes
     _prepare(x, dy, *[weights[k] for k in BLOCK_WEIGHTS])
     batch, seq, d = x.shape
@@ -359,8 +362,8 @@ def block_step(x, weights: dict, heads: int, eps: float = 1e-5, dy=None, workspa
         p.dx = o["dx"].data_ptr()
         for k in BLOCK_WEIGHTS:
             setattr(p, "d" + k if k.startswith("w") else "d" + k, o["d" + k].data_ptr())
-    L.call("chelis_cuda_block_step", ctypes.byref(p),
-           None if workspace is None else workspace.data_ptr())
+    L.call("chelis_cuda_block_step_dp" if reduce_grads else "chelis_cuda_block_step",
+           ctypes.byref(p), None if workspace is None else workspace.data_ptr())
     return o
 
 

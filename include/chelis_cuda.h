@@ -484,6 +484,17 @@ int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p);
 /* workspace: device memory of chelis_cuda_block_workspace_bytes bytes, or
  * NULL to take it from the library's stream-ordered pool for the call. */
 int chelis_cuda_block_step(const chelis_block_params *p, void *workspace);
+/* chelis_cuda_block_step for one rank of a data-parallel step: with a
+ * communicator open (chelis_cuda_dp_init, more than one rank), each of the
+ * eight parameter gradients is summed across the ranks as soon as the
+ * reverse pass has written it, on the library's communication stream, while
+ * the reverse pass goes on (dln*_gamma / dln*_beta in one reduction when
+ * beta follows gamma in memory).  The call's stream waits for all of them
+ * before later work, so on return (stream order) every d<weight> holds the
+ * all-rank sum; x, y and dx stay this rank's.  With one rank, or dy == NULL,
+ * it is chelis_cuda_block_step.  No counterpart in the reference (it has no
+ * multi-GPU lane).  One host thread per device at a time. */
+int chelis_cuda_block_step_dp(const chelis_block_params *p, void *workspace);
 /* Phase timing of chelis_cuda_block_step (a diagnostic; no counterpart in the
  * reference).  enable != 0 creates CUDA events on the current device; every
  * later block step records them on its stream at its 16 phase boundaries

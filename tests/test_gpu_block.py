@@ -94,3 +94,17 @@ def test_block_config4_shape_matches_oracle(cuda, orc):
     y_ref, g_ref = orc.block_step(x, w, shape["heads"], 1e-5, dy)
     errs = _oracle_bound_check(out, y_ref, g_ref, 1e-5)
     print("config-4 normwise errors vs oracle:", {k: f"{v:.2e}" for k, v in errs.items()})
+
+
+def test_block_step_dp_is_block_step_on_one_rank(cuda):
+    """Without a multi-rank communicator the data-parallel entry runs the
+    same step: bit-identical outputs."""
+    import torch
+    shape = dict(batch=2, seq=128, d_model=128, heads=2, d_ff=256)
+    x, dy, w = W.block_inputs(seed=13, **shape)
+    X, DY = torch.from_numpy(x).cuda(), torch.from_numpy(dy).cuda()
+    wt = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    a = cuda.block_step(X, wt, 2, 1e-5, DY)
+    b = cuda.block_step(X, wt, 2, 1e-5, DY, reduce_grads=True)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k

@@ -1,6 +1,8 @@
 """The library's own NCCL communicator on two GPUs: every rank sums a buffer
 whose values are exact in f32 / f64 / i64, through chelis_cuda_dp_*; the
-data-parallel gradient of the sharded batch equals the full-batch one."""
+data-parallel gradient of the sharded batch equals the full-batch one, also
+for the transformer block with its gradients reduced during the reverse
+pass (chelis_cuda_block_step_dp)."""
 import os
 import socket
 
@@ -37,6 +39,24 @@ def _worker(rank, world, port, q):
         full = ops.matmul(xb, dyb, trans_a=True)
         torch.cuda.synchronize()
         out["grad"] = float((dw - full).abs().max() / full.abs().max())
+        # transformer block: each rank steps its half of the batch with the
+        # gradients reduced during the reverse pass; they must equal the
+        # full-batch gradients (one GPU, same kernels) within f32 rel 1e-5
+        from chelis_b200 import workloads as W
+        shape = dict(batch=2, seq=128, d_model=128, heads=2, d_ff=256)
+        xn, dyn, wn = W.block_inputs(seed=21, **shape)
+        wt = {k: torch.from_numpy(v).cuda() for k, v in wn.items()}
+        X, DY = torch.from_numpy(xn).cuda(), torch.from_numpy(dyn).cuda()
+        a, b = dp.shard(2, world, rank)
+        grads = dp.FlatGrads({"d" + k: tuple(wt[k].shape) for k in ops.BLOCK_WEIGHTS}, "cuda")
+        res = {k: grads[k] for k in grads.views}
+        part = ops.block_step(X[a:b].contiguous(), wt, 2, 1e-5, DY[a:b].contiguous(), out=res,
+                              reduce_grads=True)
+        ref = ops.block_step(X, wt, 2, 1e-5, DY)
+        torch.cuda.synchronize()
+        out["block"] = max(float((part[k] - ref[k]).abs().max() / ref[k].abs().max())
+                           for k in grads.views)
+        out["block_dx"] = float((part["dx"] - ref["dx"][a:b]).abs().max() / ref["dx"].abs().max())
         dp.native_finalize()
         dist.barrier()
         dist.destroy_process_group()
@@ -71,3 +91,5 @@ def test_two_rank_native_allreduce():
         assert isinstance(out, dict), out
         assert out["torch.float32"] and out["torch.float64"] and out["torch.int64"]
         assert out["grad"] <= 1e-5
+        assert out["block"] <= 1e-5, out["block"]
+        assert out["block_dx"] <= 1e-5, out["block_dx"]
