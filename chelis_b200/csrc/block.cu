@@ -448,12 +448,20 @@ int block_dims(const chelis_block_params *p, BlockDims &d) {
 // (P, dP: [B*H, S, S] of the materialised attention path, taken from the
 // pool by chelis_cuda_block_step only when that path runs; hl: hi / lo
 // copies of q, k, v, dO for the fused path; lse, dsum: [B*H, S].)
+// The 3xTF32 hi / lo copies of every matmul operand, made once per step
+// (each tensor feeds two matmuls, forward and reverse, and its row-major
+// split serves both orientations when its row length is a multiple of 32).
+enum SplitTensor { S_H1, S_WQKV, S_O, S_WO, S_H2, S_W1, S_G, S_W2, S_DY, S_DG, S_DX2, S_DQKV, S_COUNT };
+
 struct Ws {
     float *h1, *qkv, *q, *k, *v, *P, *oh, *o, *x2, *h2, *u, *g, *dg, *dh2, *dx2, *dO, *doh, *dP,
         *dq, *dk, *dv, *dqkv, *dh1, *part, *hl, *lse, *dsum;
     float2 *st1, *st2;
+    float *shi[S_COUNT], *slo[S_COUNT];  // null when the dims do not admit cached splits
     int64_t total;
 };
+
+bool split_cache_dims(const BlockDims &d) { return d.D % 32 == 0 && d.F % 32 == 0; }
 
 int ln_grid() { return sm_count() * 2; }
 
@@ -475,6 +483,14 @@ Ws carve(const BlockDims &d, float *base) {
     w.part = take(2 * static_cast<int64_t>(ln_grid()) * d.D);
     w.st1 = reinterpret_cast<float2 *>(take(2 * d.BS));
     w.st2 = reinterpret_cast<float2 *>(take(2 * d.BS));
+    if (split_cache_dims(d)) {
+        const int64_t n[S_COUNT] = {act, 3 * d.D * d.D, act, d.D * d.D, act, d.D * d.F, ff,
+                                    d.F * d.D, act, ff, act, 3 * act};
+        for (int i = 0; i < S_COUNT; ++i) {
+            w.shi[i] = take(n[i]);
+            w.slo[i] = take(n[i]);
+        }
+    }
     w.total = off;
     return w;
 }
@@ -584,6 +600,33 @@ int mm(int ta, int tb, int64_t m, int64_t n, int64_t k, const float *a, int64_t 
        int64_t sb = 0, int64_t sc = 0) {
     return chelis_cuda_sgemm(ta, tb, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc, batch);
 }
+
+// Matmuls of the step.  With cached splits (3xTF32 mode, row lengths that
+// are multiples of 32) each operand tensor is split once, at its first use,
+// and the products run on the split copies; otherwise every product goes
+// through chelis_cuda_sgemm (its own split, or the exact tree mode).
+struct Matmuls {
+    const Ws &w;
+    bool cached = false;
+    bool done[S_COUNT] = {};
+    // the split of tensor t ([rows][cols] row-major at x), once per step
+    int split(int t, const float *x, int64_t rows, int64_t cols) {
+        if (!cached || done[t]) return CHELIS_CUDA_OK;
+        done[t] = true;
+        return chelis_cuda_tf32x3_split(0, 0, rows, cols, x, cols, 0, 1, w.shi[t], w.slo[t]);
+    }
+    // C[m][n] = op(A) . op(B); A is tensor ta_id stored [k][m] (ta) or
+    // [m][k], B is tb_id stored [n][k] (tb) or [k][n]
+    int run(int ta, int tb, int64_t m, int64_t n, int64_t k, const float *a, int a_id,
+            const float *b, int b_id, float *c) {
+        if (!cached) return mm(ta, tb, m, n, k, a, ta ? m : k, b, tb ? k : n, c, n);
+        CHELIS_TRY(split(a_id, a, ta ? k : m, ta ? m : k));
+        CHELIS_TRY(split(b_id, b, tb ? n : k, tb ? k : n));
+        return chelis_cuda_sgemm_tf32x3_presplit(m, n, k, 1, ta ? 1 : 0, w.shi[a_id],
+                                                 w.slo[a_id], tb ? 0 : 1, w.shi[b_id],
+                                                 w.slo[b_id], c, n, 0);
+    }
+};
 
 }  // namespace
 
@@ -704,6 +747,8 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
     // split copies for the fused path: [q_hi, q_lo, k_hi, k_lo, v_hi, v_lo, dO_hi, dO_lo]
     float *hl = w.hl;
     int st = CHELIS_CUDA_OK;
+    Matmuls mx{w};
+    mx.cached = gemm_mode() == CHELIS_CUDA_GEMM_3XTF32 && w.shi[0] != nullptr;
     grad_reduce::Overlap gr;
     if (reduce_grads && p->dy && (st = gr.begin(s))) {
         if (owned_big) scratch_free(owned_big, s);
@@ -717,7 +762,7 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
         mark(0, s);
         if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, w.h1, w.st1, BS, D, s))) break;
         mark(1, s);
-        if ((st = mm(0, 0, BS, 3 * D, D, w.h1, D, p->w_qkv, 3 * D, w.qkv, 3 * D))) break;
+        if ((st = mx.run(0, 0, BS, 3 * D, D, w.h1, S_H1, p->w_qkv, S_WQKV, w.qkv))) break;
         mark(2, s);
         if (fused) {
             block::qkv_heads_split_kernel<<<grid_for(BS * 3 * D / 4), 256, 0, s>>>(
@@ -744,42 +789,42 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
             if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
         }
         mark(3, s);
-        if ((st = mm(0, 0, BS, D, D, w.o, D, p->w_o, D, w.x2, D))) break;
+        if ((st = mx.run(0, 0, BS, D, D, w.o, S_O, p->w_o, S_WO, w.x2))) break;
         if ((st = add(p->x, w.x2, w.x2, BS * D, s))) break;
         mark(4, s);
         if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) break;
         mark(5, s);
-        if ((st = mm(0, 0, BS, F, D, w.h2, D, p->w_1, F, w.u, F))) break;
+        if ((st = mx.run(0, 0, BS, F, D, w.h2, S_H2, p->w_1, S_W1, w.u))) break;
         mark(6, s);
         block::gelu_fwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.g, BS * F);
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_fwd_kernel"))) break;
         mark(7, s);
-        if ((st = mm(0, 0, BS, D, F, w.g, F, p->w_2, D, p->y, D))) break;
+        if ((st = mx.run(0, 0, BS, D, F, w.g, S_G, p->w_2, S_W2, p->y))) break;
         if ((st = add(w.x2, p->y, p->y, BS * D, s))) break;
         mark(8, s);
         if (!p->dy) break;
         // ---------------- reverse mode ----------------
         const float *dy = p->dy;
-        if ((st = mm(1, 0, F, D, BS, w.g, F, dy, D, p->dw_2, D))) break;
+        if ((st = mx.run(1, 0, F, D, BS, w.g, S_G, dy, S_DY, p->dw_2))) break;
         if ((st = gr.reduce(p->dw_2, F * D, s))) break;
-        if ((st = mm(0, 1, BS, F, D, dy, D, p->w_2, D, w.dg, F))) break;
+        if ((st = mx.run(0, 1, BS, F, D, dy, S_DY, p->w_2, S_W2, w.dg))) break;
         mark(9, s);
         block::gelu_bwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.dg, BS * F);
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_bwd_kernel"))) break;
         mark(10, s);
-        if ((st = mm(1, 0, D, F, BS, w.h2, D, w.dg, F, p->dw_1, F))) break;
+        if ((st = mx.run(1, 0, D, F, BS, w.h2, S_H2, w.dg, S_DG, p->dw_1))) break;
         if ((st = gr.reduce(p->dw_1, D * F, s))) break;
-        if ((st = mm(0, 1, BS, D, F, w.dg, F, p->w_1, F, w.dh2, D))) break;
+        if ((st = mx.run(0, 1, BS, D, F, w.dg, S_DG, p->w_1, S_W1, w.dh2))) break;
         mark(11, s);
         if ((st = ln_bwd(w.x2, w.dh2, w.st2, p->ln2_gamma, dy, w.dx2, w.part, p->dln2_gamma,
                          p->dln2_beta, BS, D, s))) break;
         if ((st = gr.reduce_pair(p->dln2_gamma, p->dln2_beta, D, s))) break;
         mark(12, s);
-        if ((st = mm(1, 0, D, D, BS, w.o, D, w.dx2, D, p->dw_o, D))) break;
+        if ((st = mx.run(1, 0, D, D, BS, w.o, S_O, w.dx2, S_DX2, p->dw_o))) break;
         if ((st = gr.reduce(p->dw_o, D * D, s))) break;
-        if ((st = mm(0, 1, BS, D, D, w.dx2, D, p->w_o, D, w.dO, D))) break;
+        if ((st = mx.run(0, 1, BS, D, D, w.dx2, S_DX2, p->w_o, S_WO, w.dO))) break;
         mark(13, s);
         if (fused) {
             block::rows_heads_split_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
@@ -809,9 +854,9 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
             if ((st = check_cuda(cudaGetLastError(), "qkv_permute_kernel"))) break;
         }
         mark(14, s);
-        if ((st = mm(1, 0, D, 3 * D, BS, w.h1, D, w.dqkv, 3 * D, p->dw_qkv, 3 * D))) break;
+        if ((st = mx.run(1, 0, D, 3 * D, BS, w.h1, S_H1, w.dqkv, S_DQKV, p->dw_qkv))) break;
         if ((st = gr.reduce(p->dw_qkv, D * 3 * D, s))) break;
-        if ((st = mm(0, 1, BS, D, 3 * D, w.dqkv, 3 * D, p->w_qkv, 3 * D, w.dh1, D))) break;
+        if ((st = mx.run(0, 1, BS, D, 3 * D, w.dqkv, S_DQKV, p->w_qkv, S_WQKV, w.dh1))) break;
         mark(15, s);
         if ((st = ln_bwd(p->x, w.dh1, w.st1, p->ln1_gamma, w.dx2, p->dx, w.part, p->dln1_gamma,
                          p->dln1_beta, BS, D, s))) break;

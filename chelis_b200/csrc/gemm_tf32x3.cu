@@ -1041,23 +1041,29 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     p.kb_per_split = p.num_kb;
     p.part = nullptr;
     p.chunk_kb = CHUNK_KB;
-    // Split-K when the tile grid fills the GPU poorly (long-K weight
-    // gradients, mid-size squares): pick the split count whose CTA total
-    // wastes the fewest SM slots of its last wave (a small penalty per extra
-    // split for the partial traffic), each split keeping >= 4 k-blocks.
+    // Split-K when the tile grid fills the GPU poorly.  Each candidate split
+    // count is costed as (waves of CTA pairs) x (time of one tile: its
+    // k-blocks plus a fixed prologue / epilogue) plus the HBM traffic of the
+    // partial products (written by the epilogues, read by the reduction, and
+    // the reduced result written); the cheapest wins, each split keeping at
+    // least 4 k-blocks.  Times in microseconds at the tf32 pipe's pace
+    // (three MMAs of K = 8, four per 32-wide k-block, ~1.15 us per k-block).
     if (pair) {
-        const int64_t sms = sm_count();
-        const int64_t ctas = 2 * ((m + 2 * P_ROWS - 1) / (2 * P_ROWS)) * ((n + BN - 1) / BN) * batch;
-        if (ctas < 2 * sms && p.num_kb >= 8) {
-            double best = -1.0;
+        const int64_t clusters = sm_count() / 2;
+        const int64_t pairs = ((m + 2 * P_ROWS - 1) / (2 * P_ROWS)) * ((n + BN - 1) / BN) * batch;
+        if (pairs < 2 * clusters && p.num_kb >= 8) {
+            constexpr double kTileK = 1.15, kTileFixed = 5.0, kBytesPerUs = 5.0e6;
+            double best = 0.0;
             int best_s = 1;
             for (int sp = 1; sp <= 16 && p.num_kb / sp >= 4; ++sp) {
-                const int64_t tot = ctas * sp;
-                const double eff = static_cast<double>(tot) /
-                                   static_cast<double>(((tot + sms - 1) / sms) * sms);
-                const double score = eff - 0.02 * (sp - 1);
-                if (score > best + 1e-9) {
-                    best = score;
+                const int64_t kbs = (p.num_kb + sp - 1) / sp;
+                const int64_t waves = (pairs * sp + clusters - 1) / clusters;
+                double t = static_cast<double>(waves) * (kbs * kTileK + kTileFixed);
+                if (sp > 1)
+                    t += static_cast<double>(2 * sp + 1) * static_cast<double>(batch * m * n) * 4.0 /
+                         kBytesPerUs;
+                if (sp == 1 || t < best) {
+                    best = t;
                     best_s = sp;
                 }
             }
