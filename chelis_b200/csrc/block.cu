@@ -655,6 +655,22 @@ inline void mark(int i, cudaStream_t s) {
 inline void reset() {
     for (bool &r : g_rec) r = false;
 }
+// Destroy the phase events (on the device that created them) and turn timing off.
+void release() {
+    if (g_dev >= 0) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(g_dev);
+        for (cudaEvent_t &e : g_ev) {
+            if (e) cudaEventDestroy(e);
+            e = nullptr;
+        }
+        cudaSetDevice(prev);
+    }
+    g_dev = -1;
+    g_on = false;
+    reset();
+}
 }  // namespace block_timing
 
 extern "C" int64_t chelis_cuda_block_workspace_bytes(const chelis_block_params *p) {
@@ -715,6 +731,20 @@ struct Overlap {
         return check_cuda(cudaStreamWaitEvent(s, e, 0), "cudaStreamWaitEvent(grads reduced)");
     }
 };
+
+// Destroy the reduction events of every device.
+void release_events() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (int d = 0; d < 64; ++d)
+        for (cudaEvent_t &e : g_ev[d])
+            if (e) {
+                cudaSetDevice(d);
+                cudaEventDestroy(e);
+                e = nullptr;
+            }
+    cudaSetDevice(prev);
+}
 }  // namespace grad_reduce
 
 namespace {

@@ -35,6 +35,8 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -312,6 +314,7 @@ struct Driver {
     decltype(&cuModuleLoadData) load = nullptr;
     decltype(&cuModuleGetFunction) get = nullptr;
     decltype(&cuLaunchKernel) launch = nullptr;
+    decltype(&cuModuleUnload) unload = nullptr;
     bool ok = false;
 };
 
@@ -330,13 +333,15 @@ const Driver &driver() {
         d.load = reinterpret_cast<decltype(d.load)>(entry("cuModuleLoadData"));
         d.get = reinterpret_cast<decltype(d.get)>(entry("cuModuleGetFunction"));
         d.launch = reinterpret_cast<decltype(d.launch)>(entry("cuLaunchKernel"));
-        d.ok = d.load && d.get && d.launch;
+        d.unload = reinterpret_cast<decltype(d.unload)>(entry("cuModuleUnload"));
+        d.ok = d.load && d.get && d.launch && d.unload;
     });
     return d;
 }
 
 std::mutex g_mu;
 std::unordered_map<std::string, CUfunction> g_cache;  // key: device id + kernel text
+std::vector<std::pair<int, CUmodule>> g_modules;      // (device, module) behind g_cache
 std::atomic<int> g_enabled{1};
 std::atomic<uint64_t> g_jit_launches{0};
 std::atomic<uint64_t> g_compiles{0};
@@ -382,6 +387,7 @@ int get_kernel(const std::string &src, CUfunction *fn) {
     if (drv.get(fn, mod, "chelis_fused_jit") != CUDA_SUCCESS)
         return set_error(CHELIS_CUDA_ERR_CUDA, "cuModuleGetFunction(fused JIT) failed");
     g_cache.emplace(key, *fn);
+    g_modules.emplace_back(dev, mod);
     g_compiles++;
     return CHELIS_CUDA_OK;
 }
@@ -523,6 +529,23 @@ int try_reduce(bool f32, const chelis_fused_step *steps, int n_steps, const fuse
     a.nvec = outputs;
     a.len = len;
     return launch(fn, a, (outputs + THREADS / 32 - 1) / (THREADS / 32), s);
+}
+
+// Unload every compiled chain kernel (each on its own device) and empty the
+// cache; later calls compile again.
+int release_all() {
+    std::lock_guard<std::mutex> lock(g_mu);
+    int st = CHELIS_CUDA_OK, prev = 0;
+    cudaGetDevice(&prev);
+    const Driver &drv = driver();
+    for (auto &dm : g_modules) {
+        if (cudaSetDevice(dm.first) != cudaSuccess || !drv.unload || drv.unload(dm.second) != CUDA_SUCCESS)
+            st = set_error(CHELIS_CUDA_ERR_CUDA, "cuModuleUnload(fused JIT) failed");
+    }
+    cudaSetDevice(prev);
+    g_modules.clear();
+    g_cache.clear();
+    return st;
 }
 
 }  // namespace fusedjit

@@ -30,6 +30,13 @@ struct DeviceStreams {
     cudaStream_t up = nullptr, down = nullptr;
     cudaEvent_t ev_start = nullptr, ev_up = nullptr, ev_comp = nullptr, ev_down = nullptr;
     std::mutex lock;
+    struct Empty {};
+    DeviceStreams &operator=(Empty) {  // back to the unset state (the lock is kept)
+        ready = false;
+        up = down = nullptr;
+        ev_start = ev_up = ev_comp = ev_down = nullptr;
+        return *this;
+    }
 };
 DeviceStreams g_dev[64];
 
@@ -51,6 +58,25 @@ int streams_for_current(DeviceStreams **out) {
     }
     *out = &ds;
     return CHELIS_CUDA_OK;
+}
+
+// Destroy the upload / download streams and their events on every device.
+void release_streams() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (int d = 0; d < 64; ++d) {
+        DeviceStreams &ds = g_dev[d];
+        std::lock_guard<std::mutex> lock(ds.lock);
+        if (!ds.ready) continue;
+        cudaSetDevice(d);
+        cudaStreamSynchronize(ds.up);
+        cudaStreamSynchronize(ds.down);
+        cudaStreamDestroy(ds.up);
+        cudaStreamDestroy(ds.down);
+        for (cudaEvent_t e : {ds.ev_start, ds.ev_up, ds.ev_comp, ds.ev_down}) cudaEventDestroy(e);
+        ds = DeviceStreams::Empty();
+    }
+    cudaSetDevice(prev);
 }
 
 // `to` waits for everything enqueued on `from` so far (one reusable event:

@@ -19,8 +19,13 @@ namespace chelis {
 namespace {
 thread_local char t_error[512] = "";
 thread_local cudaStream_t t_stream = nullptr;
+// process defaults, and the calling thread's overrides (-1 = the default)
 std::atomic<int> g_gemm_mode{CHELIS_CUDA_GEMM_3XTF32};
 std::atomic<int> g_rows_mode{CHELIS_CUDA_ROWS_FAST};
+std::atomic<int> g_dgemm_kernel{CHELIS_CUDA_DGEMM_AUTO};
+thread_local int t_gemm_mode = -1;
+thread_local int t_rows_mode = -1;
+thread_local int t_dgemm_kernel = -1;
 int g_sm_count[64] = {0};
 }  // namespace
 
@@ -64,8 +69,10 @@ int sm_count() {
 // mapped (release threshold = unlimited) so repeated calls reuse it instead
 // of re-mapping physical memory at every synchronisation point; the
 // process's default pool is left as it is.
+static cudaMemPool_t g_pools[64] = {};
+
 static int library_pool(cudaMemPool_t *out) {
-    static cudaMemPool_t pools[64] = {};
+    cudaMemPool_t *pools = g_pools;
     int d = 0;
     CHELIS_TRY(check_cuda(cudaGetDevice(&d), "cudaGetDevice"));
     if (d < 0 || d >= 64) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "device index %d", d);
@@ -97,8 +104,46 @@ void scratch_free(void *ptr, cudaStream_t stream) {
     if (ptr) cudaFreeAsync(ptr, stream);
 }
 
-int gemm_mode() { return g_gemm_mode.load(); }
-int rows_mode() { return g_rows_mode.load(); }
+// Destroy the library's pools (each device synchronised first, so every
+// stream-ordered free has happened and the pool's memory goes back).
+int release_pools() {
+    int st = CHELIS_CUDA_OK, prev = 0;
+    cudaGetDevice(&prev);
+    for (int d = 0; d < 64; ++d) {
+        if (!g_pools[d]) continue;
+        cudaSetDevice(d);
+        if (cudaDeviceSynchronize() != cudaSuccess || cudaMemPoolDestroy(g_pools[d]) != cudaSuccess)
+            st = set_error(CHELIS_CUDA_ERR_CUDA, "releasing the scratch pool of device %d failed", d);
+        g_pools[d] = nullptr;
+    }
+    cudaSetDevice(prev);
+    return st;
+}
+
+int gemm_mode() { return t_gemm_mode >= 0 ? t_gemm_mode : g_gemm_mode.load(); }
+int rows_mode() { return t_rows_mode >= 0 ? t_rows_mode : g_rows_mode.load(); }
+int dgemm_kernel_choice() { return t_dgemm_kernel >= 0 ? t_dgemm_kernel : g_dgemm_kernel.load(); }
+
+namespace {
+bool valid_gemm_mode(int m) { return m == CHELIS_CUDA_GEMM_3XTF32 || m == CHELIS_CUDA_GEMM_EXACT_TREE; }
+bool valid_rows_mode(int m) { return m == CHELIS_CUDA_ROWS_EXACT || m == CHELIS_CUDA_ROWS_FAST; }
+bool valid_dgemm_kernel(int m) {
+    return m == CHELIS_CUDA_DGEMM_AUTO || m == CHELIS_CUDA_DGEMM_DMMA || m == CHELIS_CUDA_DGEMM_FFMA;
+}
+// The calling thread's modes for the lifetime of one call.
+struct ThreadModeScope {
+    int g, r, d;
+    ThreadModeScope(int gemm, int dgemm) : g(t_gemm_mode), r(t_rows_mode), d(t_dgemm_kernel) {
+        t_gemm_mode = gemm;
+        if (dgemm >= 0) t_dgemm_kernel = dgemm;
+    }
+    ~ThreadModeScope() {
+        t_gemm_mode = g;
+        t_rows_mode = r;
+        t_dgemm_kernel = d;
+    }
+};
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // strided gather used by clone (one kernel instead of one memcpy per element)
@@ -287,7 +332,7 @@ uint32_t chelis_cuda_get_wait_limit(void) {
 }
 
 int chelis_cuda_set_gemm_mode(int mode) {
-    if (mode != CHELIS_CUDA_GEMM_3XTF32 && mode != CHELIS_CUDA_GEMM_EXACT_TREE)
+    if (!valid_gemm_mode(mode))
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown GEMM mode %d", mode);
     g_gemm_mode.store(mode);
     return CHELIS_CUDA_OK;
@@ -295,12 +340,62 @@ int chelis_cuda_set_gemm_mode(int mode) {
 int chelis_cuda_get_gemm_mode(void) { return g_gemm_mode.load(); }
 
 int chelis_cuda_set_rows_mode(int mode) {
-    if (mode != CHELIS_CUDA_ROWS_EXACT && mode != CHELIS_CUDA_ROWS_FAST)
+    if (!valid_rows_mode(mode))
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown rows mode %d", mode);
     g_rows_mode.store(mode);
     return CHELIS_CUDA_OK;
 }
 int chelis_cuda_get_rows_mode(void) { return g_rows_mode.load(); }
+
+int chelis_cuda_set_dgemm_kernel(int kernel) {
+    if (!valid_dgemm_kernel(kernel))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown f64 GEMM kernel %d", kernel);
+    g_dgemm_kernel.store(kernel);
+    return CHELIS_CUDA_OK;
+}
+int chelis_cuda_get_dgemm_kernel(void) { return g_dgemm_kernel.load(); }
+
+int chelis_cuda_set_thread_modes(int gemm_mode, int rows_mode, int dgemm_kernel) {
+    if ((gemm_mode != -1 && !valid_gemm_mode(gemm_mode)) ||
+        (rows_mode != -1 && !valid_rows_mode(rows_mode)) ||
+        (dgemm_kernel != -1 && !valid_dgemm_kernel(dgemm_kernel)))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown mode (%d, %d, %d)", gemm_mode, rows_mode,
+                         dgemm_kernel);
+    t_gemm_mode = gemm_mode;
+    t_rows_mode = rows_mode;
+    t_dgemm_kernel = dgemm_kernel;
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_get_thread_modes(int *gemm_mode, int *rows_mode, int *dgemm_kernel) {
+    if (gemm_mode) *gemm_mode = chelis::gemm_mode();
+    if (rows_mode) *rows_mode = chelis::rows_mode();
+    if (dgemm_kernel) *dgemm_kernel = chelis::dgemm_kernel_choice();
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_cuda_sgemm_ex(int gemm_mode, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                         const float *a, int64_t lda, int64_t stride_a, const float *b,
+                         int64_t ldb, int64_t stride_b, float *c, int64_t ldc, int64_t stride_c,
+                         int64_t batch) {
+    if (!valid_gemm_mode(gemm_mode))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown GEMM mode %d", gemm_mode);
+    ThreadModeScope scope(gemm_mode, -1);
+    return chelis_cuda_sgemm(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb, stride_b, c,
+                             ldc, stride_c, batch);
+}
+
+int chelis_cuda_dgemm_ex(int gemm_mode, int dgemm_kernel, int trans_a, int trans_b, int64_t m,
+                         int64_t n, int64_t k, const double *a, int64_t lda, int64_t stride_a,
+                         const double *b, int64_t ldb, int64_t stride_b, double *c, int64_t ldc,
+                         int64_t stride_c, int64_t batch) {
+    if (!valid_gemm_mode(gemm_mode) || !valid_dgemm_kernel(dgemm_kernel))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "unknown GEMM mode %d / f64 kernel %d", gemm_mode,
+                         dgemm_kernel);
+    ThreadModeScope scope(gemm_mode, dgemm_kernel);
+    return chelis_cuda_dgemm(trans_a, trans_b, m, n, k, a, lda, stride_a, b, ldb, stride_b, c,
+                             ldc, stride_c, batch);
+}
 
 chelis_device_tensor_owner *chelis_device_tensor_alloc_shape(chelis_dtype dtype, int32_t rank,
                                                              const int64_t *shape) {

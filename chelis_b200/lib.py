@@ -47,6 +47,7 @@ class BlockParams(ctypes.Structure):
 
 DTYPE_F32, DTYPE_F64, DTYPE_I32, DTYPE_BOOL, DTYPE_I64 = 0, 1, 2, 3, 4
 GEMM_3XTF32, GEMM_EXACT_TREE = 0, 1
+DGEMM_AUTO, DGEMM_DMMA, DGEMM_FFMA = 0, 1, 2
 ROWS_EXACT, ROWS_FAST = 0, 1
 STATUS_NAMES = {0: "OK", 1: "DOMAIN", 2: "OVERFLOW", 3: "CUDA", 4: "UNSUPPORTED", 5: "TIMEOUT",
                 6: "NO_DEVICE"}
@@ -58,8 +59,34 @@ class ChelisCudaError(RuntimeError):
         self.status = status
 
 
+class Scalar(ctypes.Structure):
+    """chelis_scalar (crates/chelis-runtime/include/chelis_runtime.h:26)."""
+    _fields_ = [("dtype", ctypes.c_uint8), ("reserved", ctypes.c_uint8 * 7), ("bits", c_u64)]
+
+
+class HostView(ctypes.Structure):
+    """chelis_read_view / chelis_write_view (chelis_runtime_views.h:7-18)."""
+    _fields_ = [("data", c_vp), ("count", c_i64), ("dtype", ctypes.c_uint8),
+                ("reserved", ctypes.c_uint8 * 7)]
+
+
+def tagged_i64(v: int) -> Scalar:
+    """A canonical tagged i64 scalar (the metadata plan's argument form)."""
+    s = Scalar()
+    s.dtype = DTYPE_I64
+    s.bits = v & 0xFFFFFFFFFFFFFFFF
+    return s
+
+
+def exemplar(dtype: int) -> Scalar:
+    s = Scalar()
+    s.dtype = dtype
+    return s
+
+
 _P = ctypes.POINTER(GpuTensor)
 _PP = ctypes.POINTER(c_vp)
+_SP = ctypes.POINTER(Scalar)
 
 # name -> (restype, argtypes); every int-returning entry is a status code.
 SIGNATURES = {
@@ -149,6 +176,58 @@ SIGNATURES = {
     "chelis_chain_grad_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_portfolio_device": (c_int, [_PP, c_i32, _PP, c_i32]),
     "chelis_matmul_device": (c_int, [_PP, c_i32, _PP, c_i32]),
+    # modes, per-call GEMM, shutdown
+    "chelis_cuda_set_dgemm_kernel": (c_int, [c_int]),
+    "chelis_cuda_get_dgemm_kernel": (c_int, []),
+    "chelis_cuda_set_thread_modes": (c_int, [c_int, c_int, c_int]),
+    "chelis_cuda_get_thread_modes": (c_int, [ctypes.POINTER(c_int)] * 3),
+    "chelis_cuda_dgemm_kernel_for": (c_int, [c_int, c_int, c_i64, c_i64, c_i64, c_i64]),
+    "chelis_cuda_shutdown": (c_int, []),
+    "chelis_cuda_sgemm_ex": (c_int, [c_int, c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    "chelis_cuda_dgemm_ex": (c_int, [c_int, c_int, c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    # host runtime subset (include/chelis_host_runtime.h)
+    "chelis_scalar_from_bits": (Scalar, [ctypes.c_uint8, c_u64]),
+    "chelis_dtype_size": (c_i64, [ctypes.c_uint8]),
+    "chelis_metadata_plan_new": (c_vp, [Scalar, _SP, Scalar]),
+    "chelis_metadata_plan_view": (c_vp, [Scalar, _SP, _SP, Scalar, Scalar]),
+    "chelis_metadata_plan_rank": (c_i32, [c_vp]),
+    "chelis_metadata_plan_shape": (ctypes.POINTER(c_i64), [c_vp]),
+    "chelis_metadata_plan_strides": (ctypes.POINTER(c_i64), [c_vp]),
+    "chelis_metadata_plan_count": (c_i64, [c_vp]),
+    "chelis_metadata_plan_byte_count": (c_i64, [c_vp]),
+    "chelis_metadata_plan_byte_offset": (c_i64, [c_vp, Scalar]),
+    "chelis_metadata_plan_dtype": (ctypes.c_uint8, [c_vp]),
+    "chelis_metadata_plan_check_capacity": (None, [c_vp, Scalar]),
+    "chelis_metadata_plan_release": (None, [c_vp]),
+    "chelis_alloc": (c_vp, [c_i32, ctypes.POINTER(c_i64), ctypes.c_uint8]),
+    "chelis_tensor_entry_borrow": (c_vp, [c_i32, ctypes.POINTER(c_i64), ctypes.c_uint8, c_vp, c_i64]),
+    "chelis_tensor_retain": (None, [c_vp]),
+    "chelis_tensor_release": (None, [c_vp]),
+    "chelis_tensor_read_view": (HostView, [c_vp]),
+    "chelis_tensor_begin_write": (c_vp, [c_vp]),
+    "chelis_tensor_write_view": (HostView, [c_vp]),
+    "chelis_tensor_end_write": (None, [c_vp]),
+    "chelis_tensor_rank": (c_i32, [c_vp]),
+    "chelis_tensor_shape": (c_i64, [c_vp, c_i32]),
+    "chelis_tensor_numel": (c_i64, [c_vp]),
+    "chelis_tensor_byte_count": (c_i64, [c_vp]),
+    # device owner under the reference's names, and the host-array entries
+    "chelis_device_tensor_alloc": (c_vp, [c_vp]),
+    "chelis_device_tensor_borrow": (c_vp, [c_vp, c_vp, Scalar]),
+    "chelis_device_tensor_copy_from_host": (None, [c_vp, c_vp]),
+    "chelis_device_tensor_copy_to_host": (None, [c_vp, c_vp]),
+    "chelis_device_tensor_alloc_status": (c_int, [c_vp, _PP]),
+    "chelis_device_tensor_borrow_status": (c_int, [c_vp, c_vp, Scalar, _PP]),
+    "chelis_device_tensor_copy_from_host_status": (c_int, [c_vp, c_vp]),
+    "chelis_device_tensor_copy_to_host_status": (c_int, [c_vp, c_vp]),
+    "chelis_chain_fwd": (None, [_PP, c_int, _PP, c_int]),
+    "chelis_chain_grad": (None, [_PP, c_int, _PP, c_int]),
+    "chelis_portfolio": (None, [_PP, c_int, _PP, c_int]),
+    "chelis_matmul": (None, [_PP, c_int, _PP, c_int]),
+    "chelis_chain_fwd_status": (c_int, [_PP, c_int, _PP, c_int]),
+    "chelis_chain_grad_status": (c_int, [_PP, c_int, _PP, c_int]),
+    "chelis_portfolio_status": (c_int, [_PP, c_int, _PP, c_int]),
+    "chelis_matmul_status": (c_int, [_PP, c_int, _PP, c_int]),
 }
 
 _lib = None

@@ -52,6 +52,16 @@ def gemm_mode(mode: int):
 
 
 @contextlib.contextmanager
+def dgemm_kernel(kernel: int):
+    """f64 GEMM kernel (L.DGEMM_AUTO / _DMMA / _FFMA) for this thread only."""
+    L.call("chelis_cuda_set_thread_modes", -1, -1, kernel)
+    try:
+        yield
+    finally:
+        L.call("chelis_cuda_set_thread_modes", -1, -1, -1)
+
+
+@contextlib.contextmanager
 def gemm_pairs(enable: bool):
     """3xTF32 main kernel on CTA pairs (256 x 256 tiles, the default) or on
     single CTAs (128 x 256 tiles)."""

@@ -84,12 +84,19 @@ enum {
  * contraction, canonical trees); FAST rewrites divisions as reciprocal
  * multiplies (tolerance parity only). */
 enum { CHELIS_CUDA_ROWS_EXACT = 0, CHELIS_CUDA_ROWS_FAST = 1 };
+/* f64 GEMM kernel when the GEMM mode is not EXACT_TREE: the FP64 tensor
+ * path (DMMA) or the CUDA cores' FP64 FMA pipe (FFMA, half DMMA's peak on
+ * B200).  AUTO (default) picks per product: DMMA when its 128 x 128 tiles
+ * number at least the SM count, FFMA (64 x 64 tiles, four times the CTAs)
+ * for smaller products. */
+enum { CHELIS_CUDA_DGEMM_AUTO = 0, CHELIS_CUDA_DGEMM_DMMA = 1, CHELIS_CUDA_DGEMM_FFMA = 2 };
 
 /* =========================================================================
  * Runtime
  * replaces the per-call hiprtc compile + launch helpers
  * (crates/chelis-backend-hip/runtime/chelis_hip_runtime.h:409-485): kernels
- * are compiled ahead of time for sm_100a, so there is nothing to JIT.
+ * are compiled ahead of time for sm_100a, except the per-chain FusedElem
+ * kernels, which NVRTC compiles once per chain and device and caches.
  * ========================================================================= */
 int chelis_cuda_version(void);
 const char *chelis_cuda_last_error(void);
@@ -120,10 +127,30 @@ uint32_t chelis_cuda_get_wait_limit(void);
  * next chelis_cuda_device_status returns CHELIS_CUDA_ERR_TIMEOUT.  The
  * kernel always returns. */
 int chelis_cuda_selftest_bounded_wait(int skip_arrival);
+/* Process-wide default modes (a thread's own setting, below, wins). */
 int chelis_cuda_set_gemm_mode(int mode);
 int chelis_cuda_get_gemm_mode(void);
 int chelis_cuda_set_rows_mode(int mode);
 int chelis_cuda_get_rows_mode(void);
+int chelis_cuda_set_dgemm_kernel(int kernel); /* CHELIS_CUDA_DGEMM_* */
+int chelis_cuda_get_dgemm_kernel(void);
+/* The calling thread's modes (GEMM, rows, f64 kernel; -1 = follow the
+ * process default), so that threads choose exact or fast arithmetic
+ * independently; every entry point on this thread uses them.  _get reports
+ * the modes in force on this thread. */
+int chelis_cuda_set_thread_modes(int gemm_mode, int rows_mode, int dgemm_kernel);
+int chelis_cuda_get_thread_modes(int *gemm_mode, int *rows_mode, int *dgemm_kernel);
+/* The f64 kernel AUTO picks for a product of this shape
+ * (CHELIS_CUDA_DGEMM_DMMA or _FFMA). */
+int chelis_cuda_dgemm_kernel_for(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                                 int64_t batch);
+/* Release what the library created by itself: the scratch memory pools,
+ * the compiled FusedElem kernels, the host-GEMM copy streams, event pools
+ * and the data-parallel communicator (as chelis_cuda_dp_finalize(0)).  The
+ * next call re-creates what it needs.  No other call may run concurrently.
+ * The static scratch array of chelis_cuda_chain_bwd_noalloc belongs to the
+ * loaded library and stays until exit.  Returns the first failure. */
+int chelis_cuda_shutdown(void);
 
 /* =========================================================================
  * Device tensor owner
@@ -205,6 +232,17 @@ int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
 int chelis_cuda_dgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const double *a,
                       int64_t lda, int64_t stride_a, const double *b, int64_t ldb,
                       int64_t stride_b, double *c, int64_t ldc, int64_t stride_c, int64_t batch);
+/* The same products with the arithmetic chosen for this call only
+ * (CHELIS_CUDA_GEMM_* and, for f64, CHELIS_CUDA_DGEMM_*); the thread's and
+ * the process's settings are left as they were. */
+int chelis_cuda_sgemm_ex(int gemm_mode, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                         const float *a, int64_t lda, int64_t stride_a, const float *b,
+                         int64_t ldb, int64_t stride_b, float *c, int64_t ldc, int64_t stride_c,
+                         int64_t batch);
+int chelis_cuda_dgemm_ex(int gemm_mode, int dgemm_kernel, int trans_a, int trans_b, int64_t m,
+                         int64_t n, int64_t k, const double *a, int64_t lda, int64_t stride_a,
+                         const double *b, int64_t ldb, int64_t stride_b, double *c, int64_t ldc,
+                         int64_t stride_c, int64_t batch);
 /* Tile shape of the 3xTF32 main kernel: 1 (default) = 256 x 256 tiles on
  * CTA pairs (tcgen05 cta_group::2) for products with more than 128 rows,
  * 0 = 128 x 256 tiles on single CTAs.  Results are identical in both modes

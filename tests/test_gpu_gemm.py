@@ -283,3 +283,79 @@ def test_sgemm_error_grows_like_an_f32_sum(cuda, orc, m, n, k, ta, tb):
     err_blas = np.abs(blas - ref).max() / np.abs(ref).max()
     assert err <= 1e-5, (err, err_blas)
     assert err <= max(3.0 * err_blas, 2e-6), (err, err_blas)
+
+
+F64_KERNEL_SHAPES = [(1, 1, 1), (17, 33, 45), (64, 8, 4096), (300, 500, 700), (512, 512, 512),
+                     (129, 257, 1000), (1024, 1024, 256), (2048, 1536, 512)]
+
+
+@pytest.mark.parametrize("kernel", [L.DGEMM_DMMA, L.DGEMM_FFMA, L.DGEMM_AUTO])
+@pytest.mark.parametrize("m,n,k", F64_KERNEL_SHAPES)
+def test_dgemm_kernels_match_oracle(cuda, orc, kernel, m, n, k):
+    """DMMA, FFMA and the per-shape choice all meet f64 rel <= 1e-12."""
+    import torch
+    a, b = W.gemm_inputs(m, n, k, np.float64, seed=m + 7 * n + k)
+    with cuda.dgemm_kernel(kernel):
+        c = cuda.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()).cpu().numpy()
+    assert _rel_err(c, orc.gemm(a, b), a, b) <= 1e-12
+
+
+@pytest.mark.parametrize("kernel", [L.DGEMM_DMMA, L.DGEMM_FFMA])
+@pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
+def test_dgemm_kernels_transposed_batched(cuda, orc, kernel, ta, tb):
+    import torch
+    a, b = W.gemm_inputs(70, 90, 131, np.float64, seed=9, batch=3)
+    A = a.transpose(0, 2, 1).copy() if ta else a
+    B = b.transpose(0, 2, 1).copy() if tb else b
+    with cuda.dgemm_kernel(kernel):
+        c = cuda.matmul(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), ta, tb).cpu().numpy()
+    for i in range(3):
+        assert _rel_err(c[i], orc.gemm(a[i], b[i]), a[i], b[i]) <= 1e-12
+
+
+def test_dgemm_per_call_and_thread_modes(cuda, orc):
+    """chelis_cuda_dgemm_ex / _sgemm_ex choose the arithmetic for one call and
+    leave the thread's and the process's settings alone; the thread setting
+    is the thread's own."""
+    import ctypes
+    import threading
+    import torch
+    lib = L.load()
+    a, b = W.gemm_inputs(40, 60, 300, np.float64, seed=5)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    C = torch.empty(40, 60, dtype=torch.float64, device="cuda")
+    L.call("chelis_cuda_dgemm_ex", L.GEMM_EXACT_TREE, L.DGEMM_AUTO, 0, 0, 40, 60, 300, A.data_ptr(),
+           300, 0, B.data_ptr(), 60, 0, C.data_ptr(), 60, 0, 1)
+    assert (C.cpu().numpy().view(np.uint64) == orc.gemm(a, b).view(np.uint64)).all()
+    assert lib.chelis_cuda_get_gemm_mode() == L.GEMM_3XTF32
+    g = ctypes.c_int()
+    L.call("chelis_cuda_get_thread_modes", ctypes.byref(g), None, None)
+    assert g.value == L.GEMM_3XTF32
+    seen = {}
+
+    def other():
+        L.call("chelis_cuda_set_thread_modes", L.GEMM_EXACT_TREE, -1, -1)
+        v = ctypes.c_int()
+        L.call("chelis_cuda_get_thread_modes", ctypes.byref(v), None, None)
+        seen["other"] = v.value
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    L.call("chelis_cuda_get_thread_modes", ctypes.byref(g), None, None)
+    assert seen["other"] == L.GEMM_EXACT_TREE and g.value == L.GEMM_3XTF32
+    assert lib.chelis_cuda_dgemm_kernel_for(0, 0, 8192, 8192, 8192, 1) == L.DGEMM_DMMA
+    assert lib.chelis_cuda_dgemm_kernel_for(0, 0, 512, 512, 512, 1) == L.DGEMM_FFMA
+    assert lib.chelis_cuda_dgemm_kernel_for(1, 0, 8192, 8192, 8192, 1) == L.DGEMM_DMMA
+    assert lib.chelis_cuda_dgemm_kernel_for(0, 0, 256, 256, 4096, 1) == L.DGEMM_FFMA
+
+
+def test_shutdown_releases_and_library_recovers(cuda, orc):
+    import torch
+    a, b = W.gemm_inputs(256, 384, 320, np.float32, seed=3)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    c1 = cuda.matmul(A, B).cpu().numpy()
+    torch.cuda.synchronize()
+    L.call("chelis_cuda_shutdown")
+    c2 = cuda.matmul(A, B).cpu().numpy()
+    assert (c1.view(np.uint32) == c2.view(np.uint32)).all()
