@@ -821,10 +821,36 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
 #pragma unroll
         for (int i = 0; i < DH / 2; ++i) dk_acc[i] = dv_acc[i] = 0.0f;
         bool ok = true;
+        // Block n's dK / dV contributions are folded into f32 registers
+        // (rounded additions; each block is 12 tensor-core accumulations)
+        // after the rows have turned block n + 1's scores into P and dS, so
+        // the gradient MMAs of block n run while the rows work on block n + 1.
+        // The accumulators are reused by block n + 1's gradient MMAs, which
+        // wait for this thread's p_full arrival of block n + 1: the fold of
+        // block n comes before that arrival.
+        // (every wait's outcome is made warp-uniform, so the warp's lanes
+        // stay converged for the shuffles and __syncwarp below)
+        auto fold_block = [&](int n) -> bool {
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(acc_full, n & 1, DEVERR_TIMEOUT_EPILOGUE)))
+                return false;
+            tc_fence_after();
+            add_row_half<DH>(dk_acc, tm + lane_base + C::C_DK + half * (DH / 2));
+            add_row_half<DH>(dv_acc, tm + lane_base + C::C_DV + half * (DH / 2));
+            tc_fence_before();
+            return true;
+        };
         for (int n = 0; n < nblk; ++n) {
             const int s = n & 1;
             const uint32_t buf = tm + lane_base + C::C_BUF + s * C::BUF;
-            if (*abort_flag || !mbar_wait_bounded(&s_full[s], (n >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+            // this half's 16 queries: lane c < 16 holds lse, lane 16 + c dsum
+            // of query qb0 + c (one load per lane, issued before the wait)
+            const int qb0 = (i0 + n) * BQ2 + half * 16;
+            const int ql = qb0 + (lane & 15);
+            const int qlc = ql < p.seq ? ql : p.seq - 1;
+            const float stat = lane < 16 ? __fmul_rn(lse[qlc], 1.4426950408889634f) : dsum[qlc];
+            const bool go = !*abort_flag &&
+                            mbar_wait_bounded(&s_full[s], (n >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE);
+            if (!__all_sync(0xffffffffu, go)) {
                 *abort_flag = 1;
                 ok = false;
                 break;
@@ -834,16 +860,15 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
             tmem_ld_32x32b_x16(buf + C::O_ST + half * 16, sv);
             tmem_ld_32x32b_x16(buf + C::O_DPT + half * 16, dv);
             tmem_wait_ld();
-            const int qb0 = (i0 + n) * BQ2 + half * 16;
             uint32_t ph[16], pl[16], dh[16], dl[16];
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 const int qi = qb0 + c;
                 const bool valid = live && key <= qi && qi < p.seq;
-                const int qc = qi < p.seq ? qi : p.seq - 1;
-                const float L2 = __fmul_rn(lse[qc], 1.4426950408889634f);
+                const float L2 = __shfl_sync(0xffffffffu, stat, c);
+                const float Dq = __shfl_sync(0xffffffffu, stat, 16 + c);
                 const float pr = valid ? ex2_approx(__fsub_rn(__fmul_rn(__uint_as_float(sv[c]), c2), L2)) : 0.0f;
-                const float ds = __fmul_rn(__fmul_rn(pr, __fsub_rn(__uint_as_float(dv[c]), dsum[qc])), p.scale);
+                const float ds = __fmul_rn(__fmul_rn(pr, __fsub_rn(__uint_as_float(dv[c]), Dq)), p.scale);
                 split_tf32(pr, ph[c], pl[c]);
                 split_tf32(ds, dh[c], dl[c]);
             }
@@ -853,21 +878,20 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
             tmem_st_32x32b_x16(buf + C::O_DSLO + half * 16, dl);
             tmem_wait_st();
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[s]);
-            // this block's dK, dV contributions -> f32 registers (rounded
-            // additions; the block itself is 12 tensor-core accumulations).
-            // The next block's dK / dV MMAs wait for this thread's next
-            // p_full arrival, so the accumulators are read before reuse.
-            if (!mbar_wait_bounded(acc_full, n & 1, DEVERR_TIMEOUT_EPILOGUE)) {
+            if (n > 0 && !fold_block(n - 1)) {
                 *abort_flag = 1;
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            add_row_half<DH>(dk_acc, tm + lane_base + C::C_DK + half * (DH / 2));
-            add_row_half<DH>(dv_acc, tm + lane_base + C::C_DV + half * (DH / 2));
-            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[s]);
+        }
+        if (ok && nblk > 0) {
+            const bool aborted = __any_sync(0xffffffffu, *abort_flag != 0);
+            if (aborted || !fold_block(nblk - 1)) {
+                *abort_flag = 1;
+                ok = false;
+            }
         }
         if (ok && !*abort_flag && live) {
             const int64_t g = b * p.g_b + h * p.g_h + static_cast<int64_t>(key) * p.g_row +

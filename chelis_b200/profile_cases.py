@@ -5,8 +5,11 @@
     python -m chelis_b200.profile_cases chain       # config 3 forward (saving state) + adjoint
     python -m chelis_b200.profile_cases portfolio   # config 5, 4096 portfolios
     python -m chelis_b200.profile_cases block       # config 4 step, batch 1
+    python -m chelis_b200.profile_cases block8      # config 4 step at the headline batch of 8
+                                                    # (launch lists only: one metric, one pass)
     python -m chelis_b200.profile_cases attention   # config 4 attention, 8 x 16 heads x 2048 x 64,
                                                     # fused forward + reverse mode
+    python -m chelis_b200.profile_cases attention16 # the same kernels on 16 heads (one batch item)
     python -m chelis_b200.profile_cases fused       # generic FusedElem groups on 16384 x 4096 f32:
                                                     # x*gamma+beta, then sum of squares per row
 
@@ -42,9 +45,13 @@ def run(case: str) -> None:
     elif case == "block":
         x, dy, w = W.torch_block_inputs(**dict(W.BLOCK_SHAPE, batch=1))
         ops.block_step(x, w, W.BLOCK_SHAPE["heads"], 1e-5, dy)
-    elif case == "attention":
+    elif case == "block8":
+        x, dy, w = W.torch_block_inputs(**W.BLOCK_SHAPE)
+        ops.block_step(x, w, W.BLOCK_SHAPE["heads"], 1e-5, dy)
+    elif case in ("attention", "attention16"):
+        bh = 128 if case == "attention" else 16
         g = torch.Generator(device="cuda").manual_seed(3)
-        q, k, v, do = (torch.randn(128, 2048, 64, device="cuda", generator=g) for _ in range(4))
+        q, k, v, do = (torch.randn(bh, 2048, 64, device="cuda", generator=g) for _ in range(4))
         o, lse = ops.attention_causal(q, k, v, 0.125, with_lse=True)
         ops.attention_causal_bwd(q, k, v, o, lse, do, 0.125)
     elif case == "fused":
