@@ -1,0 +1,1644 @@
+// dag.cu -- executes a serialized Chelis DAG on the GPU.
+//
+// The reference turns a verified DAG into C++ source per program
+// (crates/chelis-backend-hip/src/emit.rs: emit_dag :488, the host entry
+// :660-800, the device entry :838-958) with a storage plan fixed at compile
+// time (src/memory.rs:39-98, MemoryPlan::from_shared: input mirrors, owned
+// slots reused after their last use, metadata views, terminal drops, store
+// aliases; the peak-bytes figure of src/lib.rs:47-53).  Here the same DAG,
+// as the JSON serde writes for crates/chelis-dag-core's `Dag`
+// (dag.rs:2364-2400, 2913-2920), is read at run time, checked, planned once
+// (placements, slot reuse, arena bytes) and executed node by node with this
+// library's kernels:
+//
+//   Load                  input owner (a view; no copy)
+//   Const / ConstTensor   filled slot
+//   Add..MinElem, Neg..Round, FusedElem
+//                         chelis_cuda_fused_elementwise (one kernel per
+//                         node; Expand / Permute / Shrink / Stride views
+//                         become per-input strides, stride 0 broadcasts)
+//   Sum / MaxReduce       chelis_cuda_fused_reduce; a FusedElem whose one
+//                         consumer is the reduction is inlined into it
+//                         (fuse.rs:463-500 reduction_inlined_fused_elems)
+//   BlasMatmul            chelis_cuda_sgemm / _dgemm; a transposing Permute
+//                         view of a dense operand becomes trans_a / trans_b
+//   Relu, ReluAdjoint, Softmax (last axis), Count, Cumsum (last axis)
+//                         the dedicated kernels
+//   Gather, ScatterAdd    index kernels ([05-OP-52]; bad indices set the
+//                         device error word: "numeric trap: domain in gather")
+//   Reshape, Permute, Expand, Shrink, Stride, Store
+//                         metadata views (a Reshape of a non-dense view is
+//                         materialised first)
+//   Pad, Cast, Copy, Realize
+//                         materialising kernels;  Drop: nothing
+//
+// Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
+// bound in first-Load order and outputs are the Store nodes then the roots
+// (emit.rs:5881-5934).  Outputs come back as new device owners.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "chelis_dag.h"
+#include "common.cuh"
+#include "dag_json.cuh"
+
+namespace chelis {
+int dtype_width(chelis_dtype dt);
+
+namespace dag {
+
+constexpr int kMaxRank = 8;
+
+enum class Op {
+    Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
+    Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
+    Copy, Drop, Store
+};
+
+struct Node {
+    Op op = Op::Drop;
+    std::string opname;
+    std::vector<int> in;
+    chelis_dtype dtype = 0;
+    std::vector<int64_t> shape;
+    std::vector<chelis_fused_step> steps;  // Elementwise (one step) / Fused
+    int axis = 0, batch_rank = 0;
+    bool reverse = false;
+    std::vector<int> axes;                             // Permute
+    std::vector<std::pair<int64_t, int64_t>> bounds;   // Shrink (start, end) / Pad (before, after)
+    std::vector<int64_t> step;                         // Stride
+    uint64_t bits = 0;                                 // Const / Pad fill value
+    std::vector<uint8_t> data;                         // ConstTensor payload
+    std::string name;                                  // Load / Store
+    int accumulator = -1;                              // Sum / BlasMatmul
+};
+
+// Static layout of a node's value: elements at root storage + offset +
+// sum(coord * stride).
+struct Layout {
+    int root = -1;  // node owning the storage (a Load, a slot node, or itself)
+    int64_t offset = 0;
+    std::vector<int64_t> strides;
+};
+
+enum class Place { Input, View, Slot, Output, Skip, Inlined };
+
+struct Program {
+    std::vector<Node> nodes;
+    std::vector<Layout> layout;
+    std::vector<Place> place;
+    std::vector<int> slot;        // Slot: slot index; Output: output index
+    std::vector<int64_t> slot_off;  // byte offset of each slot in the arena
+    std::vector<int64_t> slot_cap;
+    int64_t arena_bytes = 0;
+    int64_t live_peak_bytes = 0;
+    std::vector<std::string> input_labels;
+    std::vector<int> input_of_load;  // node -> input slot (Loads), -1 otherwise
+    std::vector<std::string> output_labels;
+    std::vector<int> output_node;    // the node whose value is the output
+    std::vector<int> direct_output;  // node -> output index when it writes into the owner
+};
+
+int64_t count_of(const std::vector<int64_t> &shape) {
+    int64_t c = 1;
+    for (int64_t e : shape) c *= e;
+    return c;
+}
+
+std::vector<int64_t> dense_strides(const std::vector<int64_t> &shape) {
+    std::vector<int64_t> st(shape.size(), 1);
+    int64_t run = 1;
+    for (int d = static_cast<int>(shape.size()) - 1; d >= 0; --d) {
+        st[d] = run;
+        run *= shape[d];
+    }
+    return st;
+}
+
+bool is_dense(const std::vector<int64_t> &shape, const std::vector<int64_t> &strides) {
+    int64_t run = 1;
+    for (int d = static_cast<int>(shape.size()) - 1; d >= 0; --d) {
+        if (shape[d] != 1 && strides[d] != run) return false;
+        run *= shape[d];
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- parsing
+
+int bad(const char *what, const std::string &detail = std::string()) {
+    return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: %s%s%s", what, detail.empty() ? "" : ": ",
+                     detail.c_str());
+}
+int unsupported(const std::string &what) {
+    return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "dag: %s is not supported by the CUDA lane",
+                     what.c_str());
+}
+
+// Prim (crates/chelis-numeric-core/src/prim.rs:14-37, serde variant names)
+int prim_dtype(const std::string &p) {
+    if (p == "F32") return CHELIS_DTYPE_F32;
+    if (p == "F64") return CHELIS_DTYPE_F64;
+    if (p == "Int32") return CHELIS_DTYPE_I32;
+    if (p == "Bool") return CHELIS_DTYPE_BOOL;
+    if (p == "Int64") return CHELIS_DTYPE_I64;
+    if (p == "Bf16") return CHELIS_DTYPE_BF16;
+    if (p == "F16") return CHELIS_DTYPE_F16;
+    if (p == "Int8") return CHELIS_DTYPE_I8;
+    if (p == "Int16") return CHELIS_DTYPE_I16;
+    if (p == "Key") return CHELIS_DTYPE_KEY;
+    return -1;
+}
+// scalar / tensor payload dtype names (wire_codec.rs: "f32", "int64", ...)
+int wire_dtype(const std::string &p) {
+    if (p == "f32") return CHELIS_DTYPE_F32;
+    if (p == "f64") return CHELIS_DTYPE_F64;
+    if (p == "int32") return CHELIS_DTYPE_I32;
+    if (p == "bool") return CHELIS_DTYPE_BOOL;
+    if (p == "int64") return CHELIS_DTYPE_I64;
+    if (p == "bf16") return CHELIS_DTYPE_BF16;
+    if (p == "f16") return CHELIS_DTYPE_F16;
+    if (p == "int8") return CHELIS_DTYPE_I8;
+    if (p == "int16") return CHELIS_DTYPE_I16;
+    return -1;
+}
+
+bool as_index(const json::Value *v, int64_t *out) {
+    if (!v || v->kind != json::Value::Int || v->i < 0) return false;
+    *out = v->i;
+    return true;
+}
+
+// the single key of an externally tagged enum value ({"Lit": 3})
+const json::Value *variant(const json::Value &v, const char *name) {
+    if (v.kind != json::Value::Obj || v.o.size() != 1 || v.o[0].first != name) return nullptr;
+    return &v.o[0].second;
+}
+
+// A static extent: DimInfo::Lit(n), DimInfo::Named(_, Some(n)), DimExpr /
+// RtDim literals ({"Lit": n}, {"Concrete": n}).
+bool static_extent(const json::Value &v, int64_t *out) {
+    if (const json::Value *l = variant(v, "Lit")) return as_index(l, out);
+    if (const json::Value *c = variant(v, "Concrete")) return as_index(c, out);
+    if (const json::Value *nm = variant(v, "Named")) {
+        if (nm->kind == json::Value::Arr && nm->a.size() == 2) return as_index(&nm->a[1], out);
+    }
+    return false;
+}
+
+int hex_bits(const json::Value *v, size_t digits, uint64_t *out) {
+    if (!v || v->kind != json::Value::Str || v->s.size() != digits) return bad("bad hex bits");
+    uint64_t b = 0;
+    for (char c : v->s) {
+        int h = (c >= '0' && c <= '9') ? c - '0' : (c >= 'a' && c <= 'f') ? c - 'a' + 10 : -1;
+        if (h < 0) return bad("bad hex bits");
+        b = (b << 4) | static_cast<uint64_t>(h);
+    }
+    *out = b;
+    return CHELIS_CUDA_OK;
+}
+
+// ScalarValue wire form (wire_codec.rs:488-530): {"dtype": .., "bits"|"value": ..}
+int scalar(const json::Value *v, int *dtype, uint64_t *bits) {
+    if (!v || v->kind != json::Value::Obj) return bad("scalar payload expected");
+    const json::Value *d = v->get("dtype");
+    if (!d || d->kind != json::Value::Str || (*dtype = wire_dtype(d->s)) < 0)
+        return bad("scalar dtype");
+    switch (*dtype) {
+        case CHELIS_DTYPE_F64: return hex_bits(v->get("bits"), 16, bits);
+        case CHELIS_DTYPE_F32: return hex_bits(v->get("bits"), 8, bits);
+        case CHELIS_DTYPE_F16: case CHELIS_DTYPE_BF16: return hex_bits(v->get("bits"), 4, bits);
+        case CHELIS_DTYPE_BOOL: {
+            const json::Value *b = v->get("value");
+            if (!b || b->kind != json::Value::Bool) return bad("bool scalar");
+            *bits = b->b ? 1 : 0;
+            return CHELIS_CUDA_OK;
+        }
+        default: {
+            const json::Value *i = v->get("value");
+            if (!i || i->kind != json::Value::Int) return bad("integer scalar");
+            *bits = static_cast<uint64_t>(i->i);
+            return CHELIS_CUDA_OK;
+        }
+    }
+}
+
+// TensorStorage wire form: {"dtype": .., "bits": [hex..]} / {"dtype": .., "values": [..]}
+int tensor_payload(const json::Value *v, int *dtype, std::vector<uint8_t> *out) {
+    if (!v || v->kind != json::Value::Obj) return bad("tensor payload expected");
+    const json::Value *d = v->get("dtype");
+    if (!d || d->kind != json::Value::Str || (*dtype = wire_dtype(d->s)) < 0)
+        return bad("tensor payload dtype");
+    const int w = dtype_width(static_cast<chelis_dtype>(*dtype));
+    const bool floaty = *dtype == CHELIS_DTYPE_F32 || *dtype == CHELIS_DTYPE_F64 ||
+                        *dtype == CHELIS_DTYPE_F16 || *dtype == CHELIS_DTYPE_BF16;
+    const json::Value *arr = v->get(floaty ? "bits" : "values");
+    if (!arr || arr->kind != json::Value::Arr) return bad("tensor payload values");
+    out->resize(arr->a.size() * static_cast<size_t>(w));
+    for (size_t i = 0; i < arr->a.size(); ++i) {
+        uint64_t b = 0;
+        if (floaty) {
+            CHELIS_TRY(hex_bits(&arr->a[i], static_cast<size_t>(2 * w), &b));
+        } else if (*dtype == CHELIS_DTYPE_BOOL) {
+            if (arr->a[i].kind != json::Value::Bool) return bad("bool payload");
+            b = arr->a[i].b;
+        } else {
+            if (arr->a[i].kind != json::Value::Int) return bad("integer payload");
+            b = static_cast<uint64_t>(arr->a[i].i);
+        }
+        std::memcpy(out->data() + i * w, &b, static_cast<size_t>(w));  // little-endian low bytes
+    }
+    return CHELIS_CUDA_OK;
+}
+
+// FusedStepOp (dag.rs:494-526) / binary and unary RiscOps -> step code
+int fused_code(const std::string &n) {
+    static const char *names[] = {"Add", "Sub", "Mul", "Div", "Pow", "FloorDiv", "TruncDiv",
+                                  "MaxElem", "MinElem", "Neg", "Recip", "Exp", "Log", "Sin",
+                                  "Sqrt", "Cos", "Tan", "Atan", "Tanh", "Erf", "Erfc", "Abs",
+                                  "Floor", "Ceil", "Round"};
+    for (int i = 0; i < 25; ++i)
+        if (n == names[i]) return i;
+    return -1;
+}
+
+int fused_operand(const json::Value &v, int32_t *out) {
+    int64_t i = 0;
+    if (const json::Value *e = variant(v, "External")) {
+        if (!as_index(e, &i)) return bad("fused operand");
+        *out = static_cast<int32_t>(i);
+        return CHELIS_CUDA_OK;
+    }
+    if (const json::Value *p = variant(v, "PreviousStep")) {
+        if (!as_index(p, &i)) return bad("fused operand");
+        *out = -1 - static_cast<int32_t>(i);
+        return CHELIS_CUDA_OK;
+    }
+    return bad("fused operand");
+}
+
+int axis_list(const json::Value *v, std::vector<int> *out) {
+    if (!v || v->kind != json::Value::Arr) return bad("axis list");
+    for (const auto &e : v->a) {
+        int64_t a = 0;
+        if (!as_index(&e, &a)) return bad("axis list");
+        out->push_back(static_cast<int>(a));
+    }
+    return CHELIS_CUDA_OK;
+}
+
+int bound_pairs(const json::Value *v, std::vector<std::pair<int64_t, int64_t>> *out,
+                const std::vector<int64_t> &input_shape, bool shrink) {
+    if (!v || v->kind != json::Value::Arr) return bad("bounds");
+    for (size_t d = 0; d < v->a.size(); ++d) {
+        const json::Value &p = v->a[d];
+        if (p.kind != json::Value::Arr || p.a.size() != 2) return bad("bounds");
+        int64_t lo = 0, hi = 0;
+        if (!static_extent(p.a[0], &lo)) return unsupported("a runtime bound");
+        if (shrink && p.a[1].kind == json::Value::Str && p.a[1].s == "ToEnd") {
+            if (d >= input_shape.size()) return bad("bounds rank");
+            hi = input_shape[d];
+        } else if (!static_extent(p.a[1], &hi)) {
+            return unsupported("a runtime bound");
+        }
+        out->emplace_back(lo, hi);
+    }
+    return CHELIS_CUDA_OK;
+}
+
+int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
+    Node n;
+    int64_t id = -1;
+    if (!as_index(jn.get("id"), &id) || id != static_cast<int64_t>(index))
+        return bad("node ids must be 0..n-1 in order");
+    const json::Value *inputs = jn.get("inputs");
+    if (!inputs || inputs->kind != json::Value::Arr) return bad("node inputs");
+    for (const auto &e : inputs->a) {
+        int64_t i = 0;
+        if (!as_index(&e, &i) || i >= id) return bad("inputs must name earlier nodes");
+        n.in.push_back(static_cast<int>(i));
+    }
+    const json::Value *ty = jn.get("output_type");
+    const json::Value *dims = ty ? ty->get("dims") : nullptr;
+    const json::Value *prec = ty ? ty->get("precision") : nullptr;
+    if (!dims || dims->kind != json::Value::Arr || !prec || prec->kind != json::Value::Str)
+        return bad("output_type");
+    const int dt = prim_dtype(prec->s);
+    if (dt < 0 || dt == CHELIS_DTYPE_KEY) return unsupported("precision " + prec->s);
+    n.dtype = static_cast<chelis_dtype>(dt);
+    for (const auto &d : dims->a) {
+        int64_t e = 0;
+        if (!static_extent(d, &e)) return unsupported("a symbolic extent");
+        n.shape.push_back(e);
+    }
+    if (n.shape.size() > static_cast<size_t>(kMaxRank)) return unsupported("rank above 8");
+
+    const json::Value *op = jn.get("op");
+    if (!op) return bad("node op");
+    std::string name;
+    const json::Value *body = nullptr;
+    if (op->kind == json::Value::Str) {
+        name = op->s;
+    } else if (op->kind == json::Value::Obj && op->o.size() == 1) {
+        name = op->o[0].first;
+        body = &op->o[0].second;
+    } else {
+        return bad("node op");
+    }
+    n.opname = name;
+    auto in_shape = [&](int k) -> const std::vector<int64_t> & { return nodes[n.in[k]].shape; };
+    auto need_inputs = [&](size_t k) {
+        return n.in.size() == k ? CHELIS_CUDA_OK : bad("wrong input count for", name);
+    };
+    auto field = [&](const char *f) -> const json::Value * { return body ? body->get(f) : nullptr; };
+    int64_t v = 0;
+    const int code = fused_code(name);
+    if (name == "Load") {
+        n.op = Op::Load;
+        const json::Value *nm = field("name");
+        if (!nm || nm->kind != json::Value::Str) return bad("Load name");
+        n.name = nm->s;
+        CHELIS_TRY(need_inputs(0));
+    } else if (name == "Store") {
+        n.op = Op::Store;
+        const json::Value *nm = field("name");
+        if (!nm || nm->kind != json::Value::Str) return bad("Store name");
+        n.name = nm->s;
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "Const") {
+        n.op = Op::Const;
+        int sdt = 0;
+        CHELIS_TRY(scalar(field("value"), &sdt, &n.bits));
+        if (sdt != n.dtype) return bad("Const value dtype differs from the node's precision");
+    } else if (name == "ConstTensor") {
+        n.op = Op::ConstTensor;
+        int sdt = 0;
+        CHELIS_TRY(tensor_payload(field("data"), &sdt, &n.data));
+        if (sdt != n.dtype ||
+            static_cast<int64_t>(n.data.size()) != count_of(n.shape) * dtype_width(n.dtype))
+            return bad("ConstTensor payload does not match the node's type");
+    } else if (code >= 0 && name != "TruncDiv") {
+        n.op = Op::Elementwise;
+        const bool binary = code <= CHELIS_FUSED_MIN_ELEM;
+        CHELIS_TRY(need_inputs(binary ? 2 : 1));
+        n.steps.push_back({code, 0, binary ? 1 : 0});
+    } else if (name == "FusedElem") {
+        n.op = Op::Fused;
+        const json::Value *ops = field("ops");
+        if (!ops || ops->kind != json::Value::Arr || ops->a.empty()) return bad("FusedElem ops");
+        for (const auto &st : ops->a) {
+            const json::Value *o = st.get("op");
+            const json::Value *ii = st.get("input_indices");
+            if (!o || o->kind != json::Value::Str || !ii || ii->kind != json::Value::Arr ||
+                ii->a.empty())
+                return bad("FusedElem step");
+            chelis_fused_step s{fused_code(o->s), 0, 0};
+            if (s.op < 0) return bad("FusedElem step op", o->s);
+            CHELIS_TRY(fused_operand(ii->a[0], &s.a));
+            s.b = s.a;
+            if (ii->a.size() > 1) CHELIS_TRY(fused_operand(ii->a[1], &s.b));
+            n.steps.push_back(s);
+        }
+    } else if (name == "Relu") {
+        n.op = Op::Relu;
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "ReluAdjoint") {
+        n.op = Op::ReluAdjoint;
+        CHELIS_TRY(need_inputs(2));
+    } else if (name == "Softmax") {
+        n.op = Op::Softmax;
+        CHELIS_TRY(need_inputs(1));
+        if (!as_index(field("axis"), &v)) return bad("Softmax axis");
+        n.axis = static_cast<int>(v);
+    } else if (name == "Sum" || name == "MaxReduce") {
+        n.op = name == "Sum" ? Op::Sum : Op::MaxReduce;
+        CHELIS_TRY(need_inputs(1));
+        if (!as_index(field("axis"), &v)) return bad("reduction axis");
+        n.axis = static_cast<int>(v);
+        if (n.op == Op::Sum) {
+            const json::Value *acc = field("accumulator");
+            if (!acc || acc->kind != json::Value::Str || prim_dtype(acc->s) < 0)
+                return bad("Sum accumulator");
+            n.accumulator = prim_dtype(acc->s);
+        }
+    } else if (name == "Count") {
+        n.op = Op::Count;
+        CHELIS_TRY(need_inputs(1));
+        CHELIS_TRY(axis_list(field("axes"), &n.axes));
+    } else if (name == "BlasMatmul") {
+        n.op = Op::Matmul;
+        CHELIS_TRY(need_inputs(2));
+        const json::Value *acc = field("accumulator");
+        if (!acc || acc->kind != json::Value::Str || prim_dtype(acc->s) < 0)
+            return bad("BlasMatmul accumulator");
+        n.accumulator = prim_dtype(acc->s);
+    } else if (name == "Gather" || name == "ScatterAdd") {
+        n.op = name == "Gather" ? Op::Gather : Op::ScatterAdd;
+        CHELIS_TRY(need_inputs(n.op == Op::Gather ? 2 : 3));
+        int64_t br = 0;
+        if (!as_index(field("axis"), &v) || !as_index(field("batch_rank"), &br))
+            return bad("Gather / ScatterAdd fields");
+        n.axis = static_cast<int>(v);
+        n.batch_rank = static_cast<int>(br);
+    } else if (name == "Cumsum") {
+        n.op = Op::Cumsum;
+        CHELIS_TRY(need_inputs(1));
+        const json::Value *dir = field("direction");
+        if (!as_index(field("axis"), &v) || !dir || dir->kind != json::Value::Str)
+            return bad("Cumsum fields");
+        n.axis = static_cast<int>(v);
+        if (dir->s != "Increasing" && dir->s != "Decreasing") return bad("Cumsum direction");
+        n.reverse = dir->s == "Decreasing";
+    } else if (name == "Reshape") {
+        n.op = Op::Reshape;
+        if (n.in.empty()) return bad("Reshape input");
+    } else if (name == "Permute") {
+        n.op = Op::Permute;
+        CHELIS_TRY(need_inputs(1));
+        CHELIS_TRY(axis_list(field("axes"), &n.axes));
+    } else if (name == "Expand") {
+        n.op = Op::Expand;
+        if (n.in.empty()) return bad("Expand input");
+        if (!as_index(field("axis"), &v)) return bad("Expand axis");
+        n.axis = static_cast<int>(v);
+    } else if (name == "Shrink") {
+        n.op = Op::Shrink;
+        if (n.in.empty()) return bad("Shrink input");
+        CHELIS_TRY(bound_pairs(field("bounds"), &n.bounds, in_shape(0), true));
+    } else if (name == "Stride") {
+        n.op = Op::Stride;
+        if (n.in.empty()) return bad("Stride input");
+        const json::Value *st = field("strides");
+        if (!st || st->kind != json::Value::Arr) return bad("Stride strides");
+        for (const auto &e : st->a) {
+            int64_t s = 0;
+            if (!static_extent(e, &s) || s < 1) return unsupported("a runtime stride");
+            n.step.push_back(s);
+        }
+    } else if (name == "Pad") {
+        n.op = Op::Pad;
+        if (n.in.empty()) return bad("Pad input");
+        CHELIS_TRY(bound_pairs(field("padding"), &n.bounds, in_shape(0), false));
+        int fdt = 0;
+        CHELIS_TRY(scalar(field("fill"), &fdt, &n.bits));
+        if (fdt != n.dtype) return bad("Pad fill dtype");
+    } else if (name == "Cast") {
+        n.op = Op::Cast;
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "Copy" || name == "Realize") {
+        n.op = Op::Copy;
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "Drop") {
+        n.op = Op::Drop;
+    } else {
+        return unsupported("RiscOp::" + name);
+    }
+    nodes.push_back(std::move(n));
+    return CHELIS_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- checking
+
+int check_same_shape(const Node &n, const Node &src, const char *what) {
+    if (src.shape != n.shape) return bad(what, "operand shape differs from the node's");
+    return CHELIS_CUDA_OK;
+}
+
+// Shapes and dtypes of each node against its operands; layouts of views.
+int check_and_layout(Program &P) {
+    std::vector<Node> &N = P.nodes;
+    const int count = static_cast<int>(N.size());
+    P.layout.assign(count, Layout());
+    for (int i = 0; i < count; ++i) {
+        Node &n = N[i];
+        Layout &L = P.layout[i];
+        auto src = [&](int k) -> const Node & { return N[n.in[k]]; };
+        auto own = [&] {
+            L.root = i;
+            L.offset = 0;
+            L.strides = dense_strides(n.shape);
+        };
+        const bool floating = n.dtype == CHELIS_DTYPE_F32 || n.dtype == CHELIS_DTYPE_F64;
+        switch (n.op) {
+            case Op::Load: case Op::Const: case Op::ConstTensor: case Op::Drop: own(); break;
+            case Op::Elementwise: case Op::Fused:
+                if (!floating) return unsupported(n.opname + " on a non-float precision");
+                for (size_t k = 0; k < n.in.size(); ++k) {
+                    if (src(k).dtype != n.dtype) return bad("elementwise operand dtype", n.opname);
+                    CHELIS_TRY(check_same_shape(n, src(k), n.opname.c_str()));
+                }
+                for (const auto &s : n.steps)
+                    if ((s.a >= 0 && s.a >= static_cast<int>(n.in.size())) ||
+                        (s.b >= 0 && s.b >= static_cast<int>(n.in.size())))
+                        return bad("FusedElem operand out of range");
+                own();
+                break;
+            case Op::Relu: case Op::Softmax: case Op::Cumsum:
+                if (!floating || src(0).dtype != n.dtype) return unsupported(n.opname + " precision");
+                CHELIS_TRY(check_same_shape(n, src(0), n.opname.c_str()));
+                if ((n.op == Op::Softmax || n.op == Op::Cumsum) &&
+                    (n.shape.empty() || n.axis != static_cast<int>(n.shape.size()) - 1))
+                    return unsupported(n.opname + " along a non-last axis");
+                if (n.op == Op::Softmax && n.dtype != CHELIS_DTYPE_F32)
+                    return unsupported("Softmax at f64");
+                own();
+                break;
+            case Op::ReluAdjoint:
+                if (!floating || src(0).dtype != n.dtype || src(1).dtype != n.dtype)
+                    return unsupported("ReluAdjoint precision");
+                CHELIS_TRY(check_same_shape(n, src(0), "ReluAdjoint"));
+                CHELIS_TRY(check_same_shape(n, src(1), "ReluAdjoint"));
+                own();
+                break;
+            case Op::Sum: case Op::MaxReduce: {
+                const auto &xs = src(0).shape;
+                if (!floating || src(0).dtype != n.dtype) return unsupported(n.opname + " precision");
+                if (n.op == Op::Sum && n.accumulator != n.dtype)
+                    return unsupported("Sum with a wider accumulator");
+                if (n.axis >= static_cast<int>(xs.size())) return bad("reduction axis out of range");
+                std::vector<int64_t> want = xs;
+                want.erase(want.begin() + n.axis);
+                if (want != n.shape) return bad("reduction result shape");
+                own();
+                break;
+            }
+            case Op::Count: {
+                if (src(0).dtype != CHELIS_DTYPE_BOOL || n.dtype != CHELIS_DTYPE_I64)
+                    return unsupported("Count other than bool -> i64");
+                if (static_cast<int>(n.axes.size()) != static_cast<int>(src(0).shape.size()) ||
+                    !n.shape.empty())
+                    return unsupported("Count over some axes");
+                own();
+                break;
+            }
+            case Op::Matmul: {
+                const auto &a = src(0).shape, &b = src(1).shape;
+                if (!floating || src(0).dtype != n.dtype || src(1).dtype != n.dtype ||
+                    n.accumulator != n.dtype)
+                    return unsupported("BlasMatmul precision");
+                const size_t r = n.shape.size();
+                if (r < 2 || a.size() != r || b.size() != r || a[r - 1] != b[r - 2] ||
+                    a[r - 2] != n.shape[r - 2] || b[r - 1] != n.shape[r - 1])
+                    return bad("BlasMatmul operand shapes");
+                for (size_t d = 0; d + 2 < r; ++d)
+                    if (a[d] != n.shape[d] || b[d] != n.shape[d]) return bad("BlasMatmul batch axes");
+                own();
+                break;
+            }
+            case Op::Gather: case Op::ScatterAdd: {
+                const Node &vals = src(0);
+                const Node &idx = src(1);
+                const int it = idx.dtype;
+                if (it != CHELIS_DTYPE_I64 && it != CHELIS_DTYPE_I32 && it != CHELIS_DTYPE_I16 &&
+                    it != CHELIS_DTYPE_I8)
+                    return bad("index dtype must be a signed integer ([05-SPARSE-1])");
+                if (vals.dtype != n.dtype) return bad("gather / scatter value dtype");
+                const int vr = static_cast<int>(vals.shape.size());
+                const int ir = static_cast<int>(idx.shape.size());
+                if (n.axis >= vr || n.batch_rank > n.axis || n.batch_rank > ir)
+                    return bad("gather / scatter axis or batch rank");
+                for (int d = 0; d < n.batch_rank; ++d)
+                    if (idx.shape[d] != vals.shape[d]) return bad("gather / scatter batch axes");
+                std::vector<int64_t> sel(vals.shape.begin(), vals.shape.begin() + n.axis);
+                sel.insert(sel.end(), idx.shape.begin() + n.batch_rank, idx.shape.end());
+                sel.insert(sel.end(), vals.shape.begin() + n.axis + 1, vals.shape.end());
+                if (sel.size() > static_cast<size_t>(kMaxRank)) return unsupported("gather rank");
+                if (n.op == Op::Gather) {
+                    if (sel != n.shape) return bad("Gather result shape");
+                } else {
+                    if (n.shape != vals.shape || src(2).shape != sel || src(2).dtype != n.dtype)
+                        return bad("ScatterAdd shapes");
+                }
+                own();
+                break;
+            }
+            case Op::Reshape: {
+                const Node &s = src(0);
+                if (s.dtype != n.dtype || count_of(s.shape) != count_of(n.shape))
+                    return bad("Reshape changes the element count");
+                const Layout &SL = P.layout[n.in[0]];
+                if (is_dense(s.shape, SL.strides)) {
+                    L.root = SL.root;
+                    L.offset = SL.offset;
+                    L.strides = dense_strides(n.shape);
+                } else {
+                    own();  // materialised
+                }
+                break;
+            }
+            case Op::Permute: {
+                const Node &s = src(0);
+                const size_t r = s.shape.size();
+                if (n.axes.size() != r || n.shape.size() != r || s.dtype != n.dtype)
+                    return bad("Permute axes");
+                std::vector<bool> seen(r, false);
+                const Layout &SL = P.layout[n.in[0]];
+                L.root = SL.root;
+                L.offset = SL.offset;
+                L.strides.assign(r, 0);
+                for (size_t d = 0; d < r; ++d) {
+                    const int a = n.axes[d];
+                    if (a < 0 || a >= static_cast<int>(r) || seen[a] || s.shape[a] != n.shape[d])
+                        return bad("Permute axes");
+                    seen[a] = true;
+                    L.strides[d] = SL.strides[a];
+                }
+                break;
+            }
+            case Op::Expand: {
+                const Node &s = src(0);
+                const Layout &SL = P.layout[n.in[0]];
+                const size_t r = n.shape.size();
+                if (s.dtype != n.dtype || n.axis >= static_cast<int>(r)) return bad("Expand axis");
+                L.root = SL.root;
+                L.offset = SL.offset;
+                if (s.shape.size() + 1 == r) {  // rank-increasing: insert a broadcast axis
+                    std::vector<int64_t> back = n.shape;
+                    back.erase(back.begin() + n.axis);
+                    if (back != s.shape) return bad("Expand shape");
+                    L.strides = SL.strides;
+                    L.strides.insert(L.strides.begin() + n.axis, 0);
+                } else if (s.shape.size() == r) {  // same rank: a size-1 axis broadcast
+                    for (size_t d = 0; d < r; ++d)
+                        if (static_cast<int>(d) != n.axis ? s.shape[d] != n.shape[d]
+                                                          : s.shape[d] != 1)
+                            return bad("Expand shape");
+                    L.strides = SL.strides;
+                    L.strides[n.axis] = 0;
+                } else {
+                    return bad("Expand rank");
+                }
+                break;
+            }
+            case Op::Shrink: {
+                const Node &s = src(0);
+                const Layout &SL = P.layout[n.in[0]];
+                if (n.bounds.size() != s.shape.size() || n.shape.size() != s.shape.size() ||
+                    s.dtype != n.dtype)
+                    return bad("Shrink bounds");
+                L.root = SL.root;
+                L.offset = SL.offset;
+                L.strides = SL.strides;
+                for (size_t d = 0; d < n.bounds.size(); ++d) {
+                    const auto b = n.bounds[d];
+                    if (b.first < 0 || b.second < b.first || b.second > s.shape[d] ||
+                        n.shape[d] != b.second - b.first)
+                        return bad("Shrink bounds");
+                    L.offset += b.first * SL.strides[d];
+                }
+                break;
+            }
+            case Op::Stride: {
+                const Node &s = src(0);
+                const Layout &SL = P.layout[n.in[0]];
+                if (n.step.size() != s.shape.size() || n.shape.size() != s.shape.size() ||
+                    s.dtype != n.dtype)
+                    return bad("Stride steps");
+                L.root = SL.root;
+                L.offset = SL.offset;
+                L.strides = SL.strides;
+                for (size_t d = 0; d < n.step.size(); ++d) {
+                    if (n.shape[d] != (s.shape[d] + n.step[d] - 1) / n.step[d])
+                        return bad("Stride result shape");
+                    L.strides[d] *= n.step[d];
+                }
+                break;
+            }
+            case Op::Pad: {
+                const Node &s = src(0);
+                if (n.bounds.size() != s.shape.size() || n.shape.size() != s.shape.size() ||
+                    s.dtype != n.dtype)
+                    return bad("Pad");
+                for (size_t d = 0; d < n.bounds.size(); ++d)
+                    if (n.shape[d] != s.shape[d] + n.bounds[d].first + n.bounds[d].second)
+                        return bad("Pad result shape");
+                own();
+                break;
+            }
+            case Op::Cast: {
+                const int from = src(0).dtype;
+                const bool to_float = floating;
+                const bool from_ok = from == CHELIS_DTYPE_F32 || from == CHELIS_DTYPE_F64 ||
+                                     from == CHELIS_DTYPE_I32 || from == CHELIS_DTYPE_I64 ||
+                                     from == CHELIS_DTYPE_BOOL;
+                if (!to_float || !from_ok) return unsupported("Cast to a non-float precision");
+                CHELIS_TRY(check_same_shape(n, src(0), "Cast"));
+                own();
+                break;
+            }
+            case Op::Copy:
+                if (src(0).dtype != n.dtype) return bad("Copy dtype");
+                CHELIS_TRY(check_same_shape(n, src(0), "Copy"));
+                own();
+                break;
+            case Op::Store: {
+                const Node &s = src(0);
+                if (s.dtype != n.dtype) return bad("Store dtype");
+                CHELIS_TRY(check_same_shape(n, s, "Store"));
+                L = P.layout[n.in[0]];
+                break;
+            }
+        }
+    }
+    return CHELIS_CUDA_OK;
+}
+
+bool is_view(Op op) {
+    return op == Op::Permute || op == Op::Expand || op == Op::Shrink || op == Op::Stride ||
+           op == Op::Store;
+}
+
+// ---------------------------------------------------------------- planning
+
+// Placement of every node, outputs (Store nodes, then the roots:
+// emit.rs:5901-5934), reduction-inlined FusedElems, slot reuse after last
+// use and the arena size (memory.rs:39-98).
+int plan(Program &P, const std::vector<int> &roots) {
+    std::vector<Node> &N = P.nodes;
+    const int count = static_cast<int>(N.size());
+    P.place.assign(count, Place::Slot);
+    P.slot.assign(count, -1);
+    P.input_of_load.assign(count, -1);
+    P.direct_output.assign(count, -1);
+    for (int i = 0; i < count; ++i) {
+        const Node &n = N[i];
+        if (n.op == Op::Load) {
+            P.place[i] = Place::Input;
+            int slot = -1;
+            for (size_t k = 0; k < P.input_labels.size(); ++k)
+                if (P.input_labels[k] == n.name) slot = static_cast<int>(k);
+            if (slot < 0) {
+                slot = static_cast<int>(P.input_labels.size());
+                P.input_labels.push_back(n.name);
+            }
+            P.input_of_load[i] = slot;
+        } else if (n.op == Op::Drop) {
+            P.place[i] = Place::Skip;
+        } else if (is_view(n.op) || (n.op == Op::Reshape && P.layout[i].root != i)) {
+            P.place[i] = Place::View;
+        }
+    }
+    // consumers
+    std::vector<std::vector<int>> users(count);
+    for (int i = 0; i < count; ++i)
+        for (int j : N[i].in) users[j].push_back(i);
+    // outputs
+    for (int i = 0; i < count; ++i)
+        if (N[i].op == Op::Store) {
+            P.output_labels.push_back(N[i].name);
+            P.output_node.push_back(i);
+        }
+    std::vector<int> rs = roots;
+    if (rs.empty() && count > 0) rs.push_back(count - 1);
+    for (size_t k = 0; k < rs.size(); ++k) {
+        if (rs[k] < 0 || rs[k] >= count) return bad("root out of range");
+        if (std::find(P.output_node.begin(), P.output_node.end(), rs[k]) != P.output_node.end())
+            continue;
+        P.output_labels.push_back("root" + std::to_string(k));
+        P.output_node.push_back(rs[k]);
+    }
+    std::vector<bool> is_output(count, false);
+    for (int o : P.output_node) is_output[o] = true;
+    // a FusedElem read only by a Sum / MaxReduce runs inside the reduction
+    for (int i = 0; i < count; ++i) {
+        const Node &n = N[i];
+        if ((n.op == Op::Sum || n.op == Op::MaxReduce) && N[n.in[0]].op == Op::Fused) {
+            const int f = n.in[0];
+            if (users[f].size() == 1 && !is_output[f] && N[f].in.size() <= 7)
+                P.place[f] = Place::Inlined;
+        }
+    }
+    // outputs written straight into their owners: a slot node whose value is
+    // the output unchanged (the node itself, or a Store of it)
+    for (size_t k = 0; k < P.output_node.size(); ++k) {
+        int o = P.output_node[k];
+        while (N[o].op == Op::Store) o = N[o].in[0];
+        if (P.place[o] == Place::Slot && P.direct_output[o] < 0) {
+            P.place[o] = Place::Output;
+            P.direct_output[o] = static_cast<int>(k);
+        }
+    }
+    // last use of each storage root (through views; inlined nodes' inputs
+    // are read by their reduction)
+    std::vector<int> last(count, -1);
+    auto root_of = [&](int j) { return P.layout[j].root; };
+    for (int i = 0; i < count; ++i) {
+        if (P.place[i] == Place::Inlined) continue;
+        std::vector<int> reads = N[i].in;
+        if ((N[i].op == Op::Sum || N[i].op == Op::MaxReduce) && P.place[N[i].in[0]] == Place::Inlined)
+            reads = N[N[i].in[0]].in;
+        for (int j : reads) last[root_of(j)] = std::max(last[root_of(j)], i);
+    }
+    for (int o : P.output_node) last[root_of(o)] = count;  // copied out at the end
+    // slots: best fit among slots free before node i runs
+    std::vector<int64_t> slot_free_at;  // last use of the slot's current owner
+    int64_t live = 0;
+    for (int i = 0; i < count; ++i) {
+        if (P.place[i] != Place::Slot) continue;
+        const int64_t bytes = ((std::max<int64_t>(count_of(N[i].shape), 1) *
+                                dtype_width(N[i].dtype)) + 255) / 256 * 256;
+        int best = -1;
+        for (size_t s = 0; s < P.slot_cap.size(); ++s)
+            if (slot_free_at[s] < i && P.slot_cap[s] >= bytes &&
+                (best < 0 || P.slot_cap[s] < P.slot_cap[best]))
+                best = static_cast<int>(s);
+        if (best < 0) {
+            best = static_cast<int>(P.slot_cap.size());
+            P.slot_cap.push_back(bytes);
+            slot_free_at.push_back(-1);
+        }
+        slot_free_at[best] = std::max(last[i], i);
+        P.slot[i] = best;
+        // bytes live while node i runs: slots whose owner is still needed
+        live = 0;
+        for (size_t s = 0; s < P.slot_cap.size(); ++s)
+            if (slot_free_at[s] >= i) live += P.slot_cap[s];
+        P.live_peak_bytes = std::max(P.live_peak_bytes, live);
+    }
+    P.slot_off.resize(P.slot_cap.size());
+    int64_t off = 0;
+    for (size_t s = 0; s < P.slot_cap.size(); ++s) {
+        P.slot_off[s] = off;
+        off += P.slot_cap[s];
+    }
+    P.arena_bytes = off;
+    return CHELIS_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- kernels
+
+struct Strided {
+    int32_t rank;
+    int64_t shape[kMaxRank];
+    int64_t stride[kMaxRank];
+};
+
+__device__ __forceinline__ int64_t offset_of(const Strided &s, int64_t linear) {
+    int64_t off = 0;
+    for (int d = s.rank - 1; d >= 0; --d) {
+        const int64_t c = linear % s.shape[d];
+        linear /= s.shape[d];
+        off += c * s.stride[d];
+    }
+    return off;
+}
+
+template <typename T>
+__global__ void copy_kernel(const T *__restrict__ src, Strided s, T *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = src[offset_of(s, i)];
+}
+
+template <typename T>
+__global__ void fill_kernel(T *__restrict__ dst, T v, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = v;
+}
+
+// out (dense, `o` its shape) = src at coordinate - before, or the fill
+template <typename T>
+__global__ void pad_kernel(const T *__restrict__ src, Strided s, Strided o, Strided before, T fill,
+                           T *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t rem = i, off = 0;
+        bool in = true;
+        for (int d = o.rank - 1; d >= 0; --d) {
+            const int64_t c = rem % o.shape[d] - before.shape[d];
+            rem /= o.shape[d];
+            if (c < 0 || c >= s.shape[d]) in = false;
+            off += c * s.stride[d];
+        }
+        dst[i] = in ? src[off] : fill;
+    }
+}
+
+template <typename From, typename To>
+__global__ void cast_kernel(const From *__restrict__ src, Strided s, To *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = static_cast<To>(src[offset_of(s, i)]);
+}
+
+template <typename I>
+__device__ __forceinline__ int64_t load_index(const void *p, int64_t off) {
+    return static_cast<int64_t>(static_cast<const I *>(p)[off]);
+}
+__device__ __forceinline__ int64_t read_index(const void *p, int64_t off, int width) {
+    switch (width) {
+        case 8: return load_index<int64_t>(p, off);
+        case 4: return load_index<int32_t>(p, off);
+        case 2: return load_index<int16_t>(p, off);
+        default: return load_index<int8_t>(p, off);
+    }
+}
+
+// Gather (spec [05-OP-52]): out[p, q, t] = values[p, idx[p_batch, q], t] for
+// p over values' axes before `axis`, q over the index axes after the batch
+// ones, t over values' axes after `axis`.  `v` / `x` are values' and
+// indices' layouts, the output dense.  An index outside [0, values.shape[axis])
+// writes 0 and sets the device error word.
+struct GatherGeom {
+    Strided v, x;
+    int32_t axis, batch_rank, qrank, trank;
+    int64_t qshape[kMaxRank], tshape[kMaxRank];
+    int32_t index_width;
+};
+
+template <typename T>
+__global__ void gather_kernel(const T *__restrict__ values, const void *__restrict__ idx,
+                              GatherGeom g, T *__restrict__ out, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t rem = i, voff = 0, xoff = 0;
+        for (int d = g.trank - 1; d >= 0; --d) {  // trailing value axes
+            const int64_t c = rem % g.tshape[d];
+            rem /= g.tshape[d];
+            voff += c * g.v.stride[g.axis + 1 + d];
+        }
+        for (int d = g.qrank - 1; d >= 0; --d) {  // index axes after the batch ones
+            const int64_t c = rem % g.qshape[d];
+            rem /= g.qshape[d];
+            xoff += c * g.x.stride[g.batch_rank + d];
+        }
+        for (int d = g.axis - 1; d >= 0; --d) {  // leading value axes (batch ones pair with idx)
+            const int64_t c = rem % g.v.shape[d];
+            rem /= g.v.shape[d];
+            voff += c * g.v.stride[d];
+            if (d < g.batch_rank) xoff += c * g.x.stride[d];
+        }
+        const int64_t k = read_index(idx, xoff, g.index_width);
+        if (k < 0 || k >= g.v.shape[g.axis]) {
+            report_device_error(DEVERR_BAD_INDEX);
+            out[i] = T(0);
+        } else {
+            out[i] = values[voff + k * g.v.stride[g.axis]];
+        }
+    }
+}
+
+// ScatterAdd: out (a dense copy of the target) [p, idx[p_batch, q], t] +=
+// updates[p, q, t].  One thread per (p, t) adds its updates in increasing q,
+// which is the updates' increasing flat order for every target cell.
+template <typename T>
+__global__ void scatter_add_kernel(const T *__restrict__ upd, Strided u, const void *__restrict__ idx,
+                                   GatherGeom g, T *__restrict__ out, int64_t lanes, int64_t nq) {
+    const Strided o = g.v;  // the output's dense layout and shape
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < lanes;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t rem = i, ooff = 0, uoff = 0, xbase = 0;
+        for (int d = g.trank - 1; d >= 0; --d) {
+            const int64_t c = rem % g.tshape[d];
+            rem /= g.tshape[d];
+            ooff += c * o.stride[g.axis + 1 + d];
+            uoff += c * u.stride[g.axis + g.qrank + d];
+        }
+        for (int d = g.axis - 1; d >= 0; --d) {
+            const int64_t c = rem % o.shape[d];
+            rem /= o.shape[d];
+            ooff += c * o.stride[d];
+            uoff += c * u.stride[d];
+            if (d < g.batch_rank) xbase += c * g.x.stride[d];
+        }
+        for (int64_t q = 0; q < nq; ++q) {
+            int64_t qr = q, xoff = xbase, qoff = 0;
+            for (int d = g.qrank - 1; d >= 0; --d) {
+                const int64_t c = qr % g.qshape[d];
+                qr /= g.qshape[d];
+                xoff += c * g.x.stride[g.batch_rank + d];
+                qoff += c * u.stride[g.axis + d];
+            }
+            const int64_t k = read_index(idx, xoff, g.index_width);
+            if (k < 0 || k >= o.shape[g.axis]) {
+                report_device_error(DEVERR_BAD_INDEX);
+                continue;
+            }
+            T *cell = out + ooff + k * o.stride[g.axis];
+            *cell = *cell + upd[uoff + qoff];
+        }
+    }
+}
+
+unsigned grid_for(int64_t n) {
+    int64_t b = (n + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    if (b > cap) b = cap;
+    return static_cast<unsigned>(b < 1 ? 1 : b);
+}
+
+// ---------------------------------------------------------------- running
+
+struct Value {
+    char *ptr = nullptr;  // element (0, ..., 0)
+    chelis_dtype dtype = 0;
+    std::vector<int64_t> shape, strides;
+};
+
+Strided strided(const Value &v) {
+    Strided s{};
+    s.rank = static_cast<int32_t>(v.shape.size());
+    for (int d = 0; d < s.rank; ++d) {
+        s.shape[d] = v.shape[d];
+        s.stride[d] = v.strides[d];
+    }
+    if (s.rank == 0) {
+        s.rank = 1;
+        s.shape[0] = 1;
+        s.stride[0] = 1;
+    }
+    return s;
+}
+
+template <typename T>
+int launch_copy(const Value &src, void *dst, int64_t n, cudaStream_t s) {
+    if (n == 0) return CHELIS_CUDA_OK;
+    copy_kernel<T><<<grid_for(n), 256, 0, s>>>(reinterpret_cast<const T *>(src.ptr), strided(src),
+                                               static_cast<T *>(dst), n);
+    g_launches++;
+    CHELIS_LAUNCH_CHECK("dag::copy_kernel");
+    return CHELIS_CUDA_OK;
+}
+
+int materialize(const Value &src, void *dst, cudaStream_t s) {
+    const int64_t n = count_of(src.shape);
+    switch (dtype_width(src.dtype)) {
+        case 8: return launch_copy<uint64_t>(src, dst, n, s);
+        case 4: return launch_copy<uint32_t>(src, dst, n, s);
+        case 2: return launch_copy<uint16_t>(src, dst, n, s);
+        default: return launch_copy<uint8_t>(src, dst, n, s);
+    }
+}
+
+struct Run {
+    const Program &P;
+    std::vector<Value> val;
+    char *arena = nullptr;
+    std::vector<char *> out_ptr;  // device memory of each output owner
+    std::vector<void *> temps;    // materialised operands, freed at the end
+    cudaStream_t s;
+    explicit Run(const Program &p) : P(p), val(p.nodes.size()) {}
+    ~Run() {
+        for (void *t : temps) scratch_free(t, s);
+    }
+
+    // a dense copy of `v` when it is not dense already
+    int dense(Value &v) {
+        if (is_dense(v.shape, v.strides)) return CHELIS_CUDA_OK;
+        void *t = nullptr;
+        const int64_t bytes = std::max<int64_t>(count_of(v.shape), 1) * dtype_width(v.dtype);
+        CHELIS_TRY(scratch_alloc(&t, static_cast<size_t>(bytes), s));
+        temps.push_back(t);
+        CHELIS_TRY(materialize(v, t, s));
+        v.ptr = static_cast<char *>(t);
+        v.strides = dense_strides(v.shape);
+        return CHELIS_CUDA_OK;
+    }
+
+    char *storage(int i) {
+        if (P.place[i] == Place::Output) return out_ptr[P.direct_output[i]];
+        return arena + P.slot_off[P.slot[i]];
+    }
+
+    int node(int i, const std::vector<const chelis_gpu_tensor *> &inputs);
+};
+
+int elementwise(const Node &n, const std::vector<const Value *> &ins,
+                const std::vector<chelis_fused_step> &steps, void *out, int reduce_axis, int kind) {
+    std::vector<int64_t> shape = reduce_axis >= 0 ? ins[0]->shape : n.shape;
+    int rank = static_cast<int>(shape.size());
+    std::vector<const void *> ptrs;
+    std::vector<int64_t> strides;
+    if (rank == 0) {  // a scalar group runs as shape [1]
+        shape = {1};
+        rank = 1;
+    }
+    if (rank > 6) return unsupported("an elementwise group of rank above 6");
+    for (const Value *v : ins) {
+        ptrs.push_back(v->ptr);
+        if (v->shape.empty()) strides.push_back(1);
+        else strides.insert(strides.end(), v->strides.begin(), v->strides.end());
+    }
+    if (reduce_axis >= 0)
+        return chelis_cuda_fused_reduce(n.dtype, steps.data(), static_cast<int32_t>(steps.size()),
+                                        ptrs.data(), strides.data(),
+                                        static_cast<int32_t>(ptrs.size()), shape.data(), rank,
+                                        reduce_axis, kind, out);
+    return chelis_cuda_fused_elementwise(n.dtype, steps.data(), static_cast<int32_t>(steps.size()),
+                                         ptrs.data(), strides.data(),
+                                         static_cast<int32_t>(ptrs.size()), shape.data(), rank, out);
+}
+
+int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
+    const Node &n = P.nodes[i];
+    Value &v = val[i];
+    v.dtype = n.dtype;
+    v.shape = n.shape;
+    const Place pl = P.place[i];
+    if (pl == Place::Inlined || pl == Place::Skip) return CHELIS_CUDA_OK;
+    if (pl == Place::Input) {
+        const chelis_gpu_tensor *t = inputs[P.input_of_load[i]];
+        v.ptr = static_cast<char *>(t->data);
+        v.strides.assign(t->strides, t->strides + t->rank);
+        return CHELIS_CUDA_OK;
+    }
+    if (pl == Place::View) {
+        // derived from the operand's run-time value (the plan's static
+        // layouts agree, inputs having been made dense)
+        const Value &src = val[n.in[0]];
+        v.strides.assign(n.shape.size(), 0);
+        v.ptr = src.ptr;
+        const int w = dtype_width(n.dtype);
+        switch (n.op) {
+            case Op::Store: v.ptr = src.ptr; v.strides = src.strides; break;
+            case Op::Reshape: v.strides = dense_strides(n.shape); break;
+            case Op::Permute:
+                for (size_t d = 0; d < n.axes.size(); ++d) v.strides[d] = src.strides[n.axes[d]];
+                break;
+            case Op::Expand:
+                if (src.shape.size() + 1 == n.shape.size()) {
+                    v.strides = src.strides;
+                    v.strides.insert(v.strides.begin() + n.axis, 0);
+                } else {
+                    v.strides = src.strides;
+                    v.strides[n.axis] = 0;
+                }
+                break;
+            case Op::Shrink:
+                v.strides = src.strides;
+                for (size_t d = 0; d < n.bounds.size(); ++d)
+                    v.ptr += n.bounds[d].first * src.strides[d] * w;
+                break;
+            case Op::Stride:
+                v.strides = src.strides;
+                for (size_t d = 0; d < n.step.size(); ++d) v.strides[d] *= n.step[d];
+                break;
+            default: return bad("view of an unexpected op");
+        }
+        return CHELIS_CUDA_OK;
+    }
+    // a node with its own storage
+    char *out = storage(i);
+    v.ptr = out;
+    v.strides = dense_strides(n.shape);
+    const int64_t cnt = count_of(n.shape);
+    const int w = dtype_width(n.dtype);
+    auto in = [&](int k) -> Value & { return val[n.in[k]]; };
+    switch (n.op) {
+        case Op::Const: {
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            switch (w) {
+                case 8: fill_kernel<uint64_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<uint64_t *>(out), n.bits, cnt); break;
+                case 4: fill_kernel<uint32_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<uint32_t *>(out), static_cast<uint32_t>(n.bits), cnt); break;
+                case 2: fill_kernel<uint16_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<uint16_t *>(out), static_cast<uint16_t>(n.bits), cnt); break;
+                default: fill_kernel<uint8_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<uint8_t *>(out), static_cast<uint8_t>(n.bits), cnt); break;
+            }
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::fill_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::ConstTensor:
+            if (n.data.empty()) return CHELIS_CUDA_OK;
+            return check_cuda(cudaMemcpyAsync(out, n.data.data(), n.data.size(), cudaMemcpyHostToDevice, s),
+                              "ConstTensor upload");
+        case Op::Copy: case Op::Reshape:
+            return materialize(in(0), out, s);
+        case Op::Elementwise: case Op::Fused: {
+            std::vector<const Value *> ins;
+            for (size_t k = 0; k < n.in.size(); ++k) ins.push_back(&in(static_cast<int>(k)));
+            return elementwise(n, ins, n.steps, out, -1, 0);
+        }
+        case Op::Sum: case Op::MaxReduce: {
+            const int kind = n.op == Op::Sum ? CHELIS_FUSED_REDUCE_SUM : CHELIS_FUSED_REDUCE_MAX;
+            const int f = n.in[0];
+            std::vector<const Value *> ins;
+            std::vector<chelis_fused_step> steps;
+            Value one;  // the multiplicative identity, broadcast: x * 1 is x exactly
+            if (P.place[f] == Place::Inlined) {
+                for (int j : P.nodes[f].in) ins.push_back(&val[j]);
+                steps = P.nodes[f].steps;
+            } else {
+                ins.push_back(&in(0));
+                void *t = nullptr;
+                CHELIS_TRY(scratch_alloc(&t, 8, s));
+                temps.push_back(t);
+                if (n.dtype == CHELIS_DTYPE_F32)
+                    fill_kernel<uint32_t><<<1, 32, 0, s>>>(static_cast<uint32_t *>(t), 0x3f800000u, 1);
+                else
+                    fill_kernel<uint64_t><<<1, 32, 0, s>>>(static_cast<uint64_t *>(t), 0x3ff0000000000000ull, 1);
+                g_launches++;
+                CHELIS_LAUNCH_CHECK("dag::fill_kernel");
+                one.ptr = static_cast<char *>(t);
+                one.dtype = n.dtype;
+                one.shape = in(0).shape;
+                one.strides.assign(one.shape.size(), 0);
+                ins.push_back(&one);
+                steps.push_back({CHELIS_FUSED_MUL, 0, 1});
+            }
+            return elementwise(n, ins, steps, out, n.axis, kind);
+        }
+        case Op::Relu: {
+            Value x = in(0);
+            CHELIS_TRY(dense(x));
+            return chelis_cuda_relu(n.dtype, x.ptr, out, cnt);
+        }
+        case Op::ReluAdjoint: {
+            Value x = in(0), g = in(1);
+            CHELIS_TRY(dense(x));
+            CHELIS_TRY(dense(g));
+            return chelis_cuda_relu_adjoint(n.dtype, x.ptr, g.ptr, out, cnt);
+        }
+        case Op::Softmax: {
+            Value x = in(0);
+            CHELIS_TRY(dense(x));
+            const int64_t cols = n.shape.back();
+            return chelis_cuda_softmax_rows_f32(reinterpret_cast<const float *>(x.ptr),
+                                                reinterpret_cast<float *>(out),
+                                                cols ? cnt / cols : 0, cols);
+        }
+        case Op::Cumsum: {
+            Value x = in(0);
+            CHELIS_TRY(dense(x));
+            const int64_t len = n.shape.back();
+            const int64_t lanes = len ? cnt / len : 0;
+            return n.dtype == CHELIS_DTYPE_F64
+                       ? chelis_cuda_cumsum_f64(reinterpret_cast<const double *>(x.ptr),
+                                                reinterpret_cast<double *>(out), lanes, len, n.reverse)
+                       : chelis_cuda_cumsum_f32(reinterpret_cast<const float *>(x.ptr),
+                                                reinterpret_cast<float *>(out), lanes, len, n.reverse);
+        }
+        case Op::Count: {
+            Value x = in(0);
+            CHELIS_TRY(dense(x));
+            return chelis_cuda_count_bool(reinterpret_cast<const uint8_t *>(x.ptr),
+                                          count_of(x.shape), reinterpret_cast<int64_t *>(out));
+        }
+        case Op::Matmul: {
+            const int r = static_cast<int>(n.shape.size());
+            const int64_t m = n.shape[r - 2], nn = n.shape[r - 1], k = in(0).shape[r - 1];
+            int64_t batch = 1;
+            for (int d = 0; d + 2 < r; ++d) batch *= n.shape[d];
+            // an operand is used in place when its matrix is dense or a
+            // dense transpose and its batch axes collapse to one stride
+            auto operand = [&](Value &x, int *trans, int64_t *ld, int64_t *bstride) -> int {
+                for (int pass = 0; pass < 2; ++pass) {
+                    const int64_t s1 = x.strides[r - 1], s0 = x.strides[r - 2];
+                    const int64_t rows = x.shape[r - 2], cols = x.shape[r - 1];
+                    bool ok = true;
+                    if (s1 == 1 && (s0 >= cols || rows == 1)) {
+                        *trans = 0;
+                        *ld = rows == 1 ? cols : s0;
+                    } else if (s0 == 1 && (s1 >= rows || cols == 1)) {
+                        *trans = 1;
+                        *ld = cols == 1 ? rows : s1;
+                    } else {
+                        ok = false;
+                    }
+                    // batch axes: one uniform stride over the flattened batch
+                    int64_t bs = 0;
+                    bool first = true;
+                    for (int d = r - 3; d >= 0 && ok; --d) {
+                        if (x.shape[d] == 1) continue;
+                        if (first) {
+                            bs = x.strides[d];
+                            first = false;
+                        } else {
+                            int64_t inner = 1;
+                            for (int e = d + 1; e <= r - 3; ++e) inner *= x.shape[e];
+                            if (x.strides[d] != bs * inner) ok = false;
+                        }
+                    }
+                    *bstride = bs;
+                    if (ok && *ld >= 1) return CHELIS_CUDA_OK;
+                    if (pass == 0) CHELIS_TRY(dense(x));
+                }
+                return bad("BlasMatmul operand layout");
+            };
+            Value a = in(0), b = in(1);
+            int ta = 0, tb = 0;
+            int64_t lda = 0, ldb = 0, sa = 0, sb = 0;
+            CHELIS_TRY(operand(a, &ta, &lda, &sa));
+            CHELIS_TRY(operand(b, &tb, &ldb, &sb));
+            if (n.dtype == CHELIS_DTYPE_F32)
+                return chelis_cuda_sgemm(ta, tb, m, nn, k, reinterpret_cast<const float *>(a.ptr), lda,
+                                         sa, reinterpret_cast<const float *>(b.ptr), ldb, sb,
+                                         reinterpret_cast<float *>(out), nn, m * nn, batch);
+            return chelis_cuda_dgemm(ta, tb, m, nn, k, reinterpret_cast<const double *>(a.ptr), lda, sa,
+                                     reinterpret_cast<const double *>(b.ptr), ldb, sb,
+                                     reinterpret_cast<double *>(out), nn, m * nn, batch);
+        }
+        case Op::Gather: case Op::ScatterAdd: {
+            const Value &vals = in(0);
+            const Value &idx = in(1);
+            GatherGeom g{};
+            g.axis = n.axis;
+            g.batch_rank = n.batch_rank;
+            g.index_width = dtype_width(idx.dtype);
+            g.x = strided(idx);
+            g.qrank = static_cast<int32_t>(idx.shape.size()) - n.batch_rank;
+            for (int d = 0; d < g.qrank; ++d) g.qshape[d] = idx.shape[n.batch_rank + d];
+            g.trank = static_cast<int32_t>(vals.shape.size()) - n.axis - 1;
+            for (int d = 0; d < g.trank; ++d) g.tshape[d] = vals.shape[n.axis + 1 + d];
+            if (n.op == Op::Gather) {
+                g.v = strided(vals);
+                if (cnt == 0) return CHELIS_CUDA_OK;
+                if (n.dtype == CHELIS_DTYPE_F64 || w == 8)
+                    gather_kernel<uint64_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint64_t *>(vals.ptr), idx.ptr, g, reinterpret_cast<uint64_t *>(out), cnt);
+                else if (w == 4)
+                    gather_kernel<uint32_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint32_t *>(vals.ptr), idx.ptr, g, reinterpret_cast<uint32_t *>(out), cnt);
+                else return unsupported("Gather of a 1- or 2-byte dtype");
+                g_launches++;
+                CHELIS_LAUNCH_CHECK("dag::gather_kernel");
+                return CHELIS_CUDA_OK;
+            }
+            // ScatterAdd: out = dense copy of the target, then the updates
+            if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+                return unsupported("ScatterAdd on a non-float precision");
+            CHELIS_TRY(materialize(vals, out, s));
+            Value dense_out;
+            dense_out.shape = n.shape;
+            dense_out.strides = dense_strides(n.shape);
+            g.v = strided(dense_out);
+            const Value &upd = in(2);
+            int64_t nq = 1;
+            for (int d = 0; d < g.qrank; ++d) nq *= g.qshape[d];
+            const int64_t lanes = nq ? count_of(upd.shape) / nq : 0;
+            if (lanes == 0 || nq == 0) return CHELIS_CUDA_OK;
+            if (n.dtype == CHELIS_DTYPE_F64)
+                scatter_add_kernel<double><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const double *>(upd.ptr), strided(upd), idx.ptr, g, reinterpret_cast<double *>(out), lanes, nq);
+            else
+                scatter_add_kernel<float><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const float *>(upd.ptr), strided(upd), idx.ptr, g, reinterpret_cast<float *>(out), lanes, nq);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::scatter_add_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Pad: {
+            const Value &x = in(0);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            Strided o{}, before{};
+            Value dense_out;
+            dense_out.shape = n.shape;
+            dense_out.strides = dense_strides(n.shape);
+            o = strided(dense_out);
+            Strided sx = strided(x);
+            before.rank = o.rank;
+            for (size_t d = 0; d < n.bounds.size(); ++d) before.shape[d] = n.bounds[d].first;
+            if (x.shape.empty()) sx.shape[0] = 1;
+            if (w == 8)
+                pad_kernel<uint64_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint64_t *>(x.ptr), sx, o, before, n.bits, reinterpret_cast<uint64_t *>(out), cnt);
+            else if (w == 4)
+                pad_kernel<uint32_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint32_t *>(x.ptr), sx, o, before, static_cast<uint32_t>(n.bits), reinterpret_cast<uint32_t *>(out), cnt);
+            else if (w == 2)
+                pad_kernel<uint16_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint16_t *>(x.ptr), sx, o, before, static_cast<uint16_t>(n.bits), reinterpret_cast<uint16_t *>(out), cnt);
+            else
+                pad_kernel<uint8_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint8_t *>(x.ptr), sx, o, before, static_cast<uint8_t>(n.bits), reinterpret_cast<uint8_t *>(out), cnt);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::pad_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Cast: {
+            const Value &x = in(0);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Strided sx = strided(x);
+            const bool to64 = n.dtype == CHELIS_DTYPE_F64;
+#define CHELIS_DAG_CAST(FROM)                                                                           \
+    if (to64)                                                                                           \
+        cast_kernel<FROM, double><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const FROM *>(x.ptr), sx, \
+                                                              reinterpret_cast<double *>(out), cnt);     \
+    else                                                                                                \
+        cast_kernel<FROM, float><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const FROM *>(x.ptr), sx,  \
+                                                             reinterpret_cast<float *>(out), cnt);
+            switch (x.dtype) {
+                case CHELIS_DTYPE_F32: CHELIS_DAG_CAST(float); break;
+                case CHELIS_DTYPE_F64: CHELIS_DAG_CAST(double); break;
+                case CHELIS_DTYPE_I32: CHELIS_DAG_CAST(int32_t); break;
+                case CHELIS_DTYPE_I64: CHELIS_DAG_CAST(int64_t); break;
+                default: CHELIS_DAG_CAST(uint8_t); break;  // bool: 0 / 1
+            }
+#undef CHELIS_DAG_CAST
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::cast_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        default: return bad("unexpected node kind", n.opname);
+    }
+}
+
+}  // namespace dag
+}  // namespace chelis
+
+using namespace chelis;
+
+struct chelis_dag_program {
+    dag::Program prog;
+};
+
+extern "C" {
+
+int chelis_dag_from_json(const char *text, int64_t len, chelis_dag_program **out) {
+    if (!out) return dag::bad("null output handle");
+    *out = nullptr;
+    if (!text || len < 0) return dag::bad("null or negative-length text");
+    json::Value doc;
+    json::Reader rd(text, static_cast<size_t>(len));
+    if (!rd.parse(&doc)) return dag::bad("malformed JSON", rd.error());
+    const json::Value *nodes = doc.get("nodes");
+    const json::Value *roots = doc.get("roots");
+    if (!nodes || nodes->kind != json::Value::Arr || !roots || roots->kind != json::Value::Arr)
+        return dag::bad("a Dag object has \"nodes\" and \"roots\" arrays");
+    auto p = std::make_unique<chelis_dag_program>();
+    for (size_t i = 0; i < nodes->a.size(); ++i)
+        CHELIS_TRY(dag::parse_node(nodes->a[i], i, p->prog.nodes));
+    std::vector<int> rs;
+    for (const auto &r : roots->a) {
+        int64_t v = 0;
+        if (!dag::as_index(&r, &v) || v >= static_cast<int64_t>(nodes->a.size()))
+            return dag::bad("root out of range");
+        rs.push_back(static_cast<int>(v));
+    }
+    CHELIS_TRY(dag::check_and_layout(p->prog));
+    CHELIS_TRY(dag::plan(p->prog, rs));
+    *out = p.release();
+    return CHELIS_CUDA_OK;
+}
+
+void chelis_dag_release(chelis_dag_program *p) { delete p; }
+
+int32_t chelis_dag_input_count(const chelis_dag_program *p) {
+    return p ? static_cast<int32_t>(p->prog.input_labels.size()) : -1;
+}
+const char *chelis_dag_input_label(const chelis_dag_program *p, int32_t i) {
+    if (!p || i < 0 || i >= static_cast<int32_t>(p->prog.input_labels.size())) return nullptr;
+    return p->prog.input_labels[i].c_str();
+}
+int32_t chelis_dag_output_count(const chelis_dag_program *p) {
+    return p ? static_cast<int32_t>(p->prog.output_labels.size()) : -1;
+}
+const char *chelis_dag_output_label(const chelis_dag_program *p, int32_t i) {
+    if (!p || i < 0 || i >= static_cast<int32_t>(p->prog.output_labels.size())) return nullptr;
+    return p->prog.output_labels[i].c_str();
+}
+int64_t chelis_dag_arena_bytes(const chelis_dag_program *p) { return p ? p->prog.arena_bytes : -1; }
+int64_t chelis_dag_live_peak_bytes(const chelis_dag_program *p) {
+    return p ? p->prog.live_peak_bytes : -1;
+}
+int32_t chelis_dag_slot_count(const chelis_dag_program *p) {
+    return p ? static_cast<int32_t>(p->prog.slot_cap.size()) : -1;
+}
+int64_t chelis_dag_output_bytes(const chelis_dag_program *p) {
+    if (!p) return -1;
+    int64_t b = 0;
+    for (int o : p->prog.output_node)
+        b += dag::count_of(p->prog.nodes[o].shape) * dtype_width(p->prog.nodes[o].dtype);
+    return b;
+}
+
+int chelis_dag_run_device_arena(chelis_dag_program *p, const chelis_device_tensor_owner *const *inputs,
+                                chelis_device_rank n_in, chelis_device_tensor_owner **outputs,
+                                chelis_device_rank n_out, void *arena, int64_t arena_bytes) {
+    if (!p) return dag::bad("null program");
+    const dag::Program &P = p->prog;
+    if (n_in != static_cast<int>(P.input_labels.size()) ||
+        n_out != static_cast<int>(P.output_labels.size()))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: expected %d inputs and %d outputs, got %d and %d",
+                         static_cast<int>(P.input_labels.size()),
+                         static_cast<int>(P.output_labels.size()), n_in, n_out);
+    if ((n_in && !inputs) || (n_out && !outputs)) return dag::bad("null argument array");
+    if (arena && arena_bytes < P.arena_bytes)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: arena of %lld bytes, the plan needs %lld",
+                         static_cast<long long>(arena_bytes), static_cast<long long>(P.arena_bytes));
+    for (int k = 0; k < n_out; ++k) outputs[k] = nullptr;
+    // inputs: the dtype and shape each Load declares
+    std::vector<const chelis_gpu_tensor *> views(n_in, nullptr);
+    for (int k = 0; k < n_in; ++k) {
+        views[k] = chelis_device_tensor_view(inputs[k]);
+        if (!views[k]) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in load at i64");
+    }
+    for (size_t i = 0; i < P.nodes.size(); ++i) {
+        if (P.input_of_load[i] < 0) continue;
+        const chelis_gpu_tensor *t = views[P.input_of_load[i]];
+        const dag::Node &n = P.nodes[i];
+        bool ok = t->dtype == n.dtype && t->rank == static_cast<int32_t>(n.shape.size());
+        for (int d = 0; ok && d < t->rank; ++d) ok = t->shape[d] == n.shape[d];
+        if (!ok) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in load at i64");
+    }
+    dag::Run run(P);
+    run.s = current_stream();
+    void *owned_arena = nullptr;
+    if (!arena && P.arena_bytes) {
+        CHELIS_TRY(scratch_alloc(&owned_arena, static_cast<size_t>(P.arena_bytes), run.s));
+        arena = owned_arena;
+    }
+    run.arena = static_cast<char *>(arena);
+    int st = CHELIS_CUDA_OK;
+    // output owners (outputs written in place allocate before the run)
+    run.out_ptr.assign(n_out, nullptr);
+    for (int k = 0; k < n_out && st == CHELIS_CUDA_OK; ++k) {
+        const dag::Node &n = P.nodes[P.output_node[k]];
+        outputs[k] = chelis_device_tensor_alloc_shape(n.dtype, static_cast<int32_t>(n.shape.size()),
+                                                      n.shape.data());
+        if (!outputs[k]) st = CHELIS_CUDA_ERR_CUDA;
+        else run.out_ptr[k] = static_cast<char *>(chelis_device_tensor_view(outputs[k])->data);
+    }
+    // inputs that are not dense are copied once, so every layout is known
+    std::vector<chelis_gpu_tensor> dense_in(n_in);
+    std::vector<std::vector<int64_t>> dense_strides(n_in);
+    for (int k = 0; k < n_in && st == CHELIS_CUDA_OK; ++k) {
+        const chelis_gpu_tensor *t = views[k];
+        std::vector<int64_t> shape(t->shape, t->shape + t->rank), strides(t->strides, t->strides + t->rank);
+        dense_in[k] = *t;
+        if (dag::is_dense(shape, strides)) continue;
+        dag::Value v;
+        v.ptr = static_cast<char *>(t->data);
+        v.dtype = t->dtype;
+        v.shape = shape;
+        v.strides = strides;
+        st = run.dense(v);
+        dense_strides[k] = v.strides;
+        dense_in[k].data = v.ptr;
+        dense_in[k].strides = dense_strides[k].data();
+        views[k] = &dense_in[k];
+    }
+    for (size_t i = 0; i < P.nodes.size() && st == CHELIS_CUDA_OK; ++i)
+        st = run.node(static_cast<int>(i), views);
+    // outputs not written in place: dense copies of their values
+    for (int k = 0; k < n_out && st == CHELIS_CUDA_OK; ++k) {
+        int o = P.output_node[k];
+        while (P.nodes[o].op == dag::Op::Store) o = P.nodes[o].in[0];
+        if (P.direct_output[o] == k) continue;
+        st = dag::materialize(run.val[P.output_node[k]], run.out_ptr[k], run.s);
+    }
+    if (owned_arena) scratch_free(owned_arena, run.s);
+    if (st != CHELIS_CUDA_OK) {
+        for (int k = 0; k < n_out; ++k) {
+            chelis_device_tensor_release(outputs[k]);
+            outputs[k] = nullptr;
+        }
+        return st;
+    }
+    return CHELIS_CUDA_OK;
+}
+
+int chelis_dag_run_device(chelis_dag_program *p, const chelis_device_tensor_owner *const *inputs,
+                          chelis_device_rank n_in, chelis_device_tensor_owner **outputs,
+                          chelis_device_rank n_out) {
+    return chelis_dag_run_device_arena(p, inputs, n_in, outputs, n_out, nullptr, 0);
+}
+
+int chelis_dag_run(chelis_dag_program *p, chelis_tensor **inputs, int n_in, chelis_tensor **outputs,
+                   int n_out) {
+    if (!p) return dag::bad("null program");
+    const dag::Program &P = p->prog;
+    if (n_in != static_cast<int>(P.input_labels.size()) ||
+        n_out != static_cast<int>(P.output_labels.size()))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: expected %d inputs and %d outputs, got %d and %d",
+                         static_cast<int>(P.input_labels.size()),
+                         static_cast<int>(P.output_labels.size()), n_in, n_out);
+    if ((n_in && !inputs) || (n_out && !outputs)) return dag::bad("null argument array");
+    for (int k = 0; k < n_out; ++k) outputs[k] = nullptr;
+    std::vector<chelis_device_tensor_owner *> din(n_in, nullptr), dout(n_out, nullptr);
+    int st = CHELIS_CUDA_OK;
+    for (int k = 0; k < n_in && st == CHELIS_CUDA_OK; ++k) {
+        if (!inputs[k]) {
+            st = set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in load at i64");
+            break;
+        }
+        const chelis_read_view v = chelis_tensor_read_view(inputs[k]);
+        const int32_t rank = chelis_tensor_rank(inputs[k]);
+        std::vector<int64_t> shape(rank);
+        for (int32_t d = 0; d < rank; ++d) shape[d] = chelis_tensor_shape(inputs[k], d);
+        din[k] = chelis_device_tensor_alloc_shape(v.dtype, rank, shape.data());
+        if (!din[k]) {
+            st = CHELIS_CUDA_ERR_CUDA;
+            break;
+        }
+        if (v.count)
+            st = chelis_device_tensor_copy_from_host_bytes(din[k], v.data, v.count * dtype_width(v.dtype));
+    }
+    if (st == CHELIS_CUDA_OK) st = chelis_dag_run_device(p, din.data(), n_in, dout.data(), n_out);
+    for (int k = 0; k < n_out && st == CHELIS_CUDA_OK; ++k) {
+        const chelis_gpu_tensor *d = chelis_device_tensor_view(dout[k]);
+        outputs[k] = chelis_alloc(d->rank, d->shape, d->dtype);
+        chelis_tensor_write *guard = chelis_tensor_begin_write(outputs[k]);
+        st = chelis_device_tensor_copy_to_host_status(guard, dout[k]);
+        chelis_tensor_end_write(guard);
+    }
+    if (st == CHELIS_CUDA_OK) st = chelis_cuda_device_status();
+    for (auto *o : din) chelis_device_tensor_release(o);
+    for (auto *o : dout) chelis_device_tensor_release(o);
+    if (st != CHELIS_CUDA_OK)
+        for (int k = 0; k < n_out; ++k)
+            if (outputs[k]) {
+                chelis_tensor_release(outputs[k]);
+                outputs[k] = nullptr;
+            }
+    return st;
+}
+
+}  // extern "C"

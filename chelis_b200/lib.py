@@ -46,6 +46,7 @@ class BlockParams(ctypes.Structure):
 
 
 DTYPE_F32, DTYPE_F64, DTYPE_I32, DTYPE_BOOL, DTYPE_I64 = 0, 1, 2, 3, 4
+DTYPE_BF16, DTYPE_F16 = 5, 6
 GEMM_3XTF32, GEMM_EXACT_TREE = 0, 1
 DGEMM_AUTO, DGEMM_DMMA, DGEMM_FFMA = 0, 1, 2
 ROWS_EXACT, ROWS_FAST = 0, 1
@@ -228,6 +229,23 @@ SIGNATURES = {
     "chelis_chain_grad_status": (c_int, [_PP, c_int, _PP, c_int]),
     "chelis_portfolio_status": (c_int, [_PP, c_int, _PP, c_int]),
     "chelis_matmul_status": (c_int, [_PP, c_int, _PP, c_int]),
+    "chelis_cuda_bf16_gemm_f32_acc_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64]),
+    "chelis_cuda_f16_gemm_f32_acc_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64]),
+    "chelis_cuda_gemm16": (c_int, [c_i32, c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    # DAG executor (include/chelis_dag.h)
+    "chelis_dag_from_json": (c_int, [ctypes.c_char_p, c_i64, ctypes.POINTER(c_vp)]),
+    "chelis_dag_release": (None, [c_vp]),
+    "chelis_dag_input_count": (c_i32, [c_vp]),
+    "chelis_dag_input_label": (ctypes.c_char_p, [c_vp, c_i32]),
+    "chelis_dag_output_count": (c_i32, [c_vp]),
+    "chelis_dag_output_label": (ctypes.c_char_p, [c_vp, c_i32]),
+    "chelis_dag_arena_bytes": (c_i64, [c_vp]),
+    "chelis_dag_live_peak_bytes": (c_i64, [c_vp]),
+    "chelis_dag_slot_count": (c_i32, [c_vp]),
+    "chelis_dag_output_bytes": (c_i64, [c_vp]),
+    "chelis_dag_run_device": (c_int, [c_vp, _PP, c_i32, _PP, c_i32]),
+    "chelis_dag_run_device_arena": (c_int, [c_vp, _PP, c_i32, _PP, c_i32, c_vp, c_i64]),
+    "chelis_dag_run": (c_int, [c_vp, _PP, c_int, _PP, c_int]),
 }
 
 _lib = None

@@ -220,6 +220,22 @@ int chelis_cuda_dgemm_strided_batched_row_major(const chelis_gpu_tensor *a,
                                                 int64_t a_batch_stride, int64_t b_batch_stride,
                                                 int64_t out_batch_stride);
 
+/* chelis_hipblas_bf16_gemm_f32_acc_row_major / _f16_ (chelis_hip_runtime.h:92-165):
+ * A, B and out in bf16 (f16), products and sums in f32, out rounded to the
+ * storage type once (nearest-even).  Same contiguity precondition and
+ * count == 0 no-op as the f32 helpers. */
+int chelis_cuda_bf16_gemm_f32_acc_row_major(const chelis_gpu_tensor *a, const chelis_gpu_tensor *b,
+                                            const chelis_gpu_tensor *out, int64_t m, int64_t n,
+                                            int64_t k);
+int chelis_cuda_f16_gemm_f32_acc_row_major(const chelis_gpu_tensor *a, const chelis_gpu_tensor *b,
+                                           const chelis_gpu_tensor *out, int64_t m, int64_t n,
+                                           int64_t k);
+/* Raw-pointer form for 16-bit storage (dtype CHELIS_DTYPE_BF16 or _F16):
+ * the same arguments as chelis_cuda_sgemm. */
+int chelis_cuda_gemm16(int32_t dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                       const void *a, int64_t lda, int64_t stride_a, const void *b, int64_t ldb,
+                       int64_t stride_b, void *c, int64_t ldc, int64_t stride_c, int64_t batch);
+
 /* Raw-pointer GEMM used by the helpers above and by the AD programs:
  * C[b] = op(A[b]) . op(B[b]) for b < batch, op = transpose when trans_* != 0.
  * Leading dimensions are row strides in elements.  The matmul adjoint of

@@ -1,0 +1,110 @@
+"""The DAG executor without a GPU: reading the reference's wire format,
+checking, and the storage plan (slot reuse, arena bytes).  Nothing here
+launches a kernel."""
+import ctypes
+
+import pytest
+
+from chelis_b200 import lib as L
+import _dag_programs as D
+
+
+def load(text):
+    lib = L.load()
+    h = ctypes.c_void_p()
+    raw = text.encode()
+    st = lib.chelis_dag_from_json(raw, len(raw), ctypes.byref(h))
+    return st, h
+
+
+def test_reference_wire_snapshot_parses():
+    # the exact JSON of crates/chelis-dag-core/tests/wire_behavior.rs:121-122
+    text = ('{"nodes":[{"id":0,"op":{"Load":{"name":"grads.1"}},"inputs":[],"output_type":'
+            '{"dims":[],"precision":"Int64"},"reusable_input":null,"span_id":"x","merged_spans":[],'
+            '"shape_deps":[],"result_claim_deps":[],"owner":{"decl":0,"activation":null}},{"id":1,'
+            '"op":{"Const":{"value":{"dtype":"int64","value":9007199254740993}}},"inputs":[],'
+            '"output_type":{"dims":[],"precision":"Int64"},"reusable_input":null,"span_id":"c",'
+            '"merged_spans":[],"shape_deps":[],"result_claim_deps":[],"owner":{"decl":0,'
+            '"activation":null}}],"roots":[1,0],"declarations":[{"name":"fixture","value":false}]}')
+    st, h = load(text)
+    assert st == 0, L.last_error()
+    lib = L.load()
+    try:
+        assert lib.chelis_dag_input_count(h) == 1
+        assert lib.chelis_dag_input_label(h, 0) == b"grads.1"
+        assert lib.chelis_dag_output_count(h) == 2
+        assert [lib.chelis_dag_output_label(h, i) for i in range(2)] == [b"root0", b"root1"]
+        assert lib.chelis_dag_arena_bytes(h) == 0  # the Const is written into its output
+    finally:
+        lib.chelis_dag_release(h)
+
+
+def test_plan_reuses_slots_after_last_use():
+    g = D.Dag()
+    x = g.load("x", [1000])
+    a = g.unary("Exp", x)      # slot 0
+    b = g.unary("Log", a)      # slot 1 (a is read here)
+    c = g.unary("Neg", b)      # slot 0 again (a's last reader has run)
+    d = g.unary("Exp", c)      # the output: written into its owner
+    g.roots = [d]
+    st, h = load(g.json())
+    assert st == 0, L.last_error()
+    lib = L.load()
+    try:
+        assert lib.chelis_dag_slot_count(h) == 2
+        assert lib.chelis_dag_arena_bytes(h) == 2 * 4096  # 4000 bytes rounded to 256
+        assert lib.chelis_dag_live_peak_bytes(h) == 2 * 4096
+        assert lib.chelis_dag_output_bytes(h) == 4000
+    finally:
+        lib.chelis_dag_release(h)
+
+
+def test_views_and_inlined_reductions_take_no_slots():
+    g = D.Dag()
+    x = g.load("x", [64, 32])
+    t = g.permute(x, [1, 0])                          # a view
+    e = g.fused([("Mul", (0, 0))], [t], t)            # read only by the Sum: inlined
+    s = g.sum(e, 1)
+    g.roots = [s]
+    st, h = load(g.json())
+    assert st == 0, L.last_error()
+    lib = L.load()
+    try:
+        assert lib.chelis_dag_slot_count(h) == 0
+        assert lib.chelis_dag_arena_bytes(h) == 0
+    finally:
+        lib.chelis_dag_release(h)
+
+
+def test_mlp_program_plans():
+    st, h = load(D.mlp_step_dag().json())
+    assert st == 0, L.last_error()
+    lib = L.load()
+    try:
+        assert [lib.chelis_dag_input_label(h, i) for i in range(lib.chelis_dag_input_count(h))] == \
+            [b"x", b"w1", b"b1", b"w2", b"b2", b"labels"]
+        assert lib.chelis_dag_output_count(h) == 5
+        arena, live = lib.chelis_dag_arena_bytes(h), lib.chelis_dag_live_peak_bytes(h)
+        assert 0 < live <= arena
+        # reuse: the arena is below the sum of every materialised value
+        assert arena < 2_000_000
+    finally:
+        lib.chelis_dag_release(h)
+
+
+@pytest.mark.parametrize("text,status,needle", [
+    ('{"nodes": [', 1, "malformed JSON"),
+    ('{"nodes": [], "roots": [3]}', 1, "root"),
+    ('{"nodes":[{"id":0,"op":"Iota","inputs":[],"output_type":{"dims":[{"Lit":4}],'
+     '"precision":"Int64"},"owner":{"decl":0,"activation":null}}],"roots":[0]}', 4, "Iota"),
+    ('{"nodes":[{"id":0,"op":{"Load":{"name":"x"}},"inputs":[],"output_type":{"dims":'
+     '[{"Named":["n",null]}],"precision":"F32"},"owner":{"decl":0,"activation":null}}],'
+     '"roots":[0]}', 4, "symbolic"),
+    ('{"nodes":[{"id":0,"op":"Neg","inputs":[0],"output_type":{"dims":[],"precision":"F32"},'
+     '"owner":{"decl":0,"activation":null}}],"roots":[0]}', 1, "earlier"),
+])
+def test_rejections(text, status, needle):
+    st, h = load(text)
+    assert st == status
+    assert needle in L.last_error()
+    assert not h.value

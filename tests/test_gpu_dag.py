@@ -1,0 +1,200 @@
+"""The DAG executor on the GPU: the config-1 MLP program, built the way the
+reference lowers it (tests/_dag_programs.py), run from its JSON and checked
+against the oracle's MLP step (the C lane's algorithm) within f32 rel 1e-5;
+single-op programs against numpy; the host-array entry; a caller arena."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from chelis_b200 import lib as L
+from chelis_b200 import workloads as W
+import _dag_programs as D
+
+pytestmark = pytest.mark.gpu
+
+
+def program(g):
+    h = ctypes.c_void_p()
+    raw = g.json().encode()
+    L.call("chelis_dag_from_json", raw, len(raw), ctypes.byref(h))
+    return h
+
+
+def run(h, tensors):
+    lib = L.load()
+    owners = []
+    for t in tensors:
+        t = t.contiguous()
+        dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64, torch.int64: L.DTYPE_I64}[t.dtype]
+        shape = (ctypes.c_int64 * max(t.dim(), 1))(*t.shape)
+        o = lib.chelis_device_tensor_borrow_shape(dt, t.dim(), shape, t.data_ptr(),
+                                                   t.numel() * t.element_size())
+        assert o, L.last_error()
+        owners.append(o)
+    n_out = lib.chelis_dag_output_count(h)
+    ins = (ctypes.c_void_p * len(owners))(*owners)
+    outs = (ctypes.c_void_p * n_out)()
+    L.call("chelis_dag_run_device", h, ins, len(owners), outs, n_out)
+    L.call("chelis_cuda_device_status")
+    res = []
+    for i in range(n_out):
+        v = lib.chelis_device_tensor_view(outs[i]).contents
+        shape = [v.shape[d] for d in range(v.rank)]
+        np_dt = {L.DTYPE_F32: np.float32, L.DTYPE_F64: np.float64, L.DTYPE_I64: np.int64}[v.dtype]
+        host = np.empty(shape, dtype=np_dt)
+        L.call("chelis_device_tensor_copy_to_host_bytes", host.ctypes.data, host.nbytes, outs[i])
+        res.append(host)
+        lib.chelis_device_tensor_release(outs[i])
+    L.call("chelis_cuda_synchronize")
+    for o in owners:
+        lib.chelis_device_tensor_release(o)
+    return res
+
+
+def rel(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def test_mlp_program_matches_oracle(cuda, orc):
+    x, labels, w1, b1, w2, b2 = W.mlp_inputs(seed=0)
+    h = program(D.mlp_step_dag())
+    try:
+        T = [torch.from_numpy(v).cuda() for v in (x, w1, b1, w2, b2, labels)]
+        loss, dw1, db1, dw2, db2 = run(h, T)
+        ref = orc.mlp_step(x, labels, w1, b1, w2, b2)
+        for got, want in zip((loss, dw1, db1, dw2, db2), ref):
+            assert rel(got, want) <= 1e-5
+        # twice in a row: the same bits (slots reused, nothing left over)
+        again = run(h, T)
+        for a, b in zip((loss, dw1, db1, dw2, db2), again):
+            assert np.array_equal(a, b)
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+def test_mlp_program_in_a_caller_arena(cuda, orc):
+    lib = L.load()
+    x, labels, w1, b1, w2, b2 = W.mlp_inputs(seed=0)
+    h = program(D.mlp_step_dag())
+    try:
+        T = [torch.from_numpy(v).cuda() for v in (x, w1, b1, w2, b2, labels)]
+        want = run(h, T)
+        arena = torch.empty(lib.chelis_dag_arena_bytes(h), dtype=torch.uint8, device="cuda")
+        owners = []
+        for t in T:
+            dt = {torch.float32: L.DTYPE_F32, torch.int64: L.DTYPE_I64}[t.dtype]
+            shape = (ctypes.c_int64 * t.dim())(*t.shape)
+            owners.append(lib.chelis_device_tensor_borrow_shape(dt, t.dim(), shape, t.data_ptr(),
+                                                                 t.numel() * t.element_size()))
+        ins = (ctypes.c_void_p * 6)(*owners)
+        outs = (ctypes.c_void_p * 5)()
+        assert lib.chelis_dag_run_device_arena(h, ins, 6, outs, 5, arena.data_ptr(), 16) == 1
+        L.call("chelis_dag_run_device_arena", h, ins, 6, outs, 5, arena.data_ptr(), arena.numel())
+        for i in range(5):
+            v = lib.chelis_device_tensor_view(outs[i]).contents
+            host = np.empty([v.shape[d] for d in range(v.rank)], dtype=np.float32)
+            L.call("chelis_device_tensor_copy_to_host_bytes", host.ctypes.data, host.nbytes, outs[i])
+            assert np.array_equal(host, want[i])
+            lib.chelis_device_tensor_release(outs[i])
+        for o in owners:
+            lib.chelis_device_tensor_release(o)
+    finally:
+        lib.chelis_dag_release(h)
+
+
+def single(op_builder, inputs, want):
+    g = D.Dag()
+    ids = [g.load(f"x{i}", list(a.shape), {np.float32: "f32", np.float64: "f64", np.int64: "i64"}[a.dtype.type])
+           for i, a in enumerate(inputs)]
+    g.roots = [op_builder(g, *ids)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(a).cuda() for a in inputs])
+    finally:
+        L.load().chelis_dag_release(h)
+    return got
+
+
+def test_movement_and_index_ops(cuda):
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((6, 9)).astype(np.float32)
+    idx = rng.integers(0, 9, size=(4,)).astype(np.int64)
+    # permute + stride + shrink views feeding an elementwise op
+    got = single(lambda g, a: g.unary("Neg", g.stride(g.shrink(g.permute(a, [1, 0]), [(1, 8), (0, 6)]), [2, 3])),
+                 [x], None)
+    assert np.array_equal(got, -x.T[1:8, 0:6][::2, ::3])
+    # gather along axis 1: out[r, j] = x[r, idx[j]]
+    got = single(lambda g, a, i: g.add({"Gather": {"axis": 1, "batch_rank": 0}}, [a, i], [6, 4]), [x, idx], None)
+    assert np.array_equal(got, x[:, idx])
+    # scatter-add with repeated indices (increasing update order)
+    upd = rng.standard_normal((6, 4)).astype(np.float32)
+    got = single(lambda g, a, i, u: g.add({"ScatterAdd": {"axis": 1, "batch_rank": 0}}, [a, i, u], [6, 9]),
+                 [x, idx, upd], None)
+    want = x.copy()
+    for r in range(6):
+        for j in range(4):
+            want[r, idx[j]] = np.float32(want[r, idx[j]] + upd[r, j])
+    assert np.array_equal(got, want)
+    # pad with a fill value
+    got = single(lambda g, a: g.pad(a, [(1, 2), (0, 3)], fill=7.5), [x], None)
+    want = np.full((9, 12), 7.5, np.float32)
+    want[1:7, 0:9] = x
+    assert np.array_equal(got, want)
+    # a batched matmul with a transposed operand taken in place
+    a = rng.standard_normal((3, 40, 24)).astype(np.float64)
+    b = rng.standard_normal((3, 40, 16)).astype(np.float64)
+    def bmm(g, p, q):
+        pt = g.permute(p, [0, 2, 1])
+        return g.add({"BlasMatmul": {"batch_dims": [{"Concrete": 3}], "m": {"Concrete": 24},
+                                     "n": {"Concrete": 16}, "k": {"Concrete": 40}, "accumulator": "F64"}},
+                     [pt, q], [3, 24, 16], "f64")
+    got = single(bmm, [a, b], None)
+    assert rel(got, np.einsum("bki,bkj->bij", a, b)) <= 1e-12
+
+
+def test_out_of_range_gather_index_traps(cuda):
+    x = np.ones((2, 3), np.float32)
+    idx = np.array([0, 3], np.int64)
+    g = D.Dag()
+    a = g.load("x", [2, 3])
+    i = g.load("i", [2], "i64")
+    g.roots = [g.add({"Gather": {"axis": 1, "batch_rank": 0}}, [a, i], [2, 2])]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: domain in gather"):
+            run(h, [torch.from_numpy(x).cuda(), torch.from_numpy(idx).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+def test_host_array_entry(cuda, orc):
+    """chelis_dag_run: host tensors in, runtime-owned host tensors out."""
+    lib = L.load()
+    g = D.Dag()
+    a = g.load("a", [5, 7])
+    b = g.load("b", [7], )
+    g.roots = [g.binary("Mul", a, g.expand(b, 0, 5))]
+    h = program(g)
+    rng = np.random.default_rng(2)
+    A = rng.standard_normal((5, 7)).astype(np.float32)
+    B = rng.standard_normal(7).astype(np.float32)
+    try:
+        hs = []
+        for arr in (A, B):
+            shape = (ctypes.c_int64 * arr.ndim)(*arr.shape)
+            hs.append(lib.chelis_tensor_entry_borrow(arr.ndim, shape, L.DTYPE_F32, arr.ctypes.data, arr.nbytes))
+        ins = (ctypes.c_void_p * 2)(*hs)
+        outs = (ctypes.c_void_p * 1)()
+        L.call("chelis_dag_run", h, ins, 2, outs, 1)
+        view = lib.chelis_tensor_read_view(outs[0])
+        got = np.ctypeslib.as_array(ctypes.cast(view.data, ctypes.POINTER(ctypes.c_float)), shape=(5, 7)).copy()
+        assert np.array_equal(got, A * B)
+        lib.chelis_tensor_release(outs[0])
+        for t in hs:
+            lib.chelis_tensor_release(t)
+    finally:
+        lib.chelis_dag_release(h)

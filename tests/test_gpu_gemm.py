@@ -359,3 +359,61 @@ def test_shutdown_releases_and_library_recovers(cuda, orc):
     L.call("chelis_cuda_shutdown")
     c2 = cuda.matmul(A, B).cpu().numpy()
     assert (c1.view(np.uint32) == c2.view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("m,n,k,ta,tb,batch", [(1, 1, 1, 0, 0, 1), (130, 70, 260, 0, 0, 1),
+                                                (256, 384, 512, 0, 0, 1), (64, 96, 200, 1, 0, 1),
+                                                (64, 96, 200, 0, 1, 3), (300, 129, 33, 1, 1, 2)])
+def test_gemm16_f32_accumulate(cuda, dtype, m, n, k, ta, tb, batch):
+    """bf16 / f16 storage, f32 products and sums, one rounding to the storage
+    type: |C - round16(ref)| <= half an ulp of the storage type at |ref| plus
+    the f32 accumulation bound k * 2^-23 * (|A| . |B|)."""
+    import torch
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    code = L.DTYPE_BF16 if dtype == "bf16" else L.DTYPE_F16
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    A = torch.randn((batch, k, m) if ta else (batch, m, k), device="cuda", generator=g).to(tdt)
+    B = torch.randn((batch, n, k) if tb else (batch, k, n), device="cuda", generator=g).to(tdt)
+    C = torch.empty((batch, m, n), device="cuda", dtype=tdt)
+    lda, ldb = A.shape[2], B.shape[2]
+    cuda._prepare(A)
+    L.call("chelis_cuda_gemm16", code, ta, tb, m, n, k, A.data_ptr(), lda, A[0].numel(), B.data_ptr(),
+           ldb, B[0].numel(), C.data_ptr(), n, m * n, batch)
+    torch.cuda.synchronize()
+    A64 = A.double().transpose(1, 2) if ta else A.double()
+    B64 = B.double().transpose(1, 2) if tb else B.double()
+    ref = A64 @ B64
+    bound = A64.abs() @ B64.abs()
+    ulp_half = (2.0 ** -8 if dtype == "bf16" else 2.0 ** -11) * ref.abs()
+    err = (C.double() - ref).abs()
+    assert bool((err <= ulp_half + (k + 2) * 2.0 ** -23 * bound + 1e-30).all())
+
+
+def test_gemm16_row_major_helper(cuda):
+    import ctypes
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(7)
+    A = torch.randn(70, 90, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(90, 50, device="cuda", generator=g).to(torch.bfloat16)
+    C = torch.empty(70, 50, device="cuda", dtype=torch.bfloat16)
+
+    keep = []
+
+    def desc(t):
+        shape = (ctypes.c_int64 * 2)(*t.shape)
+        strides = (ctypes.c_int64 * 2)(*t.stride())
+        keep.extend([shape, strides])
+        d = L.GpuTensor()
+        d.data, d.shape, d.strides = t.data_ptr(), shape, strides
+        d.count, d.byte_capacity, d.rank, d.dtype = t.numel(), t.numel() * 2, 2, L.DTYPE_BF16
+        return d
+
+    cuda._prepare(A)
+    da, db, dc = desc(A), desc(B), desc(C)
+    L.call("chelis_cuda_bf16_gemm_f32_acc_row_major", ctypes.byref(da), ctypes.byref(db),
+           ctypes.byref(dc), 70, 50, 90)
+    torch.cuda.synchronize()
+    ref = A.double() @ B.double()
+    bound = A.double().abs() @ B.double().abs()
+    assert bool(((C.double() - ref).abs() <= 2.0 ** -8 * ref.abs() + 92 * 2.0 ** -23 * bound).all())
