@@ -11,6 +11,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "crmath.cuh"
 
 namespace chelis {
 
@@ -62,7 +63,7 @@ __global__ void gelu_adjoint_kernel(const float *__restrict__ x, const float *__
 // row softmax s; an out-of-range label is the gather's index trap
 // ([05-OP-52], recorded in the device error word).
 __global__ void ce_nl_kernel(const float *__restrict__ s, const int64_t *__restrict__ labels,
-                             int64_t rows, int64_t classes, float *__restrict__ nl) {
+                             int64_t rows, int64_t classes, float *__restrict__ nl, int exact) {
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < rows;
          r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t label = labels[r];
@@ -71,7 +72,8 @@ __global__ void ce_nl_kernel(const float *__restrict__ s, const int64_t *__restr
             nl[r] = 0.0f;
             continue;
         }
-        nl[r] = -logf(s[r * classes + label]);
+        const float p = s[r * classes + label];
+        nl[r] = -(exact ? crmath::logf_cr(p) : logf(p));  // EXACT: CORE-MATH's bits
     }
 }
 
@@ -238,7 +240,8 @@ extern "C" int chelis_cuda_cross_entropy_f32(const float *logits, const int64_t 
     float *nl = soft + n, *q = nl + rows, *total = q + rows;
     int rc = chelis_cuda_softmax_rows_f32(logits, soft, rows, classes);
     if (rc == CHELIS_CUDA_OK) {
-        act::ce_nl_kernel<<<act_grid(rows), 256, 0, s>>>(soft, labels, rows, classes, nl);
+        act::ce_nl_kernel<<<act_grid(rows), 256, 0, s>>>(soft, labels, rows, classes, nl,
+                                                         rows_mode() == CHELIS_CUDA_ROWS_EXACT);
         g_launches++;
         rc = check_cuda(cudaGetLastError(), "act::ce_nl_kernel");
     }

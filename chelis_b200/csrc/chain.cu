@@ -30,6 +30,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "crmath.cuh"
 
 namespace chelis {
 
@@ -210,9 +211,11 @@ __device__ __forceinline__ float row_max(const float (&v)[NC][4], int n, Red<T, 
     return r;
 }
 
+// EXACT: the correctly rounded exp (CORE-MATH's results, as the C lane);
+// FAST: the MUFU approximation
 template <bool EXACT>
 __device__ __forceinline__ float exp_(float x) {
-    return EXACT ? expf(x) : __expf(x);
+    return EXACT ? crmath::expf_cr(x) : __expf(x);
 }
 template <bool EXACT>
 __device__ __forceinline__ float div_(float a, float b, float rb) {

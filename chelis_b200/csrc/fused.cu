@@ -36,6 +36,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "crmath.cuh"
 
 namespace chelis {
 
@@ -97,6 +98,13 @@ __device__ __forceinline__ float m_rint(float x) { return rintf(x); }
 __device__ __forceinline__ double m_rint(double x) { return ::rint(x); }
 __device__ __forceinline__ float m_abs(float x) { return fabsf(x); }
 __device__ __forceinline__ double m_abs(double x) { return ::fabs(x); }
+// Internal step codes past the public FusedStepOp range: f32 exp / log through
+// the correctly rounded functions (crmath.cuh) in the EXACT rows mode.
+constexpr int OP_EXP_CR = CHELIS_FUSED_ROUND + 1, OP_LOG_CR = CHELIS_FUSED_ROUND + 2;
+__device__ __forceinline__ float m_exp_cr(float x) { return crmath::expf_cr(x); }
+__device__ __forceinline__ double m_exp_cr(double x) { return ::exp(x); }
+__device__ __forceinline__ float m_log_cr(float x) { return crmath::logf_cr(x); }
+__device__ __forceinline__ double m_log_cr(double x) { return ::log(x); }
 __device__ __forceinline__ float m_exp(float x) { return expf(x); }
 __device__ __forceinline__ double m_exp(double x) { return ::exp(x); }
 __device__ __forceinline__ float m_log(float x) { return logf(x); }
@@ -167,6 +175,8 @@ __device__ __forceinline__ T apply_heavy(int op, T x, T y) {
         case CHELIS_FUSED_POW: return canon_nan(m_pow(x, y));
         case CHELIS_FUSED_EXP: return canon_nan(m_exp(x));
         case CHELIS_FUSED_LOG: return canon_nan(m_log(x));
+        case OP_EXP_CR: return canon_nan(m_exp_cr(x));
+        case OP_LOG_CR: return canon_nan(m_log_cr(x));
         case CHELIS_FUSED_SIN: return canon_nan(m_sin(x));
         case CHELIS_FUSED_COS: return canon_nan(m_cos(x));
         case CHELIS_FUSED_TAN: return canon_nan(m_tan(x));
@@ -778,8 +788,13 @@ int build_program(fused::Program &p, int &mode, const chelis_fused_step *steps, 
         if (!valid(steps[s].a) || (binary && !valid(steps[s].b)))
             return set_error(CHELIS_CUDA_ERR_DOMAIN, "fused step %d: operand out of range", s);
         p.op[s] = static_cast<uint8_t>(op);
-        switch (op) {  // libm calls with a large register or local-memory footprint
+        if (elem == 4 && rows_mode() == CHELIS_CUDA_ROWS_EXACT) {  // correctly rounded exp / log
+            if (op == CHELIS_FUSED_EXP) p.op[s] = OP_EXP_CR;
+            if (op == CHELIS_FUSED_LOG) p.op[s] = OP_LOG_CR;
+        }
+        switch (p.op[s]) {  // calls with a large register or local-memory footprint
             case CHELIS_FUSED_POW: case CHELIS_FUSED_SIN: case CHELIS_FUSED_COS: case CHELIS_FUSED_TAN:
+            case OP_EXP_CR: case OP_LOG_CR:
                 p.flags[s] |= HEAVY;
                 break;
             default: break;

@@ -39,8 +39,11 @@
 #include <vector>
 
 #include "common.cuh"
+#include "_gen/crmath_embed.inc"
 
 namespace chelis {
+int rows_mode();
+
 namespace fusedjit {
 
 constexpr int THREADS = 256;
@@ -58,6 +61,7 @@ struct Args {
 };
 
 const char *kPrelude = R"SRC(
+#include "crmath.cuh"
 struct Args {
     const void *in[8];
     void *out;
@@ -80,10 +84,19 @@ template <typename T> __device__ __forceinline__ T mx(T x, T y) { return (isnan(
 template <typename T> __device__ __forceinline__ T mn(T x, T y) { return (isnan(x) || (!isnan(y) && x <= y)) ? x : y; }
 )SRC";
 
+// f32 exp / log steps through the correctly rounded functions of crmath.cuh
+// (the EXACT rows mode: the C lane's CORE-MATH results bit for bit) rather
+// than CUDA's expf / logf; set by the entry that generates the source.
+thread_local bool t_correctly_rounded = false;
+
 // One step's expression over operands `a` (and `b`), in the dtype's spelling.
 std::string step_expr(int op, bool f32, const std::string &a, const std::string &b) {
     auto fn = [&](const char *f, const char *d) { return std::string(f32 ? f : d); };
     auto un = [&](const char *f, const char *d) { return "cn(" + fn(f, d) + "(" + a + "))"; };
+    if (f32 && t_correctly_rounded) {
+        if (op == CHELIS_FUSED_EXP) return "cn(chelis::crmath::expf_cr(" + a + "))";
+        if (op == CHELIS_FUSED_LOG) return "cn(chelis::crmath::logf_cr(" + a + "))";
+    }
     switch (op) {
         case CHELIS_FUSED_ADD: return "cn(" + fn("__fadd_rn", "__dadd_rn") + "(" + a + ", " + b + "))";
         case CHELIS_FUSED_SUB: return "cn(" + fn("__fsub_rn", "__dsub_rn") + "(" + a + ", " + b + "))";
@@ -360,7 +373,9 @@ int get_kernel(const std::string &src, CUfunction *fn) {
     const Nvrtc &n = nvrtc();
     if (!n.ok) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "NVRTC is not available");
     nvrtcProgram prog;
-    if (n.create(&prog, src.c_str(), "chelis_fused_jit.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
+    const char *headers[2] = {kEmbed_crmath_tables_cuh, kEmbed_crmath_cuh};
+    const char *names[2] = {"crmath_tables.cuh", "crmath.cuh"};
+    if (n.create(&prog, src.c_str(), "chelis_fused_jit.cu", 2, headers, names) != NVRTC_SUCCESS)
         return set_error(CHELIS_CUDA_ERR_CUDA, "nvrtcCreateProgram failed");
     const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "-ftz=false", "-prec-div=true",
                           "-prec-sqrt=true", "-default-device"};
@@ -452,6 +467,7 @@ int launch(CUfunction fn, Args &a, int64_t blocks, cudaStream_t s) {
 int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
                     int mode, void *out, cudaStream_t s) {
     if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || p.total <= 0) return -1;
+    t_correctly_rounded = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
     const int V = f32 ? 4 : 2;
     uint32_t unit = 0;
     if (p.shape[p.rank - 1] % V != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0 ||
@@ -475,6 +491,7 @@ int try_elementwise(bool f32, const chelis_fused_step *steps, int n_steps, const
 int try_reduce(bool f32, const chelis_fused_step *steps, int n_steps, const fused::Program &p,
                int mode, int axis, int kind, int64_t outputs, void *out, cudaStream_t s) {
     if (!g_enabled.load() || !nvrtc().ok || p.rank < 1 || axis != p.rank - 1 || outputs < 1) return -1;
+    t_correctly_rounded = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
     const int V = f32 ? 4 : 2;
     const int64_t len = p.shape[axis];
     const int64_t want = static_cast<int64_t>(sm_count()) * 8;

@@ -13,6 +13,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "crmath.cuh"
 
 namespace chelis {
 
@@ -61,7 +62,7 @@ __global__ void ce_rows_kernel(float *__restrict__ z, const float *__restrict__ 
     m = warp_max(m);
     nan = __any_sync(0xffffffffu, nan);
     if (nan) m = __int_as_float(0x7fc00000);
-    const float e = valid ? expf(__fsub_rn(v, m)) : 0.0f;
+    const float e = valid ? crmath::expf_cr(__fsub_rn(v, m)) : 0.0f;  // CORE-MATH's bits
     bool ve = valid;
     const float zsum = warp_tree(e, ve);
     const float s = __fdiv_rn(e, zsum);
@@ -73,7 +74,7 @@ __global__ void ce_rows_kernel(float *__restrict__ z, const float *__restrict__ 
         return;
     }
     const float s_label = __shfl_sync(0xffffffffu, s, static_cast<int>(label));
-    if (lane == 0) nl[row] = -logf(s_label);
+    if (lane == 0) nl[row] = -crmath::logf_cr(s_label);
     const float dlp = (lane == label) ? dsel : 0.0f;
     const float g = valid ? __fdiv_rn(dlp, s) : 0.0f;
     bool vq = valid;

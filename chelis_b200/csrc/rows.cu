@@ -23,6 +23,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "crmath.cuh"
 
 namespace chelis {
 
@@ -310,7 +311,10 @@ __global__ void __launch_bounds__(T)
 #pragma unroll
         for (int c = 0; c < NC; ++c)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v[c][i] = expf(__fsub_rn(v[c][i], mx));
+            for (int i = 0; i < 4; ++i) {
+                const float d = __fsub_rn(v[c][i], mx);
+                v[c][i] = EXACT ? crmath::expf_cr(d) : expf(d);  // EXACT: CORE-MATH's bits
+            }
         float z;
         if constexpr (EXACT) {
             z = block_tree<T, NC, false>(v, n, red[1]);

@@ -232,6 +232,8 @@ SIGNATURES = {
     "chelis_cuda_bf16_gemm_f32_acc_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64]),
     "chelis_cuda_f16_gemm_f32_acc_row_major": (c_int, [_P, _P, _P, c_i64, c_i64, c_i64]),
     "chelis_cuda_gemm16": (c_int, [c_i32, c_int, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64]),
+    "chelis_cuda_crmath_f32": (c_int, [c_i32, c_vp, c_vp, c_i64]),
+    "chelis_cuda_crmath_sweep_f32": (c_int, [c_i32, ctypes.c_uint32, c_i64, c_vp]),
     # DAG executor (include/chelis_dag.h)
     "chelis_dag_from_json": (c_int, [ctypes.c_char_p, c_i64, ctypes.POINTER(c_vp)]),
     "chelis_dag_release": (None, [c_vp]),

@@ -396,6 +396,14 @@ int chelis_cuda_fused_reduce(int32_t dtype, const chelis_fused_step *steps, int3
                              const void *const *inputs, const int64_t *strides, int32_t n_inputs,
                              const int64_t *shape, int32_t rank, int32_t axis, int32_t kind,
                              void *out);
+/* Correctly rounded binary32 exp / log (round to nearest even), the results
+ * of the C lane's CORE-MATH calls (crates/chelis-crmath, crmath_ffi.c:15-45)
+ * bit for bit; NaN inputs give a quiet NaN.  The EXACT rows mode and the
+ * fused groups use them.  _sweep evaluates op at the n consecutive bit
+ * patterns start, start + 1, ... (wrapping at 2^32), for exhaustive checks. */
+enum { CHELIS_CRMATH_EXP = 0, CHELIS_CRMATH_LOG = 1 };
+int chelis_cuda_crmath_f32(int32_t op, const float *x, float *y, int64_t n);
+int chelis_cuda_crmath_sweep_f32(int32_t op, uint32_t start, int64_t n, float *y);
 /* [05-OP-30] sum over the last axis / first axis of a [rows, cols] f32 tensor,
  * canonical adjacent-pair tree (kernels.rs:1703-1755 left-folds instead). */
 int chelis_cuda_row_sum_f32(const float *x, int64_t rows, int64_t cols, float *out);

@@ -39,6 +39,33 @@ float orc_erfcf(float x) { return chelis_crmath_ffi_erfcf(x); }
 double orc_exp(double x) { return chelis_crmath_ffi_exp(x); }
 double orc_sqrt(double x) { return sqrt(x); }
 
+/* Compare n results of a binary32 exp (op 0) / log (op 1) at the consecutive
+ * bit patterns start, start + 1, ... (wrapping at 2^32) with CORE-MATH: bit
+ * for bit, any NaN matching any NaN.  Returns the mismatch count and the
+ * offset of the first mismatch (-1 if none). */
+int64_t orc_crmath_check_f32(int32_t op, uint32_t start, int64_t n, const float *got,
+                             int64_t *first_bad) {
+    int64_t bad = 0, first = -1;
+#pragma omp parallel for schedule(static) reduction(+ : bad)
+    for (int64_t i = 0; i < n; ++i) {
+        uint32_t xb = start + (uint32_t)i;
+        float x;
+        memcpy(&x, &xb, 4);
+        const float want = op == 0 ? chelis_crmath_ffi_expf(x) : chelis_crmath_ffi_logf(x);
+        uint32_t wb, gb;
+        memcpy(&wb, &want, 4);
+        memcpy(&gb, &got[i], 4);
+        const int ok = (isnan(want) && isnan(got[i])) || wb == gb;
+        if (!ok) {
+            bad += 1;
+#pragma omp critical
+            if (first < 0 || i < first) first = i;
+        }
+    }
+    if (first_bad) *first_bad = first;
+    return bad;
+}
+
 /* [04-NUM-2] canonical quiet NaN (crates/chelis-backend-c/src/fp_env.rs:45-53). */
 static inline float canon_f32(float v) {
     if (isnan(v)) {

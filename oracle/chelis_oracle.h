@@ -95,6 +95,8 @@ float orc_sqrt_f32(float a);
 /* ---- CORE-MATH passthroughs for pinning against the reference fixtures ---- */
 float orc_expf(float x);
 float orc_logf(float x);
+int64_t orc_crmath_check_f32(int32_t op, uint32_t start, int64_t n, const float *got,
+                             int64_t *first_bad);
 float orc_erfcf(float x);
 double orc_exp(double x);
 double orc_sqrt(double x);

@@ -80,6 +80,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_sqrt_f32": (ctypes.c_float, [ctypes.c_float]),
         "orc_expf": (ctypes.c_float, [ctypes.c_float]),
         "orc_logf": (ctypes.c_float, [ctypes.c_float]),
+        "orc_crmath_check_f32": (ctypes.c_int64, [ctypes.c_int32, ctypes.c_uint32, ctypes.c_int64,
+                                                  ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]),
         "orc_erfcf": (ctypes.c_float, [ctypes.c_float]),
         "orc_exp": (ctypes.c_double, [ctypes.c_double]),
     }
@@ -286,6 +288,15 @@ def expf(x: float) -> float:
 
 def logf(x: float) -> float:
     return lib().orc_logf(x)
+
+
+def crmath_check_f32(op: int, start: int, got) -> tuple[int, int]:
+    """Mismatches of `got` (float32 results at bit patterns start, start+1,
+    ...) against CORE-MATH exp (op 0) / log (op 1), and the first one's offset."""
+    got = np.ascontiguousarray(got, dtype=np.float32)
+    first = ctypes.c_int64(-1)
+    bad = lib().orc_crmath_check_f32(op, start, got.size, got.ctypes.data, ctypes.byref(first))
+    return int(bad), int(first.value)
 
 
 def _fused_call(name, triplets, inputs, shape, extra):

@@ -369,3 +369,21 @@ def test_oracle_gelu_adjoint_is_the_derivative(orc):
         der = 0.5 * erfc(-xi / sqrt(2.0)) + xi * exp(-0.5 * xi * xi) / sqrt(2.0 * pi)
         ref = gi * der
         assert abs(di - ref) <= 4e-7 * max(abs(gi), 1e-30) + 1e-37, (xi, gi, di, ref)
+
+
+def test_crmath_checker_counts_mismatches(orc):
+    """The exhaustive CORE-MATH comparison itself: CORE-MATH's own results
+    pass, a planted wrong bit is found at its offset, NaNs match any NaN."""
+    start = 0x3f800000 - 500
+    bits = (np.arange(1000, dtype=np.uint64) + start).astype(np.uint32)
+    xs = bits.view(np.float32)
+    for op, f in ((0, orc.expf), (1, orc.logf)):
+        want = np.array([f(float(v)) for v in xs], dtype=np.float32)
+        assert orc.crmath_check_f32(op, start, want) == (0, -1)
+        bad = want.copy()
+        bad.view(np.uint32)[617] ^= 1
+        assert orc.crmath_check_f32(op, start, bad) == (1, 617)
+    nan_start = 0x7fc00000
+    got = np.full(4, np.float32("nan"))
+    got.view(np.uint32)[:] = 0xffc01234
+    assert orc.crmath_check_f32(0, nan_start, got) == (0, -1)
