@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int *stop = reinterpret_cast<volatile int *>(red + 6 * BQ);  // [4][BQ] stop flags
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.x);  // longest rows first
+    // heads vary fastest in launch order, so every head's longest tiles run
+    // before any shorter one (longest-first scheduling of the causal work)
+    const int bh = blockIdx.x;
+    const int qb = p.n_qblocks - 1 - static_cast<int>(blockIdx.y);  // longest rows first
     const int q0 = qb * BQ;
     int last_key = q0 + BQ - 1;
     if (last_key > p.seq - 1) last_key = p.seq - 1;
@@ -655,8 +657,8 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
     volatile int32_t *v_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 3);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int kb = blockIdx.x;           // key tile; tile 0 has the most query blocks
+    const int bh = blockIdx.x;           // heads fastest: longest tiles of every head first
+    const int kb = blockIdx.y;           // key tile; tile 0 has the most query blocks
     const int k0 = kb * BQ;
     const int i0 = k0 / BQ2;             // first query block on or below the diagonal
     const int nq = (p.seq + BQ2 - 1) / BQ2;
@@ -949,8 +951,8 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
     volatile int32_t *t_used = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = p.n_blocks - 1 - static_cast<int>(blockIdx.x);  // longest rows first
+    const int bh = blockIdx.x;                                        // heads fastest
+    const int qb = p.n_blocks - 1 - static_cast<int>(blockIdx.y);  // longest rows first
     const int q0 = qb * BQ;
     int last_key = q0 + BQ - 1;
     if (last_key > p.seq - 1) last_key = p.seq - 1;
@@ -1241,7 +1243,8 @@ int flash_fwd(int64_t bh, int64_t heads, int64_t seq, int64_t dh, float scale, c
     p.seq = static_cast<int>(seq);
     p.scale = scale;
     p.n_qblocks = static_cast<int>((seq + attn::BQ - 1) / attn::BQ);
-    dim3 grid(static_cast<unsigned>(p.n_qblocks), static_cast<unsigned>(bh));
+    if (p.n_qblocks > 65535) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "attention: sequence too long");
+    dim3 grid(static_cast<unsigned>(bh), static_cast<unsigned>(p.n_qblocks));
     auto launch = [&](auto kern, int smem) -> int {
         static uint64_t done[2] = {0, 0};
         CHELIS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(kern), smem,
@@ -1307,7 +1310,8 @@ int flash_bwd(int64_t bh, int64_t heads, int64_t seq, int64_t dh, float scale, c
     p.seq = static_cast<int>(seq);
     p.scale = scale;
     p.n_blocks = static_cast<int>((seq + attn::BQ - 1) / attn::BQ);
-    dim3 grid(static_cast<unsigned>(p.n_blocks), static_cast<unsigned>(bh));
+    if (p.n_blocks > 65535) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "attention: sequence too long");
+    dim3 grid(static_cast<unsigned>(bh), static_cast<unsigned>(p.n_blocks));
     {
         CUtensorMap mq[2], md[2], nq[2], nd[2];
         CHELIS_TRY(head_map(&mq[0], q_hi, bh, seq, d, attn::BQ2, false));

@@ -78,7 +78,17 @@ _api.PyCapsule_IsValid.restype = ctypes.c_int
 _api.PyCapsule_IsValid.argtypes = [ctypes.py_object, ctypes.c_char_p]
 _api.PyCapsule_SetName.restype = ctypes.c_int
 _api.PyCapsule_SetName.argtypes = [ctypes.py_object, ctypes.c_char_p]
-_CAPSULE_DESTRUCTOR = ctypes.CFUNCTYPE(None, ctypes.py_object)
+# The destructor runs while the capsule is being deallocated: it takes the raw
+# object pointer (a py_object argument would take a new reference to an object
+# whose count already reached zero) and queries it through raw-pointer calls.
+_CAPSULE_DESTRUCTOR = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
+_raw = ctypes.PyDLL(None)
+_raw_is_valid = _raw.PyCapsule_IsValid
+_raw_is_valid.restype = ctypes.c_int
+_raw_is_valid.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
+_raw_get_pointer = _raw.PyCapsule_GetPointer
+_raw_get_pointer.restype = ctypes.c_void_p
+_raw_get_pointer.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
 
 # exported managed tensors still owned by a capsule or a consumer:
 # address -> (struct, shape array, strides array, the DeviceTensor)
@@ -103,8 +113,8 @@ def _capsule_destructor_for(name: bytes):
     # an unconsumed capsule (name unchanged) still owns its managed tensor
     @_CAPSULE_DESTRUCTOR
     def destroy(capsule):
-        if _api.PyCapsule_IsValid(capsule, name):
-            _release_export(_api.PyCapsule_GetPointer(capsule, name))
+        if _raw_is_valid(capsule, name):
+            _release_export(_raw_get_pointer(capsule, name))
     return destroy
 
 

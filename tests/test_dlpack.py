@@ -70,3 +70,25 @@ def test_library_output_exported_to_torch(cuda):
     ref = a @ b
     assert float(((c - ref).abs() / (a.abs() @ b.abs())).max()) <= 1e-12
     assert np.isfinite(c.cpu().numpy()).all()
+
+
+def test_capsule_lifetimes_on_the_host():
+    """An unconsumed capsule releases its managed tensor when it dies; a
+    consumed one (renamed "used_dltensor") leaves that to the consumer."""
+    m = D.DLManagedTensor()
+    addr = ctypes.addressof(m)
+    D._exported[addr] = (m, None, None, None)
+    cap = D._api.PyCapsule_New(addr, b"dltensor", ctypes.cast(D._DESTROY_LEGACY, ctypes.c_void_p))
+    del cap
+    gc.collect()
+    assert addr not in D._exported
+    m2 = D.DLManagedTensor()
+    a2 = ctypes.addressof(m2)
+    D._exported[a2] = (m2, None, None, None)
+    cap = D._api.PyCapsule_New(a2, b"dltensor", ctypes.cast(D._DESTROY_LEGACY, ctypes.c_void_p))
+    D._api.PyCapsule_SetName(cap, b"used_dltensor")
+    del cap
+    gc.collect()
+    assert a2 in D._exported
+    D._legacy_deleter(ctypes.pointer(m2))   # the consumer's deleter call
+    assert a2 not in D._exported
