@@ -11,6 +11,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "gelu.cuh"
 #include "crmath.cuh"
 
 namespace chelis {
@@ -51,11 +52,7 @@ __global__ void gelu_adjoint_kernel(const float *__restrict__ x, const float *__
                                     float *__restrict__ dx, int64_t n) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float v = x[i];
-        const float pdf = __fmul_rn(0.3989422804f, expf(__fmul_rn(-0.5f, __fmul_rn(v, v))));
-        const float der = isinf(v) ? (v > 0.0f ? 1.0f : 0.0f)
-                                   : __fadd_rn(block::phi_graph(v), __fmul_rn(v, pdf));
-        dx[i] = canon(__fmul_rn(g[i], der));
+        dx[i] = canon(__fmul_rn(g[i], gelu::derivative(x[i])));
     }
 }
 

@@ -23,6 +23,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "gelu.cuh"
 
 namespace chelis {
 
@@ -264,51 +265,17 @@ __global__ void __launch_bounds__(T) softmax_scaled_bwd_kernel(const float *__re
     }
 }
 
-// ---------------------------------------------------------------------------
-// gelu = m(x) * Phi(x) with the compensated Phi graph of spec 05 section 3.3
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ float phi_graph(float x) {
-    const float c = 0x1.6a09e6p-1f;       // RN_f32(1/sqrt(2))
-    const float cl = 0x1.9fcef4p-27f;     // RN_f32(1/sqrt(2) - c)
-    const float k = 0x1.20dd76p+0f;       // RN_f32(2/sqrt(pi))
-    const float sp = 4097.0f;             // Veltkamp splitter for f32
-    const float e = erfcf(__fmul_rn(-x, c));
-    const float z = (fabsf(x) < 64.0f) ? x : 0.0f;
-    const float a = -z;
-    const float th = __fmul_rn(a, c);
-    const float ta = __fmul_rn(sp, a);
-    const float ah = __fsub_rn(ta, __fsub_rn(ta, a));
-    const float al = __fsub_rn(a, ah);
-    const float tc = __fmul_rn(sp, c);
-    const float ch = __fsub_rn(tc, __fsub_rn(tc, c));
-    const float cr = __fsub_rn(c, ch);
-    float tl = __fsub_rn(__fmul_rn(ah, ch), th);
-    tl = __fadd_rn(tl, __fmul_rn(ah, cr));
-    tl = __fadd_rn(tl, __fmul_rn(al, ch));
-    tl = __fadd_rn(tl, __fmul_rn(al, cr));
-    tl = __fadd_rn(tl, __fmul_rn(a, cl));
-    const float corr = __fmul_rn(__fmul_rn(k, expf(-__fmul_rn(th, th))), tl);
-    return __fmul_rn(0.5f, __fsub_rn(e, corr));
-}
-
+// gelu and its adjoint (gelu.cuh, shared with the GEMM epilogues)
 __global__ void gelu_fwd_kernel(const float *__restrict__ u, float *__restrict__ g, int64_t n) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float x = u[i];
-        const float m = (x < -3.40282347e+38f) ? -0.0f : x;
-        g[i] = canon(__fmul_rn(m, phi_graph(x)));
-    }
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        g[i] = gelu::value(u[i]);
 }
 
-// d gelu / dx = Phi(x) + x * phi(x), phi the standard normal density
 __global__ void gelu_bwd_kernel(const float *__restrict__ u, float *__restrict__ dg, int64_t n) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float x = u[i];
-        const float pdf = __fmul_rn(0.3989422804f, expf(__fmul_rn(-0.5f, __fmul_rn(x, x))));
-        const float der = isinf(x) ? (x > 0.0f ? 1.0f : 0.0f) : __fadd_rn(phi_graph(x), __fmul_rn(x, pdf));
-        dg[i] = canon(__fmul_rn(dg[i], der));
-    }
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dg[i] = canon(__fmul_rn(dg[i], gelu::derivative(u[i])));
 }
 
 // y = a + b
@@ -626,6 +593,24 @@ struct Matmuls {
                                                  w.slo[a_id], tb ? 0 : 1, w.shi[b_id],
                                                  w.slo[b_id], c, n, 0);
     }
+    // The product with a residual added as C is stored (tf32x3::EPI_ADD):
+    // C = A.B + in.  Without cached splits, the product then an add kernel.
+    int run_add(int ta, int tb, int64_t m, int64_t n, int64_t k, const float *a, int a_id,
+                const float *b, int b_id, float *c, const float *in, cudaStream_t s) {
+        if (!cached) {
+            CHELIS_TRY(run(ta, tb, m, n, k, a, a_id, b, b_id, c));
+            block::add_kernel<<<grid_for(m * n / 4), 256, 0, s>>>(in, c, c, m * n / 4);
+            g_launches++;
+            return check_cuda(cudaGetLastError(), "add_kernel");
+        }
+        CHELIS_TRY(split(a_id, a, ta ? k : m, ta ? m : k));
+        CHELIS_TRY(split(b_id, b, tb ? n : k, tb ? k : n));
+        tf32x3::EpiArgs e;
+        e.op = tf32x3::EPI_ADD;
+        e.in = in;
+        return sgemm_presplit_epi(m, n, k, ta ? 1 : 0, w.shi[a_id], w.slo[a_id], tb ? 0 : 1,
+                                  w.shi[b_id], w.slo[b_id], c, e);
+    }
 };
 
 }  // namespace
@@ -819,8 +804,7 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
             if ((st = check_cuda(cudaGetLastError(), "heads_permute_kernel"))) break;
         }
         mark(3, s);
-        if ((st = mx.run(0, 0, BS, D, D, w.o, S_O, p->w_o, S_WO, w.x2))) break;
-        if ((st = add(p->x, w.x2, w.x2, BS * D, s))) break;
+        if ((st = mx.run_add(0, 0, BS, D, D, w.o, S_O, p->w_o, S_WO, w.x2, p->x, s))) break;
         mark(4, s);
         if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) break;
         mark(5, s);
@@ -830,8 +814,7 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_fwd_kernel"))) break;
         mark(7, s);
-        if ((st = mx.run(0, 0, BS, D, F, w.g, S_G, p->w_2, S_W2, p->y))) break;
-        if ((st = add(w.x2, p->y, p->y, BS * D, s))) break;
+        if ((st = mx.run_add(0, 0, BS, D, F, w.g, S_G, p->w_2, S_W2, p->y, w.x2, s))) break;
         mark(8, s);
         if (!p->dy) break;
         // ---------------- reverse mode ----------------

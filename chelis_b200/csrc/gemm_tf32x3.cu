@@ -84,6 +84,22 @@ struct Params {
     int32_t splits, kb_per_split;
     float *part;
     int32_t chunk_kb;  // k-blocks per fresh accumulator (CHUNK_KB)
+    // fused epilogue (EPI_*): epi_in is indexed like C
+    int32_t epi;
+    const float *epi_in;
+};
+
+// Work folded into the store of a finished C value v at index i of C's
+// layout: EPI_ADD, C = v + in[i] (a residual add; in shares C's layout).
+// Elementwise work heavier than an add does not belong here: the epilogue
+// runs on one CTA's eight warps per SM after the tile's last MMA, so an erfc
+// per element (gelu) leaves the tensor pipe idle for its latency.  Measured:
+// gelu and its adjoint folded into the block step's epilogues (with scalar
+// stores of the tf32 splits) took the step from 10.8 to 15.0 ms at batch 8.
+enum Epi : int32_t { EPI_NONE = 0, EPI_ADD = 1 };
+struct EpiArgs {
+    int32_t op = EPI_NONE;
+    const float *in = nullptr;
 };
 
 // Operand layouts in shared memory (both written by TMA):
@@ -179,19 +195,32 @@ __device__ __forceinline__ void store_run(const float (&run)[128], int warp, int
     const int half = (warp - 2) >> 2;
     const int64_t row = m0 + quad * 32 + lane;
     if (row >= p.m) return;
-    float *crow = p.c + batch * p.stride_c + row * p.ldc;
+    const int64_t rbase = batch * p.stride_c + row * p.ldc;
+    float *crow = p.c + rbase;
+    const float *irow = p.epi == EPI_ADD ? p.epi_in + rbase : nullptr;
     const int64_t col0 = n0 + half * 128;
     const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) &&
-                        ((p.stride_c & 3) == 0);
+                        ((p.stride_c & 3) == 0) &&
+                        (!irow || (reinterpret_cast<uintptr_t>(p.epi_in) & 15) == 0);
     if (vec_ok && col0 + 128 <= p.n) {
+        if (irow) {
 #pragma unroll
-        for (int j = 0; j < 128; j += 4)
-            *reinterpret_cast<float4 *>(crow + col0 + j) =
-                make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+            for (int j = 0; j < 128; j += 4) {
+                const float4 a = *reinterpret_cast<const float4 *>(irow + col0 + j);
+                *reinterpret_cast<float4 *>(crow + col0 + j) =
+                    make_float4(__fadd_rn(run[j], a.x), __fadd_rn(run[j + 1], a.y),
+                                __fadd_rn(run[j + 2], a.z), __fadd_rn(run[j + 3], a.w));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 128; j += 4)
+                *reinterpret_cast<float4 *>(crow + col0 + j) =
+                    make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+        }
     } else {
 #pragma unroll
         for (int j = 0; j < 128; ++j)
-            if (col0 + j < p.n) crow[col0 + j] = run[j];
+            if (col0 + j < p.n) crow[col0 + j] = irow ? __fadd_rn(run[j], irow[col0 + j]) : run[j];
     }
 }
 
@@ -546,6 +575,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 q.c = p.part;
                 q.ldc = p.n;
                 q.stride_c = p.m * p.n;
+                q.epi = EPI_NONE;  // the reduction applies it to the sums
                 store_run(run, warp, lane, m0, n0, zz, q);
             } else {
                 store_run(run, warp, lane, m0, n0, batch, p);
@@ -596,9 +626,11 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ part, int splits,
 // The same sum for a dense C (ldc == n, batch items back to back) whose
 // element count is a multiple of 4: four outputs per thread, 16-byte loads
 // and stores, no index arithmetic beyond the flat offset.
+// The fused epilogue (p.epi, p.c, p.epi_*) applies to the sums.
 __global__ void splitk_reduce_dense4_kernel(const float4 *__restrict__ part, int splits,
-                                            int64_t mn4, int64_t batch, float4 *__restrict__ c) {
+                                            int64_t mn4, int64_t batch, Params p) {
     const int64_t total = batch * mn4;
+    float4 *c = reinterpret_cast<float4 *>(p.c);
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t b = batch == 1 ? 0 : i / mn4;
@@ -610,6 +642,11 @@ __global__ void splitk_reduce_dense4_kernel(const float4 *__restrict__ part, int
             acc.y = __fadd_rn(acc.y, v.y);
             acc.z = __fadd_rn(acc.z, v.z);
             acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (p.epi == EPI_ADD) {
+            const float4 a = reinterpret_cast<const float4 *>(p.epi_in)[i];
+            acc = make_float4(__fadd_rn(acc.x, a.x), __fadd_rn(acc.y, a.y), __fadd_rn(acc.z, a.z),
+                              __fadd_rn(acc.w, a.w));
         }
         c[i] = acc;
     }
@@ -1038,7 +1075,7 @@ int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMa
 int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
                       const OperandPlan &pb, const float *bhi, const float *blo, int64_t m,
                       int64_t n, int64_t k, float *c, int64_t ldc, int64_t stride_c, int64_t batch,
-                      cudaStream_t s) {
+                      cudaStream_t s, const tf32x3::EpiArgs &epi = tf32x3::EpiArgs()) {
     using namespace tf32x3;
     const bool pair = m > BM && g_pair_tiles.load();
     const int b_box = pair ? P_ROWS : BN;
@@ -1063,6 +1100,8 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     p.kb_per_split = p.num_kb;
     p.part = nullptr;
     p.chunk_kb = CHUNK_KB;
+    p.epi = epi.op;
+    p.epi_in = epi.in;
     // Split-K when the tile grid fills the GPU poorly.  Each candidate split
     // count is costed as (waves of CTA pairs) x (time of one tile: its
     // k-blocks plus a fixed prologue / epilogue) plus the HBM traffic of the
@@ -1070,7 +1109,11 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
     // the reduced result written); the cheapest wins, each split keeping at
     // least 4 k-blocks.  Times in microseconds at the tf32 pipe's pace
     // (three MMAs of K = 8, four per 32-wide k-block, ~1.15 us per k-block).
-    if (pair) {
+    // a fused epilogue on a split product runs in the 16-byte reduction only
+    const bool dense_c = ldc == n && (batch == 1 || stride_c == m * n) && (m * n) % 4 == 0 &&
+                         (reinterpret_cast<uintptr_t>(c) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(epi.in) & 15) == 0;
+    if (pair && (epi.op == tf32x3::EPI_NONE || dense_c)) {
         const int64_t clusters = sm_count() / 2;
         const int64_t pairs = ((m + 2 * P_ROWS - 1) / (2 * P_ROWS)) * ((n + BN - 1) / BN) * batch;
         if (pairs < 2 * clusters && p.num_kb >= 8) {
@@ -1117,8 +1160,7 @@ int sgemm_3xtf32_main(const OperandPlan &pa, const float *ahi, const float *alo,
             int64_t blocks = (batch * mn / 4 + 255) / 256;
             if (blocks > cap) blocks = cap;
             splitk_reduce_dense4_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-                reinterpret_cast<const float4 *>(p.part), p.splits, mn / 4, batch,
-                reinterpret_cast<float4 *>(c));
+                reinterpret_cast<const float4 *>(p.part), p.splits, mn / 4, batch, p);
         } else {
             int64_t blocks = (batch * mn + 255) / 256;
             if (blocks > cap) blocks = cap;
@@ -1217,6 +1259,22 @@ extern "C" int chelis_cuda_sgemm_tf32x3_presplit(int64_t m, int64_t n, int64_t k
     return sgemm_3xtf32_main(pa, a_hi, a_lo, pb, b_hi, b_lo, m, n, k, c, ldc, stride_c, batch,
                              current_stream());
 }
+
+namespace chelis {
+// The presplit product with a fused epilogue (tf32x3::EPI_ADD: a residual
+// added as C is stored), for the transformer block step; C dense (ldc = n),
+// one batch item.
+int sgemm_presplit_epi(int64_t m, int64_t n, int64_t k, int a_layout, const float *a_hi,
+                       const float *a_lo, int b_layout, const float *b_hi, const float *b_lo,
+                       float *c, const tf32x3::EpiArgs &epi) {
+    if (m <= 0 || n <= 0 || k <= 0)
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in matmul at i64");
+    OperandPlan pa = plan_operand(m, k, a_layout ? 1 : 2, a_layout ? 2 : 1, 1);
+    OperandPlan pb = plan_operand(n, k, b_layout ? 1 : 2, b_layout ? 2 : 1, 1);
+    return sgemm_3xtf32_main(pa, a_hi, a_lo, pb, b_hi, b_lo, m, n, k, c, n, m * n, 1,
+                             current_stream(), epi);
+}
+}  // namespace chelis
 
 extern "C" int chelis_cuda_sgemm(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
                                  const float *a, int64_t lda, int64_t stride_a, const float *b,
