@@ -142,19 +142,21 @@ __device__ __forceinline__ void load_operand(unsigned char *dst, const CUtensorM
     }
 }
 
-// Epilogue warps (2..9): fold the tile's accumulator chunks, chunk c in TMEM
-// buffer c & 1, into `run` (this thread's row, this warp's 128 columns),
-// releasing each buffer to the MMA issuer once read.  In a CTA pair the
-// release goes to rank 0's barrier (the issuer's), from both CTAs.  False
-// on a timeout or an aborted pipeline.
+// Epilogue warps (2..9): fold the tile's accumulator chunks into `run` (this
+// thread's row, this warp's 128 columns), releasing each buffer to the MMA
+// issuer once read.  Chunks are numbered from the kernel's start (c0 is this
+// tile's first): chunk c sits in TMEM buffer c & 1 and is that buffer's
+// (c >> 1)-th use.  In a CTA pair the release goes to rank 0's barrier (the
+// issuer's), from both CTAs.  False on a timeout or an aborted pipeline.
 template <bool PAIR>
-__device__ __forceinline__ bool fold_chunks(uint32_t tmem_base, int nchunks, uint64_t *chunk_full,
-                                            uint64_t *chunk_empty, int warp, int lane,
-                                            float (&run)[128], volatile uint32_t *abort_flag) {
+__device__ __forceinline__ bool fold_chunks(uint32_t tmem_base, int c0, int nchunks,
+                                            uint64_t *chunk_full, uint64_t *chunk_empty, int warp,
+                                            int lane, float (&run)[128],
+                                            volatile uint32_t *abort_flag) {
     const int quad = warp & 3;          // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;   // warps 2-5: columns 0..127, 6-9: 128..255
     const uint32_t lanes = static_cast<uint32_t>(quad * 32) << 16;
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = c0; c < c0 + nchunks; ++c) {
         const int b = c & 1;
         if (!mbar_wait_bounded(&chunk_full[b], (c >> 1) & 1, DEVERR_TIMEOUT_EPILOGUE)) {
             *abort_flag = 1;
@@ -169,7 +171,7 @@ __device__ __forceinline__ bool fold_chunks(uint32_t tmem_base, int nchunks, uin
             uint32_t r[32];
             tmem_ld_32x32b_x32(base + j * 32, r);
             tmem_wait_ld();
-            if (c == 0) {
+            if (c == c0) {
 #pragma unroll
                 for (int t = 0; t < 32; ++t) run[j * 32 + t] = __uint_as_float(r[t]);
             } else {
@@ -357,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         float run[128];
 #pragma unroll
         for (int j = 0; j < 128; ++j) run[j] = 0.0f;  // K = 0: the empty sum
-        if (fold_chunks<false>(tmem_base, nchunks, chunk_full, chunk_empty, warp, lane, run,
+        if (fold_chunks<false>(tmem_base, 0, nchunks, chunk_full, chunk_empty, warp, lane, run,
                                abort_flag))
             store_run(run, warp, lane, m0, n0, batch, p);
     }
@@ -377,8 +379,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// CTA-pair main kernel: one 256 x 256 output tile per cluster of 2 CTAs
-// (tcgen05 cta_group::2, M = 256).  Each CTA stages its 128 rows of A and
+// CTA-pair main kernel: 256 x 256 output tiles on clusters of 2 CTAs
+// (tcgen05 cta_group::2, M = 256), persistent: cluster c takes tiles c,
+// c + clusters, ... (tiles numbered batch/split-major, grouped order inside),
+// and the stage ring and the two accumulator buffers run on across tiles,
+// so the MMAs of a tile's first chunks overlap the previous tile's last fold
+// and its stores.  Each CTA stages its 128 rows of A and
 // its 128 rows of B^T (half of the tile's columns), so one pair MMA reads
 // 8 KiB of operands per SM per K-step of 8 instead of 12 KiB: the shared
 // memory port stays below its limit with the TMA writes included, and the
@@ -393,6 +399,12 @@ constexpr int P_STAGE_BYTES = 4 * P_TILE_BYTES;  // A hi, A lo, B hi, B lo
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr uint64_t P_DRAIN_NS = 200000;  // bounded drain of an aborted rank 1
 constexpr int P_GROUP = 8;                // pair-rows per group of the tile order
+// Persistent launches for tiles of at most this many k-blocks (K <= 2048 per
+// split).  Measured: K = 1024 products of the transformer block 8-10 %
+// faster persistent; 8192^3 (256 k-blocks per tile) 4 % slower, where a
+// static round-robin of ~14 tiles per cluster loses the hardware's dynamic
+// hand-out of tiles to clusters that finish early.
+constexpr int P_PERSIST_KB = 64;
 
 template <bool MN>
 __device__ __forceinline__ void load_operand_pair(unsigned char *dst, const CUtensorMap *map,
@@ -405,6 +417,37 @@ __device__ __forceinline__ void load_operand_pair(unsigned char *dst, const CUte
     } else {
         tma_load_2d_pair(dst, map, bar, kb * BK, y_kmaj);
     }
+}
+
+// Tile L of a pair launch: its rows (this CTA's 128 of A), columns (this
+// CTA's 128 of B^T), batch item, split and k-block range.  Within one batch
+// item and split, consecutive tiles walk P_GROUP pair-rows down one column of
+// tiles before moving right, so the ~74 pairs in flight share a few A and B
+// panels in L2 instead of streaming all of A.
+struct PairTile {
+    int64_t m0, n0, nb0, zz, batch;
+    int kb_lo, nk, nchunks;
+};
+__device__ __forceinline__ PairTile pair_tile(const Params &p, int64_t L, uint32_t rank) {
+    PairTile t;
+    const int64_t tiles_mn = p.pairs_m * p.tiles_n;
+    const int64_t pid = L % tiles_mn;
+    t.zz = L / tiles_mn;
+    const int64_t per_group = static_cast<int64_t>(P_GROUP) * p.tiles_n;
+    const int64_t first = (pid / per_group) * P_GROUP;
+    const int64_t rem = p.pairs_m - first;
+    const int64_t gsize = rem < P_GROUP ? rem : P_GROUP;
+    const int64_t in = pid % per_group;
+    const int64_t pm = first + in % gsize, pn = in / gsize;
+    t.m0 = pm * (2 * P_ROWS) + rank * P_ROWS;
+    t.n0 = pn * BN;
+    t.nb0 = t.n0 + rank * P_ROWS;
+    const int split = static_cast<int>(t.zz % p.splits);
+    t.batch = t.zz / p.splits;
+    t.kb_lo = split * p.kb_per_split;
+    t.nk = (p.num_kb - t.kb_lo < p.kb_per_split) ? p.num_kb - t.kb_lo : p.kb_per_split;
+    t.nchunks = (t.nk + p.chunk_kb - 1) / p.chunk_kb;
+    return t;
 }
 
 template <bool AMN, bool BMN>
@@ -431,29 +474,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
-    // Grouped tile order: consecutive pairs walk P_GROUP pair-rows down one
-    // column of tiles before moving right, so the ~74 pairs in flight share
-    // a few A and B panels in L2 instead of streaming all of A.
-    int64_t pm, pn;
-    {
-        const int64_t pid = blockIdx.x >> 1;
-        const int64_t per_group = static_cast<int64_t>(P_GROUP) * p.tiles_n;
-        const int64_t first = (pid / per_group) * P_GROUP;
-        const int64_t rem = p.pairs_m - first;
-        const int64_t gsize = rem < P_GROUP ? rem : P_GROUP;
-        const int64_t in = pid % per_group;
-        pm = first + in % gsize;
-        pn = in / gsize;
-    }
-    const int64_t m0 = pm * (2 * P_ROWS) + rank * P_ROWS;
-    const int64_t n0 = pn * BN;
-    const int64_t nb0 = n0 + rank * P_ROWS;  // this CTA's half of the columns (rows of B^T)
-    const int64_t zz = blockIdx.z;
-    const int split = static_cast<int>(zz % p.splits);
-    const int64_t batch = zz / p.splits;
-    const int kb_lo = split * p.kb_per_split;
-    const int nk = (p.num_kb - kb_lo < p.kb_per_split) ? p.num_kb - kb_lo : p.kb_per_split;
-    const int nchunks = (nk + p.chunk_kb - 1) / p.chunk_kb;
+    const int64_t total_tiles = p.pairs_m * p.tiles_n * p.batch * p.splits;
+    const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
@@ -489,28 +511,35 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
-            const int32_t ya = static_cast<int32_t>(batch * p.a_rows_per_batch + m0);
-            const int32_t yb = static_cast<int32_t>(batch * p.b_rows_per_batch + nb0);
-            const int32_t z = static_cast<int32_t>(batch);
-            for (int i = 0; i < nk; ++i) {
-                const int kb = kb_lo + i;
-                const int s = i % P_STAGES;
-                const uint32_t phase = (i / P_STAGES) & 1;
-                if (!mbar_wait_bounded(&empty[s], phase ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
-                    *abort_flag = 1;
-                    break;
+            int32_t it = 0;  // k-blocks issued since the kernel started
+            bool ok = true;
+            for (int64_t L = cluster; ok && L < total_tiles; L += clusters) {
+                const PairTile t = pair_tile(p, L, rank);
+                const int32_t ya = static_cast<int32_t>(t.batch * p.a_rows_per_batch + t.m0);
+                const int32_t yb = static_cast<int32_t>(t.batch * p.b_rows_per_batch + t.nb0);
+                const int32_t z = static_cast<int32_t>(t.batch);
+                for (int i = 0; i < t.nk; ++i, ++it) {
+                    const int kb = t.kb_lo + i;
+                    const int s = it % P_STAGES;
+                    const uint32_t phase = (it / P_STAGES) & 1;
+                    if (!mbar_wait_bounded(&empty[s], phase ^ 1, DEVERR_TIMEOUT_PRODUCER)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE_BYTES);
+                    unsigned char *st = smem + s * P_STAGE_BYTES;
+                    load_operand_pair<AMN>(st, &map_ahi, bar, kb, static_cast<int32_t>(t.m0), ya, z);
+                    load_operand_pair<AMN>(st + P_TILE_BYTES, &map_alo, bar, kb,
+                                           static_cast<int32_t>(t.m0), ya, z);
+                    load_operand_pair<BMN>(st + 2 * P_TILE_BYTES, &map_bhi, bar, kb,
+                                           static_cast<int32_t>(t.nb0), yb, z);
+                    load_operand_pair<BMN>(st + 3 * P_TILE_BYTES, &map_blo, bar, kb,
+                                           static_cast<int32_t>(t.nb0), yb, z);
+                    issued = it + 1;
                 }
-                const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
-                if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE_BYTES);
-                unsigned char *st = smem + s * P_STAGE_BYTES;
-                load_operand_pair<AMN>(st, &map_ahi, bar, kb, static_cast<int32_t>(m0), ya, z);
-                load_operand_pair<AMN>(st + P_TILE_BYTES, &map_alo, bar, kb,
-                                       static_cast<int32_t>(m0), ya, z);
-                load_operand_pair<BMN>(st + 2 * P_TILE_BYTES, &map_bhi, bar, kb,
-                                       static_cast<int32_t>(nb0), yb, z);
-                load_operand_pair<BMN>(st + 3 * P_TILE_BYTES, &map_blo, bar, kb,
-                                       static_cast<int32_t>(nb0), yb, z);
-                issued = i + 1;
+                if (*abort_flag) ok = false;
             }
         }
     } else if (warp == 1) {
@@ -518,46 +547,59 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && rank == 0) {
             constexpr uint32_t idesc = idesc_tf32(2 * P_ROWS, BN) | (AMN ? (1u << 15) : 0u) |
                                        (BMN ? (1u << 16) : 0u);
-            int cur = 0;  // accumulator buffer of the chunk in progress
-            for (int i = 0; i < nk; ++i) {
-                const int c = i / p.chunk_kb;
-                const bool first = (i % p.chunk_kb) == 0;
-                cur = c & 1;
-                // buffer `cur` last held chunk c - 2: wait until both CTAs
-                // have folded it (their epilogues arrive at cluster scope)
-                if (first && c >= 2) {
-                    if (!mbar_wait_cluster_bounded(&chunk_empty[cur], ((c >> 1) - 1) & 1,
-                                                   DEVERR_TIMEOUT_MMA)) {
+            int32_t it = 0;  // k-blocks consumed since the kernel started
+            int cc = 0;      // chunks started since the kernel started
+            int cur = 0;     // accumulator buffer of the chunk in progress
+            bool ok = true;
+            for (int64_t L = cluster; ok && L < total_tiles; L += clusters) {
+                const PairTile t = pair_tile(p, L, rank);
+                for (int i = 0; i < t.nk; ++i, ++it) {
+                    const bool first = (i % p.chunk_kb) == 0;
+                    if (first) {
+                        cur = cc & 1;
+                        // buffer `cur` last held chunk cc - 2: wait until both
+                        // CTAs have folded it (their epilogues arrive at
+                        // cluster scope)
+                        if (cc >= 2) {
+                            if (!mbar_wait_cluster_bounded(&chunk_empty[cur], ((cc >> 1) - 1) & 1,
+                                                           DEVERR_TIMEOUT_MMA)) {
+                                *abort_flag = 1;
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                    }
+                    const int s = it % P_STAGES;
+                    const uint32_t phase = (it / P_STAGES) & 1;
+                    if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
                         *abort_flag = 1;
+                        ok = false;
                         break;
                     }
                     tc_fence_after();
-                }
-                const int s = i % P_STAGES;
-                const uint32_t phase = (i / P_STAGES) & 1;
-                if (!mbar_wait_bounded(&full[s], phase, DEVERR_TIMEOUT_MMA)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t st = smem_u32(smem + s * P_STAGE_BYTES);
-                const uint32_t ahi = st, alo = st + P_TILE_BYTES;
-                const uint32_t bhi = st + 2 * P_TILE_BYTES, blo = st + 3 * P_TILE_BYTES;
-                const uint32_t d = tmem_base + static_cast<uint32_t>(cur) * ACC_COLS;
+                    const uint32_t st = smem_u32(smem + s * P_STAGE_BYTES);
+                    const uint32_t ahi = st, alo = st + P_TILE_BYTES;
+                    const uint32_t bhi = st + 2 * P_TILE_BYTES, blo = st + 3 * P_TILE_BYTES;
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(cur) * ACC_COLS;
 #pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
-                    mma_tf32_ss_pair(d, operand_desc<AMN>(alo, kk), operand_desc<BMN>(bhi, kk),
-                                     idesc, acc);
-                    mma_tf32_ss_pair(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(blo, kk),
-                                     idesc, 1u);
-                    mma_tf32_ss_pair(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(bhi, kk),
-                                     idesc, 1u);
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+                        mma_tf32_ss_pair(d, operand_desc<AMN>(alo, kk), operand_desc<BMN>(bhi, kk),
+                                         idesc, acc);
+                        mma_tf32_ss_pair(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(blo, kk),
+                                         idesc, 1u);
+                        mma_tf32_ss_pair(d, operand_desc<AMN>(ahi, kk), operand_desc<BMN>(bhi, kk),
+                                         idesc, 1u);
+                    }
+                    mma_commit_pair(&empty[s], 0x3);
+                    *consumed = it + 1;
+                    if ((i % p.chunk_kb) == p.chunk_kb - 1 || i == t.nk - 1) {
+                        mma_commit_pair(&chunk_full[cur], 0x3);
+                        ++cc;
+                    }
                 }
-                mma_commit_pair(&empty[s], 0x3);
-                *consumed = i + 1;
-                if ((i % p.chunk_kb) == p.chunk_kb - 1 || i == nk - 1)
-                    mma_commit_pair(&chunk_full[cur], 0x3);
+                if (*abort_flag) ok = false;
             }
             // on abort, release both epilogues waiting for the unfinished
             // chunk; rank 0 skips its stores
@@ -565,20 +607,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // ---------------- epilogue (warps 2..9, both CTAs) ----------------
-        float run[128];
+        int cc = 0;  // chunks folded since the kernel started
+        for (int64_t L = cluster; L < total_tiles; L += clusters) {
+            const PairTile t = pair_tile(p, L, rank);
+            float run[128];
 #pragma unroll
-        for (int j = 0; j < 128; ++j) run[j] = 0.0f;  // K = 0: the empty sum
-        if (fold_chunks<true>(tmem_base, nchunks, chunk_full, chunk_empty, warp, lane, run,
-                              abort_flag)) {
+            for (int j = 0; j < 128; ++j) run[j] = 0.0f;  // K = 0: the empty sum
+            if (!fold_chunks<true>(tmem_base, cc, t.nchunks, chunk_full, chunk_empty, warp, lane,
+                                   run, abort_flag))
+                break;
+            cc += t.nchunks;
             if (p.splits > 1) {
                 Params q = p;
                 q.c = p.part;
                 q.ldc = p.n;
                 q.stride_c = p.m * p.n;
                 q.epi = EPI_NONE;  // the reduction applies it to the sums
-                store_run(run, warp, lane, m0, n0, zz, q);
+                store_run(run, warp, lane, t.m0, t.n0, t.zz, q);
             } else {
-                store_run(run, warp, lane, m0, n0, batch, p);
+                store_run(run, warp, lane, t.m0, t.n0, t.batch, p);
             }
         }
     }
@@ -1025,6 +1072,42 @@ int ensure_smem_attr(const void *fn, int bytes, uint64_t *done_mask, const char 
     return CHELIS_CUDA_OK;
 }
 
+// Clusters of the pair kernel that fit on the device at once (its shared
+// memory allows one CTA per SM, and a pair needs two SMs of one GPC), once
+// per (kernel, device); the persistent grid launches no more than this.
+template <bool AMN, bool BMN>
+int pair_clusters(int *out) {
+    using namespace tf32x3;
+    static std::atomic<int> cached[64];
+    int d = 0;
+    CHELIS_TRY(current_device_checked(&d));
+    if (d < 64) {
+        const int c = cached[d].load(std::memory_order_relaxed);
+        if (c > 0) {
+            *out = c;
+            return CHELIS_CUDA_OK;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(sm_count()), 1, 1);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    CHELIS_TRY(check_cuda(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<AMN, BMN>, &cfg),
+                          "cudaOccupancyMaxActiveClusters(gemm_pair_kernel)"));
+    if (n < 1) return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "no CTA pair of the matmul kernel fits");
+    if (d < 64) cached[d].store(n, std::memory_order_relaxed);
+    *out = n;
+    return CHELIS_CUDA_OK;
+}
+
 template <bool AMN, bool BMN>
 int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMap &bhi,
                 const CUtensorMap &blo, const tf32x3::Params &p, bool pair, cudaStream_t s) {
@@ -1037,10 +1120,20 @@ int launch_main(const CUtensorMap &ahi, const CUtensorMap &alo, const CUtensorMa
         Params q = p;
         q.pairs_m = (p.m + 2 * P_ROWS - 1) / (2 * P_ROWS);
         q.tiles_n = (p.n + BN - 1) / BN;
-        if (2 * q.pairs_m * q.tiles_n > INT32_MAX)
-            return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "matmul tile count beyond 2^31");
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * q.pairs_m * q.tiles_n), 1,
-                           static_cast<unsigned>(p.batch * p.splits));
+        const int64_t tiles = q.pairs_m * q.tiles_n * p.batch * p.splits;
+        if (tiles == 0) return CHELIS_CUDA_OK;
+        // Short tiles (few k-blocks) run persistently, so one tile's setup and
+        // stores overlap the next one's MMAs; long tiles get one cluster
+        // each, so the hardware hands tiles to clusters as they free up.
+        int64_t clusters = tiles;
+        if (p.kb_per_split <= P_PERSIST_KB) {
+            int max_clusters = 0;
+            CHELIS_TRY((pair_clusters<AMN, BMN>(&max_clusters)));
+            if (clusters > max_clusters) clusters = max_clusters;
+        }
+        if (2 * clusters > INT32_MAX)
+            return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "matmul tile count beyond 2^30");
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
         cfg.blockDim = dim3(THREADS);
         cfg.dynamicSmemBytes = P_SMEM_BYTES;
         cfg.stream = s;
