@@ -278,6 +278,47 @@ __global__ void gelu_bwd_kernel(const float *__restrict__ u, float *__restrict__
         dg[i] = canon(__fmul_rn(dg[i], gelu::derivative(u[i])));
 }
 
+// The same two maps written straight into the tf32 split of their result
+// (hi = RN_tf32(v), lo = RN_tf32(v - hi), lo = 0 for non-finite v: the split
+// cache's layout for a row-major [rows][F] tensor when F % 32 == 0), four
+// elements per thread: the result itself is only ever read through its
+// split, so it is never stored, and the matmuls that consume it skip their
+// split pre-pass.
+__device__ __forceinline__ void split_store(float4 *__restrict__ hi, float4 *__restrict__ lo, int64_t i,
+                                            const float (&v)[4]) {
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        h[j] = tf32x3::rna_tf32(v[j]);
+        l[j] = isfinite(v[j]) ? tf32x3::rna_tf32(__fsub_rn(v[j], h[j])) : 0.0f;
+    }
+    hi[i] = make_float4(h[0], h[1], h[2], h[3]);
+    lo[i] = make_float4(l[0], l[1], l[2], l[3]);
+}
+
+__global__ void gelu_fwd_split_kernel(const float4 *__restrict__ u, float4 *__restrict__ hi,
+                                      float4 *__restrict__ lo, int64_t n4) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 x = u[i];
+        const float v[4] = {gelu::value(x.x), gelu::value(x.y), gelu::value(x.z), gelu::value(x.w)};
+        split_store(hi, lo, i, v);
+    }
+}
+
+__global__ void gelu_bwd_split_kernel(const float4 *__restrict__ u, const float4 *__restrict__ dg,
+                                      float4 *__restrict__ hi, float4 *__restrict__ lo, int64_t n4) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 x = u[i], d = __ldcs(dg + i);
+        const float v[4] = {canon(__fmul_rn(d.x, gelu::derivative(x.x))),
+                            canon(__fmul_rn(d.y, gelu::derivative(x.y))),
+                            canon(__fmul_rn(d.z, gelu::derivative(x.z))),
+                            canon(__fmul_rn(d.w, gelu::derivative(x.w)))};
+        split_store(hi, lo, i, v);
+    }
+}
+
 // y = a + b
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b,
                            float *__restrict__ y, int64_t n4) {
@@ -810,7 +851,14 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
         mark(5, s);
         if ((st = mx.run(0, 0, BS, F, D, w.h2, S_H2, p->w_1, S_W1, w.u))) break;
         mark(6, s);
-        block::gelu_fwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.g, BS * F);
+        if (mx.cached) {
+            block::gelu_fwd_split_kernel<<<grid_for(BS * F / 4), 256, 0, s>>>(
+                reinterpret_cast<const float4 *>(w.u), reinterpret_cast<float4 *>(w.shi[S_G]),
+                reinterpret_cast<float4 *>(w.slo[S_G]), BS * F / 4);
+            mx.done[S_G] = true;
+        } else {
+            block::gelu_fwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.g, BS * F);
+        }
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_fwd_kernel"))) break;
         mark(7, s);
@@ -823,7 +871,15 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
         if ((st = gr.reduce(p->dw_2, F * D, s))) break;
         if ((st = mx.run(0, 1, BS, F, D, dy, S_DY, p->w_2, S_W2, w.dg))) break;
         mark(9, s);
-        block::gelu_bwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.dg, BS * F);
+        if (mx.cached) {
+            block::gelu_bwd_split_kernel<<<grid_for(BS * F / 4), 256, 0, s>>>(
+                reinterpret_cast<const float4 *>(w.u), reinterpret_cast<const float4 *>(w.dg),
+                reinterpret_cast<float4 *>(w.shi[S_DG]), reinterpret_cast<float4 *>(w.slo[S_DG]),
+                BS * F / 4);
+            mx.done[S_DG] = true;
+        } else {
+            block::gelu_bwd_kernel<<<grid_for(BS * F), 256, 0, s>>>(w.u, w.dg, BS * F);
+        }
         g_launches++;
         if ((st = check_cuda(cudaGetLastError(), "gelu_bwd_kernel"))) break;
         mark(10, s);
