@@ -44,6 +44,21 @@ using chain::stage;
 using chain::tree4;
 using chain::tree_parts;
 
+// hi = RN_tf32(v), lo = RN_tf32(v - hi) (lo = 0 for non-finite v) of four
+// results, stored as element group i of the split: the transformer step's
+// producers write the split of a tensor that the matmuls only read split.
+__device__ __forceinline__ void split_store(float4 *__restrict__ hi, float4 *__restrict__ lo, int64_t i,
+                                            const float (&v)[4]) {
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        h[j] = tf32x3::rna_tf32(v[j]);
+        l[j] = isfinite(v[j]) ? tf32x3::rna_tf32(__fsub_rn(v[j], h[j])) : 0.0f;
+    }
+    hi[i] = make_float4(h[0], h[1], h[2], h[3]);
+    lo[i] = make_float4(l[0], l[1], l[2], l[3]);
+}
+
 // ---------------------------------------------------------------------------
 // layer_norm forward, saving (mean, sqrt(var + eps)) per row
 // ---------------------------------------------------------------------------
@@ -52,7 +67,8 @@ __global__ void __launch_bounds__(T) ln_fwd_kernel(const float *__restrict__ x,
                                                    const float *__restrict__ gamma,
                                                    const float *__restrict__ beta, float eps,
                                                    float *__restrict__ y, float2 *__restrict__ stats,
-                                                   int64_t rows, int n) {
+                                                   int64_t rows, int n, float *__restrict__ yhi,
+                                                   float *__restrict__ ylo) {
     extern __shared__ __align__(16) float smem[];
     float *sg = smem, *sb = sg + NC * 4 * T;
     Red<T, NC> rs{sb + NC * 4 * T};
@@ -78,8 +94,7 @@ __global__ void __launch_bounds__(T) ln_fwd_kernel(const float *__restrict__ x,
         const float d = __fsqrt_rn(__fadd_rn(var, eps));
         const float rd = __fdiv_rn(1.0f, d);
         if (threadIdx.x == 0) stats[r] = make_float2(mean, d);
-        if (y == nullptr) continue;  // statistics only (the standalone layer_norm adjoint)
-        float *yr = y + r * n;
+        if (y == nullptr && yhi == nullptr) continue;  // statistics only (the standalone layer_norm adjoint)
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const float4 g4 = ld4<T>(sg, c), b4 = ld4<T>(sb, c);
@@ -88,6 +103,14 @@ __global__ void __launch_bounds__(T) ln_fwd_kernel(const float *__restrict__ x,
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 o[i] = canon(__fadd_rn(__fmul_rn(div_<EXACT>(v[c][i], d, rd), at(g4, i)), at(b4, i)));
+            if (yhi != nullptr) {
+                // the tf32 split of y only (n % 32 == 0: the split cache's
+                // [rows][n] layout), y itself is read through it alone
+                if (e0 + 3 < n) split_store(reinterpret_cast<float4 *>(yhi + r * n),
+                                            reinterpret_cast<float4 *>(ylo + r * n), e0 / 4, o);
+                continue;
+            }
+            float *yr = y + r * n;
             if (vec && e0 + 3 < n) *reinterpret_cast<float4 *>(yr + e0) = make_float4(o[0], o[1], o[2], o[3]);
             else
 #pragma unroll
@@ -284,18 +307,6 @@ __global__ void gelu_bwd_kernel(const float *__restrict__ u, float *__restrict__
 // elements per thread: the result itself is only ever read through its
 // split, so it is never stored, and the matmuls that consume it skip their
 // split pre-pass.
-__device__ __forceinline__ void split_store(float4 *__restrict__ hi, float4 *__restrict__ lo, int64_t i,
-                                            const float (&v)[4]) {
-    float h[4], l[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        h[j] = tf32x3::rna_tf32(v[j]);
-        l[j] = isfinite(v[j]) ? tf32x3::rna_tf32(__fsub_rn(v[j], h[j])) : 0.0f;
-    }
-    hi[i] = make_float4(h[0], h[1], h[2], h[3]);
-    lo[i] = make_float4(l[0], l[1], l[2], l[3]);
-}
-
 __global__ void gelu_fwd_split_kernel(const float4 *__restrict__ u, float4 *__restrict__ hi,
                                       float4 *__restrict__ lo, int64_t n4) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
@@ -526,7 +537,7 @@ int smem_attr(K k, size_t bytes) {
 }
 
 int ln_fwd(const float *x, const float *g, const float *b, float eps, float *y, float2 *st,
-           int64_t rows, int64_t n, cudaStream_t s) {
+           int64_t rows, int64_t n, cudaStream_t s, float *yhi = nullptr, float *ylo = nullptr) {
     const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
     return with_rows_nc(n, [&](auto ncv) -> int {
         constexpr int NC = decltype(ncv)::value;
@@ -534,10 +545,10 @@ int ln_fwd(const float *x, const float *g, const float *b, float eps, float *y, 
         const unsigned grid = static_cast<unsigned>(rows < sm_count() * 8 ? rows : sm_count() * 8);
         if (exact) {
             CHELIS_TRY(smem_attr(block::ln_fwd_kernel<256, NC, true>, smem));
-            block::ln_fwd_kernel<256, NC, true><<<grid, 256, smem, s>>>(x, g, b, eps, y, st, rows, static_cast<int>(n));
+            block::ln_fwd_kernel<256, NC, true><<<grid, 256, smem, s>>>(x, g, b, eps, y, st, rows, static_cast<int>(n), yhi, ylo);
         } else {
             CHELIS_TRY(smem_attr(block::ln_fwd_kernel<256, NC, false>, smem));
-            block::ln_fwd_kernel<256, NC, false><<<grid, 256, smem, s>>>(x, g, b, eps, y, st, rows, static_cast<int>(n));
+            block::ln_fwd_kernel<256, NC, false><<<grid, 256, smem, s>>>(x, g, b, eps, y, st, rows, static_cast<int>(n), yhi, ylo);
         }
         g_launches++;
         CHELIS_LAUNCH_CHECK("ln_fwd_kernel");
@@ -816,7 +827,14 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
     do {
         // ---------------- forward ----------------
         mark(0, s);
-        if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, w.h1, w.st1, BS, D, s))) break;
+        if (mx.cached) {
+            if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, nullptr, w.st1, BS, D, s,
+                             w.shi[S_H1], w.slo[S_H1])))
+                break;
+            mx.done[S_H1] = true;
+        } else if ((st = ln_fwd(p->x, p->ln1_gamma, p->ln1_beta, p->eps, w.h1, w.st1, BS, D, s))) {
+            break;
+        }
         mark(1, s);
         if ((st = mx.run(0, 0, BS, 3 * D, D, w.h1, S_H1, p->w_qkv, S_WQKV, w.qkv))) break;
         mark(2, s);
@@ -847,7 +865,14 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
         mark(3, s);
         if ((st = mx.run_add(0, 0, BS, D, D, w.o, S_O, p->w_o, S_WO, w.x2, p->x, s))) break;
         mark(4, s);
-        if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) break;
+        if (mx.cached) {
+            if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, nullptr, w.st2, BS, D, s,
+                             w.shi[S_H2], w.slo[S_H2])))
+                break;
+            mx.done[S_H2] = true;
+        } else if ((st = ln_fwd(w.x2, p->ln2_gamma, p->ln2_beta, p->eps, w.h2, w.st2, BS, D, s))) {
+            break;
+        }
         mark(5, s);
         if ((st = mx.run(0, 0, BS, F, D, w.h2, S_H2, p->w_1, S_W1, w.u))) break;
         mark(6, s);

@@ -13,9 +13,9 @@
 // keyed-dropout keep bits (one bit per element, warp-ballot packed), so the
 // adjoint re-derives nothing that needs a reduction or the RNG.
 //
-// Shared memory holds gamma / beta (and the adjoint's dgamma / dbeta
-// partials) in the same chunk layout, accessed as float4 so a warp's access
-// is conflict-free.  Block reductions alternate between two scratch areas,
+// Shared memory holds gamma / beta in the same chunk layout, accessed as
+// float4 so a warp's access is conflict-free; the adjoint keeps its dgamma /
+// dbeta partials in registers (a thread owns the same columns in every row).  Block reductions alternate between two scratch areas,
 // so each costs one barrier.
 //
 // Modes: EXACT divides where the C lane divides (IEEE __fdiv_rn) and uses
@@ -286,7 +286,9 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // rows ahead, so a CTA's next rows stream in while it works on this one.
 template <int T, int NC>
 struct RowRing {
-    static constexpr int RING = 2;
+    // rows in flight per CTA: one being read, three landing (two CTAs per SM
+    // at hidden 4096 keep ~100 KB of rows in flight per SM)
+    static constexpr int RING = 4;
     static constexpr int L = NC * 4 * T;
     static constexpr int WORDS = NC * T / 8;
     static constexpr int SLOT = L + WORDS + 4;  // floats
@@ -525,9 +527,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
     constexpr int L = NC * 4 * T;
     float *sg = smem;          // gamma
     float *sb = sg + L;        // beta
-    float *pg = sb + L;        // dgamma partial of this CTA
-    float *pb = pg + L;        // dbeta partial of this CTA
-    Red<T, NC> rs{pb + L};
+    Red<T, NC> rs{sb + L};
     const int n = FULL ? NC * 4 * T : p.hidden;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
                       ((reinterpret_cast<uintptr_t>(p.keep_in) & 15) == 0) &&
                       ((reinterpret_cast<uintptr_t>(p.stats_in) & 15) == 0);
     RowRing<T, NC> rr;
-    rr.base = pb + L + 2 * (NC * (T / 32) + 8);
+    rr.base = sb + L + 2 * (NC * (T / 32) + 8);
     rr.full = reinterpret_cast<uint64_t *>(rr.base + RowRing<T, NC>::RING * RowRing<T, NC>::SLOT);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(rr.full + 2 * RowRing<T, NC>::RING);
     const int64_t r_begin = static_cast<int64_t>(blockIdx.x) * p.rows_per_cta;
@@ -551,8 +551,6 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
     }
     stage<NC, T>(sg, p.gamma, n);
     stage<NC, T>(sb, p.beta, n);
-    stage<NC, T>(pg, nullptr, n);
-    stage<NC, T>(pb, nullptr, n);
     __syncthreads();
     int64_t issued = r_begin + RowRing<T, NC>::RING;  // next row to stream (thread 0)
     // this CTA's dgamma / dbeta partials for the columns this thread owns,
@@ -820,17 +818,25 @@ __global__ void __launch_bounds__(T, NC >= 8 ? 1 : 2) bwd_kernel(Params p) {
                               DEVERR_TIMEOUT_PRODUCER);
         }
     }
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-        reinterpret_cast<float4 *>(pg)[c * T + threadIdx.x] = acc_g[c];
-        reinterpret_cast<float4 *>(pb)[c * T + threadIdx.x] = acc_b[c];
-    }
-    __syncthreads();
+    // this CTA's partials: the thread's columns of chunk c are [e0, e0 + 4)
     float *og = p.dgamma_part + static_cast<int64_t>(blockIdx.x) * n;
     float *ob = p.dbeta_part + static_cast<int64_t>(blockIdx.x) * n;
-    for (int e = threadIdx.x; e < n; e += T) {
-        og[e] = pg[e];
-        ob[e] = pb[e];
+    const bool vec_out = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.dgamma_part) & 15) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(p.dbeta_part) & 15) == 0);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int e0 = c * 4 * T + 4 * threadIdx.x;
+        if (vec_out && e0 + 3 < n) {
+            *reinterpret_cast<float4 *>(og + e0) = acc_g[c];
+            *reinterpret_cast<float4 *>(ob + e0) = acc_b[c];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (e0 + i < n) {
+                    og[e0 + i] = at(acc_g[c], i);
+                    ob[e0 + i] = at(acc_b[c], i);
+                }
+        }
     }
 }
 
@@ -922,7 +928,7 @@ int launch_chain_bwd(const ChainParams &p, int grid, cudaStream_t s) {
     const bool exact = rows_mode() == CHELIS_CUDA_ROWS_EXACT;
     return with_nc(p.hidden, [&](auto ncv) -> int {
         constexpr int NC = decltype(ncv)::value;
-        const size_t smem = 4 * NC * 4 * T * sizeof(float) + red_bytes<T, NC>() +
+        const size_t smem = 2 * NC * 4 * T * sizeof(float) + red_bytes<T, NC>() +
                             chain::RowRing<T, NC>::bytes() + 16;
         const bool full = p.hidden == NC * 4 * T;
         auto go = [&](auto kern) -> int {
@@ -941,8 +947,8 @@ int launch_chain_bwd(const ChainParams &p, int grid, cudaStream_t s) {
 }  // namespace
 
 int chain_bwd_grid(int64_t rows) {
-    // two resident CTAs per SM (shared memory: gamma, beta, two partials and
-    // the row ring), each owning a contiguous run of rows
+    // two resident CTAs per SM at hidden <= 4096 (shared memory: gamma, beta
+    // and the row ring), each owning a contiguous run of rows
     int64_t g = static_cast<int64_t>(sm_count()) * 2;
     return static_cast<int>(rows < g ? (rows < 1 ? 1 : rows) : g);
 }
