@@ -549,6 +549,9 @@ struct BwdParams {
     const float *lse, *dsum;         // [BH][S]
     float *dq, *dk, *dv;             // outputs, strides below
     int64_t g_row, g_b, g_h;
+    // 0: the gradients as f32; else their tf32 split, hi at dq / dk / dv and
+    // lo split_lo floats further on (a matmul reads them only split)
+    int64_t split_lo;
     int heads, seq;
     float scale;
     int n_blocks;
@@ -611,6 +614,24 @@ __device__ __forceinline__ void write_row_half(const float (&acc)[DH / 2], float
 #pragma unroll
     for (int i = 0; i < DH / 2; i += 4)
         *reinterpret_cast<float4 *>(dst + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+}
+// The same row half as its tf32 split: hi = RN_tf32(v) at dst, lo =
+// RN_tf32(v - hi) at dst + lo_off (lo = 0 for non-finite v); lo_off = 0
+// writes the f32 values.
+template <int DH>
+__device__ __forceinline__ void write_row_half_out(const float (&acc)[DH / 2], float *dst, int64_t lo_off) {
+    if (lo_off == 0) {
+        write_row_half<DH>(acc, dst);
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < DH / 2; i += 4) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) split_tf32(acc[i + j], h[j], l[j]);
+        *reinterpret_cast<uint4 *>(dst + i) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4 *>(dst + lo_off + i) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
 }
 
 template <int DH>
@@ -898,8 +919,8 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
         if (ok && !*abort_flag && live) {
             const int64_t g = b * p.g_b + h * p.g_h + static_cast<int64_t>(key) * p.g_row +
                               half * (DH / 2);
-            write_row_half<DH>(dk_acc, p.dk + g);
-            write_row_half<DH>(dv_acc, p.dv + g);
+            write_row_half_out<DH>(dk_acc, p.dk + g, p.split_lo);
+            write_row_half_out<DH>(dv_acc, p.dv + g, p.split_lo);
         }
     }
 
@@ -1127,8 +1148,9 @@ __global__ void __launch_bounds__(THREADS_BWD, 1)
             tc_fence_before();
         }
         if (ok && !*abort_flag && live)
-            write_row_half<DH>(dq_acc, p.dq + b * p.g_b + h * p.g_h +
-                                           static_cast<int64_t>(qrow) * p.g_row + half * (DH / 2));
+            write_row_half_out<DH>(dq_acc, p.dq + b * p.g_b + h * p.g_h +
+                                               static_cast<int64_t>(qrow) * p.g_row + half * (DH / 2),
+                                   p.split_lo);
     }
 
     tc_fence_before();
@@ -1270,7 +1292,8 @@ int flash_bwd(int64_t bh, int64_t heads, int64_t seq, int64_t dh, float scale, c
               int64_t o_row, int64_t o_b, int64_t o_h, const float *lse, const float *q_hi,
               const float *q_lo, const float *k_hi, const float *k_lo, const float *v_hi,
               const float *v_lo, const float *do_hi, const float *do_lo, float *dsum, float *dq,
-              float *dk, float *dv, int64_t g_row, int64_t g_b, int64_t g_h, cudaStream_t s) {
+              float *dk, float *dv, int64_t g_row, int64_t g_b, int64_t g_h, cudaStream_t s,
+              int64_t split_lo = 0) {
     if (!flash_attention_supported(dh))
         return set_error(CHELIS_CUDA_ERR_UNSUPPORTED, "flash attention covers head dims 32, 64");
     if (bh > 65535 || seq > (1 << 24))
@@ -1306,6 +1329,7 @@ int flash_bwd(int64_t bh, int64_t heads, int64_t seq, int64_t dh, float scale, c
     p.g_row = g_row;
     p.g_b = g_b;
     p.g_h = g_h;
+    p.split_lo = split_lo;
     p.heads = static_cast<int>(heads);
     p.seq = static_cast<int>(seq);
     p.scale = scale;

@@ -926,12 +926,16 @@ int block_step_impl(const chelis_block_params *p, void *workspace, bool reduce_g
                 static_cast<int>(H), d4);
             g_launches++;
             if ((st = check_cuda(cudaGetLastError(), "rows_heads_split_kernel"))) break;
-            // dq, dk, dv straight into the [B, S, 3, H, Dh] layout of dqkv
+            // dq, dk, dv straight into the [B, S, 3, H, Dh] layout of dqkv, or
+            // of its tf32 split when the matmuls read dqkv through the split
+            float *gq = mx.cached ? w.shi[S_DQKV] : w.dqkv;
+            const int64_t split_lo = mx.cached ? w.slo[S_DQKV] - w.shi[S_DQKV] : 0;
             if ((st = flash_bwd(BH, H, S, Dh, scale, w.q, w.k, w.v, Dh, H * S * Dh, S * Dh, w.dO, D,
                                 S * D, Dh, w.o, D, S * D, Dh, w.lse, hl, hl + act, hl + 2 * act,
                                 hl + 3 * act, hl + 4 * act, hl + 5 * act, hl + 6 * act, hl + 7 * act,
-                                w.dsum, w.dqkv, w.dqkv + D, w.dqkv + 2 * D, 3 * D, S * 3 * D, Dh, s)))
+                                w.dsum, gq, gq + D, gq + 2 * D, 3 * D, S * 3 * D, Dh, s, split_lo)))
                 break;
+            if (mx.cached) mx.done[S_DQKV] = true;
         } else {
             block::heads_permute_kernel<<<grid_for(BS * D / 4), 256, 0, s>>>(
                 w.doh, w.dO, static_cast<int>(d.B), static_cast<int>(S), static_cast<int>(H), d4, 1);
