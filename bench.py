@@ -636,7 +636,8 @@ def bench_rows(args, peaks, with_cpu):
     mlp = {"us_per_step": round(ms * 1e3, 1), "launches_per_step": launches,
            "roofline": {"bound": "latency", "achieved": round(flop / (ms * 1e-3) / 1e12, 3),
                         "unit": "TFLOP/s", "flop_per_step": flop,
-                        "note": "1.05e8 FLOP over launches_per_step dependent kernels"}}
+                        "note": "1.05e8 FLOP over launches_per_step dependent kernels; repeated "
+                                "calls replay them as one captured CUDA graph"}}
     if with_cpu:
         cores = use_all_host_cores()
         from oracle import oracle as O

@@ -8,6 +8,7 @@ namespace chelis {
 int release_pools();
 namespace fusedjit { int release_all(); }
 namespace hostgemm { void release_streams(); }
+void mlp_release_graphs();
 }  // namespace chelis
 namespace grad_reduce { void release_events(); }
 namespace block_timing { void release(); }
@@ -20,6 +21,7 @@ extern "C" int chelis_cuda_shutdown(void) {
     };
     keep_first(chelis_cuda_dp_finalize(0));
     block_timing::release();
+    mlp_release_graphs();
     grad_reduce::release_events();
     hostgemm::release_streams();
     keep_first(fusedjit::release_all());

@@ -74,3 +74,39 @@ def test_chain_forward_exact_mode_bit_exact(cuda, orc, rows, hidden):
     with cuda.rows_mode(L.ROWS_EXACT):
         rs = cuda.chain_fwd(t(x), t(g), t(b), float(eps), key, float(rate), 0).cpu().numpy()
     assert bits_equal(rs, orc.chain_fwd(x, g, b, eps, key, rate, 0))
+
+
+def test_mlp_step_graph_replays_read_current_inputs(cuda, orc):
+    """A repeated chelis_cuda_mlp_step call (same buffers and stream) runs as
+    a captured CUDA graph from the second call on; every call, the direct
+    first one, the capturing second one and the replays, must see the
+    inputs as they are at that call and stay bit-identical to the oracle."""
+    import torch
+    from chelis_b200 import lib as L
+    x, labels, w1, b1, w2, b2 = W.mlp_inputs()
+    batch, din = x.shape
+    dh, dout = w1.shape[1], w2.shape[1]
+    dev = [t(v) for v in (x, labels, w1, b1, w2, b2)]
+    outs = [torch.empty(1, dtype=torch.float32, device="cuda"),
+            torch.empty_like(dev[2]), torch.empty_like(dev[3]),
+            torch.empty_like(dev[4]), torch.empty_like(dev[5])]
+    rng = np.random.default_rng(11)
+    launches = []
+    for step in range(4):
+        x_now = (x + np.float32(0.01 * step) * rng.standard_normal(x.shape).astype(np.float32))
+        b1_now = (rng.standard_normal(b1.shape) * 0.05).astype(np.float32)
+        dev[0].copy_(torch.from_numpy(x_now))
+        dev[3].copy_(torch.from_numpy(b1_now))
+        before = L.load().chelis_cuda_launch_count()
+        L.call("chelis_cuda_mlp_step", *(v.data_ptr() for v in dev), batch, din, dh, dout,
+               *(o.data_ptr() for o in outs))
+        torch.cuda.synchronize()
+        launches.append(L.load().chelis_cuda_launch_count() - before)
+        cuda.device_status()
+        ref = orc.mlp_step(x_now, labels, w1, b1_now, w2, b2)
+        got = [o.cpu().numpy() for o in outs]
+        assert bits_equal(np.float32(got[0][0]), np.float32(ref[0])), step
+        for g, r in zip(got[1:], ref[1:]):
+            assert bits_equal(g, r), step
+    # the graph runs the same kernels the direct path launches
+    assert len(set(launches)) == 1 and launches[0] >= 10, launches
