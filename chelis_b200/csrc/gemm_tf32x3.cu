@@ -946,16 +946,33 @@ __global__ void __launch_bounds__(THREADS)
     Carry<T> tree;
     uint32_t blocks = 0;
     int col = lane;
-    for (int64_t k0 = 0; k0 < k; k0 += TK) {
-        for (int i = threadIdx.x; i < TK * TN; i += THREADS) {
+    // block k0's B tile and A leaf are loaded into registers one block ahead,
+    // so their global-memory latency overlaps the previous block's butterfly
+    // (small grids -- a few warps per SM -- are otherwise bound by it)
+    constexpr int PER = TK * TN / THREADS;
+    T bnext[PER], anext;
+    auto fetch = [&](int64_t k0) {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int i = threadIdx.x + j * THREADS;
             const int kk = i / TN, cc = i % TN;
             const int64_t gk = k0 + kk, gc = c0 + cc;
-            bs[kk][cc] = (gc < n && gk < k) ? b[gk * sb_k + gc * sb_c] : T(0);
+            bnext[j] = (gc < n && gk < k) ? b[gk * sb_k + gc * sb_c] : T(0);
         }
+        anext = (row < m && k0 + lane < k) ? a[row * sa_r + (k0 + lane) * sa_k] : T(0);
+    };
+    if (k > 0) fetch(0);
+    for (int64_t k0 = 0; k0 < k; k0 += TK) {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int i = threadIdx.x + j * THREADS;
+            bs[i / TN][i % TN] = bnext[j];
+        }
+        const T av = anext;
         __syncthreads();
+        if (k0 + TK < k) fetch(k0 + TK);
         const int64_t valid = (k - k0) < TK ? (k - k0) : TK;
         const bool lv = lane < valid;
-        const T av = (row < m && lv) ? a[row * sa_r + (k0 + lane) * sa_k] : T(0);
         T v[TN];
 #pragma unroll
         for (int j = 0; j < TN; ++j) v[j] = mul_rn(av, bs[lane][j]);

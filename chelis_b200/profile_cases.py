@@ -12,10 +12,14 @@
     python -m chelis_b200.profile_cases attention16 # the same kernels on 16 heads (one batch item)
     python -m chelis_b200.profile_cases fused       # generic FusedElem groups on 16384 x 4096 f32:
                                                     # x*gamma+beta, then sum of squares per row
+    python -m chelis_b200.profile_cases batched     # config 2b: 256 products of 512^3 f32 in one
+                                                    # batched call (persistent CTA-pair kernel)
+    python -m chelis_b200.profile_cases mlp         # config 1 step, called 4 times: a direct run,
+                                                    # the capture, then two replays of its CUDA graph
 
 Each case builds its inputs on the device, runs the hot path once and
 synchronises; inputs exceed the 126 MB L2 except where the case is smaller
-by construction (MLP-sized work is not profiled this way).
+by construction (the MLP step and the batched 512^3 products).
 """
 from __future__ import annotations
 
@@ -59,6 +63,13 @@ def run(case: str) -> None:
         x, g, be = W.torch_chain_inputs()
         ops.fused_elementwise(F.parse("mul x0 x1; add v0 x2"), [x, g, be])
         ops.fused_reduce(F.parse("mul x0 x0"), [x], axis=1)
+    elif case == "batched":
+        a, b = W.torch_gemm_inputs(512, 512, 512, torch.float32, seed=1, batch=256)
+        ops.matmul(a, b)
+    elif case == "mlp":
+        x, labels, w1, b1, w2, b2 = W.torch_mlp_inputs()
+        for _ in range(4):  # outputs dropped at once: the next call reuses their memory
+            ops.mlp_step(x, labels, w1, b1, w2, b2)
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
