@@ -17,7 +17,9 @@ job.
             126 MB L2, so no flush is needed.
   e2e       the same step from pinned host buffers: this rank's x and dy
             copied to the device, the block step, the all-reduce, and the
-            reduced gradients plus dx copied back, inside every timed step.
+            reduced gradients plus dx copied back, inside every timed step;
+            as in a training loop the next step's upload and the previous
+            step's download run on copy streams while a step computes.
   roofline  the phase group that takes the most time in the step (the
             library's phase timer: CUDA events inside chelis_cuda_block_step),
             its algorithmic FLOPs (useful f32 FLOPs; each runs as 3 tf32 MMA
@@ -390,29 +392,66 @@ def bench_block_headline(args, world, rank, peaks, pipes):
                                "term is 3 tf32 MMA terms)"}
     step_frac = fl["total"] / (ms_step * 1e-3) / 1e12 / f32_peak
 
-    # e2e: pinned host buffers every step
+    # e2e: pinned host buffers every step.  As a training loop feeds the
+    # device: step i+1's x and dy upload on one copy stream and step i's
+    # reduced gradients and dx download on another while step i computes
+    # (two device buffer sets).  Every step's copies are inside the timed
+    # region: the first upload is issued after the start event and the end
+    # waits for the last download.
     hx = x.cpu().pin_memory()
     hdy = dy.cpu().pin_memory()
     hg = torch.empty(grads.flat.numel(), dtype=torch.float32).pin_memory()
     hdx = torch.empty(x.shape, dtype=torch.float32).pin_memory()
-    xd, dyd = torch.empty_like(x), torch.empty_like(dy)
+    xd = [torch.empty_like(x) for _ in range(2)]
+    dyd = [torch.empty_like(dy) for _ in range(2)]
+    gsets = [grads, dp.FlatGrads({"d" + k: tuple(w[k].shape) for k in names}, "cuda")]
+    rsets = []
+    for g in gsets:
+        r = {"y": torch.empty_like(x), "dx": torch.empty_like(x)}
+        r.update({k: g[k] for k in g.views})
+        rsets.append(r)
+    comp = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    fetched = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        xd.copy_(hx, non_blocking=True)
-        dyd.copy_(hdy, non_blocking=True)
-        ops.block_step(xd, w, heads, 1e-5, dyd, workspace=ws, out=res, reduce_grads=True)
-        hg.copy_(grads.flat, non_blocking=True)
-        hdx.copy_(res["dx"], non_blocking=True)
+    def upload(b):
+        with torch.cuda.stream(up):
+            xd[b].copy_(hx, non_blocking=True)
+            dyd[b].copy_(hdy, non_blocking=True)
+            uploaded[b].record(up)
 
-    for _ in range(2):
-        e2e_step()
-    e_steps = max(3, args.steps // 2)
-    ems = time_region(e2e_step, e_steps, world)
+    def e2e_run(n):
+        up.wait_stream(comp)
+        upload(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                up.wait_event(computed[1 - b])  # step i-1 is done with set 1 - b
+                upload(1 - b)
+            comp.wait_event(uploaded[b])
+            comp.wait_event(fetched[b])  # step i-2's results are on the host
+            ops.block_step(xd[b], w, heads, 1e-5, dyd[b], workspace=ws, out=rsets[b],
+                           reduce_grads=True)
+            computed[b].record(comp)
+            down.wait_event(computed[b])
+            with torch.cuda.stream(down):
+                hg.copy_(gsets[b].flat, non_blocking=True)
+                hdx.copy_(rsets[b]["dx"], non_blocking=True)
+                fetched[b].record(down)
+        comp.wait_event(fetched[(n - 1) % 2])
+
+    e2e_run(2)
+    torch.cuda.synchronize()
+    e_steps = max(4, args.steps // 2)
+    ems = time_region(lambda: e2e_run(e_steps), 1, world)
     e2e = {"value": round(GLOBAL_BATCH * e_steps / (ems * 1e-3), 2), "unit": UNIT,
            "h2d_bytes_per_step": 2 * x.numel() * 4,
            "d2h_bytes_per_step": grads.flat.numel() * 4 + x.numel() * 4,
            "what": "per rank: x and dy shard H2D; block step; gradient all-reduce; reduced "
-                   "gradients and dx D2H"}
+                   "gradients and dx D2H; the next step's upload and the previous step's "
+                   "download overlap the step on two copy streams"}
     return dict(value=value, ms_per_step=ms_step, launches=launches, clocks=clk.summary(),
                 roofline=roofline, e2e=e2e,
                 breakdown={"phase_ms": phases, "group_ms": groups,
