@@ -31,10 +31,16 @@
 //                         materialised first)
 //   Pad, Cast, Copy, Realize
 //                         materialising kernels;  Drop: nothing
+//   Compare, Logical, Where
+//                         element-wise kernels over strided operands (the C
+//                         lane's C comparisons, bool logic, stored-bit select)
+//   MinReduce             warp per output, the C lane's in-order selection
+//                         (first NaN, else the first of the smallest values)
 //
 // Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
 // bound in first-Load order and outputs are the Store nodes then the roots
 // (emit.rs:5881-5934).  Outputs come back as new device owners.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -57,8 +63,12 @@ constexpr int kMaxRank = 8;
 enum class Op {
     Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
-    Copy, Drop, Store
+    Copy, Drop, Store, Compare, Logical, Where, MinReduce
 };
+
+// Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
+enum { CMP_CMPLT = 0, CMP_LT, CMP_EQ, CMP_NEQ, CMP_GT, CMP_GTE, CMP_LTE };
+enum { LOG_AND = 0, LOG_OR, LOG_NOT };
 
 struct Node {
     Op op = Op::Drop;
@@ -76,6 +86,7 @@ struct Node {
     std::vector<uint8_t> data;                         // ConstTensor payload
     std::string name;                                  // Load / Store
     int accumulator = -1;                              // Sum / BlasMatmul
+    int kind = 0;                                      // Compare / Logical (CMP_* / LOG_*)
 };
 
 // Static layout of a node's value: elements at root storage + offset +
@@ -426,6 +437,34 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
                 return bad("Sum accumulator");
             n.accumulator = prim_dtype(acc->s);
         }
+    } else if (name == "Compare") {
+        // ComparisonKind (dag.rs:528-536), in declaration order
+        static const char *kinds[] = {"CmpLt", "Lt", "Eq", "Neq", "Gt", "Gte", "Lte"};
+        n.op = Op::Compare;
+        n.kind = -1;
+        if (body && body->kind == json::Value::Str)
+            for (int i = 0; i < 7; ++i)
+                if (body->s == kinds[i]) n.kind = i;
+        if (n.kind < 0) return bad("Compare kind");
+        CHELIS_TRY(need_inputs(2));
+    } else if (name == "Logical") {
+        // LogicalKind (dag.rs:555-559)
+        static const char *kinds[] = {"And", "Or", "Not"};
+        n.op = Op::Logical;
+        n.kind = -1;
+        if (body && body->kind == json::Value::Str)
+            for (int i = 0; i < 3; ++i)
+                if (body->s == kinds[i]) n.kind = i;
+        if (n.kind < 0) return bad("Logical kind");
+        CHELIS_TRY(need_inputs(n.kind == LOG_NOT ? 1 : 2));
+    } else if (name == "Where") {
+        n.op = Op::Where;
+        CHELIS_TRY(need_inputs(3));
+    } else if (name == "MinReduce") {
+        n.op = Op::MinReduce;
+        CHELIS_TRY(need_inputs(1));
+        if (!as_index(field("axis"), &v)) return bad("reduction axis");
+        n.axis = static_cast<int>(v);
     } else if (name == "Count") {
         n.op = Op::Count;
         CHELIS_TRY(need_inputs(1));
@@ -560,6 +599,52 @@ int check_and_layout(Program &P) {
                 if (!floating || src(0).dtype != n.dtype) return unsupported(n.opname + " precision");
                 if (n.op == Op::Sum && n.accumulator != n.dtype)
                     return unsupported("Sum with a wider accumulator");
+                if (n.axis >= static_cast<int>(xs.size())) return bad("reduction axis out of range");
+                std::vector<int64_t> want = xs;
+                want.erase(want.begin() + n.axis);
+                if (want != n.shape) return bad("reduction result shape");
+                own();
+                break;
+            }
+            case Op::Compare: {
+                // [05-OP-36]: two operands of one dtype and shape, a bool result;
+                // bool admits only eq / neq
+                const int dt = src(0).dtype;
+                if (src(1).dtype != dt) return bad("Compare operand dtypes differ");
+                if (n.dtype != CHELIS_DTYPE_BOOL) return bad("Compare result must be bool");
+                if (dt == CHELIS_DTYPE_BOOL && n.kind != CMP_EQ && n.kind != CMP_NEQ)
+                    return bad("ordered comparison of bool");
+                if (dt == CHELIS_DTYPE_KEY) return unsupported("Compare of keys");
+                CHELIS_TRY(check_same_shape(n, src(0), "Compare"));
+                CHELIS_TRY(check_same_shape(n, src(1), "Compare"));
+                own();
+                break;
+            }
+            case Op::Logical:
+                // [05-OP-26..28]: bool operands only
+                for (size_t k = 0; k < n.in.size(); ++k) {
+                    if (src(static_cast<int>(k)).dtype != CHELIS_DTYPE_BOOL)
+                        return bad("Logical operand must be bool");
+                    CHELIS_TRY(check_same_shape(n, src(static_cast<int>(k)), "Logical"));
+                }
+                if (n.dtype != CHELIS_DTYPE_BOOL) return bad("Logical result must be bool");
+                own();
+                break;
+            case Op::Where:
+                // a bool condition selecting between two values of the result's dtype
+                if (src(0).dtype != CHELIS_DTYPE_BOOL) return bad("Where condition must be bool");
+                if (src(1).dtype != n.dtype || src(2).dtype != n.dtype) return bad("Where value dtype");
+                if (n.dtype == CHELIS_DTYPE_KEY) return unsupported("Where of keys");
+                for (int k = 0; k < 3; ++k) CHELIS_TRY(check_same_shape(n, src(k), "Where"));
+                own();
+                break;
+            case Op::MinReduce: {
+                const auto &xs = src(0).shape;
+                const int dt = src(0).dtype;
+                if (dt != n.dtype) return bad("MinReduce dtype");
+                if (dt != CHELIS_DTYPE_F32 && dt != CHELIS_DTYPE_F64 && dt != CHELIS_DTYPE_I32 &&
+                    dt != CHELIS_DTYPE_I64)
+                    return unsupported("MinReduce precision");
                 if (n.axis >= static_cast<int>(xs.size())) return bad("reduction axis out of range");
                 std::vector<int64_t> want = xs;
                 want.erase(want.begin() + n.axis);
@@ -1026,6 +1111,113 @@ __global__ void scatter_add_kernel(const T *__restrict__ upd, Strided u, const v
     }
 }
 
+// A stored element as the value it compares by: 16-bit floats widen to f32
+// (the C lane's comparison converts bf16 / f16 to f32 first).
+template <typename T> struct CmpVal { using V = T; __device__ static V get(T x) { return x; } };
+struct Bf16Bits { uint16_t b; };
+struct F16Bits { uint16_t b; };
+template <> struct CmpVal<Bf16Bits> {
+    using V = float;
+    __device__ static float get(Bf16Bits x) { return __uint_as_float(static_cast<uint32_t>(x.b) << 16); }
+};
+template <> struct CmpVal<F16Bits> {
+    using V = float;
+    __device__ static float get(F16Bits x) { return __half2float(__ushort_as_half(x.b)); }
+};
+
+// [05-OP-36] element-wise comparison into bool bytes: C's <, ==, !=, >, >=,
+// <= on the operands' values (a NaN makes every ordered comparison and ==
+// false and != true; signed zeros are equal; integers compare exactly).
+template <typename T>
+__global__ void compare_kernel(const T *__restrict__ a, Strided sa, const T *__restrict__ b, Strided sb,
+                               int kind, uint8_t *__restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const auto x = CmpVal<T>::get(a[offset_of(sa, i)]);
+        const auto y = CmpVal<T>::get(b[offset_of(sb, i)]);
+        bool r;
+        switch (kind) {
+            case CMP_EQ: r = x == y; break;
+            case CMP_NEQ: r = x != y; break;
+            case CMP_GT: r = x > y; break;
+            case CMP_GTE: r = x >= y; break;
+            case CMP_LTE: r = x <= y; break;
+            default: r = x < y; break;  // cmplt, lt
+        }
+        out[i] = r ? 1 : 0;
+    }
+}
+
+// [05-OP-26..28] and / or / not on bool bytes (a stored bool is 0 or 1)
+__global__ void logical_kernel(const uint8_t *__restrict__ a, Strided sa, const uint8_t *__restrict__ b,
+                               Strided sb, int kind, uint8_t *__restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const bool x = a[offset_of(sa, i)] != 0;
+        bool r;
+        if (kind == LOG_NOT) r = !x;
+        else {
+            const bool y = b[offset_of(sb, i)] != 0;
+            r = kind == LOG_AND ? (x && y) : (x || y);
+        }
+        out[i] = r ? 1 : 0;
+    }
+}
+
+// where(c, a, b): the stored bits of a where c is true, of b elsewhere
+template <typename T>
+__global__ void where_kernel(const uint8_t *__restrict__ c, Strided sc, const T *__restrict__ a, Strided sa,
+                             const T *__restrict__ b, Strided sb, T *__restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = c[offset_of(sc, i)] ? a[offset_of(sa, i)] : b[offset_of(sb, i)];
+}
+
+// MinReduce along one axis, as the C lane's in-order scan selects: the
+// first NaN if any, else the first of the smallest values (signed zeros
+// compare equal, so the earlier one is kept); the result is that element's
+// stored bits.  One warp per output: each lane scans a strided subset and the
+// lanes combine (value, position) pairs, which gives the scan's choice in
+// any grouping.  `o` maps an output index to the offset of its first
+// element; `len` / `step` walk the reduced axis.
+template <typename T>
+__device__ __forceinline__ bool min_better(T v, int64_t p, T bv, int64_t bp) {
+    // does (v, p) win over the current best (bv, bp)?  bp < 0: no best yet
+    if (bp < 0) return true;
+    const bool vn = v != v, bn = bv != bv;  // NaN tests (false for integers)
+    if (bn || vn) return vn && (!bn || p < bp);
+    return v < bv || (!(bv < v) && p < bp);
+}
+template <typename T>
+__global__ void min_reduce_kernel(const T *__restrict__ x, Strided o, int64_t len, int64_t step,
+                                  T *__restrict__ out, int64_t nout) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < nout;
+         w += warps) {
+        const T *base = x + offset_of(o, w);
+        T best = T(0);
+        int64_t bp = -1;
+        for (int64_t k = lane; k < len; k += 32) {
+            const T v = base[k * step];
+            if (min_better(v, k, best, bp)) {
+                best = v;
+                bp = k;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const T ov = __shfl_xor_sync(0xffffffffu, best, off);
+            const int64_t op = __shfl_xor_sync(0xffffffffu, bp, off);
+            if (op >= 0 && min_better(ov, op, best, bp)) {
+                best = ov;
+                bp = op;
+            }
+        }
+        if (lane == 0) out[w] = best;
+    }
+}
+
 unsigned grid_for(int64_t n) {
     int64_t b = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -1424,6 +1616,97 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
 #undef CHELIS_DAG_CAST
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::cast_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Compare: {
+            const Value &a = in(0), &b = in(1);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Strided sa = strided(a), sb = strided(b);
+            uint8_t *o = reinterpret_cast<uint8_t *>(out);
+#define CHELIS_DAG_CMP(T)                                                                                \
+    compare_kernel<T><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const T *>(a.ptr), sa,             \
+                                                    reinterpret_cast<const T *>(b.ptr), sb, n.kind, o, cnt)
+            switch (a.dtype) {
+                case CHELIS_DTYPE_F32: CHELIS_DAG_CMP(float); break;
+                case CHELIS_DTYPE_F64: CHELIS_DAG_CMP(double); break;
+                case CHELIS_DTYPE_I32: CHELIS_DAG_CMP(int32_t); break;
+                case CHELIS_DTYPE_I64: CHELIS_DAG_CMP(int64_t); break;
+                case CHELIS_DTYPE_I16: CHELIS_DAG_CMP(int16_t); break;
+                case CHELIS_DTYPE_I8: CHELIS_DAG_CMP(int8_t); break;
+                case CHELIS_DTYPE_BF16: CHELIS_DAG_CMP(Bf16Bits); break;
+                case CHELIS_DTYPE_F16: CHELIS_DAG_CMP(F16Bits); break;
+                default: CHELIS_DAG_CMP(uint8_t); break;  // bool: eq / neq of the stored 0 / 1
+            }
+#undef CHELIS_DAG_CMP
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::compare_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Logical: {
+            const Value &a = in(0);
+            const Value &b = n.kind == LOG_NOT ? in(0) : in(1);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            logical_kernel<<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint8_t *>(a.ptr), strided(a),
+                                                         reinterpret_cast<const uint8_t *>(b.ptr), strided(b),
+                                                         n.kind, reinterpret_cast<uint8_t *>(out), cnt);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::logical_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Where: {
+            const Value &c = in(0), &a = in(1), &b = in(2);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Strided sc = strided(c), sa = strided(a), sb = strided(b);
+            const uint8_t *cp = reinterpret_cast<const uint8_t *>(c.ptr);
+#define CHELIS_DAG_WHERE(T)                                                                               \
+    where_kernel<T><<<grid_for(cnt), 256, 0, s>>>(cp, sc, reinterpret_cast<const T *>(a.ptr), sa,          \
+                                                  reinterpret_cast<const T *>(b.ptr), sb,                \
+                                                  reinterpret_cast<T *>(out), cnt)
+            switch (dtype_width(n.dtype)) {
+                case 8: CHELIS_DAG_WHERE(uint64_t); break;
+                case 4: CHELIS_DAG_WHERE(uint32_t); break;
+                case 2: CHELIS_DAG_WHERE(uint16_t); break;
+                default: CHELIS_DAG_WHERE(uint8_t); break;
+            }
+#undef CHELIS_DAG_WHERE
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::where_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::MinReduce: {
+            const Value &x = in(0);
+            const int64_t len = x.shape[n.axis];
+            if (len == 0) {
+                static const char *const names[] = {"f32", "f64", "i32", "bool", "i64"};
+                return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in min_reduce at %s",
+                                 n.dtype <= CHELIS_DTYPE_I64 ? names[n.dtype] : "?");
+            }
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            // outputs walk the input's other axes; the reduced axis is `step` apart
+            Strided o{};
+            o.rank = 0;
+            for (size_t d = 0; d < x.shape.size(); ++d) {
+                if (static_cast<int>(d) == n.axis) continue;
+                o.shape[o.rank] = x.shape[d];
+                o.stride[o.rank] = x.strides[d];
+                ++o.rank;
+            }
+            const int64_t step = x.strides[n.axis];
+            int64_t blocks = (cnt + 7) / 8;
+            const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+            if (blocks > cap) blocks = cap;
+#define CHELIS_DAG_MIN(T)                                                                                 \
+    min_reduce_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, s>>>(reinterpret_cast<const T *>(x.ptr), o, \
+                                                                       len, step, reinterpret_cast<T *>(out), cnt)
+            switch (n.dtype) {
+                case CHELIS_DTYPE_F32: CHELIS_DAG_MIN(float); break;
+                case CHELIS_DTYPE_F64: CHELIS_DAG_MIN(double); break;
+                case CHELIS_DTYPE_I32: CHELIS_DAG_MIN(int32_t); break;
+                default: CHELIS_DAG_MIN(int64_t); break;
+            }
+#undef CHELIS_DAG_MIN
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::min_reduce_kernel");
             return CHELIS_CUDA_OK;
         }
         default: return bad("unexpected node kind", n.opname);

@@ -103,6 +103,22 @@ class Dag:
         del dims[axis]
         return self.add({"MaxReduce": {"axis": axis}}, [x], dims, self.prec(x))
 
+    def min_reduce(self, x, axis):
+        dims = self.dims(x)
+        del dims[axis]
+        return self.add({"MinReduce": {"axis": axis}}, [x], dims, self.prec(x))
+
+    def compare(self, kind, a, b):
+        """Compare(ComparisonKind): kind one of CmpLt, Lt, Eq, Neq, Gt, Gte, Lte."""
+        return self.add({"Compare": kind}, [a, b], self.dims(a), "bool")
+
+    def logical(self, kind, a, b=None):
+        """Logical(LogicalKind): And, Or (two bool operands) or Not (one)."""
+        return self.add({"Logical": kind}, [a] if b is None else [a, b], self.dims(a), "bool")
+
+    def where(self, cond, a, b):
+        return self.add("Where", [cond, a, b], self.dims(a), self.prec(a))
+
     def matmul(self, a, b):
         (m, k), (_, n) = self.dims(a), self.dims(b)
         return self.add({"BlasMatmul": {"batch_dims": [], "m": {"Concrete": m}, "n": {"Concrete": n},

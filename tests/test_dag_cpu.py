@@ -108,3 +108,41 @@ def test_rejections(text, status, needle):
     assert st == status
     assert needle in L.last_error()
     assert not h.value
+
+
+def test_compare_logical_where_min_reduce_plan():
+    """The mask pattern of causal attention parses, checks and plans: Compare,
+    Logical, Where over an expanded scalar, MinReduce."""
+    g = D.Dag()
+    s = g.load("s", [8, 8])
+    r, c = g.load("rows", [8, 8], "i64"), g.load("cols", [8, 8], "i64")
+    keep = g.logical("Or", g.compare("CmpLt", c, r), g.compare("Eq", c, r))
+    ninf = g.expand(g.expand(g.const(float("-inf")), 0, 8), 1, 8)
+    g.roots = [g.min_reduce(g.where(keep, s, ninf), 0), g.logical("Not", keep)]
+    st, h = load(g.json())
+    assert st == 0, L.last_error()
+    lib = L.load()
+    try:
+        assert lib.chelis_dag_input_count(h) == 3
+        assert lib.chelis_dag_output_count(h) == 2
+    finally:
+        lib.chelis_dag_release(h)
+
+
+@pytest.mark.parametrize("build,message", [
+    (lambda g, a, b, t: g.add({"Compare": "Less"}, [a, b], [4], "bool"), "Compare kind"),
+    (lambda g, a, b, t: g.compare("Lt", t, t), "ordered comparison of bool"),
+    (lambda g, a, b, t: g.add({"Compare": "Eq"}, [a, b], [4], "f32"), "Compare result must be bool"),
+    (lambda g, a, b, t: g.logical("And", a, b), "Logical operand must be bool"),
+    (lambda g, a, b, t: g.add({"Logical": "Xor"}, [t, t], [4], "bool"), "Logical kind"),
+    (lambda g, a, b, t: g.where(a, a, b), "Where condition must be bool"),
+    (lambda g, a, b, t: g.min_reduce(t, 0), "MinReduce"),
+])
+def test_compare_logical_where_min_reduce_rejections(build, message):
+    g = D.Dag()
+    a, b = g.load("a", [4]), g.load("b", [4])
+    t = g.load("t", [4], "bool")
+    g.roots = [build(g, a, b, t)]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()

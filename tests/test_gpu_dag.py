@@ -27,7 +27,8 @@ def run(h, tensors):
     owners = []
     for t in tensors:
         t = t.contiguous()
-        dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64, torch.int64: L.DTYPE_I64}[t.dtype]
+        dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64, torch.int64: L.DTYPE_I64,
+              torch.int32: L.DTYPE_I32, torch.bool: L.DTYPE_BOOL}[t.dtype]
         shape = (ctypes.c_int64 * max(t.dim(), 1))(*t.shape)
         o = lib.chelis_device_tensor_borrow_shape(dt, t.dim(), shape, t.data_ptr(),
                                                    t.numel() * t.element_size())
@@ -42,7 +43,8 @@ def run(h, tensors):
     for i in range(n_out):
         v = lib.chelis_device_tensor_view(outs[i]).contents
         shape = [v.shape[d] for d in range(v.rank)]
-        np_dt = {L.DTYPE_F32: np.float32, L.DTYPE_F64: np.float64, L.DTYPE_I64: np.int64}[v.dtype]
+        np_dt = {L.DTYPE_F32: np.float32, L.DTYPE_F64: np.float64, L.DTYPE_I64: np.int64,
+                 L.DTYPE_I32: np.int32, L.DTYPE_BOOL: np.uint8}[v.dtype]
         host = np.empty(shape, dtype=np_dt)
         L.call("chelis_device_tensor_copy_to_host_bytes", host.ctypes.data, host.nbytes, outs[i])
         res.append(host)
@@ -198,3 +200,189 @@ def test_host_array_entry(cuda, orc):
             lib.chelis_tensor_release(t)
     finally:
         lib.chelis_dag_release(h)
+
+
+# ---- Compare / Logical / Where / MinReduce (the C lane's semantics,
+# crates/chelis-backend-c/src/emit.rs comparison_operator, emit_reduce_extreme)
+
+CMP = {"CmpLt": np.less, "Lt": np.less, "Eq": np.equal, "Neq": np.not_equal,
+       "Gt": np.greater, "Gte": np.greater_equal, "Lte": np.less_equal}
+
+
+def _edge_f32(shape, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(shape).astype(np.float32)
+    flat = x.reshape(-1)
+    special = np.array([np.nan, -0.0, 0.0, np.inf, -np.inf, 1.0, 1.0, -2.5], np.float32)
+    flat[:special.size] = special
+    return x
+
+
+@pytest.mark.parametrize("kind", list(CMP))
+def test_compare_f32_ieee(cuda, kind):
+    """NaN makes every ordered comparison and eq false, neq true; -0 == +0."""
+    a = _edge_f32((6, 37), 1)
+    b = _edge_f32((6, 37), 2)
+    b.reshape(-1)[:8] = np.array([np.nan, 0.0, -0.0, np.inf, np.inf, np.nan, 1.0, -2.5], np.float32)
+    g = D.Dag()
+    x, y = g.load("a", [6, 37]), g.load("b", [6, 37])
+    g.roots = [g.compare(kind, x, y)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    with np.errstate(invalid="ignore"):
+        want = CMP[kind](a, b)
+    assert np.array_equal(got, want.astype(np.uint8))
+
+
+@pytest.mark.parametrize("prec,dt", [("i64", np.int64), ("i32", np.int32), ("f64", np.float64)])
+def test_compare_other_precisions(cuda, prec, dt):
+    rng = np.random.default_rng(4)
+    a = rng.integers(-5, 5, (9, 11)).astype(dt)
+    b = rng.integers(-5, 5, (9, 11)).astype(dt)
+    if dt == np.int64:
+        a[0, 0], b[0, 0] = np.iinfo(np.int64).min, np.iinfo(np.int64).max  # exact order at full width
+    for kind in ("Lt", "Eq", "Gte"):
+        g = D.Dag()
+        x, y = g.load("a", [9, 11], prec), g.load("b", [9, 11], prec)
+        g.roots = [g.compare(kind, x, y)]
+        h = program(g)
+        try:
+            (got,) = run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+        finally:
+            L.load().chelis_dag_release(h)
+        assert np.array_equal(got, CMP[kind](a, b).astype(np.uint8)), kind
+
+
+def test_logical_and_bool_equality(cuda):
+    rng = np.random.default_rng(5)
+    a = rng.integers(0, 2, (4, 33)).astype(bool)
+    b = rng.integers(0, 2, (4, 33)).astype(bool)
+    g = D.Dag()
+    x, y = g.load("a", [4, 33], "bool"), g.load("b", [4, 33], "bool")
+    g.roots = [g.logical("And", x, y), g.logical("Or", x, y), g.logical("Not", x),
+               g.compare("Eq", x, y), g.compare("Neq", x, y)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    for r, w in zip(got, (a & b, a | b, ~a, a == b, a != b)):
+        assert np.array_equal(r, w.astype(np.uint8))
+
+
+def test_where_keeps_stored_bits(cuda):
+    """Where selects stored bits: NaN payloads and signed zeros come through."""
+    rng = np.random.default_rng(6)
+    c = rng.integers(0, 2, (5, 40)).astype(bool)
+    a = rng.standard_normal((5, 40)).astype(np.float32)
+    b = rng.standard_normal((5, 40)).astype(np.float32)
+    a.view(np.uint32)[0, :4] = [0x7fc12345, 0xffc00001, 0x80000000, 0x00000001]
+    b.view(np.uint32)[0, :4] = [0x80000000, 0x7f800000, 0x7fa00000, 0x80000001]
+    c[0, :4] = [True, True, False, False]
+    ai = rng.integers(-9, 9, (5, 40)).astype(np.int64)
+    bi = rng.integers(-9, 9, (5, 40)).astype(np.int64)
+    g = D.Dag()
+    cc = g.load("c", [5, 40], "bool")
+    x, y = g.load("a", [5, 40]), g.load("b", [5, 40])
+    xi, yi = g.load("ai", [5, 40], "i64"), g.load("bi", [5, 40], "i64")
+    g.roots = [g.where(cc, x, y), g.where(cc, xi, yi)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(t).cuda() for t in (c, a, b, ai, bi)])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert np.array_equal(got[0].view(np.uint32), np.where(c, a, b).view(np.uint32))
+    assert np.array_equal(got[1], np.where(c, ai, bi))
+
+
+def _min_scan(x, axis):
+    """The C lane's in-order MinReduce: the first NaN, else the first of the
+    smallest values; the selected element's stored bits."""
+    x = np.moveaxis(x, axis, -1)
+    out = np.empty(x.shape[:-1], x.dtype)
+    for idx in np.ndindex(*x.shape[:-1]):
+        row = x[idx]
+        best = None
+        for v in row:
+            if best is None or (not np.isnan(best) and (np.isnan(v) or v < best)):
+                best = v
+        out[idx] = best
+    return out
+
+
+@pytest.mark.parametrize("axis", [0, 1])
+def test_min_reduce_selection_rules(cuda, axis):
+    x = np.random.default_rng(7).standard_normal((70, 45)).astype(np.float32)
+    x.view(np.uint32)[3, 5] = 0x7fc0abcd   # first NaN of its row / column
+    x.view(np.uint32)[3, 9] = 0xffc00002   # a later NaN
+    x.view(np.uint32)[10, 6] = 0xffc00003
+    x.view(np.uint32)[40, 6] = 0x7fc00004  # later NaN in column 6
+    x[12, :] = 5.0
+    x[12, 20], x[12, 30] = -0.0, 0.0       # tie of signed zeros: the first one
+    x[:, 33] = 7.0
+    x[50, 33], x[60, 33] = 0.0, -0.0
+    g = D.Dag()
+    a = g.load("x", [70, 45])
+    g.roots = [g.min_reduce(a, axis)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert np.array_equal(got.view(np.uint32), _min_scan(x, axis).view(np.uint32))
+
+
+def test_min_reduce_i64_and_strided_view(cuda):
+    """MinReduce of a permuted (strided) view and of integers."""
+    x = np.random.default_rng(8).integers(-1000, 1000, (33, 17)).astype(np.int64)
+    g = D.Dag()
+    a = g.load("x", [33, 17], "i64")
+    g.roots = [g.min_reduce(g.permute(a, [1, 0]), 1)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert np.array_equal(got, x.min(axis=0))
+
+
+def test_min_reduce_empty_axis_traps(cuda):
+    g = D.Dag()
+    a = g.load("x", [4, 0])
+    g.roots = [g.min_reduce(a, 1)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: domain in min_reduce at f32"):
+            run(h, [torch.empty((4, 0), device="cuda")])
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+def test_causal_masked_softmax_program(cuda):
+    """where(cmplt(col, row) | eq, s, -inf) then Softmax: the causal-attention
+    mask as the reference writes it (spec/05-risc-primitives.md:5146-5181),
+    against numpy."""
+    n = 64
+    s = np.random.default_rng(9).standard_normal((n, n)).astype(np.float32)
+    rows = np.repeat(np.arange(n, dtype=np.int64)[:, None], n, axis=1)
+    cols = np.repeat(np.arange(n, dtype=np.int64)[None, :], n, axis=0)
+    g = D.Dag()
+    x = g.load("s", [n, n])
+    r, c = g.load("rows", [n, n], "i64"), g.load("cols", [n, n], "i64")
+    keep = g.logical("Or", g.compare("CmpLt", c, r), g.compare("Eq", c, r))
+    ninf = g.expand(g.expand(g.const(float("-inf")), 0, n), 1, n)
+    masked = g.where(keep, x, ninf)
+    g.roots = [g.add({"Softmax": {"axis": 1}}, [masked], [n, n])]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(t).cuda() for t in (s, rows, cols)])
+    finally:
+        L.load().chelis_dag_release(h)
+    m = np.where(cols <= rows, s.astype(np.float64), -np.inf)
+    e = np.exp(m - m.max(axis=1, keepdims=True))
+    want = e / e.sum(axis=1, keepdims=True)
+    assert rel(got, want) <= 1e-6
+    assert np.all(got[np.triu_indices(n, 1)] == 0.0)
