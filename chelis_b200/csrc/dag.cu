@@ -34,8 +34,12 @@
 //   Compare, Logical, Where
 //                         element-wise kernels over strided operands (the C
 //                         lane's C comparisons, bool logic, stored-bit select)
-//   MinReduce             warp per output, the C lane's in-order selection
-//                         (first NaN, else the first of the smallest values)
+//   MinReduce, Argmax, Argmin
+//                         warp per output, the C lane's in-order selection
+//                         (first NaN, else the first extreme value)
+//   ProdReduce            sequential product per output, in axis order
+//   FloatClassify, ExtremaAdjoint
+//                         element-wise kernels
 //
 // Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
 // bound in first-Load order and outputs are the Store nodes then the roots
@@ -63,12 +67,16 @@ constexpr int kMaxRank = 8;
 enum class Op {
     Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
-    Copy, Drop, Store, Compare, Logical, Where, MinReduce
+    Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
+    FloatClassify, ExtremaAdjoint
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
 enum { CMP_CMPLT = 0, CMP_LT, CMP_EQ, CMP_NEQ, CMP_GT, CMP_GTE, CMP_LTE };
 enum { LOG_AND = 0, LOG_OR, LOG_NOT };
+// FloatClassify kinds (dtype_semantics.rs FloatClassify order); ExtremaAdjoint kind
+// (Max = 0, Min = 1) and operand (Left = 0, Right = 1) in Node::kind / Node::axis
+enum { FC_NAN = 0, FC_FINITE, FC_INFINITE };
 
 struct Node {
     Op op = Op::Drop;
@@ -460,11 +468,32 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
     } else if (name == "Where") {
         n.op = Op::Where;
         CHELIS_TRY(need_inputs(3));
-    } else if (name == "MinReduce") {
-        n.op = Op::MinReduce;
+    } else if (name == "MinReduce" || name == "Argmax" || name == "Argmin" || name == "ProdReduce") {
+        n.op = name == "MinReduce" ? Op::MinReduce
+               : name == "Argmax" ? Op::Argmax
+               : name == "Argmin" ? Op::Argmin
+                                  : Op::ProdReduce;
         CHELIS_TRY(need_inputs(1));
         if (!as_index(field("axis"), &v)) return bad("reduction axis");
         n.axis = static_cast<int>(v);
+    } else if (name == "FloatClassify") {
+        static const char *kinds[] = {"Nan", "Finite", "Infinite"};
+        n.op = Op::FloatClassify;
+        n.kind = -1;
+        if (body && body->kind == json::Value::Str)
+            for (int i = 0; i < 3; ++i)
+                if (body->s == kinds[i]) n.kind = i;
+        if (n.kind < 0) return bad("FloatClassify kind");
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "ExtremaAdjoint") {
+        n.op = Op::ExtremaAdjoint;
+        const json::Value *k = field("kind"), *o = field("operand");
+        if (!k || k->kind != json::Value::Str || (k->s != "Max" && k->s != "Min") || !o ||
+            o->kind != json::Value::Str || (o->s != "Left" && o->s != "Right"))
+            return bad("ExtremaAdjoint kind / operand");
+        n.kind = k->s == "Max" ? 0 : 1;
+        n.axis = o->s == "Left" ? 0 : 1;
+        CHELIS_TRY(need_inputs(3));
     } else if (name == "Count") {
         n.op = Op::Count;
         CHELIS_TRY(need_inputs(1));
@@ -542,6 +571,11 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
 }
 
 // ---------------------------------------------------------------- checking
+
+bool floating_dtype(int dt) {
+    return dt == CHELIS_DTYPE_F32 || dt == CHELIS_DTYPE_F64 || dt == CHELIS_DTYPE_BF16 ||
+           dt == CHELIS_DTYPE_F16;
+}
 
 int check_same_shape(const Node &n, const Node &src, const char *what) {
     if (src.shape != n.shape) return bad(what, "operand shape differs from the node's");
@@ -638,13 +672,15 @@ int check_and_layout(Program &P) {
                 for (int k = 0; k < 3; ++k) CHELIS_TRY(check_same_shape(n, src(k), "Where"));
                 own();
                 break;
-            case Op::MinReduce: {
+            case Op::MinReduce: case Op::Argmax: case Op::Argmin: case Op::ProdReduce: {
                 const auto &xs = src(0).shape;
                 const int dt = src(0).dtype;
-                if (dt != n.dtype) return bad("MinReduce dtype");
+                const bool arg = n.op == Op::Argmax || n.op == Op::Argmin;
+                if (arg ? n.dtype != CHELIS_DTYPE_I64 : dt != n.dtype)
+                    return bad("reduction result dtype", n.opname);
                 if (dt != CHELIS_DTYPE_F32 && dt != CHELIS_DTYPE_F64 && dt != CHELIS_DTYPE_I32 &&
                     dt != CHELIS_DTYPE_I64)
-                    return unsupported("MinReduce precision");
+                    return unsupported(n.opname + " precision");
                 if (n.axis >= static_cast<int>(xs.size())) return bad("reduction axis out of range");
                 std::vector<int64_t> want = xs;
                 want.erase(want.begin() + n.axis);
@@ -652,6 +688,20 @@ int check_and_layout(Program &P) {
                 own();
                 break;
             }
+            case Op::FloatClassify:
+                if (!floating_dtype(src(0).dtype)) return bad("FloatClassify operand must be a float");
+                if (n.dtype != CHELIS_DTYPE_BOOL) return bad("FloatClassify result must be bool");
+                CHELIS_TRY(check_same_shape(n, src(0), "FloatClassify"));
+                own();
+                break;
+            case Op::ExtremaAdjoint:
+                if (!floating) return unsupported("ExtremaAdjoint precision");
+                for (int k = 0; k < 3; ++k) {
+                    if (src(k).dtype != n.dtype) return bad("ExtremaAdjoint operand dtype");
+                    CHELIS_TRY(check_same_shape(n, src(k), "ExtremaAdjoint"));
+                }
+                own();
+                break;
             case Op::Count: {
                 if (src(0).dtype != CHELIS_DTYPE_BOOL || n.dtype != CHELIS_DTYPE_I64)
                     return unsupported("Count other than bool -> i64");
@@ -1173,24 +1223,27 @@ __global__ void where_kernel(const uint8_t *__restrict__ c, Strided sc, const T 
         out[i] = c[offset_of(sc, i)] ? a[offset_of(sa, i)] : b[offset_of(sb, i)];
 }
 
-// MinReduce along one axis, as the C lane's in-order scan selects: the
-// first NaN if any, else the first of the smallest values (signed zeros
-// compare equal, so the earlier one is kept); the result is that element's
-// stored bits.  One warp per output: each lane scans a strided subset and the
-// lanes combine (value, position) pairs, which gives the scan's choice in
-// any grouping.  `o` maps an output index to the offset of its first
-// element; `len` / `step` walk the reduced axis.
-template <typename T>
-__device__ __forceinline__ bool min_better(T v, int64_t p, T bv, int64_t bp) {
-    // does (v, p) win over the current best (bv, bp)?  bp < 0: no best yet
+// MinReduce / MaxReduce-style selection along one axis, as the C lane's
+// in-order scans pick (emit_reduce_extreme, emit_reduce_argcmp): the first
+// NaN if any, else the first of the smallest (MAX: largest) values, signed
+// zeros comparing equal.  The result is the chosen element's stored bits
+// (MinReduce) or its position on the axis (Argmax / Argmin, i64).  One warp
+// per output: each lane scans a strided subset and the lanes combine
+// (value, position) pairs, which gives the scan's choice in any grouping.
+// `o` maps an output index to the offset of its first element; `len` /
+// `step` walk the reduced axis.
+template <bool MAX, typename T>
+__device__ __forceinline__ bool pick_better(T v, int64_t p, T bv, int64_t bp) {
+    // does (v, p) win over the current choice (bv, bp)?  bp < 0: none yet
     if (bp < 0) return true;
     const bool vn = v != v, bn = bv != bv;  // NaN tests (false for integers)
     if (bn || vn) return vn && (!bn || p < bp);
+    if (MAX) return v > bv || (!(bv > v) && p < bp);
     return v < bv || (!(bv < v) && p < bp);
 }
-template <typename T>
-__global__ void min_reduce_kernel(const T *__restrict__ x, Strided o, int64_t len, int64_t step,
-                                  T *__restrict__ out, int64_t nout) {
+template <bool MAX, bool INDEX, typename T, typename O>
+__global__ void extreme_reduce_kernel(const T *__restrict__ x, Strided o, int64_t len, int64_t step,
+                                      O *__restrict__ out, int64_t nout) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < nout;
@@ -1200,7 +1253,7 @@ __global__ void min_reduce_kernel(const T *__restrict__ x, Strided o, int64_t le
         int64_t bp = -1;
         for (int64_t k = lane; k < len; k += 32) {
             const T v = base[k * step];
-            if (min_better(v, k, best, bp)) {
+            if (pick_better<MAX>(v, k, best, bp)) {
                 best = v;
                 bp = k;
             }
@@ -1209,12 +1262,78 @@ __global__ void min_reduce_kernel(const T *__restrict__ x, Strided o, int64_t le
         for (int off = 16; off > 0; off >>= 1) {
             const T ov = __shfl_xor_sync(0xffffffffu, best, off);
             const int64_t op = __shfl_xor_sync(0xffffffffu, bp, off);
-            if (op >= 0 && min_better(ov, op, best, bp)) {
+            if (op >= 0 && pick_better<MAX>(ov, op, best, bp)) {
                 best = ov;
                 bp = op;
             }
         }
-        if (lane == 0) out[w] = best;
+        if (lane == 0) {
+            if constexpr (INDEX) out[w] = static_cast<O>(bp);
+            else out[w] = best;
+        }
+    }
+}
+
+// ProdReduce: the product in axis order from 1 (the C lane's `acc *= x`
+// loop), one thread per output
+template <typename T>
+__global__ void prod_reduce_kernel(const T *__restrict__ x, Strided o, int64_t len, int64_t step,
+                                   T *__restrict__ out, int64_t nout) {
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; w < nout;
+         w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const T *base = x + offset_of(o, w);
+        T acc = T(1);
+        for (int64_t k = 0; k < len; ++k) acc = acc * base[k * step];
+        out[w] = acc;
+    }
+}
+template <>
+__global__ void prod_reduce_kernel<float>(const float *__restrict__ x, Strided o, int64_t len, int64_t step,
+                                          float *__restrict__ out, int64_t nout) {
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; w < nout;
+         w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float *base = x + offset_of(o, w);
+        float acc = 1.0f;
+        for (int64_t k = 0; k < len; ++k) acc = __fmul_rn(acc, base[k * step]);
+        out[w] = acc;
+    }
+}
+template <>
+__global__ void prod_reduce_kernel<double>(const double *__restrict__ x, Strided o, int64_t len, int64_t step,
+                                           double *__restrict__ out, int64_t nout) {
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; w < nout;
+         w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const double *base = x + offset_of(o, w);
+        double acc = 1.0;
+        for (int64_t k = 0; k < len; ++k) acc = __dmul_rn(acc, base[k * step]);
+        out[w] = acc;
+    }
+}
+
+// FloatClassify ([05-OP-20..22]): is_nan / is_finite / is_infinite into bool bytes
+template <typename T>
+__global__ void classify_kernel(const T *__restrict__ x, Strided sx, int kind, uint8_t *__restrict__ out,
+                                int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const auto v = CmpVal<T>::get(x[offset_of(sx, i)]);
+        const bool r = kind == FC_NAN ? isnan(v) : kind == FC_FINITE ? isfinite(v) : isinf(v);
+        out[i] = r ? 1 : 0;
+    }
+}
+
+// ExtremaAdjoint ([05-OP-40]): the cotangent where `operand` was the
+// selected side of max_elem / min_elem (left wins when it is NaN, or when
+// right is not NaN and left >= right for max, <= for min), +0 elsewhere
+template <typename T>
+__global__ void extrema_adjoint_kernel(const T *__restrict__ a, Strided sa, const T *__restrict__ b, Strided sb,
+                                       const T *__restrict__ g, Strided sg, int is_min, int right,
+                                       T *__restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const T av = a[offset_of(sa, i)], bv = b[offset_of(sb, i)];
+        const bool left = isnan(av) || (!isnan(bv) && (is_min ? av <= bv : av >= bv));
+        out[i] = (right ? !left : left) ? g[offset_of(sg, i)] : T(0);
     }
 }
 
@@ -1673,13 +1792,16 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
             CHELIS_LAUNCH_CHECK("dag::where_kernel");
             return CHELIS_CUDA_OK;
         }
-        case Op::MinReduce: {
+        case Op::MinReduce: case Op::Argmax: case Op::Argmin: case Op::ProdReduce: {
             const Value &x = in(0);
             const int64_t len = x.shape[n.axis];
-            if (len == 0) {
+            if (len == 0 && n.op != Op::ProdReduce) {
                 static const char *const names[] = {"f32", "f64", "i32", "bool", "i64"};
-                return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in min_reduce at %s",
-                                 n.dtype <= CHELIS_DTYPE_I64 ? names[n.dtype] : "?");
+                const char *what = n.op == Op::MinReduce ? "min_reduce"
+                                   : n.op == Op::Argmax  ? "argmax_reduce"
+                                                         : "argmin_reduce";
+                return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in %s at %s", what,
+                                 n.op == Op::MinReduce ? names[n.dtype] : "i64");
             }
             if (cnt == 0) return CHELIS_CUDA_OK;
             // outputs walk the input's other axes; the reduced axis is `step` apart
@@ -1695,18 +1817,61 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
             int64_t blocks = (cnt + 7) / 8;
             const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
             if (blocks > cap) blocks = cap;
-#define CHELIS_DAG_MIN(T)                                                                                 \
-    min_reduce_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, s>>>(reinterpret_cast<const T *>(x.ptr), o, \
-                                                                       len, step, reinterpret_cast<T *>(out), cnt)
-            switch (n.dtype) {
-                case CHELIS_DTYPE_F32: CHELIS_DAG_MIN(float); break;
-                case CHELIS_DTYPE_F64: CHELIS_DAG_MIN(double); break;
-                case CHELIS_DTYPE_I32: CHELIS_DAG_MIN(int32_t); break;
-                default: CHELIS_DAG_MIN(int64_t); break;
+            const unsigned gb = static_cast<unsigned>(blocks);
+            int64_t *idx = reinterpret_cast<int64_t *>(out);
+#define CHELIS_DAG_EXTREME(T)                                                                              \
+    do {                                                                                                   \
+        const T *xp = reinterpret_cast<const T *>(x.ptr);                                                  \
+        if (n.op == Op::MinReduce)                                                                         \
+            extreme_reduce_kernel<false, false, T, T><<<gb, 256, 0, s>>>(xp, o, len, step, reinterpret_cast<T *>(out), cnt); \
+        else if (n.op == Op::Argmax)                                                                       \
+            extreme_reduce_kernel<true, true, T, int64_t><<<gb, 256, 0, s>>>(xp, o, len, step, idx, cnt);  \
+        else if (n.op == Op::Argmin)                                                                       \
+            extreme_reduce_kernel<false, true, T, int64_t><<<gb, 256, 0, s>>>(xp, o, len, step, idx, cnt); \
+        else                                                                                               \
+            prod_reduce_kernel<T><<<grid_for(cnt), 256, 0, s>>>(xp, o, len, step, reinterpret_cast<T *>(out), cnt); \
+    } while (0)
+            switch (x.dtype) {
+                case CHELIS_DTYPE_F32: CHELIS_DAG_EXTREME(float); break;
+                case CHELIS_DTYPE_F64: CHELIS_DAG_EXTREME(double); break;
+                case CHELIS_DTYPE_I32: CHELIS_DAG_EXTREME(int32_t); break;
+                default: CHELIS_DAG_EXTREME(int64_t); break;
             }
-#undef CHELIS_DAG_MIN
+#undef CHELIS_DAG_EXTREME
             g_launches++;
-            CHELIS_LAUNCH_CHECK("dag::min_reduce_kernel");
+            CHELIS_LAUNCH_CHECK("dag::extreme_reduce_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::FloatClassify: {
+            const Value &x = in(0);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Strided sx = strided(x);
+            uint8_t *o = reinterpret_cast<uint8_t *>(out);
+            switch (x.dtype) {
+                case CHELIS_DTYPE_F32: classify_kernel<float><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const float *>(x.ptr), sx, n.kind, o, cnt); break;
+                case CHELIS_DTYPE_F64: classify_kernel<double><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const double *>(x.ptr), sx, n.kind, o, cnt); break;
+                case CHELIS_DTYPE_BF16: classify_kernel<Bf16Bits><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const Bf16Bits *>(x.ptr), sx, n.kind, o, cnt); break;
+                default: classify_kernel<F16Bits><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const F16Bits *>(x.ptr), sx, n.kind, o, cnt); break;
+            }
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::classify_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::ExtremaAdjoint: {
+            const Value &a = in(0), &b = in(1), &g = in(2);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            if (n.dtype == CHELIS_DTYPE_F64)
+                extrema_adjoint_kernel<double><<<grid_for(cnt), 256, 0, s>>>(
+                    reinterpret_cast<const double *>(a.ptr), strided(a), reinterpret_cast<const double *>(b.ptr),
+                    strided(b), reinterpret_cast<const double *>(g.ptr), strided(g), n.kind, n.axis,
+                    reinterpret_cast<double *>(out), cnt);
+            else
+                extrema_adjoint_kernel<float><<<grid_for(cnt), 256, 0, s>>>(
+                    reinterpret_cast<const float *>(a.ptr), strided(a), reinterpret_cast<const float *>(b.ptr),
+                    strided(b), reinterpret_cast<const float *>(g.ptr), strided(g), n.kind, n.axis,
+                    reinterpret_cast<float *>(out), cnt);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::extrema_adjoint_kernel");
             return CHELIS_CUDA_OK;
         }
         default: return bad("unexpected node kind", n.opname);

@@ -108,6 +108,25 @@ class Dag:
         del dims[axis]
         return self.add({"MinReduce": {"axis": axis}}, [x], dims, self.prec(x))
 
+    def arg_reduce(self, op, x, axis):
+        """Argmax / Argmin: i64 positions along axis."""
+        dims = self.dims(x)
+        del dims[axis]
+        return self.add({op: {"axis": axis}}, [x], dims, "i64")
+
+    def prod_reduce(self, x, axis):
+        dims = self.dims(x)
+        del dims[axis]
+        return self.add({"ProdReduce": {"axis": axis}}, [x], dims, self.prec(x))
+
+    def classify(self, kind, x):
+        """FloatClassify: Nan, Finite or Infinite."""
+        return self.add({"FloatClassify": kind}, [x], self.dims(x), "bool")
+
+    def extrema_adjoint(self, kind, operand, a, b, g):
+        return self.add({"ExtremaAdjoint": {"kind": kind, "operand": operand}}, [a, b, g],
+                        self.dims(a), self.prec(a))
+
     def compare(self, kind, a, b):
         """Compare(ComparisonKind): kind one of CmpLt, Lt, Eq, Neq, Gt, Gte, Lte."""
         return self.add({"Compare": kind}, [a, b], self.dims(a), "bool")

@@ -146,3 +146,18 @@ def test_compare_logical_where_min_reduce_rejections(build, message):
     st, h = load(g.json())
     assert st != 0
     assert message in L.last_error()
+
+
+@pytest.mark.parametrize("build,message", [
+    (lambda g, a: g.add({"Argmax": {"axis": 0}}, [a], [], "f32"), "reduction result dtype"),
+    (lambda g, a: g.add({"FloatClassify": "Odd"}, [a], [4], "bool"), "FloatClassify kind"),
+    (lambda g, a: g.add({"ExtremaAdjoint": {"kind": "Mid", "operand": "Left"}}, [a, a, a], [4], "f32"),
+     "ExtremaAdjoint kind"),
+])
+def test_arg_classify_extrema_rejections(build, message):
+    g = D.Dag()
+    a = g.load("a", [4])
+    g.roots = [build(g, a)]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()

@@ -386,3 +386,89 @@ def test_causal_masked_softmax_program(cuda):
     want = e / e.sum(axis=1, keepdims=True)
     assert rel(got, want) <= 1e-6
     assert np.all(got[np.triu_indices(n, 1)] == 0.0)
+
+
+def _arg_scan(x, axis, take_max):
+    """emit_reduce_argcmp's in-order choice: first NaN, else the first extreme."""
+    x = np.moveaxis(x, axis, -1)
+    out = np.empty(x.shape[:-1], np.int64)
+    for idx in np.ndindex(*x.shape[:-1]):
+        best, bi = None, -1
+        for i, v in enumerate(x[idx]):
+            if bi < 0:
+                best, bi = v, i
+                continue
+            better = (v > best) if take_max else (v < best)
+            if not np.isnan(best) and (np.isnan(v) or better):
+                best, bi = v, i
+        out[idx] = bi
+    return out
+
+
+@pytest.mark.parametrize("op,axis", [("Argmax", 1), ("Argmin", 1), ("Argmax", 0), ("Argmin", 0)])
+def test_argmax_argmin_selection_rules(cuda, op, axis):
+    x = np.random.default_rng(10).standard_normal((50, 41)).astype(np.float32)
+    x[4, :] = 2.0                       # ties: the first position
+    x[7, 3], x[7, 30] = np.nan, np.nan  # the first NaN wins
+    x[9, :] = 0.0
+    x[9, 5] = -0.0                      # signed zeros tie
+    x[:, 12] = 1.0
+    x[20, 12] = np.nan
+    g = D.Dag()
+    a = g.load("x", [50, 41])
+    g.roots = [g.arg_reduce(op, a, axis)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    with np.errstate(invalid="ignore"):
+        assert np.array_equal(got, _arg_scan(x, axis, op == "Argmax"))
+
+
+def test_prod_reduce_in_axis_order(cuda):
+    """ProdReduce multiplies from 1 in axis order, each product rounded to f32."""
+    x = (1.0 + 0.3 * np.random.default_rng(11).standard_normal((13, 60))).astype(np.float32)
+    g = D.Dag()
+    a = g.load("x", [13, 60])
+    g.roots = [g.prod_reduce(a, 1), g.prod_reduce(a, 0)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    for r, ax in zip(got, (1, 0)):
+        xm = np.moveaxis(x, ax, -1)
+        want = np.empty(xm.shape[:-1], np.float32)
+        for idx in np.ndindex(*xm.shape[:-1]):
+            acc = np.float32(1.0)
+            for v in xm[idx]:
+                acc = np.float32(acc * v)
+            want[idx] = acc
+        assert np.array_equal(r.view(np.uint32), want.view(np.uint32))
+
+
+def test_float_classify_and_extrema_adjoint(cuda):
+    a = _edge_f32((3, 50), 12)
+    b = _edge_f32((3, 50), 13)
+    b.reshape(-1)[:8] = np.array([1.0, np.nan, -0.0, np.inf, 3.0, np.nan, 1.0, -9.0], np.float32)
+    gr = np.random.default_rng(14).standard_normal((3, 50)).astype(np.float32)
+    g = D.Dag()
+    x, y, c = g.load("a", [3, 50]), g.load("b", [3, 50]), g.load("g", [3, 50])
+    g.roots = [g.classify("Nan", x), g.classify("Finite", x), g.classify("Infinite", x),
+               g.extrema_adjoint("Max", "Left", x, y, c), g.extrema_adjoint("Max", "Right", x, y, c),
+               g.extrema_adjoint("Min", "Left", x, y, c), g.extrema_adjoint("Min", "Right", x, y, c)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(t).cuda() for t in (a, b, gr)])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert np.array_equal(got[0], np.isnan(a).astype(np.uint8))
+    assert np.array_equal(got[1], np.isfinite(a).astype(np.uint8))
+    assert np.array_equal(got[2], np.isinf(a).astype(np.uint8))
+    with np.errstate(invalid="ignore"):
+        left_max = np.isnan(a) | (~np.isnan(b) & (a >= b))
+        left_min = np.isnan(a) | (~np.isnan(b) & (a <= b))
+    zero = np.zeros_like(gr)
+    for r, sel in zip(got[3:], (left_max, ~left_max, left_min, ~left_min)):
+        assert np.array_equal(r.view(np.uint32), np.where(sel, gr, zero).view(np.uint32))
