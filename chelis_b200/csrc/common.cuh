@@ -53,6 +53,8 @@ enum : unsigned int {
     DEVERR_TIMEOUT_EPILOGUE = 4u,
     DEVERR_TIMEOUTS = 7u,
     DEVERR_BAD_INDEX = 8u,  // an index operand outside its axis ([05-OP-52])
+    DEVERR_DROPOUT_F32 = 16u,  // a dropout rate outside [0, 1) ([05-OP-37]), f32 draw
+    DEVERR_DROPOUT_F64 = 32u,  // the same, f64 draw
 };
 
 __device__ __forceinline__ void report_device_error(unsigned int code) {

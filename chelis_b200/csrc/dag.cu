@@ -40,6 +40,11 @@
 //   ProdReduce            sequential product per output, in axis order
 //   FloatClassify, ExtremaAdjoint
 //                         element-wise kernels
+//   KeyFromSeed, Split, FoldIn, SplitN (static count)
+//                         u64 keys derived element-wise ([05-RNG-2] derive)
+//   Dropout, DropoutReplay
+//                         keyed draw per key row ([05-OP-37]), the C lane's
+//                         word / unit and rate rule
 //
 // Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
 // bound in first-Load order and outputs are the Store nodes then the roots
@@ -68,7 +73,7 @@ enum class Op {
     Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
-    FloatClassify, ExtremaAdjoint
+    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -95,6 +100,7 @@ struct Node {
     std::string name;                                  // Load / Store
     int accumulator = -1;                              // Sum / BlasMatmul
     int kind = 0;                                      // Compare / Logical (CMP_* / LOG_*)
+    int activation = -1;                               // owner.activation node, if any
 };
 
 // Static layout of a node's value: elements at root storage + offset +
@@ -348,7 +354,15 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
     if (!dims || dims->kind != json::Value::Arr || !prec || prec->kind != json::Value::Str)
         return bad("output_type");
     const int dt = prim_dtype(prec->s);
-    if (dt < 0 || dt == CHELIS_DTYPE_KEY) return unsupported("precision " + prec->s);
+    if (dt < 0) return unsupported("precision " + prec->s);
+    if (const json::Value *own = jn.get("owner")) {
+        const json::Value *act = own->get("activation");
+        int64_t a = 0;
+        if (act && act->kind != json::Value::Null) {
+            if (!as_index(act, &a) || a >= id) return bad("owner activation");
+            n.activation = static_cast<int>(a);
+        }
+    }
     n.dtype = static_cast<chelis_dtype>(dt);
     for (const auto &d : dims->a) {
         int64_t e = 0;
@@ -493,6 +507,30 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
             return bad("ExtremaAdjoint kind / operand");
         n.kind = k->s == "Max" ? 0 : 1;
         n.axis = o->s == "Left" ? 0 : 1;
+        CHELIS_TRY(need_inputs(3));
+    } else if (name == "KeyFromSeed" || name == "FoldIn") {
+        // [05-OP-69] key_from_seed, [05-OP-72] fold_in
+        n.op = name == "KeyFromSeed" ? Op::KeyFromSeed : Op::FoldIn;
+        CHELIS_TRY(need_inputs(n.op == Op::KeyFromSeed ? 1 : 2));
+    } else if (name == "Split") {
+        // one half of [05-OP-70] split_key: derive(k, 0) (Left) or derive(k, 1) (Right)
+        n.op = Op::SplitKey;
+        const json::Value *b = field("branch");
+        if (!b || b->kind != json::Value::Str || (b->s != "Left" && b->s != "Right"))
+            return bad("Split branch");
+        n.kind = b->s == "Left" ? 0 : 1;
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "SplitN") {
+        // [05-OP-71] split_keys with a static count: row j = derive(derive(k, 2), j)
+        n.op = Op::SplitN;
+        const json::Value *c = field("count");
+        const json::Value *cc = c ? variant(*c, "Concrete") : nullptr;
+        if (!cc || !as_index(cc, &v)) return unsupported("SplitN with a runtime count");
+        n.axis = static_cast<int>(v);
+        CHELIS_TRY(need_inputs(1));
+    } else if (name == "Dropout" || name == "DropoutReplay") {
+        // [05-OP-37] under an explicit key; the replay applies the same draw to the cotangent
+        n.op = Op::Dropout;
         CHELIS_TRY(need_inputs(3));
     } else if (name == "Count") {
         n.op = Op::Count;
@@ -685,6 +723,43 @@ int check_and_layout(Program &P) {
                 std::vector<int64_t> want = xs;
                 want.erase(want.begin() + n.axis);
                 if (want != n.shape) return bad("reduction result shape");
+                own();
+                break;
+            }
+            case Op::KeyFromSeed: case Op::SplitKey: case Op::FoldIn: case Op::SplitN: {
+                if (n.activation >= 0) return unsupported(n.opname + " under an activation");
+                const bool seed = n.op == Op::KeyFromSeed;
+                if (src(0).dtype != (seed ? CHELIS_DTYPE_I64 : CHELIS_DTYPE_KEY))
+                    return bad(seed ? "KeyFromSeed seed must be i64" : "key operand must be a key");
+                if (n.dtype != CHELIS_DTYPE_KEY) return bad("key operation result must be a key");
+                if (n.op == Op::FoldIn) {
+                    if (src(1).dtype != CHELIS_DTYPE_I64) return bad("FoldIn data must be i64");
+                    CHELIS_TRY(check_same_shape(n, src(1), "FoldIn"));
+                }
+                if (n.op == Op::SplitN) {
+                    std::vector<int64_t> want = src(0).shape;
+                    want.push_back(n.axis);
+                    if (want != n.shape) return bad("SplitN result shape");
+                } else {
+                    CHELIS_TRY(check_same_shape(n, src(0), n.opname.c_str()));
+                }
+                own();
+                break;
+            }
+            case Op::Dropout: {
+                if (n.activation >= 0) return unsupported("Dropout under an activation");
+                if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+                    return unsupported("Dropout precision");
+                if (src(0).dtype != n.dtype || src(1).dtype != n.dtype) return bad("Dropout operand dtype");
+                if (src(2).dtype != CHELIS_DTYPE_KEY) return bad("Dropout key must be a key");
+                CHELIS_TRY(check_same_shape(n, src(0), "Dropout"));
+                // the key is rank 0 or shaped like a leading part of the data;
+                // the rate rank 0 or a leading part of the key's shape
+                const auto &ks = src(2).shape, &rs = src(1).shape;
+                if (ks.size() > n.shape.size() || !std::equal(ks.begin(), ks.end(), n.shape.begin()))
+                    return bad("Dropout key shape");
+                if (rs.size() > ks.size() || !std::equal(rs.begin(), rs.end(), ks.begin()))
+                    return bad("Dropout rate shape");
                 own();
                 break;
             }
@@ -1337,6 +1412,68 @@ __global__ void extrema_adjoint_kernel(const T *__restrict__ a, Strided sa, cons
     }
 }
 
+// [05-RNG-2] derive(k, j) = splitmix64(k XOR rotl64(splitmix64(j), 29))
+__device__ __forceinline__ uint64_t key_derive(uint64_t k, uint64_t j) {
+    const uint64_t m = splitmix64(j);
+    return splitmix64(k ^ ((m << 29) | (m >> 35)));
+}
+
+// Key operations, element-wise over the result: KEY_SEED key = the seed's
+// bits ([05-OP-69]); KEY_SPLIT derive(k, branch) ([05-OP-70]); KEY_FOLD
+// derive(derive(k, 2), n) ([05-OP-72]); KEY_SPLITN row j of `count` new keys
+// derive(derive(k, 2), j) ([05-OP-71], the new axis last).
+enum { KEY_SEED = 0, KEY_SPLIT, KEY_FOLD, KEY_SPLITN };
+__global__ void key_kernel(const uint64_t *__restrict__ k, Strided sk, const int64_t *__restrict__ d,
+                           Strided sd, int mode, int64_t arg, uint64_t *__restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        uint64_t r;
+        switch (mode) {
+            case KEY_SEED: r = static_cast<uint64_t>(d[offset_of(sd, i)]); break;
+            case KEY_SPLIT: r = key_derive(k[offset_of(sk, i)], static_cast<uint64_t>(arg)); break;
+            case KEY_FOLD:
+                r = key_derive(key_derive(k[offset_of(sk, i)], 2), static_cast<uint64_t>(d[offset_of(sd, i)]));
+                break;
+            default: r = key_derive(key_derive(k[offset_of(sk, i / arg)], 2), static_cast<uint64_t>(i % arg)); break;
+        }
+        out[i] = r;
+    }
+}
+
+// [05-OP-37] dropout under an explicit key, as the C lane draws it: the data
+// splits into `rows` rows of `row_len` elements, one per key (a rank-0 key
+// is one row); element e of row b is dropped when the unit value of
+// word(key[b], e) -- the word's high 53 bits over 2^53, rounded to the draw's
+// precision -- is below row b's rate, else it becomes x / (1 - rate) (NaN
+// canonical).  A rate outside [0, 1) sets the device error word (the C
+// lane's "numeric trap: domain in dropout").
+template <typename T>
+__global__ void keyed_dropout_kernel(const T *__restrict__ x, Strided sx, const T *__restrict__ rate,
+                                     Strided sr, int64_t rate_size, const uint64_t *__restrict__ keys,
+                                     Strided sk, int64_t rows, int64_t row_len, T *__restrict__ out,
+                                     int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / row_len, e = i - b * row_len;
+        const T r = rate[offset_of(sr, rate_size <= 1 ? 0 : b / (rows / rate_size))];
+        if (!(r >= T(0) && r < T(1))) {
+            report_device_error(sizeof(T) == 4 ? DEVERR_DROPOUT_F32 : DEVERR_DROPOUT_F64);
+            out[i] = T(0);
+            continue;
+        }
+        const uint64_t w = rng_word(keys[offset_of(sk, b)], static_cast<uint64_t>(e));
+        const double u = static_cast<double>(w >> 11) * 0x1p-53;
+        T y;
+        if constexpr (sizeof(T) == 4) {
+            y = __double2float_rn(u) < r ? 0.0f : canon(__fdiv_rn(x[offset_of(sx, i)], __fsub_rn(1.0f, r)));
+        } else {
+            const double q = __ddiv_rn(x[offset_of(sx, i)], __dsub_rn(1.0, r));
+            y = u < r ? 0.0 : (isnan(q) ? __longlong_as_double(0x7ff8000000000000ll) : q);
+        }
+        out[i] = y;
+    }
+}
+
 unsigned grid_for(int64_t n) {
     int64_t b = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -1872,6 +2009,40 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                     reinterpret_cast<float *>(out), cnt);
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::extrema_adjoint_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::KeyFromSeed: case Op::SplitKey: case Op::FoldIn: case Op::SplitN: {
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Value &a = in(0);
+            const bool seed = n.op == Op::KeyFromSeed;
+            const Value &d = n.op == Op::FoldIn ? in(1) : a;
+            const int mode = seed ? KEY_SEED : n.op == Op::SplitKey ? KEY_SPLIT : n.op == Op::FoldIn ? KEY_FOLD : KEY_SPLITN;
+            const int64_t arg = n.op == Op::SplitKey ? n.kind : n.axis;
+            key_kernel<<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint64_t *>(a.ptr), strided(a),
+                                                     reinterpret_cast<const int64_t *>(d.ptr), strided(d), mode,
+                                                     arg, reinterpret_cast<uint64_t *>(out), cnt);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::key_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Dropout: {
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Value &x = in(0), &r = in(1), &k = in(2);
+            const int64_t rows = count_of(k.shape);
+            const int64_t row_len = rows > 0 ? cnt / rows : 0;
+            const int64_t rsize = count_of(r.shape);
+            if (n.dtype == CHELIS_DTYPE_F64)
+                keyed_dropout_kernel<double><<<grid_for(cnt), 256, 0, s>>>(
+                    reinterpret_cast<const double *>(x.ptr), strided(x), reinterpret_cast<const double *>(r.ptr),
+                    strided(r), rsize, reinterpret_cast<const uint64_t *>(k.ptr), strided(k), rows, row_len,
+                    reinterpret_cast<double *>(out), cnt);
+            else
+                keyed_dropout_kernel<float><<<grid_for(cnt), 256, 0, s>>>(
+                    reinterpret_cast<const float *>(x.ptr), strided(x), reinterpret_cast<const float *>(r.ptr),
+                    strided(r), rsize, reinterpret_cast<const uint64_t *>(k.ptr), strided(k), rows, row_len,
+                    reinterpret_cast<float *>(out), cnt);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::keyed_dropout_kernel");
             return CHELIS_CUDA_OK;
         }
         default: return bad("unexpected node kind", n.opname);

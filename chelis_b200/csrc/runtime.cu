@@ -313,7 +313,10 @@ int chelis_cuda_device_status(void) {
         if (word & DEVERR_TIMEOUTS)
             return set_error(CHELIS_CUDA_ERR_TIMEOUT,
                              "a bounded device wait gave up (error word 0x%x)", word);
-        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in gather at i64");
+        if (word & DEVERR_BAD_INDEX)
+            return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in gather at i64");
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at %s",
+                         (word & DEVERR_DROPOUT_F32) ? "f32" : "f64");
     }
     return CHELIS_CUDA_OK;
 }

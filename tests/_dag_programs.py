@@ -30,7 +30,7 @@ from __future__ import annotations
 import json
 import struct
 
-PRIM = {"f32": "F32", "f64": "F64", "i64": "Int64", "i32": "Int32", "bool": "Bool"}
+PRIM = {"f32": "F32", "f64": "F64", "i64": "Int64", "i32": "Int32", "bool": "Bool", "key": "Key"}
 
 
 def f32_scalar(v: float) -> dict:
@@ -126,6 +126,23 @@ class Dag:
     def extrema_adjoint(self, kind, operand, a, b, g):
         return self.add({"ExtremaAdjoint": {"kind": kind, "operand": operand}}, [a, b, g],
                         self.dims(a), self.prec(a))
+
+    def key_from_seed(self, seed):
+        return self.add("KeyFromSeed", [seed], self.dims(seed), "key")
+
+    def split_key(self, k, branch):
+        """Split {branch: Left | Right}: derive(k, 0) or derive(k, 1)."""
+        return self.add({"Split": {"branch": branch}}, [k], self.dims(k), "key")
+
+    def fold_in(self, k, n):
+        return self.add("FoldIn", [k, n], self.dims(k), "key")
+
+    def split_n(self, k, count):
+        return self.add({"SplitN": {"count": {"Concrete": count}}}, [k], self.dims(k) + [count], "key")
+
+    def dropout(self, x, rate, key, replay=False):
+        """Dropout / DropoutReplay: inputs [data, rate, key]."""
+        return self.add("DropoutReplay" if replay else "Dropout", [x, rate, key], self.dims(x), self.prec(x))
 
     def compare(self, kind, a, b):
         """Compare(ComparisonKind): kind one of CmpLt, Lt, Eq, Neq, Gt, Gte, Lte."""

@@ -161,3 +161,33 @@ def test_arg_classify_extrema_rejections(build, message):
     st, h = load(g.json())
     assert st != 0
     assert message in L.last_error()
+
+
+@pytest.mark.parametrize("build,message", [
+    (lambda g, x, sd: g.add({"Split": {"branch": "Middle"}}, [g.key_from_seed(sd)], [], "key"), "Split branch"),
+    (lambda g, x, sd: g.key_from_seed(x), "KeyFromSeed seed must be i64"),
+    (lambda g, x, sd: g.add({"SplitN": {"count": {"Node": 1}}}, [g.key_from_seed(sd)], [2], "key"),
+     "SplitN with a runtime count"),
+    (lambda g, x, sd: g.dropout(x, g.const(0.5), sd), "Dropout key must be a key"),
+])
+def test_key_and_dropout_rejections(build, message):
+    g = D.Dag()
+    x = g.load("x", [4])
+    sd = g.load("seed", [], "i64")
+    g.roots = [build(g, x, sd)]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()
+
+
+def test_dropout_under_an_activation_is_rejected():
+    g = D.Dag()
+    x = g.load("x", [4])
+    act = g.load("on", [], "bool")
+    k = g.key_from_seed(g.load("seed", [], "i64"))
+    d = g.dropout(x, g.const(0.5), k)
+    g.nodes[d]["owner"]["activation"] = act
+    g.roots = [d]
+    st, h = load(g.json())
+    assert st != 0
+    assert "under an activation" in L.last_error()

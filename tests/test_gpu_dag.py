@@ -44,7 +44,7 @@ def run(h, tensors):
         v = lib.chelis_device_tensor_view(outs[i]).contents
         shape = [v.shape[d] for d in range(v.rank)]
         np_dt = {L.DTYPE_F32: np.float32, L.DTYPE_F64: np.float64, L.DTYPE_I64: np.int64,
-                 L.DTYPE_I32: np.int32, L.DTYPE_BOOL: np.uint8}[v.dtype]
+                 L.DTYPE_I32: np.int32, L.DTYPE_BOOL: np.uint8, 9: np.uint64}[v.dtype]  # 9: key
         host = np.empty(shape, dtype=np_dt)
         L.call("chelis_device_tensor_copy_to_host_bytes", host.ctypes.data, host.nbytes, outs[i])
         res.append(host)
@@ -472,3 +472,99 @@ def test_float_classify_and_extrema_adjoint(cuda):
     zero = np.zeros_like(gr)
     for r, sel in zip(got[3:], (left_max, ~left_max, left_min, ~left_min)):
         assert np.array_equal(r.view(np.uint32), np.where(sel, gr, zero).view(np.uint32))
+
+
+# ---- keys and keyed dropout ([05-OP-37], [05-OP-69..72]; the C lane's
+# emit_explicitly_keyed_dropout, emit_split_key, emit_fold_in, emit_split_keys)
+
+def test_key_derivations_match_oracle(cuda, orc):
+    seeds = np.array([0, 1, 42, -7, 2 ** 62, -(2 ** 63)], np.int64)
+    data = np.array([3, -1, 0, 99, 5, 2 ** 40], np.int64)
+    g = D.Dag()
+    sd, dd = g.load("seed", [6], "i64"), g.load("n", [6], "i64")
+    k = g.key_from_seed(sd)
+    g.roots = [k, g.split_key(k, "Left"), g.split_key(k, "Right"), g.fold_in(k, dd), g.split_n(k, 3)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(seeds).cuda(), torch.from_numpy(data).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    u = [int(v) & (2 ** 64 - 1) for v in seeds]
+    assert [int(v) for v in got[0]] == u
+    assert [int(v) for v in got[1]] == [orc.derive(x, 0) for x in u]
+    assert [int(v) for v in got[2]] == [orc.derive(x, 1) for x in u]
+    assert [int(v) for v in got[3]] == [orc.derive(orc.derive(x, 2), int(n) & (2 ** 64 - 1))
+                                         for x, n in zip(u, data)]
+    assert [[int(v) for v in row] for row in got[4]] == [[orc.derive(orc.derive(x, 2), j) for j in range(3)]
+                                                         for x in u]
+
+
+@pytest.mark.parametrize("replay", [False, True])
+def test_keyed_dropout_rank0_key_matches_oracle(cuda, orc, replay):
+    """One key for the whole draw: element e of the flat data uses word(key, e)."""
+    x = np.random.default_rng(20).standard_normal((37, 129)).astype(np.float32)
+    x.view(np.uint32)[0, :2] = [0x7fc00123, 0xffc00001]  # NaN payloads come out canonical
+    g = D.Dag()
+    xs = g.load("x", [37, 129])
+    rate = g.const(0.3)
+    k = g.key_from_seed(g.load("seed", [], "i64"))
+    g.roots = [g.dropout(xs, rate, k, replay)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda(), torch.tensor(1234, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    want = orc.dropout(x, 1234, 0.3)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_keyed_dropout_per_row_keys_and_rates(cuda, orc):
+    """A key per row (the key's shape leads the data's) and a rate per row:
+    row b draws word(key[b], e) for its own elements e = 0, 1, ..."""
+    x = np.random.default_rng(21).standard_normal((6, 5, 40)).astype(np.float32)
+    seeds = np.arange(100, 106, dtype=np.int64)
+    rates = np.array([0.0, 0.1, 0.5, 0.9, 0.25, 0.75], np.float32)
+    g = D.Dag()
+    xs = g.load("x", [6, 5, 40])
+    r = g.load("rate", [6])
+    k = g.split_key(g.key_from_seed(g.load("seed", [6], "i64")), "Right")
+    g.roots = [g.dropout(xs, r, k)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(t).cuda() for t in (x, rates, seeds)])
+    finally:
+        L.load().chelis_dag_release(h)
+    for b in range(6):
+        want = orc.dropout(x[b], orc.derive(int(seeds[b]), 1), float(rates[b]))
+        assert np.array_equal(got[b].view(np.uint32), want.view(np.uint32)), b
+
+
+def test_keyed_dropout_f64(cuda, orc):
+    """At f64 the unit value is compared with the rate unrounded."""
+    x = np.random.default_rng(22).standard_normal(300)
+    g = D.Dag()
+    xs = g.load("x", [300], "f64")
+    rate = g.const(0.4, prec="f64")
+    k = g.key_from_seed(g.load("seed", [], "i64"))
+    g.roots = [g.dropout(xs, rate, k)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda(), torch.tensor(77, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    want = np.array([0.0 if orc.unit(77, e) < 0.4 else x[e] / (1.0 - 0.4) for e in range(300)])
+    assert np.array_equal(got, want)
+
+
+def test_keyed_dropout_rate_out_of_range_traps(cuda):
+    g = D.Dag()
+    xs = g.load("x", [8])
+    rate = g.const(1.0)
+    k = g.key_from_seed(g.load("seed", [], "i64"))
+    g.roots = [g.dropout(xs, rate, k)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: domain in dropout at f32"):
+            run(h, [torch.ones(8, device="cuda"), torch.tensor(1, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
