@@ -55,10 +55,26 @@ enum : unsigned int {
     DEVERR_BAD_INDEX = 8u,  // an index operand outside its axis ([05-OP-52])
     DEVERR_DROPOUT_F32 = 16u,  // a dropout rate outside [0, 1) ([05-OP-37]), f32 draw
     DEVERR_DROPOUT_F64 = 32u,  // the same, f64 draw
+    DEVERR_TRAP = 64u,         // a numeric trap recorded in g_trap_code (first one wins)
+};
+
+// A numeric trap raised on the device: kind, operation and dtype packed as
+// 1 + (kind << 16 | op << 8 | dtype), kept for the first trap only, read and
+// cleared with the error word; chelis_cuda_device_status() renders it as
+// "numeric trap: <kind> in <op> at <dtype>".
+__device__ unsigned int g_trap_code = 0;
+enum : unsigned int { TRAP_OVERFLOW = 0u, TRAP_DOMAIN = 1u, TRAP_DIVZERO = 2u };
+enum : unsigned int {
+    TRAP_OP_ADD = 0u, TRAP_OP_SUB, TRAP_OP_MUL, TRAP_OP_TRUNC_DIV, TRAP_OP_FLOOR_DIV, TRAP_OP_MOD,
+    TRAP_OP_NEG, TRAP_OP_ABS
 };
 
 __device__ __forceinline__ void report_device_error(unsigned int code) {
     atomicOr(&g_device_error, code);
+}
+__device__ __forceinline__ void report_trap(unsigned int kind, unsigned int op, unsigned int dtype) {
+    atomicCAS(&g_trap_code, 0u, 1u + ((kind << 16) | (op << 8) | dtype));
+    atomicOr(&g_device_error, static_cast<unsigned int>(DEVERR_TRAP));
 }
 
 // ---------------------------------------------------------------------------

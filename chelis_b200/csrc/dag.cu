@@ -45,6 +45,10 @@
 //   Dropout, DropoutReplay
 //                         keyed draw per key row ([05-OP-37]), the C lane's
 //                         word / unit and rate rule
+//   Add, Sub, Mul, TruncDiv, FloorDiv, Mod, MaxElem, MinElem, Neg, Abs on
+//   integers (and float Mod)
+//                         exact at the stored width; overflow / division by
+//                         zero recorded as numeric traps on the device
 //
 // Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
 // bound in first-Load order and outputs are the Store nodes then the roots
@@ -56,6 +60,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "chelis_dag.h"
@@ -73,7 +78,7 @@ enum class Op {
     Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
-    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout
+    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -82,6 +87,8 @@ enum { LOG_AND = 0, LOG_OR, LOG_NOT };
 // FloatClassify kinds (dtype_semantics.rs FloatClassify order); ExtremaAdjoint kind
 // (Max = 0, Min = 1) and operand (Left = 0, Right = 1) in Node::kind / Node::axis
 enum { FC_NAN = 0, FC_FINITE, FC_INFINITE };
+// exact integer element-wise operations (and float Mod) in Node::kind
+enum { IA_ADD = 0, IA_SUB, IA_MUL, IA_TRUNC_DIV, IA_FLOOR_DIV, IA_MOD, IA_MAX, IA_MIN, IA_NEG, IA_ABS };
 
 struct Node {
     Op op = Op::Drop;
@@ -281,6 +288,19 @@ int tensor_payload(const json::Value *v, int *dtype, std::vector<uint8_t> *out) 
     return CHELIS_CUDA_OK;
 }
 
+bool integer_dtype(int dt) {
+    return dt == CHELIS_DTYPE_I8 || dt == CHELIS_DTYPE_I16 || dt == CHELIS_DTYPE_I32 || dt == CHELIS_DTYPE_I64;
+}
+
+// the RiscOps that run as exact integer arithmetic at the stored width
+int arith_code(const std::string &n) {
+    static const char *names[] = {"Add", "Sub", "Mul", "TruncDiv", "FloorDiv", "Mod", "MaxElem", "MinElem",
+                                  "Neg", "Abs"};
+    for (int i = 0; i < 10; ++i)
+        if (n == names[i]) return i;
+    return -1;
+}
+
 // FusedStepOp (dag.rs:494-526) / binary and unary RiscOps -> step code
 int fused_code(const std::string &n) {
     static const char *names[] = {"Add", "Sub", "Mul", "Div", "Pow", "FloorDiv", "TruncDiv",
@@ -415,6 +435,11 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (sdt != n.dtype ||
             static_cast<int64_t>(n.data.size()) != count_of(n.shape) * dtype_width(n.dtype))
             return bad("ConstTensor payload does not match the node's type");
+    } else if (arith_code(name) >= 0 && (integer_dtype(n.dtype) || name == "Mod")) {
+        // integer arithmetic checked at the stored width ([04-NUM-9]); float Mod is C fmod ([05-OP-64])
+        n.op = Op::Arith;
+        n.kind = arith_code(name);
+        CHELIS_TRY(need_inputs(n.kind >= IA_NEG ? 1 : 2));
     } else if (code >= 0 && name != "TruncDiv") {
         n.op = Op::Elementwise;
         const bool binary = code <= CHELIS_FUSED_MIN_ELEM;
@@ -763,6 +788,15 @@ int check_and_layout(Program &P) {
                 own();
                 break;
             }
+            case Op::Arith:
+                if (!integer_dtype(n.dtype) && n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+                    return unsupported(n.opname + " precision");
+                for (size_t k = 0; k < n.in.size(); ++k) {
+                    if (src(static_cast<int>(k)).dtype != n.dtype) return bad("elementwise operand dtype", n.opname);
+                    CHELIS_TRY(check_same_shape(n, src(static_cast<int>(k)), n.opname.c_str()));
+                }
+                own();
+                break;
             case Op::FloatClassify:
                 if (!floating_dtype(src(0).dtype)) return bad("FloatClassify operand must be a float");
                 if (n.dtype != CHELIS_DTYPE_BOOL) return bad("FloatClassify result must be bool");
@@ -1474,6 +1508,80 @@ __global__ void keyed_dropout_kernel(const T *__restrict__ x, Strided sx, const 
     }
 }
 
+// Exact integer arithmetic at the stored width, as the C lane's checked
+// helpers compute it (chelis_runtime.h chelis_int_checked_*): add, sub, mul
+// and neg / abs of the minimum trap Overflow; trunc_div, floor_div and mod
+// trap DivZero on a zero divisor, trunc_div and floor_div Overflow on MIN /
+// -1, while mod by -1 is 0; floor_div rounds the quotient toward -inf and
+// mod keeps the dividend's sign.  A trap is recorded on the device
+// (report_trap) and the element is written as 0.  Float Mod is fmod.
+template <typename T>
+__device__ __forceinline__ T arith_int(T a, T b, int op, unsigned int dt) {
+    constexpr T lo = sizeof(T) == 8 ? static_cast<T>(INT64_MIN) : sizeof(T) == 4 ? static_cast<T>(INT32_MIN)
+                     : sizeof(T) == 2 ? static_cast<T>(INT16_MIN) : static_cast<T>(INT8_MIN);
+    constexpr T hi = static_cast<T>(~lo);
+    auto trap = [&](unsigned int kind, unsigned int top) -> T {
+        report_trap(kind, top, dt);
+        return T(0);
+    };
+    switch (op) {
+        case IA_ADD: case IA_SUB: {
+            if constexpr (sizeof(T) == 8) {
+                const uint64_t ua = static_cast<uint64_t>(a), ub = static_cast<uint64_t>(b);
+                const int64_t r = static_cast<int64_t>(op == IA_ADD ? ua + ub : ua - ub);
+                const bool ovf = op == IA_ADD ? (((a ^ r) & (b ^ r)) < 0) : (((a ^ b) & (a ^ r)) < 0);
+                return ovf ? trap(TRAP_OVERFLOW, op == IA_ADD ? TRAP_OP_ADD : TRAP_OP_SUB) : static_cast<T>(r);
+            } else {
+                const int64_t r = op == IA_ADD ? int64_t(a) + b : int64_t(a) - b;
+                return (r < lo || r > hi) ? trap(TRAP_OVERFLOW, op == IA_ADD ? TRAP_OP_ADD : TRAP_OP_SUB)
+                                          : static_cast<T>(r);
+            }
+        }
+        case IA_MUL: {
+            if constexpr (sizeof(T) == 8) {
+                const int64_t p = static_cast<int64_t>(static_cast<uint64_t>(a) * static_cast<uint64_t>(b));
+                const int64_t h = __mul64hi(static_cast<long long>(a), static_cast<long long>(b));
+                return h != (p >> 63) ? trap(TRAP_OVERFLOW, TRAP_OP_MUL) : static_cast<T>(p);
+            } else {
+                const int64_t p = int64_t(a) * b;
+                return (p < lo || p > hi) ? trap(TRAP_OVERFLOW, TRAP_OP_MUL) : static_cast<T>(p);
+            }
+        }
+        case IA_TRUNC_DIV: case IA_FLOOR_DIV: {
+            const unsigned int top = op == IA_TRUNC_DIV ? TRAP_OP_TRUNC_DIV : TRAP_OP_FLOOR_DIV;
+            if (b == 0) return trap(TRAP_DIVZERO, top);
+            if (a == lo && b == T(-1)) return trap(TRAP_OVERFLOW, top);
+            T q = static_cast<T>(a / b);
+            const T r = static_cast<T>(a % b);
+            if (op == IA_FLOOR_DIV && r != 0 && ((r < 0) != (b < 0))) q = static_cast<T>(q - 1);
+            return q;
+        }
+        case IA_MOD:
+            if (b == T(-1)) return T(0);
+            if (b == 0) return trap(TRAP_DIVZERO, TRAP_OP_MOD);
+            return static_cast<T>(a % b);
+        case IA_MAX: return a >= b ? a : b;
+        case IA_MIN: return a <= b ? a : b;
+        case IA_NEG: return a == lo ? trap(TRAP_OVERFLOW, TRAP_OP_NEG) : static_cast<T>(-a);
+        default: return a == lo ? trap(TRAP_OVERFLOW, TRAP_OP_ABS) : static_cast<T>(a < 0 ? -a : a);
+    }
+}
+template <typename T>
+__global__ void arith_kernel(const T *__restrict__ a, Strided sa, const T *__restrict__ b, Strided sb, int op,
+                             unsigned int dt, T *__restrict__ out, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const T x = a[offset_of(sa, i)], y = b[offset_of(sb, i)];
+        if constexpr (std::is_floating_point<T>::value) {
+            const T r = fmod(x, y);  // Mod: exact ([05-OP-64]); NaN canonical
+            if constexpr (sizeof(T) == 4) out[i] = r != r ? __int_as_float(0x7fc00000) : r;
+            else out[i] = r != r ? __longlong_as_double(0x7ff8000000000000ll) : r;
+        } else {
+            out[i] = arith_int<T>(x, y, op, dt);
+        }
+    }
+}
+
 unsigned grid_for(int64_t n) {
     int64_t b = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -2043,6 +2151,29 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                     reinterpret_cast<float *>(out), cnt);
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::keyed_dropout_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Arith: {
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Value &a = in(0);
+            const Value &b = n.kind >= IA_NEG ? in(0) : in(1);
+            const Strided sa = strided(a), sb = strided(b);
+            const unsigned int dt = static_cast<unsigned int>(n.dtype);
+#define CHELIS_DAG_ARITH(T)                                                                               \
+    arith_kernel<T><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const T *>(a.ptr), sa,                 \
+                                                  reinterpret_cast<const T *>(b.ptr), sb, n.kind, dt,     \
+                                                  reinterpret_cast<T *>(out), cnt)
+            switch (n.dtype) {
+                case CHELIS_DTYPE_I8: CHELIS_DAG_ARITH(int8_t); break;
+                case CHELIS_DTYPE_I16: CHELIS_DAG_ARITH(int16_t); break;
+                case CHELIS_DTYPE_I32: CHELIS_DAG_ARITH(int32_t); break;
+                case CHELIS_DTYPE_I64: CHELIS_DAG_ARITH(int64_t); break;
+                case CHELIS_DTYPE_F64: CHELIS_DAG_ARITH(double); break;
+                default: CHELIS_DAG_ARITH(float); break;
+            }
+#undef CHELIS_DAG_ARITH
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::arith_kernel");
             return CHELIS_CUDA_OK;
         }
         default: return bad("unexpected node kind", n.opname);

@@ -315,8 +315,18 @@ int chelis_cuda_device_status(void) {
                              "a bounded device wait gave up (error word 0x%x)", word);
         if (word & DEVERR_BAD_INDEX)
             return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in gather at i64");
-        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at %s",
-                         (word & DEVERR_DROPOUT_F32) ? "f32" : "f64");
+        if (word & (DEVERR_DROPOUT_F32 | DEVERR_DROPOUT_F64))
+            return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at %s",
+                             (word & DEVERR_DROPOUT_F32) ? "f32" : "f64");
+        unsigned int code = 0;
+        CHELIS_TRY(check_cuda(cudaMemcpyFromSymbol(&code, g_trap_code, sizeof(code)), "read trap code"));
+        CHELIS_TRY(check_cuda(cudaMemcpyToSymbol(g_trap_code, &zero, sizeof(zero)), "clear trap code"));
+        static const char *const kinds[] = {"overflow", "domain", "division by zero"};
+        static const char *const ops[] = {"add", "sub", "mul", "trunc_div", "floor_div", "mod", "neg", "abs"};
+        static const char *const dtypes[] = {"f32", "f64", "i32", "bool", "i64", "bf16", "f16", "i8", "i16", "key"};
+        const unsigned int c = code ? code - 1 : 0, k = c >> 16, o = (c >> 8) & 0xff, d = c & 0xff;
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: %s in %s at %s", k < 3 ? kinds[k] : "?",
+                         o < 8 ? ops[o] : "?", d < 10 ? dtypes[d] : "?");
     }
     return CHELIS_CUDA_OK;
 }

@@ -30,7 +30,8 @@ from __future__ import annotations
 import json
 import struct
 
-PRIM = {"f32": "F32", "f64": "F64", "i64": "Int64", "i32": "Int32", "bool": "Bool", "key": "Key"}
+PRIM = {"f32": "F32", "f64": "F64", "i64": "Int64", "i32": "Int32", "bool": "Bool", "key": "Key", "i8": "Int8",
+        "i16": "Int16"}
 
 
 def f32_scalar(v: float) -> dict:

@@ -28,7 +28,7 @@ def run(h, tensors):
     for t in tensors:
         t = t.contiguous()
         dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64, torch.int64: L.DTYPE_I64,
-              torch.int32: L.DTYPE_I32, torch.bool: L.DTYPE_BOOL}[t.dtype]
+              torch.int32: L.DTYPE_I32, torch.bool: L.DTYPE_BOOL, torch.int8: 7, torch.int16: 8}[t.dtype]
         shape = (ctypes.c_int64 * max(t.dim(), 1))(*t.shape)
         o = lib.chelis_device_tensor_borrow_shape(dt, t.dim(), shape, t.data_ptr(),
                                                    t.numel() * t.element_size())
@@ -44,7 +44,8 @@ def run(h, tensors):
         v = lib.chelis_device_tensor_view(outs[i]).contents
         shape = [v.shape[d] for d in range(v.rank)]
         np_dt = {L.DTYPE_F32: np.float32, L.DTYPE_F64: np.float64, L.DTYPE_I64: np.int64,
-                 L.DTYPE_I32: np.int32, L.DTYPE_BOOL: np.uint8, 9: np.uint64}[v.dtype]  # 9: key
+                 L.DTYPE_I32: np.int32, L.DTYPE_BOOL: np.uint8, 9: np.uint64,  # 9: key
+                 7: np.int8, 8: np.int16}[v.dtype]
         host = np.empty(shape, dtype=np_dt)
         L.call("chelis_device_tensor_copy_to_host_bytes", host.ctypes.data, host.nbytes, outs[i])
         res.append(host)
@@ -568,3 +569,109 @@ def test_keyed_dropout_rate_out_of_range_traps(cuda):
             run(h, [torch.ones(8, device="cuda"), torch.tensor(1, dtype=torch.int64).cuda()])
     finally:
         L.load().chelis_dag_release(h)
+
+
+# ---- exact integer arithmetic (chelis_runtime.h chelis_int_checked_*; [04-NUM-9])
+
+def _trunc_div(a, b):
+    q = abs(a) // abs(b)
+    return q if (a < 0) == (b < 0) else -q
+
+
+def _rem(a, b):
+    r = abs(a) % abs(b)
+    return r if a >= 0 else -r
+
+
+INT_OPS = {"Add": lambda a, b: a + b, "Sub": lambda a, b: a - b, "Mul": lambda a, b: a * b,
+           "TruncDiv": _trunc_div, "FloorDiv": lambda a, b: a // b, "Mod": lambda a, b: 0 if b == -1 else _rem(a, b),
+           "MaxElem": max, "MinElem": min}
+
+
+@pytest.mark.parametrize("prec,dt", [("i64", np.int64), ("i32", np.int32), ("i16", np.int16), ("i8", np.int8)])
+def test_integer_arithmetic_exact(cuda, prec, dt):
+    info = np.iinfo(dt)
+    rng = np.random.default_rng(30)
+    lim = 2 ** (info.bits // 2 - 2)  # products stay in range
+    a = rng.integers(-lim, lim, 257).astype(dt)
+    b = rng.integers(-lim, lim, 257).astype(dt)
+    b[b == 0] = 3
+    b[:4] = [-1, 1, -7, 7]
+    a[:4] = [info.min + 1, -13, 13, -14]
+    g = D.Dag()
+    x, y = g.load("a", [257], prec), g.load("b", [257], prec)
+    g.roots = [g.binary(op, x, y) for op in INT_OPS] + [g.unary("Neg", x), g.unary("Abs", x)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    for (name, f), r in zip(INT_OPS.items(), got):
+        if name == "Mul":
+            want = [f(int(p), int(q)) for p, q in zip(a[4:], b[4:])]
+            assert [int(v) for v in r[4:]] == want, name
+            continue
+        want = [f(int(p), int(q)) for p, q in zip(a, b)]
+        assert [int(v) for v in r] == want, name
+    assert [int(v) for v in got[-2]] == [-int(v) for v in a]
+    assert [int(v) for v in got[-1]] == [abs(int(v)) for v in a]
+
+
+@pytest.mark.parametrize("op,prec,av,bv,message", [
+    ("Add", "i64", 2 ** 63 - 1, 1, "overflow in add at i64"),
+    ("Sub", "i32", -(2 ** 31), 1, "overflow in sub at i32"),
+    ("Mul", "i64", 2 ** 32, 2 ** 31, "overflow in mul at i64"),
+    ("Mul", "i16", 300, 300, "overflow in mul at i16"),
+    ("TruncDiv", "i64", 5, 0, "division by zero in trunc_div at i64"),
+    ("FloorDiv", "i32", -(2 ** 31), -1, "overflow in floor_div at i32"),
+    ("Mod", "i64", 5, 0, "division by zero in mod at i64"),
+    ("Neg", "i8", -128, 0, "overflow in neg at i8"),
+    ("Abs", "i64", -(2 ** 63), 0, "overflow in abs at i64"),
+])
+def test_integer_arithmetic_traps(cuda, op, prec, av, bv, message):
+    dt = {"i64": np.int64, "i32": np.int32, "i16": np.int16, "i8": np.int8}[prec]
+    a = np.array([1, av, 2], dt)
+    b = np.array([1, bv, 1], dt)
+    g = D.Dag()
+    x, y = g.load("a", [3], prec), g.load("b", [3], prec)
+    g.roots = [g.unary(op, x) if op in ("Neg", "Abs") else g.binary(op, x, y)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: " + message):
+            run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")  # read-and-clear: the next check is clean
+
+
+def test_integer_mod_of_minimum_by_minus_one_is_zero(cuda):
+    a = np.array([-(2 ** 63), 7, -7], np.int64)
+    b = np.array([-1, -1, -1], np.int64)
+    g = D.Dag()
+    x, y = g.load("a", [3], "i64"), g.load("b", [3], "i64")
+    g.roots = [g.binary("Mod", x, y)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert list(got) == [0, 0, 0]
+
+
+def test_float_mod_is_fmod(cuda):
+    rng = np.random.default_rng(31)
+    a = (rng.standard_normal(200) * 10).astype(np.float32)
+    b = rng.standard_normal(200).astype(np.float32)
+    b[0], a[1], b[2] = 0.0, np.inf, np.inf
+    g = D.Dag()
+    x, y = g.load("a", [200]), g.load("b", [200])
+    g.roots = [g.binary("Mod", x, y)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    with np.errstate(invalid="ignore"):
+        want = np.fmod(a, b)
+    want[np.isnan(want)] = np.float32(np.nan)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
