@@ -969,8 +969,10 @@ int check_and_layout(Program &P) {
                 const bool to_float = floating;
                 const bool from_ok = from == CHELIS_DTYPE_F32 || from == CHELIS_DTYPE_F64 ||
                                      from == CHELIS_DTYPE_I32 || from == CHELIS_DTYPE_I64 ||
+                                     from == CHELIS_DTYPE_I16 || from == CHELIS_DTYPE_I8 ||
                                      from == CHELIS_DTYPE_BOOL;
-                if (!to_float || !from_ok) return unsupported("Cast to a non-float precision");
+                const bool to_ok = to_float || integer_dtype(n.dtype) || n.dtype == CHELIS_DTYPE_BOOL;
+                if (!to_ok || !from_ok) return unsupported("Cast between these precisions");
                 CHELIS_TRY(check_same_shape(n, src(0), "Cast"));
                 own();
                 break;
@@ -1169,6 +1171,50 @@ __global__ void cast_kernel(const From *__restrict__ src, Strided s, To *__restr
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
         dst[i] = static_cast<To>(src[offset_of(s, i)]);
+}
+
+// The checked cast to an integer or bool target (the reference's default
+// cast, host_emit.rs checked_cast_*): from a float, a non-finite or
+// non-integral value traps Domain and an out-of-range one Overflow; from an
+// integer or bool, an out-of-range value traps Overflow; to bool, only 0 and 1
+// are admitted (others trap Domain) and 1 gives true.  A trapping element is
+// written as 0 and recorded with report_trap.
+template <typename From, typename To>
+__global__ void cast_checked_kernel(const From *__restrict__ src, Strided s, To *__restrict__ dst, int64_t n,
+                                    unsigned int to_dt) {
+    constexpr bool to_bool = sizeof(To) == 1 && !std::is_signed<To>::value;
+    constexpr int64_t lo = to_bool ? 0 : sizeof(To) == 8 ? INT64_MIN : sizeof(To) == 4 ? INT32_MIN
+                                                          : sizeof(To) == 2 ? INT16_MIN : INT8_MIN;
+    constexpr int64_t hi = to_bool ? 1 : sizeof(To) == 8 ? INT64_MAX : sizeof(To) == 4 ? INT32_MAX
+                                                          : sizeof(To) == 2 ? INT16_MAX : INT8_MAX;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const From x = src[offset_of(s, i)];
+        int64_t w = 0;
+        bool domain = false, overflow = false;
+        if constexpr (std::is_floating_point<From>::value) {
+            const double v = static_cast<double>(x);
+            if (!isfinite(v) || trunc(v) != v || (to_bool && v != 0.0 && v != 1.0)) {
+                domain = true;
+            } else if (to_bool) {
+                w = v == 1.0 ? 1 : 0;
+            } else if (sizeof(To) == 8 ? (v < -9223372036854775808.0 || v >= 9223372036854775808.0)
+                                       : (v < static_cast<double>(lo) || v > static_cast<double>(hi))) {
+                overflow = true;
+            } else {
+                w = static_cast<int64_t>(v);
+            }
+        } else {
+            w = static_cast<int64_t>(x);
+            if (to_bool) domain = w != 0 && w != 1;
+            else overflow = w < lo || w > hi;
+        }
+        if (domain || overflow) {
+            report_trap(domain ? TRAP_DOMAIN : TRAP_OVERFLOW, TRAP_OP_CAST, to_dt);
+            w = 0;
+        }
+        dst[i] = static_cast<To>(w);
+    }
 }
 
 template <typename I>
@@ -1612,6 +1658,24 @@ Strided strided(const Value &v) {
     return s;
 }
 
+// Cast of x (source type From) to the node's dtype: floats by C conversion,
+// integers and bool by the checked cast (cast_checked_kernel).
+template <typename From>
+void launch_cast(const Value &x, char *out, int64_t cnt, chelis_dtype to, cudaStream_t s) {
+    const Strided sx = strided(x);
+    const From *src = reinterpret_cast<const From *>(x.ptr);
+    const unsigned int g = grid_for(cnt), d = static_cast<unsigned int>(to);
+    switch (to) {
+        case CHELIS_DTYPE_F64: cast_kernel<From, double><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<double *>(out), cnt); break;
+        case CHELIS_DTYPE_F32: cast_kernel<From, float><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<float *>(out), cnt); break;
+        case CHELIS_DTYPE_I64: cast_checked_kernel<From, int64_t><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<int64_t *>(out), cnt, d); break;
+        case CHELIS_DTYPE_I32: cast_checked_kernel<From, int32_t><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<int32_t *>(out), cnt, d); break;
+        case CHELIS_DTYPE_I16: cast_checked_kernel<From, int16_t><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<int16_t *>(out), cnt, d); break;
+        case CHELIS_DTYPE_I8: cast_checked_kernel<From, int8_t><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<int8_t *>(out), cnt, d); break;
+        default: cast_checked_kernel<From, uint8_t><<<g, 256, 0, s>>>(src, sx, reinterpret_cast<uint8_t *>(out), cnt, d); break;
+    }
+}
+
 template <typename T>
 int launch_copy(const Value &src, void *dst, int64_t n, cudaStream_t s) {
     if (n == 0) return CHELIS_CUDA_OK;
@@ -1961,23 +2025,15 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
         case Op::Cast: {
             const Value &x = in(0);
             if (cnt == 0) return CHELIS_CUDA_OK;
-            const Strided sx = strided(x);
-            const bool to64 = n.dtype == CHELIS_DTYPE_F64;
-#define CHELIS_DAG_CAST(FROM)                                                                           \
-    if (to64)                                                                                           \
-        cast_kernel<FROM, double><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const FROM *>(x.ptr), sx, \
-                                                              reinterpret_cast<double *>(out), cnt);     \
-    else                                                                                                \
-        cast_kernel<FROM, float><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const FROM *>(x.ptr), sx,  \
-                                                             reinterpret_cast<float *>(out), cnt);
             switch (x.dtype) {
-                case CHELIS_DTYPE_F32: CHELIS_DAG_CAST(float); break;
-                case CHELIS_DTYPE_F64: CHELIS_DAG_CAST(double); break;
-                case CHELIS_DTYPE_I32: CHELIS_DAG_CAST(int32_t); break;
-                case CHELIS_DTYPE_I64: CHELIS_DAG_CAST(int64_t); break;
-                default: CHELIS_DAG_CAST(uint8_t); break;  // bool: 0 / 1
+                case CHELIS_DTYPE_F32: launch_cast<float>(x, out, cnt, n.dtype, s); break;
+                case CHELIS_DTYPE_F64: launch_cast<double>(x, out, cnt, n.dtype, s); break;
+                case CHELIS_DTYPE_I8: launch_cast<int8_t>(x, out, cnt, n.dtype, s); break;
+                case CHELIS_DTYPE_I16: launch_cast<int16_t>(x, out, cnt, n.dtype, s); break;
+                case CHELIS_DTYPE_I32: launch_cast<int32_t>(x, out, cnt, n.dtype, s); break;
+                case CHELIS_DTYPE_I64: launch_cast<int64_t>(x, out, cnt, n.dtype, s); break;
+                default: launch_cast<uint8_t>(x, out, cnt, n.dtype, s); break;  // bool: 0 / 1
             }
-#undef CHELIS_DAG_CAST
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::cast_kernel");
             return CHELIS_CUDA_OK;

@@ -145,6 +145,9 @@ class Dag:
         """Dropout / DropoutReplay: inputs [data, rate, key]."""
         return self.add("DropoutReplay" if replay else "Dropout", [x, rate, key], self.dims(x), self.prec(x))
 
+    def cast(self, x, prec):
+        return self.add({"Cast": {"new_precision": PRIM[prec]}}, [x], self.dims(x), prec)
+
     def compare(self, kind, a, b):
         """Compare(ComparisonKind): kind one of CmpLt, Lt, Eq, Neq, Gt, Gte, Lte."""
         return self.add({"Compare": kind}, [a, b], self.dims(a), "bool")

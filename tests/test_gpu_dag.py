@@ -675,3 +675,64 @@ def test_float_mod_is_fmod(cuda):
         want = np.fmod(a, b)
     want[np.isnan(want)] = np.float32(np.nan)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ---- the checked cast (host_emit.rs checked_cast_*; the reference's default cast)
+
+NP = {"f32": np.float32, "f64": np.float64, "i64": np.int64, "i32": np.int32, "i16": np.int16,
+      "i8": np.int8, "bool": np.bool_}
+
+
+@pytest.mark.parametrize("src,dst,values", [
+    ("f32", "i32", [0.0, -0.0, 7.0, -2147483648.0, 2147483520.0, -3.0]),
+    ("f64", "i64", [1e18, -9223372036854775808.0, 42.0]),
+    ("f32", "i8", [127.0, -128.0, 5.0]),
+    ("f32", "bool", [0.0, 1.0, -0.0]),
+    ("i64", "i32", [2 ** 31 - 1, -(2 ** 31), 0]),
+    ("i32", "i64", [-5, 2 ** 31 - 1, 9]),
+    ("i64", "bool", [0, 1, 1]),
+    ("bool", "i64", [True, False, True]),
+    ("i64", "f32", [2 ** 53 + 1, -(2 ** 40) - 3, 16777217]),
+    ("i16", "f64", [-32768, 12, 32767]),
+])
+def test_checked_cast_values(cuda, src, dst, values):
+    x = np.array(values, NP[src])
+    g = D.Dag()
+    a = g.load("x", [len(values)], src)
+    g.roots = [g.cast(a, dst)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    if dst == "bool":
+        assert list(got) == [1 if v == 1 else 0 for v in values]
+    elif dst in ("f32", "f64"):
+        want = np.array([NP[dst](int(v)) for v in values], NP[dst])
+        assert np.array_equal(got, want)
+    else:
+        assert [int(v) for v in got] == [int(v) for v in values]
+
+
+@pytest.mark.parametrize("src,dst,bad,message", [
+    ("f32", "i32", 1.5, "domain in cast at i32"),
+    ("f32", "i64", float("inf"), "domain in cast at i64"),
+    ("f32", "i64", float("nan"), "domain in cast at i64"),
+    ("f32", "i32", 3e9, "overflow in cast at i32"),
+    ("f64", "i64", 9.3e18, "overflow in cast at i64"),
+    ("i64", "i8", 300, "overflow in cast at i8"),
+    ("i64", "bool", 2, "domain in cast at bool"),
+    ("f32", "bool", 0.5, "domain in cast at bool"),
+])
+def test_checked_cast_traps(cuda, src, dst, bad, message):
+    x = np.array([1, bad, 0], NP[src])
+    g = D.Dag()
+    a = g.load("x", [3], src)
+    g.roots = [g.cast(a, dst)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: " + message):
+            run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")
