@@ -78,7 +78,7 @@ enum class Op {
     Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
-    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith
+    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -88,6 +88,8 @@ enum { LOG_AND = 0, LOG_OR, LOG_NOT };
 // (Max = 0, Min = 1) and operand (Left = 0, Right = 1) in Node::kind / Node::axis
 enum { FC_NAN = 0, FC_FINITE, FC_INFINITE };
 // exact integer element-wise operations (and float Mod) in Node::kind
+// NamedCast modes (NamedCastMode order)
+enum { NC_TRUNC = 0, NC_SATURATE, NC_WRAP };
 enum { IA_ADD = 0, IA_SUB, IA_MUL, IA_TRUNC_DIV, IA_FLOOR_DIV, IA_MOD, IA_MAX, IA_MIN, IA_NEG, IA_ABS };
 
 struct Node {
@@ -618,6 +620,17 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         int fdt = 0;
         CHELIS_TRY(scalar(field("fill"), &fdt, &n.bits));
         if (fdt != n.dtype) return bad("Pad fill dtype");
+    } else if (name == "NamedCast") {
+        // cast_trunc [05-OP-6], cast_saturate [05-OP-23], cast_wrap [05-OP-24]
+        static const char *modes[] = {"Trunc", "Saturate", "Wrap"};
+        n.op = Op::NamedCast;
+        const json::Value *m = field("mode");
+        n.kind = -1;
+        if (m && m->kind == json::Value::Str)
+            for (int i = 0; i < 3; ++i)
+                if (m->s == modes[i]) n.kind = i;
+        if (n.kind < 0) return bad("NamedCast mode");
+        CHELIS_TRY(need_inputs(1));
     } else if (name == "Cast") {
         n.op = Op::Cast;
         CHELIS_TRY(need_inputs(1));
@@ -785,6 +798,18 @@ int check_and_layout(Program &P) {
                     return bad("Dropout key shape");
                 if (rs.size() > ks.size() || !std::equal(rs.begin(), rs.end(), ks.begin()))
                     return bad("Dropout rate shape");
+                own();
+                break;
+            }
+            case Op::NamedCast: {
+                const int from = src(0).dtype;
+                const bool ffrom = from == CHELIS_DTYPE_F32 || from == CHELIS_DTYPE_F64;
+                if (!integer_dtype(n.dtype)) return bad("NamedCast targets a signed integer");
+                if (n.kind == NC_TRUNC && !ffrom) return bad("cast_trunc converts a float source");
+                if (n.kind == NC_WRAP && !integer_dtype(from)) return bad("cast_wrap converts an integer source");
+                if (n.kind == NC_SATURATE && !ffrom && !integer_dtype(from))
+                    return bad("cast_saturate converts a float or integer source");
+                CHELIS_TRY(check_same_shape(n, src(0), "NamedCast"));
                 own();
                 break;
             }
@@ -1212,6 +1237,49 @@ __global__ void cast_checked_kernel(const From *__restrict__ src, Strided s, To 
         if (domain || overflow) {
             report_trap(domain ? TRAP_DOMAIN : TRAP_OVERFLOW, TRAP_OP_CAST, to_dt);
             w = 0;
+        }
+        dst[i] = static_cast<To>(w);
+    }
+}
+
+// The named lossy casts to a signed integer (host_emit.rs named_cast_c_expr):
+// cast_trunc (float source) truncates toward zero, trapping Domain on a
+// non-finite value and Overflow out of range; cast_saturate truncates and
+// clamps to the target range, trapping Domain on NaN only; cast_wrap
+// (integer source) keeps the target width's low bits, sign-extended.
+template <typename From, typename To>
+__global__ void named_cast_kernel(const From *__restrict__ src, Strided s, int mode, To *__restrict__ dst,
+                                  int64_t n, unsigned int to_dt) {
+    constexpr int bits = 8 * sizeof(To);
+    constexpr int64_t lo = bits == 64 ? INT64_MIN : -(int64_t(1) << (bits - 1));
+    constexpr int64_t hi = bits == 64 ? INT64_MAX : (int64_t(1) << (bits - 1)) - 1;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const From x = src[offset_of(s, i)];
+        int64_t w = 0;
+        if constexpr (std::is_floating_point<From>::value) {
+            const double v = static_cast<double>(x);
+            if (mode == NC_TRUNC) {
+                const double t = trunc(v);
+                if (!isfinite(v)) report_trap(TRAP_DOMAIN, TRAP_OP_CAST_TRUNC, to_dt);
+                else if (bits == 64 ? (t < -9223372036854775808.0 || t >= 9223372036854775808.0)
+                                    : (t < static_cast<double>(lo) || t > static_cast<double>(hi)))
+                    report_trap(TRAP_OVERFLOW, TRAP_OP_CAST_TRUNC, to_dt);
+                else w = static_cast<int64_t>(t);
+            } else {  // saturate
+                if (isnan(v)) report_trap(TRAP_DOMAIN, TRAP_OP_CAST_SATURATE, to_dt);
+                else if (v <= static_cast<double>(lo)) w = lo;
+                else if (v >= static_cast<double>(hi)) w = hi;
+                else w = static_cast<int64_t>(trunc(v));
+            }
+        } else {
+            const int64_t v = static_cast<int64_t>(x);
+            if (mode == NC_SATURATE) w = v < lo ? lo : (v > hi ? hi : v);
+            else if (bits >= 8 * static_cast<int>(sizeof(From))) w = v;
+            else {
+                const uint64_t sign = uint64_t(1) << (bits - 1), mask = (sign << 1) - 1;
+                w = static_cast<int64_t>(((static_cast<uint64_t>(v) & mask) ^ sign) - sign);
+            }
         }
         dst[i] = static_cast<To>(w);
     }
@@ -1658,6 +1726,19 @@ Strided strided(const Value &v) {
     return s;
 }
 
+template <typename From>
+void launch_named_cast(const Value &x, char *out, int64_t cnt, chelis_dtype to, int mode, cudaStream_t s) {
+    const Strided sx = strided(x);
+    const From *src = reinterpret_cast<const From *>(x.ptr);
+    const unsigned int g = grid_for(cnt), d = static_cast<unsigned int>(to);
+    switch (to) {
+        case CHELIS_DTYPE_I64: named_cast_kernel<From, int64_t><<<g, 256, 0, s>>>(src, sx, mode, reinterpret_cast<int64_t *>(out), cnt, d); break;
+        case CHELIS_DTYPE_I32: named_cast_kernel<From, int32_t><<<g, 256, 0, s>>>(src, sx, mode, reinterpret_cast<int32_t *>(out), cnt, d); break;
+        case CHELIS_DTYPE_I16: named_cast_kernel<From, int16_t><<<g, 256, 0, s>>>(src, sx, mode, reinterpret_cast<int16_t *>(out), cnt, d); break;
+        default: named_cast_kernel<From, int8_t><<<g, 256, 0, s>>>(src, sx, mode, reinterpret_cast<int8_t *>(out), cnt, d); break;
+    }
+}
+
 // Cast of x (source type From) to the node's dtype: floats by C conversion,
 // integers and bool by the checked cast (cast_checked_kernel).
 template <typename From>
@@ -2036,6 +2117,21 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
             }
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::cast_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::NamedCast: {
+            const Value &x = in(0);
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            switch (x.dtype) {
+                case CHELIS_DTYPE_F32: launch_named_cast<float>(x, out, cnt, n.dtype, n.kind, s); break;
+                case CHELIS_DTYPE_F64: launch_named_cast<double>(x, out, cnt, n.dtype, n.kind, s); break;
+                case CHELIS_DTYPE_I8: launch_named_cast<int8_t>(x, out, cnt, n.dtype, n.kind, s); break;
+                case CHELIS_DTYPE_I16: launch_named_cast<int16_t>(x, out, cnt, n.dtype, n.kind, s); break;
+                case CHELIS_DTYPE_I32: launch_named_cast<int32_t>(x, out, cnt, n.dtype, n.kind, s); break;
+                default: launch_named_cast<int64_t>(x, out, cnt, n.dtype, n.kind, s); break;
+            }
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::named_cast_kernel");
             return CHELIS_CUDA_OK;
         }
         case Op::Compare: {

@@ -148,6 +148,10 @@ class Dag:
     def cast(self, x, prec):
         return self.add({"Cast": {"new_precision": PRIM[prec]}}, [x], self.dims(x), prec)
 
+    def named_cast(self, x, mode, prec):
+        """NamedCast {mode: Trunc | Saturate | Wrap} to a signed integer."""
+        return self.add({"NamedCast": {"mode": mode, "new_precision": PRIM[prec]}}, [x], self.dims(x), prec)
+
     def compare(self, kind, a, b):
         """Compare(ComparisonKind): kind one of CmpLt, Lt, Eq, Neq, Gt, Gte, Lte."""
         return self.add({"Compare": kind}, [a, b], self.dims(a), "bool")

@@ -191,3 +191,17 @@ def test_dropout_under_an_activation_is_rejected():
     st, h = load(g.json())
     assert st != 0
     assert "under an activation" in L.last_error()
+
+
+@pytest.mark.parametrize("mode,src,message", [
+    ("Trunc", "i64", "cast_trunc converts a float source"),
+    ("Wrap", "f32", "cast_wrap converts an integer source"),
+    ("Round", "f32", "NamedCast mode"),
+])
+def test_named_cast_rejections(mode, src, message):
+    g = D.Dag()
+    a = g.load("a", [4], src)
+    g.roots = [g.named_cast(a, mode, "i32")]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()

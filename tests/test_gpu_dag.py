@@ -736,3 +736,52 @@ def test_checked_cast_traps(cuda, src, dst, bad, message):
     finally:
         L.load().chelis_dag_release(h)
     L.call("chelis_cuda_device_status")
+
+
+# ---- named lossy casts (cast_trunc [05-OP-6], cast_saturate [05-OP-23], cast_wrap [05-OP-24])
+
+def _wrap(v, bits):
+    v &= (1 << bits) - 1
+    return v - (1 << bits) if v >= 1 << (bits - 1) else v
+
+
+@pytest.mark.parametrize("mode,src,dst,values,want", [
+    ("Trunc", "f32", "i32", [2.9, -2.9, -0.0, 1e9, -2147483648.0], [2, -2, 0, 1000000000, -2147483648]),
+    ("Trunc", "f64", "i8", [127.9, -128.99, 3.5], [127, -128, 3]),
+    ("Saturate", "f32", "i8", [300.0, -1e30, 5.7, -5.7, float("inf"), float("-inf")], [127, -128, 5, -5, 127, -128]),
+    ("Saturate", "f64", "i64", [1e19, -1e19, 123.9], [2 ** 63 - 1, -(2 ** 63), 123]),
+    ("Saturate", "i64", "i16", [40000, -40000, 12], [32767, -32768, 12]),
+    ("Wrap", "i64", "i8", [300, -129, 127, 2 ** 40 + 5], [_wrap(300, 8), _wrap(-129, 8), 127, 5]),
+    ("Wrap", "i32", "i64", [-5, 7, 2 ** 31 - 1], [-5, 7, 2 ** 31 - 1]),
+])
+def test_named_cast_values(cuda, mode, src, dst, values, want):
+    x = np.array(values, NP[src])
+    g = D.Dag()
+    a = g.load("x", [len(values)], src)
+    g.roots = [g.named_cast(a, mode, dst)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert [int(v) for v in got] == want
+
+
+@pytest.mark.parametrize("mode,src,dst,bad,message", [
+    ("Trunc", "f32", "i32", float("nan"), "domain in cast_trunc at i32"),
+    ("Trunc", "f32", "i32", float("inf"), "domain in cast_trunc at i32"),
+    ("Trunc", "f64", "i8", 128.5, "overflow in cast_trunc at i8"),
+    ("Saturate", "f32", "i64", float("nan"), "domain in cast_saturate at i64"),
+])
+def test_named_cast_traps(cuda, mode, src, dst, bad, message):
+    x = np.array([1, bad, 0], NP[src])
+    g = D.Dag()
+    a = g.load("x", [3], src)
+    g.roots = [g.named_cast(a, mode, dst)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: " + message):
+            run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")
