@@ -56,7 +56,9 @@ enum : unsigned int {
     DEVERR_DROPOUT_F32 = 16u,  // a dropout rate outside [0, 1) ([05-OP-37]), f32 draw
     DEVERR_DROPOUT_F64 = 32u,  // the same, f64 draw
     DEVERR_TRAP = 64u,         // a numeric trap recorded in g_trap_code (first one wins)
+    DEVERR_SHIFT = 128u,       // a negative shift count, recorded in g_shift_count
 };
+__device__ unsigned long long g_shift_count = 0;  // the first negative count reported (its bits)
 
 // A numeric trap raised on the device: kind, operation and dtype packed as
 // 1 + (kind << 16 | op << 8 | dtype), kept for the first trap only, read and

@@ -90,7 +90,8 @@ enum { FC_NAN = 0, FC_FINITE, FC_INFINITE };
 // exact integer element-wise operations (and float Mod) in Node::kind
 // NamedCast modes (NamedCastMode order)
 enum { NC_TRUNC = 0, NC_SATURATE, NC_WRAP };
-enum { IA_ADD = 0, IA_SUB, IA_MUL, IA_TRUNC_DIV, IA_FLOOR_DIV, IA_MOD, IA_MAX, IA_MIN, IA_NEG, IA_ABS };
+enum { IA_ADD = 0, IA_SUB, IA_MUL, IA_TRUNC_DIV, IA_FLOOR_DIV, IA_MOD, IA_MAX, IA_MIN, IA_NEG, IA_ABS,
+       IA_AND, IA_OR, IA_XOR, IA_SHL, IA_SHR };
 
 struct Node {
     Op op = Op::Drop;
@@ -437,11 +438,22 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (sdt != n.dtype ||
             static_cast<int64_t>(n.data.size()) != count_of(n.shape) * dtype_width(n.dtype))
             return bad("ConstTensor payload does not match the node's type");
+    } else if (name == "Bitwise") {
+        // [05-OP-47] BitwiseKind: And, Or, Xor, ShiftLeft, ShiftRight
+        static const char *kinds[] = {"And", "Or", "Xor", "ShiftLeft", "ShiftRight"};
+        n.op = Op::Arith;
+        n.kind = -1;
+        if (body && body->kind == json::Value::Str)
+            for (int i = 0; i < 5; ++i)
+                if (body->s == kinds[i]) n.kind = IA_AND + i;
+        if (n.kind < 0) return bad("Bitwise kind");
+        if (!integer_dtype(n.dtype)) return bad("Bitwise operands must be integers");
+        CHELIS_TRY(need_inputs(2));
     } else if (arith_code(name) >= 0 && (integer_dtype(n.dtype) || name == "Mod")) {
         // integer arithmetic checked at the stored width ([04-NUM-9]); float Mod is C fmod ([05-OP-64])
         n.op = Op::Arith;
         n.kind = arith_code(name);
-        CHELIS_TRY(need_inputs(n.kind >= IA_NEG ? 1 : 2));
+        CHELIS_TRY(need_inputs(n.kind == IA_NEG || n.kind == IA_ABS ? 1 : 2));
     } else if (code >= 0 && name != "TruncDiv") {
         n.op = Op::Elementwise;
         const bool binary = code <= CHELIS_FUSED_MIN_ELEM;
@@ -1677,7 +1689,29 @@ __device__ __forceinline__ T arith_int(T a, T b, int op, unsigned int dt) {
         case IA_MAX: return a >= b ? a : b;
         case IA_MIN: return a <= b ? a : b;
         case IA_NEG: return a == lo ? trap(TRAP_OVERFLOW, TRAP_OP_NEG) : static_cast<T>(-a);
-        default: return a == lo ? trap(TRAP_OVERFLOW, TRAP_OP_ABS) : static_cast<T>(a < 0 ? -a : a);
+        case IA_ABS: return a == lo ? trap(TRAP_OVERFLOW, TRAP_OP_ABS) : static_cast<T>(a < 0 ? -a : a);
+        case IA_AND: return static_cast<T>(a & b);
+        case IA_OR: return static_cast<T>(a | b);
+        case IA_XOR: return static_cast<T>(a ^ b);
+        default: {
+            // width-bounded two's-complement shifts (chelis_runtime.h
+            // chelis_int_shl / _shr): a count of at least the width gives 0
+            // (left) or the sign fill (right); a negative count is reported
+            constexpr int bits = 8 * sizeof(T);
+            const int64_t amount = static_cast<int64_t>(b);
+            if (amount < 0) {
+                atomicCAS(&g_shift_count, 0ull, static_cast<unsigned long long>(amount));
+                atomicOr(&g_device_error, static_cast<unsigned int>(DEVERR_SHIFT));
+                return T(0);
+            }
+            if (op == IA_SHL) {
+                if (amount >= bits) return T(0);
+                using U = typename std::make_unsigned<T>::type;
+                return static_cast<T>(static_cast<U>(static_cast<U>(a) << amount));
+            }
+            if (amount >= bits) return a < 0 ? T(-1) : T(0);
+            return static_cast<T>(a >> amount);  // arithmetic shift of a signed value
+        }
     }
 }
 template <typename T>
@@ -2308,7 +2342,7 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
         case Op::Arith: {
             if (cnt == 0) return CHELIS_CUDA_OK;
             const Value &a = in(0);
-            const Value &b = n.kind >= IA_NEG ? in(0) : in(1);
+            const Value &b = n.kind == IA_NEG || n.kind == IA_ABS ? in(0) : in(1);
             const Strided sa = strided(a), sb = strided(b);
             const unsigned int dt = static_cast<unsigned int>(n.dtype);
 #define CHELIS_DAG_ARITH(T)                                                                               \

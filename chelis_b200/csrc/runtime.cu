@@ -318,6 +318,13 @@ int chelis_cuda_device_status(void) {
         if (word & (DEVERR_DROPOUT_F32 | DEVERR_DROPOUT_F64))
             return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in dropout at %s",
                              (word & DEVERR_DROPOUT_F32) ? "f32" : "f64");
+        if (word & DEVERR_SHIFT) {
+            unsigned long long bits = 0, zero64 = 0;
+            CHELIS_TRY(check_cuda(cudaMemcpyFromSymbol(&bits, g_shift_count, sizeof(bits)), "read shift count"));
+            CHELIS_TRY(check_cuda(cudaMemcpyToSymbol(g_shift_count, &zero64, sizeof(zero64)), "clear shift count"));
+            return set_error(CHELIS_CUDA_ERR_DOMAIN, "shift amount must be non-negative, got %lld",
+                             static_cast<long long>(bits));
+        }
         unsigned int code = 0;
         CHELIS_TRY(check_cuda(cudaMemcpyFromSymbol(&code, g_trap_code, sizeof(code)), "read trap code"));
         CHELIS_TRY(check_cuda(cudaMemcpyToSymbol(g_trap_code, &zero, sizeof(zero)), "clear trap code"));

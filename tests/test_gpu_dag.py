@@ -785,3 +785,52 @@ def test_named_cast_traps(cuda, mode, src, dst, bad, message):
     finally:
         L.load().chelis_dag_release(h)
     L.call("chelis_cuda_device_status")
+
+
+# ---- Bitwise ([05-OP-47]; chelis_runtime.h chelis_int_shl / chelis_int_shr)
+
+def _shl(v, k, bits):
+    return 0 if k >= bits else _wrap(v << k, bits)
+
+
+def _shr(v, k, bits):
+    return (-1 if v < 0 else 0) if k >= bits else v >> k
+
+
+@pytest.mark.parametrize("prec,dt,bits", [("i64", np.int64, 64), ("i32", np.int32, 32), ("i8", np.int8, 8)])
+def test_bitwise(cuda, prec, dt, bits):
+    rng = np.random.default_rng(40)
+    info = np.iinfo(dt)
+    a = rng.integers(info.min, info.max, 300, endpoint=True, dtype=np.int64).astype(dt)
+    b = rng.integers(info.min, info.max, 300, endpoint=True, dtype=np.int64).astype(dt)
+    k = rng.integers(0, min(bits + 10, int(info.max)), 300).astype(dt)
+    g = D.Dag()
+    x, y, c = g.load("a", [300], prec), g.load("b", [300], prec), g.load("k", [300], prec)
+    bw = lambda kind, p, q: g.add({"Bitwise": kind}, [p, q], [300], prec)
+    g.roots = [bw("And", x, y), bw("Or", x, y), bw("Xor", x, y), bw("ShiftLeft", x, c), bw("ShiftRight", x, c)]
+    h = program(g)
+    try:
+        got = run(h, [torch.from_numpy(t).cuda() for t in (a, b, k)])
+    finally:
+        L.load().chelis_dag_release(h)
+    A, B, K = [int(v) for v in a], [int(v) for v in b], [int(v) for v in k]
+    assert [int(v) for v in got[0]] == [p & q for p, q in zip(A, B)]
+    assert [int(v) for v in got[1]] == [p | q for p, q in zip(A, B)]
+    assert [int(v) for v in got[2]] == [p ^ q for p, q in zip(A, B)]
+    assert [int(v) for v in got[3]] == [_shl(p, q, bits) for p, q in zip(A, K)]
+    assert [int(v) for v in got[4]] == [_shr(p, q, bits) for p, q in zip(A, K)]
+
+
+def test_negative_shift_count_is_reported(cuda):
+    a = np.array([1, 2, 3], np.int64)
+    k = np.array([0, -3, 1], np.int64)
+    g = D.Dag()
+    x, c = g.load("a", [3], "i64"), g.load("k", [3], "i64")
+    g.roots = [g.add({"Bitwise": "ShiftLeft"}, [x, c], [3], "i64")]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="shift amount must be non-negative, got -3"):
+            run(h, [torch.from_numpy(a).cuda(), torch.from_numpy(k).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")
