@@ -27,6 +27,9 @@ int current_device_checked(int *device);
 int scratch_alloc(void **ptr, size_t bytes, cudaStream_t stream);
 void scratch_free(void *ptr, cudaStream_t stream);
 int sm_count();
+// GuardedFail messages, by id, for chelis_cuda_device_status (runtime.cu)
+uint32_t register_fail_message(const char *message);
+void unregister_fail_message(uint32_t id);
 // data-parallel communicator (dp.cu): its size (1 when none is open), the
 // library's communication stream, an f32 sum all-reduce on a given stream
 int dp_nranks();
@@ -57,7 +60,9 @@ enum : unsigned int {
     DEVERR_DROPOUT_F64 = 32u,  // the same, f64 draw
     DEVERR_TRAP = 64u,         // a numeric trap recorded in g_trap_code (first one wins)
     DEVERR_SHIFT = 128u,       // a negative shift count, recorded in g_shift_count
+    DEVERR_FAIL = 256u,        // a GuardedFail fired: its message id in g_fail_id
 };
+__device__ unsigned int g_fail_id = 0;  // the first fired guard's registered message id
 __device__ unsigned long long g_shift_count = 0;  // the first negative count reported (its bits)
 
 // A numeric trap raised on the device: kind, operation and dtype packed as

@@ -49,6 +49,8 @@
 //   integers (and float Mod)
 //                         exact at the stored width; overflow / division by
 //                         zero recorded as numeric traps on the device
+//   GuardedFail           the fallback, and the node's message reported by
+//                         chelis_cuda_device_status when the condition fires
 //
 // Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
 // bound in first-Load order and outputs are the Store nodes then the roots
@@ -78,7 +80,8 @@ enum class Op {
     Load, Const, ConstTensor, Elementwise, Fused, Relu, ReluAdjoint, Softmax, Sum, MaxReduce,
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
-    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast
+    FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
+    GuardedFail
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -111,6 +114,8 @@ struct Node {
     int accumulator = -1;                              // Sum / BlasMatmul
     int kind = 0;                                      // Compare / Logical (CMP_* / LOG_*)
     int activation = -1;                               // owner.activation node, if any
+    std::string message;                               // GuardedFail
+    uint32_t fail_id = 0;                              // its registered message id
 };
 
 // Static layout of a node's value: elements at root storage + offset +
@@ -137,6 +142,13 @@ struct Program {
     std::vector<std::string> output_labels;
     std::vector<int> output_node;    // the node whose value is the output
     std::vector<int> direct_output;  // node -> output index when it writes into the owner
+    std::vector<uint32_t> fail_ids;  // registered GuardedFail messages, released with the program
+    ~Program() {
+        for (uint32_t id : fail_ids) unregister_fail_message(id);
+    }
+    Program() = default;
+    Program(const Program &) = delete;
+    Program &operator=(const Program &) = delete;
 };
 
 int64_t count_of(const std::vector<int64_t> &shape) {
@@ -632,6 +644,16 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         int fdt = 0;
         CHELIS_TRY(scalar(field("fill"), &fdt, &n.bits));
         if (fdt != n.dtype) return bad("Pad fill dtype");
+    } else if (name == "GuardedFail") {
+        // [05-OP-68]: abort with `message` where the condition fires
+        // (true when trap_on_true, else false); the result is the fallback
+        n.op = Op::GuardedFail;
+        const json::Value *m = field("message"), *t = field("trap_on_true");
+        if (!m || m->kind != json::Value::Str || !t || t->kind != json::Value::Bool)
+            return bad("GuardedFail message / trap_on_true");
+        n.message = m->s;
+        n.kind = t->b ? 1 : 0;
+        CHELIS_TRY(need_inputs(2));
     } else if (name == "NamedCast") {
         // cast_trunc [05-OP-6], cast_saturate [05-OP-23], cast_wrap [05-OP-24]
         static const char *modes[] = {"Trunc", "Saturate", "Wrap"};
@@ -813,6 +835,12 @@ int check_and_layout(Program &P) {
                 own();
                 break;
             }
+            case Op::GuardedFail:
+                if (src(0).dtype != CHELIS_DTYPE_BOOL) return bad("GuardedFail condition must be bool");
+                if (src(1).dtype != n.dtype) return bad("GuardedFail fallback dtype");
+                CHELIS_TRY(check_same_shape(n, src(1), "GuardedFail"));
+                own();
+                break;
             case Op::NamedCast: {
                 const int from = src(0).dtype;
                 const bool ffrom = from == CHELIS_DTYPE_F32 || from == CHELIS_DTYPE_F64;
@@ -1295,6 +1323,17 @@ __global__ void named_cast_kernel(const From *__restrict__ src, Strided s, int m
         }
         dst[i] = static_cast<To>(w);
     }
+}
+
+// GuardedFail: any condition element equal to `fires` (1 or 0) records the
+// guard's message id (the first guard to fire in stream order keeps it)
+__global__ void guard_kernel(const uint8_t *__restrict__ c, Strided sc, int fires, uint32_t id, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        if ((c[offset_of(sc, i)] != 0) == (fires != 0)) {
+            atomicCAS(&g_fail_id, 0u, id);
+            atomicOr(&g_device_error, static_cast<unsigned int>(DEVERR_FAIL));
+        }
 }
 
 template <typename I>
@@ -2153,6 +2192,17 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
             CHELIS_LAUNCH_CHECK("dag::cast_kernel");
             return CHELIS_CUDA_OK;
         }
+        case Op::GuardedFail: {
+            const Value &c = in(0);
+            const int64_t nc = count_of(c.shape);
+            if (nc > 0) {
+                guard_kernel<<<grid_for(nc), 256, 0, s>>>(reinterpret_cast<const uint8_t *>(c.ptr), strided(c),
+                                                          n.kind, n.fail_id, nc);
+                g_launches++;
+                CHELIS_LAUNCH_CHECK("dag::guard_kernel");
+            }
+            return materialize(in(1), out, s);
+        }
         case Op::NamedCast: {
             const Value &x = in(0);
             if (cnt == 0) return CHELIS_CUDA_OK;
@@ -2400,6 +2450,11 @@ int chelis_dag_from_json(const char *text, int64_t len, chelis_dag_program **out
     }
     CHELIS_TRY(dag::check_and_layout(p->prog));
     CHELIS_TRY(dag::plan(p->prog, rs));
+    for (auto &n : p->prog.nodes)
+        if (n.op == dag::Op::GuardedFail) {
+            n.fail_id = register_fail_message(n.message.c_str());
+            p->prog.fail_ids.push_back(n.fail_id);
+        }
     *out = p.release();
     return CHELIS_CUDA_OK;
 }

@@ -9,7 +9,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
+#include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "common.cuh"
@@ -266,6 +269,30 @@ int validate_device_pointer(const void *data, int32_t device) {
 
 }  // namespace
 
+namespace chelis {
+namespace {
+std::mutex g_fail_mu;
+std::unordered_map<uint32_t, std::string> g_fail_messages;
+uint32_t g_fail_next = 1;
+}  // namespace
+uint32_t register_fail_message(const char *message) {
+    std::lock_guard<std::mutex> lk(g_fail_mu);
+    const uint32_t id = g_fail_next++;
+    g_fail_messages[id] = message;
+    return id;
+}
+void unregister_fail_message(uint32_t id) {
+    std::lock_guard<std::mutex> lk(g_fail_mu);
+    g_fail_messages.erase(id);
+}
+// the registered message of guard `id` (a default text if it was released)
+std::string fail_message(uint32_t id) {
+    std::lock_guard<std::mutex> lk(g_fail_mu);
+    const auto it = g_fail_messages.find(id);
+    return it != g_fail_messages.end() ? it->second : std::string("a guarded abort fired");
+}
+}  // namespace chelis
+
 extern "C" {
 
 int chelis_cuda_version(void) { return 1; }
@@ -313,6 +340,12 @@ int chelis_cuda_device_status(void) {
         if (word & DEVERR_TIMEOUTS)
             return set_error(CHELIS_CUDA_ERR_TIMEOUT,
                              "a bounded device wait gave up (error word 0x%x)", word);
+        if (word & DEVERR_FAIL) {
+            unsigned int id = 0;
+            CHELIS_TRY(check_cuda(cudaMemcpyFromSymbol(&id, g_fail_id, sizeof(id)), "read fail id"));
+            CHELIS_TRY(check_cuda(cudaMemcpyToSymbol(g_fail_id, &zero, sizeof(zero)), "clear fail id"));
+            return set_error(CHELIS_CUDA_ERR_FAIL, "%s", fail_message(id).c_str());
+        }
         if (word & DEVERR_BAD_INDEX)
             return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in gather at i64");
         if (word & (DEVERR_DROPOUT_F32 | DEVERR_DROPOUT_F64))
@@ -333,7 +366,8 @@ int chelis_cuda_device_status(void) {
                                           "cast_trunc", "cast_saturate"};
         static const char *const dtypes[] = {"f32", "f64", "i32", "bool", "i64", "bf16", "f16", "i8", "i16", "key"};
         const unsigned int c = code ? code - 1 : 0, k = c >> 16, o = (c >> 8) & 0xff, d = c & 0xff;
-        return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: %s in %s at %s", k < 3 ? kinds[k] : "?",
+        return set_error(k == 0 ? CHELIS_CUDA_ERR_OVERFLOW : CHELIS_CUDA_ERR_DOMAIN,
+                         "numeric trap: %s in %s at %s", k < 3 ? kinds[k] : "?",
                          o < 11 ? ops[o] : "?", d < 10 ? dtypes[d] : "?");
     }
     return CHELIS_CUDA_OK;

@@ -51,7 +51,7 @@ GEMM_3XTF32, GEMM_EXACT_TREE = 0, 1
 DGEMM_AUTO, DGEMM_DMMA, DGEMM_FFMA = 0, 1, 2
 ROWS_EXACT, ROWS_FAST = 0, 1
 STATUS_NAMES = {0: "OK", 1: "DOMAIN", 2: "OVERFLOW", 3: "CUDA", 4: "UNSUPPORTED", 5: "TIMEOUT",
-                6: "NO_DEVICE"}
+                6: "NO_DEVICE", 7: "FAIL"}
 
 
 class ChelisCudaError(RuntimeError):

@@ -72,7 +72,8 @@ enum {
     CHELIS_CUDA_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
     CHELIS_CUDA_ERR_UNSUPPORTED = 4, /* shape/dtype/layout this build does not admit */
     CHELIS_CUDA_ERR_TIMEOUT = 5,     /* a bounded device wait gave up */
-    CHELIS_CUDA_ERR_NO_DEVICE = 6
+    CHELIS_CUDA_ERR_NO_DEVICE = 6,
+    CHELIS_CUDA_ERR_FAIL = 7         /* a program's own abort fired (GuardedFail): its message */
 };
 
 /* GEMM arithmetic for f32 (matmul lowering, spec/05-risc-primitives.md:4962-5000). */
@@ -108,8 +109,12 @@ int chelis_cuda_set_stream(void *cuda_stream);
 void *chelis_cuda_get_stream(void);
 int chelis_cuda_synchronize(void);
 /* Read-and-clear the device error word: CHELIS_CUDA_ERR_TIMEOUT if a bounded
- * device wait gave up, CHELIS_CUDA_ERR_DOMAIN if an index operand was out of
- * range ([05-OP-52]), since the last call.
+ * device wait gave up; CHELIS_CUDA_ERR_FAIL with the message of a DAG's
+ * GuardedFail that fired; CHELIS_CUDA_ERR_DOMAIN / _OVERFLOW for a numeric
+ * trap raised on the device (an index operand out of range ([05-OP-52]), a
+ * dropout rate outside [0, 1), integer overflow or division by zero, a
+ * checked cast), with the reference's "numeric trap: <kind> in <op> at
+ * <dtype>" message; since the last call.
  * Synchronises the stream.  Replaces the debug failure flag readback of
  * chelis_hip_runtime.h:487-524. */
 int chelis_cuda_device_status(void);

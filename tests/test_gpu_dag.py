@@ -834,3 +834,28 @@ def test_negative_shift_count_is_reported(cuda):
     finally:
         L.load().chelis_dag_release(h)
     L.call("chelis_cuda_device_status")
+
+
+# ---- GuardedFail ([05-OP-68]; the C lane's emit_guarded_fail)
+
+@pytest.mark.parametrize("trap_on_true", [True, False])
+def test_guarded_fail(cuda, trap_on_true):
+    """The result is the fallback; where the condition fires the program
+    aborts with its own message (CHELIS_CUDA_ERR_FAIL)."""
+    fb = np.arange(6, dtype=np.float32)
+    quiet = np.full(4, not trap_on_true)
+    loud = quiet.copy()
+    loud[2] = trap_on_true
+    g = D.Dag()
+    c, x = g.load("c", [4], "bool"), g.load("x", [6])
+    g.roots = [g.add({"GuardedFail": {"message": "withdrawal exceeds the balance", "trap_on_true": trap_on_true}},
+                     [c, x], [6])]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(quiet).cuda(), torch.from_numpy(fb).cuda()])
+        assert np.array_equal(got, fb)
+        with pytest.raises(L.ChelisCudaError, match="withdrawal exceeds the balance") as e:
+            run(h, [torch.from_numpy(loud).cuda(), torch.from_numpy(fb).cuda()])
+        assert e.value.status == 7
+    finally:
+        L.load().chelis_dag_release(h)
