@@ -45,6 +45,7 @@
 //   Dropout, DropoutReplay
 //                         keyed draw per key row ([05-OP-37]), the C lane's
 //                         word / unit and rate rule
+//   UniformLike           keyed affine sampler per key row ([05-OP-8])
 //   Add, Sub, Mul, TruncDiv, FloorDiv, Mod, MaxElem, MinElem, Neg, Abs on
 //   integers (and float Mod)
 //                         exact at the stored width; overflow / division by
@@ -81,7 +82,7 @@ enum class Op {
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
     FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
-    GuardedFail
+    GuardedFail, UniformLike
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -579,6 +580,10 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (!cc || !as_index(cc, &v)) return unsupported("SplitN with a runtime count");
         n.axis = static_cast<int>(v);
         CHELIS_TRY(need_inputs(1));
+    } else if (name == "UniformLike") {
+        // [05-OP-8] under an explicit key: inputs [template, low, high, key]
+        n.op = Op::UniformLike;
+        CHELIS_TRY(need_inputs(4));
     } else if (name == "Dropout" || name == "DropoutReplay") {
         // [05-OP-37] under an explicit key; the replay applies the same draw to the cotangent
         n.op = Op::Dropout;
@@ -814,6 +819,25 @@ int check_and_layout(Program &P) {
                     if (want != n.shape) return bad("SplitN result shape");
                 } else {
                     CHELIS_TRY(check_same_shape(n, src(0), n.opname.c_str()));
+                }
+                own();
+                break;
+            }
+            case Op::UniformLike: {
+                if (n.activation >= 0) return unsupported("UniformLike under an activation");
+                if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+                    return unsupported("UniformLike precision");
+                for (int k = 0; k < 3; ++k)
+                    if (src(k).dtype != n.dtype) return bad("UniformLike operand dtype");
+                if (src(3).dtype != CHELIS_DTYPE_KEY) return bad("UniformLike key must be a key");
+                CHELIS_TRY(check_same_shape(n, src(0), "UniformLike"));
+                const auto &ks = src(3).shape;
+                if (ks.size() > n.shape.size() || !std::equal(ks.begin(), ks.end(), n.shape.begin()))
+                    return bad("UniformLike key shape");
+                for (int k = 1; k < 3; ++k) {
+                    const auto &bs = src(k).shape;
+                    if (bs.size() > ks.size() || !std::equal(bs.begin(), bs.end(), ks.begin()))
+                        return bad("UniformLike bound shape");
                 }
                 own();
                 break;
@@ -1769,6 +1793,34 @@ __global__ void arith_kernel(const T *__restrict__ a, Strided sa, const T *__res
     }
 }
 
+// [05-OP-8] uniform_like under an explicit key, as the C lane samples it:
+// rows as for keyed dropout; element e of row b is fma(high - low, u, low)
+// with u the unit value of word(key[b], e) and the span, u and the fma at the
+// result's precision (f32: u rounded to f32, span in f32, fmaf).  A row whose
+// bounds are non-finite, reversed or give a non-finite span traps Domain.
+template <typename T>
+__global__ void keyed_uniform_kernel(const T *__restrict__ lo, Strided sl, int64_t lo_size,
+                                     const T *__restrict__ hi, Strided sh, int64_t hi_size,
+                                     const uint64_t *__restrict__ keys, Strided sk, int64_t rows, int64_t row_len,
+                                     T *__restrict__ out, int64_t n, unsigned int dt) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / row_len, e = i - b * row_len;
+        const T l = lo[offset_of(sl, lo_size <= 1 ? 0 : b / (rows / lo_size))];
+        const T h = hi[offset_of(sh, hi_size <= 1 ? 0 : b / (rows / hi_size))];
+        const T span = h - l;
+        if (!(isfinite(l) && isfinite(h) && l <= h && isfinite(span))) {
+            report_trap(TRAP_DOMAIN, TRAP_OP_UNIFORM_LIKE, dt);
+            out[i] = T(0);
+            continue;
+        }
+        const uint64_t w = rng_word(keys[offset_of(sk, b)], static_cast<uint64_t>(e));
+        const double u = static_cast<double>(w >> 11) * 0x1p-53;
+        if constexpr (sizeof(T) == 4) out[i] = __fmaf_rn(span, __double2float_rn(u), l);
+        else out[i] = __fma_rn(span, u, l);
+    }
+}
+
 unsigned grid_for(int64_t n) {
     int64_t b = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -2367,6 +2419,28 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                                                      arg, reinterpret_cast<uint64_t *>(out), cnt);
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::key_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::UniformLike: {
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const Value &l = in(1), &h = in(2), &k = in(3);
+            const int64_t rows = count_of(k.shape);
+            const int64_t row_len = rows > 0 ? cnt / rows : 0;
+            const unsigned int dt = static_cast<unsigned int>(n.dtype);
+            if (n.dtype == CHELIS_DTYPE_F64)
+                keyed_uniform_kernel<double><<<grid_for(cnt), 256, 0, s>>>(
+                    reinterpret_cast<const double *>(l.ptr), strided(l), count_of(l.shape),
+                    reinterpret_cast<const double *>(h.ptr), strided(h), count_of(h.shape),
+                    reinterpret_cast<const uint64_t *>(k.ptr), strided(k), rows, row_len,
+                    reinterpret_cast<double *>(out), cnt, dt);
+            else
+                keyed_uniform_kernel<float><<<grid_for(cnt), 256, 0, s>>>(
+                    reinterpret_cast<const float *>(l.ptr), strided(l), count_of(l.shape),
+                    reinterpret_cast<const float *>(h.ptr), strided(h), count_of(h.shape),
+                    reinterpret_cast<const uint64_t *>(k.ptr), strided(k), rows, row_len,
+                    reinterpret_cast<float *>(out), cnt, dt);
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::keyed_uniform_kernel");
             return CHELIS_CUDA_OK;
         }
         case Op::Dropout: {

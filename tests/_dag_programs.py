@@ -152,6 +152,9 @@ class Dag:
         """NamedCast {mode: Trunc | Saturate | Wrap} to a signed integer."""
         return self.add({"NamedCast": {"mode": mode, "new_precision": PRIM[prec]}}, [x], self.dims(x), prec)
 
+    def uniform_like(self, template, low, high, key):
+        return self.add("UniformLike", [template, low, high, key], self.dims(template), self.prec(template))
+
     def compare(self, kind, a, b):
         """Compare(ComparisonKind): kind one of CmpLt, Lt, Eq, Neq, Gt, Gte, Lte."""
         return self.add({"Compare": kind}, [a, b], self.dims(a), "bool")

@@ -859,3 +859,57 @@ def test_guarded_fail(cuda, trap_on_true):
         assert e.value.status == 7
     finally:
         L.load().chelis_dag_release(h)
+
+
+# ---- UniformLike ([05-OP-8]; the C lane's emit_explicitly_keyed_uniform_like)
+
+def _round_f32(x):
+    """The float32 nearest to the exact rational x (ties to even)."""
+    from fractions import Fraction
+    f = np.float32(float(x))
+    cands = [np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))]
+    best = min(cands, key=lambda c: (abs(Fraction(float(c)) - x), int(np.array(c).view(np.uint32)) & 1))
+    return best
+
+
+def test_uniform_like_f32_and_f64_match_the_sampler(cuda, orc):
+    from fractions import Fraction
+    g = D.Dag()
+    t32, t64 = g.load("t32", [4, 50]), g.load("t64", [4, 50], "f64")
+    k = g.key_from_seed(g.load("seed", [4], "i64"))
+    lo32, hi32 = g.load("lo", [4]), g.load("hi", [4])
+    g.roots = [g.uniform_like(t32, lo32, hi32, k),
+               g.uniform_like(t64, g.const(-1.5, prec="f64"), g.const(2.25, prec="f64"), g.split_key(k, "Left"))]
+    seeds = np.array([3, 9, -4, 100], np.int64)
+    lows = np.array([0.0, -2.0, 5.0, 1e-3], np.float32)
+    highs = np.array([1.0, 3.0, 5.0, 7.5], np.float32)
+    h = program(g)
+    try:
+        got = run(h, [torch.zeros(4, 50).cuda(), torch.zeros(4, 50, dtype=torch.float64).cuda(),
+                      torch.from_numpy(seeds).cuda(), torch.from_numpy(lows).cuda(), torch.from_numpy(highs).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    for b in range(4):
+        key = int(seeds[b]) & (2 ** 64 - 1)
+        span = np.float32(highs[b] - lows[b])
+        for e in range(50):
+            u = np.float32(orc.unit(key, e))
+            want = _round_f32(Fraction(float(span)) * Fraction(float(u)) + Fraction(float(lows[b])))
+            assert got[0][b, e].view(np.uint32) == np.float32(want).view(np.uint32), (b, e)
+            k2 = orc.derive(key, 0)
+            w64 = float(Fraction(3.75) * Fraction(orc.unit(k2, e)) + Fraction(-1.5))
+            assert got[1][b, e] == w64, (b, e)
+
+
+def test_uniform_like_bad_bounds_trap(cuda):
+    g = D.Dag()
+    t = g.load("t", [8])
+    k = g.key_from_seed(g.load("seed", [], "i64"))
+    g.roots = [g.uniform_like(t, g.const(2.0), g.const(1.0), k)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: domain in uniform_like at f32"):
+            run(h, [torch.zeros(8).cuda(), torch.tensor(5, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")
