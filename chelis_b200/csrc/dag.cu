@@ -46,6 +46,7 @@
 //                         keyed draw per key row ([05-OP-37]), the C lane's
 //                         word / unit and rate rule
 //   UniformLike           keyed affine sampler per key row ([05-OP-8])
+//   Iota                  start + i over the declared extent, length checked
 //   Add, Sub, Mul, TruncDiv, FloorDiv, Mod, MaxElem, MinElem, Neg, Abs on
 //   integers (and float Mod)
 //                         exact at the stored width; overflow / division by
@@ -82,7 +83,7 @@ enum class Op {
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
     FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
-    GuardedFail, UniformLike
+    GuardedFail, UniformLike, Iota
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -580,6 +581,10 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (!cc || !as_index(cc, &v)) return unsupported("SplitN with a runtime count");
         n.axis = static_cast<int>(v);
         CHELIS_TRY(need_inputs(1));
+    } else if (name == "Iota") {
+        // [05-OP-54] range(start, end) as a rank-one i64 tensor
+        n.op = Op::Iota;
+        CHELIS_TRY(need_inputs(2));
     } else if (name == "UniformLike") {
         // [05-OP-8] under an explicit key: inputs [template, low, high, key]
         n.op = Op::UniformLike;
@@ -823,6 +828,14 @@ int check_and_layout(Program &P) {
                 own();
                 break;
             }
+            case Op::Iota:
+                if (n.activation >= 0) return unsupported("Iota under an activation");
+                for (int k = 0; k < 2; ++k)
+                    if (src(k).dtype != CHELIS_DTYPE_I64 || !src(k).shape.empty())
+                        return bad("Iota bounds must be i64 scalars");
+                if (n.dtype != CHELIS_DTYPE_I64 || n.shape.size() != 1) return bad("Iota result must be i64[n]");
+                own();
+                break;
             case Op::UniformLike: {
                 if (n.activation >= 0) return unsupported("UniformLike under an activation");
                 if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
@@ -1821,6 +1834,29 @@ __global__ void keyed_uniform_kernel(const T *__restrict__ lo, Strided sl, int64
     }
 }
 
+// [05-OP-54] range(start, end) into a declared extent `len`: the count is
+// max(end - start, 0), an overflowing difference traps Overflow and a count
+// other than the declared extent Domain (op "range"); element i is start + i.
+__global__ void iota_kernel(const int64_t *__restrict__ start, const int64_t *__restrict__ end, int64_t len,
+                            int64_t *__restrict__ out) {
+    const int64_t s = *start, e = *end;
+    bool ok = true;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const int64_t d = static_cast<int64_t>(static_cast<uint64_t>(e) - static_cast<uint64_t>(s));
+        if (e > s && d < 0) {
+            report_trap(TRAP_OVERFLOW, TRAP_OP_RANGE, CHELIS_DTYPE_I64);
+            ok = false;
+        } else if ((e <= s ? 0 : d) != len) {
+            report_trap(TRAP_DOMAIN, TRAP_OP_RANGE, CHELIS_DTYPE_I64);
+            ok = false;
+        }
+    }
+    (void)ok;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < len;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = static_cast<int64_t>(static_cast<uint64_t>(s) + static_cast<uint64_t>(i));
+}
+
 unsigned grid_for(int64_t n) {
     int64_t b = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -2419,6 +2455,14 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                                                      arg, reinterpret_cast<uint64_t *>(out), cnt);
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::key_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::Iota: {
+            iota_kernel<<<grid_for(cnt > 0 ? cnt : 1), 256, 0, s>>>(reinterpret_cast<const int64_t *>(in(0).ptr),
+                                                                    reinterpret_cast<const int64_t *>(in(1).ptr), cnt,
+                                                                    reinterpret_cast<int64_t *>(out));
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::iota_kernel");
             return CHELIS_CUDA_OK;
         }
         case Op::UniformLike: {

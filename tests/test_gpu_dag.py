@@ -913,3 +913,63 @@ def test_uniform_like_bad_bounds_trap(cuda):
     finally:
         L.load().chelis_dag_release(h)
     L.call("chelis_cuda_device_status")
+
+
+# ---- Iota ([05-OP-54]; the C lane's emit_iota)
+
+def _iota(g, start, end, n):
+    return g.add("Iota", [start, end], [n], "i64")
+
+
+@pytest.mark.parametrize("start,end,n", [(-3, 5, 8), (5, 2, 0), (0, 1, 1), (2 ** 62, 2 ** 62 + 4, 4)])
+def test_iota_values(cuda, start, end, n):
+    g = D.Dag()
+    a, b = g.load("start", [], "i64"), g.load("end", [], "i64")
+    g.roots = [_iota(g, a, b, n)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.tensor(start, dtype=torch.int64).cuda(), torch.tensor(end, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert [int(v) for v in got] == list(range(start, end))
+
+
+@pytest.mark.parametrize("start,end,n,message", [
+    (0, 4, 5, "domain in range at i64"),
+    (-(2 ** 63), 2 ** 63 - 1, 3, "overflow in range at i64"),
+])
+def test_iota_traps(cuda, start, end, n, message):
+    g = D.Dag()
+    a, b = g.load("start", [], "i64"), g.load("end", [], "i64")
+    g.roots = [_iota(g, a, b, n)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: " + message):
+            run(h, [torch.tensor(start, dtype=torch.int64).cuda(), torch.tensor(end, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")
+
+
+def test_iota_causal_mask_program(cuda):
+    """The causal mask from iota: keep[i, j] = j <= i, then where(keep, s, -inf)
+    and Softmax, against numpy."""
+    n = 48
+    s = np.random.default_rng(50).standard_normal((n, n)).astype(np.float32)
+    g = D.Dag()
+    x = g.load("s", [n, n])
+    zero, size = g.load("zero", [], "i64"), g.load("n", [], "i64")
+    ix = _iota(g, zero, size, n)
+    rows, cols = g.expand(ix, 1, n), g.expand(ix, 0, n)
+    keep = g.logical("Not", g.compare("Gt", cols, rows))
+    ninf = g.expand(g.expand(g.const(float("-inf")), 0, n), 1, n)
+    g.roots = [g.add({"Softmax": {"axis": 1}}, [g.where(keep, x, ninf)], [n, n])]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(s).cuda(), torch.tensor(0, dtype=torch.int64).cuda(),
+                         torch.tensor(n, dtype=torch.int64).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    m = np.where(np.arange(n)[None, :] <= np.arange(n)[:, None], s.astype(np.float64), -np.inf)
+    e = np.exp(m - m.max(axis=1, keepdims=True))
+    assert rel(got, e / e.sum(axis=1, keepdims=True)) <= 1e-6
