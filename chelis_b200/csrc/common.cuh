@@ -74,7 +74,7 @@ enum : unsigned int { TRAP_OVERFLOW = 0u, TRAP_DOMAIN = 1u, TRAP_DIVZERO = 2u };
 enum : unsigned int {
     TRAP_OP_ADD = 0u, TRAP_OP_SUB, TRAP_OP_MUL, TRAP_OP_TRUNC_DIV, TRAP_OP_FLOOR_DIV, TRAP_OP_MOD,
     TRAP_OP_NEG, TRAP_OP_ABS, TRAP_OP_CAST, TRAP_OP_CAST_TRUNC, TRAP_OP_CAST_SATURATE, TRAP_OP_UNIFORM_LIKE,
-    TRAP_OP_RANGE
+    TRAP_OP_RANGE, TRAP_OP_REDUCE_WINDOW_SUM
 };
 
 __device__ __forceinline__ void report_device_error(unsigned int code) {

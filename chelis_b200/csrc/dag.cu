@@ -47,6 +47,9 @@
 //                         word / unit and rate rule
 //   UniformLike           keyed affine sampler per key row ([05-OP-8])
 //   Iota                  start + i over the declared extent, length checked
+//   ReduceWindow, ReduceWindowGrad
+//                         thread per output (forward) / per input position
+//                         (adjoint), canonical trees in window order
 //   Add, Sub, Mul, TruncDiv, FloorDiv, Mod, MaxElem, MinElem, Neg, Abs on
 //   integers (and float Mod)
 //                         exact at the stored width; overflow / division by
@@ -62,6 +65,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <limits>
 #include <memory>
 #include <string>
 #include <type_traits>
@@ -83,7 +87,7 @@ enum class Op {
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
     FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
-    GuardedFail, UniformLike, Iota
+    GuardedFail, UniformLike, Iota, ReduceWindow, ReduceWindowGrad
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -93,6 +97,8 @@ enum { LOG_AND = 0, LOG_OR, LOG_NOT };
 // (Max = 0, Min = 1) and operand (Left = 0, Right = 1) in Node::kind / Node::axis
 enum { FC_NAN = 0, FC_FINITE, FC_INFINITE };
 // exact integer element-wise operations (and float Mod) in Node::kind
+// ReduceWindowKind (dag.rs:587-592 order)
+enum { RW_MAX = 0, RW_MIN, RW_SUM, RW_MEAN };
 // NamedCast modes (NamedCastMode order)
 enum { NC_TRUNC = 0, NC_SATURATE, NC_WRAP };
 enum { IA_ADD = 0, IA_SUB, IA_MUL, IA_TRUNC_DIV, IA_FLOOR_DIV, IA_MOD, IA_MAX, IA_MIN, IA_NEG, IA_ABS,
@@ -118,6 +124,7 @@ struct Node {
     int activation = -1;                               // owner.activation node, if any
     std::string message;                               // GuardedFail
     uint32_t fail_id = 0;                              // its registered message id
+    std::vector<int64_t> window, wstride;             // ReduceWindow(Grad)
 };
 
 // Static layout of a node's value: elements at root storage + offset +
@@ -581,6 +588,27 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (!cc || !as_index(cc, &v)) return unsupported("SplitN with a runtime count");
         n.axis = static_cast<int>(v);
         CHELIS_TRY(need_inputs(1));
+    } else if (name == "ReduceWindow" || name == "ReduceWindowGrad") {
+        // [05-OP-39] windowed reductions over the trailing axes (spec 05 2.3.1)
+        static const char *kinds[] = {"Max", "Min", "Sum", "Mean"};
+        n.op = name == "ReduceWindow" ? Op::ReduceWindow : Op::ReduceWindowGrad;
+        const json::Value *r = field("reducer"), *w = field("window_shape"), *st = field("strides");
+        n.kind = -1;
+        if (r && r->kind == json::Value::Str)
+            for (int i = 0; i < 4; ++i)
+                if (r->s == kinds[i]) n.kind = i;
+        if (n.kind < 0) return bad("ReduceWindow reducer");
+        if (!w || w->kind != json::Value::Arr || !st || st->kind != json::Value::Arr || w->a.empty() ||
+            w->a.size() != st->a.size())
+            return bad("ReduceWindow window_shape / strides ([05-RWIN-1])");
+        for (size_t k = 0; k < w->a.size(); ++k) {
+            int64_t a = 0, b = 0;
+            if (!as_index(&w->a[k], &a) || !as_index(&st->a[k], &b) || a < 1 || b < 1)
+                return bad("ReduceWindow window_shape / strides ([05-RWIN-1])");
+            n.window.push_back(a);
+            n.wstride.push_back(b);
+        }
+        CHELIS_TRY(need_inputs(n.op == Op::ReduceWindow ? 1 : 2));
     } else if (name == "Iota") {
         // [05-OP-54] range(start, end) as a rank-one i64 tensor
         n.op = Op::Iota;
@@ -824,6 +852,29 @@ int check_and_layout(Program &P) {
                     if (want != n.shape) return bad("SplitN result shape");
                 } else {
                     CHELIS_TRY(check_same_shape(n, src(0), n.opname.c_str()));
+                }
+                own();
+                break;
+            }
+            case Op::ReduceWindow: case Op::ReduceWindowGrad: {
+                const Node &x = src(0);
+                const size_t r = x.shape.size(), nw = n.window.size();
+                if (nw > r) return bad("ReduceWindow window arity above the input rank ([05-RWIN-1])");
+                if (x.dtype != n.dtype) return bad("window reductions preserve the operand dtype");
+                const bool fl = n.dtype == CHELIS_DTYPE_F32 || n.dtype == CHELIS_DTYPE_F64;
+                if (!fl && (n.op == Op::ReduceWindowGrad || n.kind == RW_MEAN || !integer_dtype(n.dtype)))
+                    return unsupported(n.opname + " precision");
+                std::vector<int64_t> outs = x.shape;
+                for (size_t k = 0; k < nw; ++k) {
+                    const int64_t d = x.shape[r - nw + k] - n.window[k];
+                    if (d < 0) return bad("ReduceWindow window larger than its axis ([05-RWIN-1])");
+                    outs[r - nw + k] = d / n.wstride[k] + 1;
+                }
+                if (n.op == Op::ReduceWindow) {
+                    if (outs != n.shape) return bad("ReduceWindow result shape");
+                } else {
+                    if (src(1).dtype != n.dtype || src(1).shape != outs) return bad("ReduceWindowGrad cotangent");
+                    CHELIS_TRY(check_same_shape(n, x, "ReduceWindowGrad"));
                 }
                 own();
                 break;
@@ -1857,6 +1908,200 @@ __global__ void iota_kernel(const int64_t *__restrict__ start, const int64_t *__
         out[i] = static_cast<int64_t>(static_cast<uint64_t>(s) + static_cast<uint64_t>(i));
 }
 
+// Window geometry: the input (rank axes, strides in elements), the output
+// extents, and the trailing `nw` windowed axes' window and stride.
+struct WinGeom {
+    int32_t rank, nw;
+    int64_t in_shape[kMaxRank], in_stride[kMaxRank], out_shape[kMaxRank];
+    int64_t win[kMaxRank], step[kMaxRank];
+    int64_t volume;
+};
+
+// The canonical adjacent-pair tree over a sequence of leaves (the C lane's
+// carry tree: completed 2^d-leaf subtrees in level[d], the partial ones
+// combined from the lowest level up at the end).
+template <typename T>
+struct LeafTree {
+    T level[24];
+    uint32_t count = 0;
+    template <typename Add>
+    __device__ void push(T v, Add add) {
+        int d = 0;
+        for (uint32_t c = count; c & 1u; c >>= 1, ++d) v = add(level[d], v);
+        level[d] = v;
+        ++count;
+    }
+    template <typename Add>
+    __device__ T total(Add add) const {
+        T tot = T(0);
+        bool found = false;
+        for (int d = 0; d < 24; ++d)
+            if ((count >> d) & 1u) {
+                tot = found ? add(level[d], tot) : level[d];
+                found = true;
+            }
+        return tot;
+    }
+};
+
+template <typename T>
+__device__ __forceinline__ T win_add(T a, T b, unsigned int dt) {
+    if constexpr (std::is_floating_point<T>::value) {
+        return a + b;
+    } else {
+        // checked at the stored width; an overflow traps in reduce_window_sum
+        bool ovf;
+        T r;
+        if constexpr (sizeof(T) == 8) {
+            const int64_t q = static_cast<int64_t>(static_cast<uint64_t>(a) + static_cast<uint64_t>(b));
+            ovf = ((a ^ q) & (b ^ q)) < 0;
+            r = static_cast<T>(q);
+        } else {
+            const int64_t q = int64_t(a) + b;
+            ovf = q < int64_t(std::numeric_limits<T>::min()) || q > int64_t(std::numeric_limits<T>::max());
+            r = static_cast<T>(q);
+        }
+        if (ovf) {
+            report_trap(TRAP_OVERFLOW, TRAP_OP_REDUCE_WINDOW_SUM, dt);
+            return T(0);
+        }
+        return r;
+    }
+}
+
+// offset of window leaf `leaf` (row-major over the window) of output `o`
+__device__ __forceinline__ int64_t win_base(const WinGeom &g, int64_t o) {
+    int64_t off = 0;
+    const int lead = g.rank - g.nw;
+    for (int d = g.rank - 1; d >= 0; --d) {
+        const int64_t c = o % g.out_shape[d];
+        o /= g.out_shape[d];
+        off += (d >= lead ? c * g.step[d - lead] : c) * g.in_stride[d];
+    }
+    return off;
+}
+__device__ __forceinline__ int64_t win_leaf(const WinGeom &g, int64_t leaf) {
+    int64_t off = 0;
+    const int lead = g.rank - g.nw;
+    for (int j = g.nw - 1; j >= 0; --j) {
+        off += (leaf % g.win[j]) * g.in_stride[lead + j];
+        leaf /= g.win[j];
+    }
+    return off;
+}
+
+// [05-OP-39] forward: max / min pick in row-major window order (first NaN,
+// else the first extreme); sum / mean combine the leaves by the canonical
+// tree at the operand width (integers checked: overflow in
+// reduce_window_sum), mean dividing the root by the window volume.
+template <typename T>
+__global__ void window_reduce_kernel(const T *__restrict__ x, WinGeom g, int kind, T *__restrict__ out,
+                                     int64_t nout, unsigned int dt) {
+    for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < nout;
+         o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const T *base = x + win_base(g, o);
+        if (kind == RW_MAX || kind == RW_MIN) {
+            T best = T(0);
+            int64_t bp = -1;
+            for (int64_t l = 0; l < g.volume; ++l) {
+                const T v = base[win_leaf(g, l)];
+                const bool better = kind == RW_MAX ? pick_better<true>(v, l, best, bp) : pick_better<false>(v, l, best, bp);
+                if (better) {
+                    best = v;
+                    bp = l;
+                }
+            }
+            out[o] = best;
+        } else {
+            LeafTree<T> t;
+            auto add = [&](T a, T b) { return win_add<T>(a, b, dt); };
+            for (int64_t l = 0; l < g.volume; ++l) t.push(base[win_leaf(g, l)], add);
+            T r = t.total(add);
+            if constexpr (std::is_floating_point<T>::value) {
+                if (kind == RW_MEAN) r = r / static_cast<T>(g.volume);
+                out[o] = r != r ? (sizeof(T) == 4 ? T(__int_as_float(0x7fc00000)) : T(__longlong_as_double(0x7ff8000000000000ll))) : r;
+            } else {
+                out[o] = r;
+            }
+        }
+    }
+}
+
+// ReduceWindowGrad: input position p folds, by the canonical tree in window
+// order, the contributions of the windows covering it: g (sum), g / volume
+// (mean); for max / min only where p is the window's first NaN (full g) or,
+// with no NaN, one of its k values equal to the extreme (g / k).
+template <typename T>
+__global__ void window_grad_kernel(const T *__restrict__ x, const T *__restrict__ gr, WinGeom g, int kind,
+                                   T *__restrict__ out, int64_t nin) {
+    const int lead = g.rank - g.nw;
+    for (int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < nin;
+         p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t c[kMaxRank], lo[kMaxRank], hi[kMaxRank], cur[kMaxRank];
+        int64_t q = p, xoff = 0;
+        for (int d = g.rank - 1; d >= 0; --d) {
+            c[d] = q % g.in_shape[d];
+            q /= g.in_shape[d];
+            xoff += c[d] * g.in_stride[d];
+        }
+        bool any = true;
+        for (int j = 0; j < g.nw; ++j) {
+            const int64_t i = c[lead + j], w = g.win[j], s = g.step[j];
+            const int64_t a = i - w + 1;
+            lo[j] = a <= 0 ? 0 : (a + s - 1) / s;
+            hi[j] = i / s;
+            if (hi[j] > g.out_shape[lead + j] - 1) hi[j] = g.out_shape[lead + j] - 1;
+            if (lo[j] > hi[j]) any = false;
+            cur[j] = lo[j];
+        }
+        LeafTree<T> t;
+        auto add = [](T a, T b) { return a + b; };
+        const T xp = x[xoff];
+        while (any) {
+            // output index of window `cur` (leading coordinates those of p)
+            int64_t o = 0;
+            for (int d = 0; d < g.rank; ++d) o = o * g.out_shape[d] + (d < lead ? c[d] : cur[d - lead]);
+            T contribution = gr[o];
+            bool push = true;
+            if (kind == RW_MEAN) {
+                contribution = contribution / static_cast<T>(g.volume);
+            } else if (kind == RW_MAX || kind == RW_MIN) {
+                const T *base = x + win_base(g, o);
+                T best = T(0);
+                int64_t bp = -1;
+                for (int64_t l = 0; l < g.volume; ++l) {
+                    const T v = base[win_leaf(g, l)];
+                    const bool better = kind == RW_MAX ? pick_better<true>(v, l, best, bp) : pick_better<false>(v, l, best, bp);
+                    if (better) {
+                        best = v;
+                        bp = l;
+                    }
+                }
+                if (best != best) {
+                    push = base + win_leaf(g, bp) == x + xoff;
+                } else if (!(xp == best)) {
+                    push = false;
+                } else {
+                    int64_t ties = 0;
+                    for (int64_t l = 0; l < g.volume; ++l) ties += base[win_leaf(g, l)] == best ? 1 : 0;
+                    contribution = contribution / static_cast<T>(ties);
+                }
+            }
+            if (push) t.push(contribution, add);
+            // next covering window, row-major
+            int j = g.nw - 1;
+            while (j >= 0 && cur[j] == hi[j]) {
+                cur[j] = lo[j];
+                --j;
+            }
+            if (j < 0) break;
+            ++cur[j];
+        }
+        const T r = t.total(add);
+        out[p] = r != r ? (sizeof(T) == 4 ? T(__int_as_float(0x7fc00000)) : T(__longlong_as_double(0x7ff8000000000000ll))) : r;
+    }
+}
+
 unsigned grid_for(int64_t n) {
     int64_t b = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -2455,6 +2700,52 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                                                      arg, reinterpret_cast<uint64_t *>(out), cnt);
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::key_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::ReduceWindow: case Op::ReduceWindowGrad: {
+            const Value &x = in(0);
+            WinGeom g{};
+            g.rank = static_cast<int32_t>(x.shape.size());
+            g.nw = static_cast<int32_t>(n.window.size());
+            g.volume = 1;
+            const int lead = g.rank - g.nw;
+            for (int d = 0; d < g.rank; ++d) {
+                g.in_shape[d] = x.shape[d];
+                g.in_stride[d] = x.strides[d];
+                g.out_shape[d] = d < lead ? x.shape[d] : (x.shape[d] - n.window[d - lead]) / n.wstride[d - lead] + 1;
+            }
+            for (int j = 0; j < g.nw; ++j) {
+                g.win[j] = n.window[j];
+                g.step[j] = n.wstride[j];
+                g.volume *= n.window[j];
+            }
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            const unsigned int dt = static_cast<unsigned int>(n.dtype);
+            if (n.op == Op::ReduceWindowGrad) {
+                Value gv = in(1);
+                CHELIS_TRY(dense(gv));
+                if (n.dtype == CHELIS_DTYPE_F64)
+                    window_grad_kernel<double><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const double *>(x.ptr),
+                        reinterpret_cast<const double *>(gv.ptr), g, n.kind, reinterpret_cast<double *>(out), cnt);
+                else
+                    window_grad_kernel<float><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const float *>(x.ptr),
+                        reinterpret_cast<const float *>(gv.ptr), g, n.kind, reinterpret_cast<float *>(out), cnt);
+            } else {
+#define CHELIS_DAG_WIN(T)                                                                                 \
+    window_reduce_kernel<T><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const T *>(x.ptr), g, n.kind,   \
+                                                          reinterpret_cast<T *>(out), cnt, dt)
+                switch (n.dtype) {
+                    case CHELIS_DTYPE_F64: CHELIS_DAG_WIN(double); break;
+                    case CHELIS_DTYPE_I64: CHELIS_DAG_WIN(int64_t); break;
+                    case CHELIS_DTYPE_I32: CHELIS_DAG_WIN(int32_t); break;
+                    case CHELIS_DTYPE_I16: CHELIS_DAG_WIN(int16_t); break;
+                    case CHELIS_DTYPE_I8: CHELIS_DAG_WIN(int8_t); break;
+                    default: CHELIS_DAG_WIN(float); break;
+                }
+#undef CHELIS_DAG_WIN
+            }
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::window_kernel");
             return CHELIS_CUDA_OK;
         }
         case Op::Iota: {

@@ -364,12 +364,13 @@ int chelis_cuda_device_status(void) {
         static const char *const kinds[] = {"overflow", "domain", "division by zero"};
         static const char *const ops[] = {"add", "sub", "mul", "trunc_div", "floor_div", "mod", "neg", "abs", "cast",
                                           "cast_trunc", "cast_saturate",
-                                          "uniform_like", "range"};
+                                          "uniform_like", "range",
+                                          "reduce_window_sum"};
         static const char *const dtypes[] = {"f32", "f64", "i32", "bool", "i64", "bf16", "f16", "i8", "i16", "key"};
         const unsigned int c = code ? code - 1 : 0, k = c >> 16, o = (c >> 8) & 0xff, d = c & 0xff;
         return set_error(k == 0 ? CHELIS_CUDA_ERR_OVERFLOW : CHELIS_CUDA_ERR_DOMAIN,
                          "numeric trap: %s in %s at %s", k < 3 ? kinds[k] : "?",
-                         o < 13 ? ops[o] : "?", d < 10 ? dtypes[d] : "?");
+                         o < 14 ? ops[o] : "?", d < 10 ? dtypes[d] : "?");
     }
     return CHELIS_CUDA_OK;
 }

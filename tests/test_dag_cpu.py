@@ -95,8 +95,8 @@ def test_mlp_program_plans():
 @pytest.mark.parametrize("text,status,needle", [
     ('{"nodes": [', 1, "malformed JSON"),
     ('{"nodes": [], "roots": [3]}', 1, "root"),
-    ('{"nodes":[{"id":0,"op":"Iota","inputs":[],"output_type":{"dims":[{"Lit":4}],'
-     '"precision":"Int64"},"owner":{"decl":0,"activation":null}}],"roots":[0]}', 4, "Iota"),
+    ('{"nodes":[{"id":0,"op":"KeySelect","inputs":[],"output_type":{"dims":[{"Lit":4}],'
+     '"precision":"Key"},"owner":{"decl":0,"activation":null}}],"roots":[0]}', 4, "KeySelect"),
     ('{"nodes":[{"id":0,"op":{"Load":{"name":"x"}},"inputs":[],"output_type":{"dims":'
      '[{"Named":["n",null]}],"precision":"F32"},"owner":{"decl":0,"activation":null}}],'
      '"roots":[0]}', 4, "symbolic"),
@@ -202,6 +202,22 @@ def test_named_cast_rejections(mode, src, message):
     g = D.Dag()
     a = g.load("a", [4], src)
     g.roots = [g.named_cast(a, mode, "i32")]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()
+
+
+@pytest.mark.parametrize("body,dims,message", [
+    ({"reducer": "Max", "window_shape": [2], "strides": [2, 1]}, [3], "window_shape / strides"),
+    ({"reducer": "Max", "window_shape": [0], "strides": [1]}, [3], "window_shape / strides"),
+    ({"reducer": "Median", "window_shape": [2], "strides": [1]}, [5], "ReduceWindow reducer"),
+    ({"reducer": "Sum", "window_shape": [7], "strides": [1]}, [1], "window larger than its axis"),
+    ({"reducer": "Sum", "window_shape": [2], "strides": [2]}, [4], "ReduceWindow result shape"),
+])
+def test_reduce_window_rejections(body, dims, message):
+    g = D.Dag()
+    a = g.load("a", [6])
+    g.roots = [g.add({"ReduceWindow": body}, [a], dims)]
     st, h = load(g.json())
     assert st != 0
     assert message in L.last_error()

@@ -973,3 +973,114 @@ def test_iota_causal_mask_program(cuda):
     m = np.where(np.arange(n)[None, :] <= np.arange(n)[:, None], s.astype(np.float64), -np.inf)
     e = np.exp(m - m.max(axis=1, keepdims=True))
     assert rel(got, e / e.sum(axis=1, keepdims=True)) <= 1e-6
+
+
+# ---- ReduceWindow / ReduceWindowGrad ([05-OP-39], spec/05-risc-primitives.md 2.3.1)
+
+def _rw(g, op, x, kind, win, steps, out_dims=None, gr=None):
+    body = {"reducer": kind, "window_shape": list(win), "strides": list(steps)}
+    if op == "ReduceWindow":
+        return g.add({"ReduceWindow": body}, [x], out_dims, g.prec(x))
+    return g.add({"ReduceWindowGrad": body}, [x, gr], g.dims(x), g.prec(x))
+
+
+def _windows(shape, win, steps):
+    """For each output index (row-major), its window's leaf positions (row-major)."""
+    r, nw = len(shape), len(win)
+    lead = shape[:r - nw]
+    outs = [(shape[r - nw + k] - win[k]) // steps[k] + 1 for k in range(nw)]
+    res = []
+    for oc in np.ndindex(*(list(lead) + outs)):
+        leaves = []
+        for lc in np.ndindex(*win):
+            leaves.append(tuple(oc[:r - nw]) + tuple(oc[r - nw + k] * steps[k] + lc[k] for k in range(nw)))
+        res.append(leaves)
+    return list(lead) + outs, res
+
+
+def _pick(vals, take_max):
+    best, bi = None, -1
+    for i, v in enumerate(vals):
+        if bi < 0:
+            best, bi = v, i
+            continue
+        if not np.isnan(best) and (np.isnan(v) or (v > best if take_max else v < best)):
+            best, bi = v, i
+    return best, bi
+
+
+@pytest.mark.parametrize("kind", ["Sum", "Mean", "Max", "Min"])
+def test_reduce_window_and_grad_match_the_c_lane(cuda, orc, kind):
+    shape, win, steps = (2, 3, 9, 8), (3, 2), (2, 2)
+    rng = np.random.default_rng(60)
+    x = rng.standard_normal(shape).astype(np.float32)
+    x[0, 0, :3, :2] = 1.5            # ties inside one window
+    x[1, 2, 4, 4] = np.nan           # a NaN window
+    out_dims, wins = _windows(shape, win, steps)
+    gr = rng.standard_normal(out_dims).astype(np.float32)
+    g = D.Dag()
+    a, b = g.load("x", list(shape)), g.load("g", out_dims)
+    g.roots = [_rw(g, "ReduceWindow", a, kind, win, steps, out_dims), _rw(g, "ReduceWindowGrad", a, kind, win, steps, gr=b)]
+    h = program(g)
+    try:
+        fwd, din = run(h, [torch.from_numpy(x).cuda(), torch.from_numpy(gr).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    vol = win[0] * win[1]
+    want = np.empty(len(wins), np.float32)
+    contrib = {}
+    for o, leaves in enumerate(wins):
+        vals = np.array([x[p] for p in leaves], np.float32)
+        gv = gr.reshape(-1)[o]
+        if kind in ("Sum", "Mean"):
+            t = np.float32(orc.tree_sum(vals))
+            want[o] = t if kind == "Sum" else np.float32(t / np.float32(vol))
+            c = gv if kind == "Sum" else np.float32(gv / np.float32(vol))
+            for p in leaves:
+                contrib.setdefault(p, []).append(c)
+        else:
+            best, bi = _pick(vals, kind == "Max")
+            want[o] = best
+            if np.isnan(best):
+                contrib.setdefault(leaves[bi], []).append(gv)
+            else:
+                ties = int((vals == best).sum())
+                for p, v in zip(leaves, vals):
+                    if v == best:
+                        contrib.setdefault(p, []).append(np.float32(gv / np.float32(ties)))
+    want = want.reshape(out_dims)
+    with np.errstate(invalid="ignore"):
+        assert np.array_equal(fwd.view(np.uint32), want.view(np.uint32)) or \
+            (kind in ("Sum", "Mean") and np.array_equal(np.isnan(fwd), np.isnan(want)) and
+             np.array_equal(np.nan_to_num(fwd), np.nan_to_num(want)))
+    dwant = np.zeros(shape, np.float32)
+    for p, cs in contrib.items():
+        dwant[p] = np.float32(orc.tree_sum(np.array(cs, np.float32)))
+    assert np.array_equal(din.view(np.uint32), dwant.view(np.uint32)) or \
+        (np.array_equal(np.isnan(din), np.isnan(dwant)) and np.array_equal(np.nan_to_num(din), np.nan_to_num(dwant)))
+
+
+def test_reduce_window_integer_sum_and_overflow(cuda):
+    x = np.arange(40, dtype=np.int32).reshape(5, 8)
+    g = D.Dag()
+    a = g.load("x", [5, 8], "i32")
+    g.roots = [_rw(g, "ReduceWindow", a, "Sum", (2, 3), (1, 2), [4, 3]), _rw(g, "ReduceWindow", a, "Max", (5,), (3,), [5, 2])]
+    h = program(g)
+    try:
+        sums, mx = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    want = np.array([[x[i:i + 2, j * 2:j * 2 + 3].sum() for j in range(3)] for i in range(4)])
+    assert np.array_equal(sums, want)
+    assert np.array_equal(mx, np.array([[x[i, j * 3:j * 3 + 5].max() for j in range(2)] for i in range(5)]))
+    big = np.full((1, 4), 2 ** 30, np.int32)
+    g = D.Dag()
+    a = g.load("x", [1, 4], "i32")
+    g.roots = [_rw(g, "ReduceWindow", a, "Sum", (4,), (1,), [1, 1])]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match="numeric trap: overflow in reduce_window_sum at i32"):
+            run(h, [torch.from_numpy(big).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    L.call("chelis_cuda_device_status")
