@@ -74,14 +74,29 @@ enum : unsigned int { TRAP_OVERFLOW = 0u, TRAP_DOMAIN = 1u, TRAP_DIVZERO = 2u };
 enum : unsigned int {
     TRAP_OP_ADD = 0u, TRAP_OP_SUB, TRAP_OP_MUL, TRAP_OP_TRUNC_DIV, TRAP_OP_FLOOR_DIV, TRAP_OP_MOD,
     TRAP_OP_NEG, TRAP_OP_ABS, TRAP_OP_CAST, TRAP_OP_CAST_TRUNC, TRAP_OP_CAST_SATURATE, TRAP_OP_UNIFORM_LIKE,
-    TRAP_OP_RANGE, TRAP_OP_REDUCE_WINDOW_SUM
+    TRAP_OP_RANGE, TRAP_OP_REDUCE_WINDOW_SUM, TRAP_OP_GATHER, TRAP_OP_SCATTER_ADD, TRAP_OP_SCATTER,
+    TRAP_OP_SCATTER_ELEMENTS
 };
+// The offending index of a sparse-index trap ([05-SPARSE-1]): index, axis and
+// the axis extent, written by the thread whose trap was recorded first.
+__device__ long long g_trap_index[3] = {0, 0, 0};
+enum : unsigned int { TRAP_DTYPE_I64 = 4u };
 
 __device__ __forceinline__ void report_device_error(unsigned int code) {
     atomicOr(&g_device_error, code);
 }
 __device__ __forceinline__ void report_trap(unsigned int kind, unsigned int op, unsigned int dtype) {
     atomicCAS(&g_trap_code, 0u, 1u + ((kind << 16) | (op << 8) | dtype));
+    atomicOr(&g_device_error, static_cast<unsigned int>(DEVERR_TRAP));
+}
+// An index outside [0, extent) of a gather or scatter: a domain trap at i64
+// that also keeps the offending index for the message.
+__device__ __forceinline__ void report_index_trap(unsigned int op, int64_t index, int axis, int64_t extent) {
+    if (atomicCAS(&g_trap_code, 0u, 1u + ((TRAP_DOMAIN << 16) | (op << 8) | TRAP_DTYPE_I64)) == 0u) {
+        g_trap_index[0] = index;
+        g_trap_index[1] = axis;
+        g_trap_index[2] = extent;
+    }
     atomicOr(&g_device_error, static_cast<unsigned int>(DEVERR_TRAP));
 }
 

@@ -24,7 +24,8 @@
 //                         view of a dense operand becomes trans_a / trans_b
 //   Relu, ReluAdjoint, Softmax (last axis), Count, Cumsum (last axis)
 //                         the dedicated kernels
-//   Gather, ScatterAdd    index kernels ([05-OP-52]; bad indices set the
+//   Gather, ScatterAdd, Scatter, ScatterElements
+//                         index kernels ([05-OP-52]; bad indices set the
 //                         device error word: "numeric trap: domain in gather")
 //   Reshape, Permute, Expand, Shrink, Stride, Store
 //                         metadata views (a Reshape of a non-dense view is
@@ -87,7 +88,7 @@ enum class Op {
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
     FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
-    GuardedFail, UniformLike, Iota, ReduceWindow, ReduceWindowGrad
+    GuardedFail, UniformLike, Iota, ReduceWindow, ReduceWindowGrad, Scatter, ScatterElements
 };
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
@@ -632,8 +633,14 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (!acc || acc->kind != json::Value::Str || prim_dtype(acc->s) < 0)
             return bad("BlasMatmul accumulator");
         n.accumulator = prim_dtype(acc->s);
-    } else if (name == "Gather" || name == "ScatterAdd") {
-        n.op = name == "Gather" ? Op::Gather : Op::ScatterAdd;
+    } else if (name == "ScatterElements") {
+        // element-wise replace-scatter (ONNX ScatterElements; spec 05 3.5.1)
+        n.op = Op::ScatterElements;
+        CHELIS_TRY(need_inputs(3));
+        if (!as_index(field("axis"), &v)) return bad("ScatterElements axis");
+        n.axis = static_cast<int>(v);
+    } else if (name == "Gather" || name == "ScatterAdd" || name == "Scatter") {
+        n.op = name == "Gather" ? Op::Gather : name == "ScatterAdd" ? Op::ScatterAdd : Op::Scatter;
         CHELIS_TRY(need_inputs(n.op == Op::Gather ? 2 : 3));
         int64_t br = 0;
         if (!as_index(field("axis"), &v) || !as_index(field("batch_rank"), &br))
@@ -987,7 +994,7 @@ int check_and_layout(Program &P) {
                 own();
                 break;
             }
-            case Op::Gather: case Op::ScatterAdd: {
+            case Op::Gather: case Op::ScatterAdd: case Op::Scatter: {
                 const Node &vals = src(0);
                 const Node &idx = src(1);
                 const int it = idx.dtype;
@@ -1011,6 +1018,23 @@ int check_and_layout(Program &P) {
                     if (n.shape != vals.shape || src(2).shape != sel || src(2).dtype != n.dtype)
                         return bad("ScatterAdd shapes");
                 }
+                own();
+                break;
+            }
+            case Op::ScatterElements: {
+                const Node &data = src(0), &idx = src(1), &upd = src(2);
+                const int it = idx.dtype;
+                if (it != CHELIS_DTYPE_I64 && it != CHELIS_DTYPE_I32 && it != CHELIS_DTYPE_I16 &&
+                    it != CHELIS_DTYPE_I8)
+                    return bad("index dtype must be a signed integer ([05-SPARSE-1])");
+                if (data.dtype != n.dtype || upd.dtype != n.dtype) return bad("ScatterElements value dtype");
+                const size_t r = data.shape.size();
+                if (n.axis >= static_cast<int>(r) || idx.shape.size() != r || upd.shape != idx.shape ||
+                    n.shape != data.shape)
+                    return bad("ScatterElements shapes");
+                for (size_t d = 0; d < r; ++d)
+                    if (static_cast<int>(d) != n.axis && idx.shape[d] > data.shape[d])
+                        return bad("ScatterElements index extent beyond the data");
                 own();
                 break;
             }
@@ -1441,7 +1465,7 @@ __device__ __forceinline__ int64_t read_index(const void *p, int64_t off, int wi
 // p over values' axes before `axis`, q over the index axes after the batch
 // ones, t over values' axes after `axis`.  `v` / `x` are values' and
 // indices' layouts, the output dense.  An index outside [0, values.shape[axis])
-// writes 0 and sets the device error word.
+// writes 0 and records a domain trap with the index.
 struct GatherGeom {
     Strided v, x;
     int32_t axis, batch_rank, qrank, trank;
@@ -1473,7 +1497,7 @@ __global__ void gather_kernel(const T *__restrict__ values, const void *__restri
         }
         const int64_t k = read_index(idx, xoff, g.index_width);
         if (k < 0 || k >= g.v.shape[g.axis]) {
-            report_device_error(DEVERR_BAD_INDEX);
+            report_index_trap(TRAP_OP_GATHER, k, g.axis, g.v.shape[g.axis]);
             out[i] = T(0);
         } else {
             out[i] = values[voff + k * g.v.stride[g.axis]];
@@ -1486,7 +1510,7 @@ __global__ void gather_kernel(const T *__restrict__ values, const void *__restri
 // which is the updates' increasing flat order for every target cell.
 template <typename T>
 __global__ void scatter_add_kernel(const T *__restrict__ upd, Strided u, const void *__restrict__ idx,
-                                   GatherGeom g, T *__restrict__ out, int64_t lanes, int64_t nq) {
+                                   GatherGeom g, T *__restrict__ out, int64_t lanes, int64_t nq, int replace) {
     const Strided o = g.v;  // the output's dense layout and shape
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < lanes;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -1514,11 +1538,41 @@ __global__ void scatter_add_kernel(const T *__restrict__ upd, Strided u, const v
             }
             const int64_t k = read_index(idx, xoff, g.index_width);
             if (k < 0 || k >= o.shape[g.axis]) {
-                report_device_error(DEVERR_BAD_INDEX);
+                report_index_trap(replace ? TRAP_OP_SCATTER : TRAP_OP_SCATTER_ADD, k, g.axis, o.shape[g.axis]);
                 continue;
             }
             T *cell = out + ooff + k * o.stride[g.axis];
-            *cell = *cell + upd[uoff + qoff];
+            if (replace) *cell = upd[uoff + qoff];  // Scatter: the last write in update order wins
+            else *cell = *cell + upd[uoff + qoff];
+        }
+    }
+}
+
+// ScatterElements: update c (indices' shape) replaces data[c with its axis
+// coordinate set to indices[c]].  One thread per line of updates along the
+// axis, visited in order, so the last write in row-major update order wins.
+template <typename T>
+__global__ void scatter_elements_kernel(const T *__restrict__ upd, Strided su, const void *__restrict__ idx,
+                                        Strided si, int index_width, Strided o, int axis, T *__restrict__ out,
+                                        int64_t lanes, int64_t len) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < lanes;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t rem = i, uoff = 0, xoff = 0, ooff = 0;
+        for (int d = su.rank - 1; d >= 0; --d) {
+            if (d == axis) continue;
+            const int64_t c = rem % su.shape[d];
+            rem /= su.shape[d];
+            uoff += c * su.stride[d];
+            xoff += c * si.stride[d];
+            ooff += c * o.stride[d];
+        }
+        for (int64_t j = 0; j < len; ++j) {
+            const int64_t k = read_index(idx, xoff + j * si.stride[axis], index_width);
+            if (k < 0 || k >= o.shape[axis]) {
+                report_index_trap(TRAP_OP_SCATTER_ELEMENTS, k, axis, o.shape[axis]);
+                continue;
+            }
+            out[ooff + k * o.stride[axis]] = upd[uoff + j * su.stride[axis]];
         }
     }
 }
@@ -2440,7 +2494,7 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                                      reinterpret_cast<const double *>(b.ptr), ldb, sb,
                                      reinterpret_cast<double *>(out), nn, m * nn, batch);
         }
-        case Op::Gather: case Op::ScatterAdd: {
+        case Op::Gather: case Op::ScatterAdd: case Op::Scatter: {
             const Value &vals = in(0);
             const Value &idx = in(1);
             GatherGeom g{};
@@ -2459,13 +2513,16 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                     gather_kernel<uint64_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint64_t *>(vals.ptr), idx.ptr, g, reinterpret_cast<uint64_t *>(out), cnt);
                 else if (w == 4)
                     gather_kernel<uint32_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint32_t *>(vals.ptr), idx.ptr, g, reinterpret_cast<uint32_t *>(out), cnt);
-                else return unsupported("Gather of a 1- or 2-byte dtype");
+                else if (w == 2)
+                    gather_kernel<uint16_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint16_t *>(vals.ptr), idx.ptr, g, reinterpret_cast<uint16_t *>(out), cnt);
+                else
+                    gather_kernel<uint8_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<const uint8_t *>(vals.ptr), idx.ptr, g, reinterpret_cast<uint8_t *>(out), cnt);
                 g_launches++;
                 CHELIS_LAUNCH_CHECK("dag::gather_kernel");
                 return CHELIS_CUDA_OK;
             }
-            // ScatterAdd: out = dense copy of the target, then the updates
-            if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+            // ScatterAdd / Scatter: out = dense copy of the target, then the updates
+            if (n.op == Op::ScatterAdd && n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
                 return unsupported("ScatterAdd on a non-float precision");
             CHELIS_TRY(materialize(vals, out, s));
             Value dense_out;
@@ -2477,12 +2534,52 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
             for (int d = 0; d < g.qrank; ++d) nq *= g.qshape[d];
             const int64_t lanes = nq ? count_of(upd.shape) / nq : 0;
             if (lanes == 0 || nq == 0) return CHELIS_CUDA_OK;
-            if (n.dtype == CHELIS_DTYPE_F64)
-                scatter_add_kernel<double><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const double *>(upd.ptr), strided(upd), idx.ptr, g, reinterpret_cast<double *>(out), lanes, nq);
-            else
-                scatter_add_kernel<float><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const float *>(upd.ptr), strided(upd), idx.ptr, g, reinterpret_cast<float *>(out), lanes, nq);
+            if (n.op == Op::Scatter) {
+                // replacement copies stored bits: any element width
+#define CHELIS_DAG_SCATTER(T)                                                                              \
+    scatter_add_kernel<T><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const T *>(upd.ptr), strided(upd), \
+                                                          idx.ptr, g, reinterpret_cast<T *>(out), lanes, nq, 1)
+                switch (dtype_width(n.dtype)) {
+                    case 8: CHELIS_DAG_SCATTER(uint64_t); break;
+                    case 4: CHELIS_DAG_SCATTER(uint32_t); break;
+                    case 2: CHELIS_DAG_SCATTER(uint16_t); break;
+                    default: CHELIS_DAG_SCATTER(uint8_t); break;
+                }
+#undef CHELIS_DAG_SCATTER
+            } else if (n.dtype == CHELIS_DTYPE_F64) {
+                scatter_add_kernel<double><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const double *>(upd.ptr), strided(upd), idx.ptr, g, reinterpret_cast<double *>(out), lanes, nq, 0);
+            } else {
+                scatter_add_kernel<float><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const float *>(upd.ptr), strided(upd), idx.ptr, g, reinterpret_cast<float *>(out), lanes, nq, 0);
+            }
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::scatter_add_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::ScatterElements: {
+            const Value &data = in(0), &idx = in(1), &upd = in(2);
+            CHELIS_TRY(materialize(data, out, s));
+            const int64_t len = upd.shape[n.axis];
+            const int64_t nu = count_of(upd.shape);
+            const int64_t lanes = len ? nu / len : 0;
+            if (lanes == 0 || len == 0) return CHELIS_CUDA_OK;
+            Value dense_out;
+            dense_out.shape = n.shape;
+            dense_out.strides = dense_strides(n.shape);
+            const Strided so = strided(dense_out), su = strided(upd), si = strided(idx);
+            const int iw = dtype_width(idx.dtype);
+#define CHELIS_DAG_SCATTER_EL(T)                                                                           \
+    scatter_elements_kernel<T><<<grid_for(lanes), 256, 0, s>>>(reinterpret_cast<const T *>(upd.ptr), su, idx.ptr, \
+                                                               si, iw, so, n.axis, reinterpret_cast<T *>(out),    \
+                                                               lanes, len)
+            switch (dtype_width(n.dtype)) {
+                case 8: CHELIS_DAG_SCATTER_EL(uint64_t); break;
+                case 4: CHELIS_DAG_SCATTER_EL(uint32_t); break;
+                case 2: CHELIS_DAG_SCATTER_EL(uint16_t); break;
+                default: CHELIS_DAG_SCATTER_EL(uint8_t); break;
+            }
+#undef CHELIS_DAG_SCATTER_EL
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::scatter_elements_kernel");
             return CHELIS_CUDA_OK;
         }
         case Op::Pad: {

@@ -365,12 +365,22 @@ int chelis_cuda_device_status(void) {
         static const char *const ops[] = {"add", "sub", "mul", "trunc_div", "floor_div", "mod", "neg", "abs", "cast",
                                           "cast_trunc", "cast_saturate",
                                           "uniform_like", "range",
-                                          "reduce_window_sum"};
+                                          "reduce_window_sum", "gather", "scatter_add", "scatter",
+                                          "scatter_elements"};
         static const char *const dtypes[] = {"f32", "f64", "i32", "bool", "i64", "bf16", "f16", "i8", "i16", "key"};
+        constexpr unsigned int n_ops = sizeof(ops) / sizeof(ops[0]);
         const unsigned int c = code ? code - 1 : 0, k = c >> 16, o = (c >> 8) & 0xff, d = c & 0xff;
+        const char *op = o < n_ops ? ops[o] : "?";
+        if (o >= TRAP_OP_GATHER && o < n_ops) {
+            // the reference's sparse-index failure: the index line, then the trap line
+            long long at[3] = {0, 0, 0};
+            CHELIS_TRY(check_cuda(cudaMemcpyFromSymbol(at, g_trap_index, sizeof(at)), "read trap index"));
+            return set_error(CHELIS_CUDA_ERR_DOMAIN,
+                             "%s index %lld out of bounds at axis %lld of extent %lld\nnumeric trap: domain in %s at i64",
+                             op, at[0], at[1], at[2], op);
+        }
         return set_error(k == 0 ? CHELIS_CUDA_ERR_OVERFLOW : CHELIS_CUDA_ERR_DOMAIN,
-                         "numeric trap: %s in %s at %s", k < 3 ? kinds[k] : "?",
-                         o < 14 ? ops[o] : "?", d < 10 ? dtypes[d] : "?");
+                         "numeric trap: %s in %s at %s", k < 3 ? kinds[k] : "?", op, d < 10 ? dtypes[d] : "?");
     }
     return CHELIS_CUDA_OK;
 }

@@ -31,7 +31,7 @@ import json
 import struct
 
 PRIM = {"f32": "F32", "f64": "F64", "i64": "Int64", "i32": "Int32", "bool": "Bool", "key": "Key", "i8": "Int8",
-        "i16": "Int16"}
+        "i16": "Int16", "f16": "F16", "bf16": "Bf16"}
 
 
 def f32_scalar(v: float) -> dict:

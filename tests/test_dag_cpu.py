@@ -221,3 +221,20 @@ def test_reduce_window_rejections(body, dims, message):
     st, h = load(g.json())
     assert st != 0
     assert message in L.last_error()
+
+
+@pytest.mark.parametrize("ishape,ushape,iprec,message", [
+    ([2, 2], [2, 3], "i64", "ScatterElements shapes"),
+    ([2], [2], "i64", "ScatterElements shapes"),
+    ([3, 2], [3, 2], "i64", "index extent beyond the data"),
+    ([2, 2], [2, 2], "f32", "index dtype must be a signed integer"),
+])
+def test_scatter_elements_rejections(ishape, ushape, iprec, message):
+    g = D.Dag()
+    a = g.load("a", [2, 3])
+    i = g.load("i", ishape, iprec)
+    u = g.load("u", ushape)
+    g.roots = [g.add({"ScatterElements": {"axis": 1}}, [a, i, u], [2, 3])]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()

@@ -28,7 +28,8 @@ def run(h, tensors):
     for t in tensors:
         t = t.contiguous()
         dt = {torch.float32: L.DTYPE_F32, torch.float64: L.DTYPE_F64, torch.int64: L.DTYPE_I64,
-              torch.int32: L.DTYPE_I32, torch.bool: L.DTYPE_BOOL, torch.int8: 7, torch.int16: 8}[t.dtype]
+              torch.int32: L.DTYPE_I32, torch.bool: L.DTYPE_BOOL, torch.int8: 7, torch.int16: 8,
+              torch.float16: L.DTYPE_F16, torch.bfloat16: L.DTYPE_BF16}[t.dtype]
         shape = (ctypes.c_int64 * max(t.dim(), 1))(*t.shape)
         o = lib.chelis_device_tensor_borrow_shape(dt, t.dim(), shape, t.data_ptr(),
                                                    t.numel() * t.element_size())
@@ -45,7 +46,7 @@ def run(h, tensors):
         shape = [v.shape[d] for d in range(v.rank)]
         np_dt = {L.DTYPE_F32: np.float32, L.DTYPE_F64: np.float64, L.DTYPE_I64: np.int64,
                  L.DTYPE_I32: np.int32, L.DTYPE_BOOL: np.uint8, 9: np.uint64,  # 9: key
-                 7: np.int8, 8: np.int16}[v.dtype]
+                 7: np.int8, 8: np.int16, L.DTYPE_F16: np.uint16, L.DTYPE_BF16: np.uint16}[v.dtype]
         host = np.empty(shape, dtype=np_dt)
         L.call("chelis_device_tensor_copy_to_host_bytes", host.ctypes.data, host.nbytes, outs[i])
         res.append(host)
@@ -168,8 +169,159 @@ def test_out_of_range_gather_index_traps(cuda):
     g.roots = [g.add({"Gather": {"axis": 1, "batch_rank": 0}}, [a, i], [2, 2])]
     h = program(g)
     try:
-        with pytest.raises(L.ChelisCudaError, match="numeric trap: domain in gather"):
+        with pytest.raises(L.ChelisCudaError, match="gather index 3 out of bounds at axis 1 of extent 3\nnumeric trap: domain in gather at i64"):
             run(h, [torch.from_numpy(x).cuda(), torch.from_numpy(idx).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+# crates/chelis-backend-c/tests/exec_compile.rs:761-900: the sparse mappings
+# move stored bits.  Base cell i holds seed + i, update cell i holds
+# seed + i + 32 (bool: ((i / 2 + i) % 2) ^ update); `map` names, per output
+# cell, the update cell it holds, or -(base cell) - 1.
+SPARSE_SEEDS = [("f32", 0x3F800000), ("f64", 0x3FF0000000000000), ("f16", 0x3C00), ("bf16", 0x3F80),
+                ("i8", 10), ("i16", 100), ("i32", 100), ("i64", 9_007_199_254_740_993), ("bool", 0)]
+SPARSE_CASES = [
+    ({"Gather": {"axis": 1, "batch_rank": 0}}, [2, 3, 2], [2, 2, 2, 2], [2, 0, 1, 2],
+     [4, 5, 0, 1, 2, 3, 4, 5, 10, 11, 6, 7, 8, 9, 10, 11]),
+    ({"Scatter": {"axis": 1, "batch_rank": 0}}, [2, 3, 2], [2, 3, 2], [2, 0, 2, 0],
+     [6, 7, -3, -4, 4, 5, 14, 15, -9, -10, 12, 13]),
+    ({"ScatterElements": {"axis": 1}}, [2, 3], [2, 3], [2, 0, 1, 1], [1, -2, 0, -4, 3, -6]),
+]
+_STORAGE = {"f32": (np.uint32, torch.float32), "f64": (np.uint64, torch.float64), "f16": (np.uint16, torch.float16),
+            "bf16": (np.uint16, torch.bfloat16), "i8": (np.uint8, torch.int8), "i16": (np.uint16, torch.int16),
+            "i32": (np.uint32, torch.int32), "i64": (np.uint64, torch.int64), "bool": (np.uint8, torch.bool)}
+
+
+def _bits_tensor(bits, shape, prec):
+    np_t, torch_t = _STORAGE[prec]
+    raw = np.asarray(bits, dtype=np.uint64).astype(np_t).reshape(shape)
+    signed = {np.uint8: np.uint8, np.uint16: np.int16, np.uint32: np.int32, np.uint64: np.int64}[np_t]
+    return torch.from_numpy(raw.view(signed).copy()).view(torch_t).cuda()
+
+
+@pytest.mark.parametrize("index_prec", ["i32", "i64"])
+@pytest.mark.parametrize("prec,seed", SPARSE_SEEDS)
+def test_sparse_mappings_preserve_stored_bits(cuda, prec, seed, index_prec):
+    def bits(i, update):
+        if prec == "bool":
+            return ((i // 2 + i) % 2) ^ update
+        return seed + i + (32 if update else 0)
+    for op, base_shape, out_shape, selected, mapping in SPARSE_CASES:
+        gather = "Gather" in op
+        elements = "ScatterElements" in op
+        update_shape = [2, 2] if elements else [2, 2, 2, 2]
+        g = D.Dag()
+        base = g.load("base", base_shape, prec)
+        idx = g.load("indices", [2, 2], index_prec)
+        ins = [base, idx] + ([] if gather else [g.load("updates", update_shape, prec)])
+        g.roots = [g.add(op, ins, out_shape, prec)]
+        h = program(g)
+        try:
+            nb, nu = int(np.prod(base_shape)), int(np.prod(update_shape))
+            args = [_bits_tensor([bits(i, 0) for i in range(nb)], base_shape, prec),
+                    torch.tensor(selected, dtype=torch.int32 if index_prec == "i32" else torch.int64).view(2, 2).cuda()]
+            if not gather:
+                args.append(_bits_tensor([bits(i, 1) for i in range(nu)], update_shape, prec))
+            (got,) = run(h, args)
+        finally:
+            L.load().chelis_dag_release(h)
+        np_t = _STORAGE[prec][0]
+        want = np.array([bits(-m - 1, 0) if m < 0 else bits(m, (not gather)) for m in mapping],
+                        dtype=np.uint64).astype(np_t)
+        assert list(got.shape) == out_shape, op
+        assert np.array_equal(got.reshape(-1).view(np_t), want), (op, prec, index_prec)
+
+
+def _scatter_replace(target, idx, upd, axis, batch_rank):
+    """eval.rs scatter_replace: updates visited in row-major order, last write wins."""
+    out = target.copy()
+    qrank = idx.ndim - batch_rank
+    for c in np.ndindex(*upd.shape):
+        p, q, t = c[:axis], c[axis:axis + qrank], c[axis + qrank:]
+        k = int(idx[p[:batch_rank] + q])
+        out[p + (k,) + t] = upd[c]
+    return out
+
+
+def _scatter_elements(data, idx, upd, axis):
+    """eval.rs:2276 scatter_elements, the same order rule."""
+    out = data.copy()
+    for c in np.ndindex(*upd.shape):
+        d = list(c)
+        d[axis] = int(idx[c])
+        out[tuple(d)] = upd[c]
+    return out
+
+
+@pytest.mark.parametrize("axis,batch_rank", [(0, 0), (1, 0), (1, 1), (2, 1)])
+def test_scatter_last_write_wins(cuda, axis, batch_rank):
+    rng = np.random.default_rng(60 + axis + batch_rank)
+    shape = [3, 5, 4]
+    lead = shape[:batch_rank]
+    qshape = [6, 2]                                   # many duplicates into an axis of 3..5
+    idx = rng.integers(0, shape[axis], size=lead + qshape)
+    upd_shape = shape[:axis] + qshape + shape[axis + 1:]
+    target = rng.standard_normal(shape).astype(np.float64)
+    upd = rng.standard_normal(upd_shape).astype(np.float64)
+    g = D.Dag()
+    a = g.load("t", shape, "f64")
+    i = g.load("i", lead + qshape, "i64")
+    u = g.load("u", upd_shape, "f64")
+    g.roots = [g.add({"Scatter": {"axis": axis, "batch_rank": batch_rank}}, [a, i, u], shape, "f64")]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda() for x in (target, idx, upd)])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert np.array_equal(got, _scatter_replace(target, idx, upd, axis, batch_rank))
+
+
+@pytest.mark.parametrize("axis", [0, 1, 2])
+@pytest.mark.parametrize("prec", ["f32", "i64", "i16"])
+def test_scatter_elements_last_write_wins(cuda, axis, prec):
+    rng = np.random.default_rng(70 + axis)
+    shape = [4, 5, 6]
+    ishape = [3, 4, 5]
+    ishape[axis] = 9                                  # longer than the axis: duplicates
+    dt = {"f32": np.float32, "i64": np.int64, "i16": np.int16}[prec]
+    data = (rng.standard_normal(shape) * 100).astype(dt)
+    upd = (rng.standard_normal(ishape) * 100).astype(dt)
+    idx = rng.integers(0, shape[axis], size=ishape).astype(np.int32)
+    g = D.Dag()
+    a = g.load("d", shape, prec)
+    i = g.load("i", ishape, "i32")
+    u = g.load("u", ishape, prec)
+    g.roots = [g.add({"ScatterElements": {"axis": axis}}, [a, i, u], shape, prec)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda() for x in (data, idx, upd)])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert np.array_equal(got, _scatter_elements(data, idx, upd, axis))
+
+
+@pytest.mark.parametrize("op,message", [
+    ({"Scatter": {"axis": 1, "batch_rank": 0}}, "scatter index 3 out of bounds at axis 1 of extent 3"),
+    ({"ScatterElements": {"axis": 1}}, "scatter_elements index -1 out of bounds at axis 1 of extent 3"),
+    ({"ScatterAdd": {"axis": 1, "batch_rank": 0}}, "scatter_add index 3 out of bounds at axis 1 of extent 3"),
+])
+def test_out_of_range_scatter_index_traps(cuda, op, message):
+    elements = "ScatterElements" in op
+    x = np.zeros((2, 3), np.float32)
+    idx = np.array([[0, -1], [1, 2]] if elements else [0, 3], np.int64)
+    ushape = [2, 2]
+    g = D.Dag()
+    a = g.load("x", [2, 3])
+    i = g.load("i", list(idx.shape), "i64")
+    u = g.load("u", ushape)
+    g.roots = [g.add(op, [a, i, u], [2, 3])]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match=message):
+            run(h, [torch.from_numpy(x).cuda(), torch.from_numpy(idx).cuda(),
+                    torch.ones(ushape, device="cuda")])
+        L.call("chelis_cuda_device_status")  # cleared by the report
     finally:
         L.load().chelis_dag_release(h)
 
