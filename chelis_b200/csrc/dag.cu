@@ -25,7 +25,10 @@
 //   Relu, ReluAdjoint, Softmax (last axis), Count, Cumsum (last axis)
 //                         the dedicated kernels
 //   Gather, ScatterAdd, Scatter, ScatterElements
-//                         index kernels ([05-OP-52]; bad indices set the
+//                         index kernels
+//   Shape                 a constant (extents are concrete)
+//   OrderedAdjointSum     the adjacent-pair tree over List cotangents
+//   UniformBoundAdjoint   a bound's pathwise adjoint under the forward key ([05-OP-52]; bad indices set the
 //                         device error word: "numeric trap: domain in gather")
 //   Reshape, Permute, Expand, Shrink, Stride, Store
 //                         metadata views (a Reshape of a non-dense view is
@@ -88,8 +91,11 @@ enum class Op {
     Count, Matmul, Gather, ScatterAdd, Cumsum, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
     FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
-    GuardedFail, UniformLike, Iota, ReduceWindow, ReduceWindowGrad, Scatter, ScatterElements
+    GuardedFail, UniformLike, Iota, ReduceWindow, ReduceWindowGrad, Scatter, ScatterElements, Shape,
+    OrderedAdjointSum, UniformBoundAdjoint
 };
+
+constexpr int kMaxAdjointInputs = 64;  // OrderedAdjointSum inputs taken in one launch
 
 // Compare kinds (ComparisonKind order) and Logical kinds (LogicalKind order)
 enum { CMP_CMPLT = 0, CMP_LT, CMP_EQ, CMP_NEQ, CMP_GT, CMP_GTE, CMP_LTE };
@@ -610,6 +616,33 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
             n.wstride.push_back(b);
         }
         CHELIS_TRY(need_inputs(n.op == Op::ReduceWindow ? 1 : 2));
+    } else if (name == "Shape") {
+        // a scalar read of one input extent; the input's values are never read
+        n.op = Op::Shape;
+        CHELIS_TRY(need_inputs(1));
+        if (!as_index(field("axis"), &v)) return bad("Shape axis");
+        n.axis = static_cast<int>(v);
+    } else if (name == "OrderedAdjointSum") {
+        // spec/06 2.4: the adjacent-pair tree over queued List cotangent
+        // contributions; `groups` gives each group's input count
+        n.op = Op::OrderedAdjointSum;
+        const json::Value *gr = field("groups");
+        if (!gr || gr->kind != json::Value::Arr) return bad("OrderedAdjointSum groups");
+        size_t total = 0;
+        for (const auto &e : gr->a) {
+            if (!as_index(&e, &v) || v < 1) return bad("OrderedAdjointSum group width");
+            n.window.push_back(v);
+            total += static_cast<size_t>(v);
+        }
+        CHELIS_TRY(need_inputs(total));
+    } else if (name == "UniformBoundAdjoint") {
+        // [05-OP-8] inputs [template, g, key]; the bound's pathwise adjoint
+        n.op = Op::UniformBoundAdjoint;
+        const json::Value *b = field("bound");
+        n.kind = -1;
+        if (b && b->kind == json::Value::Str) n.kind = b->s == "Low" ? 0 : b->s == "High" ? 1 : -1;
+        if (n.kind < 0) return bad("UniformBoundAdjoint bound");
+        CHELIS_TRY(need_inputs(3));
     } else if (name == "Iota") {
         // [05-OP-54] range(start, end) as a rank-one i64 tensor
         n.op = Op::Iota;
@@ -886,6 +919,36 @@ int check_and_layout(Program &P) {
                 own();
                 break;
             }
+            case Op::Shape: {
+                const Node &x = src(0);
+                if (n.axis >= static_cast<int>(x.shape.size())) return bad("Shape axis beyond the input rank");
+                if (n.dtype != CHELIS_DTYPE_I64 || !n.shape.empty()) return bad("Shape result must be an i64 scalar");
+                // extents are concrete here: the read is a constant written into its output
+                n.bits = static_cast<uint64_t>(x.shape[n.axis]);
+                own();
+                break;
+            }
+            case Op::OrderedAdjointSum: {
+                if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+                    return unsupported("OrderedAdjointSum precision");
+                if (!n.shape.empty()) return bad("OrderedAdjointSum result must be a scalar");
+                if (n.in.size() > static_cast<size_t>(kMaxAdjointInputs))
+                    return unsupported("OrderedAdjointSum with more than 64 inputs");
+                size_t k = 0;
+                for (int64_t width : n.window) {
+                    const Node &first = src(static_cast<int>(k));
+                    for (int64_t j = 0; j < width; ++j, ++k) {
+                        const Node &x = src(static_cast<int>(k));
+                        if (x.dtype != n.dtype) return bad("OrderedAdjointSum contribution dtype");
+                        if (x.shape.size() > 1 || (x.shape.empty() && width != 1))
+                            return bad("OrderedAdjointSum contributions are rank-one columns or one scalar");
+                        if (count_of(x.shape) != count_of(first.shape))
+                            return bad("ordered List cotangent columns have different lengths");
+                    }
+                }
+                own();
+                break;
+            }
             case Op::Iota:
                 if (n.activation >= 0) return unsupported("Iota under an activation");
                 for (int k = 0; k < 2; ++k)
@@ -910,6 +973,21 @@ int check_and_layout(Program &P) {
                     if (bs.size() > ks.size() || !std::equal(bs.begin(), bs.end(), ks.begin()))
                         return bad("UniformLike bound shape");
                 }
+                own();
+                break;
+            }
+            case Op::UniformBoundAdjoint: {
+                if (n.activation >= 0) return unsupported("UniformBoundAdjoint under an activation");
+                if (n.dtype != CHELIS_DTYPE_F32 && n.dtype != CHELIS_DTYPE_F64)
+                    return unsupported("UniformBoundAdjoint precision");
+                const Node &t = src(0), &g = src(1), &k = src(2);
+                if (t.dtype != n.dtype || g.dtype != n.dtype) return bad("UniformBoundAdjoint operand dtype");
+                if (g.shape != t.shape) return bad("UniformBoundAdjoint cotangent shape");
+                if (k.dtype != CHELIS_DTYPE_KEY) return bad("UniformBoundAdjoint key must be a key");
+                if (k.shape.size() > t.shape.size() || !std::equal(k.shape.begin(), k.shape.end(), t.shape.begin()))
+                    return bad("UniformBoundAdjoint key shape");
+                if (n.shape.size() > k.shape.size() || !std::equal(n.shape.begin(), n.shape.end(), k.shape.begin()))
+                    return bad("UniformBoundAdjoint result is not a leading part of its keys' shape");
                 own();
                 break;
             }
@@ -2081,6 +2159,108 @@ __global__ void window_reduce_kernel(const T *__restrict__ x, WinGeom g, int kin
     }
 }
 
+// OrderedAdjointSum: the leaves are each group's columns interleaved row
+// first, then input order, groups in order; the result is their
+// adjacent-pair tree (level by level, an odd last element carried up).  One
+// block: thread t folds the aligned run of `chunk` leaves (a power of two)
+// starting at t * chunk, which is a complete subtree of that tree (the last
+// run is the tree of what remains), then the block pairs the runs' sums level
+// by level in shared memory.  One leaf is the adjoint unchanged; a NaN made by
+// the additions is written canonical; no leaves give +0.
+constexpr int kAdjointThreads = 1024;
+struct AdjointLeaves {
+    const void *ptr[kMaxAdjointInputs];
+    int64_t stride[kMaxAdjointInputs];
+    int32_t first[kMaxAdjointInputs];   // a group's first input
+    int32_t width[kMaxAdjointInputs];   // its input count
+    int64_t leaf0[kMaxAdjointInputs + 1];  // its first leaf
+    int32_t ngroups;
+};
+
+template <typename T>
+__device__ __forceinline__ T adjoint_leaf(const AdjointLeaves &a, int64_t l) {
+    int g = 0;
+    while (g + 1 < a.ngroups && l >= a.leaf0[g + 1]) ++g;
+    const int64_t r = (l - a.leaf0[g]) / a.width[g];
+    const int in = a.first[g] + static_cast<int>((l - a.leaf0[g]) % a.width[g]);
+    return static_cast<const T *>(a.ptr[in])[r * a.stride[in]];
+}
+
+// The adjacent-pair tree of leaf(0 .. n) folded by one block of NT threads:
+// thread t folds the aligned run of `chunk` leaves (a power of two with
+// ceil(n / chunk) <= NT) starting at t * chunk, a complete subtree of the
+// tree (the last run is the tree of what remains), then the block pairs the
+// runs' sums level by level in `part`.  Every thread returns the total; no
+// leaves give +0.  The leaf function is expected to round its own products
+// (no contraction into the additions).
+template <typename T, int NT, typename Leaf>
+__device__ T block_pair_tree(int64_t n, int64_t chunk, Leaf leaf, T *part) {
+    const int64_t runs = (n + chunk - 1) / chunk;
+    auto add = [](T x, T y) { return x + y; };
+    for (int64_t t = threadIdx.x; t < runs; t += NT) {
+        LeafTree<T> tree;
+        const int64_t lo = t * chunk, hi = lo + chunk < n ? lo + chunk : n;
+        for (int64_t l = lo; l < hi; ++l) tree.push(leaf(l), add);
+        part[t] = tree.total(add);
+    }
+    __syncthreads();
+    for (int64_t m = runs; m > 1; m = (m + 1) / 2) {
+        T v = T(0);
+        const int64_t j = threadIdx.x;
+        if (j < (m + 1) / 2) v = 2 * j + 1 < m ? part[2 * j] + part[2 * j + 1] : part[2 * j];
+        __syncthreads();
+        if (j < (m + 1) / 2) part[j] = v;
+        __syncthreads();
+    }
+    const T r = runs > 0 ? part[0] : T(0);
+    __syncthreads();  // `part` may be reused by the caller
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ T canonical_nan(T r) {
+    if (r == r) return r;
+    if constexpr (sizeof(T) == 4) return __int_as_float(0x7fc00000);
+    else return __longlong_as_double(0x7ff8000000000000ll);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kAdjointThreads) ordered_adjoint_sum_kernel(AdjointLeaves a, int64_t n, int64_t chunk,
+                                                                              T *__restrict__ out) {
+    __shared__ T part[kAdjointThreads];
+    const T r = block_pair_tree<T, kAdjointThreads>(n, chunk, [&](int64_t l) { return adjoint_leaf<T>(a, l); }, part);
+    if (threadIdx.x == 0) *out = n > 1 ? canonical_nan(r) : r;
+}
+
+// [05-OP-8] the pathwise adjoint of a UniformLike bound: element i of the
+// cotangent g contributes g_i * (1 - u_i) to `low` and g_i * u_i to `high`,
+// u_i the forward draw's unit (rounded to f32 for an f32 draw), each product
+// and the sum at the draw's precision.  Result element e (one block) sums by
+// one adjacent-pair tree the rows of g whose keys fall in its leading-part
+// group, in row-major order.
+constexpr int kBoundThreads = 256;
+template <typename T>
+__global__ void __launch_bounds__(kBoundThreads) uniform_bound_adjoint_kernel(
+    const T *__restrict__ g, Strided sg, const uint64_t *__restrict__ keys, Strided sk, int64_t row_len,
+    int64_t rows_per_group, int64_t chunk, int high, T *__restrict__ out) {
+    __shared__ T part[kBoundThreads];
+    const int64_t e = blockIdx.x, n = rows_per_group * row_len, base = e * n;
+    auto leaf = [&](int64_t l) -> T {
+        const int64_t i = base + l, b = i / row_len, k = i - b * row_len;
+        const uint64_t w = rng_word(keys[offset_of(sk, b)], static_cast<uint64_t>(k));
+        const double u = static_cast<double>(w >> 11) * 0x1p-53;
+        const T x = g[offset_of(sg, i)];
+        if constexpr (sizeof(T) == 4) {
+            const float uf = __double2float_rn(u);
+            return __fmul_rn(x, high ? uf : __fsub_rn(1.0f, uf));
+        } else {
+            return __dmul_rn(x, high ? u : __dsub_rn(1.0, u));
+        }
+    };
+    const T r = block_pair_tree<T, kBoundThreads>(n, chunk, leaf, part);
+    if (threadIdx.x == 0) out[e] = canonical_nan(r);
+}
+
 // ReduceWindowGrad: input position p folds, by the canonical tree in window
 // order, the contributions of the windows covering it: g (sum), g / volume
 // (mean); for max / min only where p is the window's first NaN (full g) or,
@@ -2352,7 +2532,7 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
     const int w = dtype_width(n.dtype);
     auto in = [&](int k) -> Value & { return val[n.in[k]]; };
     switch (n.op) {
-        case Op::Const: {
+        case Op::Const: case Op::Shape: {
             if (cnt == 0) return CHELIS_CUDA_OK;
             switch (w) {
                 case 8: fill_kernel<uint64_t><<<grid_for(cnt), 256, 0, s>>>(reinterpret_cast<uint64_t *>(out), n.bits, cnt); break;
@@ -2843,6 +3023,59 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
             }
             g_launches++;
             CHELIS_LAUNCH_CHECK("dag::window_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::OrderedAdjointSum: {
+            AdjointLeaves a{};
+            int64_t leaves = 0;
+            int k = 0;
+            for (size_t g = 0; g < n.window.size(); ++g) {
+                const int width = static_cast<int>(n.window[g]);
+                a.first[g] = k;
+                a.width[g] = width;
+                a.leaf0[g] = leaves;
+                for (int j = 0; j < width; ++j, ++k) {
+                    const Value &x = in(k);
+                    a.ptr[k] = x.ptr;
+                    a.stride[k] = x.shape.empty() ? 0 : x.strides[0];
+                }
+                leaves += count_of(in(a.first[g]).shape) * width;
+            }
+            a.ngroups = static_cast<int32_t>(n.window.size());
+            a.leaf0[a.ngroups] = leaves;
+            int64_t chunk = 1;
+            while ((leaves + chunk - 1) / chunk > kAdjointThreads) chunk *= 2;
+            if (n.dtype == CHELIS_DTYPE_F64)
+                ordered_adjoint_sum_kernel<double><<<1, kAdjointThreads, 0, s>>>(a, leaves, chunk,
+                                                                                 reinterpret_cast<double *>(out));
+            else
+                ordered_adjoint_sum_kernel<float><<<1, kAdjointThreads, 0, s>>>(a, leaves, chunk,
+                                                                                reinterpret_cast<float *>(out));
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::ordered_adjoint_sum_kernel");
+            return CHELIS_CUDA_OK;
+        }
+        case Op::UniformBoundAdjoint: {
+            const Value &g = in(1), &k = in(2);
+            const int64_t rows = count_of(k.shape), total = count_of(g.shape), groups = cnt;
+            const int64_t row_len = rows > 0 ? total / rows : 0;
+            const int64_t rows_per_group = groups > 0 ? rows / groups : 0;
+            if (groups == 0) return CHELIS_CUDA_OK;
+            const int64_t leaves = rows_per_group * row_len;
+            int64_t chunk = 1;
+            while ((leaves + chunk - 1) / chunk > kBoundThreads) chunk *= 2;
+            if (groups > INT32_MAX) return unsupported("UniformBoundAdjoint with more than 2^31 result elements");
+            const unsigned int grid = static_cast<unsigned int>(groups);
+            if (n.dtype == CHELIS_DTYPE_F64)
+                uniform_bound_adjoint_kernel<double><<<grid, kBoundThreads, 0, s>>>(
+                    reinterpret_cast<const double *>(g.ptr), strided(g), reinterpret_cast<const uint64_t *>(k.ptr),
+                    strided(k), row_len, rows_per_group, chunk, n.kind, reinterpret_cast<double *>(out));
+            else
+                uniform_bound_adjoint_kernel<float><<<grid, kBoundThreads, 0, s>>>(
+                    reinterpret_cast<const float *>(g.ptr), strided(g), reinterpret_cast<const uint64_t *>(k.ptr),
+                    strided(k), row_len, rows_per_group, chunk, n.kind, reinterpret_cast<float *>(out));
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::uniform_bound_adjoint_kernel");
             return CHELIS_CUDA_OK;
         }
         case Op::Iota: {

@@ -238,3 +238,42 @@ def test_scatter_elements_rejections(ishape, ushape, iprec, message):
     st, h = load(g.json())
     assert st != 0
     assert message in L.last_error()
+
+
+@pytest.mark.parametrize("body,dims,shapes,message", [
+    ({"groups": [2]}, [], [[3], [4]], "ordered List cotangent columns have different lengths"),
+    ({"groups": [2]}, [], [[], []], "rank-one columns or one scalar"),
+    ({"groups": [1]}, [3], [[3]], "result must be a scalar"),
+    ({"groups": [0, 1]}, [], [[3]], "group width"),
+])
+def test_ordered_adjoint_sum_rejections(body, dims, shapes, message):
+    g = D.Dag()
+    ins = [g.load(f"c{i}", s) for i, s in enumerate(shapes)]
+    g.roots = [g.add({"OrderedAdjointSum": body}, ins, dims)]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()
+
+
+def test_shape_rejections():
+    g = D.Dag()
+    x = g.load("x", [3])
+    g.roots = [g.add({"Shape": {"axis": 1}}, [x], [], "i64")]
+    st, h = load(g.json())
+    assert st != 0
+    assert "Shape axis beyond the input rank" in L.last_error()
+
+
+@pytest.mark.parametrize("bound,kshape,dims,message", [
+    ("Middle", [4], [4], "UniformBoundAdjoint bound"),
+    ("Low", [5], [5], "UniformBoundAdjoint key shape"),
+    ("Low", [4], [4, 6], "not a leading part of its keys' shape"),
+])
+def test_uniform_bound_adjoint_rejections(bound, kshape, dims, message):
+    g = D.Dag()
+    t, cot = g.load("t", [4, 6]), g.load("g", [4, 6])
+    k = g.key_from_seed(g.load("seed", kshape, "i64"))
+    g.roots = [g.add({"UniformBoundAdjoint": {"bound": bound}}, [t, cot, k], dims)]
+    st, h = load(g.json())
+    assert st != 0
+    assert message in L.last_error()

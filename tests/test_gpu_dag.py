@@ -326,6 +326,84 @@ def test_out_of_range_scatter_index_traps(cuda, op, message):
         L.load().chelis_dag_release(h)
 
 
+def _pair_tree(leaves):
+    """grad.rs / eval.rs:5470 OrderedAdjointSum: adjacent pairs level by level,
+    an odd last element carried; one leaf unchanged; none gives +0."""
+    xs = list(leaves)
+    if not xs:
+        return None
+    if len(xs) == 1:
+        return xs[0]
+    while len(xs) > 1:
+        xs = [xs[i] + xs[i + 1] if i + 1 < len(xs) else xs[i] for i in range(0, len(xs), 2)]
+    return xs[0]
+
+
+@pytest.mark.parametrize("prec,groups", [
+    ("f32", [(2, 5), (1, None), (3, 7)]),          # (width, rows); rows None: a scalar
+    ("f32", [(2, 3000), (1, None), (3, 3000)]),    # 15001 leaves: runs of 16 per thread
+    ("f64", [(1, 1), (4, 257)]),
+    ("f32", [(1, None)]),                          # one leaf: the adjoint unchanged
+    ("f32", [(2, 0)]),                             # empty columns: +0
+])
+def test_ordered_adjoint_sum(cuda, prec, groups):
+    dt = np.float32 if prec == "f32" else np.float64
+    rng = np.random.default_rng(80 + len(groups))
+    g = D.Dag()
+    ins, arrays, leaves, widths = [], [], [], []
+    for gi, (width, rows) in enumerate(groups):
+        shape = [] if rows is None else [rows]
+        cols = []
+        for j in range(width):
+            a = np.asarray(rng.standard_normal(shape) * 10.0 ** rng.integers(-3, 4, size=shape), dtype=dt)
+            cols.append(a.reshape(-1))
+            ins.append(g.load(f"c{gi}_{j}", shape, prec))
+            arrays.append(a)
+        widths.append(width)
+        for r in range(1 if rows is None else rows):   # row first, then input order
+            leaves.extend(c[r] for c in cols)
+    g.roots = [g.add({"OrderedAdjointSum": {"groups": widths}}, ins, [], prec)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(a).cuda() for a in arrays])
+    finally:
+        L.load().chelis_dag_release(h)
+    want = _pair_tree(leaves)
+    want = dt(0) if want is None else want
+    assert got.shape == ()
+    assert got.tobytes() == np.asarray(want, dtype=dt).tobytes()
+
+
+def test_ordered_adjoint_sum_nan_and_zero_rules(cuda):
+    payload = np.array([0x7FC01234], np.uint32).view(np.float32)[0]
+    neg0 = np.float32(-0.0)
+    cases = [([payload], 0x7FC01234),                 # one leaf: its payload kept
+             ([np.float32(1), payload], 0x7FC00000),  # an addition: canonical NaN
+             ([neg0, neg0, neg0], 0x80000000)]        # -0 + -0 stays -0
+    for vals, bits in cases:
+        g = D.Dag()
+        ins = [g.load(f"v{i}", [], "f32") for i in range(len(vals))]
+        g.roots = [g.add({"OrderedAdjointSum": {"groups": [1] * len(vals)}}, ins, [], "f32")]
+        h = program(g)
+        try:
+            (got,) = run(h, [torch.from_numpy(np.array(v, np.float32)).cuda() for v in vals])
+        finally:
+            L.load().chelis_dag_release(h)
+        assert int(got.view(np.uint32)) == bits
+
+
+def test_shape_reads_the_extent(cuda):
+    g = D.Dag()
+    x = g.load("x", [3, 5, 7])
+    g.roots = [g.add({"Shape": {"axis": a}}, [x], [], "i64") for a in range(3)]
+    h = program(g)
+    try:
+        got = run(h, [torch.zeros(3, 5, 7, device="cuda")])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert [int(v) for v in got] == [3, 5, 7]
+
+
 def test_host_array_entry(cuda, orc):
     """chelis_dag_run: host tensors in, runtime-owned host tensors out."""
     lib = L.load()
@@ -1065,6 +1143,56 @@ def test_uniform_like_bad_bounds_trap(cuda):
     finally:
         L.load().chelis_dag_release(h)
     L.call("chelis_cuda_device_status")
+
+
+@pytest.mark.parametrize("prec,shape,key_rank,out_rank", [
+    ("f32", [4, 50], 1, 1),        # a key per row, a bound per row
+    ("f32", [4, 3, 700], 2, 1),    # 12 key rows summed in groups of 3 (2100 leaves: runs of 16)
+    ("f64", [6, 40], 1, 0),        # every row into one scalar
+    ("f32", [33], 0, 0),           # one scalar key
+])
+@pytest.mark.parametrize("bound", ["Low", "High"])
+def test_uniform_bound_adjoint(cuda, orc, prec, shape, key_rank, out_rank, bound):
+    """dtype_semantics.rs:4429: leaf g_i * (1 - u_i) (Low) or g_i * u_i (High),
+    u_i rounded to f32 for an f32 draw, each product rounded, then the
+    adjacent-pair tree in row-major order at the draw's precision."""
+    dt = np.float32 if prec == "f32" else np.float64
+    rng = np.random.default_rng(90 + len(shape) + key_rank)
+    gv = (rng.standard_normal(shape) * 3).astype(dt)
+    kshape = shape[:key_rank]
+    seeds = rng.integers(-2 ** 40, 2 ** 40, size=kshape).astype(np.int64)
+    g = D.Dag()
+    t = g.load("t", shape, prec)
+    cot = g.load("g", shape, prec)
+    k = g.key_from_seed(g.load("seed", kshape, "i64"))
+    g.roots = [g.add({"UniformBoundAdjoint": {"bound": bound}}, [t, cot, k], shape[:out_rank], prec)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.zeros(shape, dtype=torch.float32 if prec == "f32" else torch.float64).cuda(),
+                         torch.from_numpy(gv).cuda(), torch.from_numpy(seeds).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    rows = int(np.prod(kshape)) if kshape else 1
+    row_len = gv.size // rows
+    groups = int(np.prod(shape[:out_rank])) if out_rank else 1
+    keys = [int(v) & (2 ** 64 - 1) for v in seeds.reshape(-1)] if kshape else [int(seeds) & (2 ** 64 - 1)]
+    flat = gv.reshape(-1)
+    per = gv.size // groups
+    want = []
+    for e in range(groups):
+        leaves = []
+        for i in range(e * per, (e + 1) * per):
+            u = orc.unit(keys[i // row_len], i % row_len)
+            if prec == "f32":
+                u = np.float32(u)
+                w = u if bound == "High" else np.float32(1.0) - u
+            else:
+                w = u if bound == "High" else 1.0 - u
+            leaves.append(dt(flat[i] * dt(w)))
+        want.append(_pair_tree(leaves))
+    want = np.array(want, dtype=dt).reshape(shape[:out_rank])
+    assert got.shape == want.shape
+    assert got.tobytes() == want.tobytes()
 
 
 # ---- Iota ([05-OP-54]; the C lane's emit_iota)
