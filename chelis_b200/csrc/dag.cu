@@ -61,7 +61,7 @@
 //   GuardedFail           the fallback, and the node's message reported by
 //                         chelis_cuda_device_status when the condition fires
 //
-// Shapes must be static (DimInfo::Lit or Named with a size).  Inputs are
+// Extents may be symbolic (bound per run from the inputs' shapes).  Inputs are
 // bound in first-Load order and outputs are the Store nodes then the roots
 // (emit.rs:5881-5934).  Outputs come back as new device owners.
 #include <cuda_fp16.h>
@@ -71,6 +71,7 @@
 #include <cstring>
 #include <limits>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <type_traits>
 #include <vector>
@@ -132,6 +133,7 @@ struct Node {
     std::string message;                               // GuardedFail
     uint32_t fail_id = 0;                              // its registered message id
     std::vector<int64_t> window, wstride;             // ReduceWindow(Grad)
+    std::vector<std::string> dim_names;                // per axis: the unbound name, or ""
 };
 
 // Static layout of a node's value: elements at root storage + offset +
@@ -243,15 +245,94 @@ const json::Value *variant(const json::Value &v, const char *name) {
     return &v.o[0].second;
 }
 
-// A static extent: DimInfo::Lit(n), DimInfo::Named(_, Some(n)), DimExpr /
-// RtDim literals ({"Lit": n}, {"Concrete": n}).
-bool static_extent(const json::Value &v, int64_t *out) {
-    if (const json::Value *l = variant(v, "Lit")) return as_index(l, out);
-    if (const json::Value *c = variant(v, "Concrete")) return as_index(c, out);
-    if (const json::Value *nm = variant(v, "Named")) {
-        if (nm->kind == json::Value::Arr && nm->a.size() == 2) return as_index(&nm->a[1], out);
+// Symbolic extents.  A program is parsed once with every unbound name read
+// as 1 (placeholder mode: the ops are checked, the shapes are not), and again
+// for each set of bindings its inputs' shapes give, which is checked and
+// planned like a static program.
+struct SymbolScope {
+    const std::vector<std::pair<std::string, int64_t>> *bind = nullptr;
+    bool placeholder = false;
+    bool saw_symbol = false;
+    int placeholders = 0;  // placeholder reads so far
+};
+thread_local SymbolScope t_sym;
+
+// the extent a name stands for: a binding, the placeholder, or an error
+int symbol_extent(const std::string &name, int64_t *out, bool *found) {
+    *found = true;
+    if (t_sym.bind) {
+        for (const auto &b : *t_sym.bind)
+            if (b.first == name) {
+                *out = b.second;
+                return CHELIS_CUDA_OK;
+            }
+        return bad("missing symbolic dimension binding", "`" + name + "`");
     }
-    return false;
+    if (t_sym.placeholder) {
+        t_sym.saw_symbol = true;
+        ++t_sym.placeholders;
+        *out = 1;
+        return CHELIS_CUDA_OK;
+    }
+    *found = false;
+    return CHELIS_CUDA_OK;
+}
+
+// An extent: DimInfo::Lit(n) / Named(_, Some(n)) / Named(name, None), the
+// DimExpr forms Concrete(n), Sym(name), Mul(a, b), Div(a, b) (exact, as
+// DimExpr::evaluate, dag.rs:293-317), RtDim::Lit(n) / Sym(name).  *found is
+// false for any other form (a runtime bound the caller names).
+int extent_expr(const json::Value &v, int64_t *out, bool *found) {
+    *found = true;
+    if (const json::Value *l = variant(v, "Lit")) return as_index(l, out) ? CHELIS_CUDA_OK : bad("extent literal");
+    if (const json::Value *c = variant(v, "Concrete"))
+        return as_index(c, out) ? CHELIS_CUDA_OK : bad("extent literal");
+    if (const json::Value *nm = variant(v, "Named")) {
+        if (nm->kind != json::Value::Arr || nm->a.size() != 2 || nm->a[0].kind != json::Value::Str)
+            return bad("Named dimension");
+        if (nm->a[1].kind != json::Value::Null)
+            return as_index(&nm->a[1], out) ? CHELIS_CUDA_OK : bad("Named dimension size");
+        return symbol_extent(nm->a[0].s, out, found);
+    }
+    if (const json::Value *sy = variant(v, "Sym")) {
+        if (sy->kind != json::Value::Str) return bad("Sym dimension");
+        return symbol_extent(sy->s, out, found);
+    }
+    const json::Value *mul = variant(v, "Mul"), *div = variant(v, "Div");
+    if (mul || div) {
+        const json::Value *ab = mul ? mul : div;
+        if (ab->kind != json::Value::Arr || ab->a.size() != 2) return bad("dimension expression");
+        int64_t a = 0, b = 0;
+        bool fa = false, fb = false;
+        const int before = t_sym.placeholders;
+        CHELIS_TRY(extent_expr(ab->a[0], &a, &fa));
+        CHELIS_TRY(extent_expr(ab->a[1], &b, &fb));
+        if (!fa || !fb) {
+            *found = false;
+            return CHELIS_CUDA_OK;
+        }
+        if (mul) {
+            if (a != 0 && b > std::numeric_limits<int64_t>::max() / a)
+                return bad("symbolic dimension product overflowed usize");
+            *out = a * b;
+        } else {
+            if (b == 0) return bad("symbolic dimension expression divided by zero");
+            // (a placeholder operand is not its value: the check waits for the binding)
+            if (a % b != 0 && t_sym.placeholders == before)
+                return bad("symbolic dimension expression is not evenly divisible");
+            *out = a / b;
+        }
+        return CHELIS_CUDA_OK;
+    }
+    *found = false;
+    return CHELIS_CUDA_OK;
+}
+
+// an extent, or CHELIS_CUDA_ERR_UNSUPPORTED naming `what` for a runtime form
+int extent(const json::Value &v, int64_t *out, const char *what) {
+    bool found = false;
+    CHELIS_TRY(extent_expr(v, out, &found));
+    return found ? CHELIS_CUDA_OK : unsupported(what);
 }
 
 int hex_bits(const json::Value *v, size_t digits, uint64_t *out) {
@@ -375,12 +456,12 @@ int bound_pairs(const json::Value *v, std::vector<std::pair<int64_t, int64_t>> *
         const json::Value &p = v->a[d];
         if (p.kind != json::Value::Arr || p.a.size() != 2) return bad("bounds");
         int64_t lo = 0, hi = 0;
-        if (!static_extent(p.a[0], &lo)) return unsupported("a runtime bound");
+        CHELIS_TRY(extent(p.a[0], &lo, "a runtime bound"));
         if (shrink && p.a[1].kind == json::Value::Str && p.a[1].s == "ToEnd") {
             if (d >= input_shape.size()) return bad("bounds rank");
             hi = input_shape[d];
-        } else if (!static_extent(p.a[1], &hi)) {
-            return unsupported("a runtime bound");
+        } else {
+            CHELIS_TRY(extent(p.a[1], &hi, "a runtime bound"));
         }
         out->emplace_back(lo, hi);
     }
@@ -417,8 +498,13 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
     n.dtype = static_cast<chelis_dtype>(dt);
     for (const auto &d : dims->a) {
         int64_t e = 0;
-        if (!static_extent(d, &e)) return unsupported("a symbolic extent");
+        CHELIS_TRY(extent(d, &e, "a runtime extent"));
         n.shape.push_back(e);
+        const json::Value *nm = variant(d, "Named");
+        n.dim_names.push_back(nm && nm->kind == json::Value::Arr && nm->a.size() == 2 &&
+                                      nm->a[1].kind == json::Value::Null
+                                  ? nm->a[0].s
+                                  : std::string());
     }
     if (n.shape.size() > static_cast<size_t>(kMaxRank)) return unsupported("rank above 8");
 
@@ -712,7 +798,8 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         if (!st || st->kind != json::Value::Arr) return bad("Stride strides");
         for (const auto &e : st->a) {
             int64_t s = 0;
-            if (!static_extent(e, &s) || s < 1) return unsupported("a runtime stride");
+            CHELIS_TRY(extent(e, &s, "a runtime stride"));
+            if (s < 1) return bad("Stride step below 1");
             n.step.push_back(s);
         }
     } else if (name == "Pad") {
@@ -1259,36 +1346,27 @@ bool is_view(Op op) {
 // Placement of every node, outputs (Store nodes, then the roots:
 // emit.rs:5901-5934), reduction-inlined FusedElems, slot reuse after last
 // use and the arena size (memory.rs:39-98).
-int plan(Program &P, const std::vector<int> &roots) {
-    std::vector<Node> &N = P.nodes;
+// The entry's interface: inputs in the order of the first Load of each name;
+// outputs the Stores in node order, then the roots not already outputs
+// (labels "root<i>").
+int io_plan(Program &P, const std::vector<int> &roots) {
+    const std::vector<Node> &N = P.nodes;
     const int count = static_cast<int>(N.size());
-    P.place.assign(count, Place::Slot);
-    P.slot.assign(count, -1);
     P.input_of_load.assign(count, -1);
-    P.direct_output.assign(count, -1);
+    P.input_labels.clear();
+    P.output_labels.clear();
+    P.output_node.clear();
     for (int i = 0; i < count; ++i) {
-        const Node &n = N[i];
-        if (n.op == Op::Load) {
-            P.place[i] = Place::Input;
-            int slot = -1;
-            for (size_t k = 0; k < P.input_labels.size(); ++k)
-                if (P.input_labels[k] == n.name) slot = static_cast<int>(k);
-            if (slot < 0) {
-                slot = static_cast<int>(P.input_labels.size());
-                P.input_labels.push_back(n.name);
-            }
-            P.input_of_load[i] = slot;
-        } else if (n.op == Op::Drop) {
-            P.place[i] = Place::Skip;
-        } else if (is_view(n.op) || (n.op == Op::Reshape && P.layout[i].root != i)) {
-            P.place[i] = Place::View;
+        if (N[i].op != Op::Load) continue;
+        int slot = -1;
+        for (size_t k = 0; k < P.input_labels.size(); ++k)
+            if (P.input_labels[k] == N[i].name) slot = static_cast<int>(k);
+        if (slot < 0) {
+            slot = static_cast<int>(P.input_labels.size());
+            P.input_labels.push_back(N[i].name);
         }
+        P.input_of_load[i] = slot;
     }
-    // consumers
-    std::vector<std::vector<int>> users(count);
-    for (int i = 0; i < count; ++i)
-        for (int j : N[i].in) users[j].push_back(i);
-    // outputs
     for (int i = 0; i < count; ++i)
         if (N[i].op == Op::Store) {
             P.output_labels.push_back(N[i].name);
@@ -1303,6 +1381,30 @@ int plan(Program &P, const std::vector<int> &roots) {
         P.output_labels.push_back("root" + std::to_string(k));
         P.output_node.push_back(rs[k]);
     }
+    return CHELIS_CUDA_OK;
+}
+
+int plan(Program &P, const std::vector<int> &roots) {
+    std::vector<Node> &N = P.nodes;
+    const int count = static_cast<int>(N.size());
+    P.place.assign(count, Place::Slot);
+    P.slot.assign(count, -1);
+    P.direct_output.assign(count, -1);
+    CHELIS_TRY(io_plan(P, roots));
+    for (int i = 0; i < count; ++i) {
+        const Node &n = N[i];
+        if (n.op == Op::Load) {
+            P.place[i] = Place::Input;
+        } else if (n.op == Op::Drop) {
+            P.place[i] = Place::Skip;
+        } else if (is_view(n.op) || (n.op == Op::Reshape && P.layout[i].root != i)) {
+            P.place[i] = Place::View;
+        }
+    }
+    // consumers
+    std::vector<std::vector<int>> users(count);
+    for (int i = 0; i < count; ++i)
+        for (int j : N[i].in) users[j].push_back(i);
     std::vector<bool> is_output(count, false);
     for (int o : P.output_node) is_output[o] = true;
     // a FusedElem read only by a Sum / MaxReduce runs inside the reduction
@@ -3161,8 +3263,97 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
 using namespace chelis;
 
 struct chelis_dag_program {
-    dag::Program prog;
+    dag::Program prog;  // the planned program; for a symbolic one, its interface only
+    // symbolic extents: the nodes are re-parsed and planned for each binding
+    bool symbolic = false;
+    json::Value nodes;
+    std::vector<int> roots;
+    std::vector<std::string> symbols;  // in the order their first Load axis appears
+    struct Source {
+        int input, axis, symbol;
+    };
+    std::vector<Source> sources;       // every Load axis a name is bound from
+    std::mutex mu;
+    std::vector<std::pair<std::vector<int64_t>, std::shared_ptr<chelis_dag_program>>> cache;  // newest last
 };
+
+namespace chelis {
+namespace dag {
+
+constexpr size_t kMaxBindings = 8;  // planned instances kept per symbolic program
+
+// Parse, check and plan `nodes` with every name bound (`bind` null: a static
+// program).
+int build(const json::Value &nodes, const std::vector<int> &roots,
+          const std::vector<std::pair<std::string, int64_t>> *bind, Program &P) {
+    t_sym = SymbolScope{};
+    t_sym.bind = bind;
+    int st = CHELIS_CUDA_OK;
+    for (size_t i = 0; i < nodes.a.size() && st == CHELIS_CUDA_OK; ++i) st = parse_node(nodes.a[i], i, P.nodes);
+    t_sym = SymbolScope{};
+    CHELIS_TRY(st);
+    CHELIS_TRY(check_and_layout(P));
+    CHELIS_TRY(plan(P, roots));
+    for (auto &n : P.nodes)
+        if (n.op == Op::GuardedFail) {
+            n.fail_id = register_fail_message(n.message.c_str());
+            P.fail_ids.push_back(n.fail_id);
+        }
+    return CHELIS_CUDA_OK;
+}
+
+std::vector<std::pair<std::string, int64_t>> bindings(const chelis_dag_program &p, const std::vector<int64_t> &v) {
+    std::vector<std::pair<std::string, int64_t>> b;
+    for (size_t k = 0; k < p.symbols.size(); ++k) b.emplace_back(p.symbols[k], v[k]);
+    return b;
+}
+
+// The symbols' values read from the inputs' shapes; every Load axis that
+// names a symbol must agree (the generated entries' check, emit.rs:1141-1170).
+int bind_values(const chelis_dag_program &p, const chelis_gpu_tensor *const *views, std::vector<int64_t> *values) {
+    values->assign(p.symbols.size(), -1);
+    std::vector<int> first(p.symbols.size(), -1);
+    for (size_t k = 0; k < p.sources.size(); ++k) {
+        const auto &src = p.sources[k];
+        const chelis_gpu_tensor *t = views[src.input];
+        if (!t || src.axis >= t->rank) return set_error(CHELIS_CUDA_ERR_DOMAIN, "numeric trap: domain in load at i64");
+        const int64_t e = t->shape[src.axis];
+        int64_t &v = (*values)[src.symbol];
+        if (v < 0) {
+            v = e;
+            first[src.symbol] = static_cast<int>(k);
+        } else if (v != e) {
+            const std::string &name = p.symbols[src.symbol];
+            return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: symbolic dim `%s` mismatch: %s[%d]=%lld but %s=%lld",
+                             name.c_str(), p.prog.input_labels[src.input].c_str(), src.axis,
+                             static_cast<long long>(e), name.c_str(), static_cast<long long>(v));
+        }
+    }
+    return CHELIS_CUDA_OK;
+}
+
+// The planned instance for these values: from the cache, or built and cached.
+int instance(chelis_dag_program &p, const std::vector<int64_t> &values, std::shared_ptr<chelis_dag_program> *out) {
+    std::lock_guard<std::mutex> lock(p.mu);
+    for (size_t k = 0; k < p.cache.size(); ++k)
+        if (p.cache[k].first == values) {
+            auto hit = p.cache[k];
+            p.cache.erase(p.cache.begin() + static_cast<std::ptrdiff_t>(k));
+            p.cache.push_back(hit);
+            *out = hit.second;
+            return CHELIS_CUDA_OK;
+        }
+    auto inst = std::make_shared<chelis_dag_program>();
+    const auto b = bindings(p, values);
+    CHELIS_TRY(build(p.nodes, p.roots, &b, inst->prog));
+    if (p.cache.size() >= kMaxBindings) p.cache.erase(p.cache.begin());
+    p.cache.emplace_back(values, inst);
+    *out = inst;
+    return CHELIS_CUDA_OK;
+}
+
+}  // namespace dag
+}  // namespace chelis
 
 extern "C" {
 
@@ -3177,9 +3368,6 @@ int chelis_dag_from_json(const char *text, int64_t len, chelis_dag_program **out
     const json::Value *roots = doc.get("roots");
     if (!nodes || nodes->kind != json::Value::Arr || !roots || roots->kind != json::Value::Arr)
         return dag::bad("a Dag object has \"nodes\" and \"roots\" arrays");
-    auto p = std::make_unique<chelis_dag_program>();
-    for (size_t i = 0; i < nodes->a.size(); ++i)
-        CHELIS_TRY(dag::parse_node(nodes->a[i], i, p->prog.nodes));
     std::vector<int> rs;
     for (const auto &r : roots->a) {
         int64_t v = 0;
@@ -3187,14 +3375,73 @@ int chelis_dag_from_json(const char *text, int64_t len, chelis_dag_program **out
             return dag::bad("root out of range");
         rs.push_back(static_cast<int>(v));
     }
-    CHELIS_TRY(dag::check_and_layout(p->prog));
-    CHELIS_TRY(dag::plan(p->prog, rs));
-    for (auto &n : p->prog.nodes)
-        if (n.op == dag::Op::GuardedFail) {
-            n.fail_id = register_fail_message(n.message.c_str());
-            p->prog.fail_ids.push_back(n.fail_id);
+    auto p = std::make_unique<chelis_dag_program>();
+    // one parse with unbound names read as placeholders: every op is checked
+    // here; a program with no unbound name is planned from it at once
+    dag::t_sym = dag::SymbolScope{};
+    dag::t_sym.placeholder = true;
+    int st = CHELIS_CUDA_OK;
+    for (size_t i = 0; i < nodes->a.size() && st == CHELIS_CUDA_OK; ++i)
+        st = dag::parse_node(nodes->a[i], i, p->prog.nodes);
+    const bool symbolic = dag::t_sym.saw_symbol;
+    dag::t_sym = dag::SymbolScope{};
+    CHELIS_TRY(st);
+    if (!symbolic) {
+        CHELIS_TRY(dag::check_and_layout(p->prog));
+        CHELIS_TRY(dag::plan(p->prog, rs));
+        for (auto &n : p->prog.nodes)
+            if (n.op == dag::Op::GuardedFail) {
+                n.fail_id = register_fail_message(n.message.c_str());
+                p->prog.fail_ids.push_back(n.fail_id);
+            }
+        *out = p.release();
+        return CHELIS_CUDA_OK;
+    }
+    p->symbolic = true;
+    CHELIS_TRY(dag::io_plan(p->prog, rs));
+    for (size_t i = 0; i < p->prog.nodes.size(); ++i) {
+        const dag::Node &n = p->prog.nodes[i];
+        if (n.op != dag::Op::Load) continue;
+        for (size_t a = 0; a < n.dim_names.size(); ++a) {
+            if (n.dim_names[a].empty()) continue;
+            int sym = -1;
+            for (size_t k = 0; k < p->symbols.size(); ++k)
+                if (p->symbols[k] == n.dim_names[a]) sym = static_cast<int>(k);
+            if (sym < 0) {
+                sym = static_cast<int>(p->symbols.size());
+                p->symbols.push_back(n.dim_names[a]);
+            }
+            p->sources.push_back({p->prog.input_of_load[i], static_cast<int>(a), sym});
         }
+    }
+    p->nodes = *nodes;
+    p->roots = rs;
     *out = p.release();
+    return CHELIS_CUDA_OK;
+}
+
+int32_t chelis_dag_symbol_count(const chelis_dag_program *p) {
+    return p ? static_cast<int32_t>(p->symbols.size()) : -1;
+}
+const char *chelis_dag_symbol_name(const chelis_dag_program *p, int32_t i) {
+    if (!p || i < 0 || i >= static_cast<int32_t>(p->symbols.size())) return nullptr;
+    return p->symbols[i].c_str();
+}
+
+int chelis_dag_bind(chelis_dag_program *p, const int64_t *values, int32_t n, chelis_dag_program **out) {
+    if (!p || !out) return dag::bad("null program or output handle");
+    *out = nullptr;
+    if (!p->symbolic) return dag::bad("the program has no symbolic extent to bind");
+    if (n != static_cast<int32_t>(p->symbols.size()) || (n && !values))
+        return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: expected %d symbol values, got %d",
+                         static_cast<int>(p->symbols.size()), static_cast<int>(n));
+    std::vector<int64_t> v(values, values + (n ? n : 0));
+    for (int64_t e : v)
+        if (e < 0) return dag::bad("a symbol value below 0");
+    auto q = std::make_unique<chelis_dag_program>();
+    const auto b = dag::bindings(*p, v);
+    CHELIS_TRY(dag::build(p->nodes, p->roots, &b, q->prog));
+    *out = q.release();
     return CHELIS_CUDA_OK;
 }
 
@@ -3214,15 +3461,15 @@ const char *chelis_dag_output_label(const chelis_dag_program *p, int32_t i) {
     if (!p || i < 0 || i >= static_cast<int32_t>(p->prog.output_labels.size())) return nullptr;
     return p->prog.output_labels[i].c_str();
 }
-int64_t chelis_dag_arena_bytes(const chelis_dag_program *p) { return p ? p->prog.arena_bytes : -1; }
+int64_t chelis_dag_arena_bytes(const chelis_dag_program *p) { return p && !p->symbolic ? p->prog.arena_bytes : -1; }
 int64_t chelis_dag_live_peak_bytes(const chelis_dag_program *p) {
-    return p ? p->prog.live_peak_bytes : -1;
+    return p && !p->symbolic ? p->prog.live_peak_bytes : -1;
 }
 int32_t chelis_dag_slot_count(const chelis_dag_program *p) {
-    return p ? static_cast<int32_t>(p->prog.slot_cap.size()) : -1;
+    return p && !p->symbolic ? static_cast<int32_t>(p->prog.slot_cap.size()) : -1;
 }
 int64_t chelis_dag_output_bytes(const chelis_dag_program *p) {
-    if (!p) return -1;
+    if (!p || p->symbolic) return -1;
     int64_t b = 0;
     for (int o : p->prog.output_node)
         b += dag::count_of(p->prog.nodes[o].shape) * dtype_width(p->prog.nodes[o].dtype);
@@ -3240,6 +3487,16 @@ int chelis_dag_run_device_arena(chelis_dag_program *p, const chelis_device_tenso
                          static_cast<int>(P.input_labels.size()),
                          static_cast<int>(P.output_labels.size()), n_in, n_out);
     if ((n_in && !inputs) || (n_out && !outputs)) return dag::bad("null argument array");
+    if (p->symbolic) {
+        // bind the names from the inputs' shapes, then run that planned instance
+        std::vector<const chelis_gpu_tensor *> tv(n_in, nullptr);
+        for (int k = 0; k < n_in; ++k) tv[k] = chelis_device_tensor_view(inputs[k]);
+        std::vector<int64_t> values;
+        CHELIS_TRY(dag::bind_values(*p, tv.data(), &values));
+        std::shared_ptr<chelis_dag_program> inst;
+        CHELIS_TRY(dag::instance(*p, values, &inst));
+        return chelis_dag_run_device_arena(inst.get(), inputs, n_in, outputs, n_out, arena, arena_bytes);
+    }
     if (arena && arena_bytes < P.arena_bytes)
         return set_error(CHELIS_CUDA_ERR_DOMAIN, "dag: arena of %lld bytes, the plan needs %lld",
                          static_cast<long long>(arena_bytes), static_cast<long long>(P.arena_bytes));

@@ -245,6 +245,9 @@ SIGNATURES = {
     "chelis_dag_live_peak_bytes": (c_i64, [c_vp]),
     "chelis_dag_slot_count": (c_i32, [c_vp]),
     "chelis_dag_output_bytes": (c_i64, [c_vp]),
+    "chelis_dag_symbol_count": (c_i32, [c_vp]),
+    "chelis_dag_symbol_name": (ctypes.c_char_p, [c_vp, c_i32]),
+    "chelis_dag_bind": (c_int, [c_vp, ctypes.POINTER(c_i64), c_i32, ctypes.POINTER(c_vp)]),
     "chelis_dag_run_device": (c_int, [c_vp, _PP, c_i32, _PP, c_i32]),
     "chelis_dag_run_device_arena": (c_int, [c_vp, _PP, c_i32, _PP, c_i32, c_vp, c_i64]),
     "chelis_dag_run": (c_int, [c_vp, _PP, c_int, _PP, c_int]),

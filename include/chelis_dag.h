@@ -12,18 +12,32 @@
  *
  * Inputs are bound in the order of the first Load of each name and outputs
  * are the Store nodes in node order, then the roots (labels "root<i>"), as
- * the generated entries order them (emit.rs:5881-5934).  Shapes must be
- * static.  Supported RiscOps: Load, Store, Const, ConstTensor, Add, Sub,
- * Mul, Div, Pow, FloorDiv, MaxElem, MinElem, Neg, Recip, Exp, Log, Sin,
- * Sqrt, Cos, Tan, Atan, Tanh, Erf, Erfc, Abs, Floor, Ceil, Round (f32 / f64,
- * broadcast through views), FusedElem, Relu, ReluAdjoint, Softmax (last
- * axis, f32), Sum and MaxReduce (any axis; a FusedElem read only by the
- * reduction runs inside it), Count (all axes), BlasMatmul (batched,
- * transposed views taken in place), Gather and ScatterAdd (any signed
- * integer index dtype, batch_rank), Cumsum (last axis), Reshape, Permute,
- * Expand, Shrink, Stride, Pad, Cast (to f32 / f64), Copy, Realize, Drop.
- * Any other op, or a symbolic extent, is CHELIS_CUDA_ERR_UNSUPPORTED at
- * load time (the HIP lane's Unsupported result, lib.rs:104).
+ * the generated entries order them (emit.rs:5881-5934).
+ *
+ * Extents: literal, Named with a size, or symbolic -- DimInfo::Named(name,
+ * None), DimExpr Sym / Mul / Div and RtDim::Sym.  A program with symbolic
+ * extents binds each name from the input axes its Loads declare with it
+ * (every such axis must agree: "symbolic dim `n` mismatch: x[0]=5 but n=4",
+ * the generated entries' check, emit.rs:1141-1170) and is checked and
+ * planned once per set of values (the latest eight are kept).  Runtime
+ * bounds read from a node (RtDim::Node, InputAxis) are
+ * CHELIS_CUDA_ERR_UNSUPPORTED.
+ *
+ * Supported RiscOps: Load, Store, Const, ConstTensor; the elementwise
+ * arithmetic (Add, Sub, Mul, Div, Pow, FloorDiv, TruncDiv, Mod, MaxElem,
+ * MinElem, Neg, Recip, Exp, Log, Sin, Sqrt, Cos, Tan, Atan, Tanh, Erf, Erfc,
+ * Abs, Floor, Ceil, Round on f32 / f64; the integer forms at i8-i64 with the
+ * C lane's traps), Bitwise, Compare, Logical, Where, FloatClassify,
+ * ExtremaAdjoint, FusedElem, Relu, ReluAdjoint, Softmax (last axis, f32),
+ * Sum, MaxReduce, MinReduce, ProdReduce, Argmax, Argmin, Count, Cumsum
+ * (last axis), ReduceWindow, ReduceWindowGrad, BlasMatmul (batched,
+ * transposed views taken in place), Gather, ScatterAdd, Scatter,
+ * ScatterElements, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
+ * NamedCast, Copy, Realize, Drop, Shape, Iota, GuardedFail, the keyed RNG
+ * (KeyFromSeed, Split, FoldIn, SplitN, Dropout, DropoutReplay, UniformLike,
+ * UniformBoundAdjoint) and OrderedAdjointSum.  Any other op, or a node
+ * under a runtime activation, is CHELIS_CUDA_ERR_UNSUPPORTED at load time
+ * (the HIP lane's Unsupported result, lib.rs:104).
  */
 #ifndef CHELIS_DAG_H
 #define CHELIS_DAG_H
@@ -50,6 +64,14 @@ const char *chelis_dag_input_label(const chelis_dag_program *program, int32_t i)
 int32_t chelis_dag_output_count(const chelis_dag_program *program);
 const char *chelis_dag_output_label(const chelis_dag_program *program, int32_t i);
 
+/* Symbolic extents: the names to bind (0 for a static program), and a
+ * static program with the names bound to `values` (in symbol order), for the
+ * plan queries below or a caller-sized arena; release it with
+ * chelis_dag_release.  The plan queries return -1 for an unbound program. */
+int32_t chelis_dag_symbol_count(const chelis_dag_program *program);
+const char *chelis_dag_symbol_name(const chelis_dag_program *program, int32_t i);
+int chelis_dag_bind(chelis_dag_program *program, const int64_t *values, int32_t n,
+                    chelis_dag_program **out);
 /* The storage plan (memory.rs:39-98): every value that needs storage of its
  * own (not an input, a view, an output, a dropped or an inlined node) gets a
  * slot; a slot is reused by a later value once every reader of its previous
@@ -76,7 +98,8 @@ int chelis_dag_run_device_arena(chelis_dag_program *program,
                                 chelis_device_rank n_out, void *arena, int64_t arena_bytes);
 /* Generated-entry host-array ABI (emit.rs:660-800): host inputs, new
  * runtime-owned host outputs; returns with the work complete and the device
- * error word checked (an out-of-range Gather / ScatterAdd index is
+ * error word checked (an out-of-range Gather / Scatter index is the
+ * reference's "gather index 3 out of bounds at axis 1 of extent 3" then
  * "numeric trap: domain in gather at i64"). */
 int chelis_dag_run(chelis_dag_program *program, chelis_tensor **inputs, int n_in,
                    chelis_tensor **outputs, int n_out);

@@ -42,8 +42,19 @@ def f64_scalar(v: float) -> dict:
     return {"dtype": "f64", "bits": "%016x" % struct.unpack("<Q", struct.pack("<d", v))[0]}
 
 
-def lit(n: int) -> dict:
-    return {"Lit": n}
+def lit(n) -> dict:
+    """An RtDim: a literal, or a symbolic name ({"Sym": name})."""
+    return {"Lit": n} if isinstance(n, int) else {"Sym": n}
+
+
+def dim_info(d) -> dict:
+    """A DimInfo: Lit(n), or Named(name, None) for a symbolic extent."""
+    return {"Lit": d} if isinstance(d, int) else {"Named": [d, None]}
+
+
+def dim_expr(d) -> dict:
+    """A DimExpr: Concrete(n) or Sym(name)."""
+    return {"Concrete": d} if isinstance(d, int) else {"Sym": d}
 
 
 class Dag:
@@ -55,13 +66,13 @@ class Dag:
         i = len(self.nodes)
         self.nodes.append({
             "id": i, "op": op, "inputs": list(inputs),
-            "output_type": {"dims": [lit(d) for d in dims], "precision": PRIM[prec]},
+            "output_type": {"dims": [dim_info(d) for d in dims], "precision": PRIM[prec]},
             "reusable_input": None, "span_id": None, "merged_spans": [], "shape_deps": [],
             "result_claim_deps": [], "owner": {"decl": 0, "activation": None}})
         return i
 
-    def dims(self, i: int) -> list[int]:
-        return [d["Lit"] for d in self.nodes[i]["output_type"]["dims"]]
+    def dims(self, i: int) -> list:
+        return [d["Lit"] if "Lit" in d else d["Named"][0] for d in self.nodes[i]["output_type"]["dims"]]
 
     def prec(self, i: int) -> str:
         inv = {v: k for k, v in PRIM.items()}
@@ -168,8 +179,8 @@ class Dag:
 
     def matmul(self, a, b):
         (m, k), (_, n) = self.dims(a), self.dims(b)
-        return self.add({"BlasMatmul": {"batch_dims": [], "m": {"Concrete": m}, "n": {"Concrete": n},
-                                        "k": {"Concrete": k}, "accumulator": PRIM[self.prec(a)]}},
+        return self.add({"BlasMatmul": {"batch_dims": [], "m": dim_expr(m), "n": dim_expr(n),
+                                        "k": dim_expr(k), "accumulator": PRIM[self.prec(a)]}},
                         [a, b], [m, n], self.prec(a))
 
     def permute(self, x, axes):

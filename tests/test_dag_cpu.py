@@ -98,8 +98,9 @@ def test_mlp_program_plans():
     ('{"nodes":[{"id":0,"op":"KeySelect","inputs":[],"output_type":{"dims":[{"Lit":4}],'
      '"precision":"Key"},"owner":{"decl":0,"activation":null}}],"roots":[0]}', 4, "KeySelect"),
     ('{"nodes":[{"id":0,"op":{"Load":{"name":"x"}},"inputs":[],"output_type":{"dims":'
-     '[{"Named":["n",null]}],"precision":"F32"},"owner":{"decl":0,"activation":null}}],'
-     '"roots":[0]}', 4, "symbolic"),
+     '[{"Lit":4}],"precision":"F32"},"owner":{"decl":0,"activation":null}},{"id":1,"op":{"Shrink":'
+     '{"bounds":[[{"Node":2},{"Lit":4}]]}},"inputs":[0],"output_type":{"dims":[{"Lit":4}],"precision":"F32"},'
+     '"owner":{"decl":0,"activation":null}}],"roots":[1]}', 4, "a runtime bound"),
     ('{"nodes":[{"id":0,"op":"Neg","inputs":[0],"output_type":{"dims":[],"precision":"F32"},'
      '"owner":{"decl":0,"activation":null}}],"roots":[0]}', 1, "earlier"),
 ])
@@ -277,3 +278,79 @@ def test_uniform_bound_adjoint_rejections(bound, kshape, dims, message):
     st, h = load(g.json())
     assert st != 0
     assert message in L.last_error()
+
+
+def _symbolic_program():
+    """x[n, 64] @ w[64, 32] -> Relu -> column sums, plus a bias expanded to n rows."""
+    g = D.Dag()
+    x = g.load("x", ["n", 64])
+    w = g.load("w", [64, 32])
+    b = g.load("b", [32])
+    h = g.unary("Relu", g.binary("Add", g.matmul(x, w), g.expand(b, 0, "n")))
+    g.roots = [g.sum(h, 0), h]
+    return g
+
+
+def test_symbolic_program_loads_and_binds():
+    lib = L.load()
+    st, h = load(_symbolic_program().json())
+    assert st == 0, L.last_error()
+    try:
+        assert lib.chelis_dag_symbol_count(h) == 1
+        assert lib.chelis_dag_symbol_name(h, 0) == b"n"
+        assert lib.chelis_dag_input_count(h) == 3
+        assert lib.chelis_dag_output_count(h) == 2
+        assert lib.chelis_dag_arena_bytes(h) == -1          # unbound: no plan yet
+        for n in (1, 300):
+            bound = ctypes.c_void_p()
+            vals = (ctypes.c_int64 * 1)(n)
+            assert lib.chelis_dag_bind(h, vals, 1, ctypes.byref(bound)) == 0, L.last_error()
+            try:
+                assert lib.chelis_dag_symbol_count(bound) == 0
+                assert lib.chelis_dag_output_bytes(bound) == 4 * 32 + 4 * n * 32
+                # the same plan a static program of that size gets
+                g = _symbolic_program()
+                for node in g.nodes:
+                    node["output_type"]["dims"] = [{"Lit": n} if "Named" in d else d
+                                                   for d in node["output_type"]["dims"]]
+                st2, h2 = load(g.json())
+                assert st2 == 0, L.last_error()
+                try:
+                    for q in ("chelis_dag_arena_bytes", "chelis_dag_live_peak_bytes", "chelis_dag_slot_count"):
+                        assert getattr(lib, q)(bound) == getattr(lib, q)(h2), q
+                finally:
+                    lib.chelis_dag_release(h2)
+            finally:
+                lib.chelis_dag_release(bound)
+        bound = ctypes.c_void_p()
+        assert lib.chelis_dag_bind(h, (ctypes.c_int64 * 2)(1, 2), 2, ctypes.byref(bound)) != 0
+        assert "expected 1 symbol values" in L.last_error()
+    finally:
+        lib.chelis_dag_release(h)
+
+
+def test_symbol_bound_by_no_input_is_reported_at_bind():
+    g = D.Dag()
+    x = g.load("x", [4])
+    g.roots = [g.expand(x, 0, "m")]          # m names no input axis
+    st, h = load(g.json())
+    assert st == 0, L.last_error()
+    lib = L.load()
+    try:
+        assert lib.chelis_dag_symbol_count(h) == 0
+        assert lib.chelis_dag_arena_bytes(h) == -1
+        bound = ctypes.c_void_p()
+        assert lib.chelis_dag_bind(h, None, 0, ctypes.byref(bound)) == 1
+        assert "missing symbolic dimension binding: `m`" in L.last_error()
+        assert not bound.value
+    finally:
+        lib.chelis_dag_release(h)
+
+
+def test_symbolic_program_still_rejects_unsupported_ops():
+    g = D.Dag()
+    x = g.load("x", ["n"])
+    g.roots = [g.add("KeySelect", [x], ["n"])]
+    st, h = load(g.json())
+    assert st == 4
+    assert "KeySelect" in L.last_error()

@@ -1364,3 +1364,89 @@ def test_reduce_window_integer_sum_and_overflow(cuda):
     finally:
         L.load().chelis_dag_release(h)
     L.call("chelis_cuda_device_status")
+
+
+# ---- symbolic extents: names bound from the inputs' shapes per run
+
+def _sym_mlp(n):
+    """x[n, 64] @ w[64, 32] + b -> Relu; column sums and the activations.
+    `n` is a name (symbolic program) or an int (static program)."""
+    g = D.Dag()
+    x = g.load("x", [n, 64])
+    w = g.load("w", [64, 32])
+    b = g.load("b", [32])
+    h = g.unary("Relu", g.binary("Add", g.matmul(x, w), g.expand(b, 0, n)))
+    g.roots = [g.sum(h, 0), h]
+    return g
+
+
+def test_symbolic_program_runs_at_each_binding(cuda):
+    rng = np.random.default_rng(7)
+    w = torch.from_numpy(rng.standard_normal((64, 32)).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal(32).astype(np.float32)).cuda()
+    hs = program(_sym_mlp("n"))
+    launches = []
+    try:
+        for n in (100, 37, 100, 1, 37):                    # repeats reuse the planned instance
+            x = torch.from_numpy(rng.standard_normal((n, 64)).astype(np.float32)).cuda()
+            got = run(hs, [x, w, b])
+            hn = program(_sym_mlp(n))
+            try:
+                want = run(hn, [x, w, b])
+            finally:
+                L.load().chelis_dag_release(hn)
+            assert len(got) == len(want) == 2
+            for a, e in zip(got, want):
+                assert a.shape == e.shape and a.tobytes() == e.tobytes(), n
+            ref = np.maximum(x.cpu().double().numpy() @ w.cpu().double().numpy() + b.cpu().double().numpy(), 0)
+            assert rel(got[0], ref.sum(0)) <= 1e-5
+    finally:
+        L.load().chelis_dag_release(hs)
+
+
+def test_symbolic_dim_mismatch_is_reported(cuda):
+    g = D.Dag()
+    a, c = g.load("a", ["n", 4]), g.load("c", ["n", 4])
+    g.roots = [g.binary("Add", a, c)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match=r"symbolic dim `n` mismatch: c\[0\]=3 but n=5"):
+            run(h, [torch.zeros(5, 4, device="cuda"), torch.zeros(3, 4, device="cuda")])
+        (got,) = run(h, [torch.ones(3, 4, device="cuda"), torch.ones(3, 4, device="cuda")])
+        assert got.shape == (3, 4) and (got == 2).all()
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+def test_symbolic_program_in_a_caller_arena(cuda):
+    """chelis_dag_bind gives the plan for a binding; its arena runs the symbolic program."""
+    lib = L.load()
+    hs = program(_sym_mlp("n"))
+    bound = ctypes.c_void_p()
+    try:
+        L.call("chelis_dag_bind", hs, (ctypes.c_int64 * 1)(50), 1, ctypes.byref(bound))
+        need = lib.chelis_dag_arena_bytes(bound)
+        assert need > 0
+        arena = torch.empty(need, dtype=torch.uint8, device="cuda")
+        rng = np.random.default_rng(8)
+        ts = [torch.from_numpy(rng.standard_normal(s).astype(np.float32)).cuda() for s in ((50, 64), (64, 32), (32,))]
+        owners = []
+        for t in ts:
+            shape = (ctypes.c_int64 * t.dim())(*t.shape)
+            owners.append(lib.chelis_device_tensor_borrow_shape(L.DTYPE_F32, t.dim(), shape, t.data_ptr(),
+                                                                t.numel() * 4))
+        ins = (ctypes.c_void_p * 3)(*owners)
+        outs = (ctypes.c_void_p * 2)()
+        L.call("chelis_dag_run_device_arena", hs, ins, 3, outs, 2, arena.data_ptr(), need)
+        L.call("chelis_cuda_synchronize")
+        with pytest.raises(L.ChelisCudaError, match="arena of"):
+            L.call("chelis_dag_run_device_arena", hs, ins, 3, outs, 2, arena.data_ptr(), need - 256)
+        for o in list(outs):
+            if o:
+                lib.chelis_device_tensor_release(o)
+        for o in owners:
+            lib.chelis_device_tensor_release(o)
+    finally:
+        if bound.value:
+            lib.chelis_dag_release(bound)
+        lib.chelis_dag_release(hs)
