@@ -28,7 +28,10 @@
 //                         index kernels
 //   Shape                 a constant (extents are concrete)
 //   OrderedAdjointSum     the adjacent-pair tree over List cotangents
-//   UniformBoundAdjoint   a bound's pathwise adjoint under the forward key ([05-OP-52]; bad indices set the
+//   UniformBoundAdjoint   a bound's pathwise adjoint under the forward key
+//   ExtentWitness, CheckedExtent, CheckedUnitAxis
+//                         shape contracts, decided when the program is planned
+//                         and reported when the node runs ([05-OP-52]; bad indices set the
 //                         device error word: "numeric trap: domain in gather")
 //   Reshape, Permute, Expand, Shrink, Stride, Store
 //                         metadata views (a Reshape of a non-dense view is
@@ -93,7 +96,7 @@ enum class Op {
     Copy, Drop, Store, Compare, Logical, Where, MinReduce, Argmax, Argmin, ProdReduce,
     FloatClassify, ExtremaAdjoint, KeyFromSeed, SplitKey, FoldIn, SplitN, Dropout, Arith, NamedCast,
     GuardedFail, UniformLike, Iota, ReduceWindow, ReduceWindowGrad, Scatter, ScatterElements, Shape,
-    OrderedAdjointSum, UniformBoundAdjoint
+    OrderedAdjointSum, UniformBoundAdjoint, ExtentWitness, CheckedExtent
 };
 
 constexpr int kMaxAdjointInputs = 64;  // OrderedAdjointSum inputs taken in one launch
@@ -134,6 +137,8 @@ struct Node {
     uint32_t fail_id = 0;                              // its registered message id
     std::vector<int64_t> window, wstride;             // ReduceWindow(Grad)
     std::vector<std::string> dim_names;                // per axis: the unbound name, or ""
+    std::vector<std::pair<std::string, bool>> claims;  // ExtentWitness (claim, requirement_declares) /
+                                                       // CheckedExtent labels
 };
 
 // Static layout of a node's value: elements at root storage + offset +
@@ -708,6 +713,64 @@ int parse_node(const json::Value &jn, size_t index, std::vector<Node> &nodes) {
         CHELIS_TRY(need_inputs(1));
         if (!as_index(field("axis"), &v)) return bad("Shape axis");
         n.axis = static_cast<int>(v);
+    } else if (name == "ExtentWitness" || name == "CheckedExtent") {
+        // shape contracts (dag.rs:1236-1275): an observed extent checked
+        // against literal requirements and other witnesses, as a scalar i64
+        n.op = name == "ExtentWitness" ? Op::ExtentWitness : Op::CheckedExtent;
+        const json::Value *ax = field("axis");
+        const json::Value *axl = ax ? variant(*ax, "Lit") : nullptr;
+        if (!axl || !as_index(axl, &v)) return bad("shape contract axis", name);
+        n.axis = static_cast<int>(v);
+        const json::Value *cl = field("claims");
+        if (!cl || cl->kind != json::Value::Arr) return bad("shape contract claims", name);
+        if (n.op == Op::ExtentWitness) {
+            static const char *sites[] = {"LiteralResultClaim", "Caller", "LocalExpand", "ResultClaim",
+                                          "LocalAscriptionClaim"};
+            const json::Value *st = field("site");
+            n.kind = -1;
+            for (int k = 0; k < 5 && st; ++k)
+                if ((st->kind == json::Value::Str && st->s == sites[k]) ||
+                    (st->kind == json::Value::Obj && st->o.size() == 1 && st->o[0].first == sites[k]))
+                    n.kind = k;
+            if (n.kind < 0) return bad("ExtentWitness site");
+            const json::Value *pm = field("parameter");
+            if (!pm || pm->kind != json::Value::Str) return bad("ExtentWitness parameter");
+            n.name = pm->s;
+            const json::Value *rq = field("requirements");
+            if (!rq || rq->kind != json::Value::Arr) return bad("ExtentWitness requirements");
+            for (const auto &r : rq->a) {
+                int sdt = 0;
+                uint64_t bits = 0;
+                CHELIS_TRY(scalar(&r, &sdt, &bits));
+                if (sdt != CHELIS_DTYPE_I64) return bad("extent witness requires i64");
+                n.window.push_back(static_cast<int64_t>(bits));
+            }
+            for (const auto &c : cl->a) {
+                const json::Value *cn = c.get("claim"), *rd = c.get("requirement_declares");
+                if (!cn || cn->kind != json::Value::Str || !rd || rd->kind != json::Value::Bool)
+                    return bad("ExtentWitness claim");
+                n.claims.emplace_back(cn->s, rd->b);
+            }
+            if (n.in.size() != 1 + n.claims.size()) return bad("wrong input count for", name);
+        } else {
+            const json::Value *ow = field("owner");
+            if (!ow || ow->kind != json::Value::Str || (ow->s != "reshape" && ow->s != "concat"))
+                return bad("CheckedExtent owner");
+            n.name = ow->s;
+            for (const auto &c : cl->a) {
+                if (c.kind != json::Value::Str) return bad("CheckedExtent claim");
+                n.claims.emplace_back(c.s, false);
+            }
+            if (n.in.size() != 1 + n.claims.size()) return bad("wrong input count for", name);
+        }
+    } else if (name == "CheckedUnitAxis") {
+        // the tensor with one axis refined to 1 after its witness: a view
+        n.op = Op::Reshape;
+        CHELIS_TRY(need_inputs(2));
+        const json::Value *ax = field("axis");
+        const json::Value *axl = ax ? variant(*ax, "Lit") : nullptr;
+        if (!axl || !as_index(axl, &v)) return bad("CheckedUnitAxis axis");
+        n.axis = static_cast<int>(v);
     } else if (name == "OrderedAdjointSum") {
         // spec/06 2.4: the adjacent-pair tree over queued List cotangent
         // contributions; `groups` gives each group's input count
@@ -858,6 +921,16 @@ int check_same_shape(const Node &n, const Node &src, const char *what) {
 }
 
 // Shapes and dtypes of each node against its operands; layouts of views.
+// an i64 scalar whose value the plan knows: a Const, a Shape read or a
+// decided shape contract
+bool host_extent(const Node &n, int64_t *out) {
+    if (n.dtype != CHELIS_DTYPE_I64 || !n.shape.empty()) return false;
+    if (n.op != Op::Const && n.op != Op::Shape && n.op != Op::ExtentWitness && n.op != Op::CheckedExtent)
+        return false;
+    *out = static_cast<int64_t>(n.bits);
+    return true;
+}
+
 int check_and_layout(Program &P) {
     std::vector<Node> &N = P.nodes;
     const int count = static_cast<int>(N.size());
@@ -1012,6 +1085,68 @@ int check_and_layout(Program &P) {
                 if (n.dtype != CHELIS_DTYPE_I64 || !n.shape.empty()) return bad("Shape result must be an i64 scalar");
                 // extents are concrete here: the read is a constant written into its output
                 n.bits = static_cast<uint64_t>(x.shape[n.axis]);
+                own();
+                break;
+            }
+            case Op::ExtentWitness: case Op::CheckedExtent: {
+                // every extent is concrete here, so the contract is decided now;
+                // a broken one is reported when the node runs
+                if (n.dtype != CHELIS_DTYPE_I64 || !n.shape.empty()) return bad("a shape contract result must be an i64 scalar", n.opname);
+                char buf[512];
+                n.message.clear();
+                if (n.op == Op::ExtentWitness) {
+                    if (n.kind == 0 || (n.kind == 4 && !n.window.empty())) {
+                        if (n.window.empty()) return bad("ExtentWitness literal claim without a requirement");
+                        n.bits = static_cast<uint64_t>(n.window[0]);  // the claimed extent itself
+                        own();
+                        break;
+                    }
+                    const Node &x = src(0);
+                    if (n.axis >= static_cast<int>(x.shape.size())) return bad("extent witness axis out of bounds");
+                    const int64_t observed = x.shape[n.axis];
+                    const char *op = n.kind == 1 ? "load" : n.kind == 2 ? "expand" : "shape";
+                    const std::string label = n.kind == 2 ? "node " + std::to_string(n.in[0]) : n.name;
+                    for (int64_t req : n.window)
+                        if (n.message.empty() && req != observed) {
+                            snprintf(buf, sizeof buf,
+                                     "extent `%lld`: claimed = %lld, %s axis %d = %lld\nnumeric trap: domain in %s at i64",
+                                     static_cast<long long>(req), static_cast<long long>(req), label.c_str(), n.axis,
+                                     static_cast<long long>(observed), op);
+                            n.message = buf;
+                        }
+                    for (size_t k = 0; k < n.claims.size() && n.message.empty(); ++k) {
+                        const Node &e = src(static_cast<int>(k + 1));
+                        if (e.op != Op::ExtentWitness) return bad("extent claim requires a witness edge");
+                        const int64_t required = static_cast<int64_t>(e.bits);
+                        if (required == observed) continue;
+                        char here[160], there[160];
+                        snprintf(here, sizeof here, "%s axis %d = %lld", label.c_str(), n.axis,
+                                 static_cast<long long>(observed));
+                        snprintf(there, sizeof there, "%s axis %d = %lld", e.name.c_str(), e.axis,
+                                 static_cast<long long>(required));
+                        const bool declares = n.claims[k].second;
+                        snprintf(buf, sizeof buf, "extent `%s`: %s, %s\nnumeric trap: domain in %s at i64",
+                                 n.claims[k].first.c_str(), declares ? there : here, declares ? here : there, op);
+                        n.message = buf;
+                    }
+                    n.bits = static_cast<uint64_t>(observed);
+                } else {
+                    int64_t actual = 0;
+                    if (!host_extent(src(0), &actual)) return unsupported("CheckedExtent over a computed extent");
+                    for (size_t k = 0; k < n.claims.size() && n.message.empty(); ++k) {
+                        int64_t required = 0;
+                        if (!host_extent(src(static_cast<int>(k + 1)), &required))
+                            return unsupported("CheckedExtent over a computed extent");
+                        if (required != actual) {
+                            snprintf(buf, sizeof buf,
+                                     "extent `%s`: claimed = %lld, %s axis %d = %lld\nnumeric trap: domain in %s at i64",
+                                     n.claims[k].first.c_str(), static_cast<long long>(required), n.name.c_str(),
+                                     n.axis, static_cast<long long>(actual), n.name.c_str());
+                            n.message = buf;
+                        }
+                    }
+                    n.bits = static_cast<uint64_t>(actual);
+                }
                 own();
                 break;
             }
@@ -1205,6 +1340,12 @@ int check_and_layout(Program &P) {
             }
             case Op::Reshape: {
                 const Node &s = src(0);
+                if (n.opname == "CheckedUnitAxis") {
+                    std::vector<int64_t> want = s.shape;
+                    if (n.axis >= static_cast<int>(want.size())) return bad("CheckedUnitAxis axis");
+                    if (want[n.axis] != 1) return bad("CheckedUnitAxis over an axis whose extent is not 1");
+                    if (n.shape != want) return bad("CheckedUnitAxis result shape");
+                }
                 if (s.dtype != n.dtype || count_of(s.shape) != count_of(n.shape))
                     return bad("Reshape changes the element count");
                 const Layout &SL = P.layout[n.in[0]];
@@ -2634,6 +2775,9 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
     const int w = dtype_width(n.dtype);
     auto in = [&](int k) -> Value & { return val[n.in[k]]; };
     switch (n.op) {
+        case Op::ExtentWitness: case Op::CheckedExtent:
+            if (!n.message.empty()) return set_error(CHELIS_CUDA_ERR_DOMAIN, "%s", n.message.c_str());
+            // fall through: the extent is a constant
         case Op::Const: case Op::Shape: {
             if (cnt == 0) return CHELIS_CUDA_OK;
             switch (w) {

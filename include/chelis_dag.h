@@ -35,7 +35,8 @@
  * ScatterElements, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
  * NamedCast, Copy, Realize, Drop, Shape, Iota, GuardedFail, the keyed RNG
  * (KeyFromSeed, Split, FoldIn, SplitN, Dropout, DropoutReplay, UniformLike,
- * UniformBoundAdjoint) and OrderedAdjointSum.  Any other op, or a node
+ * UniformBoundAdjoint), OrderedAdjointSum and the shape contracts
+ * (ExtentWitness, CheckedExtent, CheckedUnitAxis).  Any other op, or a node
  * under a runtime activation, is CHELIS_CUDA_ERR_UNSUPPORTED at load time
  * (the HIP lane's Unsupported result, lib.rs:104).
  */

@@ -354,3 +354,14 @@ def test_symbolic_program_still_rejects_unsupported_ops():
     st, h = load(g.json())
     assert st == 4
     assert "KeySelect" in L.last_error()
+
+
+def test_broken_static_contract_loads_and_fails_only_when_run():
+    g = D.Dag()
+    x = g.load("x", [5, 4])
+    w = g.add({"ExtentWitness": {"site": "Caller", "parameter": "x", "axis": {"Lit": 0},
+                                 "requirements": [{"dtype": "int64", "value": 8}], "claims": []}}, [x], [], "i64")
+    g.roots = [w]
+    st, h = load(g.json())
+    assert st == 0, L.last_error()
+    L.load().chelis_dag_release(h)

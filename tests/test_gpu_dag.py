@@ -1450,3 +1450,83 @@ def test_symbolic_program_in_a_caller_arena(cuda):
         if bound.value:
             lib.chelis_dag_release(bound)
         lib.chelis_dag_release(hs)
+
+
+# ---- shape contracts (ExtentWitness / CheckedExtent / CheckedUnitAxis;
+# eval.rs:5149-5299): decided from the bound extents, reported when the node runs
+
+def _witness(g, x, param, axis, reqs=(), claims=(), site="Caller"):
+    body = {"site": site, "parameter": param, "axis": {"Lit": axis},
+            "requirements": [{"dtype": "int64", "value": r} for r in reqs],
+            "claims": [{"claim": c, "requirement_declares": d} for c, d, _ in claims]}
+    return g.add({"ExtentWitness": body}, [x] + [e for _, _, e in claims], [], "i64")
+
+
+def _contract_program():
+    g = D.Dag()
+    x, y = g.load("x", ["n", 4]), g.load("y", ["m", 4])
+    wx = _witness(g, x, "x", 0)
+    wy = _witness(g, y, "y", 0, claims=[("n", True, wx)])
+    w4 = _witness(g, x, "x", 1, reqs=[4])
+    g.roots = [wx, wy, w4, g.binary("Add", x, x)]
+    return g
+
+
+def test_extent_witnesses_pass_and_return_the_extent(cuda):
+    h = program(_contract_program())
+    try:
+        got = run(h, [torch.ones(5, 4, device="cuda"), torch.ones(5, 4, device="cuda")])
+    finally:
+        L.load().chelis_dag_release(h)
+    assert [int(v) for v in got[:3]] == [5, 5, 4]
+    assert (got[3] == 2).all()
+
+
+def test_extent_witness_claim_mismatch_is_reported(cuda):
+    h = program(_contract_program())
+    try:
+        with pytest.raises(L.ChelisCudaError,
+                           match=r"extent `n`: x axis 0 = 5, y axis 0 = 3\nnumeric trap: domain in load at i64"):
+            run(h, [torch.ones(5, 4, device="cuda"), torch.ones(3, 4, device="cuda")])
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+@pytest.mark.parametrize("site,message", [
+    ("Caller", r"extent `8`: claimed = 8, x axis 0 = 5\nnumeric trap: domain in load at i64"),
+    ("LocalExpand", r"extent `8`: claimed = 8, node 0 axis 0 = 5\nnumeric trap: domain in expand at i64"),
+])
+def test_extent_witness_literal_requirement(cuda, site, message):
+    g = D.Dag()
+    x = g.load("x", ["n", 4])
+    g.roots = [_witness(g, x, "x", 0, reqs=[8], site=site)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError, match=message):
+            run(h, [torch.ones(5, 4, device="cuda")])
+        (got,) = run(h, [torch.ones(8, 4, device="cuda")])
+        assert int(got) == 8
+    finally:
+        L.load().chelis_dag_release(h)
+
+
+def test_checked_extent_and_unit_axis(cuda):
+    g = D.Dag()
+    x = g.load("x", ["n", 1])
+    shape0 = g.add({"Shape": {"axis": 0}}, [x], [], "i64")
+    six = g.add({"Const": {"value": {"dtype": "int64", "value": 6}}}, [], [], "i64")
+    chk = g.add({"CheckedExtent": {"owner": "reshape", "claims": ["n"], "axis": {"Lit": 0}}}, [shape0, six], [], "i64")
+    w1 = _witness(g, x, "x", 1, reqs=[1])
+    unit = g.add({"CheckedUnitAxis": {"axis": {"Lit": 1}}}, [x, w1], ["n", 1])
+    g.roots = [chk, g.binary("Mul", unit, unit)]
+    h = program(g)
+    try:
+        with pytest.raises(L.ChelisCudaError,
+                           match=r"extent `n`: claimed = 6, reshape axis 0 = 5\nnumeric trap: domain in reshape at i64"):
+            run(h, [torch.ones(5, 1, device="cuda")])
+        xs = torch.arange(6, dtype=torch.float32, device="cuda").view(6, 1)
+        got = run(h, [xs])
+        assert int(got[0]) == 6
+        assert np.array_equal(got[1], (xs * xs).cpu().numpy())
+    finally:
+        L.load().chelis_dag_release(h)
