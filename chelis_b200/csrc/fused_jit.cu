@@ -231,12 +231,32 @@ std::string kernel_source(bool f32, const chelis_fused_step *steps, int n_steps,
 std::string reduce_source(bool f32, const chelis_fused_step *steps, int n_steps, int n_inputs,
                           int rank, uint32_t unit_inner, bool i32, bool sum) {
     const int V = f32 ? 4 : 2;
+    const int PASS = 32 * V;  // leaves one warp covers per pass: a complete subtree
+    constexpr int G = 4;      // passes loaded together: G passes from an aligned start are a subtree too
+    constexpr int LOG_G = 2;  // (eight measured slower than four: register pressure)
     const std::string T = f32 ? "float" : "double";
     const std::string add = f32 ? "__fadd_rn" : "__dadd_rn";
-    const std::string body = vector_body(f32, steps, n_steps, n_inputs, rank, unit_inner, i32,
-                                         "w * a.len + c0 + lane * " + std::to_string(V));
-    if (body.empty()) return "";
     const std::string last = "s" + std::to_string(n_steps - 1) + "_";
+    auto body_at = [&](const std::string &offset) {
+        return vector_body(f32, steps, n_steps, n_inputs, rank, unit_inner, i32,
+                           "w * a.len + c0 + " + offset + " + lane * " + std::to_string(V));
+    };
+    if (body_at("0").empty()) return "";
+    // the lane's V leaves as their subtree (sum), or the in-order max update
+    auto lane_sum = [&]() {
+        if (V == 4)
+            return add + "(" + add + "(" + last + "0, " + last + "1), " + add + "(" + last + "2, " + last + "3))";
+        return add + "(" + last + "0, " + last + "1)";
+    };
+    auto max_update = [&](const std::string &offset) {
+        std::string u;
+        for (int e = 0; e < V; ++e) {
+            const std::string v = last + std::to_string(e);
+            u += "    if (isnan(" + v + ")) nan = true; else if (!(best > " + v + ")) { best = " + v +
+                 "; at = c0 + " + offset + " + lane * " + std::to_string(V) + " + " + std::to_string(e) + "; }\n";
+        }
+        return u;
+    };
     std::string s = kPrelude;
     s += "extern \"C\" __global__ void __launch_bounds__(256) chelis_fused_jit(Args a) {\n";
     s += "  const int lane = threadIdx.x & 31;\n";
@@ -249,23 +269,46 @@ std::string reduce_source(bool f32, const chelis_fused_step *steps, int n_steps,
                                          : std::string("__longlong_as_double(0xfff0000000000000ll)")) +
              "; long long at = -1; bool nan = false;\n";
     }
-    s += "  for (long long c0 = 0; c0 < a.len; c0 += " + std::to_string(32 * V) + ") {\n";
-    s += body;
+    s += "  long long c0 = 0;\n";
+    // groups of G passes: every load of the group is issued before the
+    // reductions, so a warp keeps G vectors per lane in flight
+    s += "  for (; c0 + " + std::to_string(G * PASS) + " <= a.len; c0 += " + std::to_string(G * PASS) + ") {\n";
+    if (sum) s += "    " + T + " tg[" + std::to_string(G) + "];\n";
+    for (int u = 0; u < G; ++u) {
+        const std::string off = std::to_string(u * PASS);
+        s += "    {\n" + body_at(off);
+        if (sum) s += "    tg[" + std::to_string(u) + "] = " + lane_sum() + ";\n";
+        else s += max_update(off);
+        s += "    }\n";
+    }
     if (sum) {
-        if (V == 4)
-            s += "    " + T + " t = " + add + "(" + add + "(" + last + "0, " + last + "1), " + add + "(" +
-                 last + "2, " + last + "3));\n";
-        else
-            s += "    " + T + " t = " + add + "(" + last + "0, " + last + "1);\n";
+        s += "    for (int off = 1; off < 32; off <<= 1) {\n";
+        s += "      #pragma unroll\n";
+        s += "      for (int u = 0; u < " + std::to_string(G) + "; ++u) tg[u] = " + add +
+             "(tg[u], __shfl_xor_sync(0xffffffffu, tg[u], off));\n";
+        s += "    }\n";
+        // the G pass subtrees pair up level by level into the group's subtree
+        for (int h = 1; h < G; h <<= 1)
+            for (int u = 0; u < G; u += 2 * h)
+                s += "    tg[" + std::to_string(u) + "] = " + add + "(tg[" + std::to_string(u) + "], tg[" +
+                     std::to_string(u + h) + "]);\n";
+        s += "    " + T + " t = tg[0];\n";
+        // it enters the carry tree at depth log2(G) (count is a multiple of G here)
+        s += "    { int depth = " + std::to_string(LOG_G) + "; for (long long pending = count >> " +
+             std::to_string(LOG_G) + "; pending & 1; pending >>= 1, ++depth) t = " + add +
+             "(level[depth], t); level[depth] = t; count += " + std::to_string(G) + "; }\n";
+    }
+    s += "  }\n";
+    // the remaining passes, one at a time
+    s += "  for (; c0 < a.len; c0 += " + std::to_string(PASS) + ") {\n";
+    s += body_at("0");
+    if (sum) {
+        s += "    " + T + " t = " + lane_sum() + ";\n";
         s += "    for (int off = 1; off < 32; off <<= 1) t = " + add + "(t, __shfl_xor_sync(0xffffffffu, t, off));\n";
         s += "    { int depth = 0; for (long long pending = count++; pending & 1; pending >>= 1, ++depth) t = " +
              add + "(level[depth], t); level[depth] = t; }\n";
     } else {
-        for (int e = 0; e < V; ++e) {
-            const std::string v = last + std::to_string(e);
-            s += "    if (isnan(" + v + ")) nan = true; else if (!(best > " + v + ")) { best = " + v +
-                 "; at = c0 + lane * " + std::to_string(V) + " + " + std::to_string(e) + "; }\n";
-        }
+        s += max_update("0");
     }
     s += "  }\n";
     if (sum) {

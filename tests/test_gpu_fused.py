@@ -316,7 +316,7 @@ def test_compiled_last_axis_reduction_matches_interpreter(cuda, dtype, kind, cha
     v = 4 if dtype == np.float32 else 2
     # one warp per output: the compiled form takes row counts that fill the
     # GPU (>= 8 warps per SM)
-    for rows, passes in ((1250, 1), (1250, 5), (1250, 32)):
+    for rows, passes in ((1250, 1), (1250, 5), (1250, 7), (1250, 11), (1250, 32), (1250, 45)):
         cols = 32 * v * passes
         x = _special_mix(rng, (rows, cols), dtype)
         x[1, :] = 0.0
