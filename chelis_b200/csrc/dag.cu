@@ -962,9 +962,10 @@ int check_and_layout(Program &P) {
             case Op::Relu: case Op::Softmax: case Op::Cumsum:
                 if (!floating || src(0).dtype != n.dtype) return unsupported(n.opname + " precision");
                 CHELIS_TRY(check_same_shape(n, src(0), n.opname.c_str()));
-                if ((n.op == Op::Softmax || n.op == Op::Cumsum) &&
-                    (n.shape.empty() || n.axis != static_cast<int>(n.shape.size()) - 1))
+                if (n.op == Op::Softmax && (n.shape.empty() || n.axis != static_cast<int>(n.shape.size()) - 1))
                     return unsupported(n.opname + " along a non-last axis");
+                if (n.op == Op::Cumsum && (n.shape.empty() || n.axis >= static_cast<int>(n.shape.size())))
+                    return bad("Cumsum axis");
                 if (n.op == Op::Softmax && n.dtype != CHELIS_DTYPE_F32)
                     return unsupported("Softmax at f64");
                 own();
@@ -1274,9 +1275,15 @@ int check_and_layout(Program &P) {
             case Op::Count: {
                 if (src(0).dtype != CHELIS_DTYPE_BOOL || n.dtype != CHELIS_DTYPE_I64)
                     return unsupported("Count other than bool -> i64");
-                if (static_cast<int>(n.axes.size()) != static_cast<int>(src(0).shape.size()) ||
-                    !n.shape.empty())
-                    return unsupported("Count over some axes");
+                // axes: distinct positions of the input, listed in descending order (dag.rs Count)
+                const int r = static_cast<int>(src(0).shape.size());
+                std::vector<int64_t> kept;
+                for (size_t k = 0; k < n.axes.size(); ++k)
+                    if (n.axes[k] < 0 || n.axes[k] >= r || (k > 0 && n.axes[k] >= n.axes[k - 1]))
+                        return bad("Count axes must be distinct input axes in descending order");
+                for (int d = 0; d < r; ++d)
+                    if (std::find(n.axes.begin(), n.axes.end(), d) == n.axes.end()) kept.push_back(src(0).shape[d]);
+                if (kept != n.shape) return bad("Count result shape");
                 own();
                 break;
             }
@@ -1793,6 +1800,54 @@ struct GatherGeom {
     int64_t qshape[kMaxRank], tshape[kMaxRank];
     int32_t index_width;
 };
+
+template <typename T>
+__device__ __forceinline__ T canonical_nan(T r) {
+    if (r == r) return r;
+    if constexpr (sizeof(T) == 4) return __int_as_float(0x7fc00000);
+    else return __longlong_as_double(0x7ff8000000000000ll);
+}
+
+// Cumsum along a leading axis (spec 05 4310-4325, the C lane's scan): the
+// first element of a line is its first prefix, each later one is added to
+// the previous prefix in axis order (reversed for a decreasing scan); NaN
+// results are stored canonical.  One thread per line; adjacent threads take
+// adjacent lines, which are adjacent in memory for a dense input.
+template <typename T>
+__global__ void cumsum_axis_kernel(const T *__restrict__ x, Strided lines, int64_t xstep, Strided o, int64_t ostep,
+                                   int64_t len, int reverse, T *__restrict__ out, int64_t lanes) {
+    for (int64_t l = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; l < lanes;
+         l += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t xb = offset_of(lines, l), ob = offset_of(o, l);
+        T acc = T(0);
+        for (int64_t t = 0; t < len; ++t) {
+            const int64_t i = reverse ? len - 1 - t : t;
+            const T v = x[xb + i * xstep];
+            if (t == 0) acc = v;
+            else if constexpr (sizeof(T) == 4) acc = __fadd_rn(acc, v);
+            else acc = __dadd_rn(acc, v);
+            out[ob + i * ostep] = canonical_nan(acc);
+        }
+    }
+}
+
+// Count over some axes: block b counts the true elements of output b's
+// counted sub-space (`counted`, in input axis order) at `kept`'s offset; the
+// count is exact in any order.
+__global__ void count_axes_kernel(const uint8_t *__restrict__ x, Strided kept, Strided counted, int64_t outputs,
+                                  int64_t volume, int64_t *__restrict__ out) {
+    __shared__ unsigned long long part[4];
+    for (int64_t o = blockIdx.x; o < outputs; o += gridDim.x) {
+        const int64_t base = offset_of(kept, o);
+        unsigned long long c = 0;
+        for (int64_t e = threadIdx.x; e < volume; e += blockDim.x) c += x[base + offset_of(counted, e)] != 0;
+        for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+        __syncthreads();
+        if (threadIdx.x == 0) out[o] = static_cast<int64_t>(part[0] + part[1] + part[2] + part[3]);
+        __syncthreads();
+    }
+}
 
 template <typename T>
 __global__ void gather_kernel(const T *__restrict__ values, const void *__restrict__ idx,
@@ -2461,13 +2516,6 @@ __device__ T block_pair_tree(int64_t n, int64_t chunk, Leaf leaf, T *part) {
 }
 
 template <typename T>
-__device__ __forceinline__ T canonical_nan(T r) {
-    if (r == r) return r;
-    if constexpr (sizeof(T) == 4) return __int_as_float(0x7fc00000);
-    else return __longlong_as_double(0x7ff8000000000000ll);
-}
-
-template <typename T>
 __global__ void __launch_bounds__(kAdjointThreads) ordered_adjoint_sum_kernel(AdjointLeaves a, int64_t n, int64_t chunk,
                                                                               T *__restrict__ out) {
     __shared__ T part[kAdjointThreads];
@@ -2850,6 +2898,32 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                                                 cols ? cnt / cols : 0, cols);
         }
         case Op::Cumsum: {
+            if (n.axis != static_cast<int>(n.shape.size()) - 1) {
+                // a leading axis: one thread per line, the scan in axis order
+                const Value &x = in(0);
+                const int64_t len = n.shape[n.axis];
+                const int64_t lanes = len ? cnt / len : 0;
+                if (lanes == 0) return CHELIS_CUDA_OK;
+                Strided lines{}, o{};
+                const std::vector<int64_t> ds = dense_strides(n.shape);
+                for (int d = 0; d < static_cast<int>(n.shape.size()); ++d) {
+                    if (d == n.axis) continue;
+                    lines.shape[lines.rank] = o.shape[o.rank] = n.shape[d];
+                    lines.stride[lines.rank++] = x.strides[d];
+                    o.stride[o.rank++] = ds[d];
+                }
+                if (n.dtype == CHELIS_DTYPE_F64)
+                    cumsum_axis_kernel<double><<<grid_for(lanes), 256, 0, s>>>(
+                        reinterpret_cast<const double *>(x.ptr), lines, x.strides[n.axis], o, ds[n.axis], len,
+                        n.reverse, reinterpret_cast<double *>(out), lanes);
+                else
+                    cumsum_axis_kernel<float><<<grid_for(lanes), 256, 0, s>>>(
+                        reinterpret_cast<const float *>(x.ptr), lines, x.strides[n.axis], o, ds[n.axis], len,
+                        n.reverse, reinterpret_cast<float *>(out), lanes);
+                g_launches++;
+                CHELIS_LAUNCH_CHECK("dag::cumsum_axis_kernel");
+                return CHELIS_CUDA_OK;
+            }
             Value x = in(0);
             CHELIS_TRY(dense(x));
             const int64_t len = n.shape.back();
@@ -2861,10 +2935,28 @@ int Run::node(int i, const std::vector<const chelis_gpu_tensor *> &inputs) {
                                                 reinterpret_cast<float *>(out), lanes, len, n.reverse);
         }
         case Op::Count: {
-            Value x = in(0);
-            CHELIS_TRY(dense(x));
-            return chelis_cuda_count_bool(reinterpret_cast<const uint8_t *>(x.ptr),
-                                          count_of(x.shape), reinterpret_cast<int64_t *>(out));
+            const Value &x = in(0);
+            if (n.shape.empty()) {
+                Value d = x;
+                CHELIS_TRY(dense(d));
+                return chelis_cuda_count_bool(reinterpret_cast<const uint8_t *>(d.ptr), count_of(d.shape),
+                                              reinterpret_cast<int64_t *>(out));
+            }
+            if (cnt == 0) return CHELIS_CUDA_OK;
+            Strided kept{}, counted{};
+            for (int d = 0; d < static_cast<int>(x.shape.size()); ++d) {
+                Strided &t = std::find(n.axes.begin(), n.axes.end(), d) == n.axes.end() ? kept : counted;
+                t.shape[t.rank] = x.shape[d];
+                t.stride[t.rank] = x.strides[d];
+                ++t.rank;
+            }
+            const int64_t volume = count_of(in(0).shape) / cnt;
+            const unsigned grid = static_cast<unsigned>(cnt < 65535 ? cnt : 65535);
+            count_axes_kernel<<<grid, 128, 0, s>>>(reinterpret_cast<const uint8_t *>(x.ptr), kept, counted, cnt,
+                                                   volume, reinterpret_cast<int64_t *>(out));
+            g_launches++;
+            CHELIS_LAUNCH_CHECK("dag::count_axes_kernel");
+            return CHELIS_CUDA_OK;
         }
         case Op::Matmul: {
             const int r = static_cast<int>(n.shape.size());

@@ -29,8 +29,8 @@
  * Abs, Floor, Ceil, Round on f32 / f64; the integer forms at i8-i64 with the
  * C lane's traps), Bitwise, Compare, Logical, Where, FloatClassify,
  * ExtremaAdjoint, FusedElem, Relu, ReluAdjoint, Softmax (last axis, f32),
- * Sum, MaxReduce, MinReduce, ProdReduce, Argmax, Argmin, Count, Cumsum
- * (last axis), ReduceWindow, ReduceWindowGrad, BlasMatmul (batched,
+ * Sum, MaxReduce, MinReduce, ProdReduce, Argmax, Argmin, Count (any axes),
+ * Cumsum (any axis), ReduceWindow, ReduceWindowGrad, BlasMatmul (batched,
  * transposed views taken in place), Gather, ScatterAdd, Scatter,
  * ScatterElements, Reshape, Permute, Expand, Shrink, Stride, Pad, Cast,
  * NamedCast, Copy, Realize, Drop, Shape, Iota, GuardedFail, the keyed RNG

@@ -365,3 +365,12 @@ def test_broken_static_contract_loads_and_fails_only_when_run():
     st, h = load(g.json())
     assert st == 0, L.last_error()
     L.load().chelis_dag_release(h)
+
+
+def test_count_axes_must_descend():
+    g = D.Dag()
+    m = g.load("m", [3, 4], "bool")
+    g.roots = [g.add({"Count": {"axes": [0, 1]}}, [m], [], "i64")]
+    st, h = load(g.json())
+    assert st != 0
+    assert "descending order" in L.last_error()

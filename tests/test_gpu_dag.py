@@ -1530,3 +1530,54 @@ def test_checked_extent_and_unit_axis(cuda):
         assert np.array_equal(got[1], (xs * xs).cpu().numpy())
     finally:
         L.load().chelis_dag_release(h)
+
+
+@pytest.mark.parametrize("axes", [[2], [1], [0], [2, 0], [2, 1], [2, 1, 0]])
+@pytest.mark.parametrize("permuted", [False, True])
+def test_count_over_axes(cuda, axes, permuted):
+    """Count (dag.rs: true elements over the listed axes, descending, i64)
+    against numpy, on a dense mask and on a permuted view of one."""
+    rng = np.random.default_rng(sum(axes) + 10 * permuted)
+    base = rng.random((6, 5, 4)) < 0.4
+    g = D.Dag()
+    m = g.load("m", [6, 5, 4], "bool")
+    if permuted:
+        m = g.permute(m, [2, 1, 0])
+        view = base.transpose(2, 1, 0)
+    else:
+        view = base
+    dims = [d for i, d in enumerate(view.shape) if i not in axes]
+    g.roots = [g.add({"Count": {"axes": axes}}, [m], dims, "i64")]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(base).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    want = np.count_nonzero(view, axis=tuple(axes))
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("prec", ["f32", "f64"])
+@pytest.mark.parametrize("axis,reverse", [(0, False), (0, True), (1, False), (1, True)])
+def test_cumsum_along_a_leading_axis(cuda, orc, prec, axis, reverse):
+    """Cumsum over axis 0 / 1 of a rank-3 value equals the oracle's scan
+    (orc_cumsum, the C lane's order) applied to that axis moved last."""
+    dt = np.float32 if prec == "f32" else np.float64
+    rng = np.random.default_rng(axis * 2 + reverse)
+    x = (rng.standard_normal((33, 20, 7)) * 10.0 ** rng.integers(-3, 4, size=(33, 20, 7))).astype(dt)
+    x[3, 4, 5] = np.nan
+    g = D.Dag()
+    a = g.load("x", list(x.shape), prec)
+    g.roots = [g.add({"Cumsum": {"axis": axis, "direction": "Decreasing" if reverse else "Increasing"}},
+                     [a], list(x.shape), prec)]
+    h = program(g)
+    try:
+        (got,) = run(h, [torch.from_numpy(x).cuda()])
+    finally:
+        L.load().chelis_dag_release(h)
+    moved = np.ascontiguousarray(np.moveaxis(x, axis, -1))
+    length = moved.shape[-1]
+    want = orc.cumsum(moved.reshape(-1, length), reverse=reverse).reshape(moved.shape)
+    want = np.moveaxis(want, -1, axis)
+    w = np.uint32 if prec == "f32" else np.uint64
+    assert np.array_equal(got.view(w), want.view(w))
